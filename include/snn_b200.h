@@ -1,0 +1,126 @@
+/*
+ * snn_b200.h -- C ABI of libsnnb200.so, the B200 (sm_100a) backend for the
+ * fused 2:4-sparse Conv/Linear + BatchNorm + LIF/IF (+SEW residual add)
+ * layer of SparseSNN's sengine.
+ *
+ * Plain pointers and sizes only.  Device pointers are CUDA global-memory
+ * pointers; `stream` is a cudaStream_t passed as void*.  Every entry point
+ * returns 0 on success and a negative SNN_E* code on failure; the message of
+ * the last failure on the calling thread is available from
+ * snn_last_error_message().  Kernel launches never allocate, synchronise or
+ * change host state, so they may be captured into a CUDA graph.
+ *
+ * Tensor layouts (the reference's, sengine/kernels/interleaved_templates.py:95-154):
+ *   data      [T*B][H][W][Cin]  fp16, NHWC, timestep-major
+ *   out       [T*B][OH][OW][Cout] fp16 spikes (or spikes + residual),
+ *             or fp32 BatchNorm output when neuron == SNN_NEURON_NONE
+ *   state     [B*OH*OW][Cout]   fp32 membrane (read at start when
+ *             SNN_FLAG_READ_STATE, final v written when SNN_FLAG_WRITE_STATE)
+ *   bn_scale, bn_bias [Cout]    fp32, epilogue computes acc*scale + bias
+ *             (the reference keeps BN out of the weights,
+ *             sengine/optimizer.py:160-183)
+ *   residual  [T*B][OH][OW][Cout] fp16 (SEW ADD identity)
+ *   weight    packed 2:4 blob produced by snn_pack_weight_24
+ */
+#ifndef SNN_B200_H
+#define SNN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SNN_ABI_VERSION 1
+
+enum {
+  SNN_OK = 0,
+  SNN_E_INVALID = -1,      /* bad argument or unsupported geometry */
+  SNN_E_NOT_24 = -2,       /* weight has a group of 4 with more than 2 non-zeros */
+  SNN_E_CUDA = -3,         /* CUDA runtime / driver call failed */
+  SNN_E_NO_DEVICE = -4,    /* no sm_100 device */
+  SNN_E_DEVICE = -5        /* kernel reported a bounded-wait timeout */
+};
+
+enum { SNN_NEURON_LIF = 0, SNN_NEURON_IF = 1, SNN_NEURON_NONE = 2 };
+enum { SNN_FLAG_READ_STATE = 1, SNN_FLAG_WRITE_STATE = 2 };
+
+/* One fused layer.  Linear layers are 1x1 convs over H=1, W=rows, B=1. */
+typedef struct snn_conv_desc {
+  int32_t T, B, Cin, H, W;
+  int32_t Cout, KH, KW, stride, pad;
+  int32_t neuron;            /* SNN_NEURON_* */
+  int32_t flags;             /* SNN_FLAG_* */
+  float tau, v_threshold, v_reset;
+} snn_conv_desc;
+
+/* Library ABI version (SNN_ABI_VERSION). */
+int snn_abi_version(void);
+
+/* Checks for an sm_100 device and resolves the driver's tensor-map encoder.
+ * Replaces the per-kernel `int init(void)` of the reference's exported
+ * TileLang .so (sengine/build/export_standalone.py:1-8, called by
+ * sengine/csrc/cpp_executor.cu:637-652). */
+int snn_init(void);
+
+/* Output spatial size for a descriptor. */
+int snn_conv_out_shape(const snn_conv_desc* d, int32_t* OH, int32_t* OW);
+
+/* Bytes of the packed weight blob: compressed fp16 values [Cout_pad][K/2]
+ * followed (256-byte aligned) by metadata words [Cout_pad/128][K/32][128]. */
+int snn_conv_weight_bytes(const snn_conv_desc* d, size_t* bytes);
+
+/* Host-side 2:4 packer.  `w` is the pruned weight in the reference's
+ * PyTorch layout [Cout][Cin][KH][KW] fp32 (host memory); groups of 4 run
+ * along Cin inside each (kh,kw) tap (sengine/optimizer.py:499-523 order).
+ * Writes snn_conv_weight_bytes() bytes to `blob` (host memory).
+ * Returns SNN_E_NOT_24 if a group has more than 2 non-zeros. */
+int snn_pack_weight_24(const snn_conv_desc* d, const float* w, void* blob);
+
+/* Fused sparse conv + BN + neuron over T.  The 6-pointer + stream shape of
+ * the reference's TileLang `call(data, weight, state, bn_scale, bn_bias,
+ * out, stream)` (typedef TLCallFn6, sengine/csrc/sengine_exec.cu:443; call
+ * site sengine/csrc/cpp_executor.cu:909-913), with the layer geometry passed
+ * as a descriptor because one library serves every shape. */
+int snn_conv_forward(const snn_conv_desc* d, const void* data, const void* weight,
+                     float* state, const float* bn_scale, const float* bn_bias,
+                     void* out, void* stream);
+
+/* Same with the SEW residual: out = spike + residual (the "LIF then Add"
+ * epilogue of sengine/kernels/interleaved_templates.py:230-288, with LIF
+ * decay, which the reference executor cannot dispatch: it passes at most 6
+ * arguments, sengine/csrc/cpp_executor.cu:895-914). */
+int snn_conv_forward_res(const snn_conv_desc* d, const void* data, const void* weight,
+                         float* state, const float* bn_scale, const float* bn_bias,
+                         const void* residual, void* out, void* stream);
+
+/* Dense direct-conv stem + BN + neuron (the Cin=3 first layer, which the
+ * reference keeps dense: sengine/graph_slicer.py:106 skips Cin<4 and the
+ * executor runs naive_conv2d_bn_nhwc_kernel, sengine/csrc/cpp_executor.cu:306-347).
+ * x: [Tin][B][Cin][H][W] fp32 NCHW with Tin = 1 (input repeated over T,
+ * models/sewresnet.py:199-201) or Tin = T.  w: [Cout][Cin][KH][KW] fp32.
+ * out: [T][B][OH][OW][Cout] fp16 spikes. */
+int snn_stem_forward(const snn_conv_desc* d, int32_t Tin, const float* x, const float* w,
+                     const float* bn_scale, const float* bn_bias, void* out, void* stream);
+
+/* Classifier tail: global average pool over HW, mean over T, then
+ * logits = feat @ fc_w^T + fc_b (models/sewresnet.py:207-210; the reference
+ * executor runs global_avgpool, temporal_mean and a cuBLAS GEMM,
+ * sengine/csrc/cpp_executor.cu:108-139,991-1016).
+ * x: [T][B][HW][C] fp16; fc_w: [NC][C] fp32; fc_b: [NC] fp32; logits: [B][NC] fp32. */
+int snn_head_forward(int32_t T, int32_t B, int32_t HW, int32_t C, int32_t NC,
+                     const void* x, const float* fc_w, const float* fc_b, float* logits,
+                     void* stream);
+
+/* Reads (and with reset != 0 clears) the device error word that kernels set
+ * when a bounded wait times out.  Synchronises the device. */
+int snn_get_device_error(uint32_t* code, int reset);
+
+/* Message of the last failure on this thread ("" if none). */
+const char* snn_last_error_message(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SNN_B200_H */

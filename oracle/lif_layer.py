@@ -1,0 +1,167 @@
+"""Fused Conv/Linear + BN + LIF (+SEW add) oracle in numpy.
+
+TEST INFRASTRUCTURE ONLY -- see ``oracle/__init__.py``.
+
+Restates the reference PyTorch path for one layer:
+
+* ``SeqToANNContainer(Conv2d, BatchNorm2d)`` (reference ``models/layers.py:26-31``):
+  merge T and B, run the conv (``bias=False``, ``models/sewresnet.py:18-24``)
+  and eval-mode BatchNorm2d, split back.
+* ``MultiStepLIFNeuron`` (reference ``models/neurons.py:187-211``) over
+  ``LIFNeuron.forward`` (``:121-146``): state starts at 0 every forward
+  (``:207``); per step
+  ``v = v*(1-1/tau) + x/tau``; ``spike = (v - v_th >= 0)`` (``heaviside``,
+  ``:69-78``, forward is ``x.ge(0)``); hard reset
+  ``v = (1-spike)*v + spike*v_reset``.
+* ``MultiStepIFNeuron``: ``v = v + x`` then the same fire/reset.
+* SEW ``ADD`` connect: ``out = spike + identity`` (``models/sewresnet.py:50-66``).
+
+The conv is an im2col matrix product accumulated in float64 and rounded to
+float32 once, which is at least as accurate as the reference's float32 conv.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+
+
+@dataclass
+class BNParams:
+    gamma: np.ndarray
+    beta: np.ndarray
+    mean: np.ndarray
+    var: np.ndarray
+    eps: float = 1e-5
+
+    def scale_bias(self):
+        """Per-channel ``(scale, bias)`` with ``bn(y) = y*scale + bias``.
+
+        Restates reference ``sengine/optimizer.py:160-183`` (float64 math,
+        stored as float32; conv bias 0): ``scale = gamma/sqrt(var+eps)``,
+        ``bias = scale*(0-mean) + beta``.
+        """
+        g = self.gamma.astype(np.float64)
+        s = g / np.sqrt(self.var.astype(np.float64) + self.eps)
+        b = s * (0.0 - self.mean.astype(np.float64)) + self.beta.astype(np.float64)
+        return s.astype(np.float32), b.astype(np.float32)
+
+
+def conv2d_nchw(x: np.ndarray, w: np.ndarray, stride: int = 1, pad: int = 0) -> np.ndarray:
+    """``x [N,C,H,W]`` * ``w [F,C,KH,KW]`` -> ``[N,F,OH,OW]`` float32."""
+    n, c, h, wd = x.shape
+    f, c2, kh, kw = w.shape
+    assert c == c2
+    oh = (h + 2 * pad - kh) // stride + 1
+    ow = (wd + 2 * pad - kw) // stride + 1
+    xp = np.zeros((n, c, h + 2 * pad, wd + 2 * pad), np.float64)
+    xp[:, :, pad:pad + h, pad:pad + wd] = x
+    cols = np.empty((n, oh, ow, kh, kw, c), np.float64)
+    for i in range(kh):
+        for j in range(kw):
+            patch = xp[:, :, i:i + stride * oh:stride, j:j + stride * ow:stride]
+            cols[:, :, :, i, j, :] = np.transpose(patch, (0, 2, 3, 1))
+    wk = np.transpose(w.astype(np.float64), (0, 2, 3, 1)).reshape(f, -1)
+    y = cols.reshape(n * oh * ow, -1) @ wk.T
+    return np.ascontiguousarray(
+        np.transpose(y.reshape(n, oh, ow, f), (0, 3, 1, 2))).astype(np.float32)
+
+
+def batchnorm_eval(y: np.ndarray, bn: BNParams) -> np.ndarray:
+    """Eval-mode BatchNorm2d/1d on channel dim 1, float32 result."""
+    shp = (1, -1) + (1,) * (y.ndim - 2)
+    inv = 1.0 / np.sqrt(bn.var.astype(np.float64) + bn.eps)
+    out = (y.astype(np.float64) - bn.mean.reshape(shp)) * (inv * bn.gamma).reshape(shp) \
+        + bn.beta.reshape(shp)
+    return out.astype(np.float32)
+
+
+def multistep_lif(x_seq: np.ndarray, tau: float = 2.0, v_th: float = 1.0,
+                  v_reset: float = 0.0, v0: np.ndarray | None = None,
+                  neuron: str = "lif"):
+    """Run the neuron over ``x_seq [T, ...]`` (float32 arithmetic).
+
+    Returns ``(spikes [T,...], h [T,...] pre-reset membrane, v_final)``.
+    """
+    x_seq = x_seq.astype(np.float32)
+    v = np.zeros_like(x_seq[0]) if v0 is None else v0.astype(np.float32).copy()
+    decay = np.float32(1.0 - 1.0 / tau)
+    tau32 = np.float32(tau)
+    spikes = np.empty_like(x_seq)
+    hs = np.empty_like(x_seq)
+    for t in range(x_seq.shape[0]):
+        if neuron == "lif":
+            v = (v * decay + x_seq[t] / tau32).astype(np.float32)
+        else:
+            v = (v + x_seq[t]).astype(np.float32)
+        hs[t] = v
+        s = ((v - np.float32(v_th)) >= 0).astype(np.float32)
+        v = ((np.float32(1.0) - s) * v + s * np.float32(v_reset)).astype(np.float32)
+        spikes[t] = s
+    return spikes, hs, v
+
+
+def fused_layer(x_seq: np.ndarray, w: np.ndarray, bn: BNParams, *, stride: int = 1,
+                pad: int | None = None, tau: float = 2.0, v_th: float = 1.0,
+                v_reset: float = 0.0, residual: np.ndarray | None = None,
+                neuron: str = "lif", v0: np.ndarray | None = None):
+    """One fused layer over ``x_seq [T,B,C,H,W]``.
+
+    Returns dict with ``out`` (spikes, plus ``residual`` when given),
+    ``spikes``, ``h`` (pre-reset membrane per step), ``v`` (final membrane
+    ``[B,F,OH,OW]``) and ``bn_out`` (BN output per step, the neuron input).
+    """
+    t, b = x_seq.shape[:2]
+    if pad is None:
+        pad = w.shape[2] // 2
+    y = conv2d_nchw(x_seq.reshape((t * b,) + x_seq.shape[2:]), w, stride, pad)
+    z = batchnorm_eval(y, bn).reshape((t, b) + y.shape[1:])
+    spikes, h, v = multistep_lif(z, tau, v_th, v_reset, v0=v0, neuron=neuron)
+    out = spikes if residual is None else (spikes + residual.astype(np.float32))
+    return {"out": out, "spikes": spikes, "h": h, "v": v, "bn_out": z}
+
+
+def make_config0(seed: int = 0, T: int = 4, B: int = 16, C: int = 128, F: int = 128,
+                 H: int = 32, W: int = 32, k: int = 3, p_spike: float = 0.2):
+    """Seeded config-0 style inputs (numpy RNG; shapes per the layer spec).
+
+    Spikes ~ Bernoulli(p); W Kaiming-normal (fan_out, relu gain) then 2:4
+    pruned along C per tap; BN gamma~U(.5,1.5), beta~N(0,.1),
+    mean~N(0,.1), var~U(.5,1.5).
+    """
+    from .pack24 import prune_conv_weight
+    rng = np.random.default_rng(seed)
+    x = (rng.random((T, B, C, H, W)) < p_spike).astype(np.float32)
+    std = np.sqrt(2.0 / (F * k * k))
+    w = (rng.standard_normal((F, C, k, k)) * std).astype(np.float32)
+    w = prune_conv_weight(w)
+    bn = BNParams(gamma=rng.uniform(0.5, 1.5, F).astype(np.float32),
+                  beta=(rng.standard_normal(F) * 0.1).astype(np.float32),
+                  mean=(rng.standard_normal(F) * 0.1).astype(np.float32),
+                  var=rng.uniform(0.5, 1.5, F).astype(np.float32))
+    return x, w, bn
+
+
+def spike_agreement(spk_gpu: np.ndarray, spk_ref: np.ndarray, h_ref: np.ndarray,
+                    v_th: float = 1.0, band: float = 1e-2):
+    """Parity rule for spikes over ``[T, ...]`` arrays.
+
+    Returns ``(fraction_equal, all_explained, n_mismatch, diverged_mask)``.
+    A neuron's FIRST mismatching step must lie at ``|h_ref - v_th| < band``
+    (``h_ref`` = oracle pre-reset membrane); after that step the two
+    trajectories legitimately differ (the reset happened on one side only),
+    so later steps of that neuron are counted but not re-judged.
+    ``diverged_mask`` marks neurons with any mismatch (excluded from the
+    final-membrane comparison).
+    """
+    mism = spk_gpu != spk_ref
+    frac = 1.0 - float(mism.mean()) if mism.size else 1.0
+    near = np.abs(h_ref - v_th) < band
+    seen = np.zeros(mism.shape[1:], bool)
+    ok = True
+    for t in range(mism.shape[0]):
+        first = mism[t] & ~seen
+        if (first & ~near[t]).any():
+            ok = False
+        seen |= mism[t]
+    return frac, ok, int(mism.sum()), seen

@@ -1,0 +1,363 @@
+// C ABI of libsnnb200.so: descriptor validation, tensor-map construction,
+// launches of the fused sparse layer, the dense stem and the classifier head.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+#include <cuda_fp16.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/snn_b200.h"
+#include "snn_conv.cuh"
+#include "snn_glue.cuh"
+
+namespace {
+
+thread_local char g_msg[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_msg, sizeof(g_msg), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+__device__ unsigned g_device_err = 0;
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::mutex g_init_mu;
+bool g_inited = false;
+int g_init_status = SNN_E_NO_DEVICE;
+
+int ensure_init() {
+  std::lock_guard<std::mutex> lk(g_init_mu);
+  if (g_inited) return g_init_status;
+  g_inited = true;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return g_init_status = fail(SNN_E_NO_DEVICE, "cudaGetDevice: %s", cudaGetErrorString(e));
+  cudaDeviceProp prop;
+  e = cudaGetDeviceProperties(&prop, dev);
+  if (e != cudaSuccess) return g_init_status = fail(SNN_E_CUDA, "cudaGetDeviceProperties: %s", cudaGetErrorString(e));
+  if (prop.major != 10 || prop.minor != 0)
+    return g_init_status = fail(SNN_E_NO_DEVICE, "device sm_%d%d is not sm_100", prop.major, prop.minor);
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+  if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
+    return g_init_status = fail(SNN_E_CUDA, "cuTensorMapEncodeTiled unavailable");
+  g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  e = cudaFuncSetAttribute(snn::fused_sparse_conv_lif_kernel,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, snn::kSmemBytes);
+  if (e != cudaSuccess) return g_init_status = fail(SNN_E_CUDA, "smem attribute: %s", cudaGetErrorString(e));
+  return g_init_status = SNN_OK;
+}
+
+struct Geometry {
+  int OH, OW, K, Fpad, n_kb, cin_blocks;
+};
+
+int check_desc(const snn_conv_desc* d, Geometry* g) {
+  if (!d) return fail(SNN_E_INVALID, "null descriptor");
+  if (d->T < 1 || d->B < 1 || d->H < 1 || d->W < 1 || d->Cout < 1 || d->KH < 1 || d->KW < 1)
+    return fail(SNN_E_INVALID, "non-positive dimension");
+  if (d->Cin < 64 || d->Cin % 64)
+    return fail(SNN_E_INVALID, "Cin=%d must be a positive multiple of 64", d->Cin);
+  if (d->stride != 1 && d->stride != 2) return fail(SNN_E_INVALID, "stride must be 1 or 2");
+  if (d->pad < 0 || d->pad >= d->KH || d->pad >= d->KW) return fail(SNN_E_INVALID, "bad pad");
+  if (d->stride == 2 && ((d->H & 1) || (d->W & 1)))
+    return fail(SNN_E_INVALID, "stride-2 layers need even H and W");
+  if (d->neuron < SNN_NEURON_LIF || d->neuron > SNN_NEURON_NONE)
+    return fail(SNN_E_INVALID, "bad neuron kind");
+  if (d->neuron == SNN_NEURON_LIF && !(d->tau > 0.f)) return fail(SNN_E_INVALID, "tau must be > 0");
+  g->OH = (d->H + 2 * d->pad - d->KH) / d->stride + 1;
+  g->OW = (d->W + 2 * d->pad - d->KW) / d->stride + 1;
+  if (g->OH < 1 || g->OW < 1) return fail(SNN_E_INVALID, "empty output");
+  g->K = d->KH * d->KW * d->Cin;
+  g->Fpad = (d->Cout + snn::kBM - 1) / snn::kBM * snn::kBM;
+  g->cin_blocks = d->Cin / snn::kKB;
+  g->n_kb = d->KH * d->KW * g->cin_blocks;
+  if (g->K / 32 > snn::kMaxMetaCols)
+    return fail(SNN_E_INVALID, "K=%d exceeds the %d supported", g->K, snn::kMaxMetaCols * 32);
+  if ((long long)d->T * d->B > 0x7fffffffLL) return fail(SNN_E_INVALID, "T*B too large");
+  return SNN_OK;
+}
+
+size_t meta_offset(const Geometry& g) {
+  size_t vbytes = static_cast<size_t>(g.Fpad) * (g.K / 2) * 2;
+  return (vbytes + 255) & ~static_cast<size_t>(255);
+}
+
+int encode(CUtensorMap* map, int rank, const void* base, const cuuint64_t* dims,
+           const cuuint64_t* strides_bytes, const cuuint32_t* box, CUtensorMapSwizzle swz) {
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, rank, const_cast<void*>(base), dims,
+                        strides_bytes, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SNN_E_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return SNN_OK;
+}
+
+int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, float* state,
+                const float* scale, const float* bias, const void* residual, void* out,
+                void* stream) {
+  int st = ensure_init();
+  if (st) return st;
+  Geometry g;
+  if ((st = check_desc(d, &g))) return st;
+  if (!data || !weight || !scale || !bias || !out) return fail(SNN_E_INVALID, "null tensor pointer");
+  if ((d->flags & (SNN_FLAG_READ_STATE | SNN_FLAG_WRITE_STATE)) && !state)
+    return fail(SNN_E_INVALID, "state flags set but state is null");
+  if (d->neuron == SNN_NEURON_NONE && residual)
+    return fail(SNN_E_INVALID, "residual needs a neuron");
+  if ((reinterpret_cast<uintptr_t>(data) | reinterpret_cast<uintptr_t>(weight)) & 15)
+    return fail(SNN_E_INVALID, "data and weight must be 16-byte aligned");
+
+  snn::ConvParams p;
+  memset(&p, 0, sizeof(p));
+  const char* wbytes = static_cast<const char*>(weight);
+  {  // compressed weights [Fpad][K/2]
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(g.K / 2), static_cast<cuuint64_t>(g.Fpad)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(g.K / 2) * 2};
+    cuuint32_t box[2] = {snn::kKB / 2, snn::kBM};
+    if ((st = encode(&p.tmap_a, 2, wbytes, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B))) return st;
+  }
+  // Tile geometry in output coordinates.
+  int tw, th, tn;
+  if (g.OW >= snn::kBN) { tw = snn::kBN; th = 1; tn = 1; }
+  else if (g.OH * g.OW >= snn::kBN) { tw = g.OW; th = snn::kBN / g.OW; tn = 1; }
+  else { tw = g.OW; th = g.OH; tn = snn::kBN / (g.OH * g.OW); }
+  p.tw = tw; p.th = th; p.tn = tn;
+  p.tiles_w = (g.OW + tw - 1) / tw;
+  p.tiles_h = (g.OH + th - 1) / th;
+  const int tiles_n = (d->B + tn - 1) / tn;
+  p.box_bytes = tw * th * tn * snn::kKB * 2;
+  {
+    const size_t C = d->Cin, W = d->W, H = d->H;
+    const char* base = static_cast<const char*>(data);
+    const int nmaps = d->stride == 2 ? 4 : 1;
+    for (int m = 0; m < nmaps; ++m) {
+      const int hp = m >> 1, wp = m & 1;
+      cuuint64_t dims[4], strides[3];
+      const char* b = base;
+      if (d->stride == 1) {
+        dims[1] = W; dims[2] = H;
+        strides[0] = C * 2; strides[1] = W * C * 2;
+      } else {
+        dims[1] = (W - wp + 1) / 2; dims[2] = (H - hp + 1) / 2;
+        strides[0] = 2 * C * 2; strides[1] = 2 * W * C * 2;
+        b = base + (hp * W + wp) * C * 2;
+      }
+      dims[0] = C;
+      dims[3] = static_cast<cuuint64_t>(d->T) * d->B;
+      strides[2] = H * W * C * 2;
+      cuuint32_t box[4] = {snn::kKB, static_cast<cuuint32_t>(tw), static_cast<cuuint32_t>(th),
+                           static_cast<cuuint32_t>(tn)};
+      if ((st = encode(&p.tmap_b[m], 4, b, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+    }
+  }
+  p.meta = reinterpret_cast<const uint32_t*>(wbytes + meta_offset(g));
+  p.scale = scale; p.bias = bias; p.state = state;
+  p.residual = static_cast<const __half*>(residual);
+  p.out = out;
+  unsigned* err = nullptr;
+  cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_device_err);
+  p.err = err;
+  p.F = d->Cout; p.Cin = d->Cin; p.KW = d->KW; p.stride = d->stride; p.pad = d->pad;
+  p.n_kb = g.n_kb; p.cin_blocks = g.cin_blocks;
+  p.B = d->B; p.OH = g.OH; p.OW = g.OW; p.T = d->T;
+  p.neuron = d->neuron; p.flags = d->flags;
+  p.tau = d->tau; p.decay = 1.0f - 1.0f / d->tau;
+  if (d->neuron == SNN_NEURON_LIF) {
+    // Reference computes (1.0 - 1.0/tau) in double, then float32 (models/neurons.py:125).
+    p.decay = static_cast<float>(1.0 - 1.0 / static_cast<double>(d->tau));
+  }
+  p.v_th = d->v_threshold; p.v_reset = d->v_reset;
+  p.timeout_ns = 1000000000ull;
+
+  dim3 grid(p.tiles_w * p.tiles_h * tiles_n, g.Fpad / snn::kBM);
+  if (grid.x > 0x7fffffffu || grid.y > 65535u) return fail(SNN_E_INVALID, "grid too large");
+  snn::fused_sparse_conv_lif_kernel<<<grid, snn::kThreads, snn::kSmemBytes,
+                                       static_cast<cudaStream_t>(stream)>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));
+  return SNN_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int snn_abi_version(void) { return SNN_ABI_VERSION; }
+
+int snn_init(void) { return ensure_init(); }
+
+const char* snn_last_error_message(void) { return g_msg; }
+
+int snn_conv_out_shape(const snn_conv_desc* d, int32_t* OH, int32_t* OW) {
+  Geometry g;
+  int st = check_desc(d, &g);
+  if (st) return st;
+  if (OH) *OH = g.OH;
+  if (OW) *OW = g.OW;
+  return SNN_OK;
+}
+
+int snn_conv_weight_bytes(const snn_conv_desc* d, size_t* bytes) {
+  Geometry g;
+  int st = check_desc(d, &g);
+  if (st) return st;
+  if (!bytes) return fail(SNN_E_INVALID, "null output");
+  *bytes = meta_offset(g) + static_cast<size_t>(g.Fpad / snn::kBM) * (g.K / 32) * snn::kBM * 4;
+  return SNN_OK;
+}
+
+int snn_pack_weight_24(const snn_conv_desc* d, const float* w, void* blob) {
+  Geometry g;
+  int st = check_desc(d, &g);
+  if (st) return st;
+  if (!w || !blob) return fail(SNN_E_INVALID, "null pointer");
+  const int F = d->Cout, C = d->Cin, KH = d->KH, KW = d->KW, K = g.K;
+  uint8_t* out = static_cast<uint8_t*>(blob);
+  size_t total = 0;
+  snn_conv_weight_bytes(d, &total);
+  memset(out, 0, total);
+  __half* vals = reinterpret_cast<__half*>(out);
+  uint32_t* meta = reinterpret_cast<uint32_t*>(out + meta_offset(g));
+  // Nibble (i0 | i1<<2) per (row, group); padding rows keep (0,1).
+  const int G = K / 4;
+  uint8_t* nib = new uint8_t[static_cast<size_t>(g.Fpad) * G];
+  memset(nib, 0x4, static_cast<size_t>(g.Fpad) * G);
+  for (int f = 0; f < F; ++f) {
+    for (int kh = 0; kh < KH; ++kh) {
+      for (int kw = 0; kw < KW; ++kw) {
+        for (int c0 = 0; c0 < C; c0 += 4) {
+          float v4[4];
+          int nz[4], cnt = 0;
+          for (int i = 0; i < 4; ++i) {
+            v4[i] = w[((static_cast<size_t>(f) * C + c0 + i) * KH + kh) * KW + kw];
+            if (v4[i] != 0.f) nz[cnt++] = i;
+          }
+          if (cnt > 2) {
+            delete[] nib;
+            return fail(SNN_E_NOT_24, "row %d tap (%d,%d) channels %d..%d: %d non-zeros",
+                        f, kh, kw, c0, c0 + 3, cnt);
+          }
+          // Fill with the lowest unused positions.
+          for (int i = 0; cnt < 2 && i < 4; ++i) {
+            bool used = false;
+            for (int j = 0; j < cnt; ++j) used |= (nz[j] == i);
+            if (!used) nz[cnt++] = i;
+          }
+          if (nz[0] > nz[1]) { int t = nz[0]; nz[0] = nz[1]; nz[1] = t; }
+          const int k = (kh * KW + kw) * C + c0;
+          const int grp = k / 4;
+          vals[static_cast<size_t>(f) * (K / 2) + 2 * grp] = __float2half_rn(v4[nz[0]]);
+          vals[static_cast<size_t>(f) * (K / 2) + 2 * grp + 1] = __float2half_rn(v4[nz[1]]);
+          nib[static_cast<size_t>(f) * G + grp] = static_cast<uint8_t>(nz[0] | (nz[1] << 2));
+        }
+      }
+    }
+  }
+  const int J = K / 32;
+  for (int mt = 0; mt < g.Fpad / snn::kBM; ++mt) {
+    for (int j = 0; j < J; ++j) {
+      for (int L = 0; L < snn::kBM; ++L) {
+        const int r0 = mt * snn::kBM + 16 * (L / 16) + L % 8;
+        const int g0 = (32 * j + 16 * ((L / 8) % 2)) / 4;
+        uint32_t word = 0;
+        for (int q = 0; q < 4; ++q) {
+          word |= static_cast<uint32_t>(nib[static_cast<size_t>(r0) * G + g0 + q]) << (4 * q);
+          word |= static_cast<uint32_t>(nib[static_cast<size_t>(r0 + 8) * G + g0 + q]) << (16 + 4 * q);
+        }
+        meta[(static_cast<size_t>(mt) * J + j) * snn::kBM + L] = word;
+      }
+    }
+  }
+  delete[] nib;
+  return SNN_OK;
+}
+
+int snn_conv_forward(const snn_conv_desc* d, const void* data, const void* weight, float* state,
+                     const float* bn_scale, const float* bn_bias, void* out, void* stream) {
+  return launch_conv(d, data, weight, state, bn_scale, bn_bias, nullptr, out, stream);
+}
+
+int snn_conv_forward_res(const snn_conv_desc* d, const void* data, const void* weight,
+                         float* state, const float* bn_scale, const float* bn_bias,
+                         const void* residual, void* out, void* stream) {
+  if (!residual) return fail(SNN_E_INVALID, "null residual");
+  return launch_conv(d, data, weight, state, bn_scale, bn_bias, residual, out, stream);
+}
+
+int snn_stem_forward(const snn_conv_desc* d, int32_t Tin, const float* x, const float* w,
+                     const float* bn_scale, const float* bn_bias, void* out, void* stream) {
+  int st = ensure_init();
+  if (st) return st;
+  if (!d || !x || !w || !bn_scale || !bn_bias || !out) return fail(SNN_E_INVALID, "null pointer");
+  if (d->T < 1 || d->B < 1 || d->Cin < 1 || d->Cin > 16 || d->Cout < 1 || d->Cout > 1024 ||
+      d->KH < 1 || d->KW < 1 || d->KH * d->KW * d->Cin > 192 || d->stride < 1 || d->pad < 0)
+    return fail(SNN_E_INVALID, "unsupported stem geometry");
+  if (Tin != 1 && Tin != d->T) return fail(SNN_E_INVALID, "Tin must be 1 or T");
+  if (d->neuron == SNN_NEURON_NONE) return fail(SNN_E_INVALID, "stem needs a neuron");
+  const int OH = (d->H + 2 * d->pad - d->KH) / d->stride + 1;
+  const int OW = (d->W + 2 * d->pad - d->KW) / d->stride + 1;
+  if (OH < 1 || OW < 1) return fail(SNN_E_INVALID, "empty output");
+  snn::StemParams p;
+  p.x = x; p.w = w; p.scale = bn_scale; p.bias = bn_bias;
+  p.out = static_cast<__half*>(out);
+  p.T = d->T; p.Tin = Tin; p.B = d->B; p.Cin = d->Cin; p.H = d->H; p.W = d->W;
+  p.Cout = d->Cout; p.KH = d->KH; p.KW = d->KW; p.stride = d->stride; p.pad = d->pad;
+  p.OH = OH; p.OW = OW; p.neuron = d->neuron;
+  p.tau = d->tau; p.decay = static_cast<float>(1.0 - 1.0 / static_cast<double>(d->tau));
+  p.v_th = d->v_threshold; p.v_reset = d->v_reset;
+  const long long pixels = static_cast<long long>(d->B) * OH * OW;
+  const int px_per_block = 4;
+  dim3 block(64, px_per_block);
+  dim3 grid(static_cast<unsigned>((pixels + px_per_block - 1) / px_per_block),
+            (d->Cout + 63) / 64);
+  const size_t smem = static_cast<size_t>(64) * d->KH * d->KW * d->Cin * sizeof(float);
+  snn::stem_conv_lif_kernel<<<grid, block, smem, static_cast<cudaStream_t>(stream)>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));
+  return SNN_OK;
+}
+
+int snn_head_forward(int32_t T, int32_t B, int32_t HW, int32_t C, int32_t NC, const void* x,
+                     const float* fc_w, const float* fc_b, float* logits, void* stream) {
+  int st = ensure_init();
+  if (st) return st;
+  if (!x || !fc_w || !logits) return fail(SNN_E_INVALID, "null pointer");
+  if (T < 1 || B < 1 || HW < 1 || C < 1 || C > 4096 || NC < 1)
+    return fail(SNN_E_INVALID, "bad head shape");
+  const int threads = 256;
+  const size_t smem = static_cast<size_t>(C) * sizeof(float);
+  snn::head_pool_fc_kernel<<<B, threads, smem, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __half*>(x), fc_w, fc_b, logits, T, B, HW, C, NC);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));
+  return SNN_OK;
+}
+
+int snn_get_device_error(uint32_t* code, int reset) {
+  int st = ensure_init();
+  if (st) return st;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return fail(SNN_E_CUDA, "synchronize: %s", cudaGetErrorString(e));
+  unsigned v = 0;
+  e = cudaMemcpyFromSymbol(&v, g_device_err, sizeof(v));
+  if (e != cudaSuccess) return fail(SNN_E_CUDA, "read error word: %s", cudaGetErrorString(e));
+  if (code) *code = v;
+  if (reset) {
+    unsigned z = 0;
+    e = cudaMemcpyToSymbol(g_device_err, &z, sizeof(z));
+    if (e != cudaSuccess) return fail(SNN_E_CUDA, "clear error word: %s", cudaGetErrorString(e));
+  }
+  return SNN_OK;
+}
+
+}  // extern "C"

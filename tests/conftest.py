@@ -1,0 +1,37 @@
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+GOLDEN = ROOT / "tests" / "golden"
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+LAYER_CASES = ["c3s1", "c3s2", "c1s2", "c3res", "c3f64", "c3if", "lin"]
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a B200 (sm_100a) GPU")
+
+
+def load_layer_case(name):
+    g = dict(np.load(GOLDEN / f"layer_{name}.npz"))
+    T, B, C, F, H, W, k, s, pad, islif, lin = (int(v) for v in g["meta"])
+    g.update(T=T, B=B, C=C, F=F, H=H, W=W, k=k, stride=s, pad=pad,
+             neuron="lif" if islif else "if", linear=bool(lin))
+    return g
+
+
+@pytest.fixture(scope="session")
+def cuda_device():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    major, minor = torch.cuda.get_device_capability(0)
+    if (major, minor) != (10, 0):
+        pytest.skip(f"device sm_{major}{minor} is not sm_100")
+    from sparsesnn_b200 import build
+    build.build()
+    return torch.device("cuda:0")

@@ -1,0 +1,192 @@
+"""Generate golden fixtures by running the REAL reference PyTorch path.
+
+Run in a container that has the reference checkout (it is not needed at
+test time and never on the GPU box):
+
+    python tests/golden/make_golden.py --ref /path/to/SparseSNN
+
+It imports the reference's own modules -- ``sparse/pruning.py``
+(``prune_2_4``), ``models/neurons.py`` (``MultiStepLIFNeuron`` /
+``MultiStepIFNeuron``), ``models/layers.py`` (``SeqToANNContainer``) and
+``models/sewresnet.py`` (``sew_resnet18``) -- and records, for small seeded
+cases, the inputs, the reference-pruned weights, BN parameters and the
+reference outputs (spikes, pre-reset membrane per step, final membrane).
+The files it writes are committed next to this script and read by
+``tests/test_oracle_golden.py`` and the GPU parity tests.
+"""
+from __future__ import annotations
+
+import argparse
+import sys
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+
+
+def layer_case(ref, name, *, T, B, C, F, H, W, k, stride, pad, neuron="lif", x_max=1,
+               residual=False, seed=0, linear=False):
+    import torch
+    import torch.nn as nn
+    prune_2_4 = ref["prune_2_4"]
+    SeqToANNContainer = ref["SeqToANNContainer"]
+    g = torch.Generator().manual_seed(seed)
+    if x_max == 1:
+        x = (torch.rand((T, B, C, H, W), generator=g) < 0.2).float()
+    else:
+        x = torch.randint(0, x_max + 1, (T, B, C, H, W), generator=g).float()
+    std = (2.0 / (F * k * k)) ** 0.5
+    w = torch.randn((F, C, k, k), generator=g) * std
+    w = prune_2_4(w.permute(0, 2, 3, 1)).permute(0, 3, 1, 2).contiguous()
+    gamma = torch.rand(F, generator=g) + 0.5
+    beta = torch.randn(F, generator=g) * 0.1
+    mean = torch.randn(F, generator=g) * 0.1
+    var = torch.rand(F, generator=g) + 0.5
+    lin_bias = (torch.randn(F, generator=g) * 0.05) if linear else None
+
+    if linear:
+        # Spikformer MLP/SSA projection: Linear + BatchNorm1d + LIF on (T,B,N,C)
+        # (models/spikformer.py:63-71).  Tokens are the H*W positions.
+        lin = nn.Linear(C, F)
+        lin.weight.data.copy_(w[:, :, 0, 0])
+        lin.bias.data.copy_(lin_bias)
+        bnm = nn.BatchNorm1d(F)
+        bnm.weight.data.copy_(gamma); bnm.bias.data.copy_(beta)
+        bnm.running_mean.copy_(mean); bnm.running_var.copy_(var)
+        lin.eval(); bnm.eval()
+        xs = x.flatten(3).transpose(2, 3)                 # (T,B,N,C)
+        with torch.no_grad():
+            z = lin(xs.flatten(0, 1))
+            z = bnm(z.transpose(-1, -2)).transpose(-1, -2).reshape(T, B, H * W, F)
+            z = z.transpose(2, 3).reshape(T, B, F, H, W)  # back to (T,B,F,H,W)
+    else:
+        conv = nn.Conv2d(C, F, k, stride=stride, padding=pad, bias=False)
+        conv.weight.data.copy_(w)
+        bnm = nn.BatchNorm2d(F)
+        bnm.weight.data.copy_(gamma); bnm.bias.data.copy_(beta)
+        bnm.running_mean.copy_(mean); bnm.running_var.copy_(var)
+        seq = SeqToANNContainer(conv, bnm).eval()
+        with torch.no_grad():
+            z = seq(x)
+    neuron_mod = ref["MultiStepLIFNeuron"](tau=2.0, v_threshold=1.0, v_reset=0.0) \
+        if neuron == "lif" else ref["MultiStepIFNeuron"](v_threshold=1.0, v_reset=0.0)
+    cell = neuron_mod.neuron
+    cell.reset()
+    spikes, hs = [], []
+    with torch.no_grad():
+        for t in range(T):
+            # Same steps as the cell's forward, recording the pre-reset membrane.
+            if neuron == "lif":
+                cell.neuronal_charge(z[t])
+                hs.append(cell.v.clone())
+                s = cell.neuronal_fire()
+                cell.neuronal_reset(s)
+            else:
+                s = cell(z[t])
+                # IF: v after charge equals v_reset where it fired, else kept v.
+                hs.append(None)
+            spikes.append(s)
+        v_final = cell.v.clone()
+        # Cross-check against the unmodified multi-step module.
+        ref_spk = neuron_mod(z)
+    spikes = torch.stack(spikes)
+    assert torch.equal(spikes, ref_spk)
+    if neuron != "lif":
+        # Recompute h for IF with the same float32 ops as IFNeuron.forward.
+        v = torch.zeros_like(z[0]); hs = []
+        for t in range(T):
+            v = v + z[t]; hs.append(v.clone())
+            sp = (v - 1.0).ge(0).float(); v = (1.0 - sp) * v + sp * 0.0
+    h = torch.stack(hs)
+    out = {"x": x.numpy().astype(np.uint8), "w": w.numpy(), "gamma": gamma.numpy(),
+           "beta": beta.numpy(), "mean": mean.numpy(), "var": var.numpy(),
+           "spikes": spikes.numpy().astype(np.uint8), "h": h.numpy(),
+           "v": v_final.numpy(), "bn_out": z.numpy(),
+           "meta": np.array([T, B, C, F, H, W, k, stride, pad, int(neuron == "lif"),
+                             int(linear)], np.int64)}
+    if linear:
+        out["lin_bias"] = lin_bias.numpy()
+    if residual:
+        r = torch.randint(0, 3, spikes.shape, generator=g).float()
+        out["residual"] = r.numpy().astype(np.uint8)
+        out["out"] = (spikes + r).numpy().astype(np.uint8)
+    np.savez_compressed(HERE / f"layer_{name}.npz", **out)
+    print("wrote", name, {k: v.shape for k, v in out.items()})
+
+
+def prune_case(ref):
+    import torch
+    g = torch.Generator().manual_seed(7)
+    w = torch.randn((16, 8, 3, 3), generator=g)
+    p = ref["prune_2_4"](w.permute(0, 2, 3, 1)).permute(0, 3, 1, 2).contiguous()
+    w2 = torch.randn((6, 10), generator=g)          # last dim not a multiple of 4
+    p2 = ref["prune_2_4"](w2)
+    np.savez_compressed(HERE / "prune.npz", w=w.numpy(), pruned=p.numpy(), w2=w2.numpy(),
+                        pruned2=p2.numpy())
+    print("wrote prune")
+
+
+def model_case(ref, repo):
+    """SEW-ResNet-18 CIFAR-stem logits from the reference model class."""
+    import torch
+    import torch.nn as nn
+    sys.path.insert(0, str(repo))
+    from oracle.sew_resnet import make_params, make_input
+    P = make_params(seed=0)
+    m = ref["sew_resnet18"](in_channels=3, neuron_type="lif", num_classes=100, T=4)
+    m.conv1 = nn.Conv2d(3, 64, 3, 1, 1, bias=False)
+    m.maxpool = nn.Identity()
+    t = torch.from_numpy
+
+    def set_bn(bnm, p):
+        bnm.weight.data.copy_(t(p["gamma"])); bnm.bias.data.copy_(t(p["beta"]))
+        bnm.running_mean.copy_(t(p["mean"])); bnm.running_var.copy_(t(p["var"]))
+
+    m.conv1.weight.data.copy_(t(P["stem"]["w"])); set_bn(m.bn1, P["stem"]["bn"])
+    blocks = [b for layer in (m.layer1, m.layer2, m.layer3, m.layer4) for b in layer]
+    for blk, p in zip(blocks, P["blocks"]):
+        blk.conv1.module[0].weight.data.copy_(t(p["w1"])); set_bn(blk.conv1.module[1], p["bn1"])
+        blk.conv2.module[0].weight.data.copy_(t(p["w2"])); set_bn(blk.conv2.module[1], p["bn2"])
+        if "wd" in p:
+            ds = blk.downsample[0].module
+            ds[0].weight.data.copy_(t(p["wd"])); set_bn(ds[1], p["bnd"])
+    m.fc.weight.data.copy_(t(P["fc_w"])); m.fc.bias.data.copy_(t(P["fc_b"]))
+    m.eval()
+    x = make_input(seed=0, B=2)
+    with torch.no_grad():
+        logits = m(t(x)).numpy()
+    np.savez_compressed(HERE / "sew18_logits.npz", x=x, logits=logits)
+    print("wrote sew18 logits", logits.shape)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", required=True, help="path of the SparseSNN reference checkout")
+    a = ap.parse_args()
+    sys.path.insert(0, a.ref)
+    from sparse.pruning import prune_2_4
+    from models.neurons import MultiStepLIFNeuron, MultiStepIFNeuron
+    from models.layers import SeqToANNContainer
+    from models.sewresnet import sew_resnet18
+    ref = dict(prune_2_4=prune_2_4, MultiStepLIFNeuron=MultiStepLIFNeuron,
+               MultiStepIFNeuron=MultiStepIFNeuron, SeqToANNContainer=SeqToANNContainer,
+               sew_resnet18=sew_resnet18)
+    import torch
+    torch.set_num_threads(4)
+    prune_case(ref)
+    layer_case(ref, "c3s1", T=4, B=2, C=64, F=128, H=8, W=8, k=3, stride=1, pad=1, seed=1)
+    layer_case(ref, "c3s2", T=2, B=2, C=64, F=128, H=8, W=8, k=3, stride=2, pad=1, seed=2)
+    layer_case(ref, "c1s2", T=4, B=2, C=64, F=128, H=8, W=8, k=1, stride=2, pad=0, seed=3)
+    layer_case(ref, "c3res", T=4, B=2, C=128, F=128, H=4, W=4, k=3, stride=1, pad=1, x_max=2,
+               residual=True, seed=4)
+    layer_case(ref, "c3f64", T=4, B=2, C=64, F=64, H=8, W=8, k=3, stride=1, pad=1, seed=5)
+    layer_case(ref, "c3if", T=4, B=2, C=64, F=128, H=8, W=8, k=3, stride=1, pad=1, neuron="if",
+               seed=6)
+    layer_case(ref, "lin", T=4, B=2, C=128, F=256, H=4, W=4, k=1, stride=1, pad=0, seed=8,
+               linear=True)
+    model_case(ref, HERE.parent.parent)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,74 @@
+"""The C-ABI library loads and exports every symbol include/snn_b200.h
+declares; descriptor validation works without a GPU."""
+import ctypes
+import re
+import subprocess
+
+import pytest
+
+from conftest import ROOT
+from sparsesnn_b200 import build, runtime as rt
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _lib():
+    build.build()
+    return rt.load()
+
+
+def header_functions():
+    text = (ROOT / "include" / "snn_b200.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(snn_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_exports_every_declared_symbol(_lib):
+    names = header_functions()
+    assert names and set(names) == set(rt.EXPORTED)
+    out = subprocess.run(["nm", "-D", "--defined-only", str(rt.LIB_PATH)],
+                         capture_output=True, text=True, check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if line.strip()}
+    for n in names:
+        assert n in exported, n
+        assert hasattr(_lib, n)
+
+
+def test_abi_version(_lib):
+    assert _lib.snn_abi_version() == 1
+
+
+def test_desc_struct_layout():
+    assert ctypes.sizeof(rt.SnnConvDesc) == 15 * 4
+
+
+@pytest.mark.parametrize("kw, msg", [
+    (dict(Cin=48), "multiple of 64"),
+    (dict(stride=3), "stride"),
+    (dict(H=9, stride=2), "even"),
+    (dict(Cin=64 * 150), "exceeds"),
+])
+def test_invalid_descriptors(kw, msg):
+    base = dict(T=4, B=2, Cin=64, H=8, W=8, Cout=128, KH=3, KW=3)
+    base.update(kw)
+    d = rt.make_desc(**base)
+    with pytest.raises(rt.SnnError) as e:
+        rt.weight_bytes(d)
+    assert e.value.code == rt.SNN_E_INVALID and msg in str(e.value)
+
+
+def test_out_shape_and_weight_bytes():
+    d = rt.make_desc(T=4, B=16, Cin=128, H=32, W=32, Cout=128, KH=3, KW=3)
+    assert rt.out_shape(d) == (32, 32)
+    # values 128 x 576 fp16 + meta 1 x 36 x 128 words
+    assert rt.weight_bytes(d) == 128 * 576 * 2 + 36 * 128 * 4
+    d = rt.make_desc(T=4, B=16, Cin=64, H=32, W=32, Cout=128, KH=1, KW=1, stride=2, pad=0)
+    assert rt.out_shape(d) == (16, 16)
+
+
+def test_forward_without_device_fails_loudly(_lib):
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    d = rt.make_desc(T=1, B=1, Cin=64, H=8, W=8, Cout=128, KH=3, KW=3)
+    rc = _lib.snn_conv_forward(d, 16, 16, None, 16, 16, 16, None)
+    assert rc in (rt.SNN_E_NO_DEVICE, rt.SNN_E_CUDA)

@@ -1,0 +1,236 @@
+"""GPU parity of the fused 2:4-sparse Conv/Linear + BN + LIF layer.
+
+Checks, on every reference golden case and at the config-0 full size:
+* spikes agree at >= 99.5% of positions, and every neuron's first mismatch
+  lies at |h - v_th| < 1e-2 (h = reference pre-reset membrane);
+* final membrane within rtol 1e-2 (+ atol 1e-3) on neurons whose spike
+  trains agree;
+* BN pre-activations (neuron disabled) within the error of FP16 weight
+  rounding of the fp32 reference, and within 1e-5 relative of the oracle
+  run with the same FP16-rounded weights (accumulation order only).
+"""
+import numpy as np
+import pytest
+
+from conftest import LAYER_CASES, load_layer_case
+from oracle import lif_layer as L
+
+pytestmark = pytest.mark.gpu
+
+V_RTOL, V_ATOL = 1e-2, 1e-3
+SPIKE_MIN_AGREE = 0.995
+
+
+def to_nhwc(x_tbchw):
+    t, b, c, h, w = x_tbchw.shape
+    return np.ascontiguousarray(np.transpose(x_tbchw, (0, 1, 3, 4, 2)).reshape(t * b, h, w, c))
+
+
+def from_nhwc(y, T, B):
+    tb, oh, ow, f = y.shape
+    return np.transpose(y.reshape(T, B, oh, ow, f), (0, 1, 4, 2, 3))
+
+
+def build_layer(g, neuron=None, device="cuda"):
+    from sparsesnn_b200.layer import SparseConvBNLIF, fold_bn
+    mean = g["mean"] - g["lin_bias"] if g["linear"] else g["mean"]
+    scale, bias = fold_bn(g["gamma"], g["beta"], mean, g["var"])
+    neuron = neuron or g["neuron"]
+    if g["linear"]:
+        # Spikformer Linear over N = H*W tokens: rows = B*N, one "image" row.
+        return SparseConvBNLIF(g["w"][:, :, 0, 0], scale, bias, T=g["T"], B=1, H=1,
+                               W=g["B"] * g["H"] * g["W"], neuron=neuron, device=device)
+    return SparseConvBNLIF(g["w"], scale, bias, T=g["T"], B=g["B"], H=g["H"], W=g["W"],
+                           stride=g["stride"], pad=g["pad"], neuron=neuron, device=device)
+
+
+def layer_input(g):
+    x = g["x"].astype(np.float32)
+    if g["linear"]:
+        T, B, C = x.shape[:3]
+        tok = np.transpose(x.reshape(T, B, C, -1), (0, 1, 3, 2))       # (T,B,N,C)
+        return np.ascontiguousarray(tok.reshape(T, 1, B * tok.shape[2], C))
+    return to_nhwc(x)
+
+
+def run_case(g, neuron=None, residual=None):
+    import torch
+    from sparsesnn_b200 import runtime as rt
+    layer = build_layer(g, neuron)
+    x = torch.from_numpy(layer_input(g)).to("cuda", torch.float16)
+    state = torch.full(layer.state_shape(), 123.0, dtype=torch.float32, device="cuda")
+    res = None
+    if residual is not None:
+        res = torch.from_numpy(to_nhwc(residual.astype(np.float32))).to("cuda", torch.float16)
+    out = layer(x, state=state, residual=res, read_state=False)
+    torch.cuda.synchronize()
+    assert rt.device_error() == 0
+    return out.float().cpu().numpy(), state.cpu().numpy(), layer
+
+
+def unflatten(g, y, state=None):
+    """Kernel layouts -> reference layouts: y (T,B,F,OH,OW), v (B,F,OH,OW)."""
+    T, B, F = g["T"], g["B"], g["F"]
+    if g["linear"]:
+        H, W = g["H"], g["W"]
+        ys = np.transpose(y.reshape(T, B, H, W, F), (0, 1, 4, 2, 3))
+    else:
+        ys = from_nhwc(y, T, B)
+    oh, ow = ys.shape[3:]
+    v = None if state is None else np.transpose(state.reshape(B, oh, ow, F), (0, 3, 1, 2))
+    return ys, v
+
+
+def check_spikes_and_v(spk, v, ref_spk, ref_h, ref_v):
+    frac, explained, nmis, diverged = L.spike_agreement(spk, ref_spk, ref_h)
+    assert frac >= SPIKE_MIN_AGREE, f"spike agreement {frac:.5f}"
+    assert explained, "a spike mismatch lies away from the threshold band"
+    keep = ~diverged
+    err = np.abs(v - ref_v)[keep]
+    assert (err <= V_RTOL * np.abs(ref_v[keep]) + V_ATOL).all(), f"max v err {err.max()}"
+    return frac, nmis
+
+
+@pytest.mark.parametrize("name", LAYER_CASES)
+def test_golden_layer_parity(cuda_device, name):
+    g = load_layer_case(name)
+    res = g.get("residual")
+    y, state, _ = run_case(g, residual=res)
+    ys, v = unflatten(g, y, state)
+    if res is not None:
+        spk = ys - res.astype(np.float32)
+        assert np.isin(spk, (0.0, 1.0)).all()
+        assert np.isin(ys, (0, 1, 2, 3)).all()
+    else:
+        spk = ys
+        assert np.isin(spk, (0.0, 1.0)).all()
+    check_spikes_and_v(spk, v, g["spikes"].astype(np.float32), g["h"], g["v"])
+
+
+@pytest.mark.parametrize("name", ["c3s1", "c3s2", "c1s2", "c3res", "lin"])
+def test_golden_preactivation(cuda_device, name):
+    g = load_layer_case(name)
+    y, _, _ = run_case(g, neuron="none")
+    z, _ = unflatten(g, y)
+    ref = g["bn_out"]
+    # vs the fp32 reference: FP16 weight rounding bounds the error.
+    scale = np.abs(ref).max()
+    assert np.abs(z - ref).max() <= 5e-3 * scale
+    # vs the oracle on FP16-rounded weights: accumulation order only.
+    w16 = g["w"].astype(np.float16).astype(np.float32)
+    mean = g["mean"] - g["lin_bias"] if g["linear"] else g["mean"]
+    bn = L.BNParams(g["gamma"], g["beta"], mean, g["var"])
+    x = g["x"].astype(np.float32)
+    if g["linear"]:
+        r = L.fused_layer(x, w16, bn, stride=1, pad=0)["bn_out"]
+    else:
+        r = L.fused_layer(x, w16, bn, stride=g["stride"], pad=g["pad"])["bn_out"]
+    assert np.abs(z - r).max() <= 1e-5 * max(scale, 1.0)
+
+
+def test_state_read_and_two_calls(cuda_device):
+    """Running T=4 as two T=2 calls with the membrane carried through state
+    equals one T=4 call (reads v0 from state, writes final v)."""
+    import torch
+    g = load_layer_case("c3s1")
+    full, state_full, _ = run_case(g)
+    g2 = dict(g, T=2)
+    layer = build_layer(g2)
+    x = torch.from_numpy(layer_input(g)).to("cuda", torch.float16)
+    half = x.shape[0] // 2
+    state = torch.zeros(layer.state_shape(), dtype=torch.float32, device="cuda")
+    o1 = layer(x[:half].contiguous(), state=state)
+    o2 = layer(x[half:].contiguous(), state=state)
+    torch.cuda.synchronize()
+    got = torch.cat([o1, o2]).float().cpu().numpy()
+    assert np.array_equal(got, full)
+    assert np.array_equal(state.cpu().numpy(), state_full)
+
+
+def test_long_t_chunking(cuda_device):
+    """T=10 (> 4 timesteps per tensor-memory chunk) against the oracle."""
+    import torch
+    g = load_layer_case("c3s1")
+    rng = np.random.default_rng(11)
+    T = 10
+    x = (rng.random((T, g["B"], g["C"], g["H"], g["W"])) < 0.2).astype(np.float32)
+    gg = dict(g, T=T, x=x)
+    y, state, _ = run_case(gg)
+    ys, v = unflatten(gg, y, state)
+    bn = L.BNParams(g["gamma"], g["beta"], g["mean"], g["var"])
+    r = L.fused_layer(x, g["w"], bn, stride=1, pad=1)
+    check_spikes_and_v(ys, v, r["spikes"], r["h"], r["v"])
+
+
+def _torch_reference(x_tbchw, w, scale, bias, stride, pad, tau=2.0, v_th=1.0):
+    """Plain PyTorch fp32 reference of the same op (TF32 off), on the GPU."""
+    import torch
+    import torch.nn.functional as F
+    torch.backends.cudnn.allow_tf32 = False
+    torch.backends.cuda.matmul.allow_tf32 = False
+    T, B = x_tbchw.shape[:2]
+    z = F.conv2d(x_tbchw.flatten(0, 1), w, stride=stride, padding=pad)
+    z = z * scale[None, :, None, None] + bias[None, :, None, None]
+    z = z.view(T, B, *z.shape[1:])
+    v = torch.zeros_like(z[0])
+    spk, hs = [], []
+    for t in range(T):
+        v = v * (1.0 - 1.0 / tau) + z[t] / tau
+        hs.append(v)
+        s = (v - v_th).ge(0).float()
+        v = (1.0 - s) * v
+        spk.append(s)
+    return torch.stack(spk), torch.stack(hs), v
+
+
+def test_config0_full_size(cuda_device):
+    """Config 0: 3x3 s1 p1, Cin=Cout=128, 32x32, B=16, T=4."""
+    import torch
+    from sparsesnn_b200.layer import SparseConvBNLIF, fold_bn
+    x, w, bn = L.make_config0(seed=0)
+    scale, bias = fold_bn(bn.gamma, bn.beta, bn.mean, bn.var)
+    layer = SparseConvBNLIF(w, scale, bias, T=4, B=16, H=32, W=32)
+    xd = torch.from_numpy(to_nhwc(x)).to("cuda", torch.float16)
+    state = torch.zeros(layer.state_shape(), dtype=torch.float32, device="cuda")
+    y = layer(xd, state=state, read_state=False)
+    torch.cuda.synchronize()
+    from sparsesnn_b200 import runtime as rt
+    assert rt.device_error() == 0
+    xt = torch.from_numpy(x).cuda()
+    spk, h, v = _torch_reference(xt, torch.from_numpy(w).cuda(), torch.from_numpy(scale).cuda(),
+                                 torch.from_numpy(bias).cuda(), 1, 1)
+    ys = from_nhwc(y.float().cpu().numpy(), 4, 16)
+    vg = np.transpose(state.cpu().numpy().reshape(16, 32, 32, 128), (0, 3, 1, 2))
+    frac, nmis = check_spikes_and_v(ys, vg, spk.cpu().numpy(), h.cpu().numpy(), v.cpu().numpy())
+    print(f"config0 spike agreement {frac:.6f} ({nmis} mismatches)")
+
+
+def test_size_independent_properties(cuda_device):
+    """Large-batch properties: outputs are exact {0,1}, a zero input gives the
+    BN-bias-only trajectory, and batch images are independent (permuting the
+    batch permutes the output)."""
+    import torch
+    from sparsesnn_b200.layer import SparseConvBNLIF, fold_bn
+    x, w, bn = L.make_config0(seed=1, B=32, C=256, F=256, H=16, W=16)
+    scale, bias = fold_bn(bn.gamma, bn.beta, bn.mean, bn.var)
+    layer = SparseConvBNLIF(w, scale, bias, T=4, B=32, H=16, W=16)
+    xd = torch.from_numpy(to_nhwc(x)).to("cuda", torch.float16)
+    y = layer(xd)
+    perm = torch.randperm(32, generator=torch.Generator().manual_seed(0))
+    xp = xd.view(4, 32, 16, 16, 256)[:, perm].reshape_as(xd).contiguous()
+    yp = layer(xp)
+    torch.cuda.synchronize()
+    assert torch.equal(y.view(4, 32, 16, 16, 256)[:, perm], yp.view(4, 32, 16, 16, 256))
+    assert set(torch.unique(y).tolist()) <= {0.0, 1.0}
+    y0 = layer(torch.zeros_like(xd))
+    torch.cuda.synchronize()
+    # zero input: every pixel of a channel follows the same bias-driven trajectory
+    y0 = y0.view(4, -1, 256).float()
+    assert torch.equal(y0.amax(dim=1), y0.amin(dim=1))
+    z = torch.from_numpy(bias)
+    v = torch.zeros_like(z)
+    for t in range(4):
+        v = v * 0.5 + z / 2.0
+        s = (v - 1.0).ge(0).float()
+        v = (1.0 - s) * v
+        assert torch.equal(y0[t, 0].cpu(), s)

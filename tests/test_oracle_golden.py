@@ -1,0 +1,72 @@
+"""The oracle is pinned to fixtures made by the real reference PyTorch path.
+
+Fixtures: ``tests/golden/make_golden.py`` (imports the reference's
+``sparse/pruning.py``, ``models/neurons.py``, ``models/layers.py`` and
+``models/sewresnet.py``).
+"""
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, LAYER_CASES, load_layer_case
+from oracle import lif_layer as L
+from oracle import pack24 as P
+
+
+def test_prune_matches_reference():
+    d = np.load(GOLDEN / "prune.npz")
+    assert np.array_equal(P.prune_conv_weight(d["w"]), d["pruned"])
+    assert np.array_equal(P.prune_2_4(d["w2"]), d["pruned2"])   # padded last dim
+
+
+@pytest.mark.parametrize("name", LAYER_CASES)
+def test_layer_matches_reference(name):
+    g = load_layer_case(name)
+    x = g["x"].astype(np.float32)
+    if g["linear"]:
+        # Linear bias enters like a shifted BN mean: bn(Wx + b) == bn'(Wx).
+        bn = L.BNParams(g["gamma"], g["beta"], g["mean"] - g["lin_bias"], g["var"])
+    else:
+        bn = L.BNParams(g["gamma"], g["beta"], g["mean"], g["var"])
+    res = g.get("residual")
+    r = L.fused_layer(x, g["w"], bn, stride=g["stride"], pad=g["pad"], neuron=g["neuron"],
+                      residual=None if res is None else res.astype(np.float32))
+    # float64-accumulated conv vs the reference's float32 conv: a few ulps.
+    np.testing.assert_allclose(r["bn_out"], g["bn_out"], rtol=0, atol=1e-5)
+    np.testing.assert_allclose(r["h"], g["h"], rtol=0, atol=1e-5)
+    np.testing.assert_allclose(r["v"], g["v"], rtol=0, atol=1e-5)
+    frac, explained, _, _ = L.spike_agreement(r["spikes"], g["spikes"].astype(np.float32), g["h"])
+    assert frac == 1.0 and explained
+    if res is not None:
+        assert np.array_equal(r["out"], g["out"].astype(np.float32))
+
+
+def test_sew18_forward_matches_reference_model():
+    from oracle.sew_resnet import forward_torch, make_params
+    m = np.load(GOLDEN / "sew18_logits.npz")
+    logits = forward_torch(make_params(0), m["x"], T=4)
+    np.testing.assert_allclose(logits, m["logits"], rtol=0, atol=1e-6)
+
+
+def test_bn_fold_matches_batchnorm():
+    rng = np.random.default_rng(0)
+    f = 32
+    bn = L.BNParams(rng.uniform(0.5, 1.5, f).astype(np.float32),
+                    (rng.standard_normal(f) * 0.1).astype(np.float32),
+                    (rng.standard_normal(f) * 0.1).astype(np.float32),
+                    rng.uniform(0.5, 1.5, f).astype(np.float32))
+    y = rng.standard_normal((3, f, 5, 5)).astype(np.float32)
+    s, b = bn.scale_bias()
+    np.testing.assert_allclose(y * s[None, :, None, None] + b[None, :, None, None],
+                               L.batchnorm_eval(y, bn), rtol=1e-6, atol=1e-6)
+
+
+def test_spike_agreement_rule_flags_far_mismatch():
+    # A planted mismatch far from threshold must be rejected; one near the
+    # threshold is accepted, and later steps of a diverged neuron are ignored.
+    h = np.array([[0.2, 0.995], [0.3, 0.4]], np.float32)      # [T=2, N=2]
+    ref = (h >= 1.0).astype(np.float32)
+    near = ref.copy(); near[0, 1] = 1.0; near[1, 1] = 1.0
+    frac, ok, n, div = L.spike_agreement(near, ref, h)
+    assert ok and n == 2 and div.tolist() == [False, True]
+    far = ref.copy(); far[0, 0] = 1.0
+    assert not L.spike_agreement(far, ref, h)[1]
