@@ -1,0 +1,313 @@
+"""SEW-ResNet-18 (T=4, CIFAR 32x32, batch 128 per GPU) inference throughput.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One process per GPU (torchrun for N > 1), one model replica per GPU, batch 128
+per GPU (weak scaling), NCCL all-gather of the logits each step (the only
+collective, as in the data-parallel design).  Prints ONE JSON line on rank 0.
+
+* value: images/s of the whole job, inputs resident in HBM, each step = one
+  CUDA-graph replay of the forward (+ logits gather when N > 1), timed with
+  CUDA events between barriers, max over ranks.
+* e2e: the same through the public call ``model(x_host)`` with the input
+  copied from pinned host memory and the logits read back to host every step.
+* roofline: the fused sparse conv kernel (19 launches per forward), timed
+  with CUDA events around each launch over K eager forwards run right after
+  the timed region; FLOPs are dense-equivalent 2*M*N*K.
+* cpu_baseline (rank 0, N = 1): the CPU port of the reference PyTorch path
+  (``oracle/sew_resnet.py``) on a bounded sample of images, all host threads.
+* --impl reference: only that CPU path, as the reference arm.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "SEW-ResNet-18 T=4 images/s"
+UNIT = "images/s"
+BATCH = 128
+T_STEPS = 4
+HW = 32
+CPU_SAMPLE = 8           # images per CPU-baseline step
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=BATCH)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-steps", type=int, default=3)
+    return ap.parse_args()
+
+
+def config(args, world):
+    return {"workload": f"SEW-ResNet-18 CIFAR stem (3x3 s1, no maxpool), stages 64/128/256/512, "
+                        f"ADD, 100 classes, T={T_STEPS}, 3x{HW}x{HW}, batch {args.batch} per GPU",
+            "model": "sew_resnet18_cifar", "global_batch": args.batch * world,
+            "seq_len": T_STEPS, "parallelism": f"dp{world}",
+            "weights": "random init (Kaiming, BN stats as config 0), 2:4 pruned except stem",
+            "l2": "working set per step > 126 MB L2 (activations ~600 MB), no flush"}
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["hbm_gbs"], d["bf16_tflops"], "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def cpu_reference_images_per_s(steps, sample, threads):
+    """Time the oracle's port of the reference PyTorch forward on CPU."""
+    import torch
+    from oracle.sew_resnet import forward_torch, make_input
+    from sparsesnn_b200.sew_resnet import init_params
+    torch.set_num_threads(threads)
+    P = init_params(seed=0)
+    x = make_input(seed=0, B=sample)
+    forward_torch(P, x, T=T_STEPS)                       # warm-up
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        forward_torch(P, x, T=T_STEPS)
+        times.append(time.perf_counter() - t0)
+    return sample / (sum(times) / len(times)), times
+
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in (self.out or "").splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1])); mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    for _ in range(max(0, args.warmup)):
+        pass
+    ips, times = cpu_reference_images_per_s(max(1, args.steps), CPU_SAMPLE, threads)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    line = {"impl": "reference", "metric": METRIC, "value": ips, "unit": UNIT,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1000.0 * sum(times) / len(times), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": config(args, world),
+            "cpu_baseline": {"value": ips, "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": f"{CPU_SAMPLE} images per step, torch CPU fp32 port of "
+                                       f"the reference forward (oracle/sew_resnet.py)"},
+            "e2e": {"value": ips, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    from sparsesnn_b200.sew_resnet import SEWResNet18, conv_layer_flops, init_params
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    P = init_params(seed=0)
+    model = SEWResNet18(P, T=T_STEPS, batch=args.batch, H=HW, W=HW, device=dev)
+    g = torch.Generator().manual_seed(1234 + rank)
+    x_host = torch.randn((args.batch, 3, HW, HW), generator=g).pin_memory()
+    x_dev = x_host.to(dev)
+    logits_host = torch.empty((args.batch, model.num_classes), dtype=torch.float32).pin_memory()
+    gathered = torch.empty((world * args.batch, model.num_classes), dtype=torch.float32,
+                           device=dev) if world > 1 else None
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    def gather():
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, model.logits)
+
+    # Warm-up (eager), then capture the forward into a CUDA graph.
+    model.x_in.copy_(x_dev)
+    for _ in range(max(3, args.warmup)):
+        model.run()
+        gather()
+    torch.cuda.synchronize()
+    model.capture(warmup=1)
+    for _ in range(max(3, args.warmup)):
+        model.replay()
+        gather()
+    torch.cuda.synchronize()
+    n_launch = len(model.launches())
+
+    # ---------------- timed region A: device-resident inputs, graph replay
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(); torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            model.replay()
+            gather()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = args.batch * world / (ms / 1000.0)
+
+    # ---------------- timed region B: end to end through the public call
+    barrier(); torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps):
+        out = model(x_host)                         # H2D from pinned memory + graph replay
+        gather()
+        logits_host.copy_(out, non_blocking=True)   # D2H of the step's result
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ms_e2e = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms_e2e], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_e2e = float(t.item())
+    e2e = args.batch * world / (ms_e2e / 1000.0)
+
+    # ---------------- per-launch CUDA-event timing of the fused conv kernel
+    ops = model.launches()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in ops]
+    conv_ms = 0.0
+    per_layer = {name: 0.0 for name, _ in ops}
+    for _ in range(args.steps):
+        for (name, op), (a, b) in zip(ops, evs):
+            a.record(stream); op(); b.record(stream)
+        torch.cuda.synchronize()
+        for (name, _), (a, b) in zip(ops, evs):
+            dt = a.elapsed_time(b)
+            per_layer[name] += dt / args.steps
+    conv_names = [n for n, _ in ops if n not in ("stem", "head")]
+    conv_ms = sum(per_layer[n] for n in conv_names)
+    flops = sum(conv_layer_flops(l) for l in model.conv_layers())
+    hbm_peak, bf16_peak, peak_kind = peaks()
+    sparse_peak = 2.0 * bf16_peak
+    achieved = flops / (conv_ms / 1000.0) / 1e12
+    traffic = None
+    tf = ROOT / "profiles" / "sew18_traffic.txt"
+    if tf.exists():
+        for line in tf.read_text().splitlines():
+            if line.startswith("fused_conv_dram_bytes_per_forward:"):
+                traffic = int(float(line.split(":")[1]))
+    from sparsesnn_b200 import runtime as rt
+    if rt.device_error() != 0:
+        raise RuntimeError("fused kernel reported a device error")
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        ips, _ = cpu_reference_images_per_s(args.cpu_steps, CPU_SAMPLE, threads)
+        cpu = {"value": ips, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"{CPU_SAMPLE} images x {args.cpu_steps} forwards, torch CPU fp32 "
+                         f"port of the reference forward (oracle/sew_resnet.py)"}
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "f16", "data": "synthetic", "config": config(args, world),
+                "e2e": {"value": e2e, "unit": UNIT,
+                        "h2d_bytes_per_step": int(x_host.numel() * 4),
+                        "d2h_bytes_per_step": int(logits_host.numel() * 4)},
+                "gpu_launches": n_launch * args.steps,
+                "roofline": {"bound": "tensor", "achieved": achieved, "peak": sparse_peak,
+                             "unit": "TFLOP/s", "frac": achieved / sparse_peak,
+                             "traffic": traffic,
+                             "kernel": "fused_sparse_conv_lif_kernel (19 launches/forward)",
+                             "peak_note": f"2:4 sparse ceiling = 2 x {peak_kind} dense bf16 "
+                                          f"{bf16_peak} TFLOP/s; FLOPs dense-equivalent",
+                             "flops_per_forward": flops, "kernel_ms_per_forward": conv_ms},
+                "layer_ms": {k: round(v, 4) for k, v in per_layer.items()},
+                "clocks": clk.summary(),
+                "cpu_baseline": cpu}
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        import datetime
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
