@@ -7,6 +7,8 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <algorithm>
+#include <cmath>
 #include <cstring>
 #include <mutex>
 
@@ -31,6 +33,7 @@ __device__ unsigned g_device_err = 0;
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::mutex g_init_mu;
 bool g_inited = false;
+int g_num_sms = 148;
 int g_init_status = SNN_E_NO_DEVICE;
 
 int ensure_init() {
@@ -51,6 +54,7 @@ int ensure_init() {
   if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
     return g_init_status = fail(SNN_E_CUDA, "cuTensorMapEncodeTiled unavailable");
   g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  g_num_sms = prop.multiProcessorCount;
   e = cudaFuncSetAttribute(snn::fused_sparse_conv_lif_kernel,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, snn::kSmemBytes);
   if (e != cudaSuccess) return g_init_status = fail(SNN_E_CUDA, "smem attribute: %s", cudaGetErrorString(e));
@@ -67,6 +71,7 @@ int check_desc(const snn_conv_desc* d, Geometry* g) {
     return fail(SNN_E_INVALID, "non-positive dimension");
   if (d->Cin < 64 || d->Cin % 64)
     return fail(SNN_E_INVALID, "Cin=%d must be a positive multiple of 64", d->Cin);
+  if (d->Cout % 8) return fail(SNN_E_INVALID, "Cout=%d must be a multiple of 8", d->Cout);
   if (d->stride != 1 && d->stride != 2) return fail(SNN_E_INVALID, "stride must be 1 or 2");
   if (d->pad < 0 || d->pad >= d->KH || d->pad >= d->KW) return fail(SNN_E_INVALID, "bad pad");
   if (d->stride == 2 && ((d->H & 1) || (d->W & 1)))
@@ -114,8 +119,9 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
     return fail(SNN_E_INVALID, "state flags set but state is null");
   if (d->neuron == SNN_NEURON_NONE && residual)
     return fail(SNN_E_INVALID, "residual needs a neuron");
-  if ((reinterpret_cast<uintptr_t>(data) | reinterpret_cast<uintptr_t>(weight)) & 15)
-    return fail(SNN_E_INVALID, "data and weight must be 16-byte aligned");
+  if ((reinterpret_cast<uintptr_t>(data) | reinterpret_cast<uintptr_t>(weight) |
+       reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(residual)) & 15)
+    return fail(SNN_E_INVALID, "data, weight, out and residual must be 16-byte aligned");
 
   snn::ConvParams p;
   memset(&p, 0, sizeof(p));
@@ -126,7 +132,9 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
     cuuint32_t box[2] = {snn::kKB / 2, snn::kBM};
     if ((st = encode(&p.tmap_a, 2, wbytes, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B))) return st;
   }
-  // Tile geometry in output coordinates.
+  // Tile geometry in output coordinates: a tile is up to 64 pixels of one
+  // timestep -- a run of one output row, whole rows of one image, or whole
+  // images.
   int tw, th, tn;
   if (g.OW >= snn::kBN) { tw = snn::kBN; th = 1; tn = 1; }
   else if (g.OH * g.OW >= snn::kBN) { tw = g.OW; th = snn::kBN / g.OW; tn = 1; }
@@ -135,14 +143,21 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
   p.tiles_w = (g.OW + tw - 1) / tw;
   p.tiles_h = (g.OH + th - 1) / th;
   const int tiles_n = (d->B + tn - 1) / tn;
+  const long long n_px = static_cast<long long>(p.tiles_w) * p.tiles_h * tiles_n;
+  if (n_px > 0x7fffffffLL) return fail(SNN_E_INVALID, "too many pixel tiles");
+  p.n_px_tiles = static_cast<int>(n_px);
+  p.n_m = g.Fpad / snn::kBM;
   p.box_bytes = tw * th * tn * snn::kKB * 2;
+  p.out_box_bytes = tw * th * tn * snn::kBM * 2;
+  const cuuint32_t box5[5] = {static_cast<cuuint32_t>(snn::kKB), static_cast<cuuint32_t>(tw),
+                              static_cast<cuuint32_t>(th), static_cast<cuuint32_t>(tn), 1};
   {
-    const size_t C = d->Cin, W = d->W, H = d->H;
+    const size_t C = d->Cin, W = d->W, H = d->H, B = d->B;
     const char* base = static_cast<const char*>(data);
     const int nmaps = d->stride == 2 ? 4 : 1;
     for (int m = 0; m < nmaps; ++m) {
       const int hp = m >> 1, wp = m & 1;
-      cuuint64_t dims[4], strides[3];
+      cuuint64_t dims[5], strides[4];
       const char* b = base;
       if (d->stride == 1) {
         dims[1] = W; dims[2] = H;
@@ -152,36 +167,51 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
         strides[0] = 2 * C * 2; strides[1] = 2 * W * C * 2;
         b = base + (hp * W + wp) * C * 2;
       }
-      dims[0] = C;
-      dims[3] = static_cast<cuuint64_t>(d->T) * d->B;
-      strides[2] = H * W * C * 2;
-      cuuint32_t box[4] = {snn::kKB, static_cast<cuuint32_t>(tw), static_cast<cuuint32_t>(th),
-                           static_cast<cuuint32_t>(tn)};
-      if ((st = encode(&p.tmap_b[m], 4, b, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+      dims[0] = C; dims[3] = B; dims[4] = static_cast<cuuint64_t>(d->T);
+      strides[2] = H * W * C * 2; strides[3] = B * H * W * C * 2;
+      if ((st = encode(&p.tmap_b[m], 5, b, dims, strides, box5, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
     }
+  }
+  const bool spikes = d->neuron != SNN_NEURON_NONE;
+  if (spikes) {  // output (and residual) spike tiles: (Cout, OW, OH, B, T) fp16
+    const size_t F = d->Cout, OW = g.OW, OH = g.OH, B = d->B;
+    cuuint64_t dims[5] = {F, OW, OH, B, static_cast<cuuint64_t>(d->T)};
+    cuuint64_t strides[4] = {F * 2, OW * F * 2, OH * OW * F * 2, B * OH * OW * F * 2};
+    cuuint32_t box[5] = {static_cast<cuuint32_t>(snn::kBM), static_cast<cuuint32_t>(tw),
+                         static_cast<cuuint32_t>(th), static_cast<cuuint32_t>(tn), 1};
+    if ((st = encode(&p.tmap_out, 5, out, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE))) return st;
+    if (residual &&
+        (st = encode(&p.tmap_res, 5, residual, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE)))
+      return st;
+  } else {
+    p.out_f32 = static_cast<float*>(out);
   }
   p.meta = reinterpret_cast<const uint32_t*>(wbytes + meta_offset(g));
   p.scale = scale; p.bias = bias; p.state = state;
-  p.residual = static_cast<const __half*>(residual);
-  p.out = out;
+  p.has_res = residual != nullptr;
   unsigned* err = nullptr;
-  cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_device_err);
+  if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_device_err) != cudaSuccess)
+    return fail(SNN_E_CUDA, "error word address");
   p.err = err;
-  p.F = d->Cout; p.Cin = d->Cin; p.KW = d->KW; p.stride = d->stride; p.pad = d->pad;
+  p.F = d->Cout; p.KW = d->KW; p.stride = d->stride; p.pad = d->pad;
   p.n_kb = g.n_kb; p.cin_blocks = g.cin_blocks;
   p.B = d->B; p.OH = g.OH; p.OW = g.OW; p.T = d->T;
   p.neuron = d->neuron; p.flags = d->flags;
-  p.tau = d->tau; p.decay = 1.0f - 1.0f / d->tau;
-  if (d->neuron == SNN_NEURON_LIF) {
-    // Reference computes (1.0 - 1.0/tau) in double, then float32 (models/neurons.py:125).
-    p.decay = static_cast<float>(1.0 - 1.0 / static_cast<double>(d->tau));
-  }
+  p.tau = d->tau;
+  // Reference computes (1.0 - 1.0/tau) in double, then float32 (models/neurons.py:125).
+  p.decay = d->neuron == SNN_NEURON_LIF
+                ? static_cast<float>(1.0 - 1.0 / static_cast<double>(d->tau)) : 1.0f;
+  int e2 = 0;
+  const float mant = frexpf(d->tau, &e2);
+  p.tau_pow2 = (d->neuron == SNN_NEURON_LIF && mant == 0.5f) ? 1 : 0;
+  p.inv_tau = p.tau_pow2 ? 1.0f / d->tau : 0.0f;
   p.v_th = d->v_threshold; p.v_reset = d->v_reset;
   p.timeout_ns = 1000000000ull;
 
-  dim3 grid(p.tiles_w * p.tiles_h * tiles_n, g.Fpad / snn::kBM);
-  if (grid.x > 0x7fffffffu || grid.y > 65535u) return fail(SNN_E_INVALID, "grid too large");
-  snn::fused_sparse_conv_lif_kernel<<<grid, snn::kThreads, snn::kSmemBytes,
+  const int per_m = std::max(1, std::min(p.n_px_tiles, g_num_sms / p.n_m));
+  const long long grid = static_cast<long long>(per_m) * p.n_m;
+  if (grid > 0x7fffffffLL) return fail(SNN_E_INVALID, "grid too large");
+  snn::fused_sparse_conv_lif_kernel<<<static_cast<unsigned>(grid), snn::kThreads, snn::kSmemBytes,
                                        static_cast<cudaStream_t>(stream)>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));

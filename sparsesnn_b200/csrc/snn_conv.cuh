@@ -1,18 +1,24 @@
 // Fused 2:4-sparse implicit-GEMM Conv/Linear + BN + LIF/IF (+SEW add) over T
 // timesteps for sm_100a.
 //
-// GEMM view (per CTA):  D[cout, pixel] = W_sp[cout, k] * X[k, pixel]
+// GEMM view (per tile):  D[cout, pixel] = W_sp[cout, k] * X[k, pixel]
 //   A = compressed 2:4 weights (M = 128 output channels), K-major, 64B swizzle
-//   B = activations (N = BN output pixels per timestep), K-major, 128B swizzle;
+//   B = activations (N = 64 output pixels per timestep), K-major, 128B swizzle;
 //       one 64-channel slice of one filter tap per k-block, fetched by TMA from
-//       the NHWC input with out-of-bounds zero fill providing the conv padding
-//   D = FP32 accumulators in tensor memory, one BN-column block per timestep,
-//       so each weight k-block is staged once and used for all T timesteps
-//   E = 2:4 metadata, held in tensor memory for the CTA's whole K range
+//       the NHWC input; out-of-bounds zero fill provides the conv padding
+//   D = FP32 accumulators in tensor memory (TMEM), two buffers of
+//       kTC timesteps x 64 columns, so the epilogue of one chunk of timesteps
+//       overlaps the MMAs of the next
+//   E = 2:4 metadata, resident in TMEM for the CTA's whole K range
 //
-// Warp roles (6 warps): 0 = TMA producer, 1 = TMEM owner + MMA issuer,
-// 2..5 = metadata loader + epilogue (BN, LIF recurrence over T with the
-// membrane in registers, spike (+residual) store, final membrane store).
+// Persistent CTAs: each CTA owns one 128-channel slice (so its metadata is
+// loaded once) and walks a strided list of pixel tiles.
+//
+// Warp roles (10 warps): 0 = TMA producer, 1 = TMEM owner + MMA issuer,
+// 2..9 = epilogue: two warps per TMEM lane quarter, each owning 32 of the 64
+// pixel columns.  The epilogue applies BN, runs the LIF/IF recurrence over T
+// with the membrane in registers, adds the SEW residual (fetched by TMA),
+// stages fp16 spikes in shared memory and writes them with TMA stores.
 #pragma once
 #include <cstdint>
 #include <cuda.h>
@@ -21,61 +27,84 @@
 
 namespace snn {
 
-constexpr int kBM = 128;             // output channels per CTA (UMMA M)
-constexpr int kBN = 64;              // output pixels per timestep per CTA (UMMA N)
-constexpr int kTC = 4;               // timesteps per accumulator chunk
-constexpr int kStages = 5;           // smem pipeline depth
+constexpr int kBM = 128;             // output channels per tile (UMMA M)
+constexpr int kBN = 64;              // output pixels per timestep per tile (UMMA N)
+constexpr int kTC = 2;               // timesteps per accumulator buffer
+constexpr int kNumAcc = 2;           // accumulator buffers
+constexpr int kStages = 6;           // smem pipeline depth
 constexpr int kKB = 64;              // logical K per k-block (one 128B activation row)
 constexpr int kABytes = kBM * (kKB / 2) * 2;     // 8 KB compressed weights
 constexpr int kBBytes = kBN * kKB * 2;           // 8 KB activations per timestep
 constexpr int kStageBytes = kABytes + kTC * kBBytes;
-constexpr int kAccCols = kTC * kBN;              // 256 TMEM columns of accumulators
-constexpr int kMetaCol = kAccCols;               // metadata columns start here
+constexpr int kAccCols = kTC * kBN;              // 128 TMEM columns per buffer
+constexpr int kMetaCol = kNumAcc * kAccCols;     // metadata columns start here
 constexpr int kTmemCols = 512;
 constexpr int kMaxMetaCols = kTmemCols - kMetaCol;  // => K <= 8192
-constexpr int kThreads = 192;
-constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int kEpiWarps = 8;
+constexpr int kEpiThreads = kEpiWarps * 32;
+constexpr int kThreads = 64 + kEpiThreads;
+constexpr int kTileBytes = kBN * kBM * 2;        // fp16 [pixel][cout] staging tile
+constexpr int kBarBytes = 512;
+constexpr int kSmemBytes = kStages * kStageBytes + 4 * kTileBytes + kBarBytes + 1024;
 
 enum NeuronKind : int { kLIF = 0, kIF = 1, kNoNeuron = 2 };
 enum ConvFlags : int { kReadState = 1, kWriteState = 2 };
 enum ErrCode : unsigned { kErrTimeoutFull = 1u, kErrTimeoutEmpty = 2u, kErrTimeoutAcc = 4u,
-                          kErrTimeoutMeta = 8u, kErrTimeoutAccEmpty = 16u, kErrTimeoutDrain = 32u };
+                          kErrTimeoutMeta = 8u, kErrTimeoutAccEmpty = 16u, kErrTimeoutDrain = 32u,
+                          kErrTimeoutRes = 64u };
 
 struct ConvParams {
-  CUtensorMap tmap_a;        // compressed weights [Fpad][K/2] fp16
-  CUtensorMap tmap_b[4];     // activations, one map per (h,w) stride parity
+  CUtensorMap tmap_a;        // compressed weights [Fpad][K/2] fp16 (2D)
+  CUtensorMap tmap_b[4];     // activations (C, W', H', B, T), one map per stride parity
+  CUtensorMap tmap_out;      // output spikes (Cout, OW, OH, B, T) fp16
+  CUtensorMap tmap_res;      // residual, same geometry as the output
   const uint32_t* meta;      // [Fpad/128][K/32][128]
   const float* scale;        // [F]
   const float* bias;         // [F]
   float* state;              // [B*OH*OW][F] or null
-  const __half* residual;    // [T*B*OH*OW][F] or null
-  void* out;                 // [T*B*OH*OW][F] fp16 spikes, or fp32 BN output
+  float* out_f32;            // [T*B*OH*OW][F] (neuron == kNoNeuron only)
   unsigned* err;             // device error word
-  int F, Cin, KW, stride, pad;
+  int F, KW, stride, pad;
   int n_kb, cin_blocks;      // k-blocks, 64-channel slices per tap
   int B, OH, OW, T;
   int tw, th, tn;            // tile extent (output coords) along w, h, image
-  int tiles_w, tiles_h;      // tile grid (tiles_n implied by gridDim.x)
-  int box_bytes;             // bytes one activation TMA box delivers (tw*th*tn*128)
-  int neuron, flags;
-  float decay, tau, v_th, v_reset;
+  int tiles_w, tiles_h, n_px_tiles, n_m;
+  int box_bytes;             // bytes of one activation TMA box (tw*th*tn*128)
+  int out_box_bytes;         // bytes of one output/residual TMA box (tw*th*tn*256)
+  int neuron, flags, has_res, tau_pow2;
+  float decay, tau, inv_tau, v_th, v_reset;
   unsigned long long timeout_ns;
 };
 
 __device__ __forceinline__ int floordiv2(int d) { return (d - (d & 1)) / 2; }
+
+struct TileCoord { int w0, h0, n0; };
+
+__device__ __forceinline__ TileCoord tile_coord(const ConvParams& p, int pt) {
+  TileCoord c;
+  const int tw_i = pt % p.tiles_w;
+  const int rest = pt / p.tiles_w;
+  const int th_i = rest % p.tiles_h;
+  const int tn_i = rest / p.tiles_h;
+  c.w0 = tw_i * p.tw; c.h0 = th_i * p.th; c.n0 = tn_i * p.tn;
+  return c;
+}
 
 __global__ void __launch_bounds__(kThreads, 1)
 fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint8_t* sA = smem;                                   // kStages x kABytes
-  uint8_t* sB = smem + kStages * kABytes;               // kStages x kTC x kBBytes
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint8_t* sA = smem;                                        // kStages x kABytes
+  uint8_t* sB = smem + kStages * kABytes;                    // kStages x kTC x kBBytes
+  uint8_t* sOut = smem + kStages * kStageBytes;              // 2 x kTileBytes
+  uint8_t* sRes = sOut + 2 * kTileBytes;                     // 2 x kTileBytes
+  uint64_t* full = reinterpret_cast<uint64_t*>(sRes + 2 * kTileBytes);
   uint64_t* empty = full + kStages;
-  uint64_t* acc_full = empty + kStages;
-  uint64_t* acc_empty = acc_full + 1;
-  uint64_t* meta_ready = acc_empty + 1;
+  uint64_t* acc_full = empty + kStages;                      // [kNumAcc]
+  uint64_t* acc_empty = acc_full + kNumAcc;                  // [kNumAcc]
+  uint64_t* res_full = acc_empty + kNumAcc;                  // [2]
+  uint64_t* meta_ready = res_full + 2;
   uint64_t* drain = meta_ready + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -83,20 +112,16 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
 
-  // Tile coordinates.
-  const int tile = blockIdx.x;
-  const int tw_i = tile % p.tiles_w;
-  const int th_i = (tile / p.tiles_w) % p.tiles_h;
-  const int tn_i = tile / (p.tiles_w * p.tiles_h);
-  const int w0 = tw_i * p.tw, h0 = th_i * p.th, n0 = tn_i * p.tn;
-  const int m_tile = blockIdx.y;
+  const int m_tile = blockIdx.x % p.n_m;
+  const int first_pt = blockIdx.x / p.n_m;
+  const int pt_step = gridDim.x / p.n_m;
   const int n_chunks = (p.T + kTC - 1) / kTC;
-  const int n_meta = 2 * p.n_kb;                        // sparse K steps (32 each)
+  const int n_meta = 2 * p.n_kb;                               // sparse K steps (32 each)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-    mbar_init(acc_full, 1);
-    mbar_init(acc_empty, 128);
+    for (int b = 0; b < kNumAcc; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], kEpiThreads); }
+    mbar_init(&res_full[0], 1); mbar_init(&res_full[1], 1);
     mbar_init(meta_ready, 128);
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -105,6 +130,8 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&p.tmap_a);
     for (int i = 0; i < (p.stride == 2 ? 4 : 1); ++i) prefetch_tmap(&p.tmap_b[i]);
+    if (p.neuron != kNoNeuron) prefetch_tmap(&p.tmap_out);
+    if (p.has_res) prefetch_tmap(&p.tmap_res);
   }
   if (warp == 1) { tmem_alloc(tmem_slot, kTmemCols); tmem_relinquish(); }
   tc_fence_before();
@@ -117,82 +144,92 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
     if (lane == 0) {
       int stage = 0; uint32_t phase = 0;
       int issued = 0;
-      for (int c = 0; c < n_chunks && !*abort_flag; ++c) {
-        const int t0 = c * kTC;
-        const int tcn = min(kTC, p.T - t0);
-        for (int kb = 0; kb < p.n_kb; ++kb) {
-          if (!mbar_wait_bounded(&empty[stage], phase ^ 1, p.timeout_ns)) {
-            atomicOr(p.err, kErrTimeoutEmpty); *abort_flag = 1; break;
+      bool stop = false;
+      for (int pt = first_pt; pt < p.n_px_tiles && !stop; pt += pt_step) {
+        const TileCoord tc = tile_coord(p, pt);
+        for (int c = 0; c < n_chunks && !stop; ++c) {
+          const int t0 = c * kTC;
+          const int tcn = min(kTC, p.T - t0);
+          for (int kb = 0; kb < p.n_kb; ++kb) {
+            if (*abort_flag) { stop = true; break; }
+            if (!mbar_wait_bounded(&empty[stage], phase ^ 1, p.timeout_ns)) {
+              atomicOr(p.err, kErrTimeoutEmpty); *abort_flag = 1; stop = true; break;
+            }
+            mbar_arrive_expect_tx(&full[stage], kABytes + tcn * p.box_bytes);
+            tma_load_2d(sA + stage * kABytes, &p.tmap_a, &full[stage], kb * (kKB / 2),
+                        m_tile * kBM);
+            const int tap = kb / p.cin_blocks;
+            const int cb = kb - tap * p.cin_blocks;
+            const int kh = tap / p.KW, kw = tap - kh * p.KW;
+            int map = 0, hoff = kh - p.pad, woff = kw - p.pad;
+            if (p.stride == 2) {
+              map = (hoff & 1) * 2 + (woff & 1);
+              hoff = floordiv2(hoff); woff = floordiv2(woff);
+            }
+            for (int tt = 0; tt < tcn; ++tt) {
+              tma_load_5d(sB + (stage * kTC + tt) * kBBytes, &p.tmap_b[map], &full[stage],
+                          cb * kKB, tc.w0 + woff, tc.h0 + hoff, tc.n0, t0 + tt);
+            }
+            ++issued;
+            if (++stage == kStages) { stage = 0; phase ^= 1; }
           }
-          if (*abort_flag) break;
-          mbar_arrive_expect_tx(&full[stage], kABytes + tcn * p.box_bytes);
-          tma_load_2d(sA + stage * kABytes, &p.tmap_a, &full[stage], kb * (kKB / 2),
-                      m_tile * kBM);
-          const int tap = kb / p.cin_blocks;
-          const int cb = kb - tap * p.cin_blocks;
-          const int kh = tap / p.KW, kw = tap - kh * p.KW;
-          int map = 0, hoff = kh - p.pad, woff = kw - p.pad;
-          if (p.stride == 2) {
-            const int hp = hoff & 1, wp = woff & 1;
-            map = hp * 2 + wp;
-            hoff = floordiv2(hoff); woff = floordiv2(woff);
-          }
-          for (int t = 0; t < tcn; ++t) {
-            tma_load_4d(sB + (stage * kTC + t) * kBBytes, &p.tmap_b[map], &full[stage],
-                        cb * kKB, w0 + woff, h0 + hoff, (t0 + t) * p.B + n0);
-          }
-          ++issued;
-          if (++stage == kStages) { stage = 0; phase ^= 1; }
         }
       }
       // Let every load already issued land before the CTA can exit.
       const int n_wait = min(issued, kStages);
       for (int i = 0; i < n_wait; ++i) {
-        // Stage of the i-th most recent issue and the parity of that phase.
         const int back = issued - 1 - i;
-        const int s = back % kStages;
-        const uint32_t ph = (back / kStages) & 1;
-        if (!mbar_wait_bounded(&full[s], ph, p.timeout_ns)) atomicOr(p.err, kErrTimeoutFull);
+        if (!mbar_wait_bounded(&full[back % kStages], (back / kStages) & 1, p.timeout_ns))
+          atomicOr(p.err, kErrTimeoutFull);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = idesc_f16(kBM, kBN, true);
-      bool ok = mbar_wait_bounded(meta_ready, 0, p.timeout_ns);
-      if (!ok) { atomicOr(p.err, kErrTimeoutMeta); *abort_flag = 1; }
+      if (!mbar_wait_bounded(meta_ready, 0, p.timeout_ns)) {
+        atomicOr(p.err, kErrTimeoutMeta); *abort_flag = 1;
+      }
       tc_fence_after();
       int stage = 0; uint32_t phase = 0;
-      for (int c = 0; c < n_chunks && !*abort_flag; ++c) {
-        const int tcn = min(kTC, p.T - c * kTC);
-        if (c > 0) {
-          if (!mbar_wait_bounded(acc_empty, (c - 1) & 1, p.timeout_ns)) {
-            atomicOr(p.err, kErrTimeoutAccEmpty); *abort_flag = 1; break;
+      int acc_iter = 0;
+      bool stop = *abort_flag != 0;
+      for (int pt = first_pt; pt < p.n_px_tiles && !stop; pt += pt_step) {
+        for (int c = 0; c < n_chunks && !stop; ++c) {
+          const int tcn = min(kTC, p.T - c * kTC);
+          const int buf = acc_iter & 1;
+          const uint32_t use = static_cast<uint32_t>(acc_iter >> 1);
+          if (!mbar_wait_bounded(&acc_empty[buf], (use & 1) ^ 1, p.timeout_ns)) {
+            atomicOr(p.err, kErrTimeoutAccEmpty); *abort_flag = 1; stop = true; break;
           }
           tc_fence_after();
-        }
-        for (int kb = 0; kb < p.n_kb; ++kb) {
-          if (!mbar_wait_bounded(&full[stage], phase, p.timeout_ns)) {
-            atomicOr(p.err, kErrTimeoutFull); *abort_flag = 1; break;
-          }
-          tc_fence_after();
-          const uint32_t a_base = smem_u32(sA + stage * kABytes);
-          const uint32_t b_base = smem_u32(sB + stage * kTC * kBBytes);
-#pragma unroll
-          for (int s = 0; s < 2; ++s) {
-            const uint32_t ecol = kMetaCol + 2 * kb + s;
-            const uint32_t e_addr = tmem + (ecol & ~1u);
-            const uint32_t id = idesc | (ecol & 1u);
-            const uint64_t adesc = smem_desc_kmajor(a_base + 32 * s, 512, 4);
-            for (int t = 0; t < tcn; ++t) {
-              const uint64_t bdesc = smem_desc_kmajor(b_base + t * kBBytes + 64 * s, 1024, 2);
-              mma_sp_f16(tmem + t * kBN, adesc, bdesc, e_addr, id, (kb > 0 || s > 0) ? 1u : 0u);
+          const uint32_t d_base = tmem + buf * kAccCols;
+          for (int kb = 0; kb < p.n_kb; ++kb) {
+            if (!mbar_wait_bounded(&full[stage], phase, p.timeout_ns)) {
+              atomicOr(p.err, kErrTimeoutFull); *abort_flag = 1; stop = true; break;
             }
+            tc_fence_after();
+            const uint32_t a_base = smem_u32(sA + stage * kABytes);
+            const uint32_t b_base = smem_u32(sB + stage * kTC * kBBytes);
+#pragma unroll
+            for (int s = 0; s < 2; ++s) {
+              const uint32_t ecol = kMetaCol + 2 * kb + s;
+              const uint32_t e_addr = tmem + (ecol & ~1u);
+              const uint32_t id = idesc | (ecol & 1u);
+              const uint64_t adesc = smem_desc_kmajor(a_base + 32 * s, 512, 4);
+              for (int tt = 0; tt < tcn; ++tt) {
+                const uint64_t bdesc = smem_desc_kmajor(b_base + tt * kBBytes + 64 * s, 1024, 2);
+                mma_sp_f16(d_base + tt * kBN, adesc, bdesc, e_addr, id,
+                           (kb > 0 || s > 0) ? 1u : 0u);
+              }
+            }
+            mma_commit(&empty[stage]);
+            if (++stage == kStages) { stage = 0; phase ^= 1; }
           }
-          mma_commit(&empty[stage]);
-          if (++stage == kStages) { stage = 0; phase ^= 1; }
+          if (stop) break;
+          mma_commit(&acc_full[buf]);
+          ++acc_iter;
         }
-        mma_commit(acc_full);
       }
       // Drain: every MMA issued so far completes before TMEM is released.
       mma_commit(drain);
@@ -200,19 +237,16 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
     }
   } else {
     // ------------------------------------------------- metadata + epilogue
+    const int e = warp - 2;                      // 0..7
     const int q = warp & 3;                      // TMEM lane quarter of this warp
+    const int half = e >> 2;                     // which 32 pixel columns
     const int row = q * 32 + lane;               // output channel within the tile
+    const int et = threadIdx.x - 64;             // 0..255
+    const bool leader = (et == 0);
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
-    {
+    if (half == 0) {
       const uint32_t* src = p.meta + (static_cast<size_t>(m_tile) * n_meta) * kBM + row;
-      int j = 0;
-      for (; j + 8 <= n_meta; j += 8) {
-        uint32_t r[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) r[i] = __ldg(src + static_cast<size_t>(j + i) * kBM);
-        tmem_st8(lane_base + kMetaCol + j, r);
-      }
-      for (; j < n_meta; j += 8) {   // tail: store a full x8 group, padding with 0x44444444
+      for (int j = 0; j < n_meta; j += 8) {
         uint32_t r[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i)
@@ -228,84 +262,131 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
     const bool cvalid = cout < p.F;
     const float sc = cvalid ? p.scale[cout] : 0.f;
     const float bi = cvalid ? p.bias[cout] : 0.f;
-    const size_t P = static_cast<size_t>(p.B) * p.OH * p.OW;
+    const long long P = static_cast<long long>(p.B) * p.OH * p.OW;
     const int tile_px = p.tw * p.th;
+    const bool spikes_out = p.neuron != kNoNeuron;
 
-    float v[kBN / 32][32];
-    // Pixel index of each column (or -1 when outside the tensor).
-    auto pixel_of = [&](int col) -> long long {
+    auto pixel_of = [&](const TileCoord& tc, int col) -> long long {
       const int dn = col / tile_px;
       const int rem = col - dn * tile_px;
       const int dh = rem / p.tw;
       const int dw = rem - dh * p.tw;
-      const int n = n0 + dn, oh = h0 + dh, ow = w0 + dw;
+      const int n = tc.n0 + dn, oh = tc.h0 + dh, ow = tc.w0 + dw;
       if (dn >= p.tn || n >= p.B || oh >= p.OH || ow >= p.OW) return -1;
       return (static_cast<long long>(n) * p.OH + oh) * p.OW + ow;
     };
+    // The epilogue visits (tile, t) in a fixed order; the leader prefetches the
+    // residual tile of the next visit.
+    auto issue_res = [&](int pt, int t, int b) {
+      const TileCoord tc = tile_coord(p, pt);
+      mbar_arrive_expect_tx(&res_full[b], p.out_box_bytes);
+      tma_load_5d(sRes + b * kTileBytes, &p.tmap_res, &res_full[b], m_tile * kBM, tc.w0, tc.h0,
+                  tc.n0, t);
+    };
+    uint32_t res_issued = 0;
+    if (p.has_res && leader && first_pt < p.n_px_tiles) { issue_res(first_pt, 0, 0); ++res_issued; }
 
-#pragma unroll
-    for (int g = 0; g < kBN / 32; ++g) {
+    uint32_t u = 0;           // timestep visits so far (staging / residual buffer index)
+    int acc_iter = 0;
+    bool stop = false;
+    for (int pt = first_pt; pt < p.n_px_tiles && !stop; pt += pt_step) {
+      const TileCoord tc = tile_coord(p, pt);
+      float v[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         float v0 = 0.f;
         if ((p.flags & kReadState) && cvalid) {
-          const long long px = pixel_of(g * 32 + i);
+          const long long px = pixel_of(tc, half * 32 + i);
           if (px >= 0) v0 = p.state[px * p.F + cout];
         }
-        v[g][i] = v0;
+        v[i] = v0;
       }
-    }
-
-    for (int c = 0; c < n_chunks; ++c) {
-      const int t0 = c * kTC;
-      const int tcn = min(kTC, p.T - t0);
-      if (*abort_flag) break;
-      if (!mbar_wait_bounded(acc_full, c & 1, p.timeout_ns)) {
-        atomicOr(p.err, kErrTimeoutAcc); *abort_flag = 1; break;
-      }
-      tc_fence_after();
-      for (int t = 0; t < tcn; ++t) {
-#pragma unroll
-        for (int g = 0; g < kBN / 32; ++g) {
-          float acc[32];
-          tmem_ld32(lane_base + t * kBN + g * 32, acc);   // warp-collective: no early exit above
-          const size_t tbase = static_cast<size_t>(t0 + t) * P;
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const long long px = pixel_of(g * 32 + i);
-            if (px < 0 || !cvalid) continue;
-            const size_t o = (tbase + px) * p.F + cout;
-            const float x = fmaf(acc[i], sc, bi);
-            if (p.neuron == kNoNeuron) {
-              static_cast<float*>(p.out)[o] = x;
-              continue;
-            }
-            // Reference order: v*(1-1/tau) + x/tau, each op rounded (no FMA).
-            float h;
-            if (p.neuron == kLIF) h = __fadd_rn(__fmul_rn(v[g][i], p.decay), __fdiv_rn(x, p.tau));
-            else h = __fadd_rn(v[g][i], x);
-            const bool spike = (h - p.v_th) >= 0.f;
-            v[g][i] = spike ? p.v_reset : h;
-            float y = spike ? 1.f : 0.f;
-            if (p.residual) y += __half2float(p.residual[o]);
-            static_cast<__half*>(p.out)[o] = __float2half_rn(y);
+      for (int c = 0; c < n_chunks && !stop; ++c) {
+        const int t0 = c * kTC;
+        const int tcn = min(kTC, p.T - t0);
+        const int buf = acc_iter & 1;
+        const uint32_t use = static_cast<uint32_t>(acc_iter >> 1);
+        bool fail = !mbar_wait_bounded(&acc_full[buf], use & 1, p.timeout_ns);
+        if (fail) atomicOr(p.err, kErrTimeoutAcc);
+        tc_fence_after();
+        for (int tt = 0; tt < tcn; ++tt) {
+          const int t = t0 + tt;
+          const int sb = u & 1;
+          if (spikes_out && leader) bulk_wait_group_read<1>();   // staging[sb] free again
+          if (named_barrier_or(1, kEpiThreads, fail || *abort_flag)) { stop = true; break; }
+          if (p.has_res && leader) {
+            // Next visit: (pt, t+1), or the first timestep of the next tile.
+            int npt = pt, nt = t + 1;
+            if (nt >= p.T) { npt = pt + pt_step; nt = 0; }
+            if (npt < p.n_px_tiles) { issue_res(npt, nt, sb ^ 1); ++res_issued; }
           }
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(acc_empty);
-    }
-
-    if ((p.flags & kWriteState) && cvalid && !*abort_flag) {
+          __half* stg = reinterpret_cast<__half*>(sOut + sb * kTileBytes);
+          const __half* resb = reinterpret_cast<const __half*>(sRes + sb * kTileBytes);
+          float acc[32];
+          tmem_ld32(lane_base + buf * kAccCols + tt * kBN + half * 32, acc);
+          bool rfail = false;
+          if (p.has_res)
+            rfail = !mbar_wait_bounded(&res_full[sb], (u >> 1) & 1, p.timeout_ns);
+          if (rfail) atomicOr(p.err, kErrTimeoutRes);
+          if (spikes_out) {
 #pragma unroll
-      for (int g = 0; g < kBN / 32; ++g) {
+            for (int i = 0; i < 32; ++i) {
+              const float x = fmaf(acc[i], sc, bi);
+              // Reference order v*(1-1/tau) + x/tau, each op rounded (no FMA);
+              // x*(1/tau) equals x/tau exactly when tau is a power of two.
+              float h;
+              if (p.neuron == kLIF) {
+                const float xin = p.tau_pow2 ? __fmul_rn(x, p.inv_tau) : __fdiv_rn(x, p.tau);
+                h = __fadd_rn(__fmul_rn(v[i], p.decay), xin);
+              } else {
+                h = __fadd_rn(v[i], x);
+              }
+              const bool spike = (h - p.v_th) >= 0.f;
+              v[i] = spike ? p.v_reset : h;
+              float y = spike ? 1.f : 0.f;
+              const int off = (half * 32 + i) * kBM + row;
+              if (p.has_res) y += __half2float(resb[off]);
+              stg[off] = __float2half_rn(y);
+            }
+            fence_proxy_async_smem();
+          } else if (cvalid) {
+            const size_t tbase = static_cast<size_t>(t) * P;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const long long px = pixel_of(tc, half * 32 + i);
+              if (px >= 0) p.out_f32[(tbase + px) * p.F + cout] = fmaf(acc[i], sc, bi);
+            }
+          }
+          if (named_barrier_or(2, kEpiThreads, rfail)) { stop = true; break; }
+          if (spikes_out && leader) {
+            tma_store_5d(&p.tmap_out, sOut + sb * kTileBytes, m_tile * kBM, tc.w0, tc.h0, tc.n0, t);
+            bulk_commit_group();
+          }
+          ++u;
+        }
+        if (stop) break;
+        tc_fence_before();
+        mbar_arrive(&acc_empty[buf]);
+        ++acc_iter;
+      }
+      if (!stop && (p.flags & kWriteState) && cvalid) {
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const long long px = pixel_of(g * 32 + i);
-          if (px >= 0) p.state[px * p.F + cout] = v[g][i];
+          const long long px = pixel_of(tc, half * 32 + i);
+          if (px >= 0) p.state[px * p.F + cout] = v[i];
         }
       }
     }
+    if (leader) {
+      bulk_wait_group<0>();
+      // After an abort, let a residual prefetch that no visit consumed land.
+      if (p.has_res && res_issued > u) {
+        const uint32_t last = res_issued - 1;
+        if (!mbar_wait_bounded(&res_full[last & 1], (last >> 1) & 1, p.timeout_ns))
+          atomicOr(p.err, kErrTimeoutRes);
+      }
+    }
+    if (stop) *abort_flag = 1;
   }
 
   tc_fence_before();
