@@ -36,6 +36,20 @@ bool g_inited = false;
 int g_num_sms = 148;
 int g_init_status = SNN_E_NO_DEVICE;
 
+using ConvKernel = void (*)(const snn::ConvParams);
+
+ConvKernel conv_kernel_fn(int mode, bool res) {
+  switch (mode * 2 + (res ? 1 : 0)) {
+    case 0: return snn::fused_sparse_conv_lif_kernel<snn::kModeLifMul, false>;
+    case 1: return snn::fused_sparse_conv_lif_kernel<snn::kModeLifMul, true>;
+    case 2: return snn::fused_sparse_conv_lif_kernel<snn::kModeLifDiv, false>;
+    case 3: return snn::fused_sparse_conv_lif_kernel<snn::kModeLifDiv, true>;
+    case 4: return snn::fused_sparse_conv_lif_kernel<snn::kModeIf, false>;
+    case 5: return snn::fused_sparse_conv_lif_kernel<snn::kModeIf, true>;
+    default: return snn::fused_sparse_conv_lif_kernel<snn::kModeNone, false>;
+  }
+}
+
 int ensure_init() {
   std::lock_guard<std::mutex> lk(g_init_mu);
   if (g_inited) return g_init_status;
@@ -55,9 +69,14 @@ int ensure_init() {
     return g_init_status = fail(SNN_E_CUDA, "cuTensorMapEncodeTiled unavailable");
   g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
   g_num_sms = prop.multiProcessorCount;
-  e = cudaFuncSetAttribute(snn::fused_sparse_conv_lif_kernel,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, snn::kSmemBytes);
-  if (e != cudaSuccess) return g_init_status = fail(SNN_E_CUDA, "smem attribute: %s", cudaGetErrorString(e));
+  for (int mode = 0; mode < 4; ++mode) {
+    for (int res = 0; res < (mode == snn::kModeNone ? 1 : 2); ++res) {
+      e = cudaFuncSetAttribute(conv_kernel_fn(mode, res != 0),
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, snn::kSmemBytes);
+      if (e != cudaSuccess)
+        return g_init_status = fail(SNN_E_CUDA, "smem attribute: %s", cudaGetErrorString(e));
+    }
+  }
   return g_init_status = SNN_OK;
 }
 
@@ -148,7 +167,6 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
   p.n_px_tiles = static_cast<int>(n_px);
   p.n_m = g.Fpad / snn::kBM;
   p.box_bytes = tw * th * tn * snn::kKB * 2;
-  p.out_box_bytes = tw * th * tn * snn::kBM * 2;
   const cuuint32_t box5[5] = {static_cast<cuuint32_t>(snn::kKB), static_cast<cuuint32_t>(tw),
                               static_cast<cuuint32_t>(th), static_cast<cuuint32_t>(tn), 1};
   {
@@ -173,22 +191,11 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
     }
   }
   const bool spikes = d->neuron != SNN_NEURON_NONE;
-  if (spikes) {  // output (and residual) spike tiles: (Cout, OW, OH, B, T) fp16
-    const size_t F = d->Cout, OW = g.OW, OH = g.OH, B = d->B;
-    cuuint64_t dims[5] = {F, OW, OH, B, static_cast<cuuint64_t>(d->T)};
-    cuuint64_t strides[4] = {F * 2, OW * F * 2, OH * OW * F * 2, B * OH * OW * F * 2};
-    cuuint32_t box[5] = {static_cast<cuuint32_t>(snn::kBM), static_cast<cuuint32_t>(tw),
-                         static_cast<cuuint32_t>(th), static_cast<cuuint32_t>(tn), 1};
-    if ((st = encode(&p.tmap_out, 5, out, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE))) return st;
-    if (residual &&
-        (st = encode(&p.tmap_res, 5, residual, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE)))
-      return st;
-  } else {
-    p.out_f32 = static_cast<float*>(out);
-  }
+  if (spikes) p.out = static_cast<__half*>(out);
+  else p.out_f32 = static_cast<float*>(out);
+  p.residual = static_cast<const __half*>(residual);
   p.meta = reinterpret_cast<const uint32_t*>(wbytes + meta_offset(g));
   p.scale = scale; p.bias = bias; p.state = state;
-  p.has_res = residual != nullptr;
   unsigned* err = nullptr;
   if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_device_err) != cudaSuccess)
     return fail(SNN_E_CUDA, "error word address");
@@ -196,23 +203,27 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
   p.F = d->Cout; p.KW = d->KW; p.stride = d->stride; p.pad = d->pad;
   p.n_kb = g.n_kb; p.cin_blocks = g.cin_blocks;
   p.B = d->B; p.OH = g.OH; p.OW = g.OW; p.T = d->T;
-  p.neuron = d->neuron; p.flags = d->flags;
+  p.flags = d->flags;
   p.tau = d->tau;
   // Reference computes (1.0 - 1.0/tau) in double, then float32 (models/neurons.py:125).
   p.decay = d->neuron == SNN_NEURON_LIF
                 ? static_cast<float>(1.0 - 1.0 / static_cast<double>(d->tau)) : 1.0f;
   int e2 = 0;
   const float mant = frexpf(d->tau, &e2);
-  p.tau_pow2 = (d->neuron == SNN_NEURON_LIF && mant == 0.5f) ? 1 : 0;
-  p.inv_tau = p.tau_pow2 ? 1.0f / d->tau : 0.0f;
+  const bool tau_pow2 = d->neuron == SNN_NEURON_LIF && mant == 0.5f;
+  p.inv_tau = tau_pow2 ? 1.0f / d->tau : 0.0f;
   p.v_th = d->v_threshold; p.v_reset = d->v_reset;
-  p.timeout_ns = 1000000000ull;
+  p.timeout_ns = 4000000000ull;   // SM cycles (~2 s at the highest clock)
+  const int mode = d->neuron == SNN_NEURON_NONE ? snn::kModeNone
+                   : d->neuron == SNN_NEURON_IF ? snn::kModeIf
+                   : tau_pow2 ? snn::kModeLifMul : snn::kModeLifDiv;
 
   const int per_m = std::max(1, std::min(p.n_px_tiles, g_num_sms / p.n_m));
   const long long grid = static_cast<long long>(per_m) * p.n_m;
   if (grid > 0x7fffffffLL) return fail(SNN_E_INVALID, "grid too large");
-  snn::fused_sparse_conv_lif_kernel<<<static_cast<unsigned>(grid), snn::kThreads, snn::kSmemBytes,
-                                       static_cast<cudaStream_t>(stream)>>>(p);
+  conv_kernel_fn(mode, residual != nullptr)<<<static_cast<unsigned>(grid), snn::kThreads,
+                                               snn::kSmemBytes,
+                                               static_cast<cudaStream_t>(stream)>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));
   return SNN_OK;
@@ -329,9 +340,10 @@ int snn_stem_forward(const snn_conv_desc* d, int32_t Tin, const float* x, const 
   int st = ensure_init();
   if (st) return st;
   if (!d || !x || !w || !bn_scale || !bn_bias || !out) return fail(SNN_E_INVALID, "null pointer");
-  if (d->T < 1 || d->B < 1 || d->Cin < 1 || d->Cin > 16 || d->Cout < 1 || d->Cout > 1024 ||
-      d->KH < 1 || d->KW < 1 || d->KH * d->KW * d->Cin > 192 || d->stride < 1 || d->pad < 0)
-    return fail(SNN_E_INVALID, "unsupported stem geometry");
+  if (d->T < 1 || d->B < 1 || d->Cin < 1 || d->Cout < 8 || d->Cout % 8 || d->Cout > 2048 ||
+      d->KH < 1 || d->KW < 1 || d->stride < 1 || d->pad < 0 ||
+      static_cast<long long>(d->KH) * d->KW * d->Cin * d->Cout > 12288)
+    return fail(SNN_E_INVALID, "unsupported stem geometry (Cout multiple of 8, K*Cout <= 12288)");
   if (Tin != 1 && Tin != d->T) return fail(SNN_E_INVALID, "Tin must be 1 or T");
   if (d->neuron == SNN_NEURON_NONE) return fail(SNN_E_INVALID, "stem needs a neuron");
   const int OH = (d->H + 2 * d->pad - d->KH) / d->stride + 1;
@@ -346,11 +358,13 @@ int snn_stem_forward(const snn_conv_desc* d, int32_t Tin, const float* x, const 
   p.tau = d->tau; p.decay = static_cast<float>(1.0 - 1.0 / static_cast<double>(d->tau));
   p.v_th = d->v_threshold; p.v_reset = d->v_reset;
   const long long pixels = static_cast<long long>(d->B) * OH * OW;
-  const int px_per_block = 4;
-  dim3 block(64, px_per_block);
-  dim3 grid(static_cast<unsigned>((pixels + px_per_block - 1) / px_per_block),
-            (d->Cout + 63) / 64);
-  const size_t smem = static_cast<size_t>(64) * d->KH * d->KW * d->Cin * sizeof(float);
+  const int px_per_block = 256 / (d->Cout / 8);
+  if (px_per_block < 1) return fail(SNN_E_INVALID, "stem Cout too large");
+  const long long nblk = (pixels + px_per_block - 1) / px_per_block;
+  if (nblk > 0x7fffffffLL) return fail(SNN_E_INVALID, "stem grid too large");
+  dim3 block(256);
+  dim3 grid(static_cast<unsigned>(nblk));
+  const size_t smem = static_cast<size_t>(d->KH) * d->KW * d->Cin * d->Cout * sizeof(float);
   snn::stem_conv_lif_kernel<<<grid, block, smem, static_cast<cudaStream_t>(stream)>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));

@@ -31,7 +31,7 @@ constexpr int kBM = 128;             // output channels per tile (UMMA M)
 constexpr int kBN = 64;              // output pixels per timestep per tile (UMMA N)
 constexpr int kTC = 2;               // timesteps per accumulator buffer
 constexpr int kNumAcc = 2;           // accumulator buffers
-constexpr int kStages = 6;           // smem pipeline depth
+constexpr int kStages = 8;           // smem pipeline depth
 constexpr int kKB = 64;              // logical K per k-block (one 128B activation row)
 constexpr int kABytes = kBM * (kKB / 2) * 2;     // 8 KB compressed weights
 constexpr int kBBytes = kBN * kKB * 2;           // 8 KB activations per timestep
@@ -43,11 +43,14 @@ constexpr int kMaxMetaCols = kTmemCols - kMetaCol;  // => K <= 8192
 constexpr int kEpiWarps = 8;
 constexpr int kEpiThreads = kEpiWarps * 32;
 constexpr int kThreads = 64 + kEpiThreads;
-constexpr int kTileBytes = kBN * kBM * 2;        // fp16 [pixel][cout] staging tile
+constexpr int kXposeBytes = 32 * 32 * 2;         // per-warp [32 px][32 cout] fp16 transpose
 constexpr int kBarBytes = 512;
-constexpr int kSmemBytes = kStages * kStageBytes + 4 * kTileBytes + kBarBytes + 1024;
+constexpr int kSmemBytes = kStages * kStageBytes + kEpiWarps * kXposeBytes + kBarBytes + 1024;
 
 enum NeuronKind : int { kLIF = 0, kIF = 1, kNoNeuron = 2 };
+// Epilogue variants (template parameter): LIF with x*(1/tau) (exact when tau
+// is a power of two), LIF with x/tau, IF, and BN output without neuron.
+enum EpiMode : int { kModeLifMul = 0, kModeLifDiv = 1, kModeIf = 2, kModeNone = 3 };
 enum ConvFlags : int { kReadState = 1, kWriteState = 2 };
 enum ErrCode : unsigned { kErrTimeoutFull = 1u, kErrTimeoutEmpty = 2u, kErrTimeoutAcc = 4u,
                           kErrTimeoutMeta = 8u, kErrTimeoutAccEmpty = 16u, kErrTimeoutDrain = 32u,
@@ -56,12 +59,12 @@ enum ErrCode : unsigned { kErrTimeoutFull = 1u, kErrTimeoutEmpty = 2u, kErrTimeo
 struct ConvParams {
   CUtensorMap tmap_a;        // compressed weights [Fpad][K/2] fp16 (2D)
   CUtensorMap tmap_b[4];     // activations (C, W', H', B, T), one map per stride parity
-  CUtensorMap tmap_out;      // output spikes (Cout, OW, OH, B, T) fp16
-  CUtensorMap tmap_res;      // residual, same geometry as the output
   const uint32_t* meta;      // [Fpad/128][K/32][128]
   const float* scale;        // [F]
   const float* bias;         // [F]
   float* state;              // [B*OH*OW][F] or null
+  __half* out;               // [T*B*OH*OW][F] fp16 spikes (+ residual)
+  const __half* residual;    // [T*B*OH*OW][F] fp16 or null
   float* out_f32;            // [T*B*OH*OW][F] (neuron == kNoNeuron only)
   unsigned* err;             // device error word
   int F, KW, stride, pad;
@@ -70,10 +73,9 @@ struct ConvParams {
   int tw, th, tn;            // tile extent (output coords) along w, h, image
   int tiles_w, tiles_h, n_px_tiles, n_m;
   int box_bytes;             // bytes of one activation TMA box (tw*th*tn*128)
-  int out_box_bytes;         // bytes of one output/residual TMA box (tw*th*tn*256)
-  int neuron, flags, has_res, tau_pow2;
+  int flags;
   float decay, tau, inv_tau, v_th, v_reset;
-  unsigned long long timeout_ns;
+  unsigned long long timeout_ns;   // bounded-wait budget, in SM clock cycles
 };
 
 __device__ __forceinline__ int floordiv2(int d) { return (d - (d & 1)) / 2; }
@@ -90,6 +92,7 @@ __device__ __forceinline__ TileCoord tile_coord(const ConvParams& p, int pt) {
   return c;
 }
 
+template <int MODE, bool RES>
 __global__ void __launch_bounds__(kThreads, 1)
 fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -97,14 +100,12 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* sA = smem;                                        // kStages x kABytes
   uint8_t* sB = smem + kStages * kABytes;                    // kStages x kTC x kBBytes
-  uint8_t* sOut = smem + kStages * kStageBytes;              // 2 x kTileBytes
-  uint8_t* sRes = sOut + 2 * kTileBytes;                     // 2 x kTileBytes
-  uint64_t* full = reinterpret_cast<uint64_t*>(sRes + 2 * kTileBytes);
+  uint8_t* sX = smem + kStages * kStageBytes;                // kEpiWarps x kXposeBytes
+  uint64_t* full = reinterpret_cast<uint64_t*>(sX + kEpiWarps * kXposeBytes);
   uint64_t* empty = full + kStages;
   uint64_t* acc_full = empty + kStages;                      // [kNumAcc]
   uint64_t* acc_empty = acc_full + kNumAcc;                  // [kNumAcc]
-  uint64_t* res_full = acc_empty + kNumAcc;                  // [2]
-  uint64_t* meta_ready = res_full + 2;
+  uint64_t* meta_ready = acc_empty + kNumAcc;
   uint64_t* drain = meta_ready + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -121,7 +122,6 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
     for (int b = 0; b < kNumAcc; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], kEpiThreads); }
-    mbar_init(&res_full[0], 1); mbar_init(&res_full[1], 1);
     mbar_init(meta_ready, 128);
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -130,8 +130,6 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&p.tmap_a);
     for (int i = 0; i < (p.stride == 2 ? 4 : 1); ++i) prefetch_tmap(&p.tmap_b[i]);
-    if (p.neuron != kNoNeuron) prefetch_tmap(&p.tmap_out);
-    if (p.has_res) prefetch_tmap(&p.tmap_res);
   }
   if (warp == 1) { tmem_alloc(tmem_slot, kTmemCols); tmem_relinquish(); }
   tc_fence_before();
@@ -241,8 +239,6 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
     const int q = warp & 3;                      // TMEM lane quarter of this warp
     const int half = e >> 2;                     // which 32 pixel columns
     const int row = q * 32 + lane;               // output channel within the tile
-    const int et = threadIdx.x - 64;             // 0..255
-    const bool leader = (et == 0);
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
     if (half == 0) {
       const uint32_t* src = p.meta + (static_cast<size_t>(m_tile) * n_meta) * kBM + row;
@@ -264,7 +260,12 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
     const float bi = cvalid ? p.bias[cout] : 0.f;
     const long long P = static_cast<long long>(p.B) * p.OH * p.OW;
     const int tile_px = p.tw * p.th;
-    const bool spikes_out = p.neuron != kNoNeuron;
+    const int cbase = m_tile * kBM + q * 32;     // first output channel of this warp
+    const int nchunk8 = max(0, min(4, (p.F - cbase) / 8));   // valid 8-channel chunks
+    uint8_t* xb = sX + e * kXposeBytes;
+    // Swizzled [px][cout] fp16 layout: 64-byte rows, 16-byte chunks XOR-ed with
+    // (px>>1)&3 so both the column writes and the row reads are conflict-free.
+    auto xoff = [](int px, int c8) { return px * 64 + ((c8 ^ ((px >> 1) & 3)) << 4); };
 
     auto pixel_of = [&](const TileCoord& tc, int col) -> long long {
       const int dn = col / tile_px;
@@ -275,31 +276,18 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
       if (dn >= p.tn || n >= p.B || oh >= p.OH || ow >= p.OW) return -1;
       return (static_cast<long long>(n) * p.OH + oh) * p.OW + ow;
     };
-    // The epilogue visits (tile, t) in a fixed order; the leader prefetches the
-    // residual tile of the next visit.
-    auto issue_res = [&](int pt, int t, int b) {
-      const TileCoord tc = tile_coord(p, pt);
-      mbar_arrive_expect_tx(&res_full[b], p.out_box_bytes);
-      tma_load_5d(sRes + b * kTileBytes, &p.tmap_res, &res_full[b], m_tile * kBM, tc.w0, tc.h0,
-                  tc.n0, t);
-    };
-    uint32_t res_issued = 0;
-    if (p.has_res && leader && first_pt < p.n_px_tiles) { issue_res(first_pt, 0, 0); ++res_issued; }
 
-    uint32_t u = 0;           // timestep visits so far (staging / residual buffer index)
     int acc_iter = 0;
     bool stop = false;
     for (int pt = first_pt; pt < p.n_px_tiles && !stop; pt += pt_step) {
       const TileCoord tc = tile_coord(p, pt);
+      // In the transposed phase lane l owns pixel column half*32 + l.
+      const long long my_px = pixel_of(tc, half * 32 + lane);
       float v[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        float v0 = 0.f;
-        if ((p.flags & kReadState) && cvalid) {
-          const long long px = pixel_of(tc, half * 32 + i);
-          if (px >= 0) v0 = p.state[px * p.F + cout];
-        }
-        v[i] = v0;
+        const long long px = __shfl_sync(0xffffffffu, my_px, i);
+        v[i] = ((p.flags & kReadState) && cvalid && px >= 0) ? p.state[px * p.F + cout] : 0.f;
       }
       for (int c = 0; c < n_chunks && !stop; ++c) {
         const int t0 = c * kTC;
@@ -307,83 +295,79 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
         const int buf = acc_iter & 1;
         const uint32_t use = static_cast<uint32_t>(acc_iter >> 1);
         bool fail = !mbar_wait_bounded(&acc_full[buf], use & 1, p.timeout_ns);
-        if (fail) atomicOr(p.err, kErrTimeoutAcc);
+        fail = __any_sync(0xffffffffu, fail || *abort_flag);
+        if (fail) { atomicOr(p.err, kErrTimeoutAcc); stop = true; break; }
         tc_fence_after();
         for (int tt = 0; tt < tcn; ++tt) {
-          const int t = t0 + tt;
-          const int sb = u & 1;
-          if (spikes_out && leader) bulk_wait_group_read<1>();   // staging[sb] free again
-          if (named_barrier_or(1, kEpiThreads, fail || *abort_flag)) { stop = true; break; }
-          if (p.has_res && leader) {
-            // Next visit: (pt, t+1), or the first timestep of the next tile.
-            int npt = pt, nt = t + 1;
-            if (nt >= p.T) { npt = pt + pt_step; nt = 0; }
-            if (npt < p.n_px_tiles) { issue_res(npt, nt, sb ^ 1); ++res_issued; }
+          const size_t tbase = static_cast<size_t>(t0 + tt) * P;
+          // Residual row of this lane's pixel (64 B), fetched before the TMEM
+          // load so its latency overlaps the neuron update.
+          uint4 r4[4];
+          if constexpr (RES) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) r4[k] = make_uint4(0, 0, 0, 0);
+            if (my_px >= 0) {
+              const uint4* rp = reinterpret_cast<const uint4*>(
+                  p.residual + (tbase + my_px) * p.F + cbase);
+#pragma unroll
+              for (int k = 0; k < 4; ++k) if (k < nchunk8) r4[k] = __ldg(rp + k);
+            }
           }
-          __half* stg = reinterpret_cast<__half*>(sOut + sb * kTileBytes);
-          const __half* resb = reinterpret_cast<const __half*>(sRes + sb * kTileBytes);
           float acc[32];
           tmem_ld32(lane_base + buf * kAccCols + tt * kBN + half * 32, acc);
-          bool rfail = false;
-          if (p.has_res)
-            rfail = !mbar_wait_bounded(&res_full[sb], (u >> 1) & 1, p.timeout_ns);
-          if (rfail) atomicOr(p.err, kErrTimeoutRes);
-          if (spikes_out) {
+          if constexpr (MODE == kModeNone) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const long long px = __shfl_sync(0xffffffffu, my_px, i);
+              if (cvalid && px >= 0) p.out_f32[(tbase + px) * p.F + cout] = fmaf(acc[i], sc, bi);
+            }
+          } else {
+            // Neuron update, lane = output channel, i = pixel column.
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
               const float x = fmaf(acc[i], sc, bi);
-              // Reference order v*(1-1/tau) + x/tau, each op rounded (no FMA);
-              // x*(1/tau) equals x/tau exactly when tau is a power of two.
+              // Reference order v*(1-1/tau) + x/tau with each op rounded (no FMA).
               float h;
-              if (p.neuron == kLIF) {
-                const float xin = p.tau_pow2 ? __fmul_rn(x, p.inv_tau) : __fdiv_rn(x, p.tau);
-                h = __fadd_rn(__fmul_rn(v[i], p.decay), xin);
-              } else {
-                h = __fadd_rn(v[i], x);
-              }
+              if constexpr (MODE == kModeLifMul) h = __fadd_rn(__fmul_rn(v[i], p.decay), __fmul_rn(x, p.inv_tau));
+              else if constexpr (MODE == kModeLifDiv) h = __fadd_rn(__fmul_rn(v[i], p.decay), __fdiv_rn(x, p.tau));
+              else h = __fadd_rn(v[i], x);
               const bool spike = (h - p.v_th) >= 0.f;
               v[i] = spike ? p.v_reset : h;
-              float y = spike ? 1.f : 0.f;
-              const int off = (half * 32 + i) * kBM + row;
-              if (p.has_res) y += __half2float(resb[off]);
-              stg[off] = __float2half_rn(y);
+              *reinterpret_cast<__half*>(xb + xoff(i, lane >> 3) + (lane & 7) * 2) =
+                  __ushort_as_half(spike ? 0x3C00 : 0);
             }
-            fence_proxy_async_smem();
-          } else if (cvalid) {
-            const size_t tbase = static_cast<size_t>(t) * P;
+            __syncwarp();
+            // Row phase: lane owns pixel half*32+lane, 32 channels = 4 x 16 B.
+            uint4 o4[4];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const long long px = pixel_of(tc, half * 32 + i);
-              if (px >= 0) p.out_f32[(tbase + px) * p.F + cout] = fmaf(acc[i], sc, bi);
+            for (int k = 0; k < 4; ++k) o4[k] = *reinterpret_cast<const uint4*>(xb + xoff(lane, k));
+            if constexpr (RES) {
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                __half2* a = reinterpret_cast<__half2*>(&o4[k]);
+                const __half2* b = reinterpret_cast<const __half2*>(&r4[k]);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) a[j] = __hadd2(a[j], b[j]);
+              }
             }
+            if (my_px >= 0) {
+              uint4* op = reinterpret_cast<uint4*>(p.out + (tbase + my_px) * p.F + cbase);
+#pragma unroll
+              for (int k = 0; k < 4; ++k) if (k < nchunk8) op[k] = o4[k];
+            }
+            __syncwarp();
           }
-          if (named_barrier_or(2, kEpiThreads, rfail)) { stop = true; break; }
-          if (spikes_out && leader) {
-            tma_store_5d(&p.tmap_out, sOut + sb * kTileBytes, m_tile * kBM, tc.w0, tc.h0, tc.n0, t);
-            bulk_commit_group();
-          }
-          ++u;
         }
-        if (stop) break;
         tc_fence_before();
         mbar_arrive(&acc_empty[buf]);
         ++acc_iter;
       }
-      if (!stop && (p.flags & kWriteState) && cvalid) {
+      if (!stop && (p.flags & kWriteState)) {
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const long long px = pixel_of(tc, half * 32 + i);
-          if (px >= 0) p.state[px * p.F + cout] = v[i];
+          const long long px = __shfl_sync(0xffffffffu, my_px, i);
+          if (cvalid && px >= 0) p.state[px * p.F + cout] = v[i];
         }
-      }
-    }
-    if (leader) {
-      bulk_wait_group<0>();
-      // After an abort, let a residual prefetch that no visit consumed land.
-      if (p.has_res && res_issued > u) {
-        const uint32_t last = res_issued - 1;
-        if (!mbar_wait_bounded(&res_full[last & 1], (last >> 1) & 1, p.timeout_ns))
-          atomicOr(p.err, kErrTimeoutRes);
       }
     }
     if (stop) *abort_flag = 1;

@@ -19,53 +19,77 @@ struct StemParams {
   float tau, decay, v_th, v_reset;
 };
 
-// block = (64 output channels, 4 pixels); dynamic smem = 64 * KH*KW*Cin floats.
-__global__ void stem_conv_lif_kernel(const StemParams p) {
+// One thread = one output pixel x 8 consecutive output channels; a block of
+// 256 threads covers 256/(Cout/8) pixels.  Weights are staged in shared
+// memory as [k][cout] (dynamic smem = K*Cout floats, K = Cin*KH*KW); each
+// timestep's 8 spikes leave as one 16-byte store.
+__global__ void __launch_bounds__(256)
+stem_conv_lif_kernel(const StemParams p) {
   extern __shared__ float ws[];
   const int K = p.KH * p.KW * p.Cin;
-  const int c_base = blockIdx.y * 64;
-  const int tid = threadIdx.y * blockDim.x + threadIdx.x;
-  for (int i = tid; i < 64 * K; i += blockDim.x * blockDim.y) {
-    const int cl = i / K, k = i - cl * K;
-    const int co = c_base + cl;
-    ws[i] = co < p.Cout ? p.w[static_cast<size_t>(co) * K + k] : 0.f;
+  for (int i = threadIdx.x; i < K * p.Cout; i += blockDim.x) {
+    const int k = i / p.Cout, co = i - k * p.Cout;
+    // k = (ci*KH + kh)*KW + kw, matching the [Cout][Cin][KH][KW] source.
+    ws[i] = p.w[static_cast<size_t>(co) * K + k];
   }
   __syncthreads();
-  const int cout = c_base + threadIdx.x;
-  const long long pix = static_cast<long long>(blockIdx.x) * blockDim.y + threadIdx.y;
+  const int groups = p.Cout / 8;
+  const int px_per_block = blockDim.x / groups;
+  const int g = threadIdx.x % groups;
+  const long long pix = static_cast<long long>(blockIdx.x) * px_per_block + threadIdx.x / groups;
   const long long P = static_cast<long long>(p.B) * p.OH * p.OW;
-  if (cout >= p.Cout || pix >= P) return;
+  if (threadIdx.x >= px_per_block * groups || pix >= P) return;
   const int ow = static_cast<int>(pix % p.OW);
   const int oh = static_cast<int>((pix / p.OW) % p.OH);
   const int b = static_cast<int>(pix / (static_cast<long long>(p.OW) * p.OH));
-  const float sc = p.scale[cout], bi = p.bias[cout];
-  const float* wr = ws + threadIdx.x * K;
-  float v = 0.f, x_bn = 0.f;
+  const int c0 = g * 8;
+  float sc[8], bi[8], v[8], xb[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) { sc[j] = p.scale[c0 + j]; bi[j] = p.bias[c0 + j]; v[j] = 0.f; xb[j] = 0.f; }
   for (int t = 0; t < p.T; ++t) {
     if (t == 0 || p.Tin > 1) {
-      const float* xb = p.x + (static_cast<size_t>(p.Tin > 1 ? t : 0) * p.B + b) *
-                                  static_cast<size_t>(p.Cin) * p.H * p.W;
-      float acc = 0.f;
+      const float* xin = p.x + (static_cast<size_t>(p.Tin > 1 ? t : 0) * p.B + b) *
+                                   static_cast<size_t>(p.Cin) * p.H * p.W;
+      float acc[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+      int k = 0;
       for (int ci = 0; ci < p.Cin; ++ci) {
         for (int kh = 0; kh < p.KH; ++kh) {
           const int ih = oh * p.stride + kh - p.pad;
-          if (ih < 0 || ih >= p.H) continue;
-          for (int kw = 0; kw < p.KW; ++kw) {
+          for (int kw = 0; kw < p.KW; ++kw, ++k) {
             const int iw = ow * p.stride + kw - p.pad;
-            if (iw < 0 || iw >= p.W) continue;
-            acc = fmaf(xb[(static_cast<size_t>(ci) * p.H + ih) * p.W + iw],
-                       wr[(ci * p.KH + kh) * p.KW + kw], acc);
+            if (ih < 0 || ih >= p.H || iw < 0 || iw >= p.W) continue;
+            const float xv = __ldg(xin + (static_cast<size_t>(ci) * p.H + ih) * p.W + iw);
+            const float4 w0 = *reinterpret_cast<const float4*>(ws + k * p.Cout + c0);
+            const float4 w1 = *reinterpret_cast<const float4*>(ws + k * p.Cout + c0 + 4);
+            acc[0] = fmaf(xv, w0.x, acc[0]); acc[1] = fmaf(xv, w0.y, acc[1]);
+            acc[2] = fmaf(xv, w0.z, acc[2]); acc[3] = fmaf(xv, w0.w, acc[3]);
+            acc[4] = fmaf(xv, w1.x, acc[4]); acc[5] = fmaf(xv, w1.y, acc[5]);
+            acc[6] = fmaf(xv, w1.z, acc[6]); acc[7] = fmaf(xv, w1.w, acc[7]);
           }
         }
       }
-      x_bn = fmaf(acc, sc, bi);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) xb[j] = fmaf(acc[j], sc[j], bi[j]);
     }
-    float h;
-    if (p.neuron == 0) h = __fadd_rn(__fmul_rn(v, p.decay), __fdiv_rn(x_bn, p.tau));
-    else h = __fadd_rn(v, x_bn);
-    const bool s = (h - p.v_th) >= 0.f;
-    v = s ? p.v_reset : h;
-    p.out[(static_cast<size_t>(t) * P + pix) * p.Cout + cout] = __float2half_rn(s ? 1.f : 0.f);
+    uint32_t packed[4];
+#pragma unroll
+    for (int j = 0; j < 8; j += 2) {
+      uint32_t bits = 0;
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        float h;
+        if (p.neuron == 0) h = __fadd_rn(__fmul_rn(v[j + u], p.decay), __fdiv_rn(xb[j + u], p.tau));
+        else h = __fadd_rn(v[j + u], xb[j + u]);
+        const bool s = (h - p.v_th) >= 0.f;
+        v[j + u] = s ? p.v_reset : h;
+        bits |= (s ? 0x3C00u : 0u) << (16 * u);
+      }
+      packed[j / 2] = bits;
+    }
+    *reinterpret_cast<uint4*>(p.out + (static_cast<size_t>(t) * P + pix) * p.Cout + c0) =
+        make_uint4(packed[0], packed[1], packed[2], packed[3]);
   }
 }
 

@@ -41,15 +41,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: spins until the phase with `parity` completes or
-// `timeout_ns` of wall time passes.  Returns false on timeout.
+// Bounded wait: spins until the phase with `parity` completes or about
+// `timeout_cycles` SM clock cycles pass (checked every 64 polls so the
+// fast path stays a bare try_wait loop).  Returns false on timeout.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
-                                                  uint64_t timeout_ns) {
+                                                  uint64_t timeout_cycles) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
+  const long long t0 = clock64();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer_ns() - t0 > timeout_ns) return false;
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (static_cast<uint64_t>(clock64() - t0) > timeout_cycles) return false;
   }
 }
 
