@@ -44,7 +44,10 @@ enum {
 };
 
 enum { SNN_NEURON_LIF = 0, SNN_NEURON_IF = 1, SNN_NEURON_NONE = 2 };
-enum { SNN_FLAG_READ_STATE = 1, SNN_FLAG_WRITE_STATE = 2 };
+enum { SNN_FLAG_READ_STATE = 1, SNN_FLAG_WRITE_STATE = 2,
+       /* Always use the general kernel (streamed weights, per-tap activation
+        * tiles) even where the halo kernel applies; for testing. */
+       SNN_FLAG_FORCE_GENERIC = 4 };
 
 /* One fused layer.  Linear layers are 1x1 convs over H=1, W=rows, B=1. */
 typedef struct snn_conv_desc {

@@ -14,6 +14,7 @@
 
 #include "../../include/snn_b200.h"
 #include "snn_conv.cuh"
+#include "snn_conv_halo.cuh"
 #include "snn_glue.cuh"
 
 namespace {
@@ -50,6 +51,28 @@ ConvKernel conv_kernel_fn(int mode, bool res) {
   }
 }
 
+using HaloKernel = void (*)(const snn::HaloParams);
+
+template <int BN>
+HaloKernel halo_kernel_fn_bn(int mode, bool res) {
+  switch (mode * 2 + (res ? 1 : 0)) {
+    case 0: return snn::fused_sparse_conv_halo_kernel<snn::kModeLifMul, false, BN>;
+    case 1: return snn::fused_sparse_conv_halo_kernel<snn::kModeLifMul, true, BN>;
+    case 2: return snn::fused_sparse_conv_halo_kernel<snn::kModeLifDiv, false, BN>;
+    case 3: return snn::fused_sparse_conv_halo_kernel<snn::kModeLifDiv, true, BN>;
+    case 4: return snn::fused_sparse_conv_halo_kernel<snn::kModeIf, false, BN>;
+    case 5: return snn::fused_sparse_conv_halo_kernel<snn::kModeIf, true, BN>;
+    default: return snn::fused_sparse_conv_halo_kernel<snn::kModeNone, false, BN>;
+  }
+}
+
+HaloKernel halo_kernel_fn(int bn, int mode, bool res) {
+  return bn == 128 ? halo_kernel_fn_bn<128>(mode, res) : halo_kernel_fn_bn<64>(mode, res);
+}
+
+constexpr int kSmemLimit = 232448;          // opt-in dynamic smem per block on sm_100
+constexpr int kHaloMaxWeightBytes = 160 * 1024;
+
 int ensure_init() {
   std::lock_guard<std::mutex> lk(g_init_mu);
   if (g_inited) return g_init_status;
@@ -75,6 +98,12 @@ int ensure_init() {
                                cudaFuncAttributeMaxDynamicSharedMemorySize, snn::kSmemBytes);
       if (e != cudaSuccess)
         return g_init_status = fail(SNN_E_CUDA, "smem attribute: %s", cudaGetErrorString(e));
+      for (int bn : {64, 128}) {
+        e = cudaFuncSetAttribute(halo_kernel_fn(bn, mode, res != 0),
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+        if (e != cudaSuccess)
+          return g_init_status = fail(SNN_E_CUDA, "smem attribute: %s", cudaGetErrorString(e));
+      }
     }
   }
   return g_init_status = SNN_OK;
@@ -218,6 +247,48 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
                    : d->neuron == SNN_NEURON_IF ? snn::kModeIf
                    : tau_pow2 ? snn::kModeLifMul : snn::kModeLifDiv;
 
+  // Halo variant: stride-1 odd square kernels with "same" padding whose
+  // 128-channel weight slice fits in shared memory and images tall enough
+  // for 8-row tiles.
+  const int a_bytes = g.n_kb * snn::kABytes;
+  const bool halo = d->stride == 1 && d->KH == d->KW && (d->KH & 1) && d->KH > 1 &&
+                    d->pad == d->KH / 2 && a_bytes <= kHaloMaxWeightBytes && g.OH >= 8 &&
+                    !(d->flags & SNN_FLAG_FORCE_GENERIC);
+  if (halo) {
+    snn::HaloParams hp;
+    memset(&hp, 0, sizeof(hp));
+    const int bn = g.OH >= 16 ? 128 : 64;
+    const int th_ = bn / 8;
+    hp.KH = d->KH;
+    hp.halo_w = 8 + d->KW - 1;
+    hp.halo_bytes = hp.halo_w * (th_ + d->KH - 1) * snn::kKB * 2;
+    hp.halo_stride = (hp.halo_bytes + 1023) / 1024 * 1024;
+    hp.a_bytes = a_bytes;
+    const int fixed = 1024 + 512 + snn::kEpiWarps * snn::kXposeBytes + a_bytes;
+    hp.halo_stages = std::min(snn::kHaloMaxStages, (kSmemLimit - fixed) / hp.halo_stride);
+    if (hp.halo_stages >= 2) {
+      p.tw = 8; p.th = th_; p.tn = 1;
+      p.tiles_w = (g.OW + 7) / 8;
+      p.tiles_h = (g.OH + th_ - 1) / th_;
+      p.n_px_tiles = p.tiles_w * p.tiles_h * d->B;
+      const size_t C = d->Cin, W = d->W, H = d->H, B = d->B;
+      cuuint64_t dims[5] = {C, W, H, B, static_cast<cuuint64_t>(d->T)};
+      cuuint64_t strides[4] = {C * 2, W * C * 2, H * W * C * 2, B * H * W * C * 2};
+      cuuint32_t box[5] = {static_cast<cuuint32_t>(snn::kKB), static_cast<cuuint32_t>(hp.halo_w),
+                           static_cast<cuuint32_t>(th_ + d->KH - 1), 1, 1};
+      if ((st = encode(&p.tmap_b[0], 5, data, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)))
+        return st;
+      hp.c = p;
+      const size_t smem = static_cast<size_t>(fixed) + static_cast<size_t>(hp.halo_stages) * hp.halo_stride;
+      const int per_m = std::max(1, std::min(p.n_px_tiles, g_num_sms / p.n_m));
+      const long long grid = static_cast<long long>(per_m) * p.n_m;
+      halo_kernel_fn(bn, mode, residual != nullptr)<<<static_cast<unsigned>(grid), snn::kThreads,
+                                                      smem, static_cast<cudaStream_t>(stream)>>>(hp);
+      cudaError_t e = cudaGetLastError();
+      if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));
+      return SNN_OK;
+    }
+  }
   const int per_m = std::max(1, std::min(p.n_px_tiles, g_num_sms / p.n_m));
   const long long grid = static_cast<long long>(per_m) * p.n_m;
   if (grid > 0x7fffffffLL) return fail(SNN_E_INVALID, "grid too large");

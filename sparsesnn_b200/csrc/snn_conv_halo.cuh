@@ -1,0 +1,308 @@
+// Halo variant of the fused 2:4-sparse conv for stride-1 KxK convolutions
+// whose per-tile weights fit in shared memory (e.g. 3x3 with Cin <= 128).
+//
+// Differences from the generic kernel (snn_conv.cuh):
+//  * the CTA's 128-channel weight slice (all k-blocks) is loaded ONCE into
+//    shared memory and stays resident for the CTA's lifetime;
+//  * a tile is 8 output columns x BN/8 output rows of one image; for each
+//    (timestep, 64-channel slice) ONE TMA box loads the (8+KW-1) x (BN/8+KH-1)
+//    input halo, and every filter tap reads it through a descriptor that
+//    starts at row offset (kh*(8+KW-1) + kw) with a group stride of one halo
+//    row (the 128-byte swizzle is a function of the absolute shared-memory
+//    address, so operands may start at any 128-byte row);
+//  * timesteps are the outer loop (one BN-column accumulator); the epilogue
+//    copies the accumulator to registers and releases it before the neuron
+//    update, so the next timestep's MMAs overlap the epilogue.
+#pragma once
+#include "snn_conv.cuh"
+
+namespace snn {
+
+constexpr int kHaloMaxStages = 8;
+constexpr int kHaloMetaCol = 128;        // accumulator: columns [0,128); metadata after
+constexpr int kHaloTmemCols = 256;
+
+struct HaloParams {
+  ConvParams c;              // shared fields (tmap_a, tmap_b[0], meta, scale, ...)
+  int KH;
+  int halo_w;                // 8 + KW - 1 (pixels per halo row)
+  int halo_bytes;            // bytes one halo box delivers
+  int halo_stride;           // smem bytes per halo stage (1024-aligned)
+  int halo_stages;
+  int a_bytes;               // resident weight bytes (n_kb * kABytes)
+};
+
+template <int MODE, bool RES, int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
+  const ConvParams& p = hp.c;
+  constexpr int G = BN / 64;                 // 32-column groups per epilogue warp
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;                                              // resident weights
+  uint8_t* sH = smem + hp.a_bytes;                                 // halo stages
+  uint8_t* sX = sH + hp.halo_stages * hp.halo_stride;              // epilogue transposes
+  uint64_t* full = reinterpret_cast<uint64_t*>(sX + kEpiWarps * kXposeBytes);
+  uint64_t* empty = full + kHaloMaxStages;
+  uint64_t* a_full = empty + kHaloMaxStages;
+  uint64_t* acc_full = a_full + 1;
+  uint64_t* acc_empty = acc_full + 1;
+  uint64_t* meta_ready = acc_empty + 1;
+  uint64_t* drain = meta_ready + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int m_tile = blockIdx.x % p.n_m;
+  const int first_pt = blockIdx.x / p.n_m;
+  const int pt_step = gridDim.x / p.n_m;
+  const int n_meta = 2 * p.n_kb;
+  const int S = hp.halo_stages;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    mbar_init(a_full, 1);
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, kEpiThreads);
+    mbar_init(meta_ready, 128);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) { prefetch_tmap(&p.tmap_a); prefetch_tmap(&p.tmap_b[0]); }
+  if (warp == 1) { tmem_alloc(tmem_slot, kHaloTmemCols); tmem_relinquish(); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      mbar_arrive_expect_tx(a_full, hp.a_bytes);
+      for (int kb = 0; kb < p.n_kb; ++kb)
+        tma_load_2d(sA + kb * kABytes, &p.tmap_a, a_full, kb * (kKB / 2), m_tile * kBM);
+      int stage = 0; uint32_t phase = 0;
+      int issued = 0;
+      bool stop = false;
+      for (int pt = first_pt; pt < p.n_px_tiles && !stop; pt += pt_step) {
+        const TileCoord tc = tile_coord(p, pt);
+        for (int t = 0; t < p.T && !stop; ++t) {
+          for (int cb = 0; cb < p.cin_blocks; ++cb) {
+            if (*abort_flag) { stop = true; break; }
+            if (!mbar_wait_bounded(&empty[stage], phase ^ 1, p.timeout_ns)) {
+              atomicOr(p.err, kErrTimeoutEmpty); *abort_flag = 1; stop = true; break;
+            }
+            mbar_arrive_expect_tx(&full[stage], hp.halo_bytes);
+            tma_load_5d(sH + stage * hp.halo_stride, &p.tmap_b[0], &full[stage], cb * kKB,
+                        tc.w0 - p.pad, tc.h0 - p.pad, tc.n0, t);
+            ++issued;
+            if (++stage == S) { stage = 0; phase ^= 1; }
+          }
+        }
+      }
+      const int n_wait = min(issued, S);
+      for (int i = 0; i < n_wait; ++i) {
+        const int back = issued - 1 - i;
+        if (!mbar_wait_bounded(&full[back % S], (back / S) & 1, p.timeout_ns))
+          atomicOr(p.err, kErrTimeoutFull);
+      }
+      if (!mbar_wait_bounded(a_full, 0, p.timeout_ns)) atomicOr(p.err, kErrTimeoutFull);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(kBM, BN, true);
+      bool ok = mbar_wait_bounded(meta_ready, 0, p.timeout_ns);
+      ok = ok && mbar_wait_bounded(a_full, 0, p.timeout_ns);
+      if (!ok) { atomicOr(p.err, kErrTimeoutMeta); *abort_flag = 1; }
+      tc_fence_after();
+      const uint32_t a_base = smem_u32(sA);
+      const uint32_t h_base = smem_u32(sH);
+      const uint32_t sbo = static_cast<uint32_t>(hp.halo_w) * 128;
+      int stage = 0; uint32_t phase = 0;
+      int it = 0;
+      bool stop = *abort_flag != 0;
+      for (int pt = first_pt; pt < p.n_px_tiles && !stop; pt += pt_step) {
+        for (int t = 0; t < p.T && !stop; ++t) {
+          if (!mbar_wait_bounded(acc_empty, (it & 1) ^ 1, p.timeout_ns)) {
+            atomicOr(p.err, kErrTimeoutAccEmpty); *abort_flag = 1; stop = true; break;
+          }
+          tc_fence_after();
+          for (int cb = 0; cb < p.cin_blocks; ++cb) {
+            if (!mbar_wait_bounded(&full[stage], phase, p.timeout_ns)) {
+              atomicOr(p.err, kErrTimeoutFull); *abort_flag = 1; stop = true; break;
+            }
+            tc_fence_after();
+            const uint32_t hs = h_base + stage * hp.halo_stride;
+            for (int kh = 0; kh < hp.KH; ++kh) {
+              for (int kw = 0; kw < p.KW; ++kw) {
+                const int kb = (kh * p.KW + kw) * p.cin_blocks + cb;
+                const uint32_t brow = hs + static_cast<uint32_t>(kh * hp.halo_w + kw) * 128;
+#pragma unroll
+                for (int s = 0; s < 2; ++s) {
+                  const uint32_t ecol = kHaloMetaCol + 2 * kb + s;
+                  const uint64_t adesc = smem_desc_kmajor(a_base + kb * kABytes + 32 * s, 512, 4);
+                  const uint64_t bdesc = smem_desc_kmajor(brow + 64 * s, sbo, 2);
+                  const bool first = (cb == 0 && kh == 0 && kw == 0 && s == 0);
+                  mma_sp_f16(tmem, adesc, bdesc, tmem + (ecol & ~1u), idesc | (ecol & 1u),
+                             first ? 0u : 1u);
+                }
+              }
+            }
+            mma_commit(&empty[stage]);
+            if (++stage == S) { stage = 0; phase ^= 1; }
+          }
+          if (stop) break;
+          mma_commit(acc_full);
+          ++it;
+        }
+      }
+      mma_commit(drain);
+      if (!mbar_wait_bounded(drain, 0, p.timeout_ns)) atomicOr(p.err, kErrTimeoutDrain);
+    }
+  } else {
+    // ------------------------------------------------- metadata + epilogue
+    const int e = warp - 2;
+    const int q = warp & 3;
+    const int half = e >> 2;
+    const int row = q * 32 + lane;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    if (half == 0) {
+      const uint32_t* src = p.meta + (static_cast<size_t>(m_tile) * n_meta) * kBM + row;
+      for (int j = 0; j < n_meta; j += 8) {
+        uint32_t r[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          r[i] = (j + i < n_meta) ? __ldg(src + static_cast<size_t>(j + i) * kBM) : 0x44444444u;
+        tmem_st8(lane_base + kHaloMetaCol + j, r);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(meta_ready);
+    }
+    const int cout = m_tile * kBM + row;
+    const bool cvalid = cout < p.F;
+    const float sc = cvalid ? p.scale[cout] : 0.f;
+    const float bi = cvalid ? p.bias[cout] : 0.f;
+    const long long P = static_cast<long long>(p.B) * p.OH * p.OW;
+    const int cbase = m_tile * kBM + q * 32;
+    const int nchunk8 = max(0, min(4, (p.F - cbase) / 8));
+    uint8_t* xb = sX + e * kXposeBytes;
+    auto xoff = [](int px, int c8) { return px * 64 + ((c8 ^ ((px >> 1) & 3)) << 4); };
+
+    int it = 0;
+    bool stop = false;
+    for (int pt = first_pt; pt < p.n_px_tiles && !stop; pt += pt_step) {
+      const TileCoord tc = tile_coord(p, pt);
+      // Column j of the tile is pixel (h0 + j/8, w0 + j%8); this warp owns
+      // columns [half*BN/2, half*BN/2 + BN/2), lane l of group g owns column
+      // half*BN/2 + 32g + l in the transposed phase.
+      long long my_px[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const int col = half * (BN / 2) + g * 32 + lane;
+        const int oh = tc.h0 + col / 8, ow = tc.w0 + (col & 7);
+        my_px[g] = (oh < p.OH && ow < p.OW)
+                       ? (static_cast<long long>(tc.n0) * p.OH + oh) * p.OW + ow : -1;
+      }
+      float v[G][32];
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const long long px = __shfl_sync(0xffffffffu, my_px[g], i);
+          v[g][i] = ((p.flags & kReadState) && cvalid && px >= 0) ? p.state[px * p.F + cout] : 0.f;
+        }
+      }
+      for (int t = 0; t < p.T; ++t) {
+        bool fail = !mbar_wait_bounded(acc_full, it & 1, p.timeout_ns);
+        fail = __any_sync(0xffffffffu, fail || *abort_flag);
+        if (fail) { atomicOr(p.err, kErrTimeoutAcc); stop = true; break; }
+        tc_fence_after();
+        float acc[G][32];
+#pragma unroll
+        for (int g = 0; g < G; ++g) tmem_ld32(lane_base + half * (BN / 2) + g * 32, acc[g]);
+        tc_fence_before();
+        mbar_arrive(acc_empty);            // accumulator free: next MMAs may start
+        ++it;
+        const size_t tbase = static_cast<size_t>(t) * P;
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          uint4 r4[4];
+          if constexpr (RES) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) r4[k] = make_uint4(0, 0, 0, 0);
+            if (my_px[g] >= 0) {
+              const uint4* rp = reinterpret_cast<const uint4*>(
+                  p.residual + (tbase + my_px[g]) * p.F + cbase);
+#pragma unroll
+              for (int k = 0; k < 4; ++k) if (k < nchunk8) r4[k] = __ldg(rp + k);
+            }
+          }
+          if constexpr (MODE == kModeNone) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const long long px = __shfl_sync(0xffffffffu, my_px[g], i);
+              if (cvalid && px >= 0) p.out_f32[(tbase + px) * p.F + cout] = fmaf(acc[g][i], sc, bi);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const float x = fmaf(acc[g][i], sc, bi);
+              float h;
+              if constexpr (MODE == kModeLifMul) h = __fadd_rn(__fmul_rn(v[g][i], p.decay), __fmul_rn(x, p.inv_tau));
+              else if constexpr (MODE == kModeLifDiv) h = __fadd_rn(__fmul_rn(v[g][i], p.decay), __fdiv_rn(x, p.tau));
+              else h = __fadd_rn(v[g][i], x);
+              const bool spike = (h - p.v_th) >= 0.f;
+              v[g][i] = spike ? p.v_reset : h;
+              *reinterpret_cast<__half*>(xb + xoff(i, lane >> 3) + (lane & 7) * 2) =
+                  __ushort_as_half(spike ? 0x3C00 : 0);
+            }
+            __syncwarp();
+            uint4 o4[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) o4[k] = *reinterpret_cast<const uint4*>(xb + xoff(lane, k));
+            if constexpr (RES) {
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                __half2* a = reinterpret_cast<__half2*>(&o4[k]);
+                const __half2* b = reinterpret_cast<const __half2*>(&r4[k]);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) a[j] = __hadd2(a[j], b[j]);
+              }
+            }
+            if (my_px[g] >= 0) {
+              uint4* op = reinterpret_cast<uint4*>(p.out + (tbase + my_px[g]) * p.F + cbase);
+#pragma unroll
+              for (int k = 0; k < 4; ++k) if (k < nchunk8) op[k] = o4[k];
+            }
+            __syncwarp();
+          }
+        }
+      }
+      if (!stop && (p.flags & kWriteState)) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const long long px = __shfl_sync(0xffffffffu, my_px[g], i);
+            if (cvalid && px >= 0) p.state[px * p.F + cout] = v[g][i];
+          }
+        }
+      }
+    }
+    if (stop) *abort_flag = 1;
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kHaloTmemCols);
+  }
+}
+
+}  // namespace snn

@@ -39,7 +39,8 @@ class SparseConvBNLIF:
     """One fused 2:4-sparse Conv(+Linear) + BN + LIF/IF layer over T steps."""
 
     def __init__(self, weight, bn_scale, bn_bias, *, T, B, H, W, stride=1, pad=None,
-                 neuron="lif", tau=2.0, v_threshold=1.0, v_reset=0.0, device="cuda"):
+                 neuron="lif", tau=2.0, v_threshold=1.0, v_reset=0.0, device="cuda",
+                 force_generic=False):
         w = _np(weight).astype(np.float32)
         if w.ndim == 2:                       # Linear [out, in] -> 1x1 conv
             w = w[:, :, None, None]
@@ -57,6 +58,7 @@ class SparseConvBNLIF:
         self.T, self.B, self.Cin, self.Cout = T, B, cin, cout
         self.H, self.W = H, W
         self.out_dtype = torch.float32 if neuron == "none" else torch.float16
+        self.base_flags = rt.SNN_FLAG_FORCE_GENERIC if force_generic else 0
 
     def out_shape(self):
         return (self.T * self.B, self.OH, self.OW, self.Cout)
@@ -77,7 +79,7 @@ class SparseConvBNLIF:
             raise ValueError(f"data shape {tuple(data.shape)} does not match layer")
         if out is None:
             out = torch.empty(self.out_shape(), dtype=self.out_dtype, device=data.device)
-        flags = 0
+        flags = self.base_flags
         if state is not None:
             if tuple(state.shape) != self.state_shape() or state.dtype != torch.float32:
                 raise ValueError("state must be fp32 (B*OH*OW, Cout)")

@@ -23,6 +23,7 @@ SNN_NEURON_IF = 1
 SNN_NEURON_NONE = 2
 SNN_FLAG_READ_STATE = 1
 SNN_FLAG_WRITE_STATE = 2
+SNN_FLAG_FORCE_GENERIC = 4
 
 NEURONS = {"lif": SNN_NEURON_LIF, "if": SNN_NEURON_IF, "none": SNN_NEURON_NONE}
 

@@ -31,7 +31,7 @@ def from_nhwc(y, T, B):
     return np.transpose(y.reshape(T, B, oh, ow, f), (0, 1, 4, 2, 3))
 
 
-def build_layer(g, neuron=None, device="cuda"):
+def build_layer(g, neuron=None, device="cuda", force_generic=False):
     from sparsesnn_b200.layer import SparseConvBNLIF, fold_bn
     mean = g["mean"] - g["lin_bias"] if g["linear"] else g["mean"]
     scale, bias = fold_bn(g["gamma"], g["beta"], mean, g["var"])
@@ -39,9 +39,11 @@ def build_layer(g, neuron=None, device="cuda"):
     if g["linear"]:
         # Spikformer Linear over N = H*W tokens: rows = B*N, one "image" row.
         return SparseConvBNLIF(g["w"][:, :, 0, 0], scale, bias, T=g["T"], B=1, H=1,
-                               W=g["B"] * g["H"] * g["W"], neuron=neuron, device=device)
+                               W=g["B"] * g["H"] * g["W"], neuron=neuron, device=device,
+                               force_generic=force_generic)
     return SparseConvBNLIF(g["w"], scale, bias, T=g["T"], B=g["B"], H=g["H"], W=g["W"],
-                           stride=g["stride"], pad=g["pad"], neuron=neuron, device=device)
+                           stride=g["stride"], pad=g["pad"], neuron=neuron, device=device,
+                           force_generic=force_generic)
 
 
 def layer_input(g):
@@ -53,10 +55,10 @@ def layer_input(g):
     return to_nhwc(x)
 
 
-def run_case(g, neuron=None, residual=None):
+def run_case(g, neuron=None, residual=None, force_generic=False):
     import torch
     from sparsesnn_b200 import runtime as rt
-    layer = build_layer(g, neuron)
+    layer = build_layer(g, neuron, force_generic=force_generic)
     x = torch.from_numpy(layer_input(g)).to("cuda", torch.float16)
     state = torch.full(layer.state_shape(), 123.0, dtype=torch.float32, device="cuda")
     res = None
@@ -91,11 +93,15 @@ def check_spikes_and_v(spk, v, ref_spk, ref_h, ref_v):
     return frac, nmis
 
 
+@pytest.mark.parametrize("generic", [False, True], ids=["auto", "generic"])
 @pytest.mark.parametrize("name", LAYER_CASES)
-def test_golden_layer_parity(cuda_device, name):
+def test_golden_layer_parity(cuda_device, name, generic):
+    """Every golden case through the kernel the library picks (the halo
+    kernel for stride-1 3x3 layers on images >= 8 rows) and through the
+    general kernel."""
     g = load_layer_case(name)
     res = g.get("residual")
-    y, state, _ = run_case(g, residual=res)
+    y, state, _ = run_case(g, residual=res, force_generic=generic)
     ys, v = unflatten(g, y, state)
     if res is not None:
         spk = ys - res.astype(np.float32)
@@ -107,10 +113,11 @@ def test_golden_layer_parity(cuda_device, name):
     check_spikes_and_v(spk, v, g["spikes"].astype(np.float32), g["h"], g["v"])
 
 
+@pytest.mark.parametrize("generic", [False, True], ids=["auto", "generic"])
 @pytest.mark.parametrize("name", ["c3s1", "c3s2", "c1s2", "c3res", "lin"])
-def test_golden_preactivation(cuda_device, name):
+def test_golden_preactivation(cuda_device, name, generic):
     g = load_layer_case(name)
-    y, _, _ = run_case(g, neuron="none")
+    y, _, _ = run_case(g, neuron="none", force_generic=generic)
     z, _ = unflatten(g, y)
     ref = g["bn_out"]
     # vs the fp32 reference: FP16 weight rounding bounds the error.
@@ -183,13 +190,14 @@ def _torch_reference(x_tbchw, w, scale, bias, stride, pad, tau=2.0, v_th=1.0):
     return torch.stack(spk), torch.stack(hs), v
 
 
-def test_config0_full_size(cuda_device):
+@pytest.mark.parametrize("generic", [False, True], ids=["halo", "generic"])
+def test_config0_full_size(cuda_device, generic):
     """Config 0: 3x3 s1 p1, Cin=Cout=128, 32x32, B=16, T=4."""
     import torch
     from sparsesnn_b200.layer import SparseConvBNLIF, fold_bn
     x, w, bn = L.make_config0(seed=0)
     scale, bias = fold_bn(bn.gamma, bn.beta, bn.mean, bn.var)
-    layer = SparseConvBNLIF(w, scale, bias, T=4, B=16, H=32, W=32)
+    layer = SparseConvBNLIF(w, scale, bias, T=4, B=16, H=32, W=32, force_generic=generic)
     xd = torch.from_numpy(to_nhwc(x)).to("cuda", torch.float16)
     state = torch.zeros(layer.state_shape(), dtype=torch.float32, device="cuda")
     y = layer(xd, state=state, read_state=False)
