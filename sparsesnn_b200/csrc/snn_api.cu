@@ -41,8 +41,8 @@ using ConvKernel = void (*)(const snn::ConvParams);
 
 ConvKernel conv_kernel_fn(int mode, bool res) {
   switch (mode * 2 + (res ? 1 : 0)) {
-    case 0: return snn::fused_sparse_conv_lif_kernel<snn::kModeLifMul, false>;
-    case 1: return snn::fused_sparse_conv_lif_kernel<snn::kModeLifMul, true>;
+    case 0: return snn::fused_sparse_conv_lif_kernel<snn::kModeLifHalf, false>;
+    case 1: return snn::fused_sparse_conv_lif_kernel<snn::kModeLifHalf, true>;
     case 2: return snn::fused_sparse_conv_lif_kernel<snn::kModeLifDiv, false>;
     case 3: return snn::fused_sparse_conv_lif_kernel<snn::kModeLifDiv, true>;
     case 4: return snn::fused_sparse_conv_lif_kernel<snn::kModeIf, false>;
@@ -56,13 +56,13 @@ using HaloKernel = void (*)(const snn::HaloParams);
 template <int BN>
 HaloKernel halo_kernel_fn_bn(int mode, bool res) {
   switch (mode * 2 + (res ? 1 : 0)) {
-    case 0: return snn::fused_sparse_conv_halo_kernel<snn::kModeLifMul, false, BN>;
-    case 1: return snn::fused_sparse_conv_halo_kernel<snn::kModeLifMul, true, BN>;
-    case 2: return snn::fused_sparse_conv_halo_kernel<snn::kModeLifDiv, false, BN>;
-    case 3: return snn::fused_sparse_conv_halo_kernel<snn::kModeLifDiv, true, BN>;
-    case 4: return snn::fused_sparse_conv_halo_kernel<snn::kModeIf, false, BN>;
-    case 5: return snn::fused_sparse_conv_halo_kernel<snn::kModeIf, true, BN>;
-    default: return snn::fused_sparse_conv_halo_kernel<snn::kModeNone, false, BN>;
+    case 0: return snn::fused_sparse_conv_halo_kernel<snn::kModeLifHalf, false, BN, 3>;
+    case 1: return snn::fused_sparse_conv_halo_kernel<snn::kModeLifHalf, true, BN, 3>;
+    case 2: return snn::fused_sparse_conv_halo_kernel<snn::kModeLifDiv, false, BN, 3>;
+    case 3: return snn::fused_sparse_conv_halo_kernel<snn::kModeLifDiv, true, BN, 3>;
+    case 4: return snn::fused_sparse_conv_halo_kernel<snn::kModeIf, false, BN, 3>;
+    case 5: return snn::fused_sparse_conv_halo_kernel<snn::kModeIf, true, BN, 3>;
+    default: return snn::fused_sparse_conv_halo_kernel<snn::kModeNone, false, BN, 3>;
   }
 }
 
@@ -237,21 +237,18 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
   // Reference computes (1.0 - 1.0/tau) in double, then float32 (models/neurons.py:125).
   p.decay = d->neuron == SNN_NEURON_LIF
                 ? static_cast<float>(1.0 - 1.0 / static_cast<double>(d->tau)) : 1.0f;
-  int e2 = 0;
-  const float mant = frexpf(d->tau, &e2);
-  const bool tau_pow2 = d->neuron == SNN_NEURON_LIF && mant == 0.5f;
-  p.inv_tau = tau_pow2 ? 1.0f / d->tau : 0.0f;
+  p.inv_tau = 0.0f;
   p.v_th = d->v_threshold; p.v_reset = d->v_reset;
   p.timeout_ns = 4000000000ull;   // SM cycles (~2 s at the highest clock)
   const int mode = d->neuron == SNN_NEURON_NONE ? snn::kModeNone
                    : d->neuron == SNN_NEURON_IF ? snn::kModeIf
-                   : tau_pow2 ? snn::kModeLifMul : snn::kModeLifDiv;
+                   : d->tau == 2.0f ? snn::kModeLifHalf : snn::kModeLifDiv;
 
   // Halo variant: stride-1 odd square kernels with "same" padding whose
   // 128-channel weight slice fits in shared memory and images tall enough
   // for 8-row tiles.
   const int a_bytes = g.n_kb * snn::kABytes;
-  const bool halo = d->stride == 1 && d->KH == d->KW && (d->KH & 1) && d->KH > 1 &&
+  const bool halo = d->stride == 1 && d->KH == 3 && d->KW == 3 &&
                     d->pad == d->KH / 2 && a_bytes <= kHaloMaxWeightBytes && g.OH >= 8 &&
                     !(d->flags & SNN_FLAG_FORCE_GENERIC);
   if (halo) {
@@ -282,7 +279,7 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
       const size_t smem = static_cast<size_t>(fixed) + static_cast<size_t>(hp.halo_stages) * hp.halo_stride;
       const int per_m = std::max(1, std::min(p.n_px_tiles, g_num_sms / p.n_m));
       const long long grid = static_cast<long long>(per_m) * p.n_m;
-      halo_kernel_fn(bn, mode, residual != nullptr)<<<static_cast<unsigned>(grid), snn::kThreads,
+      halo_kernel_fn(bn, mode, residual != nullptr)<<<static_cast<unsigned>(grid), snn::kHaloThreads,
                                                       smem, static_cast<cudaStream_t>(stream)>>>(hp);
       cudaError_t e = cudaGetLastError();
       if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));

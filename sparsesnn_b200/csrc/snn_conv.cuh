@@ -48,9 +48,27 @@ constexpr int kBarBytes = 512;
 constexpr int kSmemBytes = kStages * kStageBytes + kEpiWarps * kXposeBytes + kBarBytes + 1024;
 
 enum NeuronKind : int { kLIF = 0, kIF = 1, kNoNeuron = 2 };
-// Epilogue variants (template parameter): LIF with x*(1/tau) (exact when tau
-// is a power of two), LIF with x/tau, IF, and BN output without neuron.
-enum EpiMode : int { kModeLifMul = 0, kModeLifDiv = 1, kModeIf = 2, kModeNone = 3 };
+// Epilogue variants (template parameter): LIF with tau == 2 (every scaling
+// by 1/2 is exact, so the update folds into two FMAs with the reference's
+// rounding), LIF with general tau (v*(1-1/tau) + x/tau, each op rounded),
+// IF, and BN output without neuron.
+enum EpiMode : int { kModeLifHalf = 0, kModeLifDiv = 1, kModeIf = 2, kModeNone = 3 };
+
+// One neuron step.  x2 is the BN output pre-scaled for kModeLifHalf
+// (acc*(scale/2) + bias/2 == (acc*scale + bias)/2 exactly) and the plain BN
+// output otherwise.  Returns the spike; updates v (hard reset to v_reset).
+template <int MODE>
+__device__ __forceinline__ bool neuron_step(float& v, float x2, float decay, float tau,
+                                            float v_th, float v_reset) {
+  float h;
+  if constexpr (MODE == kModeLifHalf) h = fmaf(v, 0.5f, x2);      // v*0.5 is exact
+  else if constexpr (MODE == kModeLifDiv) h = __fadd_rn(__fmul_rn(v, decay), __fdiv_rn(x2, tau));
+  else h = __fadd_rn(v, x2);
+  // (h - v_th) >= 0 is the reference's test; without flush-to-zero it equals h >= v_th.
+  const bool spike = h >= v_th;
+  v = spike ? v_reset : h;
+  return spike;
+}
 enum ConvFlags : int { kReadState = 1, kWriteState = 2 };
 enum ErrCode : unsigned { kErrTimeoutFull = 1u, kErrTimeoutEmpty = 2u, kErrTimeoutAcc = 4u,
                           kErrTimeoutMeta = 8u, kErrTimeoutAccEmpty = 16u, kErrTimeoutDrain = 32u,
@@ -323,16 +341,12 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
             }
           } else {
             // Neuron update, lane = output channel, i = pixel column.
+            const float sx = MODE == kModeLifHalf ? sc * 0.5f : sc;
+            const float bx = MODE == kModeLifHalf ? bi * 0.5f : bi;
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
-              const float x = fmaf(acc[i], sc, bi);
-              // Reference order v*(1-1/tau) + x/tau with each op rounded (no FMA).
-              float h;
-              if constexpr (MODE == kModeLifMul) h = __fadd_rn(__fmul_rn(v[i], p.decay), __fmul_rn(x, p.inv_tau));
-              else if constexpr (MODE == kModeLifDiv) h = __fadd_rn(__fmul_rn(v[i], p.decay), __fdiv_rn(x, p.tau));
-              else h = __fadd_rn(v[i], x);
-              const bool spike = (h - p.v_th) >= 0.f;
-              v[i] = spike ? p.v_reset : h;
+              const bool spike = neuron_step<MODE>(v[i], fmaf(acc[i], sx, bx), p.decay, p.tau,
+                                                   p.v_th, p.v_reset);
               *reinterpret_cast<__half*>(xb + xoff(i, lane >> 3) + (lane & 7) * 2) =
                   __ushort_as_half(spike ? 0x3C00 : 0);
             }

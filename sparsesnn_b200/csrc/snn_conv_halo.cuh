@@ -1,26 +1,36 @@
 // Halo variant of the fused 2:4-sparse conv for stride-1 KxK convolutions
-// whose per-tile weights fit in shared memory (e.g. 3x3 with Cin <= 128).
+// ("same" padding) whose per-tile weights fit in shared memory (e.g. 3x3
+// with Cin <= 128).
 //
 // Differences from the generic kernel (snn_conv.cuh):
 //  * the CTA's 128-channel weight slice (all k-blocks) is loaded ONCE into
 //    shared memory and stays resident for the CTA's lifetime;
 //  * a tile is 8 output columns x BN/8 output rows of one image; for each
-//    (timestep, 64-channel slice) ONE TMA box loads the (8+KW-1) x (BN/8+KH-1)
+//    (timestep, 64-channel slice) ONE TMA box loads the (8+K-1) x (BN/8+K-1)
 //    input halo, and every filter tap reads it through a descriptor that
-//    starts at row offset (kh*(8+KW-1) + kw) with a group stride of one halo
+//    starts at row offset (kh*(8+K-1) + kw) with a group stride of one halo
 //    row (the 128-byte swizzle is a function of the absolute shared-memory
 //    address, so operands may start at any 128-byte row);
-//  * timesteps are the outer loop (one BN-column accumulator); the epilogue
-//    copies the accumulator to registers and releases it before the neuron
-//    update, so the next timestep's MMAs overlap the epilogue.
+//  * timesteps are the outer loop; accumulators are double-buffered in
+//    TMEM (2 x BN columns), and the epilogue copies a buffer to registers and
+//    releases it before the neuron update.
+//
+// Warp roles (12 warps): 0..7 epilogue (TMEM lane quarter = warp % 4, pixel
+// half = warp / 4); 8..11 load the metadata into TMEM (one warp per lane
+// quarter), then warp 10 issues MMAs and owns TMEM and warp 11 drives TMA.
+// Placing the MMA and TMA warps on sub-partitions 2 and 3 keeps them off the
+// sub-partitions that do all the epilogue work when Cout <= 64.
 #pragma once
 #include "snn_conv.cuh"
 
 namespace snn {
 
 constexpr int kHaloMaxStages = 8;
-constexpr int kHaloMetaCol = 128;        // accumulator: columns [0,128); metadata after
-constexpr int kHaloTmemCols = 256;
+constexpr int kHaloThreads = 384;
+constexpr int kHaloMmaWarp = 10;
+constexpr int kHaloTmaWarp = 11;
+constexpr int kHaloMetaCol = 256;        // accumulators: 2 x up to 128 columns
+constexpr int kHaloTmemCols = 512;
 
 struct HaloParams {
   ConvParams c;              // shared fields (tmap_a, tmap_b[0], meta, scale, ...)
@@ -32,8 +42,8 @@ struct HaloParams {
   int a_bytes;               // resident weight bytes (n_kb * kABytes)
 };
 
-template <int MODE, bool RES, int BN>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int MODE, bool RES, int BN, int KS>
+__global__ void __launch_bounds__(kHaloThreads, 1)
 fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
   const ConvParams& p = hp.c;
   constexpr int G = BN / 64;                 // 32-column groups per epilogue warp
@@ -46,9 +56,9 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
   uint64_t* full = reinterpret_cast<uint64_t*>(sX + kEpiWarps * kXposeBytes);
   uint64_t* empty = full + kHaloMaxStages;
   uint64_t* a_full = empty + kHaloMaxStages;
-  uint64_t* acc_full = a_full + 1;
-  uint64_t* acc_empty = acc_full + 1;
-  uint64_t* meta_ready = acc_empty + 1;
+  uint64_t* acc_full = a_full + 1;          // [2]
+  uint64_t* acc_empty = acc_full + 2;       // [2]
+  uint64_t* meta_ready = acc_empty + 2;
   uint64_t* drain = meta_ready + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -64,21 +74,38 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
     mbar_init(a_full, 1);
-    mbar_init(acc_full, 1);
-    mbar_init(acc_empty, kEpiThreads);
+    for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], kEpiThreads); }
     mbar_init(meta_ready, 128);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 0 && lane == 0) { prefetch_tmap(&p.tmap_a); prefetch_tmap(&p.tmap_b[0]); }
-  if (warp == 1) { tmem_alloc(tmem_slot, kHaloTmemCols); tmem_relinquish(); }
+  if (warp == kHaloTmaWarp && lane == 0) { prefetch_tmap(&p.tmap_a); prefetch_tmap(&p.tmap_b[0]); }
+  if (warp == kHaloMmaWarp) { tmem_alloc(tmem_slot, kHaloTmemCols); tmem_relinquish(); }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
+  if (warp >= kEpiWarps) {
+    // ------------------------------------------- metadata into TMEM (warps 8..11)
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    const uint32_t* src = p.meta + (static_cast<size_t>(m_tile) * n_meta) * kBM + row;
+    for (int j = 0; j < n_meta; j += 8) {
+      uint32_t r[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        r[i] = (j + i < n_meta) ? __ldg(src + static_cast<size_t>(j + i) * kBM) : 0x44444444u;
+      tmem_st8(lane_base + kHaloMetaCol + j, r);
+    }
+    tmem_st_wait();
+    tc_fence_before();
+    mbar_arrive(meta_ready);
+  }
+
+  if (warp == kHaloTmaWarp) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       mbar_arrive_expect_tx(a_full, hp.a_bytes);
@@ -111,7 +138,7 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
       }
       if (!mbar_wait_bounded(a_full, 0, p.timeout_ns)) atomicOr(p.err, kErrTimeoutFull);
     }
-  } else if (warp == 1) {
+  } else if (warp == kHaloMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = idesc_f16(kBM, BN, true);
@@ -127,19 +154,23 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
       bool stop = *abort_flag != 0;
       for (int pt = first_pt; pt < p.n_px_tiles && !stop; pt += pt_step) {
         for (int t = 0; t < p.T && !stop; ++t) {
-          if (!mbar_wait_bounded(acc_empty, (it & 1) ^ 1, p.timeout_ns)) {
+          const int buf = it & 1;
+          if (!mbar_wait_bounded(&acc_empty[buf], ((it >> 1) & 1) ^ 1, p.timeout_ns)) {
             atomicOr(p.err, kErrTimeoutAccEmpty); *abort_flag = 1; stop = true; break;
           }
           tc_fence_after();
+          const uint32_t d_tmem = tmem + buf * BN;
           for (int cb = 0; cb < p.cin_blocks; ++cb) {
             if (!mbar_wait_bounded(&full[stage], phase, p.timeout_ns)) {
               atomicOr(p.err, kErrTimeoutFull); *abort_flag = 1; stop = true; break;
             }
             tc_fence_after();
             const uint32_t hs = h_base + stage * hp.halo_stride;
-            for (int kh = 0; kh < hp.KH; ++kh) {
-              for (int kw = 0; kw < p.KW; ++kw) {
-                const int kb = (kh * p.KW + kw) * p.cin_blocks + cb;
+#pragma unroll
+            for (int kh = 0; kh < KS; ++kh) {
+#pragma unroll
+              for (int kw = 0; kw < KS; ++kw) {
+                const int kb = (kh * KS + kw) * p.cin_blocks + cb;
                 const uint32_t brow = hs + static_cast<uint32_t>(kh * hp.halo_w + kw) * 128;
 #pragma unroll
                 for (int s = 0; s < 2; ++s) {
@@ -147,7 +178,7 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
                   const uint64_t adesc = smem_desc_kmajor(a_base + kb * kABytes + 32 * s, 512, 4);
                   const uint64_t bdesc = smem_desc_kmajor(brow + 64 * s, sbo, 2);
                   const bool first = (cb == 0 && kh == 0 && kw == 0 && s == 0);
-                  mma_sp_f16(tmem, adesc, bdesc, tmem + (ecol & ~1u), idesc | (ecol & 1u),
+                  mma_sp_f16(d_tmem, adesc, bdesc, tmem + (ecol & ~1u), idesc | (ecol & 1u),
                              first ? 0u : 1u);
                 }
               }
@@ -156,41 +187,30 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
             if (++stage == S) { stage = 0; phase ^= 1; }
           }
           if (stop) break;
-          mma_commit(acc_full);
+          mma_commit(&acc_full[buf]);
           ++it;
         }
       }
       mma_commit(drain);
       if (!mbar_wait_bounded(drain, 0, p.timeout_ns)) atomicOr(p.err, kErrTimeoutDrain);
     }
-  } else {
-    // ------------------------------------------------- metadata + epilogue
-    const int e = warp - 2;
+  } else if (warp < kEpiWarps) {
+    // ------------------------------------------------------------ epilogue
     const int q = warp & 3;
-    const int half = e >> 2;
+    const int half = warp >> 2;
     const int row = q * 32 + lane;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
-    if (half == 0) {
-      const uint32_t* src = p.meta + (static_cast<size_t>(m_tile) * n_meta) * kBM + row;
-      for (int j = 0; j < n_meta; j += 8) {
-        uint32_t r[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          r[i] = (j + i < n_meta) ? __ldg(src + static_cast<size_t>(j + i) * kBM) : 0x44444444u;
-        tmem_st8(lane_base + kHaloMetaCol + j, r);
-      }
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(meta_ready);
-    }
     const int cout = m_tile * kBM + row;
     const bool cvalid = cout < p.F;
+    const int cbase = m_tile * kBM + q * 32;
+    const bool warp_live = cbase < p.F;          // warp-uniform: any channel to write?
     const float sc = cvalid ? p.scale[cout] : 0.f;
     const float bi = cvalid ? p.bias[cout] : 0.f;
+    const float sx = MODE == kModeLifHalf ? sc * 0.5f : sc;
+    const float bx = MODE == kModeLifHalf ? bi * 0.5f : bi;
     const long long P = static_cast<long long>(p.B) * p.OH * p.OW;
-    const int cbase = m_tile * kBM + q * 32;
     const int nchunk8 = max(0, min(4, (p.F - cbase) / 8));
-    uint8_t* xb = sX + e * kXposeBytes;
+    uint8_t* xb = sX + warp * kXposeBytes;
     auto xoff = [](int px, int c8) { return px * 64 + ((c8 ^ ((px >> 1) & 3)) << 4); };
 
     int it = 0;
@@ -198,8 +218,8 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
     for (int pt = first_pt; pt < p.n_px_tiles && !stop; pt += pt_step) {
       const TileCoord tc = tile_coord(p, pt);
       // Column j of the tile is pixel (h0 + j/8, w0 + j%8); this warp owns
-      // columns [half*BN/2, half*BN/2 + BN/2), lane l of group g owns column
-      // half*BN/2 + 32g + l in the transposed phase.
+      // columns [half*BN/2, half*BN/2 + BN/2); in the transposed phase lane l
+      // of group g owns column half*BN/2 + 32g + l.
       long long my_px[G];
 #pragma unroll
       for (int g = 0; g < G; ++g) {
@@ -218,19 +238,27 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
         }
       }
       for (int t = 0; t < p.T; ++t) {
-        bool fail = !mbar_wait_bounded(acc_full, it & 1, p.timeout_ns);
+        const int buf = it & 1;
+        bool fail = !mbar_wait_bounded(&acc_full[buf], (it >> 1) & 1, p.timeout_ns);
         fail = __any_sync(0xffffffffu, fail || *abort_flag);
         if (fail) { atomicOr(p.err, kErrTimeoutAcc); stop = true; break; }
         tc_fence_after();
-        float acc[G][32];
-#pragma unroll
-        for (int g = 0; g < G; ++g) tmem_ld32(lane_base + half * (BN / 2) + g * 32, acc[g]);
-        tc_fence_before();
-        mbar_arrive(acc_empty);            // accumulator free: next MMAs may start
-        ++it;
+        if (!warp_live) {                      // no channel of this warp is real
+          tc_fence_before();
+          mbar_arrive(&acc_empty[buf]);
+          ++it;
+          continue;
+        }
         const size_t tbase = static_cast<size_t>(t) * P;
 #pragma unroll
         for (int g = 0; g < G; ++g) {
+          float acc[32];
+          tmem_ld32(lane_base + buf * BN + half * (BN / 2) + g * 32, acc);
+          if (g == G - 1) {                    // buffer drained: the MMAs it holds back may start
+            tc_fence_before();
+            mbar_arrive(&acc_empty[buf]);
+            ++it;
+          }
           uint4 r4[4];
           if constexpr (RES) {
 #pragma unroll
@@ -246,18 +274,13 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
               const long long px = __shfl_sync(0xffffffffu, my_px[g], i);
-              if (cvalid && px >= 0) p.out_f32[(tbase + px) * p.F + cout] = fmaf(acc[g][i], sc, bi);
+              if (cvalid && px >= 0) p.out_f32[(tbase + px) * p.F + cout] = fmaf(acc[i], sc, bi);
             }
           } else {
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
-              const float x = fmaf(acc[g][i], sc, bi);
-              float h;
-              if constexpr (MODE == kModeLifMul) h = __fadd_rn(__fmul_rn(v[g][i], p.decay), __fmul_rn(x, p.inv_tau));
-              else if constexpr (MODE == kModeLifDiv) h = __fadd_rn(__fmul_rn(v[g][i], p.decay), __fdiv_rn(x, p.tau));
-              else h = __fadd_rn(v[g][i], x);
-              const bool spike = (h - p.v_th) >= 0.f;
-              v[g][i] = spike ? p.v_reset : h;
+              const bool spike = neuron_step<MODE>(v[g][i], fmaf(acc[i], sx, bx), p.decay,
+                                                   p.tau, p.v_th, p.v_reset);
               *reinterpret_cast<__half*>(xb + xoff(i, lane >> 3) + (lane & 7) * 2) =
                   __ushort_as_half(spike ? 0x3C00 : 0);
             }
@@ -283,7 +306,7 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
           }
         }
       }
-      if (!stop && (p.flags & kWriteState)) {
+      if (!stop && (p.flags & kWriteState) && warp_live) {
 #pragma unroll
         for (int g = 0; g < G; ++g) {
 #pragma unroll
@@ -299,7 +322,7 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kHaloMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, kHaloTmemCols);
   }
