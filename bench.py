@@ -68,7 +68,7 @@ def peaks():
     return 6650.0, 1590.0, "fallback"
 
 
-def cpu_reference_images_per_s(steps, sample, threads):
+def cpu_reference_images_per_s(steps, sample, threads, warmup=1):
     """Time the oracle's port of the reference PyTorch forward on CPU."""
     import torch
     from oracle.sew_resnet import forward_torch, make_input
@@ -76,7 +76,8 @@ def cpu_reference_images_per_s(steps, sample, threads):
     torch.set_num_threads(threads)
     P = init_params(seed=0)
     x = make_input(seed=0, B=sample)
-    forward_torch(P, x, T=T_STEPS)                       # warm-up
+    for _ in range(warmup):
+        forward_torch(P, x, T=T_STEPS)
     times = []
     for _ in range(steps):
         t0 = time.perf_counter()
@@ -98,7 +99,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -139,9 +140,8 @@ def run_reference(args, rank):
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    for _ in range(max(0, args.warmup)):
-        pass
-    ips, times = cpu_reference_images_per_s(max(1, args.steps), CPU_SAMPLE, threads)
+    ips, times = cpu_reference_images_per_s(max(1, args.steps), CPU_SAMPLE, threads,
+                                            warmup=max(1, args.warmup))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     line = {"impl": "reference", "metric": METRIC, "value": ips, "unit": UNIT,
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -171,13 +171,15 @@ def run_ours(args, rank, world, local_rank):
     gathered = torch.empty((world * args.batch, model.num_classes), dtype=torch.float32,
                            device=dev) if world > 1 else None
 
+    from sparsesnn_b200 import dist as sd
+
     def barrier():
         if world > 1:
             dist.barrier(device_ids=[local_rank])
 
     def gather():
         if world > 1:
-            dist.all_gather_into_tensor(gathered, model.logits)
+            sd.gather_logits(model.logits, gathered)
 
     # Warm-up (eager), then capture the forward into a CUDA graph.
     model.x_in.copy_(x_dev)
@@ -193,22 +195,33 @@ def run_ours(args, rank, world, local_rank):
     n_launch = len(model.launches())
 
     # ---------------- timed region A: device-resident inputs, graph replay
+    # The clock sampler runs across the timed region plus 300 / 200 identical
+    # replays before / after it, so that even a short timed region has
+    # samples taken under the same load.
     stream = torch.cuda.current_stream(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier(); torch.cuda.synchronize()
+
+    def roll(iters):
+        # Fixed iteration counts: every rank issues the same collectives.
+        for i in range(iters):
+            model.replay()
+            gather()
+            if i % 20 == 19:
+                torch.cuda.synchronize()
+        torch.cuda.synchronize()
+
     with ClockSampler(local_rank) as clk:
+        roll(300)
+        barrier(); torch.cuda.synchronize()
         e0.record(stream)
         for _ in range(args.steps):
             model.replay()
             gather()
         e1.record(stream)
         torch.cuda.synchronize()
-    barrier()
-    ms = e0.elapsed_time(e1) / args.steps
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        barrier()
+        roll(200)
+    ms = sd.max_over_ranks(e0.elapsed_time(e1) / args.steps, device=dev)
     value = args.batch * world / (ms / 1000.0)
 
     # ---------------- timed region B: end to end through the public call
@@ -221,11 +234,7 @@ def run_ours(args, rank, world, local_rank):
     e1.record(stream)
     torch.cuda.synchronize()
     barrier()
-    ms_e2e = e0.elapsed_time(e1) / args.steps
-    if world > 1:
-        t = torch.tensor([ms_e2e], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_e2e = float(t.item())
+    ms_e2e = sd.max_over_ranks(e0.elapsed_time(e1) / args.steps, device=dev)
     e2e = args.batch * world / (ms_e2e / 1000.0)
 
     # ---------------- per-launch CUDA-event timing of the fused conv kernel
@@ -281,7 +290,7 @@ def run_ours(args, rank, world, local_rank):
                                           f"{bf16_peak} TFLOP/s; FLOPs dense-equivalent",
                              "flops_per_forward": flops, "kernel_ms_per_forward": conv_ms},
                 "layer_ms": {k: round(v, 4) for k, v in per_layer.items()},
-                "clocks": clk.summary(),
+                "clocks": dict(clk.summary(), window="timed region plus 300 replays before and 200 after"),
                 "cpu_baseline": cpu}
         print(json.dumps(line), flush=True)
 
@@ -296,12 +305,10 @@ def main():
         return
     import torch
     import torch.distributed as dist
+    from sparsesnn_b200 import dist as sd
     if world > 1:
-        import datetime
-        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         torch.cuda.set_device(local_rank)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local_rank))
+        sd.init_from_env("nccl", timeout_s=120.0, device_id=torch.device("cuda", local_rank))
     try:
         run_ours(args, rank, world, local_rank)
     finally:

@@ -408,10 +408,10 @@ int snn_stem_forward(const snn_conv_desc* d, int32_t Tin, const float* x, const 
   int st = ensure_init();
   if (st) return st;
   if (!d || !x || !w || !bn_scale || !bn_bias || !out) return fail(SNN_E_INVALID, "null pointer");
-  if (d->T < 1 || d->B < 1 || d->Cin < 1 || d->Cout < 8 || d->Cout % 8 || d->Cout > 2048 ||
+  if (d->T < 1 || d->B < 1 || d->Cin < 1 || d->Cout < 16 || d->Cout % 16 || d->Cout > 4096 ||
       d->KH < 1 || d->KW < 1 || d->stride < 1 || d->pad < 0 ||
       static_cast<long long>(d->KH) * d->KW * d->Cin * d->Cout > 12288)
-    return fail(SNN_E_INVALID, "unsupported stem geometry (Cout multiple of 8, K*Cout <= 12288)");
+    return fail(SNN_E_INVALID, "unsupported stem geometry (Cout multiple of 16, K*Cout <= 12288)");
   if (Tin != 1 && Tin != d->T) return fail(SNN_E_INVALID, "Tin must be 1 or T");
   if (d->neuron == SNN_NEURON_NONE) return fail(SNN_E_INVALID, "stem needs a neuron");
   const int OH = (d->H + 2 * d->pad - d->KH) / d->stride + 1;
@@ -426,14 +426,19 @@ int snn_stem_forward(const snn_conv_desc* d, int32_t Tin, const float* x, const 
   p.tau = d->tau; p.decay = static_cast<float>(1.0 - 1.0 / static_cast<double>(d->tau));
   p.v_th = d->v_threshold; p.v_reset = d->v_reset;
   const long long pixels = static_cast<long long>(d->B) * OH * OW;
-  const int px_per_block = 256 / (d->Cout / 8);
+  const int px_per_block = 256 / (d->Cout / 16);
   if (px_per_block < 1) return fail(SNN_E_INVALID, "stem Cout too large");
-  const long long nblk = (pixels + px_per_block - 1) / px_per_block;
-  if (nblk > 0x7fffffffLL) return fail(SNN_E_INVALID, "stem grid too large");
+  const long long nblk = std::min<long long>((pixels + px_per_block - 1) / px_per_block,
+                                             static_cast<long long>(g_num_sms) * 2);
   dim3 block(256);
   dim3 grid(static_cast<unsigned>(nblk));
   const size_t smem = static_cast<size_t>(d->KH) * d->KW * d->Cin * d->Cout * sizeof(float);
-  snn::stem_conv_lif_kernel<<<grid, block, smem, static_cast<cudaStream_t>(stream)>>>(p);
+  if (d->KH == 3 && d->KW == 3 && d->Cin == 3)
+    snn::stem_conv_lif_kernel<3, 3><<<grid, block, smem, static_cast<cudaStream_t>(stream)>>>(p);
+  else if (d->KH == 3 && d->KW == 3 && d->Cin == 2)
+    snn::stem_conv_lif_kernel<3, 2><<<grid, block, smem, static_cast<cudaStream_t>(stream)>>>(p);
+  else
+    snn::stem_conv_lif_kernel<0, 0><<<grid, block, smem, static_cast<cudaStream_t>(stream)>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));
   return SNN_OK;
@@ -444,11 +449,13 @@ int snn_head_forward(int32_t T, int32_t B, int32_t HW, int32_t C, int32_t NC, co
   int st = ensure_init();
   if (st) return st;
   if (!x || !fc_w || !logits) return fail(SNN_E_INVALID, "null pointer");
-  if (T < 1 || B < 1 || HW < 1 || C < 1 || C > 4096 || NC < 1)
-    return fail(SNN_E_INVALID, "bad head shape");
+  if (T < 1 || B < 1 || HW < 1 || C < 8 || C % 8 || C > 1024 || NC < 1)
+    return fail(SNN_E_INVALID, "bad head shape (C multiple of 8, <= 1024)");
+  if (reinterpret_cast<uintptr_t>(x) & 15) return fail(SNN_E_INVALID, "x must be 16-byte aligned");
   const int threads = 256;
-  const size_t smem = static_cast<size_t>(C) * sizeof(float);
-  snn::head_pool_fc_kernel<<<B, threads, smem, static_cast<cudaStream_t>(stream)>>>(
+  const size_t smem = static_cast<size_t>(4 + snn::kHeadImgs) * C * sizeof(float);
+  const int nblk = (B + snn::kHeadImgs - 1) / snn::kHeadImgs;
+  snn::head_pool_fc_kernel<<<nblk, threads, smem, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __half*>(x), fc_w, fc_b, logits, T, B, HW, C, NC);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));

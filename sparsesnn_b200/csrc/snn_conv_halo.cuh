@@ -239,6 +239,23 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
       }
       for (int t = 0; t < p.T; ++t) {
         const int buf = it & 1;
+        const size_t tbase = static_cast<size_t>(t) * P;
+        // Residual rows of this timestep (64 B per pixel), requested before
+        // the accumulator wait so their latency hides behind the MMAs.
+        uint4 r4[G][4];
+        if constexpr (RES) {
+#pragma unroll
+          for (int g = 0; g < G; ++g) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) r4[g][k] = make_uint4(0, 0, 0, 0);
+            if (warp_live && my_px[g] >= 0) {
+              const uint4* rp = reinterpret_cast<const uint4*>(
+                  p.residual + (tbase + my_px[g]) * p.F + cbase);
+#pragma unroll
+              for (int k = 0; k < 4; ++k) if (k < nchunk8) r4[g][k] = __ldg(rp + k);
+            }
+          }
+        }
         bool fail = !mbar_wait_bounded(&acc_full[buf], (it >> 1) & 1, p.timeout_ns);
         fail = __any_sync(0xffffffffu, fail || *abort_flag);
         if (fail) { atomicOr(p.err, kErrTimeoutAcc); stop = true; break; }
@@ -249,7 +266,6 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
           ++it;
           continue;
         }
-        const size_t tbase = static_cast<size_t>(t) * P;
 #pragma unroll
         for (int g = 0; g < G; ++g) {
           float acc[32];
@@ -258,17 +274,6 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
             tc_fence_before();
             mbar_arrive(&acc_empty[buf]);
             ++it;
-          }
-          uint4 r4[4];
-          if constexpr (RES) {
-#pragma unroll
-            for (int k = 0; k < 4; ++k) r4[k] = make_uint4(0, 0, 0, 0);
-            if (my_px[g] >= 0) {
-              const uint4* rp = reinterpret_cast<const uint4*>(
-                  p.residual + (tbase + my_px[g]) * p.F + cbase);
-#pragma unroll
-              for (int k = 0; k < 4; ++k) if (k < nchunk8) r4[k] = __ldg(rp + k);
-            }
           }
           if constexpr (MODE == kModeNone) {
 #pragma unroll
@@ -292,7 +297,7 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
 #pragma unroll
               for (int k = 0; k < 4; ++k) {
                 __half2* a = reinterpret_cast<__half2*>(&o4[k]);
-                const __half2* b = reinterpret_cast<const __half2*>(&r4[k]);
+                const __half2* b = reinterpret_cast<const __half2*>(&r4[g][k]);
 #pragma unroll
                 for (int j = 0; j < 4; ++j) a[j] = __hadd2(a[j], b[j]);
               }

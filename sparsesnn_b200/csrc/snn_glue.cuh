@@ -19,106 +19,167 @@ struct StemParams {
   float tau, decay, v_th, v_reset;
 };
 
-// One thread = one output pixel x 8 consecutive output channels; a block of
-// 256 threads covers 256/(Cout/8) pixels.  Weights are staged in shared
-// memory as [k][cout] (dynamic smem = K*Cout floats, K = Cin*KH*KW); each
-// timestep's 8 spikes leave as one 16-byte store.
-__global__ void __launch_bounds__(256)
+// One thread = one output pixel x 16 consecutive output channels
+// (Cout/16 threads per pixel, 256 threads per block).  Weights are staged in
+// shared memory as [k][cout] (dynamic smem = K*Cout floats, K = Cin*KH*KW);
+// the receptive field is gathered once into registers (KS, CIN compile-time
+// in the fast instantiation; KS = CIN = 0 selects runtime sizes), and each
+// timestep's 16 spikes leave as two 16-byte stores.
+template <int KS, int CIN>
+__global__ void __launch_bounds__(256, 2)
 stem_conv_lif_kernel(const StemParams p) {
   extern __shared__ float ws[];
-  const int K = p.KH * p.KW * p.Cin;
+  const int KH = KS ? KS : p.KH, KW = KS ? KS : p.KW, Cin = CIN ? CIN : p.Cin;
+  const int K = KH * KW * Cin;
+  // Coalesced read of the [Cout][K] source, transposed into [K][Cout].
   for (int i = threadIdx.x; i < K * p.Cout; i += blockDim.x) {
-    const int k = i / p.Cout, co = i - k * p.Cout;
+    const int co = i / K, k = i - co * K;
     // k = (ci*KH + kh)*KW + kw, matching the [Cout][Cin][KH][KW] source.
-    ws[i] = p.w[static_cast<size_t>(co) * K + k];
+    ws[k * p.Cout + co] = p.w[i];
   }
   __syncthreads();
-  const int groups = p.Cout / 8;
+  const int groups = p.Cout / 16;
   const int px_per_block = blockDim.x / groups;
   const int g = threadIdx.x % groups;
-  const long long pix = static_cast<long long>(blockIdx.x) * px_per_block + threadIdx.x / groups;
   const long long P = static_cast<long long>(p.B) * p.OH * p.OW;
-  if (threadIdx.x >= px_per_block * groups || pix >= P) return;
+  if (threadIdx.x >= px_per_block * groups) return;
+  // Persistent blocks: the staged weights serve many pixel chunks.
+  for (long long pix = static_cast<long long>(blockIdx.x) * px_per_block + threadIdx.x / groups;
+       pix < P; pix += static_cast<long long>(gridDim.x) * px_per_block) {
   const int ow = static_cast<int>(pix % p.OW);
   const int oh = static_cast<int>((pix / p.OW) % p.OH);
   const int b = static_cast<int>(pix / (static_cast<long long>(p.OW) * p.OH));
-  const int c0 = g * 8;
-  float sc[8], bi[8], v[8], xb[8];
+  const int c0 = g * 16;
+  float v[16], xb[16];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) { sc[j] = p.scale[c0 + j]; bi[j] = p.bias[c0 + j]; v[j] = 0.f; xb[j] = 0.f; }
+  for (int j = 0; j < 16; ++j) { v[j] = 0.f; xb[j] = 0.f; }
+  const int ih0 = oh * p.stride - p.pad, iw0 = ow * p.stride - p.pad;
   for (int t = 0; t < p.T; ++t) {
     if (t == 0 || p.Tin > 1) {
       const float* xin = p.x + (static_cast<size_t>(p.Tin > 1 ? t : 0) * p.B + b) *
-                                   static_cast<size_t>(p.Cin) * p.H * p.W;
-      float acc[8];
+                                   static_cast<size_t>(Cin) * p.H * p.W;
+      float acc[16];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-      int k = 0;
-      for (int ci = 0; ci < p.Cin; ++ci) {
-        for (int kh = 0; kh < p.KH; ++kh) {
-          const int ih = oh * p.stride + kh - p.pad;
-          for (int kw = 0; kw < p.KW; ++kw, ++k) {
-            const int iw = ow * p.stride + kw - p.pad;
-            if (ih < 0 || ih >= p.H || iw < 0 || iw >= p.W) continue;
-            const float xv = __ldg(xin + (static_cast<size_t>(ci) * p.H + ih) * p.W + iw);
-            const float4 w0 = *reinterpret_cast<const float4*>(ws + k * p.Cout + c0);
-            const float4 w1 = *reinterpret_cast<const float4*>(ws + k * p.Cout + c0 + 4);
-            acc[0] = fmaf(xv, w0.x, acc[0]); acc[1] = fmaf(xv, w0.y, acc[1]);
-            acc[2] = fmaf(xv, w0.z, acc[2]); acc[3] = fmaf(xv, w0.w, acc[3]);
-            acc[4] = fmaf(xv, w1.x, acc[4]); acc[5] = fmaf(xv, w1.y, acc[5]);
-            acc[6] = fmaf(xv, w1.z, acc[6]); acc[7] = fmaf(xv, w1.w, acc[7]);
+      for (int j = 0; j < 16; ++j) acc[j] = 0.f;
+#pragma unroll
+      for (int ci = 0; ci < (CIN ? CIN : 1); ++ci) {
+        for (int cr = 0; cr < (CIN ? 1 : Cin); ++cr) {
+          const int c = CIN ? ci : cr;
+#pragma unroll
+          for (int kh = 0; kh < (KS ? KS : 1); ++kh) {
+            for (int khr = 0; khr < (KS ? 1 : KH); ++khr) {
+              const int kk = KS ? kh : khr;
+              const int ih = ih0 + kk;
+              const bool hok = ih >= 0 && ih < p.H;
+#pragma unroll
+              for (int kw = 0; kw < (KS ? KS : 1); ++kw) {
+                for (int kwr = 0; kwr < (KS ? 1 : KW); ++kwr) {
+                  const int ll = KS ? kw : kwr;
+                  const int iw = iw0 + ll;
+                  const float xv = (hok && iw >= 0 && iw < p.W)
+                                       ? __ldg(xin + (static_cast<size_t>(c) * p.H + ih) * p.W + iw) : 0.f;
+                  const float* wr = ws + ((c * KH + kk) * KW + ll) * p.Cout + c0;
+#pragma unroll
+                  for (int q = 0; q < 4; ++q) {
+                    const float4 w4 = *reinterpret_cast<const float4*>(wr + 4 * q);
+                    acc[4 * q + 0] = fmaf(xv, w4.x, acc[4 * q + 0]);
+                    acc[4 * q + 1] = fmaf(xv, w4.y, acc[4 * q + 1]);
+                    acc[4 * q + 2] = fmaf(xv, w4.z, acc[4 * q + 2]);
+                    acc[4 * q + 3] = fmaf(xv, w4.w, acc[4 * q + 3]);
+                  }
+                }
+              }
+            }
           }
         }
       }
 #pragma unroll
-      for (int j = 0; j < 8; ++j) xb[j] = fmaf(acc[j], sc[j], bi[j]);
+      for (int j = 0; j < 16; ++j) xb[j] = fmaf(acc[j], __ldg(p.scale + c0 + j), __ldg(p.bias + c0 + j));
     }
-    uint32_t packed[4];
+    uint32_t packed[8];
 #pragma unroll
-    for (int j = 0; j < 8; j += 2) {
+    for (int j = 0; j < 16; j += 2) {
       uint32_t bits = 0;
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
         float h;
         if (p.neuron == 0) h = __fadd_rn(__fmul_rn(v[j + u], p.decay), __fdiv_rn(xb[j + u], p.tau));
         else h = __fadd_rn(v[j + u], xb[j + u]);
-        const bool s = (h - p.v_th) >= 0.f;
+        const bool s = h >= p.v_th;
         v[j + u] = s ? p.v_reset : h;
         bits |= (s ? 0x3C00u : 0u) << (16 * u);
       }
       packed[j / 2] = bits;
     }
-    *reinterpret_cast<uint4*>(p.out + (static_cast<size_t>(t) * P + pix) * p.Cout + c0) =
-        make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    uint4* op = reinterpret_cast<uint4*>(p.out + (static_cast<size_t>(t) * P + pix) * p.Cout + c0);
+    op[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    op[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+  }
   }
 }
 
-// One block per image: feat[c] = mean_t mean_hw x[t][b][hw][c];
-// logits[b][n] = feat . fc_w[n] + fc_b[n].  dynamic smem = C floats.
-__global__ void head_pool_fc_kernel(const __half* __restrict__ x, const float* __restrict__ fc_w,
-                                    const float* __restrict__ fc_b, float* __restrict__ logits,
-                                    int T, int B, int HW, int C, int NC) {
-  extern __shared__ float feat[];
-  const int b = blockIdx.x;
-  for (int c = threadIdx.x; c < C; c += blockDim.x) {
-    float tsum = 0.f;
-    for (int t = 0; t < T; ++t) {
-      const __half* xt = x + (static_cast<size_t>(t) * B + b) * static_cast<size_t>(HW) * C + c;
-      float s = 0.f;
-      for (int i = 0; i < HW; ++i) s += __half2float(xt[static_cast<size_t>(i) * C]);
-      tsum += s / static_cast<float>(HW);
+// One block (256 threads) per group of up to kHeadImgs images.  Phase 1:
+// for each image, thread (c8, slot) sums 8 consecutive channels (16-byte
+// loads) over every 4th (t, hw) position; the 4 partial sums are combined
+// in shared memory and scaled: feat = sum / HW / T (exact for the
+// small-integer SEW activations).  Phase 2: one warp per output class reads
+// its weight row once and applies it to every image of the group.
+// dynamic smem = (4 + kHeadImgs) * C floats.
+constexpr int kHeadImgs = 8;
+__global__ void __launch_bounds__(256)
+head_pool_fc_kernel(const __half* __restrict__ x, const float* __restrict__ fc_w,
+                    const float* __restrict__ fc_b, float* __restrict__ logits,
+                    int T, int B, int HW, int C, int NC) {
+  extern __shared__ float sm[];
+  float* part = sm;                          // [4][C]
+  float* feat = sm + 4 * C;                  // [kHeadImgs][C]
+  const int b0 = blockIdx.x * kHeadImgs;
+  const int nimg = min(kHeadImgs, B - b0);
+  const int c8n = C / 8;
+  for (int im = 0; im < nimg; ++im) {
+    const int b = b0 + im;
+    for (int task = threadIdx.x; task < c8n * 4; task += blockDim.x) {
+      const int c8 = task % c8n, slot = task / c8n;
+      float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int pos = slot; pos < T * HW; pos += 4) {
+        const int t = pos / HW, i = pos - t * HW;
+        const uint4 u = __ldg(reinterpret_cast<const uint4*>(
+            x + ((static_cast<size_t>(t) * B + b) * HW + i) * C) + c8);
+        const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __half22float2(h[j]);
+          s[2 * j] += f.x; s[2 * j + 1] += f.y;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) part[slot * C + c8 * 8 + j] = s[j];
     }
-    feat[c] = tsum / static_cast<float>(T);
+    __syncthreads();
+    for (int c = threadIdx.x; c < C; c += blockDim.x)
+      feat[im * C + c] = ((part[c] + part[C + c]) + (part[2 * C + c] + part[3 * C + c])) /
+                         static_cast<float>(HW) / static_cast<float>(T);
+    __syncthreads();
   }
-  __syncthreads();
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, nwarps = blockDim.x / 32;
   for (int n = warp; n < NC; n += nwarps) {
     const float* wr = fc_w + static_cast<size_t>(n) * C;
-    float s = 0.f;
-    for (int c = lane; c < C; c += 32) s = fmaf(feat[c], wr[c], s);
+    float acc[kHeadImgs];
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-    if (lane == 0) logits[static_cast<size_t>(b) * NC + n] = s + (fc_b ? fc_b[n] : 0.f);
+    for (int im = 0; im < kHeadImgs; ++im) acc[im] = 0.f;
+    for (int c = lane; c < C; c += 32) {
+      const float w = __ldg(wr + c);
+#pragma unroll
+      for (int im = 0; im < kHeadImgs; ++im) acc[im] = fmaf(feat[im * C + c], w, acc[im]);
+    }
+#pragma unroll
+    for (int im = 0; im < kHeadImgs; ++im) {
+      float a = acc[im];
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
+      if (lane == 0 && im < nimg)
+        logits[static_cast<size_t>(b0 + im) * NC + n] = a + (fc_b ? fc_b[n] : 0.f);
+    }
   }
 }
 

@@ -1,0 +1,208 @@
+"""The sengine-facing backend: fused anchors -> callables, and the per-node
+export shims with the reference ``init``/``call`` ABI."""
+import ctypes
+import subprocess
+import sys
+import types
+from dataclasses import dataclass, field
+from enum import Enum
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from sparsesnn_b200 import build, runtime as rt
+from sparsesnn_b200.sengine_backend import B200Compiler, export_all_kernels
+
+REF = Path("/root/reference")
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _lib():
+    build.build()
+    rt.load()
+
+
+# Minimal stand-ins with the reference IR field names (sengine/ir.py:180-269).
+class KV(Enum):
+    TileLangFusedConvBNIF = 1
+    TileLangFusedConv1x1BNIF = 2
+    ZeroCost = 3
+
+
+class NT(Enum):
+    LIF = 1
+    IF = 2
+
+
+@dataclass
+class CP:
+    in_channels: int
+    out_channels: int
+    kernel_h: int = 3
+    kernel_w: int = 3
+    stride_h: int = 1
+    stride_w: int = 1
+    pad_h: int = 1
+    pad_w: int = 1
+
+
+@dataclass
+class NP:
+    neuron_type: NT = NT.LIF
+    T: int = 4
+    tau: float = 2.0
+    v_threshold: float = 1.0
+    v_reset: float = 0.0
+
+
+@dataclass
+class Nd:
+    id: int
+    assigned_kernel: KV = KV.ZeroCost
+    conv_params: CP = None
+    neuron_params: NP = None
+    input_shapes: list = field(default_factory=list)
+    extra_attrs: dict = field(default_factory=dict)
+
+
+class IR:
+    def __init__(self, nodes):
+        self.nodes = {n.id: n for n in nodes}
+
+
+def mock_ir():
+    return IR([
+        Nd(0, KV.TileLangFusedConvBNIF, CP(64, 128), None, [(8, 64, 16, 16)],
+           {"absorbed_nids": [1]}),
+        Nd(1, KV.ZeroCost, None, NP(NT.LIF, tau=2.0, v_threshold=1.0)),
+        Nd(2, KV.TileLangFusedConv1x1BNIF, CP(128, 256, 1, 1, 2, 2, 0, 0), None,
+           [(8, 128, 16, 16)], {"absorbed_nids": [3, 4], "residual_nid": 9}),
+        Nd(3, KV.ZeroCost, None, NP(NT.IF, v_threshold=0.5)),
+        Nd(4, KV.ZeroCost),
+    ])
+
+
+def test_compile_all_reads_fusion_annotations():
+    kern = B200Compiler(mock_ir(), T=4, batch_size=2).compile_all()
+    assert sorted(kern) == [0, 2]
+    k0, k2 = kern[0], kern[2]
+    assert (k0.desc.Cin, k0.desc.Cout, k0.desc.KH, k0.desc.stride) == (64, 128, 3, 1)
+    assert k0.desc.neuron == rt.SNN_NEURON_LIF and k0.desc.tau == 2.0 and not k0.residual
+    assert (k2.desc.KH, k2.desc.stride, k2.desc.pad) == (1, 2, 0)
+    assert k2.desc.neuron == rt.SNN_NEURON_IF and k2.desc.v_threshold == 0.5 and k2.residual
+    assert (k2.OH, k2.OW) == (8, 8)
+
+
+def test_export_shims_have_reference_symbols(tmp_path):
+    kern = B200Compiler(mock_ir(), T=4, batch_size=2).compile_all()
+    sos = export_all_kernels(kern, None, str(tmp_path))
+    assert set(sos) == {0, 2}
+    for so in set(sos.values()):
+        out = subprocess.run(["nm", "-D", "--defined-only", so], capture_output=True, text=True,
+                             check=True).stdout
+        names = {line.split()[-1] for line in out.splitlines() if line.strip()}
+        assert {"init", "call", "call_res"} <= names
+        lib = ctypes.CDLL(so)
+        assert lib.init is not None and lib.call is not None
+
+
+@pytest.mark.skipif(not (REF / "sengine" / "fusion_strategy.py").exists(),
+                    reason="reference checkout not present")
+def test_reference_apply_fusion_drives_compiler():
+    """Build a Conv->LIF->Conv->LIF->Add graph with the reference IR classes,
+    run the reference's own apply_fusion, and compile its fused anchors."""
+    # onnx and colorlog are not installed; the IR and fusion modules only
+    # need them to import.
+    import logging
+    for mod in ("onnx", "onnx.numpy_helper", "onnx.helper"):
+        sys.modules.setdefault(mod, types.ModuleType(mod))
+    if "colorlog" not in sys.modules:
+        cl = types.ModuleType("colorlog")
+        cl.__dict__.update({k: v for k, v in vars(logging).items() if not k.startswith("__")})
+
+        class _ColoredFormatter(logging.Formatter):
+            def __init__(self, *a, log_colors=None, secondary_log_colors=None, reset=True,
+                         **kw):
+                super().__init__(*a, **kw)
+        cl.ColoredFormatter = _ColoredFormatter
+        sys.modules["colorlog"] = cl
+    onnx = sys.modules["onnx"]
+    for attr in ("numpy_helper", "helper"):
+        setattr(onnx, attr, sys.modules["onnx." + attr])
+    for attr in ("ModelProto", "TensorProto", "NodeProto", "GraphProto", "load", "shape_inference"):
+        setattr(onnx, attr, object)
+    if str(REF) not in sys.path:
+        sys.path.insert(0, str(REF))
+    try:
+        from sengine import ir as sir
+        from sengine.fusion_strategy import apply_fusion
+    except Exception as e:  # pragma: no cover - depends on the checkout
+        pytest.skip(f"reference sengine not importable: {e}")
+    g = sir.EngineIR()
+
+    def conv(name, inp, out, cin, cout, shape_in, shape_out):
+        n = sir.Node(id=-1, name=name, op_type=sir.OpType.Conv2d, input_names=[inp],
+                     output_names=[out], input_shapes=[shape_in], output_shapes=[shape_out])
+        n.conv_params = sir.ConvParams(in_channels=cin, out_channels=cout, kernel_h=3,
+                                       kernel_w=3, pad_h=1, pad_w=1)
+        n.bound_type = sir.BoundType.COMPUTE
+        return g.add_node(n)
+
+    def lif(name, inp, out, shape):
+        n = sir.Node(id=-1, name=name, op_type=sir.OpType.LIF, input_names=[inp],
+                     output_names=[out], input_shapes=[shape], output_shapes=[shape])
+        n.neuron_params = sir.NeuronParams(neuron_type=sir.NeuronType.LIF, T=4, tau=2.0,
+                                           v_threshold=1.0)
+        n.bound_type = sir.BoundType.MEMORY
+        return g.add_node(n)
+
+    s = (8, 64, 16, 16)
+    lif("l0", "x", "x0", s)              # block input, produced by an earlier neuron
+    c1 = conv("c1", "x0", "y1", 64, 64, s, s)
+    lif("l1", "y1", "s1", s)
+    c2 = conv("c2", "s1", "y2", 64, 64, s, s)
+    lif("l2", "y2", "s2", s)
+    add = sir.Node(id=-1, name="add", op_type=sir.OpType.Add, input_names=["s2", "x0"],
+                   output_names=["out"], input_shapes=[s, s], output_shapes=[s])
+    add.bound_type = sir.BoundType.MEMORY
+    g.add_node(add)
+    g.build_edges()
+    g.compute_topo_order()
+    apply_fusion(g, "slicer", batch_size=2)
+    kern = B200Compiler(g, T=4, batch_size=2).compile_all()
+    assert c1 in kern and c2 in kern
+    assert kern[c1].desc.neuron == rt.SNN_NEURON_LIF and kern[c1].desc.tau == 2.0
+    assert not kern[c1].residual
+    # c2 absorbed LIF + Add with the block input as residual: the SEW epilogue.
+    assert kern[c2].residual
+
+
+@pytest.mark.gpu
+def test_exported_shim_call_matches_library(cuda_device, tmp_path):
+    import torch
+    from conftest import load_layer_case
+    from sparsesnn_b200.layer import fold_bn
+    g = load_layer_case("c3s1")
+    ir = IR([Nd(0, KV.TileLangFusedConvBNIF, CP(g["C"], g["F"]), NP(),
+                [(g["B"], g["C"], g["H"], g["W"])])])
+    kern = B200Compiler(ir, T=g["T"], batch_size=g["B"]).compile_all()[0]
+    so = export_all_kernels({0: kern}, None, str(tmp_path))[0]
+    shim = ctypes.CDLL(so)
+    shim.call.argtypes = [ctypes.c_void_p] * 7
+    assert shim.init() == 0
+    x = torch.from_numpy(np.transpose(g["x"].astype(np.float32), (0, 1, 3, 4, 2))
+                         .reshape(g["T"] * g["B"], g["H"], g["W"], g["C"]).copy()).cuda().half()
+    w = torch.from_numpy(kern.pack(g["w"])).cuda()
+    sc, bi = (torch.from_numpy(a).cuda() for a in fold_bn(g["gamma"], g["beta"], g["mean"],
+                                                            g["var"]))
+    st1 = torch.zeros((g["B"] * g["H"] * g["W"], g["F"]), device="cuda")
+    st2 = torch.zeros_like(st1)
+    out1 = torch.empty((g["T"] * g["B"], g["H"], g["W"], g["F"]), dtype=torch.float16,
+                       device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    assert shim.call(x.data_ptr(), w.data_ptr(), st1.data_ptr(), sc.data_ptr(), bi.data_ptr(),
+                     out1.data_ptr(), s) == 0
+    out2 = kern(x, w, st2, sc, bi)
+    torch.cuda.synchronize()
+    assert torch.equal(out1, out2) and torch.equal(st1, st2)
