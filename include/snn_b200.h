@@ -67,6 +67,18 @@ int snn_abi_version(void);
  * sengine/csrc/cpp_executor.cu:637-652). */
 int snn_init(void);
 
+/* Kernel variants behind snn_conv_forward (all fused and numerically
+ * equivalent up to fp32 accumulation order):
+ *   GENERIC        streamed weights, one activation tile per filter tap;
+ *   HALO_RESIDENT  stride-1 3x3, weights resident in shared memory, one
+ *                  input halo per (timestep, 64-channel slice) shared by all taps;
+ *   HALO_STREAM    stride-1 3x3 on images >= 8x8, T <= 4, streamed weights
+ *                  reused across all timesteps, halo-shared taps. */
+enum { SNN_VARIANT_GENERIC = 0, SNN_VARIANT_HALO_RESIDENT = 1, SNN_VARIANT_HALO_STREAM = 2 };
+
+/* Variant snn_conv_forward will use for a descriptor (>= 0), or an error. */
+int snn_conv_variant(const snn_conv_desc* d);
+
 /* Output spatial size for a descriptor. */
 int snn_conv_out_shape(const snn_conv_desc* d, int32_t* OH, int32_t* OW);
 

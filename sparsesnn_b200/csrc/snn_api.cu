@@ -15,6 +15,7 @@
 #include "../../include/snn_b200.h"
 #include "snn_conv.cuh"
 #include "snn_conv_halo.cuh"
+#include "snn_conv_halo_stream.cuh"
 #include "snn_glue.cuh"
 
 namespace {
@@ -70,6 +71,20 @@ HaloKernel halo_kernel_fn(int bn, int mode, bool res) {
   return bn == 128 ? halo_kernel_fn_bn<128>(mode, res) : halo_kernel_fn_bn<64>(mode, res);
 }
 
+using HsKernel = void (*)(const snn::ConvParams);
+
+HsKernel hs_kernel_fn(int mode, bool res) {
+  switch (mode * 2 + (res ? 1 : 0)) {
+    case 0: return snn::fused_sparse_conv_halo_stream_kernel<snn::kModeLifHalf, false>;
+    case 1: return snn::fused_sparse_conv_halo_stream_kernel<snn::kModeLifHalf, true>;
+    case 2: return snn::fused_sparse_conv_halo_stream_kernel<snn::kModeLifDiv, false>;
+    case 3: return snn::fused_sparse_conv_halo_stream_kernel<snn::kModeLifDiv, true>;
+    case 4: return snn::fused_sparse_conv_halo_stream_kernel<snn::kModeIf, false>;
+    case 5: return snn::fused_sparse_conv_halo_stream_kernel<snn::kModeIf, true>;
+    default: return snn::fused_sparse_conv_halo_stream_kernel<snn::kModeNone, false>;
+  }
+}
+
 constexpr int kSmemLimit = 232448;          // opt-in dynamic smem per block on sm_100
 constexpr int kHaloMaxWeightBytes = 160 * 1024;
 
@@ -104,6 +119,10 @@ int ensure_init() {
         if (e != cudaSuccess)
           return g_init_status = fail(SNN_E_CUDA, "smem attribute: %s", cudaGetErrorString(e));
       }
+      e = cudaFuncSetAttribute(hs_kernel_fn(mode, res != 0),
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, snn::kHsSmemBytes);
+      if (e != cudaSuccess)
+        return g_init_status = fail(SNN_E_CUDA, "smem attribute: %s", cudaGetErrorString(e));
     }
   }
   return g_init_status = SNN_OK;
@@ -155,6 +174,17 @@ int encode(CUtensorMap* map, int rank, const void* base, const cuuint64_t* dims,
   return SNN_OK;
 }
 
+// Which kernel serves a descriptor (see the SNN_VARIANT_* values).
+int select_variant(const snn_conv_desc* d, const Geometry& g) {
+  if (d->flags & SNN_FLAG_FORCE_GENERIC) return SNN_VARIANT_GENERIC;
+  const bool s1_3x3 = d->stride == 1 && d->KH == 3 && d->KW == 3 && d->pad == 1;
+  if (!s1_3x3) return SNN_VARIANT_GENERIC;
+  const int a_bytes = g.n_kb * snn::kABytes;
+  if (a_bytes <= kHaloMaxWeightBytes && g.OH >= 8) return SNN_VARIANT_HALO_RESIDENT;
+  if (g.OH >= 8 && g.OW >= 8 && d->T <= snn::kHsMaxT) return SNN_VARIANT_HALO_STREAM;
+  return SNN_VARIANT_GENERIC;
+}
+
 int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, float* state,
                 const float* scale, const float* bias, const void* residual, void* out,
                 void* stream) {
@@ -197,7 +227,8 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
   p.n_m = g.Fpad / snn::kBM;
   p.box_bytes = tw * th * tn * snn::kKB * 2;
   const cuuint32_t box5[5] = {static_cast<cuuint32_t>(snn::kKB), static_cast<cuuint32_t>(tw),
-                              static_cast<cuuint32_t>(th), static_cast<cuuint32_t>(tn), 1};
+                              static_cast<cuuint32_t>(th), static_cast<cuuint32_t>(tn),
+                              static_cast<cuuint32_t>(snn::kTC)};
   {
     const size_t C = d->Cin, W = d->W, H = d->H, B = d->B;
     const char* base = static_cast<const char*>(data);
@@ -248,10 +279,8 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
   // 128-channel weight slice fits in shared memory and images tall enough
   // for 8-row tiles.
   const int a_bytes = g.n_kb * snn::kABytes;
-  const bool halo = d->stride == 1 && d->KH == 3 && d->KW == 3 &&
-                    d->pad == d->KH / 2 && a_bytes <= kHaloMaxWeightBytes && g.OH >= 8 &&
-                    !(d->flags & SNN_FLAG_FORCE_GENERIC);
-  if (halo) {
+  const int variant = select_variant(d, g);
+  if (variant == SNN_VARIANT_HALO_RESIDENT) {
     snn::HaloParams hp;
     memset(&hp, 0, sizeof(hp));
     const int bn = g.OH >= 16 ? 128 : 64;
@@ -286,6 +315,36 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
       return SNN_OK;
     }
   }
+  // Streaming-weight halo variant: stride-1 3x3 "same" convs on images of
+  // at least 8x8 whose weights do not fit in shared memory, T <= 4.
+  if (variant == SNN_VARIANT_HALO_STREAM) {
+    snn::ConvParams ph = p;
+    ph.tw = 8; ph.th = 8; ph.tn = 1;
+    ph.tiles_w = (g.OW + 7) / 8;
+    ph.tiles_h = (g.OH + 7) / 8;
+    ph.n_px_tiles = ph.tiles_w * ph.tiles_h * d->B;
+    const size_t C = d->Cin, W = d->W, H = d->H, B = d->B;
+    cuuint64_t dims[5] = {C, W, H, B, static_cast<cuuint64_t>(d->T)};
+    cuuint64_t strides[4] = {C * 2, W * C * 2, H * W * C * 2, B * H * W * C * 2};
+    cuuint32_t box[5] = {static_cast<cuuint32_t>(snn::kKB), 10, 10, 1,
+                         static_cast<cuuint32_t>(snn::kHsMaxT)};
+    if ((st = encode(&ph.tmap_b[0], 5, data, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)))
+      return st;
+    {  // weights as (Cin/2 el of one tap, Fpad rows, 9 taps): one box = 3 taps x 128 rows
+      cuuint64_t wd[3] = {C / 2, static_cast<cuuint64_t>(g.Fpad), 9};
+      cuuint64_t ws[2] = {static_cast<cuuint64_t>(g.K / 2) * 2, (C / 2) * 2};
+      cuuint32_t wb[3] = {snn::kKB / 2, snn::kBM, 3};
+      if ((st = encode(&ph.tmap_b[1], 3, weight, wd, ws, wb, CU_TENSOR_MAP_SWIZZLE_64B))) return st;
+    }
+    const int per_m = std::max(1, std::min(ph.n_px_tiles, g_num_sms / ph.n_m));
+    const long long grid = static_cast<long long>(per_m) * ph.n_m;
+    hs_kernel_fn(mode, residual != nullptr)<<<static_cast<unsigned>(grid), snn::kHaloThreads,
+                                               snn::kHsSmemBytes,
+                                               static_cast<cudaStream_t>(stream)>>>(ph);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));
+    return SNN_OK;
+  }
   const int per_m = std::max(1, std::min(p.n_px_tiles, g_num_sms / p.n_m));
   const long long grid = static_cast<long long>(per_m) * p.n_m;
   if (grid > 0x7fffffffLL) return fail(SNN_E_INVALID, "grid too large");
@@ -306,6 +365,13 @@ int snn_abi_version(void) { return SNN_ABI_VERSION; }
 int snn_init(void) { return ensure_init(); }
 
 const char* snn_last_error_message(void) { return g_msg; }
+
+int snn_conv_variant(const snn_conv_desc* d) {
+  Geometry g;
+  int st = check_desc(d, &g);
+  if (st) return st;
+  return select_variant(d, g);
+}
 
 int snn_conv_out_shape(const snn_conv_desc* d, int32_t* OH, int32_t* OW) {
   Geometry g;
@@ -449,13 +515,13 @@ int snn_head_forward(int32_t T, int32_t B, int32_t HW, int32_t C, int32_t NC, co
   int st = ensure_init();
   if (st) return st;
   if (!x || !fc_w || !logits) return fail(SNN_E_INVALID, "null pointer");
-  if (T < 1 || B < 1 || HW < 1 || C < 8 || C % 8 || C > 1024 || NC < 1)
-    return fail(SNN_E_INVALID, "bad head shape (C multiple of 8, <= 1024)");
+  if (T < 1 || B < 1 || HW < 1 || C < 8 || C % 8 || C > 704 || NC < 1)
+    return fail(SNN_E_INVALID, "bad head shape (C multiple of 8, <= 704)");
   if (reinterpret_cast<uintptr_t>(x) & 15) return fail(SNN_E_INVALID, "x must be 16-byte aligned");
-  const int threads = 256;
-  const size_t smem = static_cast<size_t>(4 + snn::kHeadImgs) * C * sizeof(float);
-  const int nblk = (B + snn::kHeadImgs - 1) / snn::kHeadImgs;
-  snn::head_pool_fc_kernel<<<nblk, threads, smem, static_cast<cudaStream_t>(stream)>>>(
+  if (reinterpret_cast<uintptr_t>(fc_w) & 15) return fail(SNN_E_INVALID, "fc_w must be 16-byte aligned");
+  const int threads = 1024;
+  const size_t smem = static_cast<size_t>(snn::kHeadSlots + 1) * C * sizeof(float);
+  snn::head_pool_fc_kernel<<<B, threads, smem, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __half*>(x), fc_w, fc_b, logits, T, B, HW, C, NC);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));

@@ -171,7 +171,9 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
             if (!mbar_wait_bounded(&empty[stage], phase ^ 1, p.timeout_ns)) {
               atomicOr(p.err, kErrTimeoutEmpty); *abort_flag = 1; stop = true; break;
             }
-            mbar_arrive_expect_tx(&full[stage], kABytes + tcn * p.box_bytes);
+            // One activation box spans the chunk's kTC timesteps (a timestep
+            // beyond T is outside the tensor: zero-filled, never read).
+            mbar_arrive_expect_tx(&full[stage], kABytes + kTC * p.box_bytes);
             tma_load_2d(sA + stage * kABytes, &p.tmap_a, &full[stage], kb * (kKB / 2),
                         m_tile * kBM);
             const int tap = kb / p.cin_blocks;
@@ -182,10 +184,8 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
               map = (hoff & 1) * 2 + (woff & 1);
               hoff = floordiv2(hoff); woff = floordiv2(woff);
             }
-            for (int tt = 0; tt < tcn; ++tt) {
-              tma_load_5d(sB + (stage * kTC + tt) * kBBytes, &p.tmap_b[map], &full[stage],
-                          cb * kKB, tc.w0 + woff, tc.h0 + hoff, tc.n0, t0 + tt);
-            }
+            tma_load_5d(sB + stage * kTC * kBBytes, &p.tmap_b[map], &full[stage],
+                        cb * kKB, tc.w0 + woff, tc.h0 + hoff, tc.n0, t0);
             ++issued;
             if (++stage == kStages) { stage = 0; phase ^= 1; }
           }
@@ -234,7 +234,7 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
               const uint32_t id = idesc | (ecol & 1u);
               const uint64_t adesc = smem_desc_kmajor(a_base + 32 * s, 512, 4);
               for (int tt = 0; tt < tcn; ++tt) {
-                const uint64_t bdesc = smem_desc_kmajor(b_base + tt * kBBytes + 64 * s, 1024, 2);
+                const uint64_t bdesc = smem_desc_kmajor(b_base + tt * p.box_bytes + 64 * s, 1024, 2);
                 mma_sp_f16(d_base + tt * kBN, adesc, bdesc, e_addr, id,
                            (kb > 0 || s > 0) ? 1u : 0u);
               }

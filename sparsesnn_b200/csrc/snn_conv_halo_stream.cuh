@@ -1,0 +1,344 @@
+// Streaming-weight halo variant for stride-1 3x3 convolutions whose weight
+// slice is too large to stay resident (e.g. Cin = 256), on images of at
+// least 8x8.  A tile is 8x8 output pixels of one image (UMMA N = 64); all T
+// timesteps (T <= 4) accumulate in TMEM at once, so every weight tile that
+// enters shared memory is reused for all T timesteps -- consecutive MMAs
+// share the A operand through the tensor core's A collector
+// (fill / use / lastuse) and A is read from shared memory once per tap.
+//
+// Per (tile, 64-channel slice cb): the producer loads the T input halos
+// (10x10 pixels each) as ONE 5D TMA box spanning the timesteps, then the
+// slice's weights in three kernel-row stages, each ONE 3D box of 3 taps x
+// 128 rows.  A TMA box costs a fixed few hundred cycles whatever its size,
+// so the kernel issues as few, large boxes as it can.  Every tap reads a
+// halo through a descriptor offset of (kh*10 + kw) rows.
+//
+// Warp roles as in the resident halo kernel: 0..7 epilogue, 8..11 metadata,
+// 10 MMA + TMEM owner, 11 TMA.
+#pragma once
+#include "snn_conv_halo.cuh"
+
+namespace snn {
+
+constexpr int kHsMaxT = 4;
+constexpr int kHsBN = 64;
+constexpr int kHsHaloStages = 2;                   // each stage: the halos of all T timesteps
+constexpr int kHsAStages = 4;
+constexpr int kHsAStageBytes = 3 * kABytes;        // one kernel row: 3 taps, one 3D TMA box
+constexpr int kHsHaloBytes = 10 * 10 * kKB * 2;    // 12800 per timestep
+constexpr int kHsHaloStride = kHsMaxT * kHsHaloBytes;  // 51200 (1024-aligned)
+constexpr int kHsMetaCol = 256;
+constexpr int kHsSmemBytes = kHsAStages * kHsAStageBytes + kHsHaloStages * kHsHaloStride +
+                             kEpiWarps * kXposeBytes + 512 + 1024;
+
+template <int OP>
+__device__ __forceinline__ void mma_sp_f16_coll(uint32_t d, uint64_t a, uint64_t b, uint32_t e,
+                                                uint32_t id, uint32_t acc) {
+  if constexpr (OP == 0) {
+    mma_sp_f16(d, a, b, e, id, acc);
+  } else if constexpr (OP == 1) {
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.sp.cta_group::1.kind::f16.collector::a::fill [%0], %1, %2, [%5], %3, {%6, %6, %6, %6}, p;\n\t}"
+        ::"r"(d), "l"(a), "l"(b), "r"(id), "r"(acc), "r"(e), "r"(0u) : "memory");
+  } else if constexpr (OP == 2) {
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.sp.cta_group::1.kind::f16.collector::a::use [%0], %1, %2, [%5], %3, {%6, %6, %6, %6}, p;\n\t}"
+        ::"r"(d), "l"(a), "l"(b), "r"(id), "r"(acc), "r"(e), "r"(0u) : "memory");
+  } else {
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.sp.cta_group::1.kind::f16.collector::a::lastuse [%0], %1, %2, [%5], %3, {%6, %6, %6, %6}, p;\n\t}"
+        ::"r"(d), "l"(a), "l"(b), "r"(id), "r"(acc), "r"(e), "r"(0u) : "memory");
+  }
+}
+
+template <int MODE, bool RES>
+__global__ void __launch_bounds__(kHaloThreads, 1)
+fused_sparse_conv_halo_stream_kernel(const __grid_constant__ ConvParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;                                              // weight ring
+  uint8_t* sH = smem + kHsAStages * kHsAStageBytes;                // halo ring
+  uint8_t* sX = sH + kHsHaloStages * kHsHaloStride;                // epilogue transposes
+  uint64_t* a_full = reinterpret_cast<uint64_t*>(sX + kEpiWarps * kXposeBytes);
+  uint64_t* a_empty = a_full + kHsAStages;
+  uint64_t* h_full = a_empty + kHsAStages;
+  uint64_t* h_empty = h_full + kHsHaloStages;
+  uint64_t* acc_full = h_empty + kHsHaloStages;   // [kHsMaxT]
+  uint64_t* acc_empty = acc_full + kHsMaxT;       // [kHsMaxT]
+  uint64_t* meta_ready = acc_empty + kHsMaxT;
+  uint64_t* drain = meta_ready + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int m_tile = blockIdx.x % p.n_m;
+  const int first_pt = blockIdx.x / p.n_m;
+  const int pt_step = gridDim.x / p.n_m;
+  const int n_meta = 2 * p.n_kb;
+  const int T = p.T;
+  // CTAs start their channel-slice loop at different slices so that the CTAs
+  // sharing a weight slice do not all request the same weight rows at once.
+  const int cb_rot = first_pt % p.cin_blocks;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kHsAStages; ++s) { mbar_init(&a_full[s], 1); mbar_init(&a_empty[s], 1); }
+    for (int s = 0; s < kHsHaloStages; ++s) { mbar_init(&h_full[s], 1); mbar_init(&h_empty[s], 1); }
+    for (int t = 0; t < kHsMaxT; ++t) { mbar_init(&acc_full[t], 1); mbar_init(&acc_empty[t], kEpiThreads); }
+    mbar_init(meta_ready, 128);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == kHaloTmaWarp && lane == 0) { prefetch_tmap(&p.tmap_b[0]); prefetch_tmap(&p.tmap_b[1]); }
+  if (warp == kHaloMmaWarp) { tmem_alloc(tmem_slot, kHaloTmemCols); tmem_relinquish(); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp >= kEpiWarps) {
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    const uint32_t* src = p.meta + (static_cast<size_t>(m_tile) * n_meta) * kBM + row;
+    for (int j = 0; j < n_meta; j += 8) {
+      uint32_t r[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        r[i] = (j + i < n_meta) ? __ldg(src + static_cast<size_t>(j + i) * kBM) : 0x44444444u;
+      tmem_st8(lane_base + kHsMetaCol + j, r);
+    }
+    tmem_st_wait();
+    tc_fence_before();
+    mbar_arrive(meta_ready);
+  }
+
+  if (warp == kHaloTmaWarp) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int as = 0, hs = 0; uint32_t aph = 0, hph = 0;
+      int a_issued = 0, h_issued = 0;
+      bool stop = false;
+      for (int pt = first_pt; pt < p.n_px_tiles && !stop; pt += pt_step) {
+        const TileCoord tc = tile_coord(p, pt);
+        for (int cbi = 0; cbi < p.cin_blocks && !stop; ++cbi) {
+          const int cb = (cbi + cb_rot) % p.cin_blocks;
+          if (*abort_flag) { stop = true; break; }
+          if (!mbar_wait_bounded(&h_empty[hs], hph ^ 1, p.timeout_ns)) {
+            atomicOr(p.err, kErrTimeoutEmpty); *abort_flag = 1; stop = true; break;
+          }
+          // All T halos in one box (timesteps beyond T are outside the tensor:
+          // zero-filled and never read).
+          mbar_arrive_expect_tx(&h_full[hs], kHsHaloStride);
+          tma_load_5d(sH + hs * kHsHaloStride, &p.tmap_b[0], &h_full[hs], cb * kKB,
+                      tc.w0 - 1, tc.h0 - 1, tc.n0, 0);
+          ++h_issued;
+          if (++hs == kHsHaloStages) { hs = 0; hph ^= 1; }
+          for (int kh = 0; kh < 3 && !stop; ++kh) {
+            if (*abort_flag) { stop = true; break; }
+            if (!mbar_wait_bounded(&a_empty[as], aph ^ 1, p.timeout_ns)) {
+              atomicOr(p.err, kErrTimeoutEmpty); *abort_flag = 1; stop = true; break;
+            }
+            // Weights of taps (kh, 0..2) for slice cb: [tap][128 rows][32 el].
+            mbar_arrive_expect_tx(&a_full[as], kHsAStageBytes);
+            tma_load_3d(sA + as * kHsAStageBytes, &p.tmap_b[1], &a_full[as], cb * (kKB / 2),
+                        m_tile * kBM, kh * 3);
+            ++a_issued;
+            if (++as == kHsAStages) { as = 0; aph ^= 1; }
+          }
+        }
+      }
+      for (int i = 0; i < min(h_issued, kHsHaloStages); ++i) {
+        const int back = h_issued - 1 - i;
+        if (!mbar_wait_bounded(&h_full[back % kHsHaloStages], (back / kHsHaloStages) & 1, p.timeout_ns))
+          atomicOr(p.err, kErrTimeoutFull);
+      }
+      for (int i = 0; i < min(a_issued, kHsAStages); ++i) {
+        const int back = a_issued - 1 - i;
+        if (!mbar_wait_bounded(&a_full[back % kHsAStages], (back / kHsAStages) & 1, p.timeout_ns))
+          atomicOr(p.err, kErrTimeoutFull);
+      }
+    }
+  } else if (warp == kHaloMmaWarp) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(kBM, kHsBN, true);
+      if (!mbar_wait_bounded(meta_ready, 0, p.timeout_ns)) { atomicOr(p.err, kErrTimeoutMeta); *abort_flag = 1; }
+      tc_fence_after();
+      const uint32_t a_base = smem_u32(sA);
+      const uint32_t h_base = smem_u32(sH);
+      int as = 0, hs = 0; uint32_t aph = 0, hph = 0;
+      int tile_it = 0;
+      bool stop = *abort_flag != 0;
+      for (int pt = first_pt; pt < p.n_px_tiles && !stop; pt += pt_step) {
+        // Every timestep's accumulator must be drained by the epilogue.
+        for (int t = 0; t < T && !stop; ++t) {
+          if (!mbar_wait_bounded(&acc_empty[t], (tile_it & 1) ^ 1, p.timeout_ns)) {
+            atomicOr(p.err, kErrTimeoutAccEmpty); *abort_flag = 1; stop = true;
+          }
+        }
+        if (stop) break;
+        tc_fence_after();
+        for (int cbi = 0; cbi < p.cin_blocks && !stop; ++cbi) {
+          const int cb = (cbi + cb_rot) % p.cin_blocks;
+          if (!mbar_wait_bounded(&h_full[hs], hph, p.timeout_ns)) {
+            atomicOr(p.err, kErrTimeoutFull); *abort_flag = 1; stop = true; break;
+          }
+          const uint32_t hstage = h_base + hs * kHsHaloStride;
+          tc_fence_after();
+          for (int kh = 0; kh < 3; ++kh) {
+            if (!mbar_wait_bounded(&a_full[as], aph, p.timeout_ns)) {
+              atomicOr(p.err, kErrTimeoutFull); *abort_flag = 1; stop = true; break;
+            }
+            tc_fence_after();
+            const uint32_t abase = a_base + as * kHsAStageBytes;
+#pragma unroll
+            for (int kw = 0; kw < 3; ++kw) {
+              const int kb = (kh * 3 + kw) * p.cin_blocks + cb;
+              const uint32_t boff = static_cast<uint32_t>(kh * 10 + kw) * 128;
+#pragma unroll
+              for (int s = 0; s < 2; ++s) {
+                const uint32_t ecol = kHsMetaCol + 2 * kb + s;
+                const uint32_t e_addr = tmem + (ecol & ~1u);
+                const uint32_t id = idesc | (ecol & 1u);
+                const uint64_t adesc = smem_desc_kmajor(abase + kw * kABytes + 32 * s, 512, 4);
+                const uint32_t acc = (cbi > 0 || kh > 0 || kw > 0 || s > 0) ? 1u : 0u;
+                const uint32_t bt = hstage + boff + 64 * s;    // timestep t at + t*kHsHaloBytes
+                if (T == 1) {
+                  mma_sp_f16_coll<0>(tmem, adesc, smem_desc_kmajor(bt, 1280, 2), e_addr, id, acc);
+                } else {
+                  mma_sp_f16_coll<1>(tmem, adesc, smem_desc_kmajor(bt, 1280, 2), e_addr, id, acc);
+                  for (int t = 1; t < T - 1; ++t)
+                    mma_sp_f16_coll<2>(tmem + t * kHsBN, adesc,
+                                       smem_desc_kmajor(bt + t * kHsHaloBytes, 1280, 2), e_addr, id, acc);
+                  mma_sp_f16_coll<3>(tmem + (T - 1) * kHsBN, adesc,
+                                     smem_desc_kmajor(bt + (T - 1) * kHsHaloBytes, 1280, 2), e_addr, id, acc);
+                }
+              }
+            }
+            mma_commit(&a_empty[as]);
+            if (++as == kHsAStages) { as = 0; aph ^= 1; }
+          }
+          if (stop) break;
+          mma_commit(&h_empty[hs]);          // this slice's halos are consumed
+          if (++hs == kHsHaloStages) { hs = 0; hph ^= 1; }
+        }
+        if (stop) break;
+        for (int t = 0; t < T; ++t) mma_commit(&acc_full[t]);
+        ++tile_it;
+      }
+      mma_commit(drain);
+      if (!mbar_wait_bounded(drain, 0, p.timeout_ns)) atomicOr(p.err, kErrTimeoutDrain);
+    }
+  } else if (warp < kEpiWarps) {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const int half = warp >> 2;                  // pixel columns [32*half, 32*half+32)
+    const int row = q * 32 + lane;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    const int cout = m_tile * kBM + row;
+    const bool cvalid = cout < p.F;
+    const int cbase = m_tile * kBM + q * 32;
+    const bool warp_live = cbase < p.F;
+    const float sc = cvalid ? p.scale[cout] : 0.f;
+    const float bi = cvalid ? p.bias[cout] : 0.f;
+    const float sx = MODE == kModeLifHalf ? sc * 0.5f : sc;
+    const float bx = MODE == kModeLifHalf ? bi * 0.5f : bi;
+    const long long P = static_cast<long long>(p.B) * p.OH * p.OW;
+    const int nchunk8 = max(0, min(4, (p.F - cbase) / 8));
+    uint8_t* xb = sX + warp * kXposeBytes;
+    auto xoff = [](int px, int c8) { return px * 64 + ((c8 ^ ((px >> 1) & 3)) << 4); };
+
+    int tile_it = 0;
+    bool stop = false;
+    for (int pt = first_pt; pt < p.n_px_tiles && !stop; pt += pt_step) {
+      const TileCoord tc = tile_coord(p, pt);
+      const int col = half * 32 + lane;
+      const int oh = tc.h0 + col / 8, ow = tc.w0 + (col & 7);
+      const long long my_px = (oh < p.OH && ow < p.OW)
+                                  ? (static_cast<long long>(tc.n0) * p.OH + oh) * p.OW + ow : -1;
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const long long px = __shfl_sync(0xffffffffu, my_px, i);
+        v[i] = ((p.flags & kReadState) && cvalid && px >= 0) ? p.state[px * p.F + cout] : 0.f;
+      }
+      for (int t = 0; t < T; ++t) {
+        const size_t tbase = static_cast<size_t>(t) * P;
+        uint4 r4[4];
+        if constexpr (RES) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) r4[k] = make_uint4(0, 0, 0, 0);
+          if (warp_live && my_px >= 0) {
+            const uint4* rp = reinterpret_cast<const uint4*>(p.residual + (tbase + my_px) * p.F + cbase);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) if (k < nchunk8) r4[k] = __ldg(rp + k);
+          }
+        }
+        bool fail = !mbar_wait_bounded(&acc_full[t], tile_it & 1, p.timeout_ns);
+        fail = __any_sync(0xffffffffu, fail || *abort_flag);
+        if (fail) { atomicOr(p.err, kErrTimeoutAcc); stop = true; break; }
+        tc_fence_after();
+        float acc[32];
+        if (warp_live) tmem_ld32(lane_base + t * kHsBN + half * 32, acc);
+        tc_fence_before();
+        mbar_arrive(&acc_empty[t]);              // the next tile's MMAs may reuse it
+        if (!warp_live) continue;
+        if constexpr (MODE == kModeNone) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const long long px = __shfl_sync(0xffffffffu, my_px, i);
+            if (cvalid && px >= 0) p.out_f32[(tbase + px) * p.F + cout] = fmaf(acc[i], sc, bi);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const bool spike = neuron_step<MODE>(v[i], fmaf(acc[i], sx, bx), p.decay, p.tau,
+                                                 p.v_th, p.v_reset);
+            *reinterpret_cast<__half*>(xb + xoff(i, lane >> 3) + (lane & 7) * 2) =
+                __ushort_as_half(spike ? 0x3C00 : 0);
+          }
+          __syncwarp();
+          uint4 o4[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) o4[k] = *reinterpret_cast<const uint4*>(xb + xoff(lane, k));
+          if constexpr (RES) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              __half2* a = reinterpret_cast<__half2*>(&o4[k]);
+              const __half2* b = reinterpret_cast<const __half2*>(&r4[k]);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) a[j] = __hadd2(a[j], b[j]);
+            }
+          }
+          if (my_px >= 0) {
+            uint4* op = reinterpret_cast<uint4*>(p.out + (tbase + my_px) * p.F + cbase);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) if (k < nchunk8) op[k] = o4[k];
+          }
+          __syncwarp();
+        }
+      }
+      ++tile_it;
+      if (!stop && (p.flags & kWriteState) && warp_live) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const long long px = __shfl_sync(0xffffffffu, my_px, i);
+          if (cvalid && px >= 0) p.state[px * p.F + cout] = v[i];
+        }
+      }
+    }
+    if (stop) *abort_flag = 1;
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kHaloMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kHaloTmemCols);
+  }
+}
+
+}  // namespace snn

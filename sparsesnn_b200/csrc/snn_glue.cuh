@@ -118,68 +118,58 @@ stem_conv_lif_kernel(const StemParams p) {
   }
 }
 
-// One block (256 threads) per group of up to kHeadImgs images.  Phase 1:
-// for each image, thread (c8, slot) sums 8 consecutive channels (16-byte
-// loads) over every 4th (t, hw) position; the 4 partial sums are combined
-// in shared memory and scaled: feat = sum / HW / T (exact for the
-// small-integer SEW activations).  Phase 2: one warp per output class reads
-// its weight row once and applies it to every image of the group.
-// dynamic smem = (4 + kHeadImgs) * C floats.
-constexpr int kHeadImgs = 8;
-__global__ void __launch_bounds__(256)
+// One block (1024 threads) per image.  Phase 1: thread (c8, slot) sums 8
+// consecutive channels (16-byte loads) over every 16th (t, hw) position; the
+// partial sums are combined in shared memory and scaled: feat = sum / HW / T
+// (exact for the small-integer SEW activations).  Phase 2: one warp per
+// output class, 16-byte weight loads.  dynamic smem = 17*C floats.
+constexpr int kHeadSlots = 16;
+__global__ void __launch_bounds__(1024)
 head_pool_fc_kernel(const __half* __restrict__ x, const float* __restrict__ fc_w,
                     const float* __restrict__ fc_b, float* __restrict__ logits,
                     int T, int B, int HW, int C, int NC) {
   extern __shared__ float sm[];
-  float* part = sm;                          // [4][C]
-  float* feat = sm + 4 * C;                  // [kHeadImgs][C]
-  const int b0 = blockIdx.x * kHeadImgs;
-  const int nimg = min(kHeadImgs, B - b0);
+  float* part = sm;                          // [kHeadSlots][C]
+  float* feat = sm + kHeadSlots * C;         // [C]
+  const int b = blockIdx.x;
   const int c8n = C / 8;
-  for (int im = 0; im < nimg; ++im) {
-    const int b = b0 + im;
-    for (int task = threadIdx.x; task < c8n * 4; task += blockDim.x) {
-      const int c8 = task % c8n, slot = task / c8n;
-      float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      for (int pos = slot; pos < T * HW; pos += 4) {
-        const int t = pos / HW, i = pos - t * HW;
-        const uint4 u = __ldg(reinterpret_cast<const uint4*>(
-            x + ((static_cast<size_t>(t) * B + b) * HW + i) * C) + c8);
-        const __half2* h = reinterpret_cast<const __half2*>(&u);
+  for (int task = threadIdx.x; task < c8n * kHeadSlots; task += blockDim.x) {
+    const int c8 = task % c8n, slot = task / c8n;
+    float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int pos = slot; pos < T * HW; pos += kHeadSlots) {
+      const int t = pos / HW, i = pos - t * HW;
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(
+          x + ((static_cast<size_t>(t) * B + b) * HW + i) * C) + c8);
+      const __half2* h = reinterpret_cast<const __half2*>(&u);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 f = __half22float2(h[j]);
-          s[2 * j] += f.x; s[2 * j + 1] += f.y;
-        }
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __half22float2(h[j]);
+        s[2 * j] += f.x; s[2 * j + 1] += f.y;
       }
-#pragma unroll
-      for (int j = 0; j < 8; ++j) part[slot * C + c8 * 8 + j] = s[j];
     }
-    __syncthreads();
-    for (int c = threadIdx.x; c < C; c += blockDim.x)
-      feat[im * C + c] = ((part[c] + part[C + c]) + (part[2 * C + c] + part[3 * C + c])) /
-                         static_cast<float>(HW) / static_cast<float>(T);
-    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < 8; ++j) part[slot * C + c8 * 8 + j] = s[j];
   }
+  __syncthreads();
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    float acc = 0.f;
+#pragma unroll
+    for (int sl = 0; sl < kHeadSlots; ++sl) acc += part[sl * C + c];
+    feat[c] = acc / static_cast<float>(HW) / static_cast<float>(T);
+  }
+  __syncthreads();
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, nwarps = blockDim.x / 32;
   for (int n = warp; n < NC; n += nwarps) {
-    const float* wr = fc_w + static_cast<size_t>(n) * C;
-    float acc[kHeadImgs];
-#pragma unroll
-    for (int im = 0; im < kHeadImgs; ++im) acc[im] = 0.f;
-    for (int c = lane; c < C; c += 32) {
-      const float w = __ldg(wr + c);
-#pragma unroll
-      for (int im = 0; im < kHeadImgs; ++im) acc[im] = fmaf(feat[im * C + c], w, acc[im]);
+    const float4* wr = reinterpret_cast<const float4*>(fc_w + static_cast<size_t>(n) * C);
+    float acc = 0.f;
+    for (int c4 = lane; c4 < C / 4; c4 += 32) {
+      const float4 w = __ldg(wr + c4);
+      const float4 f = *reinterpret_cast<const float4*>(feat + 4 * c4);
+      acc = fmaf(f.x, w.x, fmaf(f.y, w.y, fmaf(f.z, w.z, fmaf(f.w, w.w, acc))));
     }
 #pragma unroll
-    for (int im = 0; im < kHeadImgs; ++im) {
-      float a = acc[im];
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
-      if (lane == 0 && im < nimg)
-        logits[static_cast<size_t>(b0 + im) * NC + n] = a + (fc_b ? fc_b[n] : 0.f);
-    }
+    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (lane == 0) logits[static_cast<size_t>(b) * NC + n] = acc + (fc_b ? fc_b[n] : 0.f);
   }
 }
 

@@ -24,12 +24,15 @@ SNN_NEURON_NONE = 2
 SNN_FLAG_READ_STATE = 1
 SNN_FLAG_WRITE_STATE = 2
 SNN_FLAG_FORCE_GENERIC = 4
+SNN_VARIANT_GENERIC = 0
+SNN_VARIANT_HALO_RESIDENT = 1
+SNN_VARIANT_HALO_STREAM = 2
 
 NEURONS = {"lif": SNN_NEURON_LIF, "if": SNN_NEURON_IF, "none": SNN_NEURON_NONE}
 
 # Every symbol include/snn_b200.h declares.
 EXPORTED = (
-    "snn_abi_version", "snn_init", "snn_conv_out_shape", "snn_conv_weight_bytes",
+    "snn_abi_version", "snn_init", "snn_conv_variant", "snn_conv_out_shape", "snn_conv_weight_bytes",
     "snn_pack_weight_24", "snn_conv_forward", "snn_conv_forward_res", "snn_stem_forward",
     "snn_head_forward", "snn_get_device_error", "snn_last_error_message",
 )
@@ -62,6 +65,7 @@ def _declare(lib):
     sig = {
         "snn_abi_version": ([], ctypes.c_int),
         "snn_init": ([], ctypes.c_int),
+        "snn_conv_variant": ([D], ctypes.c_int),
         "snn_conv_out_shape": ([D, ctypes.POINTER(i32), ctypes.POINTER(i32)], ctypes.c_int),
         "snn_conv_weight_bytes": ([D, ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
         "snn_pack_weight_24": ([D, P, P], ctypes.c_int),
@@ -106,6 +110,14 @@ def make_desc(*, T, B, Cin, H, W, Cout, KH, KW, stride=1, pad=None, neuron="lif"
         pad = KH // 2
     return SnnConvDesc(T, B, Cin, H, W, Cout, KH, KW, stride, pad, NEURONS[neuron], flags,
                        tau, v_threshold, v_reset)
+
+
+def variant(desc: SnnConvDesc) -> int:
+    """Kernel variant the library picks for ``desc`` (SNN_VARIANT_*)."""
+    v = load().snn_conv_variant(ctypes.byref(desc))
+    if v < 0:
+        check(v)
+    return v
 
 
 def out_shape(desc: SnnConvDesc):

@@ -72,3 +72,20 @@ def test_forward_without_device_fails_loudly(_lib):
     d = rt.make_desc(T=1, B=1, Cin=64, H=8, W=8, Cout=128, KH=3, KW=3)
     rc = _lib.snn_conv_forward(d, 16, 16, None, 16, 16, 16, None)
     assert rc in (rt.SNN_E_NO_DEVICE, rt.SNN_E_CUDA)
+
+
+@pytest.mark.parametrize("kw, expect", [
+    (dict(Cin=128, H=32, W=32), rt.SNN_VARIANT_HALO_RESIDENT),      # config 0
+    (dict(Cin=64, H=32, W=32, Cout=64), rt.SNN_VARIANT_HALO_RESIDENT),
+    (dict(Cin=256, H=8, W=8, Cout=256), rt.SNN_VARIANT_HALO_STREAM),
+    (dict(Cin=512, H=16, W=16, Cout=512), rt.SNN_VARIANT_HALO_STREAM),
+    (dict(Cin=256, H=8, W=8, T=5), rt.SNN_VARIANT_GENERIC),          # T > 4
+    (dict(Cin=512, H=4, W=4), rt.SNN_VARIANT_GENERIC),               # image < 8x8
+    (dict(Cin=64, H=32, W=32, stride=2), rt.SNN_VARIANT_GENERIC),
+    (dict(Cin=64, H=32, W=32, KH=1, KW=1, pad=0), rt.SNN_VARIANT_GENERIC),
+    (dict(Cin=128, H=32, W=32, flags=rt.SNN_FLAG_FORCE_GENERIC), rt.SNN_VARIANT_GENERIC),
+])
+def test_variant_selection(kw, expect):
+    base = dict(T=4, B=2, Cin=64, H=8, W=8, Cout=128, KH=3, KW=3)
+    base.update(kw)
+    assert rt.variant(rt.make_desc(**base)) == expect

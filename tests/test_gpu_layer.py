@@ -242,3 +242,35 @@ def test_size_independent_properties(cuda_device):
         s = (v - 1.0).ge(0).float()
         v = (1.0 - s) * v
         assert torch.equal(y0[t, 0].cpu(), s)
+
+
+@pytest.mark.parametrize("T", [1, 2, 3, 4])
+@pytest.mark.parametrize("residual", [False, True], ids=["plain", "res"])
+def test_halo_stream_variant(cuda_device, T, residual):
+    """Streaming-weight halo kernel (Cin=256 on 8x8 and 16x8 images) against
+    the oracle, for every timestep count it serves (collector A reuse across
+    1..4 timesteps) and with the SEW residual."""
+    import torch
+    from sparsesnn_b200 import runtime as rt
+    from sparsesnn_b200.layer import SparseConvBNLIF, fold_bn
+    for (H, W) in ((8, 8), (16, 8)):
+        x, w, bn = L.make_config0(seed=10 + T, T=T, B=3, C=256, F=256, H=H, W=W)
+        scale, bias = fold_bn(bn.gamma, bn.beta, bn.mean, bn.var)
+        layer = SparseConvBNLIF(w, scale, bias, T=T, B=3, H=H, W=W)
+        assert rt.variant(layer.desc) == rt.SNN_VARIANT_HALO_STREAM
+        xd = torch.from_numpy(to_nhwc(x)).to("cuda", torch.float16)
+        res_np = None
+        res = None
+        if residual:
+            rng = np.random.default_rng(T)
+            res_np = rng.integers(0, 3, (T, 3, 256, H, W)).astype(np.float32)
+            res = torch.from_numpy(to_nhwc(res_np)).to("cuda", torch.float16)
+        state = torch.zeros(layer.state_shape(), dtype=torch.float32, device="cuda")
+        y = layer(xd, state=state, residual=res, read_state=False)
+        torch.cuda.synchronize()
+        assert rt.device_error() == 0
+        r = L.fused_layer(x, w, bn, stride=1, pad=1)
+        ys = from_nhwc(y.float().cpu().numpy(), T, 3)
+        spk = ys - res_np if residual else ys
+        v = np.transpose(state.cpu().numpy().reshape(3, H, W, 256), (0, 3, 1, 2))
+        check_spikes_and_v(spk, v, r["spikes"], r["h"], r["v"])
