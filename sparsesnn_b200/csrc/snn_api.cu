@@ -54,21 +54,24 @@ ConvKernel conv_kernel_fn(int mode, bool res) {
 
 using HaloKernel = void (*)(const snn::HaloParams);
 
-template <int BN>
+template <int BN, bool M64>
 HaloKernel halo_kernel_fn_bn(int mode, bool res) {
   switch (mode * 2 + (res ? 1 : 0)) {
-    case 0: return snn::fused_sparse_conv_halo_kernel<snn::kModeLifHalf, false, BN, 3>;
-    case 1: return snn::fused_sparse_conv_halo_kernel<snn::kModeLifHalf, true, BN, 3>;
-    case 2: return snn::fused_sparse_conv_halo_kernel<snn::kModeLifDiv, false, BN, 3>;
-    case 3: return snn::fused_sparse_conv_halo_kernel<snn::kModeLifDiv, true, BN, 3>;
-    case 4: return snn::fused_sparse_conv_halo_kernel<snn::kModeIf, false, BN, 3>;
-    case 5: return snn::fused_sparse_conv_halo_kernel<snn::kModeIf, true, BN, 3>;
-    default: return snn::fused_sparse_conv_halo_kernel<snn::kModeNone, false, BN, 3>;
+    case 0: return snn::fused_sparse_conv_halo_kernel<snn::kModeLifHalf, false, BN, 3, M64>;
+    case 1: return snn::fused_sparse_conv_halo_kernel<snn::kModeLifHalf, true, BN, 3, M64>;
+    case 2: return snn::fused_sparse_conv_halo_kernel<snn::kModeLifDiv, false, BN, 3, M64>;
+    case 3: return snn::fused_sparse_conv_halo_kernel<snn::kModeLifDiv, true, BN, 3, M64>;
+    case 4: return snn::fused_sparse_conv_halo_kernel<snn::kModeIf, false, BN, 3, M64>;
+    case 5: return snn::fused_sparse_conv_halo_kernel<snn::kModeIf, true, BN, 3, M64>;
+    default: return snn::fused_sparse_conv_halo_kernel<snn::kModeNone, false, BN, 3, M64>;
   }
 }
 
-HaloKernel halo_kernel_fn(int bn, int mode, bool res) {
-  return bn == 128 ? halo_kernel_fn_bn<128>(mode, res) : halo_kernel_fn_bn<64>(mode, res);
+// bn = 128 with m64 selects the M = 64 MMA path (layers of at most 64 channels).
+HaloKernel halo_kernel_fn(int bn, bool m64, int mode, bool res) {
+  if (bn == 128) return m64 ? halo_kernel_fn_bn<128, true>(mode, res)
+                            : halo_kernel_fn_bn<128, false>(mode, res);
+  return halo_kernel_fn_bn<64, false>(mode, res);
 }
 
 using HsKernel = void (*)(const snn::ConvParams);
@@ -113,8 +116,8 @@ int ensure_init() {
                                cudaFuncAttributeMaxDynamicSharedMemorySize, snn::kSmemBytes);
       if (e != cudaSuccess)
         return g_init_status = fail(SNN_E_CUDA, "smem attribute: %s", cudaGetErrorString(e));
-      for (int bn : {64, 128}) {
-        e = cudaFuncSetAttribute(halo_kernel_fn(bn, mode, res != 0),
+      for (int v = 0; v < 3; ++v) {
+        e = cudaFuncSetAttribute(halo_kernel_fn(v ? 128 : 64, v == 2, mode, res != 0),
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
         if (e != cudaSuccess)
           return g_init_status = fail(SNN_E_CUDA, "smem attribute: %s", cudaGetErrorString(e));
@@ -156,6 +159,8 @@ int check_desc(const snn_conv_desc* d, Geometry* g) {
   if (g->K / 32 > snn::kMaxMetaCols)
     return fail(SNN_E_INVALID, "K=%d exceeds the %d supported", g->K, snn::kMaxMetaCols * 32);
   if ((long long)d->T * d->B > 0x7fffffffLL) return fail(SNN_E_INVALID, "T*B too large");
+  if ((long long)d->B * g->OH * g->OW > 0x7fffffffLL)
+    return fail(SNN_E_INVALID, "B*OH*OW too large");
   return SNN_OK;
 }
 
@@ -284,13 +289,15 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
     snn::HaloParams hp;
     memset(&hp, 0, sizeof(hp));
     const int bn = g.OH >= 16 ? 128 : 64;
+    const bool m64 = bn == 128 && d->Cout <= 64;
     const int th_ = bn / 8;
     hp.KH = d->KH;
     hp.halo_w = 8 + d->KW - 1;
     hp.halo_bytes = hp.halo_w * (th_ + d->KH - 1) * snn::kKB * 2;
     hp.halo_stride = (hp.halo_bytes + 1023) / 1024 * 1024;
     hp.a_bytes = a_bytes;
-    const int fixed = 1024 + 512 + snn::kEpiWarps * snn::kXposeBytes + a_bytes;
+    const int fixed = 1024 + 512 + (m64 ? snn::kHalo64XposeBytes : snn::kEpiWarps * snn::kXposeBytes) +
+                      a_bytes;
     hp.halo_stages = std::min(snn::kHaloMaxStages, (kSmemLimit - fixed) / hp.halo_stride);
     if (hp.halo_stages >= 2) {
       p.tw = 8; p.th = th_; p.tn = 1;
@@ -308,7 +315,7 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
       const size_t smem = static_cast<size_t>(fixed) + static_cast<size_t>(hp.halo_stages) * hp.halo_stride;
       const int per_m = std::max(1, std::min(p.n_px_tiles, g_num_sms / p.n_m));
       const long long grid = static_cast<long long>(per_m) * p.n_m;
-      halo_kernel_fn(bn, mode, residual != nullptr)<<<static_cast<unsigned>(grid), snn::kHaloThreads,
+      halo_kernel_fn(bn, m64, mode, residual != nullptr)<<<static_cast<unsigned>(grid), snn::kHaloThreads,
                                                       smem, static_cast<cudaStream_t>(stream)>>>(hp);
       cudaError_t e = cudaGetLastError();
       if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));

@@ -17,8 +17,9 @@
 // Warp roles (10 warps): 0 = TMA producer, 1 = TMEM owner + MMA issuer,
 // 2..9 = epilogue: two warps per TMEM lane quarter, each owning 32 of the 64
 // pixel columns.  The epilogue applies BN, runs the LIF/IF recurrence over T
-// with the membrane in registers, adds the SEW residual (fetched by TMA),
-// stages fp16 spikes in shared memory and writes them with TMA stores.
+// with the membrane in registers, stages fp16 spikes in a per-warp transpose
+// tile, adds the SEW residual and writes 16-byte vectors (see the store stage
+// below).
 #pragma once
 #include <cstdint>
 #include <cuda.h>
@@ -69,6 +70,59 @@ __device__ __forceinline__ bool neuron_step(float& v, float x2, float decay, flo
   v = spike ? v_reset : h;
   return spike;
 }
+// ------------------------------------------------------ epilogue store stage
+// An epilogue warp owns 32 output channels (one per TMEM lane) x 32 pixel
+// columns.  The neuron loop writes the warp's spikes column by column into a
+// per-warp transpose tile ([32 px][32 ch] fp16 in 64-byte rows whose 16-byte
+// chunks are XOR-ed with (px>>1)&3, so the column writes and the row reads
+// are both conflict-free).  The tile leaves with four lanes per pixel: lane l
+// stores 16-byte chunk l%4 of column 8j + l/4, so one warp store covers 8
+// pixels x 64 contiguous bytes (8 cache lines instead of 32).  The SEW
+// residual is read with the same lane mapping.
+__device__ __forceinline__ int xpose_off(int px, int c8) {
+  return px * 64 + ((c8 ^ ((px >> 1) & 3)) << 4);
+}
+// Spike of this lane's channel at column i.
+__device__ __forceinline__ void xpose_put(uint8_t* xb, int i, int lane, bool spike) {
+  *reinterpret_cast<__half*>(xb + xpose_off(i, lane >> 3) + (lane & 7) * 2) =
+      __ushort_as_half(spike ? 0x3C00 : 0);
+}
+// Pixels this lane stores (columns 8j + lane/4), from each lane's pixel of
+// column `lane` (-1 = outside the output).
+__device__ __forceinline__ void store_rows(int my_px, int lane, int (&rows)[4]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) rows[j] = __shfl_sync(0xffffffffu, my_px, 8 * j + (lane >> 2));
+}
+__device__ __forceinline__ void load_residual_rows(const __half* res, size_t tbase,
+                                                   const int (&rows)[4], int F, int cbase,
+                                                   int lane, bool chunk_ok, uint4 (&r4)[4]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    r4[j] = make_uint4(0, 0, 0, 0);
+    if (chunk_ok && rows[j] >= 0)
+      r4[j] = __ldg(reinterpret_cast<const uint4*>(res + (tbase + rows[j]) * F + cbase) +
+                    (lane & 3));
+  }
+}
+template <bool RES>
+__device__ __forceinline__ void store_xpose_rows(__half* out, const uint8_t* xb, size_t tbase,
+                                                 const int (&rows)[4], int F, int cbase,
+                                                 int lane, bool chunk_ok, const uint4 (&r4)[4]) {
+  const int c8 = lane & 3;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint4 o = *reinterpret_cast<const uint4*>(xb + xpose_off(8 * j + (lane >> 2), c8));
+    if constexpr (RES) {
+      __half2* a = reinterpret_cast<__half2*>(&o);
+      const __half2* b = reinterpret_cast<const __half2*>(&r4[j]);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) a[u] = __hadd2(a[u], b[u]);
+    }
+    if (chunk_ok && rows[j] >= 0)
+      reinterpret_cast<uint4*>(out + (tbase + rows[j]) * F + cbase)[c8] = o;
+  }
+}
+
 enum ConvFlags : int { kReadState = 1, kWriteState = 2 };
 enum ErrCode : unsigned { kErrTimeoutFull = 1u, kErrTimeoutEmpty = 2u, kErrTimeoutAcc = 4u,
                           kErrTimeoutMeta = 8u, kErrTimeoutAccEmpty = 16u, kErrTimeoutDrain = 32u,
@@ -280,32 +334,34 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
     const int tile_px = p.tw * p.th;
     const int cbase = m_tile * kBM + q * 32;     // first output channel of this warp
     const int nchunk8 = max(0, min(4, (p.F - cbase) / 8));   // valid 8-channel chunks
+    const bool chunk_ok = (lane & 3) < nchunk8;
     uint8_t* xb = sX + e * kXposeBytes;
-    // Swizzled [px][cout] fp16 layout: 64-byte rows, 16-byte chunks XOR-ed with
-    // (px>>1)&3 so both the column writes and the row reads are conflict-free.
-    auto xoff = [](int px, int c8) { return px * 64 + ((c8 ^ ((px >> 1) & 3)) << 4); };
 
-    auto pixel_of = [&](const TileCoord& tc, int col) -> long long {
+    auto pixel_of = [&](const TileCoord& tc, int col) -> int {
       const int dn = col / tile_px;
       const int rem = col - dn * tile_px;
       const int dh = rem / p.tw;
       const int dw = rem - dh * p.tw;
       const int n = tc.n0 + dn, oh = tc.h0 + dh, ow = tc.w0 + dw;
       if (dn >= p.tn || n >= p.B || oh >= p.OH || ow >= p.OW) return -1;
-      return (static_cast<long long>(n) * p.OH + oh) * p.OW + ow;
+      return (n * p.OH + oh) * p.OW + ow;
     };
 
     int acc_iter = 0;
     bool stop = false;
     for (int pt = first_pt; pt < p.n_px_tiles && !stop; pt += pt_step) {
       const TileCoord tc = tile_coord(p, pt);
-      // In the transposed phase lane l owns pixel column half*32 + l.
-      const long long my_px = pixel_of(tc, half * 32 + lane);
+      // Lane l's pixel is column half*32 + l (neuron phase: lane = channel,
+      // so the column's pixel comes by shuffle).
+      const int my_px = pixel_of(tc, half * 32 + lane);
+      int rows[4];
+      store_rows(my_px, lane, rows);
       float v[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        const long long px = __shfl_sync(0xffffffffu, my_px, i);
-        v[i] = ((p.flags & kReadState) && cvalid && px >= 0) ? p.state[px * p.F + cout] : 0.f;
+        const int px = __shfl_sync(0xffffffffu, my_px, i);
+        v[i] = ((p.flags & kReadState) && cvalid && px >= 0)
+                   ? p.state[static_cast<size_t>(px) * p.F + cout] : 0.f;
       }
       for (int c = 0; c < n_chunks && !stop; ++c) {
         const int t0 = c * kTC;
@@ -318,25 +374,16 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
         tc_fence_after();
         for (int tt = 0; tt < tcn; ++tt) {
           const size_t tbase = static_cast<size_t>(t0 + tt) * P;
-          // Residual row of this lane's pixel (64 B), fetched before the TMEM
-          // load so its latency overlaps the neuron update.
+          // Residual rows, fetched before the TMEM load so their latency
+          // overlaps the neuron update.
           uint4 r4[4];
-          if constexpr (RES) {
-#pragma unroll
-            for (int k = 0; k < 4; ++k) r4[k] = make_uint4(0, 0, 0, 0);
-            if (my_px >= 0) {
-              const uint4* rp = reinterpret_cast<const uint4*>(
-                  p.residual + (tbase + my_px) * p.F + cbase);
-#pragma unroll
-              for (int k = 0; k < 4; ++k) if (k < nchunk8) r4[k] = __ldg(rp + k);
-            }
-          }
+          if constexpr (RES) load_residual_rows(p.residual, tbase, rows, p.F, cbase, lane, chunk_ok, r4);
           float acc[32];
           tmem_ld32(lane_base + buf * kAccCols + tt * kBN + half * 32, acc);
           if constexpr (MODE == kModeNone) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
-              const long long px = __shfl_sync(0xffffffffu, my_px, i);
+              const int px = __shfl_sync(0xffffffffu, my_px, i);
               if (cvalid && px >= 0) p.out_f32[(tbase + px) * p.F + cout] = fmaf(acc[i], sc, bi);
             }
           } else {
@@ -344,31 +391,11 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
             const float sx = MODE == kModeLifHalf ? sc * 0.5f : sc;
             const float bx = MODE == kModeLifHalf ? bi * 0.5f : bi;
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const bool spike = neuron_step<MODE>(v[i], fmaf(acc[i], sx, bx), p.decay, p.tau,
-                                                   p.v_th, p.v_reset);
-              *reinterpret_cast<__half*>(xb + xoff(i, lane >> 3) + (lane & 7) * 2) =
-                  __ushort_as_half(spike ? 0x3C00 : 0);
-            }
+            for (int i = 0; i < 32; ++i)
+              xpose_put(xb, i, lane, neuron_step<MODE>(v[i], fmaf(acc[i], sx, bx), p.decay, p.tau,
+                                                       p.v_th, p.v_reset));
             __syncwarp();
-            // Row phase: lane owns pixel half*32+lane, 32 channels = 4 x 16 B.
-            uint4 o4[4];
-#pragma unroll
-            for (int k = 0; k < 4; ++k) o4[k] = *reinterpret_cast<const uint4*>(xb + xoff(lane, k));
-            if constexpr (RES) {
-#pragma unroll
-              for (int k = 0; k < 4; ++k) {
-                __half2* a = reinterpret_cast<__half2*>(&o4[k]);
-                const __half2* b = reinterpret_cast<const __half2*>(&r4[k]);
-#pragma unroll
-                for (int j = 0; j < 4; ++j) a[j] = __hadd2(a[j], b[j]);
-              }
-            }
-            if (my_px >= 0) {
-              uint4* op = reinterpret_cast<uint4*>(p.out + (tbase + my_px) * p.F + cbase);
-#pragma unroll
-              for (int k = 0; k < 4; ++k) if (k < nchunk8) op[k] = o4[k];
-            }
+            store_xpose_rows<RES>(p.out, xb, tbase, rows, p.F, cbase, lane, chunk_ok, r4);
             __syncwarp();
           }
         }
@@ -379,8 +406,8 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
       if (!stop && (p.flags & kWriteState)) {
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const long long px = __shfl_sync(0xffffffffu, my_px, i);
-          if (cvalid && px >= 0) p.state[px * p.F + cout] = v[i];
+          const int px = __shfl_sync(0xffffffffu, my_px, i);
+          if (cvalid && px >= 0) p.state[static_cast<size_t>(px) * p.F + cout] = v[i];
         }
       }
     }

@@ -19,7 +19,17 @@
 // half = warp / 4); 8..11 load the metadata into TMEM (one warp per lane
 // quarter), then warp 10 issues MMAs and owns TMEM and warp 11 drives TMA.
 // Placing the MMA and TMA warps on sub-partitions 2 and 3 keeps them off the
-// sub-partitions that do all the epilogue work when Cout <= 64.
+// sub-partitions that do most of the epilogue work.
+//
+// M64 (layers with at most 64 output channels, BN = 128): the MMAs use M = 64,
+// whose accumulator keeps 16 rows in each TMEM lane quarter (rows 16q..16q+15
+// in lanes 32q..32q+15), so all eight epilogue warps hold real channels: warp
+// (q, half) reads its 16 lanes x 64 columns with one 16x32bx2 load (thread t:
+// channel 16q + t%16, 32 consecutive columns).  The 2:4 metadata of an M = 64
+// MMA uses the same per-lane word format as M = 128, in lanes 32q..32q+15 for
+// rows 16q..16q+15; the loader takes those words from M = 128 lanes 16q..16q+15
+// of the packed blob.  Spikes go through a [64 px][64 ch] tile shared by the
+// four warps of a half, so every warp store writes whole 128-byte pixel rows.
 #pragma once
 #include "snn_conv.cuh"
 
@@ -31,6 +41,8 @@ constexpr int kHaloMmaWarp = 10;
 constexpr int kHaloTmaWarp = 11;
 constexpr int kHaloMetaCol = 256;        // accumulators: 2 x up to 128 columns
 constexpr int kHaloTmemCols = 512;
+constexpr int kHalo64TileBytes = 64 * 128;                 // [64 px][64 ch] fp16
+constexpr int kHalo64XposeBytes = 4 * kHalo64TileBytes;    // 2 buffers x 2 halves
 
 struct HaloParams {
   ConvParams c;              // shared fields (tmap_a, tmap_b[0], meta, scale, ...)
@@ -42,9 +54,17 @@ struct HaloParams {
   int a_bytes;               // resident weight bytes (n_kb * kABytes)
 };
 
-template <int MODE, bool RES, int BN, int KS>
+// Byte offset of (pixel px, 16-byte channel chunk c16) in an M64 spike tile:
+// 128-byte pixel rows, chunk index XOR-ed with 4 for pixels 32..63 so the two
+// pixels one store instruction writes land in different banks.
+__device__ __forceinline__ int tile64_off(int px, int c16) {
+  return px * 128 + ((c16 ^ (((px >> 5) & 1) << 2)) << 4);
+}
+
+template <int MODE, bool RES, int BN, int KS, bool M64 = false>
 __global__ void __launch_bounds__(kHaloThreads, 1)
 fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
+  static_assert(!M64 || BN == 128, "the M = 64 path tiles 128 pixels");
   const ConvParams& p = hp.c;
   constexpr int G = BN / 64;                 // 32-column groups per epilogue warp
   extern __shared__ uint8_t smem_raw[];
@@ -53,7 +73,7 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
   uint8_t* sA = smem;                                              // resident weights
   uint8_t* sH = smem + hp.a_bytes;                                 // halo stages
   uint8_t* sX = sH + hp.halo_stages * hp.halo_stride;              // epilogue transposes
-  uint64_t* full = reinterpret_cast<uint64_t*>(sX + kEpiWarps * kXposeBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sX + (M64 ? kHalo64XposeBytes : kEpiWarps * kXposeBytes));
   uint64_t* empty = full + kHaloMaxStages;
   uint64_t* a_full = empty + kHaloMaxStages;
   uint64_t* acc_full = a_full + 1;          // [2]
@@ -90,14 +110,16 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
   if (warp >= kEpiWarps) {
     // ------------------------------------------- metadata into TMEM (warps 8..11)
     const int q = warp & 3;
-    const int row = q * 32 + lane;
+    // Blob lane whose words this TMEM lane takes (-1: unused by M = 64).
+    const int row = M64 ? (lane < 16 ? q * 16 + lane : -1) : q * 32 + lane;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
-    const uint32_t* src = p.meta + (static_cast<size_t>(m_tile) * n_meta) * kBM + row;
+    const uint32_t* src = p.meta + (static_cast<size_t>(m_tile) * n_meta) * kBM + max(row, 0);
     for (int j = 0; j < n_meta; j += 8) {
       uint32_t r[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i)
-        r[i] = (j + i < n_meta) ? __ldg(src + static_cast<size_t>(j + i) * kBM) : 0x44444444u;
+        r[i] = (j + i < n_meta && row >= 0) ? __ldg(src + static_cast<size_t>(j + i) * kBM)
+                                            : 0x44444444u;
       tmem_st8(lane_base + kHaloMetaCol + j, r);
     }
     tmem_st_wait();
@@ -141,7 +163,7 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
   } else if (warp == kHaloMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = idesc_f16(kBM, BN, true);
+      const uint32_t idesc = idesc_f16(M64 ? 64 : kBM, BN, true);
       bool ok = mbar_wait_bounded(meta_ready, 0, p.timeout_ns);
       ok = ok && mbar_wait_bounded(a_full, 0, p.timeout_ns);
       if (!ok) { atomicOr(p.err, kErrTimeoutMeta); *abort_flag = 1; }
@@ -194,7 +216,110 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
       mma_commit(drain);
       if (!mbar_wait_bounded(drain, 0, p.timeout_ns)) atomicOr(p.err, kErrTimeoutDrain);
     }
-  } else if (warp < kEpiWarps) {
+  } else if (M64 && warp < kEpiWarps) {
+    // ------------------------------------------------------- epilogue, M = 64
+    const int q = warp & 3;
+    const int half = warp >> 2;
+    const int ch = q * 16 + (lane & 15);         // this thread's output channel
+    const bool cvalid = ch < p.F;
+    const float sc = cvalid ? p.scale[ch] : 0.f;
+    const float bi = cvalid ? p.bias[ch] : 0.f;
+    const float sx = MODE == kModeLifHalf ? sc * 0.5f : sc;
+    const float bx = MODE == kModeLifHalf ? bi * 0.5f : bi;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    const long long P = static_cast<long long>(p.B) * p.OH * p.OW;
+    const int col0 = half * 64 + (lane >> 4) * 32;   // neuron phase: columns col0 + i
+    const int tcol0 = (lane >> 4) * 32;              // ... as tile rows
+    const int c16 = lane & 7;                        // row phase: 16-byte channel chunk
+    const bool chunk_ok = c16 * 8 < p.F;
+    const int bar_id = 1 + half;                     // named barrier of the half's 4 warps
+
+    int it = 0;
+    bool stop = false;
+    for (int pt = first_pt; pt < p.n_px_tiles && !stop; pt += pt_step) {
+      const TileCoord tc = tile_coord(p, pt);
+      // Column j of the tile is pixel (h0 + j/8, w0 + j%8).
+      auto px_of = [&](int col) -> int {
+        const int oh = tc.h0 + col / 8, ow = tc.w0 + (col & 7);
+        return (oh < p.OH && ow < p.OW) ? (tc.n0 * p.OH + oh) * p.OW + ow : -1;
+      };
+      // Row phase: this warp stores tile rows q*16 + 4j + lane/8 of its half.
+      int rows[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) rows[j] = px_of(half * 64 + q * 16 + 4 * j + (lane >> 3));
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int px = px_of(col0 + i);
+        v[i] = ((p.flags & kReadState) && cvalid && px >= 0)
+                   ? p.state[static_cast<size_t>(px) * p.F + ch] : 0.f;
+      }
+      for (int t = 0; t < p.T; ++t) {
+        const int buf = it & 1;
+        const size_t tbase = static_cast<size_t>(t) * P;
+        uint8_t* tile = sX + (buf * 2 + half) * kHalo64TileBytes;
+        uint4 r4[4];
+        if constexpr (RES) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            r4[j] = make_uint4(0, 0, 0, 0);
+            if (chunk_ok && rows[j] >= 0)
+              r4[j] = __ldg(reinterpret_cast<const uint4*>(p.residual + (tbase + rows[j]) * p.F) + c16);
+          }
+        }
+        bool fail = !mbar_wait_bounded(&acc_full[buf], (it >> 1) & 1, p.timeout_ns);
+        fail = __any_sync(0xffffffffu, fail || *abort_flag);
+        if (!fail) {
+          tc_fence_after();
+          float acc[32];
+          tmem_ld16x2_32(lane_base + buf * BN + half * 64, acc);
+          tc_fence_before();
+          mbar_arrive(&acc_empty[buf]);          // buffer drained: the next MMAs may start
+          if constexpr (MODE == kModeNone) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const int px = px_of(col0 + i);
+              if (cvalid && px >= 0) p.out_f32[(tbase + px) * p.F + ch] = fmaf(acc[i], sc, bi);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const bool spike = neuron_step<MODE>(v[i], fmaf(acc[i], sx, bx), p.decay, p.tau,
+                                                   p.v_th, p.v_reset);
+              *reinterpret_cast<__half*>(tile + tile64_off(tcol0 + i, ch >> 3) + (ch & 7) * 2) =
+                  __ushort_as_half(spike ? 0x3C00 : 0);
+            }
+          }
+        }
+        ++it;
+        // The four warps of this half agree on aborting and see each other's
+        // tile rows; the next use of this tile buffer is two barriers away.
+        if (named_barrier_or(bar_id, 128, fail)) { atomicOr(p.err, kErrTimeoutAcc); stop = true; break; }
+        if constexpr (MODE != kModeNone) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint4 o = *reinterpret_cast<const uint4*>(tile + tile64_off(q * 16 + 4 * j + (lane >> 3), c16));
+            if constexpr (RES) {
+              __half2* a = reinterpret_cast<__half2*>(&o);
+              const __half2* b = reinterpret_cast<const __half2*>(&r4[j]);
+#pragma unroll
+              for (int u = 0; u < 4; ++u) a[u] = __hadd2(a[u], b[u]);
+            }
+            if (chunk_ok && rows[j] >= 0)
+              reinterpret_cast<uint4*>(p.out + (tbase + rows[j]) * p.F)[c16] = o;
+          }
+        }
+      }
+      if (!stop && (p.flags & kWriteState)) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int px = px_of(col0 + i);
+          if (cvalid && px >= 0) p.state[static_cast<size_t>(px) * p.F + ch] = v[i];
+        }
+      }
+    }
+    if (stop) *abort_flag = 1;
+  } else if (!M64 && warp < kEpiWarps) {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;
     const int half = warp >> 2;
@@ -210,51 +335,45 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
     const float bx = MODE == kModeLifHalf ? bi * 0.5f : bi;
     const long long P = static_cast<long long>(p.B) * p.OH * p.OW;
     const int nchunk8 = max(0, min(4, (p.F - cbase) / 8));
+    const bool chunk_ok = (lane & 3) < nchunk8;
     uint8_t* xb = sX + warp * kXposeBytes;
-    auto xoff = [](int px, int c8) { return px * 64 + ((c8 ^ ((px >> 1) & 3)) << 4); };
 
     int it = 0;
     bool stop = false;
     for (int pt = first_pt; pt < p.n_px_tiles && !stop; pt += pt_step) {
       const TileCoord tc = tile_coord(p, pt);
       // Column j of the tile is pixel (h0 + j/8, w0 + j%8); this warp owns
-      // columns [half*BN/2, half*BN/2 + BN/2); in the transposed phase lane l
-      // of group g owns column half*BN/2 + 32g + l.
-      long long my_px[G];
+      // columns [half*BN/2, half*BN/2 + BN/2) in G groups of 32; my_px[g] is
+      // the pixel of the group's column `lane` (the store rows are derived
+      // from it by shuffles where needed, to keep registers for the membrane).
+      int my_px[G];
 #pragma unroll
       for (int g = 0; g < G; ++g) {
         const int col = half * (BN / 2) + g * 32 + lane;
         const int oh = tc.h0 + col / 8, ow = tc.w0 + (col & 7);
-        my_px[g] = (oh < p.OH && ow < p.OW)
-                       ? (static_cast<long long>(tc.n0) * p.OH + oh) * p.OW + ow : -1;
+        my_px[g] = (oh < p.OH && ow < p.OW) ? (tc.n0 * p.OH + oh) * p.OW + ow : -1;
       }
       float v[G][32];
 #pragma unroll
       for (int g = 0; g < G; ++g) {
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const long long px = __shfl_sync(0xffffffffu, my_px[g], i);
-          v[g][i] = ((p.flags & kReadState) && cvalid && px >= 0) ? p.state[px * p.F + cout] : 0.f;
+          const int px = __shfl_sync(0xffffffffu, my_px[g], i);
+          v[g][i] = ((p.flags & kReadState) && cvalid && px >= 0)
+                        ? p.state[static_cast<size_t>(px) * p.F + cout] : 0.f;
         }
       }
       for (int t = 0; t < p.T; ++t) {
         const int buf = it & 1;
         const size_t tbase = static_cast<size_t>(t) * P;
-        // Residual rows of this timestep (64 B per pixel), requested before
-        // the accumulator wait so their latency hides behind the MMAs.
+        // Residual rows: group 0's are requested before the accumulator wait
+        // (their latency hides behind the MMAs), group g+1's right after group
+        // g's neuron update, when its accumulator registers are free.
         uint4 r4[G][4];
         if constexpr (RES) {
-#pragma unroll
-          for (int g = 0; g < G; ++g) {
-#pragma unroll
-            for (int k = 0; k < 4; ++k) r4[g][k] = make_uint4(0, 0, 0, 0);
-            if (warp_live && my_px[g] >= 0) {
-              const uint4* rp = reinterpret_cast<const uint4*>(
-                  p.residual + (tbase + my_px[g]) * p.F + cbase);
-#pragma unroll
-              for (int k = 0; k < 4; ++k) if (k < nchunk8) r4[g][k] = __ldg(rp + k);
-            }
-          }
+          int rows[4];
+          store_rows(my_px[0], lane, rows);
+          load_residual_rows(p.residual, tbase, rows, p.F, cbase, lane, chunk_ok, r4[0]);
         }
         bool fail = !mbar_wait_bounded(&acc_full[buf], (it >> 1) & 1, p.timeout_ns);
         fail = __any_sync(0xffffffffu, fail || *abort_flag);
@@ -278,35 +397,25 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
           if constexpr (MODE == kModeNone) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
-              const long long px = __shfl_sync(0xffffffffu, my_px[g], i);
+              const int px = __shfl_sync(0xffffffffu, my_px[g], i);
               if (cvalid && px >= 0) p.out_f32[(tbase + px) * p.F + cout] = fmaf(acc[i], sc, bi);
             }
           } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const bool spike = neuron_step<MODE>(v[g][i], fmaf(acc[i], sx, bx), p.decay,
-                                                   p.tau, p.v_th, p.v_reset);
-              *reinterpret_cast<__half*>(xb + xoff(i, lane >> 3) + (lane & 7) * 2) =
-                  __ushort_as_half(spike ? 0x3C00 : 0);
-            }
+            for (int i = 0; i < 32; ++i)
+              xpose_put(xb, i, lane, neuron_step<MODE>(v[g][i], fmaf(acc[i], sx, bx), p.decay,
+                                                       p.tau, p.v_th, p.v_reset));
             __syncwarp();
-            uint4 o4[4];
-#pragma unroll
-            for (int k = 0; k < 4; ++k) o4[k] = *reinterpret_cast<const uint4*>(xb + xoff(lane, k));
             if constexpr (RES) {
-#pragma unroll
-              for (int k = 0; k < 4; ++k) {
-                __half2* a = reinterpret_cast<__half2*>(&o4[k]);
-                const __half2* b = reinterpret_cast<const __half2*>(&r4[g][k]);
-#pragma unroll
-                for (int j = 0; j < 4; ++j) a[j] = __hadd2(a[j], b[j]);
+              if (g + 1 < G) {
+                int rows[4];
+                store_rows(my_px[g + 1], lane, rows);
+                load_residual_rows(p.residual, tbase, rows, p.F, cbase, lane, chunk_ok, r4[g + 1]);
               }
             }
-            if (my_px[g] >= 0) {
-              uint4* op = reinterpret_cast<uint4*>(p.out + (tbase + my_px[g]) * p.F + cbase);
-#pragma unroll
-              for (int k = 0; k < 4; ++k) if (k < nchunk8) op[k] = o4[k];
-            }
+            int rows[4];
+            store_rows(my_px[g], lane, rows);
+            store_xpose_rows<RES>(p.out, xb, tbase, rows, p.F, cbase, lane, chunk_ok, r4[g]);
             __syncwarp();
           }
         }
@@ -316,8 +425,8 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
         for (int g = 0; g < G; ++g) {
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            const long long px = __shfl_sync(0xffffffffu, my_px[g], i);
-            if (cvalid && px >= 0) p.state[px * p.F + cout] = v[g][i];
+            const int px = __shfl_sync(0xffffffffu, my_px[g], i);
+            if (cvalid && px >= 0) p.state[static_cast<size_t>(px) * p.F + cout] = v[g][i];
           }
         }
       }

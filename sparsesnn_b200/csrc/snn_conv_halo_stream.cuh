@@ -248,8 +248,8 @@ fused_sparse_conv_halo_stream_kernel(const __grid_constant__ ConvParams p) {
     const float bx = MODE == kModeLifHalf ? bi * 0.5f : bi;
     const long long P = static_cast<long long>(p.B) * p.OH * p.OW;
     const int nchunk8 = max(0, min(4, (p.F - cbase) / 8));
+    const bool chunk_ok = (lane & 3) < nchunk8;
     uint8_t* xb = sX + warp * kXposeBytes;
-    auto xoff = [](int px, int c8) { return px * 64 + ((c8 ^ ((px >> 1) & 3)) << 4); };
 
     int tile_it = 0;
     bool stop = false;
@@ -257,26 +257,20 @@ fused_sparse_conv_halo_stream_kernel(const __grid_constant__ ConvParams p) {
       const TileCoord tc = tile_coord(p, pt);
       const int col = half * 32 + lane;
       const int oh = tc.h0 + col / 8, ow = tc.w0 + (col & 7);
-      const long long my_px = (oh < p.OH && ow < p.OW)
-                                  ? (static_cast<long long>(tc.n0) * p.OH + oh) * p.OW + ow : -1;
+      const int my_px = (oh < p.OH && ow < p.OW) ? (tc.n0 * p.OH + oh) * p.OW + ow : -1;
+      int rows[4];
+      store_rows(my_px, lane, rows);
       float v[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        const long long px = __shfl_sync(0xffffffffu, my_px, i);
-        v[i] = ((p.flags & kReadState) && cvalid && px >= 0) ? p.state[px * p.F + cout] : 0.f;
+        const int px = __shfl_sync(0xffffffffu, my_px, i);
+        v[i] = ((p.flags & kReadState) && cvalid && px >= 0)
+                   ? p.state[static_cast<size_t>(px) * p.F + cout] : 0.f;
       }
       for (int t = 0; t < T; ++t) {
         const size_t tbase = static_cast<size_t>(t) * P;
         uint4 r4[4];
-        if constexpr (RES) {
-#pragma unroll
-          for (int k = 0; k < 4; ++k) r4[k] = make_uint4(0, 0, 0, 0);
-          if (warp_live && my_px >= 0) {
-            const uint4* rp = reinterpret_cast<const uint4*>(p.residual + (tbase + my_px) * p.F + cbase);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) if (k < nchunk8) r4[k] = __ldg(rp + k);
-          }
-        }
+        if constexpr (RES) load_residual_rows(p.residual, tbase, rows, p.F, cbase, lane, chunk_ok, r4);
         bool fail = !mbar_wait_bounded(&acc_full[t], tile_it & 1, p.timeout_ns);
         fail = __any_sync(0xffffffffu, fail || *abort_flag);
         if (fail) { atomicOr(p.err, kErrTimeoutAcc); stop = true; break; }
@@ -289,35 +283,16 @@ fused_sparse_conv_halo_stream_kernel(const __grid_constant__ ConvParams p) {
         if constexpr (MODE == kModeNone) {
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            const long long px = __shfl_sync(0xffffffffu, my_px, i);
+            const int px = __shfl_sync(0xffffffffu, my_px, i);
             if (cvalid && px >= 0) p.out_f32[(tbase + px) * p.F + cout] = fmaf(acc[i], sc, bi);
           }
         } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const bool spike = neuron_step<MODE>(v[i], fmaf(acc[i], sx, bx), p.decay, p.tau,
-                                                 p.v_th, p.v_reset);
-            *reinterpret_cast<__half*>(xb + xoff(i, lane >> 3) + (lane & 7) * 2) =
-                __ushort_as_half(spike ? 0x3C00 : 0);
-          }
+          for (int i = 0; i < 32; ++i)
+            xpose_put(xb, i, lane, neuron_step<MODE>(v[i], fmaf(acc[i], sx, bx), p.decay, p.tau,
+                                                     p.v_th, p.v_reset));
           __syncwarp();
-          uint4 o4[4];
-#pragma unroll
-          for (int k = 0; k < 4; ++k) o4[k] = *reinterpret_cast<const uint4*>(xb + xoff(lane, k));
-          if constexpr (RES) {
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              __half2* a = reinterpret_cast<__half2*>(&o4[k]);
-              const __half2* b = reinterpret_cast<const __half2*>(&r4[k]);
-#pragma unroll
-              for (int j = 0; j < 4; ++j) a[j] = __hadd2(a[j], b[j]);
-            }
-          }
-          if (my_px >= 0) {
-            uint4* op = reinterpret_cast<uint4*>(p.out + (tbase + my_px) * p.F + cbase);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) if (k < nchunk8) op[k] = o4[k];
-          }
+          store_xpose_rows<RES>(p.out, xb, tbase, rows, p.F, cbase, lane, chunk_ok, r4);
           __syncwarp();
         }
       }
@@ -325,8 +300,8 @@ fused_sparse_conv_halo_stream_kernel(const __grid_constant__ ConvParams p) {
       if (!stop && (p.flags & kWriteState) && warp_live) {
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const long long px = __shfl_sync(0xffffffffu, my_px, i);
-          if (cvalid && px >= 0) p.state[px * p.F + cout] = v[i];
+          const int px = __shfl_sync(0xffffffffu, my_px, i);
+          if (cvalid && px >= 0) p.state[static_cast<size_t>(px) * p.F + cout] = v[i];
         }
       }
     }

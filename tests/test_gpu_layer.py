@@ -274,3 +274,41 @@ def test_halo_stream_variant(cuda_device, T, residual):
         spk = ys - res_np if residual else ys
         v = np.transpose(state.cpu().numpy().reshape(3, H, W, 256), (0, 3, 1, 2))
         check_spikes_and_v(spk, v, r["spikes"], r["h"], r["v"])
+
+
+@pytest.mark.parametrize("T", [1, 3, 4])
+@pytest.mark.parametrize("residual", [False, True], ids=["plain", "res"])
+def test_m64_halo_path(cuda_device, T, residual):
+    """Layers with at most 64 output channels on images of >= 16 rows run the
+    resident-weight halo kernel with M = 64 MMAs (metadata remapped to the
+    M = 64 TMEM layout, spikes through tiles shared by four warps).  Odd T
+    checks the tile double-buffering across pixel tiles; a second call with
+    the membrane carried over checks the state read/write."""
+    import torch
+    from sparsesnn_b200 import runtime as rt
+    from sparsesnn_b200.layer import SparseConvBNLIF, fold_bn
+    B, H, W = 3, 16, 24
+    for F in (64, 32):
+        x, w, bn = L.make_config0(seed=20 + T + F, T=2 * T, B=B, C=64, F=F, H=H, W=W)
+        scale, bias = fold_bn(bn.gamma, bn.beta, bn.mean, bn.var)
+        layer = SparseConvBNLIF(w, scale, bias, T=T, B=B, H=H, W=W)
+        assert rt.variant(layer.desc) == rt.SNN_VARIANT_HALO_RESIDENT
+        res_np = None
+        if residual:
+            rng = np.random.default_rng(T + F)
+            res_np = rng.integers(0, 3, (2 * T, B, F, H, W)).astype(np.float32)
+        state = torch.zeros(layer.state_shape(), dtype=torch.float32, device="cuda")
+        outs = []
+        for half in range(2):                 # two calls, membrane carried over
+            sl = slice(half * T, (half + 1) * T)
+            xd = torch.from_numpy(to_nhwc(x[sl])).to("cuda", torch.float16)
+            res = (torch.from_numpy(to_nhwc(res_np[sl])).to("cuda", torch.float16)
+                   if residual else None)
+            outs.append(layer(xd, state=state, residual=res).float().cpu().numpy())
+        torch.cuda.synchronize()
+        assert rt.device_error() == 0
+        r = L.fused_layer(x, w, bn, stride=1, pad=1)
+        ys = np.concatenate([from_nhwc(o, T, B) for o in outs], axis=0)
+        spk = ys - res_np if residual else ys
+        v = np.transpose(state.cpu().numpy().reshape(B, H, W, F), (0, 3, 1, 2))
+        check_spikes_and_v(spk, v, r["spikes"], r["h"], r["v"])
