@@ -14,9 +14,9 @@
 // Persistent CTAs: each CTA owns one 128-channel slice (so its metadata is
 // loaded once) and walks a strided list of pixel tiles.
 //
-// Warp roles (10 warps): 0 = TMA producer, 1 = TMEM owner + MMA issuer,
-// 2..9 = epilogue: two warps per TMEM lane quarter, each owning 32 of the 64
-// pixel columns.  The epilogue applies BN, runs the LIF/IF recurrence over T
+// Warp roles (13 warps): 0 and 10..12 = TMA producers (stage s is filled by
+// producer s % 4), 1 = TMEM owner + MMA issuer, 2..9 = epilogue: two warps
+// per TMEM lane quarter, each owning 32 of the 64 pixel columns.  The epilogue applies BN, runs the LIF/IF recurrence over T
 // with the membrane in registers, stages fp16 spikes in a per-warp transpose
 // tile, adds the SEW residual and writes 16-byte vectors (see the store stage
 // below).
@@ -43,7 +43,12 @@ constexpr int kTmemCols = 512;
 constexpr int kMaxMetaCols = kTmemCols - kMetaCol;  // => K <= 8192
 constexpr int kEpiWarps = 8;
 constexpr int kEpiThreads = kEpiWarps * 32;
-constexpr int kThreads = 64 + kEpiThreads;
+// TMA producers: warp 0 and warps 10..12.  One thread issues tensor copies
+// one after another (a few hundred cycles each, whatever the box size), so
+// several producer warps, each owning every kProducers-th pipeline stage,
+// keep enough boxes in flight.
+constexpr int kProducers = 4;
+constexpr int kThreads = (2 + kEpiWarps + kProducers - 1) * 32;
 constexpr int kXposeBytes = 32 * 32 * 2;         // per-warp [32 px][32 cout] fp16 transpose
 constexpr int kBarBytes = 512;
 constexpr int kSmemBytes = kStages * kStageBytes + kEpiWarps * kXposeBytes + kBarBytes + 1024;
@@ -209,18 +214,23 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer
+  if (warp == 0 || warp >= 2 + kEpiWarps) {
+    // ----------------------------------------------------------- producers
+    const int prod = warp == 0 ? 0 : warp - (1 + kEpiWarps);   // 0..kProducers-1
     if (lane == 0) {
       int stage = 0; uint32_t phase = 0;
-      int issued = 0;
+      int seq = 0;                       // pipeline fill index (all producers)
+      int issued = 0, last = -1;         // this producer's fills
       bool stop = false;
       for (int pt = first_pt; pt < p.n_px_tiles && !stop; pt += pt_step) {
         const TileCoord tc = tile_coord(p, pt);
         for (int c = 0; c < n_chunks && !stop; ++c) {
           const int t0 = c * kTC;
-          const int tcn = min(kTC, p.T - t0);
-          for (int kb = 0; kb < p.n_kb; ++kb) {
+          for (int kb = 0; kb < p.n_kb; ++kb, ++seq) {
+            if (seq % kProducers != prod) {
+              if (++stage == kStages) { stage = 0; phase ^= 1; }
+              continue;
+            }
             if (*abort_flag) { stop = true; break; }
             if (!mbar_wait_bounded(&empty[stage], phase ^ 1, p.timeout_ns)) {
               atomicOr(p.err, kErrTimeoutEmpty); *abort_flag = 1; stop = true; break;
@@ -240,15 +250,17 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
             }
             tma_load_5d(sB + stage * kTC * kBBytes, &p.tmap_b[map], &full[stage],
                         cb * kKB, tc.w0 + woff, tc.h0 + hoff, tc.n0, t0);
-            ++issued;
+            ++issued; last = seq;
             if (++stage == kStages) { stage = 0; phase ^= 1; }
           }
         }
       }
-      // Let every load already issued land before the CTA can exit.
-      const int n_wait = min(issued, kStages);
+      // Let every load this producer issued land before the CTA can exit:
+      // its fills are seq = last, last - kProducers, ... (at most
+      // kStages / kProducers of them can still be in flight).
+      const int n_wait = min(issued, kStages / kProducers);
       for (int i = 0; i < n_wait; ++i) {
-        const int back = issued - 1 - i;
+        const int back = last - i * kProducers;
         if (!mbar_wait_bounded(&full[back % kStages], (back / kStages) & 1, p.timeout_ns))
           atomicOr(p.err, kErrTimeoutFull);
       }
@@ -257,6 +269,10 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = idesc_f16(kBM, kBN, true);
+      const uint32_t idesc2 = idesc_f16(kBM, kTC * kBN, true);
+      const bool merge_ts = p.box_bytes == kBBytes;   // tiles of exactly 64 pixels
+      const uint64_t a_desc0 = smem_desc_kmajor(smem_u32(sA), 512, 4);
+      const uint64_t b_desc0 = smem_desc_kmajor(smem_u32(sB), 1024, 2);
       if (!mbar_wait_bounded(meta_ready, 0, p.timeout_ns)) {
         atomicOr(p.err, kErrTimeoutMeta); *abort_flag = 1;
       }
@@ -279,18 +295,23 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
               atomicOr(p.err, kErrTimeoutFull); *abort_flag = 1; stop = true; break;
             }
             tc_fence_after();
-            const uint32_t a_base = smem_u32(sA + stage * kABytes);
-            const uint32_t b_base = smem_u32(sB + stage * kTC * kBBytes);
+            // Descriptors advance by adding (byte offset >> 4) to the start
+            // address field (shared-memory addresses stay below 2^18).
+            const uint64_t ad = a_desc0 + ((stage * kABytes) >> 4);
+            const uint64_t bd = b_desc0 + ((stage * kTC * kBBytes) >> 4);
 #pragma unroll
             for (int s = 0; s < 2; ++s) {
               const uint32_t ecol = kMetaCol + 2 * kb + s;
               const uint32_t e_addr = tmem + (ecol & ~1u);
-              const uint32_t id = idesc | (ecol & 1u);
-              const uint64_t adesc = smem_desc_kmajor(a_base + 32 * s, 512, 4);
-              for (int tt = 0; tt < tcn; ++tt) {
-                const uint64_t bdesc = smem_desc_kmajor(b_base + tt * p.box_bytes + 64 * s, 1024, 2);
-                mma_sp_f16(d_base + tt * kBN, adesc, bdesc, e_addr, id,
-                           (kb > 0 || s > 0) ? 1u : 0u);
+              const uint32_t acc = (kb > 0 || s > 0) ? 1u : 0u;
+              if (merge_ts && tcn == kTC) {
+                // Both timesteps' 64-pixel tiles are consecutive rows of the
+                // box: one N = 128 MMA covers them.
+                mma_sp_f16(d_base, ad + 2 * s, bd + 4 * s, e_addr, idesc2 | (ecol & 1u), acc);
+              } else {
+                for (int tt = 0; tt < tcn; ++tt)
+                  mma_sp_f16(d_base + tt * kBN, ad + 2 * s, bd + ((tt * p.box_bytes + 64 * s) >> 4),
+                             e_addr, idesc | (ecol & 1u), acc);
               }
             }
             mma_commit(&empty[stage]);

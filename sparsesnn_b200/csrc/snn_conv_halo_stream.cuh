@@ -13,8 +13,8 @@
 // so the kernel issues as few, large boxes as it can.  Every tap reads a
 // halo through a descriptor offset of (kh*10 + kw) rows.
 //
-// Warp roles as in the resident halo kernel: 0..7 epilogue, 8..11 metadata,
-// 10 MMA + TMEM owner, 11 TMA.
+// Warp roles: 0..7 epilogue, 8..11 metadata, then 10 = MMA + TMEM owner,
+// 11 = halo loads, 8 and 9 = weight loads.
 #pragma once
 #include "snn_conv_halo.cuh"
 
@@ -115,48 +115,59 @@ fused_sparse_conv_halo_stream_kernel(const __grid_constant__ ConvParams p) {
     mbar_arrive(meta_ready);
   }
 
-  if (warp == kHaloTmaWarp) {
-    // ------------------------------------------------------------ producer
+  if (warp == kHaloTmaWarp || warp == 8 || warp == 9) {
+    // ----------------------------------------------------------- producers
+    // Warp 11 loads the halos; warps 8 and 9 load the weight stages (fill j
+    // by warp 8 + j % 2).  A thread issues tensor copies one after another,
+    // so spreading them over three warps keeps more boxes in flight.
     if (lane == 0) {
+      const bool halo_warp = warp == kHaloTmaWarp;
+      const int wprod = warp - 8;
       int as = 0, hs = 0; uint32_t aph = 0, hph = 0;
-      int a_issued = 0, h_issued = 0;
+      int a_seq = 0, a_issued = 0, a_last = -1, h_issued = 0;
       bool stop = false;
       for (int pt = first_pt; pt < p.n_px_tiles && !stop; pt += pt_step) {
         const TileCoord tc = tile_coord(p, pt);
         for (int cbi = 0; cbi < p.cin_blocks && !stop; ++cbi) {
           const int cb = (cbi + cb_rot) % p.cin_blocks;
           if (*abort_flag) { stop = true; break; }
-          if (!mbar_wait_bounded(&h_empty[hs], hph ^ 1, p.timeout_ns)) {
-            atomicOr(p.err, kErrTimeoutEmpty); *abort_flag = 1; stop = true; break;
-          }
-          // All T halos in one box (timesteps beyond T are outside the tensor:
-          // zero-filled and never read).
-          mbar_arrive_expect_tx(&h_full[hs], kHsHaloStride);
-          tma_load_5d(sH + hs * kHsHaloStride, &p.tmap_b[0], &h_full[hs], cb * kKB,
-                      tc.w0 - 1, tc.h0 - 1, tc.n0, 0);
-          ++h_issued;
-          if (++hs == kHsHaloStages) { hs = 0; hph ^= 1; }
-          for (int kh = 0; kh < 3 && !stop; ++kh) {
-            if (*abort_flag) { stop = true; break; }
-            if (!mbar_wait_bounded(&a_empty[as], aph ^ 1, p.timeout_ns)) {
+          if (halo_warp) {
+            if (!mbar_wait_bounded(&h_empty[hs], hph ^ 1, p.timeout_ns)) {
               atomicOr(p.err, kErrTimeoutEmpty); *abort_flag = 1; stop = true; break;
             }
-            // Weights of taps (kh, 0..2) for slice cb: [tap][128 rows][32 el].
-            mbar_arrive_expect_tx(&a_full[as], kHsAStageBytes);
-            tma_load_3d(sA + as * kHsAStageBytes, &p.tmap_b[1], &a_full[as], cb * (kKB / 2),
-                        m_tile * kBM, kh * 3);
-            ++a_issued;
+            // All T halos in one box (timesteps beyond T are outside the
+            // tensor: zero-filled and never read).
+            mbar_arrive_expect_tx(&h_full[hs], kHsHaloStride);
+            tma_load_5d(sH + hs * kHsHaloStride, &p.tmap_b[0], &h_full[hs], cb * kKB,
+                        tc.w0 - 1, tc.h0 - 1, tc.n0, 0);
+            ++h_issued;
+            if (++hs == kHsHaloStages) { hs = 0; hph ^= 1; }
+            continue;
+          }
+          for (int kh = 0; kh < 3 && !stop; ++kh, ++a_seq) {
+            if ((a_seq & 1) == wprod) {
+              if (*abort_flag) { stop = true; break; }
+              if (!mbar_wait_bounded(&a_empty[as], aph ^ 1, p.timeout_ns)) {
+                atomicOr(p.err, kErrTimeoutEmpty); *abort_flag = 1; stop = true; break;
+              }
+              // Weights of taps (kh, 0..2) for slice cb: [tap][128 rows][32 el].
+              mbar_arrive_expect_tx(&a_full[as], kHsAStageBytes);
+              tma_load_3d(sA + as * kHsAStageBytes, &p.tmap_b[1], &a_full[as], cb * (kKB / 2),
+                          m_tile * kBM, kh * 3);
+              ++a_issued; a_last = a_seq;
+            }
             if (++as == kHsAStages) { as = 0; aph ^= 1; }
           }
         }
       }
+      // Let every load this warp issued land before the CTA can exit.
       for (int i = 0; i < min(h_issued, kHsHaloStages); ++i) {
         const int back = h_issued - 1 - i;
         if (!mbar_wait_bounded(&h_full[back % kHsHaloStages], (back / kHsHaloStages) & 1, p.timeout_ns))
           atomicOr(p.err, kErrTimeoutFull);
       }
-      for (int i = 0; i < min(a_issued, kHsAStages); ++i) {
-        const int back = a_issued - 1 - i;
+      for (int i = 0; i < min(a_issued, kHsAStages / 2); ++i) {
+        const int back = a_last - 2 * i;
         if (!mbar_wait_bounded(&a_full[back % kHsAStages], (back / kHsAStages) & 1, p.timeout_ns))
           atomicOr(p.err, kErrTimeoutFull);
       }
