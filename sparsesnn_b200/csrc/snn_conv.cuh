@@ -32,11 +32,12 @@ constexpr int kBM = 128;             // output channels per tile (UMMA M)
 constexpr int kBN = 64;              // output pixels per timestep per tile (UMMA N)
 constexpr int kTC = 2;               // timesteps per accumulator buffer
 constexpr int kNumAcc = 2;           // accumulator buffers
-constexpr int kStages = 8;           // smem pipeline depth
+constexpr int kStages = 4;           // smem pipeline depth
+constexpr int kKbPerStage = 2;       // k-blocks per pipeline stage
 constexpr int kKB = 64;              // logical K per k-block (one 128B activation row)
 constexpr int kABytes = kBM * (kKB / 2) * 2;     // 8 KB compressed weights
 constexpr int kBBytes = kBN * kKB * 2;           // 8 KB activations per timestep
-constexpr int kStageBytes = kABytes + kTC * kBBytes;
+constexpr int kStageBytes = kKbPerStage * (kABytes + kTC * kBBytes);
 constexpr int kAccCols = kTC * kBN;              // 128 TMEM columns per buffer
 constexpr int kMetaCol = kNumAcc * kAccCols;     // metadata columns start here
 constexpr int kTmemCols = 512;
@@ -175,8 +176,9 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint8_t* sA = smem;                                        // kStages x kABytes
-  uint8_t* sB = smem + kStages * kABytes;                    // kStages x kTC x kBBytes
+  // Stage s holds k-blocks (A: kKbPerStage x kABytes; B: kKbPerStage x kTC x kBBytes).
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + kStages * kKbPerStage * kABytes;
   uint8_t* sX = smem + kStages * kStageBytes;                // kEpiWarps x kXposeBytes
   uint64_t* full = reinterpret_cast<uint64_t*>(sX + kEpiWarps * kXposeBytes);
   uint64_t* empty = full + kStages;
@@ -226,7 +228,7 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
         const TileCoord tc = tile_coord(p, pt);
         for (int c = 0; c < n_chunks && !stop; ++c) {
           const int t0 = c * kTC;
-          for (int kb = 0; kb < p.n_kb; ++kb, ++seq) {
+          for (int kb0 = 0; kb0 < p.n_kb; kb0 += kKbPerStage, ++seq) {
             if (seq % kProducers != prod) {
               if (++stage == kStages) { stage = 0; phase ^= 1; }
               continue;
@@ -237,19 +239,23 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
             }
             // One activation box spans the chunk's kTC timesteps (a timestep
             // beyond T is outside the tensor: zero-filled, never read).
-            mbar_arrive_expect_tx(&full[stage], kABytes + kTC * p.box_bytes);
-            tma_load_2d(sA + stage * kABytes, &p.tmap_a, &full[stage], kb * (kKB / 2),
-                        m_tile * kBM);
-            const int tap = kb / p.cin_blocks;
-            const int cb = kb - tap * p.cin_blocks;
-            const int kh = tap / p.KW, kw = tap - kh * p.KW;
-            int map = 0, hoff = kh - p.pad, woff = kw - p.pad;
-            if (p.stride == 2) {
-              map = (hoff & 1) * 2 + (woff & 1);
-              hoff = floordiv2(hoff); woff = floordiv2(woff);
+            const int nk = min(kKbPerStage, p.n_kb - kb0);
+            mbar_arrive_expect_tx(&full[stage], nk * (kABytes + kTC * p.box_bytes));
+            for (int j = 0; j < nk; ++j) {
+              const int kb = kb0 + j;
+              tma_load_2d(sA + (stage * kKbPerStage + j) * kABytes, &p.tmap_a, &full[stage],
+                          kb * (kKB / 2), m_tile * kBM);
+              const int tap = kb / p.cin_blocks;
+              const int cb = kb - tap * p.cin_blocks;
+              const int kh = tap / p.KW, kw = tap - kh * p.KW;
+              int map = 0, hoff = kh - p.pad, woff = kw - p.pad;
+              if (p.stride == 2) {
+                map = (hoff & 1) * 2 + (woff & 1);
+                hoff = floordiv2(hoff); woff = floordiv2(woff);
+              }
+              tma_load_5d(sB + (stage * kKbPerStage + j) * kTC * kBBytes, &p.tmap_b[map], &full[stage],
+                          cb * kKB, tc.w0 + woff, tc.h0 + hoff, tc.n0, t0);
             }
-            tma_load_5d(sB + stage * kTC * kBBytes, &p.tmap_b[map], &full[stage],
-                        cb * kKB, tc.w0 + woff, tc.h0 + hoff, tc.n0, t0);
             ++issued; last = seq;
             if (++stage == kStages) { stage = 0; phase ^= 1; }
           }
@@ -290,28 +296,32 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
           }
           tc_fence_after();
           const uint32_t d_base = tmem + buf * kAccCols;
-          for (int kb = 0; kb < p.n_kb; ++kb) {
+          for (int kb0 = 0; kb0 < p.n_kb; kb0 += kKbPerStage) {
             if (!mbar_wait_bounded(&full[stage], phase, p.timeout_ns)) {
               atomicOr(p.err, kErrTimeoutFull); *abort_flag = 1; stop = true; break;
             }
             tc_fence_after();
-            // Descriptors advance by adding (byte offset >> 4) to the start
-            // address field (shared-memory addresses stay below 2^18).
-            const uint64_t ad = a_desc0 + ((stage * kABytes) >> 4);
-            const uint64_t bd = b_desc0 + ((stage * kTC * kBBytes) >> 4);
+            const int nk = min(kKbPerStage, p.n_kb - kb0);
+            for (int j = 0; j < nk; ++j) {
+              const int kb = kb0 + j;
+              // Descriptors advance by adding (byte offset >> 4) to the start
+              // address field (shared-memory addresses stay below 2^18).
+              const uint64_t ad = a_desc0 + (((stage * kKbPerStage + j) * kABytes) >> 4);
+              const uint64_t bd = b_desc0 + (((stage * kKbPerStage + j) * kTC * kBBytes) >> 4);
 #pragma unroll
-            for (int s = 0; s < 2; ++s) {
-              const uint32_t ecol = kMetaCol + 2 * kb + s;
-              const uint32_t e_addr = tmem + (ecol & ~1u);
-              const uint32_t acc = (kb > 0 || s > 0) ? 1u : 0u;
-              if (merge_ts && tcn == kTC) {
-                // Both timesteps' 64-pixel tiles are consecutive rows of the
-                // box: one N = 128 MMA covers them.
-                mma_sp_f16(d_base, ad + 2 * s, bd + 4 * s, e_addr, idesc2 | (ecol & 1u), acc);
-              } else {
-                for (int tt = 0; tt < tcn; ++tt)
-                  mma_sp_f16(d_base + tt * kBN, ad + 2 * s, bd + ((tt * p.box_bytes + 64 * s) >> 4),
-                             e_addr, idesc | (ecol & 1u), acc);
+              for (int s = 0; s < 2; ++s) {
+                const uint32_t ecol = kMetaCol + 2 * kb + s;
+                const uint32_t e_addr = tmem + (ecol & ~1u);
+                const uint32_t acc = (kb > 0 || s > 0) ? 1u : 0u;
+                if (merge_ts && tcn == kTC) {
+                  // Both timesteps' 64-pixel tiles are consecutive rows of the
+                  // box: one N = 128 MMA covers them.
+                  mma_sp_f16(d_base, ad + 2 * s, bd + 4 * s, e_addr, idesc2 | (ecol & 1u), acc);
+                } else {
+                  for (int tt = 0; tt < tcn; ++tt)
+                    mma_sp_f16(d_base + tt * kBN, ad + 2 * s, bd + ((tt * p.box_bytes + 64 * s) >> 4),
+                               e_addr, idesc | (ecol & 1u), acc);
+                }
               }
             }
             mma_commit(&empty[stage]);
