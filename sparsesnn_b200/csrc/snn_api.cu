@@ -88,6 +88,20 @@ HsKernel hs_kernel_fn(int mode, bool res) {
   }
 }
 
+using StemKernel = void (*)(const snn::StemParams);
+
+StemKernel stem_rows_fn(int cin, int mode) {
+  if (cin == 3) {
+    if (mode == snn::kModeLifHalf) return snn::stem_rows_kernel<3, snn::kModeLifHalf>;
+    if (mode == snn::kModeLifDiv) return snn::stem_rows_kernel<3, snn::kModeLifDiv>;
+    return snn::stem_rows_kernel<3, snn::kModeIf>;
+  }
+  if (mode == snn::kModeLifHalf) return snn::stem_rows_kernel<1, snn::kModeLifHalf>;
+  if (mode == snn::kModeLifDiv) return snn::stem_rows_kernel<1, snn::kModeLifDiv>;
+  return snn::stem_rows_kernel<1, snn::kModeIf>;
+}
+constexpr int kStemRowsSmemMax = 96 * 1024;
+
 constexpr int kSmemLimit = 232448;          // opt-in dynamic smem per block on sm_100
 constexpr int kHaloMaxWeightBytes = 160 * 1024;
 
@@ -121,6 +135,14 @@ int ensure_init() {
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
         if (e != cudaSuccess)
           return g_init_status = fail(SNN_E_CUDA, "smem attribute: %s", cudaGetErrorString(e));
+      }
+      if (mode != snn::kModeNone && res == 0) {
+        for (int cin : {1, 3}) {
+          e = cudaFuncSetAttribute(stem_rows_fn(cin, mode),
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, kStemRowsSmemMax);
+          if (e != cudaSuccess)
+            return g_init_status = fail(SNN_E_CUDA, "smem attribute: %s", cudaGetErrorString(e));
+        }
       }
       e = cudaFuncSetAttribute(hs_kernel_fn(mode, res != 0),
                                cudaFuncAttributeMaxDynamicSharedMemorySize, snn::kHsSmemBytes);
@@ -498,6 +520,24 @@ int snn_stem_forward(const snn_conv_desc* d, int32_t Tin, const float* x, const 
   p.OH = OH; p.OW = OW; p.neuron = d->neuron;
   p.tau = d->tau; p.decay = static_cast<float>(1.0 - 1.0 / static_cast<double>(d->tau));
   p.v_th = d->v_threshold; p.v_reset = d->v_reset;
+  // Row-tiled fast path: 3x3 s1 p1, 64 channels, input repeated over T,
+  // rows of at most 128 pixels.
+  if (Tin == 1 && d->KH == 3 && d->KW == 3 && d->stride == 1 && d->pad == 1 && d->Cout == 64 &&
+      (d->Cin == 1 || d->Cin == 3) && OW <= snn::kStemPx) {
+    const int mode = d->neuron == SNN_NEURON_IF ? snn::kModeIf
+                     : d->tau == 2.0f ? snn::kModeLifHalf : snn::kModeLifDiv;
+    const int R = snn::kStemPx / OW;
+    const size_t smem = static_cast<size_t>(snn::stem_rows_smem_floats(d->Cin, R, OW)) * 4 +
+                        2 * snn::kStemPx * 128;
+    const long long nblk = static_cast<long long>(d->B) * ((OH + R - 1) / R);
+    if (smem <= static_cast<size_t>(kStemRowsSmemMax) && nblk <= 0x7fffffffLL) {
+      stem_rows_fn(d->Cin, mode)<<<static_cast<unsigned>(nblk), snn::kStemThreads, smem,
+                                   static_cast<cudaStream_t>(stream)>>>(p);
+      cudaError_t e = cudaGetLastError();
+      if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));
+      return SNN_OK;
+    }
+  }
   const long long pixels = static_cast<long long>(d->B) * OH * OW;
   const int px_per_block = 256 / (d->Cout / 16);
   if (px_per_block < 1) return fail(SNN_E_INVALID, "stem Cout too large");

@@ -1,11 +1,14 @@
 // Memory-bound glue around the fused sparse layers of an SNN ResNet:
-//  * stem_conv_lif_kernel: dense direct conv (small Cin, e.g. RGB) + BN +
-//    LIF/IF over T, computed once when the input is repeated over T
-//    (direct encoding) and written as fp16 NHWC spikes per timestep.
+//  * stem_rows_kernel / stem_conv_lif_kernel: dense direct conv (small Cin,
+//    e.g. RGB) + BN + LIF/IF over T, computed once when the input is
+//    repeated over T (direct encoding) and written as fp16 NHWC spikes per
+//    timestep (row-tiled fast path for 3x3 / 64-channel stems; the general
+//    kernel covers other shapes and per-timestep inputs).
 //  * head_pool_fc_kernel: global average pool + mean over T + linear head.
 #pragma once
 #include <cstdint>
 #include <cuda_fp16.h>
+#include "snn_conv.cuh"
 
 namespace snn {
 
@@ -115,6 +118,133 @@ stem_conv_lif_kernel(const StemParams p) {
     op[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
     op[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
   }
+  }
+}
+
+// Row-tiled stem for the direct-encoding case (input repeated over T) of a
+// 3x3 stride-1 pad-1 conv with 64 output channels on images at most 128
+// pixels wide.  A block computes R = 128 / OW whole output rows of one image:
+//  * the zero-padded input rows (CIN x (R+2) x (OW+2)), the weights
+//    ([tap][64] fp32) and BN scale/bias are staged in shared memory;
+//  * 256 threads: warp w computes pixels 32*(w/2) + lane of the block and
+//    output channels 32*(w%2) .. +31 (weight reads are warp-wide broadcasts,
+//    input reads consecutive words);
+//  * BN once, then LIF/IF over T in registers; each timestep's spikes go to
+//    a [128 px][64 ch] fp16 tile (128-byte rows, 16-byte chunks XOR-ed with
+//    px & 7) and leave as fully coalesced 16-byte stores, since the block's
+//    output rows are contiguous in the NHWC tensor.  Two tiles alternate, so
+//    one barrier per timestep suffices.
+constexpr int kStemPx = 128;
+constexpr int kStemThreads = 256;
+
+// Shared-memory layout of stem_rows_kernel, in floats: input rows, then the
+// weights (16-byte aligned for float4 reads), scale, bias; the spike tiles
+// start at stem_rows_smem_floats (128-byte aligned).
+__host__ __device__ constexpr int stem_rows_ws_offset(int cin, int R, int OW) {
+  return (cin * (R + 2) * (OW + 2) + 31) / 32 * 32;
+}
+__host__ __device__ constexpr int stem_rows_smem_floats(int cin, int R, int OW) {
+  return (stem_rows_ws_offset(cin, R, OW) + 9 * cin * 64 + 128 + 31) / 32 * 32;
+}
+
+template <int CIN, int MODE>
+__global__ void __launch_bounds__(kStemThreads)
+stem_rows_kernel(const StemParams p) {
+  extern __shared__ __align__(128) float sm[];
+  const int OW = p.OW, R = kStemPx / OW, OWp = OW + 2;
+  const int HWp = (R + 2) * OWp;
+  const int bpi = (p.OH + R - 1) / R;                 // blocks per image
+  const int b = blockIdx.x / bpi, oh0 = (blockIdx.x % bpi) * R;
+  float* xs = sm;                                     // [CIN][R+2][OW+2]
+  float* ws = sm + stem_rows_ws_offset(CIN, R, OW);   // [9*CIN][64], 16-byte aligned
+  float* sc = ws + 9 * CIN * 64;                      // [64]
+  float* bi = sc + 64;                                // [64]
+  uint8_t* tiles = reinterpret_cast<uint8_t*>(sm + stem_rows_smem_floats(CIN, R, OW));
+  const int tid = threadIdx.x;
+  for (int i = tid; i < 9 * CIN * 64; i += kStemThreads) {
+    const int co = i / (9 * CIN), k = i - co * (9 * CIN);   // source [Cout][Cin][3][3]
+    ws[k * 64 + co] = p.w[i];
+  }
+  if (tid < 64) { sc[tid] = p.scale[tid]; bi[tid] = p.bias[tid]; }
+  const float* xin = p.x + static_cast<size_t>(b) * CIN * p.H * p.W;
+  for (int i = tid; i < CIN * HWp; i += kStemThreads) {
+    const int ci = i / HWp, rem = i - ci * HWp;
+    const int r = rem / OWp, c = rem - r * OWp;
+    const int ih = oh0 - 1 + r, iw = c - 1;
+    xs[i] = (ih >= 0 && ih < p.H && iw >= 0 && iw < p.W)
+                ? __ldg(xin + (static_cast<size_t>(ci) * p.H + ih) * p.W + iw) : 0.f;
+  }
+  __syncthreads();
+
+  const int warp = tid / 32, lane = tid % 32;
+  const int pxl = (warp >> 1) * 32 + lane;            // pixel within the block
+  const int ch0 = (warp & 1) * 32;
+  const int r = pxl / OW, c = pxl - (pxl / OW) * OW;
+  const bool in_tile = pxl < R * OW;
+  float acc[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) acc[j] = 0.f;
+  if (in_tile) {
+#pragma unroll
+    for (int ci = 0; ci < CIN; ++ci) {
+#pragma unroll
+      for (int kh = 0; kh < 3; ++kh) {
+#pragma unroll
+        for (int kw = 0; kw < 3; ++kw) {
+          const float xv = xs[ci * HWp + (r + kh) * OWp + c + kw];
+          const float4* wr = reinterpret_cast<const float4*>(ws + ((ci * 3 + kh) * 3 + kw) * 64 + ch0);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 w4 = wr[q];
+            acc[4 * q + 0] = fmaf(xv, w4.x, acc[4 * q + 0]);
+            acc[4 * q + 1] = fmaf(xv, w4.y, acc[4 * q + 1]);
+            acc[4 * q + 2] = fmaf(xv, w4.z, acc[4 * q + 2]);
+            acc[4 * q + 3] = fmaf(xv, w4.w, acc[4 * q + 3]);
+          }
+        }
+      }
+    }
+  }
+  // BN output (pre-scaled by 1/2 for the tau = 2 LIF step, as in the conv epilogues).
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const float s = MODE == kModeLifHalf ? sc[ch0 + j] * 0.5f : sc[ch0 + j];
+    const float o = MODE == kModeLifHalf ? bi[ch0 + j] * 0.5f : bi[ch0 + j];
+    acc[j] = fmaf(acc[j], s, o);
+    v[j] = 0.f;
+  }
+  const int nrows = min(R, p.OH - oh0);
+  const int n16 = nrows * OW * 8;                     // 16-byte chunks of the block's output
+  const long long P = static_cast<long long>(p.B) * p.OH * OW;
+  for (int t = 0; t < p.T; ++t) {
+    uint8_t* tile = tiles + (t & 1) * (kStemPx * 128);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint32_t w[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        uint32_t bits = 0;
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int j = 8 * q + 2 * u + e;
+          if (neuron_step<MODE>(v[j], acc[j], p.decay, p.tau, p.v_th, p.v_reset))
+            bits |= 0x3C00u << (16 * e);
+        }
+        w[u] = bits;
+      }
+      const int cg = (ch0 >> 3) + q;
+      *reinterpret_cast<uint4*>(tile + pxl * 128 + ((cg ^ (pxl & 7)) << 4)) =
+          make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    __syncthreads();
+    uint4* dst = reinterpret_cast<uint4*>(
+        p.out + ((static_cast<size_t>(t) * P + static_cast<size_t>(b) * p.OH * OW +
+                  static_cast<size_t>(oh0) * OW) * 64));
+    for (int i = tid; i < n16; i += kStemThreads) {
+      const int px = i >> 3, cg = i & 7;
+      dst[i] = *reinterpret_cast<const uint4*>(tile + px * 128 + ((cg ^ (px & 7)) << 4));
+    }
   }
 }
 

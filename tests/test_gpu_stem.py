@@ -1,0 +1,63 @@
+"""GPU parity of the dense stem (conv + BN + neuron over T) through the C ABI:
+the row-tiled kernel (3x3 s1 p1, 64 channels, input repeated over T) on
+widths that do and do not divide its 128-pixel tile, and the general kernel
+(per-timestep input, other channel counts)."""
+import ctypes
+
+import numpy as np
+import pytest
+
+from oracle import lif_layer as L
+
+pytestmark = pytest.mark.gpu
+
+
+def run_stem(x, w, scale, bias, T, neuron, tau, Tin):
+    import torch
+    from sparsesnn_b200 import runtime as rt
+    lib = rt.load()
+    B, Cin, H, W = x.shape[1:]
+    Cout = w.shape[0]
+    d = rt.make_desc(T=T, B=B, Cin=Cin, H=H, W=W, Cout=Cout, KH=3, KW=3, stride=1, pad=1,
+                     neuron=neuron, tau=tau)
+    xd = torch.from_numpy(x).cuda()
+    wd = torch.from_numpy(w).cuda()
+    sd = torch.from_numpy(scale).cuda()
+    bd = torch.from_numpy(bias).cuda()
+    out = torch.empty((T * B, H, W, Cout), dtype=torch.float16, device="cuda")
+    rc = lib.snn_stem_forward(ctypes.byref(d), Tin, xd.data_ptr(), wd.data_ptr(), sd.data_ptr(),
+                              bd.data_ptr(), out.data_ptr(), None)
+    assert rc == 0, lib.snn_last_error_message()
+    torch.cuda.synchronize()
+    assert rt.device_error() == 0
+    return np.transpose(out.float().cpu().numpy().reshape(T, B, H, W, Cout), (0, 1, 4, 2, 3))
+
+
+def reference(x, w, scale, bias, T, neuron, tau):
+    z = np.stack([L.conv2d_nchw(x[t], w, 1, 1) for t in range(x.shape[0])])
+    z = (z * scale[None, None, :, None, None] + bias[None, None, :, None, None]).astype(np.float32)
+    if z.shape[0] == 1:
+        z = np.repeat(z, T, 0)
+    return L.multistep_lif(z, tau=tau, neuron=neuron)
+
+
+@pytest.mark.parametrize("case", [
+    dict(H=32, W=32, Cout=64, neuron="lif", tau=2.0, Tin=1),     # CIFAR stem (row-tiled)
+    dict(H=12, W=40, Cout=64, neuron="lif", tau=3.0, Tin=1),     # 128 % 40 != 0, general tau
+    dict(H=9, W=7, Cout=64, neuron="if", tau=2.0, Tin=1),       # IF, short image
+    dict(H=16, W=16, Cout=32, neuron="lif", tau=2.0, Tin=1),     # general kernel (32 channels)
+    dict(H=16, W=16, Cout=64, neuron="lif", tau=2.0, Tin=4),     # general kernel (input per timestep)
+], ids=["cifar", "w40_tau3", "if_9x7", "c32_general", "tin4_general"])
+def test_stem_parity(cuda_device, case):
+    rng = np.random.default_rng(7)
+    T, B, Cin = 4, 3, 3
+    H, W, Cout = case["H"], case["W"], case["Cout"]
+    x = rng.standard_normal((case["Tin"], B, Cin, H, W)).astype(np.float32)
+    w = (rng.standard_normal((Cout, Cin, 3, 3)) * 0.3).astype(np.float32)
+    scale = rng.uniform(0.5, 1.5, Cout).astype(np.float32)
+    bias = rng.normal(0, 0.1, Cout).astype(np.float32)
+    got = run_stem(x, w, scale, bias, T, case["neuron"], case["tau"], case["Tin"])
+    spk, h, _ = reference(x, w, scale, bias, T, case["neuron"], case["tau"])
+    assert set(np.unique(got)) <= {0.0, 1.0}
+    frac, ok, _, _ = L.spike_agreement(got, spk, h)
+    assert frac >= 0.995 and ok, frac
