@@ -168,9 +168,10 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
       ok = ok && mbar_wait_bounded(a_full, 0, p.timeout_ns);
       if (!ok) { atomicOr(p.err, kErrTimeoutMeta); *abort_flag = 1; }
       tc_fence_after();
-      const uint32_t a_base = smem_u32(sA);
-      const uint32_t h_base = smem_u32(sH);
       const uint32_t sbo = static_cast<uint32_t>(hp.halo_w) * 128;
+      const uint64_t a_desc0 = smem_desc_kmajor(smem_u32(sA), 512, 4);
+      const uint64_t h_desc0 = smem_desc_kmajor(smem_u32(sH), sbo, 2);
+      const int halo_row16 = hp.halo_w * 8;            // one halo row of pixels, in 16-byte units
       int stage = 0; uint32_t phase = 0;
       int it = 0;
       bool stop = *abort_flag != 0;
@@ -187,20 +188,21 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
               atomicOr(p.err, kErrTimeoutFull); *abort_flag = 1; stop = true; break;
             }
             tc_fence_after();
-            const uint32_t hs = h_base + stage * hp.halo_stride;
+            // Descriptors advance by adding (byte offset >> 4) to the start
+            // address field; the issue loop is the MMA thread's critical path.
+            const uint64_t hd = h_desc0 + static_cast<uint32_t>(stage * hp.halo_stride >> 4);
 #pragma unroll
             for (int kh = 0; kh < KS; ++kh) {
 #pragma unroll
               for (int kw = 0; kw < KS; ++kw) {
                 const int kb = (kh * KS + kw) * p.cin_blocks + cb;
-                const uint32_t brow = hs + static_cast<uint32_t>(kh * hp.halo_w + kw) * 128;
+                const uint64_t ad = a_desc0 + static_cast<uint32_t>(kb * (kABytes >> 4));
+                const uint64_t bd = hd + static_cast<uint32_t>(kh * halo_row16 + kw * 8);
+                const uint32_t e_addr = tmem + kHaloMetaCol + 2 * kb;
 #pragma unroll
                 for (int s = 0; s < 2; ++s) {
-                  const uint32_t ecol = kHaloMetaCol + 2 * kb + s;
-                  const uint64_t adesc = smem_desc_kmajor(a_base + kb * kABytes + 32 * s, 512, 4);
-                  const uint64_t bdesc = smem_desc_kmajor(brow + 64 * s, sbo, 2);
                   const bool first = (cb == 0 && kh == 0 && kw == 0 && s == 0);
-                  mma_sp_f16(d_tmem, adesc, bdesc, tmem + (ecol & ~1u), idesc | (ecol & 1u),
+                  mma_sp_f16(d_tmem, ad + 2 * s, bd + 4 * s, e_addr, idesc | static_cast<uint32_t>(s),
                              first ? 0u : 1u);
                 }
               }
