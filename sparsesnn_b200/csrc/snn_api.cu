@@ -40,16 +40,22 @@ int g_init_status = SNN_E_NO_DEVICE;
 
 using ConvKernel = void (*)(const snn::ConvParams);
 
-ConvKernel conv_kernel_fn(int mode, bool res) {
+template <int TC>
+ConvKernel conv_kernel_fn_tc(int mode, bool res) {
   switch (mode * 2 + (res ? 1 : 0)) {
-    case 0: return snn::fused_sparse_conv_lif_kernel<snn::kModeLifHalf, false>;
-    case 1: return snn::fused_sparse_conv_lif_kernel<snn::kModeLifHalf, true>;
-    case 2: return snn::fused_sparse_conv_lif_kernel<snn::kModeLifDiv, false>;
-    case 3: return snn::fused_sparse_conv_lif_kernel<snn::kModeLifDiv, true>;
-    case 4: return snn::fused_sparse_conv_lif_kernel<snn::kModeIf, false>;
-    case 5: return snn::fused_sparse_conv_lif_kernel<snn::kModeIf, true>;
-    default: return snn::fused_sparse_conv_lif_kernel<snn::kModeNone, false>;
+    case 0: return snn::fused_sparse_conv_lif_kernel<snn::kModeLifHalf, false, TC>;
+    case 1: return snn::fused_sparse_conv_lif_kernel<snn::kModeLifHalf, true, TC>;
+    case 2: return snn::fused_sparse_conv_lif_kernel<snn::kModeLifDiv, false, TC>;
+    case 3: return snn::fused_sparse_conv_lif_kernel<snn::kModeLifDiv, true, TC>;
+    case 4: return snn::fused_sparse_conv_lif_kernel<snn::kModeIf, false, TC>;
+    case 5: return snn::fused_sparse_conv_lif_kernel<snn::kModeIf, true, TC>;
+    default: return snn::fused_sparse_conv_lif_kernel<snn::kModeNone, false, TC>;
   }
+}
+
+// tc = timesteps per accumulator (2 or 4, see snn::GenCfg).
+ConvKernel conv_kernel_fn(int mode, bool res, int tc) {
+  return tc == 4 ? conv_kernel_fn_tc<4>(mode, res) : conv_kernel_fn_tc<2>(mode, res);
 }
 
 using HaloKernel = void (*)(const snn::HaloParams);
@@ -126,10 +132,13 @@ int ensure_init() {
   g_num_sms = prop.multiProcessorCount;
   for (int mode = 0; mode < 4; ++mode) {
     for (int res = 0; res < (mode == snn::kModeNone ? 1 : 2); ++res) {
-      e = cudaFuncSetAttribute(conv_kernel_fn(mode, res != 0),
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, snn::kSmemBytes);
-      if (e != cudaSuccess)
-        return g_init_status = fail(SNN_E_CUDA, "smem attribute: %s", cudaGetErrorString(e));
+      for (int tc : {2, 4}) {
+        e = cudaFuncSetAttribute(conv_kernel_fn(mode, res != 0, tc),
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 tc == 4 ? snn::GenCfg<4>::kSmemBytes : snn::GenCfg<2>::kSmemBytes);
+        if (e != cudaSuccess)
+          return g_init_status = fail(SNN_E_CUDA, "smem attribute: %s", cudaGetErrorString(e));
+      }
       for (int v = 0; v < 3; ++v) {
         e = cudaFuncSetAttribute(halo_kernel_fn(v ? 128 : 64, v == 2, mode, res != 0),
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
@@ -253,9 +262,14 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
   p.n_px_tiles = static_cast<int>(n_px);
   p.n_m = g.Fpad / snn::kBM;
   p.box_bytes = tw * th * tn * snn::kKB * 2;
+  // Timesteps per accumulator of the general kernel: all four (N = 256 MMAs,
+  // one accumulator) when every CTA owns a single 64-pixel tile and T is a
+  // multiple of 4, else two (double-buffered accumulators).
+  const int tc = (d->T % 4 == 0 && p.box_bytes == snn::kBBytes &&
+                  static_cast<long long>(p.n_px_tiles) * p.n_m <= g_num_sms) ? 4 : 2;
   const cuuint32_t box5[5] = {static_cast<cuuint32_t>(snn::kKB), static_cast<cuuint32_t>(tw),
                               static_cast<cuuint32_t>(th), static_cast<cuuint32_t>(tn),
-                              static_cast<cuuint32_t>(snn::kTC)};
+                              static_cast<cuuint32_t>(tc)};
   {
     const size_t C = d->Cin, W = d->W, H = d->H, B = d->B;
     const char* base = static_cast<const char*>(data);
@@ -377,9 +391,10 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
   const int per_m = std::max(1, std::min(p.n_px_tiles, g_num_sms / p.n_m));
   const long long grid = static_cast<long long>(per_m) * p.n_m;
   if (grid > 0x7fffffffLL) return fail(SNN_E_INVALID, "grid too large");
-  conv_kernel_fn(mode, residual != nullptr)<<<static_cast<unsigned>(grid), snn::kThreads,
-                                               snn::kSmemBytes,
-                                               static_cast<cudaStream_t>(stream)>>>(p);
+  conv_kernel_fn(mode, residual != nullptr, tc)<<<
+      static_cast<unsigned>(grid), snn::kThreads,
+      tc == 4 ? snn::GenCfg<4>::kSmemBytes : snn::GenCfg<2>::kSmemBytes,
+      static_cast<cudaStream_t>(stream)>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));
   return SNN_OK;

@@ -6,9 +6,8 @@
 //   B = activations (N = 64 output pixels per timestep), K-major, 128B swizzle;
 //       one 64-channel slice of one filter tap per k-block, fetched by TMA from
 //       the NHWC input; out-of-bounds zero fill provides the conv padding
-//   D = FP32 accumulators in tensor memory (TMEM), two buffers of
-//       kTC timesteps x 64 columns, so the epilogue of one chunk of timesteps
-//       overlaps the MMAs of the next
+//   D = FP32 accumulators in tensor memory (TMEM): TC timesteps x 64 columns
+//       per buffer (see GenCfg)
 //   E = 2:4 metadata, resident in TMEM for the CTA's whole K range
 //
 // Persistent CTAs: each CTA owns one 128-channel slice (so its metadata is
@@ -30,16 +29,10 @@ namespace snn {
 
 constexpr int kBM = 128;             // output channels per tile (UMMA M)
 constexpr int kBN = 64;              // output pixels per timestep per tile (UMMA N)
-constexpr int kTC = 2;               // timesteps per accumulator buffer
-constexpr int kNumAcc = 2;           // accumulator buffers
-constexpr int kStages = 4;           // smem pipeline depth
-constexpr int kKbPerStage = 2;       // k-blocks per pipeline stage
 constexpr int kKB = 64;              // logical K per k-block (one 128B activation row)
 constexpr int kABytes = kBM * (kKB / 2) * 2;     // 8 KB compressed weights
 constexpr int kBBytes = kBN * kKB * 2;           // 8 KB activations per timestep
-constexpr int kStageBytes = kKbPerStage * (kABytes + kTC * kBBytes);
-constexpr int kAccCols = kTC * kBN;              // 128 TMEM columns per buffer
-constexpr int kMetaCol = kNumAcc * kAccCols;     // metadata columns start here
+constexpr int kMetaCol = 256;                    // metadata columns start here
 constexpr int kTmemCols = 512;
 constexpr int kMaxMetaCols = kTmemCols - kMetaCol;  // => K <= 8192
 constexpr int kEpiWarps = 8;
@@ -52,7 +45,25 @@ constexpr int kProducers = 4;
 constexpr int kThreads = (2 + kEpiWarps + kProducers - 1) * 32;
 constexpr int kXposeBytes = 32 * 32 * 2;         // per-warp [32 px][32 cout] fp16 transpose
 constexpr int kBarBytes = 512;
-constexpr int kSmemBytes = kStages * kStageBytes + kEpiWarps * kXposeBytes + kBarBytes + 1024;
+
+// Pipeline shapes of the general kernel, by timesteps per accumulator (TC):
+//  * TC = 2: two TMEM accumulators of 2 x 64 columns (the epilogue of one
+//    chunk of timesteps overlaps the next chunk's MMAs); stages of two
+//    k-blocks, so each wait/commit pair of the MMA thread covers four MMAs;
+//  * TC = 4: one accumulator of 4 x 64 columns and N = 256 MMAs (one per
+//    k-block half for all four timesteps), for layers where each CTA owns a
+//    single pixel tile, so nothing would overlap a second buffer anyway.
+template <int TC>
+struct GenCfg {
+  static constexpr int kTC = TC;
+  static constexpr int kNumAcc = TC == 4 ? 1 : 2;
+  static constexpr int kStages = TC == 4 ? 5 : 4;
+  static constexpr int kKbPerStage = TC == 4 ? 1 : 2;
+  static constexpr int kStageBytes = kKbPerStage * (kABytes + kTC * kBBytes);
+  static constexpr int kAccCols = kTC * kBN;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kEpiWarps * kXposeBytes + kBarBytes + 1024;
+  static_assert(kNumAcc * kAccCols <= kMetaCol, "accumulators overlap the metadata columns");
+};
 
 enum NeuronKind : int { kLIF = 0, kIF = 1, kNoNeuron = 2 };
 // Epilogue variants (template parameter): LIF with tau == 2 (every scaling
@@ -170,9 +181,13 @@ __device__ __forceinline__ TileCoord tile_coord(const ConvParams& p, int pt) {
   return c;
 }
 
-template <int MODE, bool RES>
+template <int MODE, bool RES, int TC>
 __global__ void __launch_bounds__(kThreads, 1)
 fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
+  using Cfg = GenCfg<TC>;
+  constexpr int kTC = Cfg::kTC, kNumAcc = Cfg::kNumAcc, kStages = Cfg::kStages;
+  constexpr int kKbPerStage = Cfg::kKbPerStage, kStageBytes = Cfg::kStageBytes;
+  constexpr int kAccCols = Cfg::kAccCols;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -222,7 +237,6 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
     if (lane == 0) {
       int stage = 0; uint32_t phase = 0;
       int seq = 0;                       // pipeline fill index (all producers)
-      int issued = 0, last = -1;         // this producer's fills
       bool stop = false;
       for (int pt = first_pt; pt < p.n_px_tiles && !stop; pt += pt_step) {
         const TileCoord tc = tile_coord(p, pt);
@@ -256,17 +270,15 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
               tma_load_5d(sB + (stage * kKbPerStage + j) * kTC * kBBytes, &p.tmap_b[map], &full[stage],
                           cb * kKB, tc.w0 + woff, tc.h0 + hoff, tc.n0, t0);
             }
-            ++issued; last = seq;
             if (++stage == kStages) { stage = 0; phase ^= 1; }
           }
         }
       }
-      // Let every load this producer issued land before the CTA can exit:
-      // its fills are seq = last, last - kProducers, ... (at most
-      // kStages / kProducers of them can still be in flight).
-      const int n_wait = min(issued, kStages / kProducers);
-      for (int i = 0; i < n_wait; ++i) {
-        const int back = last - i * kProducers;
+      // Let every load this producer issued land before the CTA can exit.
+      // Only the last kStages fills can still be in flight, one per stage,
+      // so waiting on their parity cannot alias an older phase.
+      for (int back = max(0, seq - kStages); back < seq; ++back) {
+        if (back % kProducers != prod) continue;
         if (!mbar_wait_bounded(&full[back % kStages], (back / kStages) & 1, p.timeout_ns))
           atomicOr(p.err, kErrTimeoutFull);
       }
@@ -289,8 +301,8 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
       for (int pt = first_pt; pt < p.n_px_tiles && !stop; pt += pt_step) {
         for (int c = 0; c < n_chunks && !stop; ++c) {
           const int tcn = min(kTC, p.T - c * kTC);
-          const int buf = acc_iter & 1;
-          const uint32_t use = static_cast<uint32_t>(acc_iter >> 1);
+          const int buf = acc_iter % kNumAcc;
+          const uint32_t use = static_cast<uint32_t>(acc_iter / kNumAcc);
           if (!mbar_wait_bounded(&acc_empty[buf], (use & 1) ^ 1, p.timeout_ns)) {
             atomicOr(p.err, kErrTimeoutAccEmpty); *abort_flag = 1; stop = true; break;
           }
@@ -397,8 +409,8 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
       for (int c = 0; c < n_chunks && !stop; ++c) {
         const int t0 = c * kTC;
         const int tcn = min(kTC, p.T - t0);
-        const int buf = acc_iter & 1;
-        const uint32_t use = static_cast<uint32_t>(acc_iter >> 1);
+        const int buf = acc_iter % kNumAcc;
+        const uint32_t use = static_cast<uint32_t>(acc_iter / kNumAcc);
         bool fail = !mbar_wait_bounded(&acc_full[buf], use & 1, p.timeout_ns);
         fail = __any_sync(0xffffffffu, fail || *abort_flag);
         if (fail) { atomicOr(p.err, kErrTimeoutAcc); stop = true; break; }
