@@ -211,13 +211,30 @@ int encode(CUtensorMap* map, int rank, const void* base, const cuuint64_t* dims,
 }
 
 // Which kernel serves a descriptor (see the SNN_VARIANT_* values).
+// Pixels per tile of the general kernel: up to 64 pixels of one timestep --
+// a run of one output row, whole rows of one image, or whole images.
+void general_tile(const Geometry& g, int B, int* tw, int* th, int* tn) {
+  if (g.OW >= snn::kBN) { *tw = snn::kBN; *th = 1; *tn = 1; }
+  else if (g.OH * g.OW >= snn::kBN) { *tw = g.OW; *th = snn::kBN / g.OW; *tn = 1; }
+  else { *tw = g.OW; *th = g.OH; *tn = std::max(1, std::min(B, snn::kBN / (g.OH * g.OW))); }
+}
+int general_tile_px(const Geometry& g) {
+  int tw, th, tn;
+  general_tile(g, 1 << 30, &tw, &th, &tn);
+  return tw * th * tn;
+}
+
 int select_variant(const snn_conv_desc* d, const Geometry& g) {
   if (d->flags & SNN_FLAG_FORCE_GENERIC) return SNN_VARIANT_GENERIC;
   const bool s1_3x3 = d->stride == 1 && d->KH == 3 && d->KW == 3 && d->pad == 1;
   if (!s1_3x3) return SNN_VARIANT_GENERIC;
   const int a_bytes = g.n_kb * snn::kABytes;
   if (a_bytes <= kHaloMaxWeightBytes && g.OH >= 8) return SNN_VARIANT_HALO_RESIDENT;
-  if (g.OH >= 8 && g.OW >= 8 && d->T <= snn::kHsMaxT) return SNN_VARIANT_HALO_STREAM;
+  // With streamed weights the general kernel is faster whenever its tiles
+  // hold exactly 64 pixels (its MMAs then cover two or four timesteps at
+  // once); the streaming halo kernel serves the other image sizes.
+  if (g.OH >= 8 && g.OW >= 8 && d->T <= snn::kHsMaxT && general_tile_px(g) != snn::kBN)
+    return SNN_VARIANT_HALO_STREAM;
   return SNN_VARIANT_GENERIC;
 }
 
@@ -250,9 +267,7 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
   // timestep -- a run of one output row, whole rows of one image, or whole
   // images.
   int tw, th, tn;
-  if (g.OW >= snn::kBN) { tw = snn::kBN; th = 1; tn = 1; }
-  else if (g.OH * g.OW >= snn::kBN) { tw = g.OW; th = snn::kBN / g.OW; tn = 1; }
-  else { tw = g.OW; th = g.OH; tn = snn::kBN / (g.OH * g.OW); }
+  general_tile(g, d->B, &tw, &th, &tn);
   p.tw = tw; p.th = th; p.tn = tn;
   p.tiles_w = (g.OW + tw - 1) / tw;
   p.tiles_h = (g.OH + th - 1) / th;

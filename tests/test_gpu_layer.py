@@ -247,13 +247,14 @@ def test_size_independent_properties(cuda_device):
 @pytest.mark.parametrize("T", [1, 2, 3, 4])
 @pytest.mark.parametrize("residual", [False, True], ids=["plain", "res"])
 def test_halo_stream_variant(cuda_device, T, residual):
-    """Streaming-weight halo kernel (Cin=256 on 8x8 and 16x8 images) against
-    the oracle, for every timestep count it serves (collector A reuse across
-    1..4 timesteps) and with the SEW residual."""
+    """Streaming-weight halo kernel (Cin=256 on 12x12 and 8x12 images, whose
+    general-kernel tiles would not hold 64 pixels) against the oracle, for
+    every timestep count it serves (collector A reuse across 1..4 timesteps)
+    and with the SEW residual."""
     import torch
     from sparsesnn_b200 import runtime as rt
     from sparsesnn_b200.layer import SparseConvBNLIF, fold_bn
-    for (H, W) in ((8, 8), (16, 8)):
+    for (H, W) in ((12, 12), (8, 12)):
         x, w, bn = L.make_config0(seed=10 + T, T=T, B=3, C=256, F=256, H=H, W=W)
         scale, bias = fold_bn(bn.gamma, bn.beta, bn.mean, bn.var)
         layer = SparseConvBNLIF(w, scale, bias, T=T, B=3, H=H, W=W)
