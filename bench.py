@@ -158,7 +158,7 @@ def run_reference(args, rank):
 def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
-    from sparsesnn_b200.sew_resnet import SEWResNet18, conv_layer_flops, init_params
+    from sparsesnn_b200.sew_resnet import SEWResNet18, conv_layer_bytes, conv_layer_flops, init_params
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -253,6 +253,9 @@ def run_ours(args, rank, world, local_rank):
     conv_names = [n for n, _ in ops if n not in ("stem", "head")]
     conv_ms = sum(per_layer[n] for n in conv_names)
     flops = sum(conv_layer_flops(l) for l in model.conv_layers())
+    alg_bytes = sum(conv_layer_bytes(blk["l1"], False) + conv_layer_bytes(blk["l2"], True) +
+                    (conv_layer_bytes(blk["ds"], False) if blk["ds"] is not None else 0)
+                    for blk in model.blocks)
     hbm_peak, bf16_peak, peak_kind = peaks()
     sparse_peak = 2.0 * bf16_peak
     achieved = flops / (conv_ms / 1000.0) / 1e12
@@ -288,7 +291,11 @@ def run_ours(args, rank, world, local_rank):
                              "kernel": "fused_sparse_conv_lif_kernel (19 launches/forward)",
                              "peak_note": f"2:4 sparse ceiling = 2 x {peak_kind} dense bf16 "
                                           f"{bf16_peak} TFLOP/s; FLOPs dense-equivalent",
-                             "flops_per_forward": flops, "kernel_ms_per_forward": conv_ms},
+                             "flops_per_forward": flops, "kernel_ms_per_forward": conv_ms,
+                             "hbm_view": {"achieved": alg_bytes / (conv_ms / 1000.0) / 1e9,
+                                          "peak": hbm_peak, "unit": "GB/s",
+                                          "frac": alg_bytes / (conv_ms / 1000.0) / 1e9 / hbm_peak,
+                                          "algorithmic_bytes_per_forward": alg_bytes}},
                 "layer_ms": {k: round(v, 4) for k, v in per_layer.items()},
                 "clocks": dict(clk.summary(), window="timed region plus 300 replays before and 200 after"),
                 "cpu_baseline": cpu}
