@@ -11,6 +11,7 @@
 #include <cmath>
 #include <cstring>
 #include <mutex>
+#include <utility>
 
 #include "../../include/snn_b200.h"
 #include "snn_conv.cuh"
@@ -109,6 +110,26 @@ StemKernel stem_rows_fn(int cin, int mode) {
 constexpr int kStemRowsSmemMax = 96 * 1024;
 
 constexpr int kSmemLimit = 232448;          // opt-in dynamic smem per block on sm_100
+
+// Launches with programmatic stream serialization: the kernel may be
+// scheduled while its predecessor in the stream drains (the kernels run their
+// prologue on constant data, then griddepcontrol.wait before touching stream
+// data).  Returns the launch status.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, void* stream,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 constexpr int kHaloMaxWeightBytes = 160 * 1024;
 
 int ensure_init() {
@@ -366,9 +387,9 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
       const size_t smem = static_cast<size_t>(fixed) + static_cast<size_t>(hp.halo_stages) * hp.halo_stride;
       const int per_m = std::max(1, std::min(p.n_px_tiles, g_num_sms / p.n_m));
       const long long grid = static_cast<long long>(per_m) * p.n_m;
-      halo_kernel_fn(bn, m64, mode, residual != nullptr)<<<static_cast<unsigned>(grid), snn::kHaloThreads,
-                                                      smem, static_cast<cudaStream_t>(stream)>>>(hp);
-      cudaError_t e = cudaGetLastError();
+      cudaError_t e = launch_pdl(halo_kernel_fn(bn, m64, mode, residual != nullptr),
+                                 dim3(static_cast<unsigned>(grid)), dim3(snn::kHaloThreads), smem,
+                                 stream, hp);
       if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));
       return SNN_OK;
     }
@@ -396,21 +417,19 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
     }
     const int per_m = std::max(1, std::min(ph.n_px_tiles, g_num_sms / ph.n_m));
     const long long grid = static_cast<long long>(per_m) * ph.n_m;
-    hs_kernel_fn(mode, residual != nullptr)<<<static_cast<unsigned>(grid), snn::kHaloThreads,
-                                               snn::kHsSmemBytes,
-                                               static_cast<cudaStream_t>(stream)>>>(ph);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(hs_kernel_fn(mode, residual != nullptr),
+                               dim3(static_cast<unsigned>(grid)), dim3(snn::kHaloThreads),
+                               snn::kHsSmemBytes, stream, ph);
     if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));
     return SNN_OK;
   }
   const int per_m = std::max(1, std::min(p.n_px_tiles, g_num_sms / p.n_m));
   const long long grid = static_cast<long long>(per_m) * p.n_m;
   if (grid > 0x7fffffffLL) return fail(SNN_E_INVALID, "grid too large");
-  conv_kernel_fn(mode, residual != nullptr, tc)<<<
-      static_cast<unsigned>(grid), snn::kThreads,
-      tc == 4 ? snn::GenCfg<4>::kSmemBytes : snn::GenCfg<2>::kSmemBytes,
-      static_cast<cudaStream_t>(stream)>>>(p);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(conv_kernel_fn(mode, residual != nullptr, tc),
+                             dim3(static_cast<unsigned>(grid)), dim3(snn::kThreads),
+                             tc == 4 ? snn::GenCfg<4>::kSmemBytes : snn::GenCfg<2>::kSmemBytes,
+                             stream, p);
   if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));
   return SNN_OK;
 }
@@ -561,9 +580,8 @@ int snn_stem_forward(const snn_conv_desc* d, int32_t Tin, const float* x, const 
                         2 * snn::kStemPx * 128;
     const long long nblk = static_cast<long long>(d->B) * ((OH + R - 1) / R);
     if (smem <= static_cast<size_t>(kStemRowsSmemMax) && nblk <= 0x7fffffffLL) {
-      stem_rows_fn(d->Cin, mode)<<<static_cast<unsigned>(nblk), snn::kStemThreads, smem,
-                                   static_cast<cudaStream_t>(stream)>>>(p);
-      cudaError_t e = cudaGetLastError();
+      cudaError_t e = launch_pdl(stem_rows_fn(d->Cin, mode), dim3(static_cast<unsigned>(nblk)),
+                                 dim3(snn::kStemThreads), smem, stream, p);
       if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));
       return SNN_OK;
     }
@@ -576,13 +594,10 @@ int snn_stem_forward(const snn_conv_desc* d, int32_t Tin, const float* x, const 
   dim3 block(256);
   dim3 grid(static_cast<unsigned>(nblk));
   const size_t smem = static_cast<size_t>(d->KH) * d->KW * d->Cin * d->Cout * sizeof(float);
-  if (d->KH == 3 && d->KW == 3 && d->Cin == 3)
-    snn::stem_conv_lif_kernel<3, 3><<<grid, block, smem, static_cast<cudaStream_t>(stream)>>>(p);
-  else if (d->KH == 3 && d->KW == 3 && d->Cin == 2)
-    snn::stem_conv_lif_kernel<3, 2><<<grid, block, smem, static_cast<cudaStream_t>(stream)>>>(p);
-  else
-    snn::stem_conv_lif_kernel<0, 0><<<grid, block, smem, static_cast<cudaStream_t>(stream)>>>(p);
-  cudaError_t e = cudaGetLastError();
+  StemKernel k = (d->KH == 3 && d->KW == 3 && d->Cin == 3)   ? snn::stem_conv_lif_kernel<3, 3>
+                 : (d->KH == 3 && d->KW == 3 && d->Cin == 2) ? snn::stem_conv_lif_kernel<3, 2>
+                                                             : snn::stem_conv_lif_kernel<0, 0>;
+  cudaError_t e = launch_pdl(k, grid, block, smem, stream, p);
   if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));
   return SNN_OK;
 }
@@ -598,9 +613,8 @@ int snn_head_forward(int32_t T, int32_t B, int32_t HW, int32_t C, int32_t NC, co
   if (reinterpret_cast<uintptr_t>(fc_w) & 15) return fail(SNN_E_INVALID, "fc_w must be 16-byte aligned");
   const int threads = 1024;
   const size_t smem = static_cast<size_t>(snn::kHeadSlots + 1) * C * sizeof(float);
-  snn::head_pool_fc_kernel<<<B, threads, smem, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __half*>(x), fc_w, fc_b, logits, T, B, HW, C, NC);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(snn::head_pool_fc_kernel, dim3(B), dim3(threads), smem, stream,
+                             static_cast<const __half*>(x), fc_w, fc_b, logits, T, B, HW, C, NC);
   if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));
   return SNN_OK;
 }

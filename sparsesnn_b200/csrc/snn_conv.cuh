@@ -226,6 +226,7 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
     for (int i = 0; i < (p.stride == 2 ? 4 : 1); ++i) prefetch_tmap(&p.tmap_b[i]);
   }
   if (warp == 1) { tmem_alloc(tmem_slot, kTmemCols); tmem_relinquish(); }
+  pdl_launch_dependents();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -235,6 +236,7 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
     // ----------------------------------------------------------- producers
     const int prod = warp == 0 ? 0 : warp - (1 + kEpiWarps);   // 0..kProducers-1
     if (lane == 0) {
+      pdl_wait();                        // activations come from the previous kernel
       int stage = 0; uint32_t phase = 0;
       int seq = 0;                       // pipeline fill index (all producers)
       bool stop = false;
@@ -375,6 +377,7 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
     const float bi = cvalid ? p.bias[cout] : 0.f;
     const long long P = static_cast<long long>(p.B) * p.OH * p.OW;
     const int tile_px = p.tw * p.th;
+    pdl_wait();                          // residual, output and state belong to the stream
     const int cbase = m_tile * kBM + q * 32;     // first output channel of this warp
     const int nchunk8 = max(0, min(4, (p.F - cbase) / 8));   // valid 8-channel chunks
     const bool chunk_ok = (lane & 3) < nchunk8;

@@ -102,6 +102,7 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
   }
   if (warp == kHaloTmaWarp && lane == 0) { prefetch_tmap(&p.tmap_a); prefetch_tmap(&p.tmap_b[0]); }
   if (warp == kHaloMmaWarp) { tmem_alloc(tmem_slot, kHaloTmemCols); tmem_relinquish(); }
+  pdl_launch_dependents();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -133,6 +134,7 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
       mbar_arrive_expect_tx(a_full, hp.a_bytes);
       for (int kb = 0; kb < p.n_kb; ++kb)
         tma_load_2d(sA + kb * kABytes, &p.tmap_a, a_full, kb * (kKB / 2), m_tile * kBM);
+      pdl_wait();                        // activations come from the previous kernel
       int stage = 0; uint32_t phase = 0;
       int issued = 0;
       bool stop = false;
@@ -235,6 +237,7 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
     const int c16 = lane & 7;                        // row phase: 16-byte channel chunk
     const bool chunk_ok = c16 * 8 < p.F;
     const int bar_id = 1 + half;                     // named barrier of the half's 4 warps
+    pdl_wait();                                      // residual, output and state
 
     int it = 0;
     bool stop = false;
@@ -339,6 +342,7 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
     const int nchunk8 = max(0, min(4, (p.F - cbase) / 8));
     const bool chunk_ok = (lane & 3) < nchunk8;
     uint8_t* xb = sX + warp * kXposeBytes;
+    pdl_wait();                          // residual, output and state belong to the stream
 
     int it = 0;
     bool stop = false;

@@ -93,6 +93,7 @@ fused_sparse_conv_halo_stream_kernel(const __grid_constant__ ConvParams p) {
   }
   if (warp == kHaloTmaWarp && lane == 0) { prefetch_tmap(&p.tmap_b[0]); prefetch_tmap(&p.tmap_b[1]); }
   if (warp == kHaloMmaWarp) { tmem_alloc(tmem_slot, kHaloTmemCols); tmem_relinquish(); }
+  pdl_launch_dependents();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -122,6 +123,7 @@ fused_sparse_conv_halo_stream_kernel(const __grid_constant__ ConvParams p) {
     // so spreading them over three warps keeps more boxes in flight.
     if (lane == 0) {
       const bool halo_warp = warp == kHaloTmaWarp;
+      if (halo_warp) pdl_wait();         // activations come from the previous kernel
       const int wprod = warp - 8;
       int as = 0, hs = 0; uint32_t aph = 0, hph = 0;
       int a_seq = 0, a_issued = 0, a_last = -1, h_issued = 0;
@@ -261,6 +263,7 @@ fused_sparse_conv_halo_stream_kernel(const __grid_constant__ ConvParams p) {
     const int nchunk8 = max(0, min(4, (p.F - cbase) / 8));
     const bool chunk_ok = (lane & 3) < nchunk8;
     uint8_t* xb = sX + warp * kXposeBytes;
+    pdl_wait();                          // residual, output and state belong to the stream
 
     int tile_it = 0;
     bool stop = false;

@@ -32,6 +32,8 @@ template <int KS, int CIN>
 __global__ void __launch_bounds__(256, 2)
 stem_conv_lif_kernel(const StemParams p) {
   extern __shared__ float ws[];
+  pdl_launch_dependents();
+  pdl_wait();
   const int KH = KS ? KS : p.KH, KW = KS ? KS : p.KW, Cin = CIN ? CIN : p.Cin;
   const int K = KH * KW * Cin;
   // Coalesced read of the [Cout][K] source, transposed into [K][Cout].
@@ -166,6 +168,8 @@ stem_rows_kernel(const StemParams p) {
     ws[k * 64 + co] = p.w[i];
   }
   if (tid < 64) { sc[tid] = p.scale[tid]; bi[tid] = p.bias[tid]; }
+  pdl_launch_dependents();
+  pdl_wait();                                         // input and output belong to the stream
   const float* xin = p.x + static_cast<size_t>(b) * CIN * p.H * p.W;
   for (int i = tid; i < CIN * HWp; i += kStemThreads) {
     const int ci = i / HWp, rem = i - ci * HWp;
@@ -262,6 +266,8 @@ head_pool_fc_kernel(const __half* __restrict__ x, const float* __restrict__ fc_w
   float* part = sm;                          // [kHeadSlots][C]
   float* feat = sm + kHeadSlots * C;         // [C]
   const int b = blockIdx.x;
+  pdl_launch_dependents();
+  pdl_wait();
   const int c8n = C / 8;
   for (int task = threadIdx.x; task < c8n * kHeadSlots; task += blockDim.x) {
     const int c8 = task % c8n, slot = task / c8n;

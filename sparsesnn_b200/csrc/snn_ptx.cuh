@@ -56,6 +56,18 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
 }
 
+// ------------------------------------------- programmatic dependent launch
+// Kernels are launched with programmatic stream serialization: a kernel may
+// start while its predecessor in the stream drains, runs its prologue on
+// constant data (barriers, TMEM, weights, metadata), and waits here before
+// touching anything the predecessor writes or reads.  Without a programmatic
+// predecessor the wait returns at once.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Lets the next kernel in the stream be scheduled (onto SMs this grid frees).
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // --------------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
                                             int c0, int c1) {
