@@ -13,8 +13,8 @@
 // Persistent CTAs: each CTA owns one 128-channel slice (so its metadata is
 // loaded once) and walks a strided list of pixel tiles.
 //
-// Warp roles (13 warps): 0 and 10..12 = TMA producers (stage s is filled by
-// producer s % 4), 1 = TMEM owner + MMA issuer, 2..9 = epilogue: two warps
+// Warp roles (11 warps): 0 and 10 = TMA producers (pipeline fill i is issued
+// by producer i % 2), 1 = TMEM owner + MMA issuer, 2..9 = epilogue: two warps
 // per TMEM lane quarter, each owning 32 of the 64 pixel columns.  The epilogue applies BN, runs the LIF/IF recurrence over T
 // with the membrane in registers, stages fp16 spikes in a per-warp transpose
 // tile, adds the SEW residual and writes 16-byte vectors (see the store stage
@@ -37,11 +37,11 @@ constexpr int kTmemCols = 512;
 constexpr int kMaxMetaCols = kTmemCols - kMetaCol;  // => K <= 8192
 constexpr int kEpiWarps = 8;
 constexpr int kEpiThreads = kEpiWarps * 32;
-// TMA producers: warp 0 and warps 10..12.  One thread issues tensor copies
-// one after another (a few hundred cycles each, whatever the box size), so
-// several producer warps, each owning every kProducers-th pipeline stage,
-// keep enough boxes in flight.
-constexpr int kProducers = 4;
+// TMA producers: warp 0 and warp 10.  One thread issues tensor copies one
+// after another (a few hundred cycles each, whatever the box size), so two
+// producer warps, each filling every other pipeline stage, keep enough
+// boxes in flight.
+constexpr int kProducers = 2;
 constexpr int kThreads = (2 + kEpiWarps + kProducers - 1) * 32;
 constexpr int kXposeBytes = 32 * 32 * 2;         // per-warp [32 px][32 cout] fp16 transpose
 constexpr int kBarBytes = 512;
@@ -414,39 +414,66 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
         const int tcn = min(kTC, p.T - t0);
         const int buf = acc_iter % kNumAcc;
         const uint32_t use = static_cast<uint32_t>(acc_iter / kNumAcc);
+        // Residual rows of the first two timesteps, fetched before the wait so
+        // their latency overlaps the MMAs.
+        uint4 r4[2][4];
+        if constexpr (RES) {
+#pragma unroll
+          for (int u = 0; u < 2; ++u)
+            if (u < tcn)
+              load_residual_rows(p.residual, static_cast<size_t>(t0 + u) * P, rows, p.F, cbase, lane,
+                                 chunk_ok, r4[u]);
+        }
         bool fail = !mbar_wait_bounded(&acc_full[buf], use & 1, p.timeout_ns);
         fail = __any_sync(0xffffffffu, fail || *abort_flag);
         if (fail) { atomicOr(p.err, kErrTimeoutAcc); stop = true; break; }
         tc_fence_after();
-        for (int tt = 0; tt < tcn; ++tt) {
-          const size_t tbase = static_cast<size_t>(t0 + tt) * P;
-          // Residual rows, fetched before the TMEM load so their latency
-          // overlaps the neuron update.
-          uint4 r4[4];
-          if constexpr (RES) load_residual_rows(p.residual, tbase, rows, p.F, cbase, lane, chunk_ok, r4);
-          float acc[32];
-          tmem_ld32(lane_base + buf * kAccCols + tt * kBN + half * 32, acc);
-          if constexpr (MODE == kModeNone) {
+        // Timesteps in pairs: both accumulators of a pair come in one TMEM
+        // round trip; the buffer is released once its last pair is loaded.
+        for (int t2 = 0; t2 < tcn; t2 += 2) {
+          const int np = min(2, tcn - t2);
+          uint32_t accr[2][32];
+          tmem_ld32_nowait(lane_base + buf * kAccCols + t2 * kBN + half * 32, accr[0]);
+          if (np > 1) tmem_ld32_nowait(lane_base + buf * kAccCols + (t2 + 1) * kBN + half * 32, accr[1]);
+          tmem_wait_ld();
+          if (t2 + 2 >= tcn) {                 // buffer drained: the MMAs it holds back may start
+            tc_fence_before();
+            mbar_arrive(&acc_empty[buf]);
+          }
+          if constexpr (RES) {
+            if (t2 > 0) {                      // later pairs: fetched now, used after the update
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const int px = __shfl_sync(0xffffffffu, my_px, i);
-              if (cvalid && px >= 0) p.out_f32[(tbase + px) * p.F + cout] = fmaf(acc[i], sc, bi);
+              for (int u = 0; u < 2; ++u)
+                if (u < np)
+                  load_residual_rows(p.residual, static_cast<size_t>(t0 + t2 + u) * P, rows, p.F,
+                                     cbase, lane, chunk_ok, r4[u]);
             }
-          } else {
-            // Neuron update, lane = output channel, i = pixel column.
-            const float sx = MODE == kModeLifHalf ? sc * 0.5f : sc;
-            const float bx = MODE == kModeLifHalf ? bi * 0.5f : bi;
+          }
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-              xpose_put(xb, i, lane, neuron_step<MODE>(v[i], fmaf(acc[i], sx, bx), p.decay, p.tau,
-                                                       p.v_th, p.v_reset));
-            __syncwarp();
-            store_xpose_rows<RES>(p.out, xb, tbase, rows, p.F, cbase, lane, chunk_ok, r4);
-            __syncwarp();
+          for (int u = 0; u < 2; ++u) {
+            if (u >= np) break;
+            const size_t tbase = static_cast<size_t>(t0 + t2 + u) * P;
+            if constexpr (MODE == kModeNone) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                const int px = __shfl_sync(0xffffffffu, my_px, i);
+                if (cvalid && px >= 0)
+                  p.out_f32[(tbase + px) * p.F + cout] = fmaf(__uint_as_float(accr[u][i]), sc, bi);
+              }
+            } else {
+              // Neuron update, lane = output channel, i = pixel column.
+              const float sx = MODE == kModeLifHalf ? sc * 0.5f : sc;
+              const float bx = MODE == kModeLifHalf ? bi * 0.5f : bi;
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                xpose_put(xb, i, lane, neuron_step<MODE>(v[i], fmaf(__uint_as_float(accr[u][i]), sx, bx),
+                                                         p.decay, p.tau, p.v_th, p.v_reset));
+              __syncwarp();
+              store_xpose_rows<RES>(p.out, xb, tbase, rows, p.F, cbase, lane, chunk_ok, r4[u]);
+              __syncwarp();
+            }
           }
         }
-        tc_fence_before();
-        mbar_arrive(&acc_empty[buf]);
         ++acc_iter;
       }
       if (!stop && (p.flags & kWriteState)) {
