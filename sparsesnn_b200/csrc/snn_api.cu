@@ -367,9 +367,16 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
     hp.halo_w = 8 + d->KW - 1;
     hp.halo_bytes = hp.halo_w * (th_ + d->KH - 1) * snn::kKB * 2;
     hp.halo_stride = (hp.halo_bytes + 1023) / 1024 * 1024;
-    hp.a_bytes = a_bytes;
+    // M = 64 keeps only the 64 real weight rows resident (box of 64 rows).
+    hp.a_bytes = m64 ? a_bytes / 2 : a_bytes;
+    if (m64) {
+      cuuint64_t dims[2] = {static_cast<cuuint64_t>(g.K / 2), static_cast<cuuint64_t>(g.Fpad)};
+      cuuint64_t strides[1] = {static_cast<cuuint64_t>(g.K / 2) * 2};
+      cuuint32_t box[2] = {snn::kKB / 2, 64};
+      if ((st = encode(&p.tmap_a, 2, wbytes, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B))) return st;
+    }
     const int fixed = 1024 + 512 + (m64 ? snn::kHalo64XposeBytes : snn::kEpiWarps * snn::kXposeBytes) +
-                      a_bytes;
+                      hp.a_bytes;
     hp.halo_stages = std::min(snn::kHaloMaxStages, (kSmemLimit - fixed) / hp.halo_stride);
     if (hp.halo_stages >= 2) {
       p.tw = 8; p.th = th_; p.tn = 1;

@@ -67,6 +67,7 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
   static_assert(!M64 || BN == 128, "the M = 64 path tiles 128 pixels");
   const ConvParams& p = hp.c;
   constexpr int G = BN / 64;                 // 32-column groups per epilogue warp
+  constexpr int kAKb = (M64 ? 64 : kBM) * (kKB / 2) * 2;   // resident weight bytes per k-block
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -133,7 +134,7 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
     if (lane == 0) {
       mbar_arrive_expect_tx(a_full, hp.a_bytes);
       for (int kb = 0; kb < p.n_kb; ++kb)
-        tma_load_2d(sA + kb * kABytes, &p.tmap_a, a_full, kb * (kKB / 2), m_tile * kBM);
+        tma_load_2d(sA + kb * kAKb, &p.tmap_a, a_full, kb * (kKB / 2), m_tile * kBM);
       pdl_wait();                        // activations come from the previous kernel
       int stage = 0; uint32_t phase = 0;
       int issued = 0;
@@ -198,7 +199,7 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
 #pragma unroll
               for (int kw = 0; kw < KS; ++kw) {
                 const int kb = (kh * KS + kw) * p.cin_blocks + cb;
-                const uint64_t ad = a_desc0 + static_cast<uint32_t>(kb * (kABytes >> 4));
+                const uint64_t ad = a_desc0 + static_cast<uint32_t>(kb * (kAKb >> 4));
                 const uint64_t bd = hd + static_cast<uint32_t>(kh * halo_row16 + kw * 8);
                 const uint32_t e_addr = tmem + kHaloMetaCol + 2 * kb;
 #pragma unroll
@@ -237,6 +238,9 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
     const int c16 = lane & 7;                        // row phase: 16-byte channel chunk
     const bool chunk_ok = c16 * 8 < p.F;
     const int bar_id = 1 + half;                     // named barrier of the half's 4 warps
+    // Neuron phase: this thread writes tile rows tcol0 + i (i < 32), all with
+    // bit 5 = lane/16, at byte (tcol0 + i)*128 + put_off.
+    const int put_off = (((ch >> 3) ^ ((lane >> 4) << 2)) << 4) + (ch & 7) * 2;
     pdl_wait();                                      // residual, output and state
 
     int it = 0;
@@ -291,7 +295,7 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
             for (int i = 0; i < 32; ++i) {
               const bool spike = neuron_step<MODE>(v[i], fmaf(acc[i], sx, bx), p.decay, p.tau,
                                                    p.v_th, p.v_reset);
-              *reinterpret_cast<__half*>(tile + tile64_off(tcol0 + i, ch >> 3) + (ch & 7) * 2) =
+              *reinterpret_cast<__half*>(tile + (tcol0 + i) * 128 + put_off) =
                   __ushort_as_half(spike ? 0x3C00 : 0);
             }
           }
