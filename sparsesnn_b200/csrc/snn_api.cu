@@ -299,10 +299,10 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
   p.n_m = g.Fpad / snn::kBM;
   p.box_bytes = tw * th * tn * snn::kKB * 2;
   // Timesteps per accumulator of the general kernel: all four (N = 256 MMAs,
-  // one accumulator) when every CTA owns a single 64-pixel tile and T is a
-  // multiple of 4, else two (double-buffered accumulators).
-  const int tc = (d->T % 4 == 0 && p.box_bytes == snn::kBBytes &&
-                  static_cast<long long>(p.n_px_tiles) * p.n_m <= g_num_sms) ? 4 : 2;
+  // one accumulator) for 64-pixel tiles when T is a multiple of 4 -- the
+  // wider MMAs win even though a CTA's next tile then waits for the
+  // epilogue to drain the accumulator -- else two (N = 128, double-buffered).
+  const int tc = (d->T % 4 == 0 && p.box_bytes == snn::kBBytes) ? 4 : 2;
   const cuuint32_t box5[5] = {static_cast<cuuint32_t>(snn::kKB), static_cast<cuuint32_t>(tw),
                               static_cast<cuuint32_t>(th), static_cast<cuuint32_t>(tn),
                               static_cast<cuuint32_t>(tc)};

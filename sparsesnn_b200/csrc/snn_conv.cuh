@@ -51,8 +51,10 @@ constexpr int kBarBytes = 512;
 //    chunk of timesteps overlaps the next chunk's MMAs); stages of two
 //    k-blocks, so each wait/commit pair of the MMA thread covers four MMAs;
 //  * TC = 4: one accumulator of 4 x 64 columns and N = 256 MMAs (one per
-//    k-block half for all four timesteps), for layers where each CTA owns a
-//    single pixel tile, so nothing would overlap a second buffer anyway.
+//    k-block half for all four timesteps).  A sparse MMA whose A, B and
+//    metadata all change costs about 120 cycles up to N = 128 but runs at
+//    its operand rate (160 cycles) at N = 256, so this wins even though the
+//    next tile's MMAs wait for the epilogue to drain the single accumulator.
 template <int TC>
 struct GenCfg {
   static constexpr int kTC = TC;
