@@ -68,6 +68,40 @@ def peaks():
     return 6650.0, 1590.0, "fallback"
 
 
+def spikformer_linear_layers(dev, stream, sparse_peak, iters=10):
+    """The Linear + BN + LIF twin at Spikformer-8-384 shapes (T=4, batch 32,
+    196 tokens: 6272 rows per timestep; q/k/v/proj 384->384, fc1 384->1536,
+    fc2 1536->384), random 2:4 weights and Bernoulli(0.2) spikes: per-layer
+    CUDA-event time and dense-equivalent TFLOP/s against the 2:4 ceiling."""
+    import numpy as np
+    import torch
+    from sparsesnn_b200.layer import SparseConvBNLIF
+    from sparsesnn_b200.pruning import prune_2_4_last
+    T, rows = 4, 32 * 196
+    out = {}
+    for name, cin, cout in (("qkv", 384, 384), ("fc1", 384, 1536), ("fc2", 1536, 384)):
+        rng = np.random.default_rng(0)
+        w = prune_2_4_last(rng.standard_normal((cout, cin)).astype(np.float32) * (2.0 / cin) ** 0.5)
+        layer = SparseConvBNLIF(w, np.ones(cout, np.float32), np.zeros(cout, np.float32),
+                                T=T, B=1, H=1, W=rows, device=dev)
+        x = (torch.rand((T, 1, rows, cin), device=dev) < 0.2).half()
+        y = torch.empty((T, 1, rows, cout), dtype=torch.float16, device=dev)
+        for _ in range(3):
+            layer(x, out=y)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(iters):
+            layer(x, out=y)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / iters
+        tflops = 2.0 * T * rows * cin * cout / (ms / 1000.0) / 1e12
+        out[name] = {"us": round(ms * 1000.0, 2), "tflops": round(tflops, 1),
+                     "frac": round(tflops / sparse_peak, 4), "rows": T * rows, "cin": cin, "cout": cout}
+    return out
+
+
 def cpu_reference_images_per_s(steps, sample, threads, warmup=1):
     """Time the oracle's port of the reference PyTorch forward on CPU."""
     import torch
@@ -269,6 +303,8 @@ def run_ours(args, rank, world, local_rank):
     if rt.device_error() != 0:
         raise RuntimeError("fused kernel reported a device error")
 
+    linear = spikformer_linear_layers(dev, stream, sparse_peak) if rank == 0 else None
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
@@ -297,6 +333,7 @@ def run_ours(args, rank, world, local_rank):
                                           "frac": alg_bytes / (conv_ms / 1000.0) / 1e9 / hbm_peak,
                                           "algorithmic_bytes_per_forward": alg_bytes}},
                 "layer_ms": {k: round(v, 4) for k, v in per_layer.items()},
+                "spikformer_linear": linear,
                 "clocks": dict(clk.summary(), window="timed region plus 300 replays before and 200 after"),
                 "cpu_baseline": cpu}
         print(json.dumps(line), flush=True)

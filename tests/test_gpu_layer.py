@@ -313,3 +313,27 @@ def test_m64_halo_path(cuda_device, T, residual):
         spk = ys - res_np if residual else ys
         v = np.transpose(state.cpu().numpy().reshape(B, H, W, F), (0, 3, 1, 2))
         check_spikes_and_v(spk, v, r["spikes"], r["h"], r["v"])
+
+
+@pytest.mark.parametrize("cin, cout", [(384, 1536), (1536, 384), (384, 384)],
+                         ids=["fc1", "fc2", "qkv"])
+def test_spikformer_linear_shapes(cuda_device, cin, cout):
+    """The Linear + BN + LIF twin at Spikformer-8-384 feature sizes (tokens of
+    4 images x 196 patches as rows; 2:4 along the input dim) against the
+    oracle run as a 1x1 conv over the rows."""
+    import torch
+    from sparsesnn_b200 import runtime as rt
+    from sparsesnn_b200.layer import SparseConvBNLIF, fold_bn
+    T, rows = 4, 4 * 196
+    x, w, bn = L.make_config0(seed=31 + cin, T=T, B=1, C=cin, F=cout, H=1, W=rows, k=1)
+    scale, bias = fold_bn(bn.gamma, bn.beta, bn.mean, bn.var)
+    layer = SparseConvBNLIF(w[:, :, 0, 0], scale, bias, T=T, B=1, H=1, W=rows)
+    xd = torch.from_numpy(to_nhwc(x)).to("cuda", torch.float16)
+    state = torch.zeros(layer.state_shape(), dtype=torch.float32, device="cuda")
+    y = layer(xd, state=state, read_state=False)
+    torch.cuda.synchronize()
+    assert rt.device_error() == 0
+    r = L.fused_layer(x, w, bn, stride=1, pad=0)
+    ys = from_nhwc(y.float().cpu().numpy(), T, 1)
+    v = np.transpose(state.cpu().numpy().reshape(1, 1, rows, cout), (0, 3, 1, 2))
+    check_spikes_and_v(ys, v, r["spikes"], r["h"], r["v"])
