@@ -19,7 +19,8 @@
  *   bn_scale, bn_bias [Cout]    fp32, epilogue computes acc*scale + bias
  *             (the reference keeps BN out of the weights,
  *             sengine/optimizer.py:160-183)
- *   residual  [T*B][OH][OW][Cout] fp16 (SEW ADD identity)
+ *   residual  [T*B][OH][OW][Cout] fp16 (SEW ADD identity, or the
+ *             real-valued skip input of an Add that precedes the neuron)
  *   weight    packed 2:4 blob produced by snn_pack_weight_24
  */
 #ifndef SNN_B200_H
@@ -32,7 +33,7 @@
 extern "C" {
 #endif
 
-#define SNN_ABI_VERSION 1
+#define SNN_ABI_VERSION 2
 
 enum {
   SNN_OK = 0,
@@ -49,13 +50,29 @@ enum { SNN_FLAG_READ_STATE = 1, SNN_FLAG_WRITE_STATE = 2,
         * tiles) even where the halo kernel applies; for testing. */
        SNN_FLAG_FORCE_GENERIC = 4 };
 
-/* One fused layer.  Linear layers are 1x1 convs over H=1, W=rows, B=1. */
+/* Where the residual of a fused Add enters the epilogue (the reference's
+ * pattern strings and templates, sengine/kernels/interleaved_templates.py:371-397):
+ *   ADD_AFTER   "Conv2d+LIF+Add": out = spike + residual (SEW ADD,
+ *               conv1x1_bn_if_add, :230-288);
+ *   ADD_BEFORE  "Conv2d+Add+LIF": the neuron integrates bn + residual
+ *               (conv1x1_bn_add_lif, :163-221);
+ *   TWO_NEURON  "Conv2d+IF+Add+LIF": s1 = neuron(bn); out = neuron2(s1 +
+ *               residual), two membranes (conv1x1_bn_if_add_lif, :297-364);
+ *               only through snn_conv_forward_res2. */
+enum { SNN_RES_ADD_AFTER = 0, SNN_RES_ADD_BEFORE = 1, SNN_RES_TWO_NEURON = 2 };
+
+/* One fused layer.  Linear layers are 1x1 convs over H=1, W=rows, B=1.
+ * The fields after v_reset only matter for the residual entry points; a
+ * zero-initialised tail selects the SEW ADD. */
 typedef struct snn_conv_desc {
   int32_t T, B, Cin, H, W;
   int32_t Cout, KH, KW, stride, pad;
-  int32_t neuron;            /* SNN_NEURON_* */
+  int32_t neuron;            /* SNN_NEURON_* (the first neuron) */
   int32_t flags;             /* SNN_FLAG_* */
   float tau, v_threshold, v_reset;
+  int32_t res_mode;          /* SNN_RES_* */
+  int32_t neuron2;           /* TWO_NEURON: SNN_NEURON_LIF or SNN_NEURON_IF */
+  float tau2, v_threshold2, v_reset2;
 } snn_conv_desc;
 
 /* Library ABI version (SNN_ABI_VERSION). */
@@ -69,7 +86,8 @@ int snn_init(void);
 
 /* Kernel variants behind snn_conv_forward (all fused and numerically
  * equivalent up to fp32 accumulation order):
- *   GENERIC        streamed weights, one activation tile per filter tap;
+ *   GENERIC        streamed weights, one activation tile per filter tap
+ *                  (also every ADD_BEFORE / TWO_NEURON residual layer);
  *   HALO_RESIDENT  stride-1 3x3, weights resident in shared memory, one
  *                  input halo per (timestep, 64-channel slice) shared by all taps;
  *   HALO_STREAM    stride-1 3x3 on images >= 8x8, T <= 4, streamed weights
@@ -102,13 +120,25 @@ int snn_conv_forward(const snn_conv_desc* d, const void* data, const void* weigh
                      float* state, const float* bn_scale, const float* bn_bias,
                      void* out, void* stream);
 
-/* Same with the SEW residual: out = spike + residual (the "LIF then Add"
- * epilogue of sengine/kernels/interleaved_templates.py:230-288, with LIF
- * decay, which the reference executor cannot dispatch: it passes at most 6
- * arguments, sengine/csrc/cpp_executor.cu:895-914). */
+/* Same with a residual: d->res_mode SNN_RES_ADD_AFTER gives the SEW
+ * out = spike + residual (the "LIF then Add" epilogue of
+ * sengine/kernels/interleaved_templates.py:230-288, with LIF decay);
+ * SNN_RES_ADD_BEFORE feeds bn + residual to the neuron (:163-221, with LIF
+ * decay where the neuron is a LIF).  The reference executor cannot dispatch
+ * either: it passes at most 6 arguments, sengine/csrc/cpp_executor.cu:895-914. */
 int snn_conv_forward_res(const snn_conv_desc* d, const void* data, const void* weight,
                          float* state, const float* bn_scale, const float* bn_bias,
                          const void* residual, void* out, void* stream);
+
+/* Two neurons around the Add (d->res_mode == SNN_RES_TWO_NEURON): s1 =
+ * neuron(bn) with membrane `state`, out = neuron2(s1 + residual) with
+ * membrane `state2` (same flags), fp16 spikes.  Argument order of the
+ * reference template conv1x1_bn_if_add_lif (data, weight, state1, state2,
+ * bn_scale, bn_bias, residual, output; interleaved_templates.py:297-364). */
+int snn_conv_forward_res2(const snn_conv_desc* d, const void* data, const void* weight,
+                          float* state, float* state2, const float* bn_scale,
+                          const float* bn_bias, const void* residual, void* out,
+                          void* stream);
 
 /* Dense direct-conv stem + BN + neuron (the Cin=3 first layer, which the
  * reference keeps dense: sengine/graph_slicer.py:106 skips Cin<4 and the

@@ -15,6 +15,14 @@ Restates the reference PyTorch path for one layer:
   ``v = (1-spike)*v + spike*v_reset``.
 * ``MultiStepIFNeuron``: ``v = v + x`` then the same fire/reset.
 * SEW ``ADD`` connect: ``out = spike + identity`` (``models/sewresnet.py:50-66``).
+* The other residual epilogues of the reference's fused templates
+  (``sengine/kernels/interleaved_templates.py``): Add before the neuron,
+  ``neuron(bn + residual)`` (``conv1x1_bn_add_lif``, ``:163-221``), and two
+  neurons around the Add, ``neuron2(neuron(bn) + residual)``
+  (``conv1x1_bn_if_add_lif``, ``:297-364``).  Each neuron follows the
+  module semantics above (LIF with its decay, IF without); the reference
+  templates integrate without decay in both places (their ``TODO: add LIF
+  decay``, ``:378-381``), which is the IF case here.
 
 The conv is an im2col matrix product accumulated in float64 and rounded to
 float32 once, which is at least as accurate as the reference's float32 conv.
@@ -104,20 +112,41 @@ def multistep_lif(x_seq: np.ndarray, tau: float = 2.0, v_th: float = 1.0,
 def fused_layer(x_seq: np.ndarray, w: np.ndarray, bn: BNParams, *, stride: int = 1,
                 pad: int | None = None, tau: float = 2.0, v_th: float = 1.0,
                 v_reset: float = 0.0, residual: np.ndarray | None = None,
-                neuron: str = "lif", v0: np.ndarray | None = None):
+                neuron: str = "lif", v0: np.ndarray | None = None,
+                res_mode: str = "add_after", neuron2: str = "lif", tau2: float = 2.0,
+                v_th2: float = 1.0, v_reset2: float = 0.0, v0_2: np.ndarray | None = None):
     """One fused layer over ``x_seq [T,B,C,H,W]``.
 
     Returns dict with ``out`` (spikes, plus ``residual`` when given),
     ``spikes``, ``h`` (pre-reset membrane per step), ``v`` (final membrane
     ``[B,F,OH,OW]``) and ``bn_out`` (BN output per step, the neuron input).
+    ``res_mode`` places the residual: ``add_after`` (SEW, ``out = spike +
+    residual``), ``add_before`` (the neuron integrates ``bn + residual``) or
+    ``two_neuron`` (``out = neuron2(spike + residual)``; adds ``spikes2``,
+    ``h2`` and ``v2``, and ``spikes``/``h``/``v`` stay the first neuron's).
     """
     t, b = x_seq.shape[:2]
     if pad is None:
         pad = w.shape[2] // 2
     y = conv2d_nchw(x_seq.reshape((t * b,) + x_seq.shape[2:]), w, stride, pad)
     z = batchnorm_eval(y, bn).reshape((t, b) + y.shape[1:])
-    spikes, h, v = multistep_lif(z, tau, v_th, v_reset, v0=v0, neuron=neuron)
-    out = spikes if residual is None else (spikes + residual.astype(np.float32))
+    if residual is not None and res_mode == "add_before":
+        x_in = (z + residual.astype(np.float32)).astype(np.float32)
+    else:
+        x_in = z
+    spikes, h, v = multistep_lif(x_in, tau, v_th, v_reset, v0=v0, neuron=neuron)
+    if residual is None:
+        return {"out": spikes, "spikes": spikes, "h": h, "v": v, "bn_out": z}
+    if res_mode == "add_before":
+        return {"out": spikes, "spikes": spikes, "h": h, "v": v, "bn_out": z}
+    if res_mode == "two_neuron":
+        x2 = (spikes + residual.astype(np.float32)).astype(np.float32)
+        s2, h2, v2 = multistep_lif(x2, tau2, v_th2, v_reset2, v0=v0_2, neuron=neuron2)
+        return {"out": s2, "spikes": spikes, "h": h, "v": v, "bn_out": z,
+                "spikes2": s2, "h2": h2, "v2": v2}
+    if res_mode != "add_after":
+        raise ValueError(f"unknown res_mode {res_mode!r}")
+    out = spikes + residual.astype(np.float32)
     return {"out": out, "spikes": spikes, "h": h, "v": v, "bn_out": z}
 
 

@@ -41,22 +41,28 @@ int g_init_status = SNN_E_NO_DEVICE;
 
 using ConvKernel = void (*)(const snn::ConvParams);
 
+template <int MODE, int TC>
+ConvKernel conv_kernel_fn_rm(int rm) {
+  switch (rm) {
+    case snn::kResAddAfter: return snn::fused_sparse_conv_lif_kernel<MODE, snn::kResAddAfter, TC>;
+    case snn::kResAddBefore: return snn::fused_sparse_conv_lif_kernel<MODE, snn::kResAddBefore, TC>;
+    case snn::kResTwoNeuron: return snn::fused_sparse_conv_lif_kernel<MODE, snn::kResTwoNeuron, TC>;
+    default: return snn::fused_sparse_conv_lif_kernel<MODE, snn::kResNone, TC>;
+  }
+}
 template <int TC>
-ConvKernel conv_kernel_fn_tc(int mode, bool res) {
-  switch (mode * 2 + (res ? 1 : 0)) {
-    case 0: return snn::fused_sparse_conv_lif_kernel<snn::kModeLifHalf, false, TC>;
-    case 1: return snn::fused_sparse_conv_lif_kernel<snn::kModeLifHalf, true, TC>;
-    case 2: return snn::fused_sparse_conv_lif_kernel<snn::kModeLifDiv, false, TC>;
-    case 3: return snn::fused_sparse_conv_lif_kernel<snn::kModeLifDiv, true, TC>;
-    case 4: return snn::fused_sparse_conv_lif_kernel<snn::kModeIf, false, TC>;
-    case 5: return snn::fused_sparse_conv_lif_kernel<snn::kModeIf, true, TC>;
-    default: return snn::fused_sparse_conv_lif_kernel<snn::kModeNone, false, TC>;
+ConvKernel conv_kernel_fn_tc(int mode, int rm) {
+  switch (mode) {
+    case snn::kModeLifHalf: return conv_kernel_fn_rm<snn::kModeLifHalf, TC>(rm);
+    case snn::kModeLifDiv: return conv_kernel_fn_rm<snn::kModeLifDiv, TC>(rm);
+    case snn::kModeIf: return conv_kernel_fn_rm<snn::kModeIf, TC>(rm);
+    default: return snn::fused_sparse_conv_lif_kernel<snn::kModeNone, snn::kResNone, TC>;
   }
 }
 
-// tc = timesteps per accumulator (2 or 4, see snn::GenCfg).
-ConvKernel conv_kernel_fn(int mode, bool res, int tc) {
-  return tc == 4 ? conv_kernel_fn_tc<4>(mode, res) : conv_kernel_fn_tc<2>(mode, res);
+// tc = timesteps per accumulator (2 or 4, see snn::GenCfg); rm = snn::ResMode.
+ConvKernel conv_kernel_fn(int mode, int rm, int tc) {
+  return tc == 4 ? conv_kernel_fn_tc<4>(mode, rm) : conv_kernel_fn_tc<2>(mode, rm);
 }
 
 using HaloKernel = void (*)(const snn::HaloParams);
@@ -154,11 +160,14 @@ int ensure_init() {
   for (int mode = 0; mode < 4; ++mode) {
     for (int res = 0; res < (mode == snn::kModeNone ? 1 : 2); ++res) {
       for (int tc : {2, 4}) {
-        e = cudaFuncSetAttribute(conv_kernel_fn(mode, res != 0, tc),
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 tc == 4 ? snn::GenCfg<4>::kSmemBytes : snn::GenCfg<2>::kSmemBytes);
-        if (e != cudaSuccess)
-          return g_init_status = fail(SNN_E_CUDA, "smem attribute: %s", cudaGetErrorString(e));
+        // res == 1 covers every residual epilogue of the general kernel.
+        for (int rm = res; rm <= (res ? snn::kResTwoNeuron : 0); ++rm) {
+          e = cudaFuncSetAttribute(conv_kernel_fn(mode, rm, tc),
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   tc == 4 ? snn::GenCfg<4>::kSmemBytes : snn::GenCfg<2>::kSmemBytes);
+          if (e != cudaSuccess)
+            return g_init_status = fail(SNN_E_CUDA, "smem attribute: %s", cudaGetErrorString(e));
+        }
       }
       for (int v = 0; v < 3; ++v) {
         e = cudaFuncSetAttribute(halo_kernel_fn(v ? 128 : 64, v == 2, mode, res != 0),
@@ -247,6 +256,8 @@ int general_tile_px(const Geometry& g) {
 
 int select_variant(const snn_conv_desc* d, const Geometry& g) {
   if (d->flags & SNN_FLAG_FORCE_GENERIC) return SNN_VARIANT_GENERIC;
+  // Only the general kernel has the Add-before-neuron and two-neuron epilogues.
+  if (d->res_mode != SNN_RES_ADD_AFTER) return SNN_VARIANT_GENERIC;
   const bool s1_3x3 = d->stride == 1 && d->KH == 3 && d->KW == 3 && d->pad == 1;
   if (!s1_3x3) return SNN_VARIANT_GENERIC;
   const int a_bytes = g.n_kb * snn::kABytes;
@@ -259,9 +270,10 @@ int select_variant(const snn_conv_desc* d, const Geometry& g) {
   return SNN_VARIANT_GENERIC;
 }
 
+// rm: snn::ResMode of the call (kResNone when residual is null).
 int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, float* state,
-                const float* scale, const float* bias, const void* residual, void* out,
-                void* stream) {
+                float* state2, const float* scale, const float* bias, const void* residual,
+                int rm, void* out, void* stream) {
   int st = ensure_init();
   if (st) return st;
   Geometry g;
@@ -271,6 +283,14 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
     return fail(SNN_E_INVALID, "state flags set but state is null");
   if (d->neuron == SNN_NEURON_NONE && residual)
     return fail(SNN_E_INVALID, "residual needs a neuron");
+  if (rm == snn::kResTwoNeuron) {
+    if ((d->flags & (SNN_FLAG_READ_STATE | SNN_FLAG_WRITE_STATE)) && !state2)
+      return fail(SNN_E_INVALID, "state flags set but state2 is null");
+    if (d->neuron2 != SNN_NEURON_LIF && d->neuron2 != SNN_NEURON_IF)
+      return fail(SNN_E_INVALID, "neuron2 must be LIF or IF");
+    if (d->neuron2 == SNN_NEURON_LIF && !(d->tau2 > 0.0f))
+      return fail(SNN_E_INVALID, "tau2 must be positive");
+  }
   if ((reinterpret_cast<uintptr_t>(data) | reinterpret_cast<uintptr_t>(weight) |
        reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(residual)) & 15)
     return fail(SNN_E_INVALID, "data, weight, out and residual must be 16-byte aligned");
@@ -332,7 +352,7 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
   else p.out_f32 = static_cast<float*>(out);
   p.residual = static_cast<const __half*>(residual);
   p.meta = reinterpret_cast<const uint32_t*>(wbytes + meta_offset(g));
-  p.scale = scale; p.bias = bias; p.state = state;
+  p.scale = scale; p.bias = bias; p.state = state; p.state2 = state2;
   unsigned* err = nullptr;
   if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_device_err) != cudaSuccess)
     return fail(SNN_E_CUDA, "error word address");
@@ -347,6 +367,12 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
                 ? static_cast<float>(1.0 - 1.0 / static_cast<double>(d->tau)) : 1.0f;
   p.inv_tau = 0.0f;
   p.v_th = d->v_threshold; p.v_reset = d->v_reset;
+  if (rm == snn::kResTwoNeuron) {
+    p.n2_lif = d->neuron2 == SNN_NEURON_LIF;
+    p.tau2 = p.n2_lif ? d->tau2 : 1.0f;
+    p.decay2 = p.n2_lif ? static_cast<float>(1.0 - 1.0 / static_cast<double>(d->tau2)) : 1.0f;
+    p.v_th2 = d->v_threshold2; p.v_reset2 = d->v_reset2;
+  }
   p.timeout_ns = 4000000000ull;   // SM cycles (~2 s at the highest clock)
   const int mode = d->neuron == SNN_NEURON_NONE ? snn::kModeNone
                    : d->neuron == SNN_NEURON_IF ? snn::kModeIf
@@ -433,7 +459,7 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
   const int per_m = std::max(1, std::min(p.n_px_tiles, g_num_sms / p.n_m));
   const long long grid = static_cast<long long>(per_m) * p.n_m;
   if (grid > 0x7fffffffLL) return fail(SNN_E_INVALID, "grid too large");
-  cudaError_t e = launch_pdl(conv_kernel_fn(mode, residual != nullptr, tc),
+  cudaError_t e = launch_pdl(conv_kernel_fn(mode, rm, tc),
                              dim3(static_cast<unsigned>(grid)), dim3(snn::kThreads),
                              tc == 4 ? snn::GenCfg<4>::kSmemBytes : snn::GenCfg<2>::kSmemBytes,
                              stream, p);
@@ -544,14 +570,32 @@ int snn_pack_weight_24(const snn_conv_desc* d, const float* w, void* blob) {
 
 int snn_conv_forward(const snn_conv_desc* d, const void* data, const void* weight, float* state,
                      const float* bn_scale, const float* bn_bias, void* out, void* stream) {
-  return launch_conv(d, data, weight, state, bn_scale, bn_bias, nullptr, out, stream);
+  return launch_conv(d, data, weight, state, nullptr, bn_scale, bn_bias, nullptr, snn::kResNone,
+                     out, stream);
 }
 
 int snn_conv_forward_res(const snn_conv_desc* d, const void* data, const void* weight,
                          float* state, const float* bn_scale, const float* bn_bias,
                          const void* residual, void* out, void* stream) {
+  if (!d) return fail(SNN_E_INVALID, "null descriptor");
   if (!residual) return fail(SNN_E_INVALID, "null residual");
-  return launch_conv(d, data, weight, state, bn_scale, bn_bias, residual, out, stream);
+  if (d->res_mode != SNN_RES_ADD_AFTER && d->res_mode != SNN_RES_ADD_BEFORE)
+    return fail(SNN_E_INVALID, "snn_conv_forward_res takes res_mode ADD_AFTER or ADD_BEFORE");
+  return launch_conv(d, data, weight, state, nullptr, bn_scale, bn_bias, residual,
+                     d->res_mode == SNN_RES_ADD_BEFORE ? snn::kResAddBefore : snn::kResAddAfter,
+                     out, stream);
+}
+
+int snn_conv_forward_res2(const snn_conv_desc* d, const void* data, const void* weight,
+                          float* state, float* state2, const float* bn_scale,
+                          const float* bn_bias, const void* residual, void* out,
+                          void* stream) {
+  if (!d) return fail(SNN_E_INVALID, "null descriptor");
+  if (!residual) return fail(SNN_E_INVALID, "null residual");
+  if (d->res_mode != SNN_RES_TWO_NEURON)
+    return fail(SNN_E_INVALID, "snn_conv_forward_res2 takes res_mode TWO_NEURON");
+  return launch_conv(d, data, weight, state, state2, bn_scale, bn_bias, residual,
+                     snn::kResTwoNeuron, out, stream);
 }
 
 int snn_stem_forward(const snn_conv_desc* d, int32_t Tin, const float* x, const float* w,

@@ -89,6 +89,15 @@ __device__ __forceinline__ bool neuron_step(float& v, float x2, float decay, flo
   v = spike ? v_reset : h;
   return spike;
 }
+// Second neuron of the kResTwoNeuron epilogue (LIF with general tau, or IF;
+// for tau = 2 the LIF form gives the same bits as the folded one).
+__device__ __forceinline__ bool neuron2_step(float& v, float x, bool lif, float decay, float tau,
+                                             float v_th, float v_reset) {
+  const float h = lif ? __fadd_rn(__fmul_rn(v, decay), __fdiv_rn(x, tau)) : __fadd_rn(v, x);
+  const bool spike = h >= v_th;
+  v = spike ? v_reset : h;
+  return spike;
+}
 // ------------------------------------------------------ epilogue store stage
 // An epilogue warp owns 32 output channels (one per TMEM lane) x 32 pixel
 // columns.  The neuron loop writes the warp's spikes column by column into a
@@ -105,6 +114,17 @@ __device__ __forceinline__ int xpose_off(int px, int c8) {
 __device__ __forceinline__ void xpose_put(uint8_t* xb, int i, int lane, bool spike) {
   *reinterpret_cast<__half*>(xb + xpose_off(i, lane >> 3) + (lane & 7) * 2) =
       __ushort_as_half(spike ? 0x3C00 : 0);
+}
+// Residual of this lane's channel at column i, from a transpose tile that
+// holds the residual rows in store layout (the same place xpose_put writes).
+__device__ __forceinline__ float xpose_get(const uint8_t* xb, int i, int lane) {
+  return __half2float(*reinterpret_cast<const __half*>(xb + xpose_off(i, lane >> 3) + (lane & 7) * 2));
+}
+// Residual rows (store layout, see load_residual_rows) into the tile.
+__device__ __forceinline__ void xpose_put_rows(uint8_t* xb, int lane, const uint4 (&r4)[4]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    *reinterpret_cast<uint4*>(xb + xpose_off(8 * j + (lane >> 2), lane & 3)) = r4[j];
 }
 // Pixels this lane stores (columns 8j + lane/4), from each lane's pixel of
 // column `lane` (-1 = outside the output).
@@ -143,6 +163,10 @@ __device__ __forceinline__ void store_xpose_rows(__half* out, const uint8_t* xb,
 }
 
 enum ConvFlags : int { kReadState = 1, kWriteState = 2 };
+// Residual epilogues of the general kernel (template parameter RM): none;
+// out = spike + residual (SEW ADD); the neuron integrates bn + residual;
+// two neurons, out = neuron2(neuron(bn) + residual).
+enum ResMode : int { kResNone = 0, kResAddAfter = 1, kResAddBefore = 2, kResTwoNeuron = 3 };
 enum ErrCode : unsigned { kErrTimeoutFull = 1u, kErrTimeoutEmpty = 2u, kErrTimeoutAcc = 4u,
                           kErrTimeoutMeta = 8u, kErrTimeoutAccEmpty = 16u, kErrTimeoutDrain = 32u,
                           kErrTimeoutRes = 64u };
@@ -154,6 +178,7 @@ struct ConvParams {
   const float* scale;        // [F]
   const float* bias;         // [F]
   float* state;              // [B*OH*OW][F] or null
+  float* state2;             // second membrane (kResTwoNeuron), same layout
   __half* out;               // [T*B*OH*OW][F] fp16 spikes (+ residual)
   const __half* residual;    // [T*B*OH*OW][F] fp16 or null
   float* out_f32;            // [T*B*OH*OW][F] (neuron == kNoNeuron only)
@@ -166,6 +191,8 @@ struct ConvParams {
   int box_bytes;             // bytes of one activation TMA box (tw*th*tn*128)
   int flags;
   float decay, tau, inv_tau, v_th, v_reset;
+  int n2_lif;                // kResTwoNeuron: second neuron is a LIF (else IF)
+  float decay2, tau2, v_th2, v_reset2;
   unsigned long long timeout_ns;   // bounded-wait budget, in SM clock cycles
 };
 
@@ -183,9 +210,11 @@ __device__ __forceinline__ TileCoord tile_coord(const ConvParams& p, int pt) {
   return c;
 }
 
-template <int MODE, bool RES, int TC>
+template <int MODE, int RM, int TC>
 __global__ void __launch_bounds__(kThreads, 1)
 fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
+  constexpr bool RES = RM != kResNone;
+  static_assert(MODE != kModeNone || RM == kResNone, "a residual epilogue needs a neuron");
   using Cfg = GenCfg<TC>;
   constexpr int kTC = Cfg::kTC, kNumAcc = Cfg::kNumAcc, kStages = Cfg::kStages;
   constexpr int kKbPerStage = Cfg::kKbPerStage, kStageBytes = Cfg::kStageBytes;
@@ -405,11 +434,14 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
       int rows[4];
       store_rows(my_px, lane, rows);
       float v[32];
+      float v2[RM == kResTwoNeuron ? 32 : 1];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         const int px = __shfl_sync(0xffffffffu, my_px, i);
-        v[i] = ((p.flags & kReadState) && cvalid && px >= 0)
-                   ? p.state[static_cast<size_t>(px) * p.F + cout] : 0.f;
+        const bool rd = (p.flags & kReadState) && cvalid && px >= 0;
+        v[i] = rd ? p.state[static_cast<size_t>(px) * p.F + cout] : 0.f;
+        if constexpr (RM == kResTwoNeuron)
+          v2[i] = rd ? p.state2[static_cast<size_t>(px) * p.F + cout] : 0.f;
       }
       for (int c = 0; c < n_chunks && !stop; ++c) {
         const int t0 = c * kTC;
@@ -466,12 +498,33 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
               // Neuron update, lane = output channel, i = pixel column.
               const float sx = MODE == kModeLifHalf ? sc * 0.5f : sc;
               const float bx = MODE == kModeLifHalf ? bi * 0.5f : bi;
+              if constexpr (RM == kResAddBefore || RM == kResTwoNeuron) {
+                // The residual enters the neuron: its rows go through the
+                // transpose tile, each lane reads its channel per column and
+                // the spike overwrites that same half.
+                xpose_put_rows(xb, lane, r4[u]);
+                __syncwarp();
+              }
 #pragma unroll
-              for (int i = 0; i < 32; ++i)
-                xpose_put(xb, i, lane, neuron_step<MODE>(v[i], fmaf(__uint_as_float(accr[u][i]), sx, bx),
-                                                         p.decay, p.tau, p.v_th, p.v_reset));
+              for (int i = 0; i < 32; ++i) {
+                float x = fmaf(__uint_as_float(accr[u][i]), sx, bx);
+                if constexpr (RM == kResAddBefore) {
+                  // kModeLifHalf: x is bn/2, and bn/2 + r/2 rounds to exactly
+                  // (bn + r)/2, the folded form of the neuron's input.
+                  const float r = xpose_get(xb, i, lane);
+                  x = __fadd_rn(x, MODE == kModeLifHalf ? r * 0.5f : r);
+                }
+                bool spike = neuron_step<MODE>(v[i], x, p.decay, p.tau, p.v_th, p.v_reset);
+                if constexpr (RM == kResTwoNeuron) {
+                  const float x2 = __fadd_rn(spike ? 1.f : 0.f, xpose_get(xb, i, lane));
+                  spike = neuron2_step(v2[i], x2, p.n2_lif != 0, p.decay2, p.tau2, p.v_th2,
+                                       p.v_reset2);
+                }
+                xpose_put(xb, i, lane, spike);
+              }
               __syncwarp();
-              store_xpose_rows<RES>(p.out, xb, tbase, rows, p.F, cbase, lane, chunk_ok, r4[u]);
+              store_xpose_rows<RM == kResAddAfter>(p.out, xb, tbase, rows, p.F, cbase, lane, chunk_ok,
+                                                   r4[u]);
               __syncwarp();
             }
           }
@@ -482,7 +535,10 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const int px = __shfl_sync(0xffffffffu, my_px, i);
-          if (cvalid && px >= 0) p.state[static_cast<size_t>(px) * p.F + cout] = v[i];
+          if (cvalid && px >= 0) {
+            p.state[static_cast<size_t>(px) * p.F + cout] = v[i];
+            if constexpr (RM == kResTwoNeuron) p.state2[static_cast<size_t>(px) * p.F + cout] = v2[i];
+          }
         }
       }
     }

@@ -36,11 +36,19 @@ def _np(x):
 
 
 class SparseConvBNLIF:
-    """One fused 2:4-sparse Conv(+Linear) + BN + LIF/IF layer over T steps."""
+    """One fused 2:4-sparse Conv(+Linear) + BN + LIF/IF layer over T steps.
+
+    ``res_mode`` says where a residual passed to ``__call__`` enters:
+    ``"add_after"`` (SEW ADD, ``out = spike + residual``), ``"add_before"``
+    (the neuron integrates ``bn + residual``) or ``"two_neuron"`` (``out =
+    neuron2(spike + residual)``, second membrane ``state2``; ``neuron2``,
+    ``tau2``, ``v_threshold2``, ``v_reset2`` describe that neuron).
+    """
 
     def __init__(self, weight, bn_scale, bn_bias, *, T, B, H, W, stride=1, pad=None,
                  neuron="lif", tau=2.0, v_threshold=1.0, v_reset=0.0, device="cuda",
-                 force_generic=False):
+                 force_generic=False, res_mode="add_after", neuron2="lif", tau2=2.0,
+                 v_threshold2=1.0, v_reset2=0.0):
         w = _np(weight).astype(np.float32)
         if w.ndim == 2:                       # Linear [out, in] -> 1x1 conv
             w = w[:, :, None, None]
@@ -48,7 +56,9 @@ class SparseConvBNLIF:
         self.desc = rt.make_desc(T=T, B=B, Cin=cin, H=H, W=W, Cout=cout, KH=kh, KW=kw,
                                  stride=stride, pad=(kh // 2 if pad is None else pad),
                                  neuron=neuron, tau=tau, v_threshold=v_threshold,
-                                 v_reset=v_reset)
+                                 v_reset=v_reset, res_mode=res_mode, neuron2=neuron2,
+                                 tau2=tau2, v_threshold2=v_threshold2, v_reset2=v_reset2)
+        self.res_mode = res_mode
         self.OH, self.OW = rt.out_shape(self.desc)
         blob = rt.pack_weight_24(self.desc, w)
         self.device = torch.device(device)
@@ -67,11 +77,13 @@ class SparseConvBNLIF:
         return (self.B * self.OH * self.OW, self.Cout)
 
     def __call__(self, data, state=None, residual=None, out=None, *, read_state=None,
-                 write_state=None, stream=None):
+                 write_state=None, stream=None, state2=None):
         """Run the layer; returns ``out``.
 
         ``state`` (optional) is the membrane buffer: read at start unless
         ``read_state=False`` and final v written unless ``write_state=False``.
+        ``state2`` is the second neuron's membrane (``res_mode="two_neuron"``,
+        same shape and flags as ``state``).
         """
         if data.dtype != torch.float16 or not data.is_contiguous():
             raise ValueError("data must be contiguous fp16 (T*B, H, W, Cin)")
@@ -91,9 +103,24 @@ class SparseConvBNLIF:
         s = stream if stream is not None else torch.cuda.current_stream(data.device).cuda_stream
         lib = rt.load()
         sp = state.data_ptr() if state is not None else None
+        if self.res_mode == "two_neuron":
+            if residual is None:
+                raise ValueError("res_mode two_neuron needs a residual")
+            if (state is None) != (state2 is None):
+                raise ValueError("two_neuron takes both membranes or neither")
+            if state2 is not None and (tuple(state2.shape) != self.state_shape()
+                                       or state2.dtype != torch.float32):
+                raise ValueError("state2 must be fp32 (B*OH*OW, Cout)")
         if residual is not None:
             if residual.dtype != torch.float16 or tuple(residual.shape) != self.out_shape():
                 raise ValueError("residual must be fp16 (T*B, OH, OW, Cout)")
+        if self.res_mode == "two_neuron":
+            rt.check(lib.snn_conv_forward_res2(
+                self.desc, data.data_ptr(), self.weight_blob.data_ptr(), sp,
+                state2.data_ptr() if state2 is not None else None,
+                self.bn_scale.data_ptr(), self.bn_bias.data_ptr(), residual.data_ptr(),
+                out.data_ptr(), s))
+        elif residual is not None:
             rt.check(lib.snn_conv_forward_res(
                 self.desc, data.data_ptr(), self.weight_blob.data_ptr(), sp,
                 self.bn_scale.data_ptr(), self.bn_bias.data_ptr(), residual.data_ptr(),

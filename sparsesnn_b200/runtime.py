@@ -27,13 +27,17 @@ SNN_FLAG_FORCE_GENERIC = 4
 SNN_VARIANT_GENERIC = 0
 SNN_VARIANT_HALO_RESIDENT = 1
 SNN_VARIANT_HALO_STREAM = 2
+SNN_RES_ADD_AFTER = 0
+SNN_RES_ADD_BEFORE = 1
+SNN_RES_TWO_NEURON = 2
 
 NEURONS = {"lif": SNN_NEURON_LIF, "if": SNN_NEURON_IF, "none": SNN_NEURON_NONE}
 
 # Every symbol include/snn_b200.h declares.
 EXPORTED = (
     "snn_abi_version", "snn_init", "snn_conv_variant", "snn_conv_out_shape", "snn_conv_weight_bytes",
-    "snn_pack_weight_24", "snn_conv_forward", "snn_conv_forward_res", "snn_stem_forward",
+    "snn_pack_weight_24", "snn_conv_forward", "snn_conv_forward_res", "snn_conv_forward_res2",
+    "snn_stem_forward",
     "snn_head_forward", "snn_get_device_error", "snn_last_error_message",
 )
 
@@ -45,6 +49,8 @@ class SnnConvDesc(ctypes.Structure):
         ("KH", ctypes.c_int32), ("KW", ctypes.c_int32), ("stride", ctypes.c_int32),
         ("pad", ctypes.c_int32), ("neuron", ctypes.c_int32), ("flags", ctypes.c_int32),
         ("tau", ctypes.c_float), ("v_threshold", ctypes.c_float), ("v_reset", ctypes.c_float),
+        ("res_mode", ctypes.c_int32), ("neuron2", ctypes.c_int32),
+        ("tau2", ctypes.c_float), ("v_threshold2", ctypes.c_float), ("v_reset2", ctypes.c_float),
     ]
 
 
@@ -71,6 +77,7 @@ def _declare(lib):
         "snn_pack_weight_24": ([D, P, P], ctypes.c_int),
         "snn_conv_forward": ([D, P, P, P, P, P, P, P], ctypes.c_int),
         "snn_conv_forward_res": ([D, P, P, P, P, P, P, P, P], ctypes.c_int),
+        "snn_conv_forward_res2": ([D, P, P, P, P, P, P, P, P, P], ctypes.c_int),
         "snn_stem_forward": ([D, i32, P, P, P, P, P, P], ctypes.c_int),
         "snn_head_forward": ([i32, i32, i32, i32, i32, P, P, P, P, P], ctypes.c_int),
         "snn_get_device_error": ([ctypes.POINTER(ctypes.c_uint32), ctypes.c_int], ctypes.c_int),
@@ -104,12 +111,18 @@ def check(rc: int) -> None:
         raise SnnError(rc, msg.decode() if msg else "")
 
 
+RES_MODES = {"add_after": SNN_RES_ADD_AFTER, "add_before": SNN_RES_ADD_BEFORE,
+             "two_neuron": SNN_RES_TWO_NEURON}
+
+
 def make_desc(*, T, B, Cin, H, W, Cout, KH, KW, stride=1, pad=None, neuron="lif",
-              flags=0, tau=2.0, v_threshold=1.0, v_reset=0.0) -> SnnConvDesc:
+              flags=0, tau=2.0, v_threshold=1.0, v_reset=0.0, res_mode="add_after",
+              neuron2="lif", tau2=2.0, v_threshold2=1.0, v_reset2=0.0) -> SnnConvDesc:
     if pad is None:
         pad = KH // 2
     return SnnConvDesc(T, B, Cin, H, W, Cout, KH, KW, stride, pad, NEURONS[neuron], flags,
-                       tau, v_threshold, v_reset)
+                       tau, v_threshold, v_reset, RES_MODES[res_mode], NEURONS[neuron2],
+                       tau2, v_threshold2, v_reset2)
 
 
 def variant(desc: SnnConvDesc) -> int:

@@ -10,6 +10,10 @@ if str(ROOT) not in sys.path:
     sys.path.insert(0, str(ROOT))
 
 LAYER_CASES = ["c3s1", "c3s2", "c1s2", "c3res", "c3f64", "c3if", "lin"]
+# Residual epilogues other than the SEW ADD (Add before the neuron; two
+# neurons around the Add).
+RES_CASES = ["c3addlif", "c1twon"]
+RES_MODES = {0: "add_after", 1: "add_before", 2: "two_neuron"}
 
 
 def pytest_configure(config):
@@ -20,7 +24,12 @@ def load_layer_case(name):
     g = dict(np.load(GOLDEN / f"layer_{name}.npz"))
     T, B, C, F, H, W, k, s, pad, islif, lin = (int(v) for v in g["meta"])
     g.update(T=T, B=B, C=C, F=F, H=H, W=W, k=k, stride=s, pad=pad,
-             neuron="lif" if islif else "if", linear=bool(lin))
+             neuron="lif" if islif else "if", linear=bool(lin), res_mode="add_after",
+             neuron2="lif")
+    if "res_meta" in g:
+        mode, lif2 = (int(v) for v in g["res_meta"])
+        g.update(res_mode=RES_MODES[mode], neuron2="lif" if lif2 else "if",
+                 residual=g["residual_f"])
     return g
 
 

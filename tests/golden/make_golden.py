@@ -115,6 +115,86 @@ def layer_case(ref, name, *, T, B, C, F, H, W, k, stride, pad, neuron="lif", x_m
     print("wrote", name, {k: v.shape for k, v in out.items()})
 
 
+def run_neuron(ref, kind, inp):
+    """Reference multi-step neuron (tau 2 / v_th 1 / v_reset 0) over ``inp``
+    ``(T, ...)``: spikes, pre-reset membrane per step and final membrane,
+    cross-checked against the unmodified multi-step module."""
+    import torch
+    mod = ref["MultiStepLIFNeuron"](tau=2.0, v_threshold=1.0, v_reset=0.0) \
+        if kind == "lif" else ref["MultiStepIFNeuron"](v_threshold=1.0, v_reset=0.0)
+    cell = mod.neuron
+    cell.reset()
+    spikes, hs = [], []
+    with torch.no_grad():
+        for t in range(inp.shape[0]):
+            if kind == "lif":
+                cell.neuronal_charge(inp[t])
+                hs.append(cell.v.clone())
+                s = cell.neuronal_fire()
+                cell.neuronal_reset(s)
+            else:
+                s = cell(inp[t])
+            spikes.append(s)
+        v_final = cell.v.clone()
+        ref_spk = mod(inp)
+    spikes = torch.stack(spikes)
+    assert torch.equal(spikes, ref_spk)
+    if kind != "lif":
+        v = torch.zeros_like(inp[0]); hs = []
+        for t in range(inp.shape[0]):
+            v = v + inp[t]; hs.append(v.clone())
+            sp = (v - 1.0).ge(0).float(); v = (1.0 - sp) * v + sp * 0.0
+    return spikes, torch.stack(hs), v_final
+
+
+def residual_case(ref, name, *, mode, neuron, neuron2="lif", T, B, C, F, H, W, k, seed):
+    """The reference's other residual epilogues, run through its modules:
+    ``mode="add_before"``: Conv -> BN -> Add(residual) -> neuron (pattern
+    ``Conv2d+Add+LIF``, ``sengine/kernels/interleaved_templates.py:163-221``);
+    ``mode="two_neuron"``: Conv -> BN -> neuron -> Add(residual) -> neuron2
+    (``Conv2d+IF+Add+LIF``, ``:297-364``).  The residual is a real-valued
+    fp16-representable tensor (an MS-ResNet style skip input)."""
+    import torch
+    import torch.nn as nn
+    pad = k // 2
+    g = torch.Generator().manual_seed(seed)
+    x = (torch.rand((T, B, C, H, W), generator=g) < 0.2).float()
+    std = (2.0 / (F * k * k)) ** 0.5
+    w = torch.randn((F, C, k, k), generator=g) * std
+    w = ref["prune_2_4"](w.permute(0, 2, 3, 1)).permute(0, 3, 1, 2).contiguous()
+    gamma = torch.rand(F, generator=g) + 0.5
+    beta = torch.randn(F, generator=g) * 0.1
+    mean = torch.randn(F, generator=g) * 0.1
+    var = torch.rand(F, generator=g) + 0.5
+    conv = nn.Conv2d(C, F, k, stride=1, padding=pad, bias=False)
+    conv.weight.data.copy_(w)
+    bnm = nn.BatchNorm2d(F)
+    bnm.weight.data.copy_(gamma); bnm.bias.data.copy_(beta)
+    bnm.running_mean.copy_(mean); bnm.running_var.copy_(var)
+    seq = ref["SeqToANNContainer"](conv, bnm).eval()
+    with torch.no_grad():
+        z = seq(x)
+    r = (torch.randn(z.shape, generator=g) * 0.5).half().float()
+    out = {"x": x.numpy().astype(np.uint8), "w": w.numpy(), "gamma": gamma.numpy(),
+           "beta": beta.numpy(), "mean": mean.numpy(), "var": var.numpy(), "bn_out": z.numpy(),
+           "residual_f": r.numpy(),
+           "meta": np.array([T, B, C, F, H, W, k, 1, pad, int(neuron == "lif"), 0], np.int64)}
+    if mode == "add_before":
+        spikes, h, v = run_neuron(ref, neuron, z + r)
+        out.update(spikes=spikes.numpy().astype(np.uint8), h=h.numpy(), v=v.numpy(),
+                   out=spikes.numpy().astype(np.uint8),
+                   res_meta=np.array([1, int(neuron2 == "lif")], np.int64))
+    else:
+        s1, h1, v1 = run_neuron(ref, neuron, z)
+        s2, h2, v2 = run_neuron(ref, neuron2, s1 + r)
+        out.update(spikes=s1.numpy().astype(np.uint8), h=h1.numpy(), v=v1.numpy(),
+                   spikes2=s2.numpy().astype(np.uint8), h2=h2.numpy(), v2=v2.numpy(),
+                   out=s2.numpy().astype(np.uint8),
+                   res_meta=np.array([2, int(neuron2 == "lif")], np.int64))
+    np.savez_compressed(HERE / f"layer_{name}.npz", **out)
+    print("wrote", name, {k: v.shape for k, v in out.items()})
+
+
 def prune_case(ref):
     import torch
     g = torch.Generator().manual_seed(7)
@@ -185,6 +265,10 @@ def main():
                seed=6)
     layer_case(ref, "lin", T=4, B=2, C=128, F=256, H=4, W=4, k=1, stride=1, pad=0, seed=8,
                linear=True)
+    residual_case(ref, "c3addlif", mode="add_before", neuron="lif", T=4, B=2, C=64, F=128,
+                  H=8, W=8, k=3, seed=9)
+    residual_case(ref, "c1twon", mode="two_neuron", neuron="if", neuron2="lif", T=4, B=2,
+                  C=128, F=64, H=8, W=8, k=1, seed=10)
     model_case(ref, HERE.parent.parent)
 
 

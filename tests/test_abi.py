@@ -34,11 +34,25 @@ def test_exports_every_declared_symbol(_lib):
 
 
 def test_abi_version(_lib):
-    assert _lib.snn_abi_version() == 1
+    assert _lib.snn_abi_version() == 2
 
 
 def test_desc_struct_layout():
-    assert ctypes.sizeof(rt.SnnConvDesc) == 15 * 4
+    assert ctypes.sizeof(rt.SnnConvDesc) == 20 * 4
+    assert rt.SnnConvDesc.res_mode.offset == 15 * 4
+
+
+def test_residual_entry_points_validate_mode(_lib):
+    """forward_res takes ADD_AFTER / ADD_BEFORE, forward_res2 only TWO_NEURON;
+    the checks come before any device work."""
+    d = rt.make_desc(T=4, B=2, Cin=64, H=8, W=8, Cout=128, KH=3, KW=3, res_mode="two_neuron")
+    rc = _lib.snn_conv_forward_res(d, 16, 16, None, 16, 16, 16, 16, None)
+    assert rc == rt.SNN_E_INVALID
+    d = rt.make_desc(T=4, B=2, Cin=64, H=8, W=8, Cout=128, KH=3, KW=3, res_mode="add_before")
+    rc = _lib.snn_conv_forward_res2(d, 16, 16, None, None, 16, 16, 16, 16, None)
+    assert rc == rt.SNN_E_INVALID
+    rc = _lib.snn_conv_forward_res2(d, 16, 16, None, None, 16, 16, None, 16, None)
+    assert rc == rt.SNN_E_INVALID
 
 
 @pytest.mark.parametrize("kw, msg", [
@@ -86,6 +100,9 @@ def test_forward_without_device_fails_loudly(_lib):
     (dict(Cin=64, H=32, W=32, stride=2), rt.SNN_VARIANT_GENERIC),
     (dict(Cin=64, H=32, W=32, KH=1, KW=1, pad=0), rt.SNN_VARIANT_GENERIC),
     (dict(Cin=128, H=32, W=32, flags=rt.SNN_FLAG_FORCE_GENERIC), rt.SNN_VARIANT_GENERIC),
+    # only the general kernel has the Add-before-neuron and two-neuron epilogues
+    (dict(Cin=128, H=32, W=32, res_mode="add_before"), rt.SNN_VARIANT_GENERIC),
+    (dict(Cin=256, H=12, W=12, Cout=256, res_mode="two_neuron"), rt.SNN_VARIANT_GENERIC),
 ])
 def test_variant_selection(kw, expect):
     base = dict(T=4, B=2, Cin=64, H=8, W=8, Cout=128, KH=3, KW=3)

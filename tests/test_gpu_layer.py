@@ -12,7 +12,7 @@ Checks, on every reference golden case and at the config-0 full size:
 import numpy as np
 import pytest
 
-from conftest import LAYER_CASES, load_layer_case
+from conftest import LAYER_CASES, RES_CASES, load_layer_case
 from oracle import lif_layer as L
 
 pytestmark = pytest.mark.gpu
@@ -337,3 +337,104 @@ def test_spikformer_linear_shapes(cuda_device, cin, cout):
     ys = from_nhwc(y.float().cpu().numpy(), T, 1)
     v = np.transpose(state.cpu().numpy().reshape(1, 1, rows, cout), (0, 3, 1, 2))
     check_spikes_and_v(ys, v, r["spikes"], r["h"], r["v"])
+
+
+# ------------------------------------------------------------- residual modes
+BAND = 1e-2
+
+
+def check_two_neuron(out, v1, v2, ref, v_th=1.0, v_th2=1.0):
+    """Parity rule for neuron2(neuron(bn) + residual): a neuron's first output
+    mismatch must lie where the second neuron's pre-reset membrane is within
+    the band of its threshold, or where the first neuron was within its band
+    at this or an earlier step (its spike may have flipped there).  Final
+    membranes are compared on neurons that never came near either threshold."""
+    s2 = ref["spikes2"].astype(np.float32)
+    mism = out != s2
+    frac = 1.0 - float(mism.mean())
+    assert frac >= SPIKE_MIN_AGREE, f"spike agreement {frac:.5f}"
+    near1 = np.maximum.accumulate(np.abs(ref["h"] - v_th) < BAND, axis=0)
+    near2 = np.abs(ref["h2"] - v_th2) < BAND
+    seen = np.zeros(mism.shape[1:], bool)
+    for t in range(mism.shape[0]):
+        first = mism[t] & ~seen
+        assert not (first & ~near1[t] & ~near2[t]).any(), f"unexplained mismatch at t={t}"
+        seen |= mism[t]
+    clean1 = ~near1[-1]
+    clean2 = clean1 & ~seen & ~near2.any(axis=0)
+    for v, rv, keep in ((v1, ref["v"], clean1), (v2, ref["v2"], clean2)):
+        err = np.abs(v - rv)[keep]
+        assert (err <= V_RTOL * np.abs(rv[keep]) + V_ATOL).all(), f"max v err {err.max()}"
+
+
+def run_res_layer(x, w, bn, res, *, T, B, H, W, stride=1, pad=None, neuron="lif", tau=2.0,
+                  res_mode="add_before", neuron2="lif", tau2=2.0, force_generic=False,
+                  state_init=None):
+    import torch
+    from sparsesnn_b200 import runtime as rt
+    from sparsesnn_b200.layer import SparseConvBNLIF, fold_bn
+    scale, bias = fold_bn(bn.gamma, bn.beta, bn.mean, bn.var)
+    layer = SparseConvBNLIF(w, scale, bias, T=T, B=B, H=H, W=W, stride=stride, pad=pad,
+                            neuron=neuron, tau=tau, res_mode=res_mode, neuron2=neuron2,
+                            tau2=tau2, force_generic=force_generic)
+    assert rt.variant(layer.desc) == rt.SNN_VARIANT_GENERIC
+    xd = torch.from_numpy(to_nhwc(x)).to("cuda", torch.float16)
+    rd = torch.from_numpy(to_nhwc(res)).to("cuda", torch.float16)
+    st = torch.full(layer.state_shape(), 123.0, dtype=torch.float32, device="cuda")
+    st2 = torch.full(layer.state_shape(), -7.0, dtype=torch.float32, device="cuda") \
+        if res_mode == "two_neuron" else None
+    y = layer(xd, state=st, residual=rd, read_state=False, state2=st2)
+    torch.cuda.synchronize()
+    assert rt.device_error() == 0
+    oh, ow = layer.OH, layer.OW
+    F = w.shape[0]
+    ys = from_nhwc(y.float().cpu().numpy(), T, B)
+    to_bfhw = lambda s: np.transpose(s.cpu().numpy().reshape(B, oh, ow, F), (0, 3, 1, 2))
+    return ys, to_bfhw(st), (to_bfhw(st2) if st2 is not None else None)
+
+
+@pytest.mark.parametrize("generic", [False, True], ids=["auto", "generic"])
+@pytest.mark.parametrize("name", RES_CASES)
+def test_golden_residual_modes(cuda_device, name, generic):
+    """The reference's Add-before-LIF and IF+Add+LIF epilogues against its
+    own modules' outputs (golden fixtures)."""
+    g = load_layer_case(name)
+    bn = L.BNParams(g["gamma"], g["beta"], g["mean"], g["var"])
+    ys, v, v2 = run_res_layer(g["x"].astype(np.float32), g["w"], bn, g["residual"], T=g["T"],
+                              B=g["B"], H=g["H"], W=g["W"], pad=g["pad"], neuron=g["neuron"],
+                              res_mode=g["res_mode"], neuron2=g["neuron2"],
+                              force_generic=generic)
+    assert np.isin(ys, (0.0, 1.0)).all()
+    if g["res_mode"] == "two_neuron":
+        check_two_neuron(ys, v, v2, g)
+    else:
+        check_spikes_and_v(ys, v, g["spikes"].astype(np.float32), g["h"], g["v"])
+
+
+@pytest.mark.parametrize("T", [4, 3], ids=["T4", "T3"])
+@pytest.mark.parametrize("mode, neuron, tau, neuron2, tau2", [
+    ("add_before", "lif", 2.0, "lif", 2.0),
+    ("add_before", "lif", 3.0, "lif", 2.0),
+    ("add_before", "if", 2.0, "lif", 2.0),
+    ("two_neuron", "if", 2.0, "lif", 2.0),
+    ("two_neuron", "lif", 2.0, "lif", 3.0),
+    ("two_neuron", "lif", 3.0, "if", 2.0),
+], ids=["addlif", "addlif_tau3", "addif", "if_add_lif", "lif_add_lif3", "lif3_add_if"])
+@pytest.mark.parametrize("k", [3, 1])
+def test_residual_modes_vs_oracle(cuda_device, T, mode, neuron, tau, neuron2, tau2, k):
+    """Every neuron combination of both epilogues, 3x3 and 1x1, with four
+    timesteps per accumulator (T=4) and two (T=3), 192 output channels (a
+    partial 128-channel tile), real-valued residual."""
+    B, C, F, H, W = 2, 64, 192, 8, 8
+    x, w, bn = L.make_config0(seed=40 + T + k, T=T, B=B, C=C, F=F, H=H, W=W, k=k)
+    rng = np.random.default_rng(50 + T)
+    res = (rng.standard_normal((T, B, F, H, W)) * 0.5).astype(np.float16).astype(np.float32)
+    ys, v, v2 = run_res_layer(x, w, bn, res, T=T, B=B, H=H, W=W, pad=k // 2, neuron=neuron,
+                              tau=tau, res_mode=mode, neuron2=neuron2, tau2=tau2)
+    r = L.fused_layer(x, w, bn, stride=1, pad=k // 2, tau=tau, neuron=neuron, residual=res,
+                      res_mode=mode, neuron2=neuron2, tau2=tau2)
+    assert np.isin(ys, (0.0, 1.0)).all()
+    if mode == "two_neuron":
+        check_two_neuron(ys, v, v2, r)
+    else:
+        check_spikes_and_v(ys, v, r["spikes"], r["h"], r["v"])

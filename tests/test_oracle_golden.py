@@ -7,7 +7,7 @@ Fixtures: ``tests/golden/make_golden.py`` (imports the reference's
 import numpy as np
 import pytest
 
-from conftest import GOLDEN, LAYER_CASES, load_layer_case
+from conftest import GOLDEN, LAYER_CASES, RES_CASES, load_layer_case
 from oracle import lif_layer as L
 from oracle import pack24 as P
 
@@ -38,6 +38,25 @@ def test_layer_matches_reference(name):
     assert frac == 1.0 and explained
     if res is not None:
         assert np.array_equal(r["out"], g["out"].astype(np.float32))
+
+
+@pytest.mark.parametrize("name", RES_CASES)
+def test_residual_modes_match_reference(name):
+    """Add-before-neuron and two-neuron epilogues against the reference
+    modules (Conv -> BN -> Add -> LIF; Conv -> BN -> IF -> Add -> LIF)."""
+    g = load_layer_case(name)
+    bn = L.BNParams(g["gamma"], g["beta"], g["mean"], g["var"])
+    r = L.fused_layer(g["x"].astype(np.float32), g["w"], bn, stride=g["stride"], pad=g["pad"],
+                      neuron=g["neuron"], residual=g["residual"], res_mode=g["res_mode"],
+                      neuron2=g["neuron2"])
+    np.testing.assert_allclose(r["bn_out"], g["bn_out"], rtol=0, atol=1e-5)
+    np.testing.assert_allclose(r["h"], g["h"], rtol=0, atol=1e-5)
+    np.testing.assert_allclose(r["v"], g["v"], rtol=0, atol=1e-5)
+    assert np.array_equal(r["spikes"], g["spikes"].astype(np.float32))
+    if g["res_mode"] == "two_neuron":
+        np.testing.assert_allclose(r["h2"], g["h2"], rtol=0, atol=1e-5)
+        np.testing.assert_allclose(r["v2"], g["v2"], rtol=0, atol=1e-5)
+    assert np.array_equal(r["out"], g["out"].astype(np.float32))
 
 
 def test_sew18_forward_matches_reference_model():

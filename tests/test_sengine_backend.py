@@ -102,7 +102,7 @@ def test_export_shims_have_reference_symbols(tmp_path):
         out = subprocess.run(["nm", "-D", "--defined-only", so], capture_output=True, text=True,
                              check=True).stdout
         names = {line.split()[-1] for line in out.splitlines() if line.strip()}
-        assert {"init", "call", "call_res"} <= names
+        assert {"init", "call", "call_res", "call_res2"} <= names
         lib = ctypes.CDLL(so)
         assert lib.init is not None and lib.call is not None
 
@@ -125,6 +125,10 @@ def test_reference_apply_fusion_drives_compiler():
             def __init__(self, *a, log_colors=None, secondary_log_colors=None, reset=True,
                          **kw):
                 super().__init__(*a, **kw)
+
+            def format(self, record):
+                record.log_color = record.reset = ""
+                return super().format(record)
         cl.ColoredFormatter = _ColoredFormatter
         sys.modules["colorlog"] = cl
     onnx = sys.modules["onnx"]
@@ -157,16 +161,35 @@ def test_reference_apply_fusion_drives_compiler():
         n.bound_type = sir.BoundType.MEMORY
         return g.add_node(n)
 
+    def neuron(name, inp, out, shape, kind="LIF"):
+        n = lif(name, inp, out, shape)
+        if kind == "IF":
+            g.nodes[n].op_type = sir.OpType.IF
+            g.nodes[n].neuron_params.neuron_type = sir.NeuronType.IF
+        return n
+
+    def add(name, a, b, out, shape):
+        n = sir.Node(id=-1, name=name, op_type=sir.OpType.Add, input_names=[a, b],
+                     output_names=[out], input_shapes=[shape, shape], output_shapes=[shape])
+        n.bound_type = sir.BoundType.MEMORY
+        return g.add_node(n)
+
     s = (8, 64, 16, 16)
     lif("l0", "x", "x0", s)              # block input, produced by an earlier neuron
     c1 = conv("c1", "x0", "y1", 64, 64, s, s)
     lif("l1", "y1", "s1", s)
     c2 = conv("c2", "s1", "y2", 64, 64, s, s)
     lif("l2", "y2", "s2", s)
-    add = sir.Node(id=-1, name="add", op_type=sir.OpType.Add, input_names=["s2", "x0"],
-                   output_names=["out"], input_shapes=[s, s], output_shapes=[s])
-    add.bound_type = sir.BoundType.MEMORY
-    g.add_node(add)
+    add("add", "s2", "x0", "out", s)
+    # Conv -> Add(skip) -> LIF (Add before the neuron) and Conv -> IF -> Add(skip)
+    # -> LIF (two neurons around the Add).
+    c3 = conv("c3", "out", "y3", 64, 64, s, s)
+    add("add3", "y3", "x0", "z3", s)
+    lif("l3", "z3", "s3", s)
+    c4 = conv("c4", "s3", "y4", 64, 64, s, s)
+    neuron("l4", "y4", "s4", s, kind="IF")
+    add("add4", "s4", "s3", "z4", s)
+    lif("l5", "z4", "s5", s)
     g.build_edges()
     g.compute_topo_order()
     apply_fusion(g, "slicer", batch_size=2)
@@ -175,7 +198,14 @@ def test_reference_apply_fusion_drives_compiler():
     assert kern[c1].desc.neuron == rt.SNN_NEURON_LIF and kern[c1].desc.tau == 2.0
     assert not kern[c1].residual
     # c2 absorbed LIF + Add with the block input as residual: the SEW epilogue.
-    assert kern[c2].residual
+    assert kern[c2].residual and kern[c2].res_mode == "add_after"
+    assert g.nodes[c3].extra_attrs["fusion_slice"] == "Conv2d+Add+LIF"
+    assert kern[c3].res_mode == "add_before" and kern[c3].desc.res_mode == rt.SNN_RES_ADD_BEFORE
+    assert g.nodes[c4].extra_attrs["fusion_slice"] == "Conv2d+IF+Add+LIF"
+    k4 = kern[c4]
+    assert k4.res_mode == "two_neuron" and k4.desc.res_mode == rt.SNN_RES_TWO_NEURON
+    assert k4.desc.neuron == rt.SNN_NEURON_IF and k4.desc.neuron2 == rt.SNN_NEURON_LIF
+    assert rt.variant(k4.desc) == rt.SNN_VARIANT_GENERIC
 
 
 @pytest.mark.gpu
@@ -206,3 +236,48 @@ def test_exported_shim_call_matches_library(cuda_device, tmp_path):
     out2 = kern(x, w, st2, sc, bi)
     torch.cuda.synchronize()
     assert torch.equal(out1, out2) and torch.equal(st1, st2)
+
+
+@pytest.mark.gpu
+def test_exported_two_neuron_shim_matches_golden(cuda_device, tmp_path):
+    """``call_res2`` of an exported IF+Add+LIF node (argument order of the
+    reference template) gives the same spikes and membranes as the library
+    call, and both match the reference golden case."""
+    import torch
+    from conftest import load_layer_case
+    from sparsesnn_b200.layer import fold_bn
+    g = load_layer_case("c1twon")
+    ir = IR([Nd(0, KV.TileLangFusedConv1x1BNIF, CP(g["C"], g["F"], 1, 1, 1, 1, 0, 0), None,
+                [(g["B"], g["C"], g["H"], g["W"])],
+                {"absorbed_nids": [1, 2, 3], "residual_nid": 9,
+                 "fusion_slice": "Conv2d+IF+Add+LIF"}),
+             Nd(1, KV.ZeroCost, None, NP(NT.IF)),
+             Nd(2, KV.ZeroCost),
+             Nd(3, KV.ZeroCost, None, NP(NT.LIF, tau=2.0))])
+    kern = B200Compiler(ir, T=g["T"], batch_size=g["B"]).compile_all()[0]
+    assert kern.res_mode == "two_neuron"
+    so = export_all_kernels({0: kern}, None, str(tmp_path))[0]
+    shim = ctypes.CDLL(so)
+    shim.call_res2.argtypes = [ctypes.c_void_p] * 9
+    assert shim.init() == 0
+    nhwc = lambda a: torch.from_numpy(np.ascontiguousarray(np.transpose(
+        a.astype(np.float32), (0, 1, 3, 4, 2)).reshape(g["T"] * g["B"], g["H"], g["W"], -1)))
+    x = nhwc(g["x"]).cuda().half()
+    r = nhwc(g["residual"]).cuda().half()
+    w = torch.from_numpy(kern.pack(g["w"])).cuda()
+    sc, bi = (torch.from_numpy(a).cuda() for a in fold_bn(g["gamma"], g["beta"], g["mean"],
+                                                            g["var"]))
+    m = g["B"] * g["H"] * g["W"]
+    st = [torch.zeros((m, g["F"]), device="cuda") for _ in range(4)]
+    out1 = torch.empty((g["T"] * g["B"], g["H"], g["W"], g["F"]), dtype=torch.float16,
+                       device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    assert shim.call_res2(x.data_ptr(), w.data_ptr(), st[0].data_ptr(), st[1].data_ptr(),
+                          sc.data_ptr(), bi.data_ptr(), r.data_ptr(), out1.data_ptr(), s) == 0
+    out2 = kern(x, w, st[2], st[3], sc, bi, r)
+    torch.cuda.synchronize()
+    assert torch.equal(out1, out2) and torch.equal(st[0], st[2]) and torch.equal(st[1], st[3])
+    ys = np.transpose(out1.float().cpu().numpy().reshape(g["T"], g["B"], g["H"], g["W"], g["F"]),
+                      (0, 1, 4, 2, 3))
+    frac = float((ys == g["out"]).mean())
+    assert frac >= 0.995, frac
