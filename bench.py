@@ -102,6 +102,44 @@ def spikformer_linear_layers(dev, stream, sparse_peak, iters=10):
     return out
 
 
+def spikformer_attention(dev, stream, hbm_peak, iters=12, sets=4):
+    """The fused attention core + attention LIF at the Spikformer-8-384 shape
+    (T=4, batch 32, 196 tokens, 12 heads of 32) on Bernoulli(0.09) q/k/v
+    spikes: CUDA-event time per call, rotating over `sets` input sets
+    (together larger than L2), and HBM throughput of the algorithmic bytes
+    (q, k, v read once, spikes written once, fp16)."""
+    import torch
+    from sparsesnn_b200 import runtime as rt
+    T, B, N, heads, hd = 4, 32, 196, 12, 32
+    C = heads * hd
+    lib = rt.load()
+    ins = [[(torch.rand((T * B, N, C), device=dev) < 0.09).half() for _ in range(3)]
+           for _ in range(sets)]
+    out = torch.empty((T * B, N, C), dtype=torch.float16, device=dev)
+    s = stream.cuda_stream
+
+    def call(i):
+        q, k, v = ins[i % sets]
+        rt.check(lib.snn_spikformer_attn_forward(T, B, N, heads, hd, 0.125, 2.0, 0.5, 0.0, 0,
+                                                 q.data_ptr(), k.data_ptr(), v.data_ptr(), None,
+                                                 out.data_ptr(), s))
+    for i in range(3):
+        call(i)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for i in range(iters):
+        call(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / iters
+    nbytes = 4 * T * B * N * C * 2
+    gbs = nbytes / (ms / 1000.0) / 1e9
+    return {"us": round(ms * 1000.0, 2), "GB/s": round(gbs, 1), "frac": round(gbs / hbm_peak, 4),
+            "bytes": nbytes, "shape": {"T": T, "B": B, "N": N, "heads": heads, "head_dim": hd},
+            "l2": f"{sets} input sets rotated"}
+
+
 def cpu_reference_images_per_s(steps, sample, threads, warmup=1):
     """Time the oracle's port of the reference PyTorch forward on CPU."""
     import torch
@@ -304,6 +342,9 @@ def run_ours(args, rank, world, local_rank):
         raise RuntimeError("fused kernel reported a device error")
 
     linear = spikformer_linear_layers(dev, stream, sparse_peak) if rank == 0 else None
+    attn = spikformer_attention(dev, stream, hbm_peak) if rank == 0 else None
+    if rt.device_error() != 0:
+        raise RuntimeError("a kernel reported a device error")
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -334,6 +375,7 @@ def run_ours(args, rank, world, local_rank):
                                           "algorithmic_bytes_per_forward": alg_bytes}},
                 "layer_ms": {k: round(v, 4) for k, v in per_layer.items()},
                 "spikformer_linear": linear,
+                "spikformer_attention": attn,
                 "clocks": dict(clk.summary(), window="timed region plus 300 replays before and 200 after"),
                 "cpu_baseline": cpu}
         print(json.dumps(line), flush=True)

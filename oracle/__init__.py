@@ -14,6 +14,8 @@ pack24     numpy restatement of the reference's 2:4 magnitude pruning
 lif_layer  numpy restatement of Conv2d + BatchNorm2d(eval) + multi-step LIF
            (``models/neurons.py:121-146,187-211``; ``models/layers.py:26-31``;
            ``models/sewresnet.py:50-66`` for the SEW residual add).
+attention  numpy restatement of the Spikformer attention core + attention
+           LIF (``models/spikformer.py:97,122-127``).
 sew_resnet torch-CPU port of the reference SEW-ResNet-18 forward
            (``models/sewresnet.py:123-210``) with the CIFAR stem, used as the
            timed CPU baseline and for end-to-end logit sanity checks.

@@ -18,6 +18,7 @@
 #include "snn_conv_halo.cuh"
 #include "snn_conv_halo_stream.cuh"
 #include "snn_glue.cuh"
+#include "snn_attn.cuh"
 
 namespace {
 
@@ -189,6 +190,13 @@ int ensure_init() {
         return g_init_status = fail(SNN_E_CUDA, "smem attribute: %s", cudaGetErrorString(e));
     }
   }
+  e = cudaFuncSetAttribute(snn::spikformer_attn_lif_kernel<32>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, snn::AttnCfg<32>::kSmemBytes);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(snn::spikformer_attn_lif_kernel<64>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, snn::AttnCfg<64>::kSmemBytes);
+  if (e != cudaSuccess)
+    return g_init_status = fail(SNN_E_CUDA, "smem attribute: %s", cudaGetErrorString(e));
   return g_init_status = SNN_OK;
 }
 
@@ -666,6 +674,62 @@ int snn_head_forward(int32_t T, int32_t B, int32_t HW, int32_t C, int32_t NC, co
   const size_t smem = static_cast<size_t>(snn::kHeadSlots + 1) * C * sizeof(float);
   cudaError_t e = launch_pdl(snn::head_pool_fc_kernel, dim3(B), dim3(threads), smem, stream,
                              static_cast<const __half*>(x), fc_w, fc_b, logits, T, B, HW, C, NC);
+  if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));
+  return SNN_OK;
+}
+
+int snn_spikformer_attn_forward(int32_t T, int32_t B, int32_t N, int32_t heads,
+                                int32_t head_dim, float scale, float tau, float v_threshold,
+                                float v_reset, int32_t flags, const void* q, const void* k,
+                                const void* v, float* state, void* out, void* stream) {
+  int st = ensure_init();
+  if (st) return st;
+  if (!q || !k || !v || !out) return fail(SNN_E_INVALID, "null tensor pointer");
+  if (T < 1 || B < 1 || heads < 1 || N < 1 || N > snn::kAttnMaxN)
+    return fail(SNN_E_INVALID, "bad attention shape (1 <= N <= %d)", snn::kAttnMaxN);
+  if (head_dim != 32 && head_dim != 64) return fail(SNN_E_INVALID, "head_dim must be 32 or 64");
+  if (!(tau > 0.0f)) return fail(SNN_E_INVALID, "tau must be positive");
+  if ((flags & (SNN_FLAG_READ_STATE | SNN_FLAG_WRITE_STATE)) && !state)
+    return fail(SNN_E_INVALID, "state flags set but state is null");
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
+       reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(out)) & 15)
+    return fail(SNN_E_INVALID, "q, k, v and out must be 16-byte aligned");
+  const long long TB = static_cast<long long>(T) * B;
+  const long long C = static_cast<long long>(heads) * head_dim;
+  if (TB * N * C > 0x7fffffffLL || static_cast<long long>(B) * heads > 0x7fffffffLL)
+    return fail(SNN_E_INVALID, "attention tensors too large");
+  snn::AttnParams p;
+  memset(&p, 0, sizeof(p));
+  {
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(N),
+                          static_cast<cuuint64_t>(TB)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(C) * 2, static_cast<cuuint64_t>(N * C) * 2};
+    cuuint32_t box[3] = {static_cast<cuuint32_t>(head_dim),
+                         static_cast<cuuint32_t>(std::min<int>(N, 128)), 1};
+    if ((st = encode(&p.tmap_q, 3, q, dims, strides, box,
+                     head_dim == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B)))
+      return st;
+  }
+  p.k = static_cast<const __half*>(k);
+  p.v = static_cast<const __half*>(v);
+  p.out = static_cast<__half*>(out);
+  p.state = state;
+  unsigned* err = nullptr;
+  if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_device_err) != cudaSuccess)
+    return fail(SNN_E_CUDA, "error word address");
+  p.err = err;
+  p.T = T; p.B = B; p.N = N; p.heads = heads; p.C = static_cast<int>(C); p.flags = flags;
+  p.scale = scale; p.tau = tau; p.v_th = v_threshold; p.v_reset = v_reset;
+  p.lif_half = tau == 2.0f;
+  // Reference computes (1.0 - 1.0/tau) in double, then float32 (models/neurons.py:125).
+  p.decay = static_cast<float>(1.0 - 1.0 / static_cast<double>(tau));
+  p.timeout = 4000000000ull;
+  const dim3 grid(static_cast<unsigned>(B * heads));
+  cudaError_t e = head_dim == 32
+      ? launch_pdl(snn::spikformer_attn_lif_kernel<32>, grid, dim3(snn::kAttnThreads),
+                   snn::AttnCfg<32>::kSmemBytes, stream, p)
+      : launch_pdl(snn::spikformer_attn_lif_kernel<64>, grid, dim3(snn::kAttnThreads),
+                   snn::AttnCfg<64>::kSmemBytes, stream, p);
   if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));
   return SNN_OK;
 }

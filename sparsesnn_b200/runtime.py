@@ -30,6 +30,7 @@ SNN_VARIANT_HALO_STREAM = 2
 SNN_RES_ADD_AFTER = 0
 SNN_RES_ADD_BEFORE = 1
 SNN_RES_TWO_NEURON = 2
+SNN_DEVICE_ERR_NONBINARY = 128
 
 NEURONS = {"lif": SNN_NEURON_LIF, "if": SNN_NEURON_IF, "none": SNN_NEURON_NONE}
 
@@ -37,7 +38,7 @@ NEURONS = {"lif": SNN_NEURON_LIF, "if": SNN_NEURON_IF, "none": SNN_NEURON_NONE}
 EXPORTED = (
     "snn_abi_version", "snn_init", "snn_conv_variant", "snn_conv_out_shape", "snn_conv_weight_bytes",
     "snn_pack_weight_24", "snn_conv_forward", "snn_conv_forward_res", "snn_conv_forward_res2",
-    "snn_stem_forward",
+    "snn_stem_forward", "snn_spikformer_attn_forward",
     "snn_head_forward", "snn_get_device_error", "snn_last_error_message",
 )
 
@@ -80,6 +81,9 @@ def _declare(lib):
         "snn_conv_forward_res2": ([D, P, P, P, P, P, P, P, P, P], ctypes.c_int),
         "snn_stem_forward": ([D, i32, P, P, P, P, P, P], ctypes.c_int),
         "snn_head_forward": ([i32, i32, i32, i32, i32, P, P, P, P, P], ctypes.c_int),
+        "snn_spikformer_attn_forward": ([i32, i32, i32, i32, i32, ctypes.c_float, ctypes.c_float,
+                                         ctypes.c_float, ctypes.c_float, i32, P, P, P, P, P, P],
+                                        ctypes.c_int),
         "snn_get_device_error": ([ctypes.POINTER(ctypes.c_uint32), ctypes.c_int], ctypes.c_int),
         "snn_last_error_message": ([], ctypes.c_char_p),
     }

@@ -14,6 +14,7 @@ LAYER_CASES = ["c3s1", "c3s2", "c1s2", "c3res", "c3f64", "c3if", "lin"]
 # neurons around the Add).
 RES_CASES = ["c3addlif", "c1twon"]
 RES_MODES = {0: "add_after", 1: "add_before", 2: "two_neuron"}
+ATTN_CASES = ["n64", "n196", "n100h64"]
 
 
 def pytest_configure(config):
@@ -44,3 +45,10 @@ def cuda_device():
     from sparsesnn_b200 import build
     build.build()
     return torch.device("cuda:0")
+
+
+def load_attn_case(name):
+    g = dict(np.load(GOLDEN / f"attn_{name}.npz"))
+    T, B, N, heads, hd = (int(v) for v in g["meta"])
+    g.update(T=T, B=B, N=N, heads=heads, hd=hd)
+    return g

@@ -195,6 +195,36 @@ def residual_case(ref, name, *, mode, neuron, neuron2="lif", T, B, C, F, H, W, k
     print("wrote", name, {k: v.shape for k, v in out.items()})
 
 
+def attention_case(ref_path, name, *, T, B, N, heads, hd, p_spike, seed):
+    """Spikformer attention core + attention LIF from the reference: the
+    fused graph op's forward (``sengine/tdl/attention_ops.py:50-82``) and,
+    as a cross-check, the model's own formulation (``models/spikformer.py:
+    122-127``: matmuls in float32, then ``MultiStepLIFNeuron(tau=2,
+    v_threshold=0.5)``)."""
+    import importlib.util
+    import torch
+    from models.neurons import MultiStepLIFNeuron
+    spec = importlib.util.spec_from_file_location(
+        "attention_ops", str(Path(ref_path) / "sengine" / "tdl" / "attention_ops.py"))
+    ops = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ops)
+    g = torch.Generator().manual_seed(seed)
+    C = heads * hd
+    q, k, v = ((torch.rand((T * B, N, C), generator=g) < p_spike).float() for _ in range(3))
+    with torch.no_grad():
+        fused = ops._spikformer_attn_forward(None, q, k, v, T, heads, hd, 0.125, 2.0, 0.5)
+        qh, kh, vh = (a.reshape(T, B, N, heads, hd).permute(0, 1, 3, 2, 4) for a in (q, k, v))
+        x = ((qh @ kh.transpose(-2, -1)) * 0.125) @ vh
+        x = x.transpose(2, 3).reshape(T, B, N, C)
+        model = MultiStepLIFNeuron(tau=2.0, v_threshold=0.5)(x).reshape(T * B, N, C)
+    assert torch.equal(fused, model)
+    np.savez_compressed(HERE / f"attn_{name}.npz", q=q.numpy().astype(np.uint8),
+                        k=k.numpy().astype(np.uint8), v=v.numpy().astype(np.uint8),
+                        x=x.reshape(T * B, N, C).numpy(), spikes=model.numpy().astype(np.uint8),
+                        meta=np.array([T, B, N, heads, hd], np.int64))
+    print("wrote attn", name, tuple(q.shape), "spike rate", float(model.mean()))
+
+
 def prune_case(ref):
     import torch
     g = torch.Generator().manual_seed(7)
@@ -269,6 +299,9 @@ def main():
                   H=8, W=8, k=3, seed=9)
     residual_case(ref, "c1twon", mode="two_neuron", neuron="if", neuron2="lif", T=4, B=2,
                   C=128, F=64, H=8, W=8, k=1, seed=10)
+    attention_case(a.ref, "n64", T=4, B=2, N=64, heads=2, hd=32, p_spike=0.13, seed=11)
+    attention_case(a.ref, "n196", T=4, B=2, N=196, heads=2, hd=32, p_spike=0.09, seed=12)
+    attention_case(a.ref, "n100h64", T=3, B=2, N=100, heads=2, hd=64, p_spike=0.09, seed=13)
     model_case(ref, HERE.parent.parent)
 
 

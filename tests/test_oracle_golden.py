@@ -7,7 +7,7 @@ Fixtures: ``tests/golden/make_golden.py`` (imports the reference's
 import numpy as np
 import pytest
 
-from conftest import GOLDEN, LAYER_CASES, RES_CASES, load_layer_case
+from conftest import ATTN_CASES, GOLDEN, LAYER_CASES, RES_CASES, load_attn_case, load_layer_case
 from oracle import lif_layer as L
 from oracle import pack24 as P
 
@@ -57,6 +57,16 @@ def test_residual_modes_match_reference(name):
         np.testing.assert_allclose(r["h2"], g["h2"], rtol=0, atol=1e-5)
         np.testing.assert_allclose(r["v2"], g["v2"], rtol=0, atol=1e-5)
     assert np.array_equal(r["out"], g["out"].astype(np.float32))
+
+
+@pytest.mark.parametrize("name", ATTN_CASES)
+def test_attention_matches_reference(name):
+    """Spikformer attention core + attention LIF: exact (integer counts)."""
+    from oracle.attention import spikformer_attn_lif
+    g = load_attn_case(name)
+    spk, x, _, _ = spikformer_attn_lif(g["q"], g["k"], g["v"], T=g["T"], heads=g["heads"])
+    assert np.array_equal(x, g["x"])
+    assert np.array_equal(spk, g["spikes"].astype(np.float32))
 
 
 def test_sew18_forward_matches_reference_model():
