@@ -163,8 +163,8 @@ int snn_head_forward(int32_t T, int32_t B, int32_t HW, int32_t C, int32_t NC,
  * models/spikformer.py:122-127 with attn_lif = MultiStepLIFNeuron(tau,
  * v_threshold), :97).  Per timestep and head: x = (q k^T * scale) v, then the
  * LIF over T with hard reset to v_reset.
- *   q, k, v  [T*B][N][heads*head_dim] fp16 spikes (0/1; anything else sets
- *            SNN_DEVICE_ERR_NONBINARY in the device error word)
+ *   q, k, v  [T*B][N][heads*head_dim] fp16 spikes (0/1: the kernel forms
+ *            q (k^T v) with k^T v rounded to fp16, exact for spikes)
  *   out      [T*B][N][heads*head_dim] fp16 spikes
  *   state    [B][N][heads*head_dim] fp32 membrane, per SNN_FLAG_*_STATE
  * 1 <= N <= 256, head_dim 32 or 64.  x is exact (integer counts times scale)
@@ -173,10 +173,6 @@ int snn_spikformer_attn_forward(int32_t T, int32_t B, int32_t N, int32_t heads,
                                 int32_t head_dim, float scale, float tau, float v_threshold,
                                 float v_reset, int32_t flags, const void* q, const void* k,
                                 const void* v, float* state, void* out, void* stream);
-
-/* Device error word bits (snn_get_device_error): bounded-wait timeouts are
- * the low bits; this one reports non-spike attention inputs. */
-#define SNN_DEVICE_ERR_NONBINARY 128u
 
 /* Reads (and with reset != 0 clears) the device error word that kernels set
  * when a bounded wait times out.  Synchronises the device. */

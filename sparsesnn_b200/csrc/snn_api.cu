@@ -700,18 +700,22 @@ int snn_spikformer_attn_forward(int32_t T, int32_t B, int32_t N, int32_t heads,
     return fail(SNN_E_INVALID, "attention tensors too large");
   snn::AttnParams p;
   memset(&p, 0, sizeof(p));
+  p.kv_rows = (N + 15) / 16 * 16;
   {
+    // q, k, v as 3-D {C, N, T*B}; q boxes are 128-token M-tiles, k/v boxes
+    // all kv_rows tokens (rows past N read as zero).
     cuuint64_t dims[3] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(N),
                           static_cast<cuuint64_t>(TB)};
     cuuint64_t strides[2] = {static_cast<cuuint64_t>(C) * 2, static_cast<cuuint64_t>(N * C) * 2};
-    cuuint32_t box[3] = {static_cast<cuuint32_t>(head_dim),
-                         static_cast<cuuint32_t>(std::min<int>(N, 128)), 1};
-    if ((st = encode(&p.tmap_q, 3, q, dims, strides, box,
-                     head_dim == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B)))
-      return st;
+    const CUtensorMapSwizzle swz =
+        head_dim == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
+    cuuint32_t box_q[3] = {static_cast<cuuint32_t>(head_dim),
+                           static_cast<cuuint32_t>(std::min<int>(N, 128)), 1};
+    cuuint32_t box_kv[3] = {static_cast<cuuint32_t>(head_dim), static_cast<cuuint32_t>(p.kv_rows), 1};
+    if ((st = encode(&p.tmap_q, 3, q, dims, strides, box_q, swz))) return st;
+    if ((st = encode(&p.tmap_k, 3, k, dims, strides, box_kv, swz))) return st;
+    if ((st = encode(&p.tmap_v, 3, v, dims, strides, box_kv, swz))) return st;
   }
-  p.k = static_cast<const __half*>(k);
-  p.v = static_cast<const __half*>(v);
   p.out = static_cast<__half*>(out);
   p.state = state;
   unsigned* err = nullptr;

@@ -286,6 +286,21 @@ __device__ __forceinline__ uint64_t smem_desc_kmajor(uint32_t saddr, uint32_t sb
   return d;
 }
 
+// Shared-memory matrix descriptor for an MN-major operand tile (the M or N
+// index contiguous) as written by a TMA box of rows of `row_bytes` along K:
+// one swizzle atom along M/N, 8-row groups along K `sbo_bytes` apart; `lbo`
+// is the distance between atoms along M/N (for operands wider than one).
+__device__ __forceinline__ uint64_t smem_desc_mnmajor(uint32_t saddr, uint32_t lbo_bytes,
+                                                      uint32_t sbo_bytes, uint32_t layout_type) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFF);
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFF) << 16;
+  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFF) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(layout_type & 0x7) << 61;
+  return d;
+}
+
 // Instruction descriptor, kind::f16, A=B=F16, D=F32, both K-major.
 __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool sparse) {
   return (sparse ? (1u << 2) : 0u)      // sparsity flag
@@ -293,6 +308,10 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool sparse) {
          | (0u << 7) | (0u << 10)       // A, B = F16
          | (static_cast<uint32_t>(N >> 3) << 17)
          | (static_cast<uint32_t>(M >> 4) << 24);
+}
+// Same with A and/or B MN-major (bits 15 / 16).
+__host__ __device__ constexpr uint32_t idesc_f16_major(int M, int N, bool a_mn, bool b_mn) {
+  return idesc_f16(M, N, false) | (a_mn ? (1u << 15) : 0u) | (b_mn ? (1u << 16) : 0u);
 }
 
 }  // namespace snn

@@ -30,7 +30,6 @@ SNN_VARIANT_HALO_STREAM = 2
 SNN_RES_ADD_AFTER = 0
 SNN_RES_ADD_BEFORE = 1
 SNN_RES_TWO_NEURON = 2
-SNN_DEVICE_ERR_NONBINARY = 128
 
 NEURONS = {"lif": SNN_NEURON_LIF, "if": SNN_NEURON_IF, "none": SNN_NEURON_NONE}
 
