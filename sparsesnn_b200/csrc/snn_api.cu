@@ -104,17 +104,17 @@ HsKernel hs_kernel_fn(int mode, bool res) {
 
 using StemKernel = void (*)(const snn::StemParams);
 
-StemKernel stem_rows_fn(int cin, int mode) {
+StemKernel stem_tc_fn(int cin, int mode) {
   if (cin == 3) {
-    if (mode == snn::kModeLifHalf) return snn::stem_rows_kernel<3, snn::kModeLifHalf>;
-    if (mode == snn::kModeLifDiv) return snn::stem_rows_kernel<3, snn::kModeLifDiv>;
-    return snn::stem_rows_kernel<3, snn::kModeIf>;
+    if (mode == snn::kModeLifHalf) return snn::stem_tc_kernel<3, snn::kModeLifHalf>;
+    if (mode == snn::kModeLifDiv) return snn::stem_tc_kernel<3, snn::kModeLifDiv>;
+    return snn::stem_tc_kernel<3, snn::kModeIf>;
   }
-  if (mode == snn::kModeLifHalf) return snn::stem_rows_kernel<1, snn::kModeLifHalf>;
-  if (mode == snn::kModeLifDiv) return snn::stem_rows_kernel<1, snn::kModeLifDiv>;
-  return snn::stem_rows_kernel<1, snn::kModeIf>;
+  if (mode == snn::kModeLifHalf) return snn::stem_tc_kernel<1, snn::kModeLifHalf>;
+  if (mode == snn::kModeLifDiv) return snn::stem_tc_kernel<1, snn::kModeLifDiv>;
+  return snn::stem_tc_kernel<1, snn::kModeIf>;
 }
-constexpr int kStemRowsSmemMax = 96 * 1024;
+constexpr int kStemTcSmemMax = 96 * 1024;
 
 constexpr int kSmemLimit = 232448;          // opt-in dynamic smem per block on sm_100
 
@@ -178,8 +178,8 @@ int ensure_init() {
       }
       if (mode != snn::kModeNone && res == 0) {
         for (int cin : {1, 3}) {
-          e = cudaFuncSetAttribute(stem_rows_fn(cin, mode),
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, kStemRowsSmemMax);
+          e = cudaFuncSetAttribute(stem_tc_fn(cin, mode),
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, kStemTcSmemMax);
           if (e != cudaSuccess)
             return g_init_status = fail(SNN_E_CUDA, "smem attribute: %s", cudaGetErrorString(e));
         }
@@ -628,18 +628,21 @@ int snn_stem_forward(const snn_conv_desc* d, int32_t Tin, const float* x, const 
   p.OH = OH; p.OW = OW; p.neuron = d->neuron;
   p.tau = d->tau; p.decay = static_cast<float>(1.0 - 1.0 / static_cast<double>(d->tau));
   p.v_th = d->v_threshold; p.v_reset = d->v_reset;
-  // Row-tiled fast path: 3x3 s1 p1, 64 channels, input repeated over T,
+  p.err = nullptr;
+  p.timeout = 4000000000ull;
+  if (cudaGetSymbolAddress(reinterpret_cast<void**>(&p.err), g_device_err) != cudaSuccess)
+    return fail(SNN_E_CUDA, "error word address");
+  // Tensor-core fast path: 3x3 s1 p1, 64 channels, input repeated over T,
   // rows of at most 128 pixels.
   if (Tin == 1 && d->KH == 3 && d->KW == 3 && d->stride == 1 && d->pad == 1 && d->Cout == 64 &&
       (d->Cin == 1 || d->Cin == 3) && OW <= snn::kStemPx) {
     const int mode = d->neuron == SNN_NEURON_IF ? snn::kModeIf
                      : d->tau == 2.0f ? snn::kModeLifHalf : snn::kModeLifDiv;
     const int R = snn::kStemPx / OW;
-    const size_t smem = static_cast<size_t>(snn::stem_rows_smem_floats(d->Cin, R, OW)) * 4 +
-                        2 * snn::kStemPx * 128;
+    const size_t smem = static_cast<size_t>(snn::stem_tc_smem_bytes(d->Cin, R, OW));
     const long long nblk = static_cast<long long>(d->B) * ((OH + R - 1) / R);
-    if (smem <= static_cast<size_t>(kStemRowsSmemMax) && nblk <= 0x7fffffffLL) {
-      cudaError_t e = launch_pdl(stem_rows_fn(d->Cin, mode), dim3(static_cast<unsigned>(nblk)),
+    if (smem <= static_cast<size_t>(kStemTcSmemMax) && nblk <= 0x7fffffffLL) {
+      cudaError_t e = launch_pdl(stem_tc_fn(d->Cin, mode), dim3(static_cast<unsigned>(nblk)),
                                  dim3(snn::kStemThreads), smem, stream, p);
       if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));
       return SNN_OK;

@@ -131,26 +131,37 @@ spikformer_attn_lif_kernel(const __grid_constant__ AttnParams p) {
   // GEMM 2: M = 128, N = HD, A K-major, B MN-major.
   const uint32_t idesc2 = idesc_f16_major(128, HD, false, true);
   constexpr uint32_t kKStep = (2 * Cfg::kSbo) >> 4;           // 16 rows along K, descriptor units
-  bool stop = false;
-  int passes_done = 0;
   const int n_pass = (p.T + kAttnTC - 1) / kAttnTC;
+  // Loads of a pass (thread 0).  k/v tiles are refilled as soon as GEMM 1 of
+  // the previous pass has completed and q tiles as soon as GEMM 2 has, so the
+  // next pass's loads overlap this pass's conversion and epilogue.
+  int kv_issued = 0, q_issued = 0;
+  auto issue_kv = [&](int ps) {
+    const int tcn_ = min(kAttnTC, p.T - ps * kAttnTC);
+    mbar_arrive_expect_tx(bar_kv, tcn_ * 2 * p.kv_rows * Cfg::kRowB);
+    for (int u = 0; u < tcn_; ++u) {
+      const int tb = (ps * kAttnTC + u) * p.B + b;
+      tma_load_3d(sK + u * Cfg::kKVTile, &p.tmap_k, bar_kv, h * HD, 0, tb);
+      tma_load_3d(sV + u * Cfg::kKVTile, &p.tmap_v, bar_kv, h * HD, 0, tb);
+    }
+    ++kv_issued;
+  };
+  auto issue_q = [&](int ps) {
+    const int tcn_ = min(kAttnTC, p.T - ps * kAttnTC);
+    mbar_arrive_expect_tx(bar_q, tcn_ * n_mt * q_rows * Cfg::kRowB);
+    for (int u = 0; u < tcn_; ++u)
+      for (int m = 0; m < n_mt; ++m)
+        tma_load_3d(sQ + (2 * u + m) * Cfg::kQTile, &p.tmap_q, bar_q, h * HD, m * 128,
+                    (ps * kAttnTC + u) * p.B + b);
+    ++q_issued;
+  };
+  if (tid == 0) { issue_kv(0); issue_q(0); }
+  bool stop = false;
   for (int pass = 0; pass < n_pass && !stop; ++pass) {
     const int t0 = pass * kAttnTC;
     const int tcn = min(kAttnTC, p.T - t0);
     const uint32_t ph = pass & 1;
     if (tid == 0) {
-      // Loads of the whole pass (the previous pass's MMAs are complete).
-      mbar_arrive_expect_tx(bar_kv, tcn * 2 * p.kv_rows * Cfg::kRowB);
-      for (int u = 0; u < tcn; ++u) {
-        const int tb = (t0 + u) * p.B + b;
-        tma_load_3d(sK + u * Cfg::kKVTile, &p.tmap_k, bar_kv, h * HD, 0, tb);
-        tma_load_3d(sV + u * Cfg::kKVTile, &p.tmap_v, bar_kv, h * HD, 0, tb);
-      }
-      mbar_arrive_expect_tx(bar_q, tcn * n_mt * q_rows * Cfg::kRowB);
-      for (int u = 0; u < tcn; ++u)
-        for (int m = 0; m < n_mt; ++m)
-          tma_load_3d(sQ + (2 * u + m) * Cfg::kQTile, &p.tmap_q, bar_q, h * HD, m * 128,
-                      (t0 + u) * p.B + b);
       // GEMM 1 per timestep, K = 16 tokens per MMA.
       if (!mbar_wait_bounded(bar_kv, ph, p.timeout)) {
         atomicOr(p.err, kErrTimeoutFull);
@@ -176,6 +187,7 @@ spikformer_attn_lif_kernel(const __grid_constant__ AttnParams p) {
     if (warp < HD / 16) {
       const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar_g1, ph, p.timeout));
       tc_fence_after();
+      if (ok && tid == 0 && pass + 1 < n_pass) issue_kv(pass + 1);   // k/v tiles are free
       if (ok) {
         const int e = 16 * warp + lane;
         for (int u = 0; u < tcn; ++u) {
@@ -233,8 +245,8 @@ spikformer_attn_lif_kernel(const __grid_constant__ AttnParams p) {
     if (fail) atomicOr(p.err, kErrTimeoutAcc);
     tc_fence_after();
     fail = __syncthreads_or(fail || *abort_flag);
-    passes_done = pass + 1;
     if (fail) { stop = true; break; }
+    if (tid == 0 && pass + 1 < n_pass) issue_q(pass + 1);            // q tiles are free
     if (mt < n_mt) {
       for (int u = 0; u < tcn; ++u) {
         float x[HD];
@@ -273,9 +285,9 @@ spikformer_attn_lif_kernel(const __grid_constant__ AttnParams p) {
     __syncthreads();                     // TMEM and tiles free for the next pass
   }
   if (stop && tid == 0) {
-    // Let the failed pass's loads land before the CTA's shared memory goes away.
-    const uint32_t ph = (passes_done - 1) & 1;
-    if (!mbar_wait_bounded(bar_kv, ph, p.timeout) || !mbar_wait_bounded(bar_q, ph, p.timeout))
+    // Let loads still in flight land before the CTA's shared memory goes away.
+    if (!mbar_wait_bounded(bar_kv, (kv_issued - 1) & 1, p.timeout) ||
+        !mbar_wait_bounded(bar_q, (q_issued - 1) & 1, p.timeout))
       atomicOr(p.err, kErrTimeoutDrain);
   }
   if (!stop && (p.flags & kWriteState) && tok_ok) {

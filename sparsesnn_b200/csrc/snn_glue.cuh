@@ -1,8 +1,8 @@
 // Memory-bound glue around the fused sparse layers of an SNN ResNet:
-//  * stem_rows_kernel / stem_conv_lif_kernel: dense direct conv (small Cin,
-//    e.g. RGB) + BN + LIF/IF over T, computed once when the input is
-//    repeated over T (direct encoding) and written as fp16 NHWC spikes per
-//    timestep (row-tiled fast path for 3x3 / 64-channel stems; the general
+//  * stem_tc_kernel / stem_conv_lif_kernel: dense conv (small Cin, e.g. RGB)
+//    + BN + LIF/IF over T, computed once when the input is repeated over T
+//    (direct encoding) and written as fp16 NHWC spikes per timestep
+//    (tensor-core fast path for 3x3 / 64-channel stems; the general CUDA-core
 //    kernel covers other shapes and per-timestep inputs).
 //  * head_pool_fc_kernel: global average pool + mean over T + linear head.
 #pragma once
@@ -20,6 +20,8 @@ struct StemParams {
   __half* out;         // [T][B][OH][OW][Cout]
   int T, Tin, B, Cin, H, W, Cout, KH, KW, stride, pad, OH, OW, neuron;
   float tau, decay, v_th, v_reset;
+  unsigned* err;                  // device error word (tensor-core path)
+  unsigned long long timeout;     // bounded-wait budget, SM cycles
 };
 
 // One thread = one output pixel x 16 consecutive output channels
@@ -123,51 +125,83 @@ stem_conv_lif_kernel(const StemParams p) {
   }
 }
 
-// Row-tiled stem for the direct-encoding case (input repeated over T) of a
-// 3x3 stride-1 pad-1 conv with 64 output channels on images at most 128
-// pixels wide.  A block computes R = 128 / OW whole output rows of one image:
-//  * the zero-padded input rows (CIN x (R+2) x (OW+2)), the weights
-//    ([tap][64] fp32) and BN scale/bias are staged in shared memory;
-//  * 256 threads: warp w computes pixels 32*(w/2) + lane of the block and
-//    output channels 32*(w%2) .. +31 (weight reads are warp-wide broadcasts,
-//    input reads consecutive words);
-//  * BN once, then LIF/IF over T in registers; each timestep's spikes go to
-//    a [128 px][64 ch] fp16 tile (128-byte rows, 16-byte chunks XOR-ed with
-//    px & 7) and leave as fully coalesced 16-byte stores, since the block's
-//    output rows are contiguous in the NHWC tensor.  Two tiles alternate, so
-//    one barrier per timestep suffices.
+// Tensor-core stem for the direct-encoding case (input repeated over T) of
+// a 3x3 stride-1 pad-1 conv with 64 output channels and Cin <= 3, on images
+// at most 128 pixels wide.  A block computes R = 128 / OW whole output rows
+// of one image as one M = 128 (pixels) x N = 64 (channels) x K = 32 GEMM:
+//  * A = im2col of the zero-padded input rows: row = pixel, column
+//    k = (ci*3 + kh)*3 + kw (9*Cin taps, zero beyond), fp32 K-major with
+//    128-byte swizzle; B = the weights [64][32], same layout;
+//  * 3xTF32: each fp32 operand is split into hi = tf32(x) and lo = x - hi,
+//    and D = lo*hi + hi*lo + hi*hi with kind::tf32 MMAs accumulating in fp32
+//    TMEM (the dropped lo*lo term and lo's own tf32 rounding are below fp32
+//    resolution of the sum), so the result matches an fp32 conv to within
+//    accumulation order;
+//  * epilogue: thread = pixel (TMEM lane), 64 channels: BN once, then LIF/IF
+//    over T in registers; each timestep's spikes go to a [128 px][64 ch]
+//    fp16 tile (128-byte rows, 16-byte chunks XOR-ed with px & 7) in the A
+//    tiles' space and leave as coalesced 16-byte stores (the block's output
+//    rows are contiguous in the NHWC tensor).  Two tiles alternate, so one
+//    barrier per timestep suffices.
 constexpr int kStemPx = 128;
-constexpr int kStemThreads = 256;
+constexpr int kStemThreads = 128;
+constexpr int kStemATile = kStemPx * 128;          // [128 px][32 fp32]
+constexpr int kStemBTile = 64 * 128;               // [64 ch][32 fp32]
+constexpr int kStemXsOffset = 2 * kStemATile + 2 * kStemBTile;   // input rows (floats) start here
 
-// Shared-memory layout of stem_rows_kernel, in floats: input rows, then the
-// weights (16-byte aligned for float4 reads), scale, bias; the spike tiles
-// start at stem_rows_smem_floats (128-byte aligned).
-__host__ __device__ constexpr int stem_rows_ws_offset(int cin, int R, int OW) {
-  return (cin * (R + 2) * (OW + 2) + 31) / 32 * 32;
+// Dynamic shared memory of stem_tc_kernel (bytes, before 1024 alignment).
+__host__ __device__ constexpr int stem_tc_smem_bytes(int cin, int R, int OW) {
+  return kStemXsOffset + ((cin * (R + 2) * (OW + 2) + 3) / 4 * 4 + 128) * 4 + 64 + 1024;
 }
-__host__ __device__ constexpr int stem_rows_smem_floats(int cin, int R, int OW) {
-  return (stem_rows_ws_offset(cin, R, OW) + 9 * cin * 64 + 128 + 31) / 32 * 32;
+
+__device__ __forceinline__ float to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+// Byte offset of fp32 element k of row r in a K-major tile of 128-byte rows
+// with 128-byte swizzle.
+__device__ __forceinline__ int sw128_f32(int r, int k) {
+  return r * 128 + ((((k >> 2) ^ (r & 7))) << 4) + (k & 3) * 4;
 }
 
 template <int CIN, int MODE>
 __global__ void __launch_bounds__(kStemThreads)
-stem_rows_kernel(const StemParams p) {
-  extern __shared__ __align__(128) float sm[];
+stem_tc_kernel(const StemParams p) {
+  static_assert(9 * CIN <= 32, "stem K must fit one 32-wide tile");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sAh = smem;                                  // later: spike tiles
+  uint8_t* sAl = smem + kStemATile;
+  uint8_t* sBh = smem + 2 * kStemATile;
+  uint8_t* sBl = sBh + kStemBTile;
   const int OW = p.OW, R = kStemPx / OW, OWp = OW + 2;
   const int HWp = (R + 2) * OWp;
+  float* xs = reinterpret_cast<float*>(smem + kStemXsOffset);   // [CIN][R+2][OW+2]
+  float* sc = xs + (CIN * HWp + 3) / 4 * 4;                     // [64]
+  float* bi = sc + 64;                                          // [64]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(bi + 64);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
   const int bpi = (p.OH + R - 1) / R;                 // blocks per image
   const int b = blockIdx.x / bpi, oh0 = (blockIdx.x % bpi) * R;
-  float* xs = sm;                                     // [CIN][R+2][OW+2]
-  float* ws = sm + stem_rows_ws_offset(CIN, R, OW);   // [9*CIN][64], 16-byte aligned
-  float* sc = ws + 9 * CIN * 64;                      // [64]
-  float* bi = sc + 64;                                // [64]
-  uint8_t* tiles = reinterpret_cast<uint8_t*>(sm + stem_rows_smem_floats(CIN, R, OW));
-  const int tid = threadIdx.x;
-  for (int i = tid; i < 9 * CIN * 64; i += kStemThreads) {
-    const int co = i / (9 * CIN), k = i - co * (9 * CIN);   // source [Cout][Cin][3][3]
-    ws[k * 64 + co] = p.w[i];
+  const int tid = threadIdx.x, warp = tid / 32;
+
+  if (tid == 0) { mbar_init(bar, 1); fence_mbar_init(); }
+  if (warp == 0) { tmem_alloc(tmem_slot, 64); tmem_relinquish(); }
+  // Weights (constant data): B[co][k] = w[co][k] for k < 9*CIN, split hi/lo.
+  for (int i = tid; i < 64 * 32; i += kStemThreads) {
+    const int co = i >> 5, k = i & 31;
+    const float wv = k < 9 * CIN ? __ldg(p.w + co * 9 * CIN + k) : 0.f;
+    const float hi = to_tf32(wv);
+    *reinterpret_cast<float*>(sBh + sw128_f32(co, k)) = hi;
+    *reinterpret_cast<float*>(sBl + sw128_f32(co, k)) = wv - hi;
   }
-  if (tid < 64) { sc[tid] = p.scale[tid]; bi[tid] = p.bias[tid]; }
+  if (tid < 64) {
+    // BN pre-scaled by 1/2 for the tau = 2 LIF step, as in the conv epilogues.
+    sc[tid] = MODE == kModeLifHalf ? p.scale[tid] * 0.5f : p.scale[tid];
+    bi[tid] = MODE == kModeLifHalf ? p.bias[tid] * 0.5f : p.bias[tid];
+  }
   pdl_launch_dependents();
   pdl_wait();                                         // input and output belong to the stream
   const float* xin = p.x + static_cast<size_t>(b) * CIN * p.H * p.W;
@@ -179,76 +213,104 @@ stem_rows_kernel(const StemParams p) {
                 ? __ldg(xin + (static_cast<size_t>(ci) * p.H + ih) * p.W + iw) : 0.f;
   }
   __syncthreads();
-
-  const int warp = tid / 32, lane = tid % 32;
-  const int pxl = (warp >> 1) * 32 + lane;            // pixel within the block
-  const int ch0 = (warp & 1) * 32;
-  const int r = pxl / OW, c = pxl - (pxl / OW) * OW;
-  const bool in_tile = pxl < R * OW;
-  float acc[32];
+  // im2col row of this thread's pixel, split hi/lo.
+  const int px = tid;
+  const int r = px / OW, c = px - (px / OW) * OW;
+  const bool in_tile = px < R * OW;
 #pragma unroll
-  for (int j = 0; j < 32; ++j) acc[j] = 0.f;
-  if (in_tile) {
+  for (int k4 = 0; k4 < 8; ++k4) {
+    float hi[4], lo[4];
 #pragma unroll
-    for (int ci = 0; ci < CIN; ++ci) {
+    for (int j = 0; j < 4; ++j) {
+      const int k = 4 * k4 + j;
+      float xv = 0.f;
+      if (k < 9 * CIN && in_tile) {
+        const int ci = k / 9, kh = (k % 9) / 3, kw = k % 3;
+        xv = xs[ci * HWp + (r + kh) * OWp + c + kw];
+      }
+      hi[j] = to_tf32(xv);
+      lo[j] = xv - hi[j];
+    }
+    const int off = px * 128 + ((k4 ^ (px & 7)) << 4);
+    *reinterpret_cast<float4*>(sAh + off) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+    *reinterpret_cast<float4*>(sAl + off) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+  }
+  fence_proxy_async_smem();                           // generic writes -> tensor-core reads
+  tc_fence_before();
+  __syncthreads();
+  const uint32_t tmem = *tmem_slot;
+  if (tid == 0) {
+    tc_fence_after();
+    const uint32_t idesc = idesc_tf32(kStemPx, 64);
+    const uint64_t ah = smem_desc_kmajor(smem_u32(sAh), 1024, 2);
+    const uint64_t al = smem_desc_kmajor(smem_u32(sAl), 1024, 2);
+    const uint64_t bh = smem_desc_kmajor(smem_u32(sBh), 1024, 2);
+    const uint64_t bl = smem_desc_kmajor(smem_u32(sBl), 1024, 2);
+    constexpr int kSteps = (9 * CIN + 7) / 8;          // K = 8 per MMA (+32 bytes)
 #pragma unroll
-      for (int kh = 0; kh < 3; ++kh) {
+    for (int ks = 0; ks < kSteps; ++ks) {
+      mma_tf32(tmem, al + 2 * ks, bh + 2 * ks, idesc, ks > 0 ? 1u : 0u);
+      mma_tf32(tmem, ah + 2 * ks, bl + 2 * ks, idesc, 1u);
+    }
 #pragma unroll
-        for (int kw = 0; kw < 3; ++kw) {
-          const float xv = xs[ci * HWp + (r + kh) * OWp + c + kw];
-          const float4* wr = reinterpret_cast<const float4*>(ws + ((ci * 3 + kh) * 3 + kw) * 64 + ch0);
+    for (int ks = 0; ks < kSteps; ++ks) mma_tf32(tmem, ah + 2 * ks, bh + 2 * ks, idesc, 1u);
+    mma_commit(bar);
+  }
+  const bool ok = mbar_wait_bounded(bar, 0, p.timeout);
+  if (!ok && p.err) atomicOr(p.err, kErrTimeoutAcc);
+  tc_fence_after();
+  const bool all_ok = __syncthreads_and(ok);
+  if (all_ok) {
+    // Thread = pixel = TMEM lane; BN once for the 64 channels.
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    float x[64], v[64];
 #pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const float4 w4 = wr[q];
-            acc[4 * q + 0] = fmaf(xv, w4.x, acc[4 * q + 0]);
-            acc[4 * q + 1] = fmaf(xv, w4.y, acc[4 * q + 1]);
-            acc[4 * q + 2] = fmaf(xv, w4.z, acc[4 * q + 2]);
-            acc[4 * q + 3] = fmaf(xv, w4.w, acc[4 * q + 3]);
+    for (int h = 0; h < 2; ++h) {
+      float a[32];
+      tmem_ld32(lane_base + 32 * h, a);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        x[32 * h + j] = fmaf(a[j], sc[32 * h + j], bi[32 * h + j]);
+        v[32 * h + j] = 0.f;
+      }
+    }
+    const int nrows = min(R, p.OH - oh0);
+    const int n16 = nrows * OW * 8;                   // 16-byte chunks of the block's output
+    const long long P = static_cast<long long>(p.B) * p.OH * OW;
+    for (int t = 0; t < p.T; ++t) {
+      uint8_t* tile = smem + (t & 1) * kStemATile;    // the A tiles are free after the MMAs
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        uint32_t w[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          uint32_t bits = 0;
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int j = 8 * q + 2 * u + e;
+            if (neuron_step<MODE>(v[j], x[j], p.decay, p.tau, p.v_th, p.v_reset))
+              bits |= 0x3C00u << (16 * e);
           }
+          w[u] = bits;
         }
+        *reinterpret_cast<uint4*>(tile + px * 128 + ((q ^ (px & 7)) << 4)) =
+            make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      __syncthreads();
+      uint4* dst = reinterpret_cast<uint4*>(
+          p.out + ((static_cast<size_t>(t) * P + static_cast<size_t>(b) * p.OH * OW +
+                    static_cast<size_t>(oh0) * OW) * 64));
+      for (int i = tid; i < n16; i += kStemThreads) {
+        const int pp = i >> 3, cg = i & 7;
+        dst[i] = *reinterpret_cast<const uint4*>(tile + pp * 128 + ((cg ^ (pp & 7)) << 4));
       }
     }
   }
-  // BN output (pre-scaled by 1/2 for the tau = 2 LIF step, as in the conv epilogues).
-  float v[32];
-#pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    const float s = MODE == kModeLifHalf ? sc[ch0 + j] * 0.5f : sc[ch0 + j];
-    const float o = MODE == kModeLifHalf ? bi[ch0 + j] * 0.5f : bi[ch0 + j];
-    acc[j] = fmaf(acc[j], s, o);
-    v[j] = 0.f;
-  }
-  const int nrows = min(R, p.OH - oh0);
-  const int n16 = nrows * OW * 8;                     // 16-byte chunks of the block's output
-  const long long P = static_cast<long long>(p.B) * p.OH * OW;
-  for (int t = 0; t < p.T; ++t) {
-    uint8_t* tile = tiles + (t & 1) * (kStemPx * 128);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      uint32_t w[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        uint32_t bits = 0;
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int j = 8 * q + 2 * u + e;
-          if (neuron_step<MODE>(v[j], acc[j], p.decay, p.tau, p.v_th, p.v_reset))
-            bits |= 0x3C00u << (16 * e);
-        }
-        w[u] = bits;
-      }
-      const int cg = (ch0 >> 3) + q;
-      *reinterpret_cast<uint4*>(tile + pxl * 128 + ((cg ^ (pxl & 7)) << 4)) =
-          make_uint4(w[0], w[1], w[2], w[3]);
-    }
-    __syncthreads();
-    uint4* dst = reinterpret_cast<uint4*>(
-        p.out + ((static_cast<size_t>(t) * P + static_cast<size_t>(b) * p.OH * OW +
-                  static_cast<size_t>(oh0) * OW) * 64));
-    for (int i = tid; i < n16; i += kStemThreads) {
-      const int px = i >> 3, cg = i & 7;
-      dst[i] = *reinterpret_cast<const uint4*>(tile + px * 128 + ((cg ^ (px & 7)) << 4));
-    }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 64);
   }
 }
 
