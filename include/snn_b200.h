@@ -158,6 +158,25 @@ int snn_head_forward(int32_t T, int32_t B, int32_t HW, int32_t C, int32_t NC,
                      const void* x, const float* fc_w, const float* fc_b, float* logits,
                      void* stream);
 
+/* Fused Add + neuron over T: out = spikes of neuron(a + b) (the reference's
+ * add_lif_fused_kernel, sengine/kernels/add_lif_fused.py:19-75, pattern
+ * Add -> LIF, with the model's LIF/IF, models/neurons.py:121-146).
+ * Shape from d: T, B, H, W and d->Cout channels (multiple of 8); neuron,
+ * tau, v_threshold, v_reset and the state flags as for the conv.
+ *   a, b   [T*B][H][W][C] fp16;   out [T*B][H][W][C] fp16 spikes
+ *   state  [B*H*W][C] fp32 membrane */
+int snn_add_lif_forward(const snn_conv_desc* d, const void* a, const void* b, float* state,
+                        void* out, void* stream);
+
+/* Fused MaxPool2d + neuron over T: out = spikes of neuron(maxpool(x)) (the
+ * reference's maxpool_lif_fused_kernel, sengine/kernels/pool_lif_fused.py:
+ * 15-79).  Window d->KH x d->KW, d->stride, d->pad (padding never wins the
+ * max, as in torch MaxPool2d); channels d->Cin == d->Cout (multiple of 8).
+ *   x      [T*B][H][W][C] fp16;   out [T*B][OH][OW][C] fp16 spikes
+ *   state  [B*OH*OW][C] fp32 membrane */
+int snn_maxpool_lif_forward(const snn_conv_desc* d, const void* x, float* state, void* out,
+                            void* stream);
+
 /* Spikformer attention core + attention LIF (the FusedSpikformerAttention op,
  * sengine/tdl/attention_ops.py:50-82 and :85-105; model semantics
  * models/spikformer.py:122-127 with attn_lif = MultiStepLIFNeuron(tau,

@@ -16,6 +16,8 @@ lif_layer  numpy restatement of Conv2d + BatchNorm2d(eval) + multi-step LIF
            ``models/sewresnet.py:50-66`` for the SEW residual add).
 attention  numpy restatement of the Spikformer attention core + attention
            LIF (``models/spikformer.py:97,122-127``).
+glue       numpy restatement of the Add -> LIF and MaxPool2d -> LIF patterns
+           (``models/neurons.py``; torch ``MaxPool2d`` semantics).
 sew_resnet torch-CPU port of the reference SEW-ResNet-18 forward
            (``models/sewresnet.py:123-210``) with the CIFAR stem, used as the
            timed CPU baseline and for end-to-end logit sanity checks.

@@ -477,6 +477,69 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
 
 }  // namespace
 
+namespace {
+using GlueKernel = void (*)(const snn::GlueParams);
+template <bool POOL>
+GlueKernel glue_fn(int mode) {
+  if (mode == snn::kModeLifHalf) return snn::glue_neuron_kernel<snn::kModeLifHalf, POOL>;
+  if (mode == snn::kModeLifDiv) return snn::glue_neuron_kernel<snn::kModeLifDiv, POOL>;
+  return snn::glue_neuron_kernel<snn::kModeIf, POOL>;
+}
+
+// Shared checks and launch of the Add / MaxPool + neuron glue.
+int launch_glue(const snn_conv_desc* d, bool pool, const void* a, const void* b, float* state,
+                void* out, void* stream) {
+  int st = ensure_init();
+  if (st) return st;
+  if (!d || !a || (!pool && !b) || !out) return fail(SNN_E_INVALID, "null pointer");
+  if (d->T < 1 || d->B < 1 || d->H < 1 || d->W < 1 || d->Cout < 8 || d->Cout % 8)
+    return fail(SNN_E_INVALID, "bad shape (channels a positive multiple of 8)");
+  if (d->neuron != SNN_NEURON_LIF && d->neuron != SNN_NEURON_IF)
+    return fail(SNN_E_INVALID, "neuron must be LIF or IF");
+  if (d->neuron == SNN_NEURON_LIF && !(d->tau > 0.0f)) return fail(SNN_E_INVALID, "tau must be positive");
+  if ((d->flags & (SNN_FLAG_READ_STATE | SNN_FLAG_WRITE_STATE)) && !state)
+    return fail(SNN_E_INVALID, "state flags set but state is null");
+  if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
+       reinterpret_cast<uintptr_t>(out)) & 15)
+    return fail(SNN_E_INVALID, "tensors must be 16-byte aligned");
+  snn::GlueParams p;
+  memset(&p, 0, sizeof(p));
+  p.a = static_cast<const __half*>(a);
+  p.b = static_cast<const __half*>(b);
+  p.out = static_cast<__half*>(out);
+  p.state = state;
+  p.T = d->T; p.B = d->B; p.H = d->H; p.W = d->W; p.C = d->Cout; p.flags = d->flags;
+  if (pool) {
+    if (d->Cin != d->Cout) return fail(SNN_E_INVALID, "max pool keeps the channel count (Cin == Cout)");
+    if (d->KH < 1 || d->KW < 1 || d->stride < 1 || d->pad < 0 || 2 * d->pad > std::min(d->KH, d->KW))
+      return fail(SNN_E_INVALID, "bad pool window (pad at most half the window)");
+    p.KH = d->KH; p.KW = d->KW; p.stride = d->stride; p.pad = d->pad;
+    p.OH = (d->H + 2 * d->pad - d->KH) / d->stride + 1;
+    p.OW = (d->W + 2 * d->pad - d->KW) / d->stride + 1;
+    if (p.OH < 1 || p.OW < 1) return fail(SNN_E_INVALID, "empty output");
+  } else {
+    p.OH = d->H; p.OW = d->W;
+  }
+  const long long total_in = static_cast<long long>(d->T) * d->B * d->H * d->W * d->Cout;
+  if (total_in > (1LL << 40)) return fail(SNN_E_INVALID, "tensors too large");
+  p.tau = d->tau;
+  // Reference computes (1.0 - 1.0/tau) in double, then float32 (models/neurons.py:125).
+  p.decay = d->neuron == SNN_NEURON_LIF ? static_cast<float>(1.0 - 1.0 / static_cast<double>(d->tau)) : 1.0f;
+  p.v_th = d->v_threshold; p.v_reset = d->v_reset;
+  const int mode = d->neuron == SNN_NEURON_IF ? snn::kModeIf
+                   : d->tau == 2.0f ? snn::kModeLifHalf : snn::kModeLifDiv;
+  const long long n = static_cast<long long>(d->B) * p.OH * p.OW * (d->Cout / 8);
+  const long long blocks = std::max<long long>(1, std::min<long long>((n + 255) / 256,
+                                                                    static_cast<long long>(g_num_sms) * 16));
+  cudaError_t e = pool ? launch_pdl(glue_fn<true>(mode), dim3(static_cast<unsigned>(blocks)), dim3(256),
+                                    0, stream, p)
+                       : launch_pdl(glue_fn<false>(mode), dim3(static_cast<unsigned>(blocks)), dim3(256),
+                                    0, stream, p);
+  if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));
+  return SNN_OK;
+}
+}  // namespace
+
 extern "C" {
 
 int snn_abi_version(void) { return SNN_ABI_VERSION; }
@@ -679,6 +742,16 @@ int snn_head_forward(int32_t T, int32_t B, int32_t HW, int32_t C, int32_t NC, co
                              static_cast<const __half*>(x), fc_w, fc_b, logits, T, B, HW, C, NC);
   if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));
   return SNN_OK;
+}
+
+int snn_add_lif_forward(const snn_conv_desc* d, const void* a, const void* b, float* state,
+                        void* out, void* stream) {
+  return launch_glue(d, false, a, b, state, out, stream);
+}
+
+int snn_maxpool_lif_forward(const snn_conv_desc* d, const void* x, float* state, void* out,
+                            void* stream) {
+  return launch_glue(d, true, x, nullptr, state, out, stream);
 }
 
 int snn_spikformer_attn_forward(int32_t T, int32_t B, int32_t N, int32_t heads,

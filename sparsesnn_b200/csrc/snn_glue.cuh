@@ -314,6 +314,107 @@ stem_tc_kernel(const StemParams p) {
   }
 }
 
+// ------------------------------------------------ elementwise neuron glue
+// Fused Add + neuron and MaxPool + neuron over T (the reference's
+// add_lif_fused_kernel and maxpool_lif_fused_kernel,
+// sengine/kernels/add_lif_fused.py:19-75 and pool_lif_fused.py:15-79), with
+// the neuron of the model (LIF v*(1-1/tau) + x/tau, or IF, hard reset).
+// Memory-bound: thread = (output pixel, 8 channels), 16-byte loads and
+// stores, membrane in registers across the T timesteps.
+struct GlueParams {
+  const __half* a;     // Add: [T][P][C]; MaxPool: input [T][B][H][W][C]
+  const __half* b;     // Add: second input [T][P][C]
+  __half* out;         // [T][B][OH][OW][C] spikes
+  float* state;        // [B*OH*OW][C] membrane or null
+  int T, B, H, W, C, OH, OW, KH, KW, stride, pad, flags;
+  float tau, decay, v_th, v_reset;
+};
+
+template <int MODE>
+__device__ __forceinline__ uint4 glue_neuron8(float (&v)[8], const float (&x)[8], const GlueParams& p) {
+  uint32_t w[4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    uint32_t bits = 0;
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int j = 2 * u + e;
+      // kModeLifHalf takes the input pre-halved (exact).
+      const float xi = MODE == kModeLifHalf ? x[j] * 0.5f : x[j];
+      if (neuron_step<MODE>(v[j], xi, p.decay, p.tau, p.v_th, p.v_reset)) bits |= 0x3C00u << (16 * e);
+    }
+    w[u] = bits;
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+template <int MODE, bool POOL>
+__global__ void __launch_bounds__(256)
+glue_neuron_kernel(const GlueParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int c8n = p.C / 8;
+  const long long P = static_cast<long long>(p.B) * p.OH * p.OW;
+  const long long n = P * c8n;
+  for (long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; idx < n;
+       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long pix = idx / c8n;
+    const int c8 = static_cast<int>(idx - pix * c8n);
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      v[j] = (p.flags & kReadState) ? p.state[pix * p.C + c8 * 8 + j] : 0.f;
+    for (int t = 0; t < p.T; ++t) {
+      float x[8];
+      if constexpr (POOL) {
+        const int ow = static_cast<int>(pix % p.OW);
+        const int oh = static_cast<int>((pix / p.OW) % p.OH);
+        const int b = static_cast<int>(pix / (static_cast<long long>(p.OW) * p.OH));
+        __half2 m[4];
+        const __half2 ninf = __halves2half2(__ushort_as_half(0xFC00), __ushort_as_half(0xFC00));
+#pragma unroll
+        for (int j = 0; j < 4; ++j) m[j] = ninf;
+        for (int kh = 0; kh < p.KH; ++kh) {
+          const int ih = oh * p.stride + kh - p.pad;
+          if (ih < 0 || ih >= p.H) continue;
+          for (int kw = 0; kw < p.KW; ++kw) {
+            const int iw = ow * p.stride + kw - p.pad;
+            if (iw < 0 || iw >= p.W) continue;
+            const uint4 u = __ldg(reinterpret_cast<const uint4*>(
+                p.a + (((static_cast<size_t>(t) * p.B + b) * p.H + ih) * p.W + iw) * p.C) + c8);
+            const __half2* hv = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) m[j] = __hmax2(m[j], hv[j]);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __half22float2(m[j]);
+          x[2 * j] = f.x; x[2 * j + 1] = f.y;
+        }
+      } else {
+        const size_t off = (static_cast<size_t>(t) * P + pix) * p.C;
+        const uint4 ua = __ldg(reinterpret_cast<const uint4*>(p.a + off) + c8);
+        const uint4 ub = __ldg(reinterpret_cast<const uint4*>(p.b + off) + c8);
+        const __half2* ha = reinterpret_cast<const __half2*>(&ua);
+        const __half2* hb = reinterpret_cast<const __half2*>(&ub);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 fa = __half22float2(ha[j]), fb = __half22float2(hb[j]);
+          x[2 * j] = fa.x + fb.x;                      // exact: two fp16 values
+          x[2 * j + 1] = fa.y + fb.y;
+        }
+      }
+      reinterpret_cast<uint4*>(p.out + (static_cast<size_t>(t) * P + pix) * p.C)[c8] =
+          glue_neuron8<MODE>(v, x, p);
+    }
+    if (p.flags & kWriteState) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) p.state[pix * p.C + c8 * 8 + j] = v[j];
+    }
+  }
+}
+
 // One block (1024 threads) per image.  Phase 1: thread (c8, slot) sums 8
 // consecutive channels (16-byte loads) over every 16th (t, hw) position; the
 // partial sums are combined in shared memory and scaled: feat = sum / HW / T

@@ -225,6 +225,32 @@ def attention_case(ref_path, name, *, T, B, N, heads, hd, p_spike, seed):
     print("wrote attn", name, tuple(q.shape), "spike rate", float(model.mean()))
 
 
+def glue_case(ref):
+    """MaxPool2d(3, 2, 1) -> MultiStepLIFNeuron and Add -> MultiStepLIFNeuron /
+    MultiStepIFNeuron through the reference modules (the patterns of
+    ``sengine/kernels/pool_lif_fused.py`` and ``add_lif_fused.py``)."""
+    import torch
+    import torch.nn as nn
+    g = torch.Generator().manual_seed(21)
+    T, B, C, H, W = 4, 2, 64, 9, 10
+    x = (torch.randn((T, B, C, H, W), generator=g) * 1.5).half().float()
+    pool = ref["SeqToANNContainer"](nn.MaxPool2d(3, 2, 1))
+    with torch.no_grad():
+        pooled = pool(x)
+        s_pool = ref["MultiStepLIFNeuron"](tau=2.0, v_threshold=1.0, v_reset=0.0)(pooled)
+    a = (torch.randn((T, B, C, H, W), generator=g)).half().float()
+    b = torch.randint(0, 3, (T, B, C, H, W), generator=g).float()
+    with torch.no_grad():
+        s_add = ref["MultiStepLIFNeuron"](tau=2.0, v_threshold=1.0, v_reset=0.0)(a + b)
+        s_add_if = ref["MultiStepIFNeuron"](v_threshold=1.0, v_reset=0.0)(a + b)
+    np.savez_compressed(HERE / "glue.npz", x=x.numpy(), pooled=pooled.numpy(),
+                        s_pool=s_pool.numpy().astype(np.uint8), a=a.numpy(), b=b.numpy(),
+                        s_add=s_add.numpy().astype(np.uint8),
+                        s_add_if=s_add_if.numpy().astype(np.uint8))
+    print("wrote glue", tuple(x.shape), "pool rate", float(s_pool.mean()), "add rate",
+          float(s_add.mean()))
+
+
 def prune_case(ref):
     import torch
     g = torch.Generator().manual_seed(7)
@@ -302,6 +328,7 @@ def main():
     attention_case(a.ref, "n64", T=4, B=2, N=64, heads=2, hd=32, p_spike=0.13, seed=11)
     attention_case(a.ref, "n196", T=4, B=2, N=196, heads=2, hd=32, p_spike=0.09, seed=12)
     attention_case(a.ref, "n100h64", T=3, B=2, N=100, heads=2, hd=64, p_spike=0.09, seed=13)
+    glue_case(ref)
     model_case(ref, HERE.parent.parent)
 
 

@@ -69,6 +69,19 @@ def test_attention_matches_reference(name):
     assert np.array_equal(spk, g["spikes"].astype(np.float32))
 
 
+def test_glue_matches_reference():
+    """MaxPool2d -> LIF and Add -> LIF / IF against the reference modules."""
+    from oracle.glue import add_lif, maxpool2d, maxpool_lif
+    g = np.load(GOLDEN / "glue.npz")
+    x = g["x"]
+    t, b = x.shape[:2]
+    pooled = maxpool2d(x.reshape((t * b,) + x.shape[2:]), 3, 2, 1)
+    assert np.array_equal(pooled.reshape(g["pooled"].shape), g["pooled"])
+    assert np.array_equal(maxpool_lif(x, 3, 2, 1)[0], g["s_pool"].astype(np.float32))
+    assert np.array_equal(add_lif(g["a"], g["b"])[0], g["s_add"].astype(np.float32))
+    assert np.array_equal(add_lif(g["a"], g["b"], neuron="if")[0], g["s_add_if"].astype(np.float32))
+
+
 def test_sew18_forward_matches_reference_model():
     from oracle.sew_resnet import forward_torch, make_params
     m = np.load(GOLDEN / "sew18_logits.npz")
