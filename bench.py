@@ -140,6 +140,52 @@ def spikformer_attention(dev, stream, hbm_peak, iters=12, sets=4):
             "l2": f"{sets} input sets rotated"}
 
 
+def glue_kernels(dev, stream, hbm_peak, iters=10):
+    """The fused MaxPool + LIF (SEW/MS-ResNet ImageNet stem shape: T=4, batch
+    32, 64 channels, 112x112 -> 56x56, 3x3 s2 p1) and Add + LIF (T=4, batch
+    128, 64 channels, 32x32) kernels: CUDA-event time per call and HBM
+    throughput of the algorithmic bytes (inputs read once, spikes written
+    once; every buffer set is larger than L2 or rotated)."""
+    import torch
+    from sparsesnn_b200 import runtime as rt
+    lib = rt.load()
+    s = stream.cuda_stream
+    res = {}
+    T, B, C, H = 4, 32, 64, 112
+    d = rt.make_desc(T=T, B=B, Cin=C, H=H, W=H, Cout=C, KH=3, KW=3, stride=2, pad=1)
+    x = torch.randn((T * B, H, H, C), device=dev).half()
+    y = torch.empty((T * B, H // 2, H // 2, C), dtype=torch.float16, device=dev)
+    nbytes = x.numel() * 2 + y.numel() * 2
+    runs = {"maxpool_lif": (lambda: rt.check(lib.snn_maxpool_lif_forward(d, x.data_ptr(), None,
+                                                                         y.data_ptr(), s)), nbytes)}
+    T2, B2, H2 = 4, 128, 32
+    d2 = rt.make_desc(T=T2, B=B2, Cin=C, H=H2, W=H2, Cout=C, KH=1, KW=1)
+    ab = [[torch.randn((T2 * B2, H2, H2, C), device=dev).half() for _ in range(2)] for _ in range(2)]
+    z = torch.empty((T2 * B2, H2, H2, C), dtype=torch.float16, device=dev)
+    cnt = [0]
+
+    def add_call():
+        a, b = ab[cnt[0] % 2]
+        cnt[0] += 1
+        rt.check(lib.snn_add_lif_forward(d2, a.data_ptr(), b.data_ptr(), None, z.data_ptr(), s))
+    runs["add_lif"] = (add_call, 3 * z.numel() * 2)
+    for name, (fn, nb) in runs.items():
+        for _ in range(3):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(iters):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / iters
+        gbs = nb / (ms / 1000.0) / 1e9
+        res[name] = {"us": round(ms * 1000.0, 2), "GB/s": round(gbs, 1),
+                     "frac": round(gbs / hbm_peak, 4), "bytes": nb}
+    return res
+
+
 def cpu_reference_images_per_s(steps, sample, threads, warmup=1):
     """Time the oracle's port of the reference PyTorch forward on CPU."""
     import torch
@@ -343,6 +389,7 @@ def run_ours(args, rank, world, local_rank):
 
     linear = spikformer_linear_layers(dev, stream, sparse_peak) if rank == 0 else None
     attn = spikformer_attention(dev, stream, hbm_peak) if rank == 0 else None
+    glue = glue_kernels(dev, stream, hbm_peak) if rank == 0 else None
     if rt.device_error() != 0:
         raise RuntimeError("a kernel reported a device error")
 
@@ -376,6 +423,7 @@ def run_ours(args, rank, world, local_rank):
                 "layer_ms": {k: round(v, 4) for k, v in per_layer.items()},
                 "spikformer_linear": linear,
                 "spikformer_attention": attn,
+                "glue": glue,
                 "clocks": dict(clk.summary(), window="timed region plus 300 replays before and 200 after"),
                 "cpu_baseline": cpu}
         print(json.dumps(line), flush=True)
