@@ -120,7 +120,15 @@ class SEWResNet18:
         cout, cin, kh, kw = st["w"].shape
         self.stem_desc = rt.make_desc(T=T, B=batch, Cin=cin, H=H, W=W, Cout=cout, KH=kh, KW=kw,
                                       stride=1, pad=kh // 2, tau=tau, v_threshold=v_threshold)
-        self.x_in = torch.empty((batch, cin, H, W), dtype=torch.float32, device=dev)
+        # Two input buffers: the host->device copy of the next call's images
+        # (on a copy stream) overlaps the forward that reads the other one.
+        self.x_ins = [torch.empty((batch, cin, H, W), dtype=torch.float32, device=dev)
+                      for _ in range(2)]
+        self.x_in = self.x_ins[0]
+        self._in_sel = 0                  # input buffer the launches read
+        self._next_buf = 0
+        self._copy_stream = torch.cuda.Stream(dev)
+        self._buf_free = [None, None]     # event: last forward reading buffer k is done
         self.a0 = torch.empty((T * batch, H, W, cout), dtype=torch.float16, device=dev)
         kw_ = dict(T=T, B=batch, tau=tau, v_threshold=v_threshold, device=dev)
         self.blocks = []
@@ -164,7 +172,7 @@ class SEWResNet18:
 
         def stem():
             s = torch.cuda.current_stream(self.device).cuda_stream
-            rt.check(lib.snn_stem_forward(self.stem_desc, 1, self.x_in.data_ptr(),
+            rt.check(lib.snn_stem_forward(self.stem_desc, 1, self.x_ins[self._in_sel].data_ptr(),
                                           self.stem_w.data_ptr(), self.stem_scale.data_ptr(),
                                           self.stem_bias.data_ptr(), self.a0.data_ptr(), s))
         ops.append(("stem", stem))
@@ -201,30 +209,63 @@ class SEWResNet18:
         return self._ops_cache
 
     def capture(self, warmup=3):
-        """Capture one forward into a CUDA graph (after eager warm-ups)."""
+        """Capture the forward into CUDA graphs (after eager warm-ups), one
+        per input buffer; returns the graph that reads ``x_in``."""
         s = torch.cuda.Stream(self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(s):
             for _ in range(warmup):
                 self.run()
         torch.cuda.current_stream(self.device).wait_stream(s)
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            self.run()
-        self._graph = g
-        return g
+        self._graphs = []
+        for k in range(2):
+            self._in_sel = k
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self.run()
+            self._graphs.append(g)
+        self._in_sel = 0
+        self._graph = self._graphs[0]
+        return self._graph
 
     def replay(self):
+        """Replay the forward on the images in ``x_in``."""
         self._graph.replay()
         return self.logits
 
     def __call__(self, x):
         """Public API: images ``[B, C, H, W]`` fp32 (host or device) -> logits
-        (device tensor, valid until the next call)."""
-        self.x_in.copy_(x, non_blocking=True)
+        (device tensor on the current stream, valid until the next call).
+
+        The images go to the device on a copy stream into the input buffer
+        the previous forward is not reading, so when calls follow each other
+        the copy of one batch overlaps the forward of the previous one; the
+        forward itself is ordered after its copy on the current stream.
+        ``x`` (pinned host memory for an asynchronous copy) must stay
+        unchanged until the forward that reads it has started."""
+        cur = torch.cuda.current_stream(self.device)
+        k = self._next_buf
+        self._next_buf ^= 1
+        cs = self._copy_stream
+        if self._buf_free[k] is not None:
+            cs.wait_event(self._buf_free[k])
+        else:
+            cs.wait_stream(cur)
+        with torch.cuda.stream(cs):
+            self.x_ins[k].copy_(x, non_blocking=True)
+            copied = torch.cuda.Event()
+            copied.record(cs)
+        cur.wait_event(copied)
         if self._graph is not None:
-            return self.replay()
-        return self.run()
+            self._graphs[k].replay()
+        else:
+            self._in_sel = k
+            self.run()
+            self._in_sel = 0
+        done = torch.cuda.Event()
+        done.record(cur)
+        self._buf_free[k] = done
+        return self.logits
 
     def spikes(self, name):
         """Device buffer of a layer output by trace name (for tests)."""
