@@ -804,7 +804,10 @@ int snn_spikformer_attn_forward(int32_t T, int32_t B, int32_t N, int32_t heads,
   // Reference computes (1.0 - 1.0/tau) in double, then float32 (models/neurons.py:125).
   p.decay = static_cast<float>(1.0 - 1.0 / static_cast<double>(tau));
   p.timeout = 4000000000ull;
-  const dim3 grid(static_cast<unsigned>(B * heads));
+  // Persistent: one CTA per SM (about 200 KB of shared memory each) walks
+  // the (image, head) items.
+  const dim3 grid(static_cast<unsigned>(std::min<long long>(static_cast<long long>(B) * heads,
+                                                            g_num_sms)));
   cudaError_t e = head_dim == 32
       ? launch_pdl(snn::spikformer_attn_lif_kernel<32>, grid, dim3(snn::kAttnThreads),
                    snn::AttnCfg<32>::kSmemBytes, stream, p)

@@ -74,11 +74,13 @@ def test_spikformer_8_384_full_size(cuda_device, tau, v_th):
 
 
 def test_single_token_and_small_heads(cuda_device):
-    """Edge sizes: N = 1, N = 129 (a one-row second M-tile), head_dim 64."""
+    """Edge sizes: N = 1, N = 129 (a one-row second M-tile), N = 256, head_dim
+    64, several 64-channel groups per image."""
     from sparsesnn_b200 import runtime as rt
     rng = np.random.default_rng(9)
-    for N, hd, p in ((1, 32, 0.9), (129, 32, 0.1), (33, 64, 0.2), (256, 64, 0.06)):
-        T, B, heads = 2, 3, 3
+    for N, hd, heads, p in ((1, 32, 2, 0.9), (129, 32, 4, 0.1), (33, 64, 3, 0.2),
+                            (256, 64, 1, 0.06), (256, 32, 6, 0.06)):
+        T, B = 2, 3
         q, k, v = ((rng.random((T * B, N, heads * hd)) < p).astype(np.float32) for _ in range(3))
         y = run_attn(q, k, v, T=T, heads=heads)
         assert rt.device_error() == 0
