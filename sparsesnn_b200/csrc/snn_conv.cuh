@@ -247,7 +247,7 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
     for (int b = 0; b < kNumAcc; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], kEpiThreads); }
-    mbar_init(meta_ready, 128);
+    mbar_init(meta_ready, kEpiThreads);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -388,14 +388,31 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
     const int half = e >> 2;                     // which 32 pixel columns
     const int row = q * 32 + lane;               // output channel within the tile
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
-    if (half == 0) {
+    {
+      // 2:4 metadata into TMEM before the first MMA: the two warps of a lane
+      // quarter take half of the columns each, and a lane issues up to 40
+      // loads before storing them, so the MMAs wait for a few global round
+      // trips rather than one per 8 columns (a TMEM store orders the loads
+      // after it).  Columns past n_meta get the all-zero pattern (0x4).
+      constexpr int kChunk = 40;
       const uint32_t* src = p.meta + (static_cast<size_t>(m_tile) * n_meta) * kBM + row;
-      for (int j = 0; j < n_meta; j += 8) {
-        uint32_t r[8];
+      const int hcols = (n_meta + 15) / 16 * 8;          // columns per warp, multiple of 8
+      const int c_begin = half * hcols, c_end = c_begin + hcols;
+      for (int j = c_begin; j < c_end; j += kChunk) {
+        uint32_t r[kChunk];
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-          r[i] = (j + i < n_meta) ? __ldg(src + static_cast<size_t>(j + i) * kBM) : 0x44444444u;
-        tmem_st8(lane_base + kMetaCol + j, r);
+        for (int i = 0; i < kChunk; ++i)
+          r[i] = (j + i < n_meta && j + i < c_end) ? __ldg(src + static_cast<size_t>(j + i) * kBM)
+                                                   : 0x44444444u;
+#pragma unroll
+        for (int u = 0; u < kChunk / 8; ++u) {
+          if (j + 8 * u < c_end) {
+            uint32_t r8[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) r8[i] = r[8 * u + i];
+            tmem_st8(lane_base + kMetaCol + j + 8 * u, r8);
+          }
+        }
       }
       tmem_st_wait();
       tc_fence_before();
