@@ -48,7 +48,14 @@ enum { SNN_NEURON_LIF = 0, SNN_NEURON_IF = 1, SNN_NEURON_NONE = 2 };
 enum { SNN_FLAG_READ_STATE = 1, SNN_FLAG_WRITE_STATE = 2,
        /* Always use the general kernel (streamed weights, per-tap activation
         * tiles) even where the halo kernel applies; for testing. */
-       SNN_FLAG_FORCE_GENERIC = 4 };
+       SNN_FLAG_FORCE_GENERIC = 4,
+       /* Run eligible general-kernel layers (3x3, four-timestep 64-pixel
+        * tiles, an even number of 128-channel tiles) on CTA pairs: 2-CTA
+        * clusters sharing one M = 256 MMA, each CTA loading half of the
+        * activations.  Measured 2-4 us faster per SEW-ResNet-18 stage-3/4
+        * layer in isolation but not faster inside the whole-forward CUDA
+        * graph, so it is not the default. */
+       SNN_FLAG_CTA_PAIR = 8 };
 
 /* Where the residual of a fused Add enters the epilogue (the reference's
  * pattern strings and templates, sengine/kernels/interleaved_templates.py:371-397):

@@ -65,6 +65,21 @@ ConvKernel conv_kernel_fn_tc(int mode, int rm) {
 ConvKernel conv_kernel_fn(int mode, int rm, int tc) {
   return tc == 4 ? conv_kernel_fn_tc<4>(mode, rm) : conv_kernel_fn_tc<2>(mode, rm);
 }
+// CTA-pair variant (TC = 4; spiking modes with no residual or the SEW add).
+ConvKernel conv_pair_kernel_fn(int mode, int rm) {
+  const bool res = rm == snn::kResAddAfter;
+  switch (mode) {
+    case snn::kModeLifHalf:
+      return res ? snn::fused_sparse_conv_lif_kernel<snn::kModeLifHalf, snn::kResAddAfter, 4, true>
+                 : snn::fused_sparse_conv_lif_kernel<snn::kModeLifHalf, snn::kResNone, 4, true>;
+    case snn::kModeLifDiv:
+      return res ? snn::fused_sparse_conv_lif_kernel<snn::kModeLifDiv, snn::kResAddAfter, 4, true>
+                 : snn::fused_sparse_conv_lif_kernel<snn::kModeLifDiv, snn::kResNone, 4, true>;
+    default:
+      return res ? snn::fused_sparse_conv_lif_kernel<snn::kModeIf, snn::kResAddAfter, 4, true>
+                 : snn::fused_sparse_conv_lif_kernel<snn::kModeIf, snn::kResNone, 4, true>;
+  }
+}
 
 using HaloKernel = void (*)(const snn::HaloParams);
 
@@ -137,6 +152,26 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
+// Same for a kernel launched as 2-CTA clusters (grid.x even).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl_pair(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, void* stream,
+                            Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 2;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 constexpr int kHaloMaxWeightBytes = 160 * 1024;
 
 int ensure_init() {
@@ -192,6 +227,10 @@ int ensure_init() {
   }
   e = cudaFuncSetAttribute(snn::spikformer_attn_lif_kernel<32>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, snn::AttnCfg<32>::kSmemBytes);
+  for (int mode = 0; mode < 3 && e == cudaSuccess; ++mode)
+    for (int rm = 0; rm < 2 && e == cudaSuccess; ++rm)
+      e = cudaFuncSetAttribute(conv_pair_kernel_fn(mode, rm), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               snn::GenCfg<4, true>::kSmemBytes);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(snn::spikformer_attn_lif_kernel<64>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, snn::AttnCfg<64>::kSmemBytes);
@@ -331,9 +370,15 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
   // wider MMAs win even though a CTA's next tile then waits for the
   // epilogue to drain the accumulator -- else two (N = 128, double-buffered).
   const int tc = (d->T % 4 == 0 && p.box_bytes == snn::kBBytes) ? 4 : 2;
+  // CTA pairs (on request) for those layers when the 128-channel tiles come
+  // in pairs: each CTA loads half of the four-timestep activation box.  3x3
+  // only (the 1x1 downsamples measured slower).
+  const bool pair = (d->flags & SNN_FLAG_CTA_PAIR) && tc == 4 && p.n_m % 2 == 0 &&
+                    d->neuron != SNN_NEURON_NONE && d->KH * d->KW > 1 &&
+                    (rm == snn::kResNone || rm == snn::kResAddAfter);
   const cuuint32_t box5[5] = {static_cast<cuuint32_t>(snn::kKB), static_cast<cuuint32_t>(tw),
                               static_cast<cuuint32_t>(th), static_cast<cuuint32_t>(tn),
-                              static_cast<cuuint32_t>(tc)};
+                              static_cast<cuuint32_t>(pair ? tc / 2 : tc)};
   {
     const size_t C = d->Cin, W = d->W, H = d->H, B = d->B;
     const char* base = static_cast<const char*>(data);
@@ -461,6 +506,16 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
     cudaError_t e = launch_pdl(hs_kernel_fn(mode, residual != nullptr),
                                dim3(static_cast<unsigned>(grid)), dim3(snn::kHaloThreads),
                                snn::kHsSmemBytes, stream, ph);
+    if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));
+    return SNN_OK;
+  }
+  if (pair) {
+    const int n_pairs = p.n_m / 2;
+    const int per_pair = std::max(1, std::min(p.n_px_tiles, (g_num_sms / 2) / n_pairs));
+    const long long grid = 2LL * per_pair * n_pairs;
+    if (grid > 0x7fffffffLL) return fail(SNN_E_INVALID, "grid too large");
+    cudaError_t e = launch_pdl_pair(conv_pair_kernel_fn(mode, rm), dim3(static_cast<unsigned>(grid)),
+                                    dim3(snn::kThreads), snn::GenCfg<4, true>::kSmemBytes, stream, p);
     if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));
     return SNN_OK;
   }

@@ -13,8 +13,8 @@
 // Persistent CTAs: each CTA owns one 128-channel slice (so its metadata is
 // loaded once) and walks a strided list of pixel tiles.
 //
-// Warp roles (11 warps): 0 and 10 = TMA producers (pipeline fill i is issued
-// by producer i % 2), 1 = TMEM owner + MMA issuer, 2..9 = epilogue: two warps
+// Warp roles (12 warps): 0, 10 and 11 = TMA producers (pipeline fill i is issued
+// by producer i % 3), 1 = TMEM owner + MMA issuer, 2..9 = epilogue: two warps
 // per TMEM lane quarter, each owning 32 of the 64 pixel columns.  The epilogue applies BN, runs the LIF/IF recurrence over T
 // with the membrane in registers, stages fp16 spikes in a per-warp transpose
 // tile, adds the SEW residual and writes 16-byte vectors (see the store stage
@@ -37,11 +37,12 @@ constexpr int kTmemCols = 512;
 constexpr int kMaxMetaCols = kTmemCols - kMetaCol;  // => K <= 8192
 constexpr int kEpiWarps = 8;
 constexpr int kEpiThreads = kEpiWarps * 32;
-// TMA producers: warp 0 and warp 10.  One thread issues tensor copies one
-// after another (a few hundred cycles each, whatever the box size), so two
-// producer warps, each filling every other pipeline stage, keep enough
-// boxes in flight.
-constexpr int kProducers = 2;
+// TMA producers: warps 0, 10 and 11.  One thread issues tensor copies one
+// after another (a few hundred cycles each, whatever the box size), so
+// several producer warps, producer i filling pipeline stages i, i+3, ...,
+// keep the boxes coming; twelve warps (three per SM sub-partition) keep the
+// epilogue's register budget at 168.
+constexpr int kProducers = 3;
 constexpr int kThreads = (2 + kEpiWarps + kProducers - 1) * 32;
 constexpr int kXposeBytes = 32 * 32 * 2;         // per-warp [32 px][32 cout] fp16 transpose
 constexpr int kBarBytes = 512;
@@ -55,13 +56,24 @@ constexpr int kBarBytes = 512;
 //    metadata all change costs about 120 cycles up to N = 128 but runs at
 //    its operand rate (160 cycles) at N = 256, so this wins even though the
 //    next tile's MMAs wait for the epilogue to drain the single accumulator.
-template <int TC>
+//  * CG2 (TC = 4 only, on request): a CTA pair (2-CTA cluster) computes two
+//    adjacent 128-channel tiles of the same pixels with one M = 256 MMA
+//    issued by the leader; each CTA loads its own weights and HALF of the
+//    activation box (two of the four timesteps), so a CTA moves 24 KB per
+//    k-block instead of 40 KB (the one-CTA version's k-blocks are paced by
+//    that L2-to-SM feed, ~550 cycles against 320 of MMA).  Measured: the
+//    pair's k-blocks come every ~510 cycles (the MMA then reads the peer's
+//    half of B across the pair), layers 2-4 us faster in isolation, no
+//    faster inside the whole-forward graph.
+template <int TC, bool CG2 = false>
 struct GenCfg {
+  static_assert(!CG2 || TC == 4, "CTA pairs use the four-timestep tiles");
   static constexpr int kTC = TC;
   static constexpr int kNumAcc = TC == 4 ? 1 : 2;
-  static constexpr int kStages = TC == 4 ? 5 : 4;
+  static constexpr int kStages = CG2 ? 8 : TC == 4 ? 5 : 4;
   static constexpr int kKbPerStage = TC == 4 ? 1 : 2;
-  static constexpr int kStageBytes = kKbPerStage * (kABytes + kTC * kBBytes);
+  static constexpr int kBTs = CG2 ? TC / 2 : TC;     // timesteps of the box this CTA loads
+  static constexpr int kStageBytes = kKbPerStage * (kABytes + kBTs * kBBytes);
   static constexpr int kAccCols = kTC * kBN;
   static constexpr int kSmemBytes = kStages * kStageBytes + kEpiWarps * kXposeBytes + kBarBytes + 1024;
   static_assert(kNumAcc * kAccCols <= kMetaCol, "accumulators overlap the metadata columns");
@@ -210,12 +222,14 @@ __device__ __forceinline__ TileCoord tile_coord(const ConvParams& p, int pt) {
   return c;
 }
 
-template <int MODE, int RM, int TC>
+template <int MODE, int RM, int TC, bool CG2 = false>
 __global__ void __launch_bounds__(kThreads, 1)
 fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
   constexpr bool RES = RM != kResNone;
   static_assert(MODE != kModeNone || RM == kResNone, "a residual epilogue needs a neuron");
-  using Cfg = GenCfg<TC>;
+  static_assert(!CG2 || (MODE != kModeNone && RM <= kResAddAfter), "CTA pairs: spiking, SEW or none");
+  using Cfg = GenCfg<TC, CG2>;
+  constexpr int kBTs = Cfg::kBTs;
   constexpr int kTC = Cfg::kTC, kNumAcc = Cfg::kNumAcc, kStages = Cfg::kStages;
   constexpr int kKbPerStage = Cfg::kKbPerStage, kStageBytes = Cfg::kStageBytes;
   constexpr int kAccCols = Cfg::kAccCols;
@@ -238,25 +252,47 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
 
-  const int m_tile = blockIdx.x % p.n_m;
-  const int first_pt = blockIdx.x / p.n_m;
-  const int pt_step = gridDim.x / p.n_m;
+  // CTA pairs: cluster c owns the 128-channel tiles 2*(c % pairs) + rank of
+  // the pixel tiles c / pairs, c / pairs + clusters / pairs, ...
+  uint32_t rank = 0;
+  int m_tile, first_pt, pt_step;
+  if constexpr (CG2) {
+    rank = cluster_ctarank();
+    const int n_pairs = p.n_m / 2, cl = blockIdx.x >> 1;
+    m_tile = 2 * (cl % n_pairs) + static_cast<int>(rank);
+    first_pt = cl / n_pairs;
+    pt_step = (gridDim.x >> 1) / n_pairs;
+  } else {
+    m_tile = blockIdx.x % p.n_m;
+    first_pt = blockIdx.x / p.n_m;
+    pt_step = gridDim.x / p.n_m;
+  }
   const int n_chunks = (p.T + kTC - 1) / kTC;
   const int n_meta = 2 * p.n_kb;                               // sparse K steps (32 each)
+  // Pair: one arrival per epilogue warp of both CTAs on the leader's barriers.
+  constexpr int kEpiArrivals = CG2 ? 2 * kEpiWarps : kEpiThreads;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-    for (int b = 0; b < kNumAcc; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], kEpiThreads); }
-    mbar_init(meta_ready, kEpiThreads);
+    for (int b = 0; b < kNumAcc; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], kEpiArrivals); }
+    mbar_init(meta_ready, kEpiArrivals);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
+  if constexpr (CG2) cluster_sync();     // the peer's barriers exist before anything signals them
+  // The leader's barriers in the cluster window (for the follower's signals).
+  const uint32_t full_l = CG2 ? mapa_shared(smem_u32(full), 0) : 0u;
+  const uint32_t acc_empty_l = CG2 ? mapa_shared(smem_u32(acc_empty), 0) : 0u;
+  const uint32_t meta_ready_l = CG2 ? mapa_shared(smem_u32(meta_ready), 0) : 0u;
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&p.tmap_a);
     for (int i = 0; i < (p.stride == 2 ? 4 : 1); ++i) prefetch_tmap(&p.tmap_b[i]);
   }
-  if (warp == 1) { tmem_alloc(tmem_slot, kTmemCols); tmem_relinquish(); }
+  if (warp == 1) {
+    if constexpr (CG2) { tmem_alloc_pair(tmem_slot, kTmemCols); tmem_relinquish_pair(); }
+    else { tmem_alloc(tmem_slot, kTmemCols); tmem_relinquish(); }
+  }
   pdl_launch_dependents();
   tc_fence_before();
   __syncthreads();
@@ -287,11 +323,20 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
             // One activation box spans the chunk's kTC timesteps (a timestep
             // beyond T is outside the tensor: zero-filled, never read).
             const int nk = min(kKbPerStage, p.n_kb - kb0);
-            mbar_arrive_expect_tx(&full[stage], nk * (kABytes + kTC * p.box_bytes));
+            if constexpr (CG2) {
+              // The leader's barrier counts both CTAs' bytes.
+              if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * nk * (kABytes + kBTs * p.box_bytes));
+            } else {
+              mbar_arrive_expect_tx(&full[stage], nk * (kABytes + kTC * p.box_bytes));
+            }
             for (int j = 0; j < nk; ++j) {
               const int kb = kb0 + j;
-              tma_load_2d(sA + (stage * kKbPerStage + j) * kABytes, &p.tmap_a, &full[stage],
-                          kb * (kKB / 2), m_tile * kBM);
+              if constexpr (CG2)
+                tma_load_2d_pair(sA + (stage * kKbPerStage + j) * kABytes, &p.tmap_a,
+                                 full_l + stage * 8, kb * (kKB / 2), m_tile * kBM);
+              else
+                tma_load_2d(sA + (stage * kKbPerStage + j) * kABytes, &p.tmap_a, &full[stage],
+                            kb * (kKB / 2), m_tile * kBM);
               const int tap = kb / p.cin_blocks;
               const int cb = kb - tap * p.cin_blocks;
               const int kh = tap / p.KW, kw = tap - kh * p.KW;
@@ -300,8 +345,13 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
                 map = (hoff & 1) * 2 + (woff & 1);
                 hoff = floordiv2(hoff); woff = floordiv2(woff);
               }
-              tma_load_5d(sB + (stage * kKbPerStage + j) * kTC * kBBytes, &p.tmap_b[map], &full[stage],
-                          cb * kKB, tc.w0 + woff, tc.h0 + hoff, tc.n0, t0);
+              if constexpr (CG2)
+                tma_load_5d_pair(sB + (stage * kKbPerStage + j) * kBTs * kBBytes, &p.tmap_b[map],
+                                 full_l + stage * 8, cb * kKB, tc.w0 + woff, tc.h0 + hoff, tc.n0,
+                                 t0 + kBTs * static_cast<int>(rank));
+              else
+                tma_load_5d(sB + (stage * kKbPerStage + j) * kTC * kBBytes, &p.tmap_b[map], &full[stage],
+                            cb * kKB, tc.w0 + woff, tc.h0 + hoff, tc.n0, t0);
             }
             if (++stage == kStages) { stage = 0; phase ^= 1; }
           }
@@ -309,8 +359,10 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
       }
       // Let every load this producer issued land before the CTA can exit.
       // Only the last kStages fills can still be in flight, one per stage,
-      // so waiting on their parity cannot alias an older phase.
-      for (int back = max(0, seq - kStages); back < seq; ++back) {
+      // so waiting on their parity cannot alias an older phase.  (A pair's
+      // follower signals the leader's barriers; the leader's drain covers
+      // its loads, and the pair leaves together.)
+      for (int back = max(0, seq - kStages); back < seq && (!CG2 || rank == 0); ++back) {
         if (back % kProducers != prod) continue;
         if (!mbar_wait_bounded(&full[back % kStages], (back / kStages) & 1, p.timeout_ns))
           atomicOr(p.err, kErrTimeoutFull);
@@ -318,10 +370,15 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    if (lane == 0 && (!CG2 || rank == 0)) {
       const uint32_t idesc = idesc_f16(kBM, kBN, true);
-      const uint32_t idesc2 = idesc_f16(kBM, kTC * kBN, true);
+      const uint32_t idesc2 = idesc_f16(CG2 ? 2 * kBM : kBM, kTC * kBN, true);
       const bool merge_ts = p.box_bytes == kBBytes;   // tiles of exactly 64 pixels
+      if constexpr (CG2) {
+        // The pair's MMA needs 64-pixel tiles and whole four-timestep chunks
+        // (the host launches it only then).
+        if (!merge_ts || p.T % kTC) { atomicOr(p.err, kErrTimeoutMeta); *abort_flag = 1; }
+      }
       const uint64_t a_desc0 = smem_desc_kmajor(smem_u32(sA), 512, 4);
       const uint64_t b_desc0 = smem_desc_kmajor(smem_u32(sB), 1024, 2);
       if (!mbar_wait_bounded(meta_ready, 0, p.timeout_ns)) {
@@ -352,15 +409,19 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
               // Descriptors advance by adding (byte offset >> 4) to the start
               // address field (shared-memory addresses stay below 2^18).
               const uint64_t ad = a_desc0 + (((stage * kKbPerStage + j) * kABytes) >> 4);
-              const uint64_t bd = b_desc0 + (((stage * kKbPerStage + j) * kTC * kBBytes) >> 4);
+              const uint64_t bd = b_desc0 + (((stage * kKbPerStage + j) * kBTs * kBBytes) >> 4);
 #pragma unroll
               for (int s = 0; s < 2; ++s) {
                 const uint32_t ecol = kMetaCol + 2 * kb + s;
                 const uint32_t e_addr = tmem + (ecol & ~1u);
                 const uint32_t acc = (kb > 0 || s > 0) ? 1u : 0u;
-                if (merge_ts && tcn == kTC) {
-                  // Both timesteps' 64-pixel tiles are consecutive rows of the
-                  // box: one N = 128 MMA covers them.
+                if constexpr (CG2) {
+                  // Pair: M = 256 (this CTA's rows and the follower's), N = 256
+                  // (this CTA's two timesteps, then the follower's two).
+                  mma_sp_f16_pair(d_base, ad + 2 * s, bd + 4 * s, e_addr, idesc2 | (ecol & 1u), acc);
+                } else if (merge_ts && tcn == kTC) {
+                  // The chunk's timesteps' 64-pixel tiles are consecutive rows
+                  // of the box: one N = kTC * 64 MMA covers them.
                   mma_sp_f16(d_base, ad + 2 * s, bd + 4 * s, e_addr, idesc2 | (ecol & 1u), acc);
                 } else {
                   for (int tt = 0; tt < tcn; ++tt)
@@ -369,16 +430,19 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
                 }
               }
             }
-            mma_commit(&empty[stage]);
+            if constexpr (CG2) mma_commit_pair(&empty[stage], 0x3);
+            else mma_commit(&empty[stage]);
             if (++stage == kStages) { stage = 0; phase ^= 1; }
           }
           if (stop) break;
-          mma_commit(&acc_full[buf]);
+          if constexpr (CG2) mma_commit_pair(&acc_full[buf], 0x3);
+          else mma_commit(&acc_full[buf]);
           ++acc_iter;
         }
       }
       // Drain: every MMA issued so far completes before TMEM is released.
-      mma_commit(drain);
+      if constexpr (CG2) mma_commit_pair(drain, 0x1);
+      else mma_commit(drain);
       if (!mbar_wait_bounded(drain, 0, p.timeout_ns)) atomicOr(p.err, kErrTimeoutDrain);
     }
   } else {
@@ -416,7 +480,15 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
       }
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(meta_ready);
+      if constexpr (CG2) {
+        __syncwarp();
+        if (lane == 0) {
+          if (rank == 0) mbar_arrive(meta_ready);
+          else mbar_arrive_cluster(meta_ready_l);
+        }
+      } else {
+        mbar_arrive(meta_ready);
+      }
     }
 
     const int cout = m_tile * kBM + row;
@@ -489,7 +561,15 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
           tmem_wait_ld();
           if (t2 + 2 >= tcn) {                 // buffer drained: the MMAs it holds back may start
             tc_fence_before();
-            mbar_arrive(&acc_empty[buf]);
+            if constexpr (CG2) {
+              __syncwarp();
+              if (lane == 0) {
+                if (rank == 0) mbar_arrive(&acc_empty[buf]);
+                else mbar_arrive_cluster(acc_empty_l + buf * 8);
+              }
+            } else {
+              mbar_arrive(&acc_empty[buf]);
+            }
           }
           if constexpr (RES) {
             if (t2 > 0) {                      // later pairs: fetched now, used after the update
@@ -564,9 +644,11 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
 
   tc_fence_before();
   __syncthreads();
+  if constexpr (CG2) cluster_sync();     // the leader's MMAs no longer read the follower's tiles
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
+    if constexpr (CG2) tmem_dealloc_pair(tmem, kTmemCols);
+    else tmem_dealloc(tmem, kTmemCols);
   }
 }
 

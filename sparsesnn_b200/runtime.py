@@ -24,6 +24,7 @@ SNN_NEURON_NONE = 2
 SNN_FLAG_READ_STATE = 1
 SNN_FLAG_WRITE_STATE = 2
 SNN_FLAG_FORCE_GENERIC = 4
+SNN_FLAG_CTA_PAIR = 8
 SNN_VARIANT_GENERIC = 0
 SNN_VARIANT_HALO_RESIDENT = 1
 SNN_VARIANT_HALO_STREAM = 2

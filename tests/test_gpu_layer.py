@@ -438,3 +438,47 @@ def test_residual_modes_vs_oracle(cuda_device, T, mode, neuron, tau, neuron2, ta
         check_two_neuron(ys, v, v2, r)
     else:
         check_spikes_and_v(ys, v, r["spikes"], r["h"], r["v"])
+
+
+@pytest.mark.parametrize("cin, cout, hw, k, stride", [(256, 256, 8, 3, 1), (512, 512, 4, 3, 1),
+                                                     (256, 512, 8, 3, 2)],
+                         ids=["s3", "s4", "s4_strided"])
+@pytest.mark.parametrize("residual", [False, True], ids=["plain", "res"])
+@pytest.mark.parametrize("neuron", ["lif", "if"])
+def test_cta_pair_path(cuda_device, cin, cout, hw, k, stride, residual, neuron):
+    """Stage-3/4 shapes with an even number of 128-channel tiles on CTA pairs
+    (SNN_FLAG_CTA_PAIR: one M = 256 MMA per 2-CTA cluster); parity with the
+    oracle, and the same spikes and membranes as the one-CTA path."""
+    import torch
+    from sparsesnn_b200 import runtime as rt
+    from sparsesnn_b200.layer import SparseConvBNLIF, fold_bn
+    T, B = 4, 8
+    x, w, bn = L.make_config0(seed=cin + cout + hw + k, T=T, B=B, C=cin, F=cout, H=hw, W=hw, k=k)
+    scale, bias = fold_bn(bn.gamma, bn.beta, bn.mean, bn.var)
+    outs = []
+    for pair in (True, False):
+        layer = SparseConvBNLIF(w, scale, bias, T=T, B=B, H=hw, W=hw, stride=stride, pad=k // 2,
+                                neuron=neuron)
+        if pair:
+            layer.base_flags |= rt.SNN_FLAG_CTA_PAIR
+        oh, ow = layer.OH, layer.OW
+        rng = np.random.default_rng(7)
+        res_np = rng.integers(0, 3, (T, B, cout, oh, ow)).astype(np.float32) if residual else None
+        xd = torch.from_numpy(to_nhwc(x)).to("cuda", torch.float16)
+        rd = torch.from_numpy(to_nhwc(res_np)).to("cuda", torch.float16) if residual else None
+        st = torch.full(layer.state_shape(), 3.0, dtype=torch.float32, device="cuda")
+        y = layer(xd, state=st, residual=rd, read_state=False)
+        torch.cuda.synchronize()
+        assert rt.device_error() == 0
+        outs.append((y.float().cpu().numpy(), st.cpu().numpy()))
+    (y_pair, st_pair), (y_one, st_one) = outs
+    assert np.array_equal(y_pair, y_one)
+    assert np.array_equal(st_pair, st_one)
+    # The oracle on the kernel's fp16-rounded weights (K up to 4608: with IF
+    # the fp32-weight reference drifts by the weight rounding alone).
+    w16 = w.astype(np.float16).astype(np.float32)
+    r = L.fused_layer(x, w16, bn, stride=stride, pad=k // 2, neuron=neuron)
+    ys = from_nhwc(y_pair, T, B)
+    spk = ys - res_np if residual else ys
+    v = np.transpose(st_pair.reshape(B, oh, ow, cout), (0, 3, 1, 2))
+    check_spikes_and_v(spk, v, r["spikes"], r["h"], r["v"])
