@@ -534,11 +534,11 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
 
 namespace {
 using GlueKernel = void (*)(const snn::GlueParams);
-template <bool POOL>
+template <bool POOL, int KS = 0>
 GlueKernel glue_fn(int mode) {
-  if (mode == snn::kModeLifHalf) return snn::glue_neuron_kernel<snn::kModeLifHalf, POOL>;
-  if (mode == snn::kModeLifDiv) return snn::glue_neuron_kernel<snn::kModeLifDiv, POOL>;
-  return snn::glue_neuron_kernel<snn::kModeIf, POOL>;
+  if (mode == snn::kModeLifHalf) return snn::glue_neuron_kernel<snn::kModeLifHalf, POOL, KS>;
+  if (mode == snn::kModeLifDiv) return snn::glue_neuron_kernel<snn::kModeLifDiv, POOL, KS>;
+  return snn::glue_neuron_kernel<snn::kModeIf, POOL, KS>;
 }
 
 // Shared checks and launch of the Add / MaxPool + neuron glue.
@@ -586,10 +586,13 @@ int launch_glue(const snn_conv_desc* d, bool pool, const void* a, const void* b,
   const long long n = static_cast<long long>(d->B) * p.OH * p.OW * (d->Cout / 8);
   const long long blocks = std::max<long long>(1, std::min<long long>((n + 255) / 256,
                                                                     static_cast<long long>(g_num_sms) * 16));
-  cudaError_t e = pool ? launch_pdl(glue_fn<true>(mode), dim3(static_cast<unsigned>(blocks)), dim3(256),
-                                    0, stream, p)
-                       : launch_pdl(glue_fn<false>(mode), dim3(static_cast<unsigned>(blocks)), dim3(256),
-                                    0, stream, p);
+  GlueKernel k = glue_fn<false>(mode);
+  if (pool) {
+    // Square 2x2 / 3x3 windows issue all their loads at once.
+    k = (d->KH == 3 && d->KW == 3) ? glue_fn<true, 3>(mode)
+      : (d->KH == 2 && d->KW == 2) ? glue_fn<true, 2>(mode) : glue_fn<true>(mode);
+  }
+  cudaError_t e = launch_pdl(k, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream, p);
   if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));
   return SNN_OK;
 }

@@ -348,7 +348,9 @@ __device__ __forceinline__ uint4 glue_neuron8(float (&v)[8], const float (&x)[8]
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-template <int MODE, bool POOL>
+// KS: compile-time square pool window (2 or 3: every window load is issued
+// before the max, padding reads as -inf), or 0 for a runtime window.
+template <int MODE, bool POOL, int KS = 0>
 __global__ void __launch_bounds__(256)
 glue_neuron_kernel(const GlueParams p) {
   pdl_launch_dependents();
@@ -366,7 +368,37 @@ glue_neuron_kernel(const GlueParams p) {
       v[j] = (p.flags & kReadState) ? p.state[pix * p.C + c8 * 8 + j] : 0.f;
     for (int t = 0; t < p.T; ++t) {
       float x[8];
-      if constexpr (POOL) {
+      if constexpr (POOL && KS > 0) {
+        const int ow = static_cast<int>(pix % p.OW);
+        const int oh = static_cast<int>((pix / p.OW) % p.OH);
+        const int b = static_cast<int>(pix / (static_cast<long long>(p.OW) * p.OH));
+        const uint4 ninf4 = make_uint4(0xFC00FC00u, 0xFC00FC00u, 0xFC00FC00u, 0xFC00FC00u);
+        const __half* plane = p.a + (static_cast<size_t>(t) * p.B + b) * p.H * p.W * p.C;
+        uint4 win[KS * KS];
+#pragma unroll
+        for (int kh = 0; kh < KS; ++kh) {
+#pragma unroll
+          for (int kw = 0; kw < KS; ++kw) {
+            const int ih = oh * p.stride + kh - p.pad, iw = ow * p.stride + kw - p.pad;
+            win[kh * KS + kw] = (ih >= 0 && ih < p.H && iw >= 0 && iw < p.W)
+                ? __ldg(reinterpret_cast<const uint4*>(plane + (static_cast<size_t>(ih) * p.W + iw) * p.C) + c8)
+                : ninf4;
+          }
+        }
+        __half2 m[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) m[j] = reinterpret_cast<const __half2*>(&win[0])[j];
+#pragma unroll
+        for (int w = 1; w < KS * KS; ++w) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) m[j] = __hmax2(m[j], reinterpret_cast<const __half2*>(&win[w])[j]);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __half22float2(m[j]);
+          x[2 * j] = f.x; x[2 * j + 1] = f.y;
+        }
+      } else if constexpr (POOL) {
         const int ow = static_cast<int>(pix % p.OW);
         const int oh = static_cast<int>((pix / p.OW) % p.OH);
         const int b = static_cast<int>(pix / (static_cast<long long>(p.OW) * p.OH));
