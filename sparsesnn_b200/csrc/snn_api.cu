@@ -761,8 +761,10 @@ int snn_stem_forward(const snn_conv_desc* d, int32_t Tin, const float* x, const 
                      : d->tau == 2.0f ? snn::kModeLifHalf : snn::kModeLifDiv;
     const int R = snn::kStemPx / OW;
     const size_t smem = static_cast<size_t>(snn::stem_tc_smem_bytes(d->Cin, R, OW));
-    const long long nblk = static_cast<long long>(d->B) * ((OH + R - 1) / R);
-    if (smem <= static_cast<size_t>(kStemTcSmemMax) && nblk <= 0x7fffffffLL) {
+    // Persistent blocks (three per SM: registers), each walking row tiles.
+    const long long n_tiles = static_cast<long long>(d->B) * ((OH + R - 1) / R);
+    const long long nblk = std::min<long long>(n_tiles, 3LL * g_num_sms);
+    if (smem <= static_cast<size_t>(kStemTcSmemMax) && n_tiles <= 0x7fffffffLL) {
       cudaError_t e = launch_pdl(stem_tc_fn(d->Cin, mode), dim3(static_cast<unsigned>(nblk)),
                                  dim3(snn::kStemThreads), smem, stream, p);
       if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));

@@ -166,7 +166,7 @@ __device__ __forceinline__ int sw128_f32(int r, int k) {
 }
 
 template <int CIN, int MODE>
-__global__ void __launch_bounds__(kStemThreads)
+__global__ void __launch_bounds__(kStemThreads, 3)
 stem_tc_kernel(const StemParams p) {
   static_assert(9 * CIN <= 32, "stem K must fit one 32-wide tile");
   extern __shared__ uint8_t smem_raw[];
@@ -183,13 +183,14 @@ stem_tc_kernel(const StemParams p) {
   float* bi = sc + 64;                                          // [64]
   uint64_t* bar = reinterpret_cast<uint64_t*>(bi + 64);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
-  const int bpi = (p.OH + R - 1) / R;                 // blocks per image
-  const int b = blockIdx.x / bpi, oh0 = (blockIdx.x % bpi) * R;
+  const int bpi = (p.OH + R - 1) / R;                 // row blocks per image
+  const int n_tiles = p.B * bpi;
   const int tid = threadIdx.x, warp = tid / 32;
 
   if (tid == 0) { mbar_init(bar, 1); fence_mbar_init(); }
   if (warp == 0) { tmem_alloc(tmem_slot, 64); tmem_relinquish(); }
-  // Weights (constant data): B[co][k] = w[co][k] for k < 9*CIN, split hi/lo.
+  // Weights (constant data, once per persistent block): B[co][k] = w[co][k]
+  // for k < 9*CIN, split hi/lo.
   for (int i = tid; i < 64 * 32; i += kStemThreads) {
     const int co = i >> 5, k = i & 31;
     const float wv = k < 9 * CIN ? __ldg(p.w + co * 9 * CIN + k) : 0.f;
@@ -202,65 +203,75 @@ stem_tc_kernel(const StemParams p) {
     sc[tid] = MODE == kModeLifHalf ? p.scale[tid] * 0.5f : p.scale[tid];
     bi[tid] = MODE == kModeLifHalf ? p.bias[tid] * 0.5f : p.bias[tid];
   }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
   pdl_launch_dependents();
   pdl_wait();                                         // input and output belong to the stream
-  const float* xin = p.x + static_cast<size_t>(b) * CIN * p.H * p.W;
-  for (int i = tid; i < CIN * HWp; i += kStemThreads) {
-    const int ci = i / HWp, rem = i - ci * HWp;
-    const int r = rem / OWp, c = rem - r * OWp;
-    const int ih = oh0 - 1 + r, iw = c - 1;
-    xs[i] = (ih >= 0 && ih < p.H && iw >= 0 && iw < p.W)
-                ? __ldg(xin + (static_cast<size_t>(ci) * p.H + ih) * p.W + iw) : 0.f;
-  }
-  __syncthreads();
-  // im2col row of this thread's pixel, split hi/lo.
+
   const int px = tid;
   const int r = px / OW, c = px - (px / OW) * OW;
   const bool in_tile = px < R * OW;
+  const long long P = static_cast<long long>(p.B) * p.OH * OW;
+  bool ok = true;
+  int iter = 0;
+  // Persistent: tile = R output rows of one image.
+  for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++iter) {
+    const int b = tile / bpi, oh0 = (tile % bpi) * R;
+    const float* xin = p.x + static_cast<size_t>(b) * CIN * p.H * p.W;
+    for (int i = tid; i < CIN * HWp; i += kStemThreads) {
+      const int ci = i / HWp, rem = i - ci * HWp;
+      const int rr = rem / OWp, cc = rem - rr * OWp;
+      const int ih = oh0 - 1 + rr, iw = cc - 1;
+      xs[i] = (ih >= 0 && ih < p.H && iw >= 0 && iw < p.W)
+                  ? __ldg(xin + (static_cast<size_t>(ci) * p.H + ih) * p.W + iw) : 0.f;
+    }
+    __syncthreads();                                  // xs ready; the previous tile's spike tiles are out
+    // im2col row of this thread's pixel, split hi/lo.
 #pragma unroll
-  for (int k4 = 0; k4 < 8; ++k4) {
-    float hi[4], lo[4];
+    for (int k4 = 0; k4 < 8; ++k4) {
+      float hi[4], lo[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int k = 4 * k4 + j;
-      float xv = 0.f;
-      if (k < 9 * CIN && in_tile) {
-        const int ci = k / 9, kh = (k % 9) / 3, kw = k % 3;
-        xv = xs[ci * HWp + (r + kh) * OWp + c + kw];
+      for (int j = 0; j < 4; ++j) {
+        const int k = 4 * k4 + j;
+        float xv = 0.f;
+        if (k < 9 * CIN && in_tile) {
+          const int ci = k / 9, kh = (k % 9) / 3, kw = k % 3;
+          xv = xs[ci * HWp + (r + kh) * OWp + c + kw];
+        }
+        hi[j] = to_tf32(xv);
+        lo[j] = xv - hi[j];
       }
-      hi[j] = to_tf32(xv);
-      lo[j] = xv - hi[j];
+      const int off = px * 128 + ((k4 ^ (px & 7)) << 4);
+      *reinterpret_cast<float4*>(sAh + off) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+      *reinterpret_cast<float4*>(sAl + off) = make_float4(lo[0], lo[1], lo[2], lo[3]);
     }
-    const int off = px * 128 + ((k4 ^ (px & 7)) << 4);
-    *reinterpret_cast<float4*>(sAh + off) = make_float4(hi[0], hi[1], hi[2], hi[3]);
-    *reinterpret_cast<float4*>(sAl + off) = make_float4(lo[0], lo[1], lo[2], lo[3]);
-  }
-  fence_proxy_async_smem();                           // generic writes -> tensor-core reads
-  tc_fence_before();
-  __syncthreads();
-  const uint32_t tmem = *tmem_slot;
-  if (tid == 0) {
+    fence_proxy_async_smem();                         // generic writes -> tensor-core reads
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t idesc = idesc_tf32(kStemPx, 64);
+      const uint64_t ah = smem_desc_kmajor(smem_u32(sAh), 1024, 2);
+      const uint64_t al = smem_desc_kmajor(smem_u32(sAl), 1024, 2);
+      const uint64_t bh = smem_desc_kmajor(smem_u32(sBh), 1024, 2);
+      const uint64_t bl = smem_desc_kmajor(smem_u32(sBl), 1024, 2);
+      constexpr int kSteps = (9 * CIN + 7) / 8;        // K = 8 per MMA (+32 bytes)
+#pragma unroll
+      for (int ks = 0; ks < kSteps; ++ks) {
+        mma_tf32(tmem, al + 2 * ks, bh + 2 * ks, idesc, ks > 0 ? 1u : 0u);
+        mma_tf32(tmem, ah + 2 * ks, bl + 2 * ks, idesc, 1u);
+      }
+#pragma unroll
+      for (int ks = 0; ks < kSteps; ++ks) mma_tf32(tmem, ah + 2 * ks, bh + 2 * ks, idesc, 1u);
+      mma_commit(bar);
+    }
+    const bool ok_t = mbar_wait_bounded(bar, iter & 1, p.timeout);
+    if (!ok_t && p.err) atomicOr(p.err, kErrTimeoutAcc);
     tc_fence_after();
-    const uint32_t idesc = idesc_tf32(kStemPx, 64);
-    const uint64_t ah = smem_desc_kmajor(smem_u32(sAh), 1024, 2);
-    const uint64_t al = smem_desc_kmajor(smem_u32(sAl), 1024, 2);
-    const uint64_t bh = smem_desc_kmajor(smem_u32(sBh), 1024, 2);
-    const uint64_t bl = smem_desc_kmajor(smem_u32(sBl), 1024, 2);
-    constexpr int kSteps = (9 * CIN + 7) / 8;          // K = 8 per MMA (+32 bytes)
-#pragma unroll
-    for (int ks = 0; ks < kSteps; ++ks) {
-      mma_tf32(tmem, al + 2 * ks, bh + 2 * ks, idesc, ks > 0 ? 1u : 0u);
-      mma_tf32(tmem, ah + 2 * ks, bl + 2 * ks, idesc, 1u);
-    }
-#pragma unroll
-    for (int ks = 0; ks < kSteps; ++ks) mma_tf32(tmem, ah + 2 * ks, bh + 2 * ks, idesc, 1u);
-    mma_commit(bar);
-  }
-  const bool ok = mbar_wait_bounded(bar, 0, p.timeout);
-  if (!ok && p.err) atomicOr(p.err, kErrTimeoutAcc);
-  tc_fence_after();
-  const bool all_ok = __syncthreads_and(ok);
-  if (all_ok) {
+    ok = __syncthreads_and(ok_t);
+    if (!ok) break;
     // Thread = pixel = TMEM lane; BN once for the 64 channels.
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     float x[64], v[64];
@@ -274,11 +285,11 @@ stem_tc_kernel(const StemParams p) {
         v[32 * h + j] = 0.f;
       }
     }
+    tc_fence_before();                                // the next tile's MMAs overwrite TMEM
     const int nrows = min(R, p.OH - oh0);
-    const int n16 = nrows * OW * 8;                   // 16-byte chunks of the block's output
-    const long long P = static_cast<long long>(p.B) * p.OH * OW;
+    const int n16 = nrows * OW * 8;                   // 16-byte chunks of the tile's output
     for (int t = 0; t < p.T; ++t) {
-      uint8_t* tile = smem + (t & 1) * kStemATile;    // the A tiles are free after the MMAs
+      uint8_t* tile_s = smem + (t & 1) * kStemATile;  // the A tiles are free after the MMAs
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         uint32_t w[4];
@@ -293,7 +304,7 @@ stem_tc_kernel(const StemParams p) {
           }
           w[u] = bits;
         }
-        *reinterpret_cast<uint4*>(tile + px * 128 + ((q ^ (px & 7)) << 4)) =
+        *reinterpret_cast<uint4*>(tile_s + px * 128 + ((q ^ (px & 7)) << 4)) =
             make_uint4(w[0], w[1], w[2], w[3]);
       }
       __syncthreads();
@@ -302,7 +313,7 @@ stem_tc_kernel(const StemParams p) {
                     static_cast<size_t>(oh0) * OW) * 64));
       for (int i = tid; i < n16; i += kStemThreads) {
         const int pp = i >> 3, cg = i & 7;
-        dst[i] = *reinterpret_cast<const uint4*>(tile + pp * 128 + ((cg ^ (pp & 7)) << 4));
+        dst[i] = *reinterpret_cast<const uint4*>(tile_s + pp * 128 + ((cg ^ (pp & 7)) << 4));
       }
     }
   }
