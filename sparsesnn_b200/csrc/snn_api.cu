@@ -16,6 +16,7 @@
 #include "../../include/snn_b200.h"
 #include "snn_conv.cuh"
 #include "snn_conv_halo.cuh"
+#include "snn_conv_halo4.cuh"
 #include "snn_conv_halo_stream.cuh"
 #include "snn_glue.cuh"
 #include "snn_attn.cuh"
@@ -97,6 +98,17 @@ HaloKernel halo_kernel_fn_bn(int mode, bool res) {
 }
 
 // bn = 128 with m64 selects the M = 64 MMA path (layers of at most 64 channels).
+HaloKernel halo4_kernel_fn(int mode, bool res) {
+  switch (mode * 2 + (res ? 1 : 0)) {
+    case 0: return snn::fused_sparse_conv_halo4_kernel<snn::kModeLifHalf, false>;
+    case 1: return snn::fused_sparse_conv_halo4_kernel<snn::kModeLifHalf, true>;
+    case 2: return snn::fused_sparse_conv_halo4_kernel<snn::kModeLifDiv, false>;
+    case 3: return snn::fused_sparse_conv_halo4_kernel<snn::kModeLifDiv, true>;
+    case 4: return snn::fused_sparse_conv_halo4_kernel<snn::kModeIf, false>;
+    default: return snn::fused_sparse_conv_halo4_kernel<snn::kModeIf, true>;
+  }
+}
+
 HaloKernel halo_kernel_fn(int bn, bool m64, int mode, bool res) {
   if (bn == 128) return m64 ? halo_kernel_fn_bn<128, true>(mode, res)
                             : halo_kernel_fn_bn<128, false>(mode, res);
@@ -207,6 +219,12 @@ int ensure_init() {
       }
       for (int v = 0; v < 3; ++v) {
         e = cudaFuncSetAttribute(halo_kernel_fn(v ? 128 : 64, v == 2, mode, res != 0),
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+        if (e != cudaSuccess)
+          return g_init_status = fail(SNN_E_CUDA, "smem attribute: %s", cudaGetErrorString(e));
+      }
+      if (mode != snn::kModeNone) {
+        e = cudaFuncSetAttribute(halo4_kernel_fn(mode, res != 0),
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
         if (e != cudaSuccess)
           return g_init_status = fail(SNN_E_CUDA, "smem attribute: %s", cudaGetErrorString(e));
@@ -439,6 +457,65 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
   if (variant == SNN_VARIANT_HALO_RESIDENT) {
     snn::HaloParams hp;
     memset(&hp, 0, sizeof(hp));
+    // Spiking layers with at most 64 output channels: one N = 256 MMA per
+    // tap covers 8 x 8 pixels x 4 timesteps (fused_sparse_conv_halo4_kernel).
+    if (d->Cout <= 64 && mode != snn::kModeNone && g.OW >= 8 && p.n_m == 1) {
+      const int a4 = a_bytes / 2;                // the 64 real weight rows
+      const int halo_w = 8 + d->KW - 1;
+      const int halo_bytes = snn::kKB * 2 * halo_w * snn::kH4Ts * (8 + d->KH - 1);
+      const int halo_stride = (halo_bytes + 1023) / 1024 * 1024;
+      const int fixed = 1024 + 512 + a4 + 2 * snn::kH4OutBytes;
+      const int stages = std::min(snn::kH4MaxStages, (kSmemLimit - fixed) / halo_stride);
+      if (stages >= 2) {
+        cuuint64_t wdims[3] = {static_cast<cuuint64_t>(snn::kKB / 2), static_cast<cuuint64_t>(g.Fpad),
+                               static_cast<cuuint64_t>(g.n_kb)};
+        cuuint64_t wstrides[2] = {static_cast<cuuint64_t>(g.K / 2) * 2,
+                                  static_cast<cuuint64_t>(snn::kKB / 2) * 2};
+        cuuint32_t wbox[3] = {snn::kKB / 2, 64, static_cast<cuuint32_t>(g.n_kb)};
+        if ((st = encode(&p.tmap_a, 3, wbytes, wdims, wstrides, wbox, CU_TENSOR_MAP_SWIZZLE_64B)))
+          return st;
+        p.tw = 8; p.th = 8; p.tn = 1;
+        p.tiles_w = (g.OW + 7) / 8;
+        p.tiles_h = (g.OH + 7) / 8;
+        p.n_px_tiles = p.tiles_w * p.tiles_h * d->B;
+        // Activations seen as (C, W, T, H, B): one box holds a tile's halo
+        // for four timesteps as [halo row][timestep][halo column].
+        const size_t C = d->Cin, W = d->W, H = d->H, B = d->B;
+        cuuint64_t dims[5] = {C, W, static_cast<cuuint64_t>(d->T), H, B};
+        cuuint64_t strides[4] = {C * 2, B * H * W * C * 2, W * C * 2, H * W * C * 2};
+        cuuint32_t box[5] = {static_cast<cuuint32_t>(snn::kKB), static_cast<cuuint32_t>(halo_w),
+                             static_cast<cuuint32_t>(snn::kH4Ts), static_cast<cuuint32_t>(8 + d->KH - 1), 1};
+        if ((st = encode(&p.tmap_b[0], 5, data, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)))
+          return st;
+        // Output (and SEW residual) seen as (F, OW, OH, B, T) with boxes of
+        // 64 channels x 8 x 8 pixels x 4 timesteps; channels past F and
+        // pixels or timesteps past the tensor are not stored (read as zero).
+        {
+          const size_t F = d->Cout, OW = g.OW, OH = g.OH;
+          cuuint64_t odims[5] = {F, OW, OH, B, static_cast<cuuint64_t>(d->T)};
+          cuuint64_t ostrides[4] = {F * 2, OW * F * 2, OH * OW * F * 2, B * OH * OW * F * 2};
+          cuuint32_t obox[5] = {64, 8, 8, 1, static_cast<cuuint32_t>(snn::kH4Ts)};
+          if ((st = encode(&p.tmap_b[1], 5, out, odims, ostrides, obox, CU_TENSOR_MAP_SWIZZLE_128B)))
+            return st;
+          if (residual &&
+              (st = encode(&p.tmap_b[2], 5, residual, odims, ostrides, obox, CU_TENSOR_MAP_SWIZZLE_128B)))
+            return st;
+        }
+        hp.KH = d->KH;
+        hp.halo_w = halo_w;
+        hp.halo_bytes = halo_bytes;
+        hp.halo_stride = halo_stride;
+        hp.halo_stages = stages;
+        hp.a_bytes = a4;
+        hp.c = p;
+        const size_t smem = static_cast<size_t>(fixed) + static_cast<size_t>(stages) * halo_stride;
+        const int grid = std::max(1, std::min(p.n_px_tiles, g_num_sms));
+        cudaError_t e = launch_pdl(halo4_kernel_fn(mode, residual != nullptr), dim3(grid),
+                                   dim3(snn::kH4Threads), smem, stream, hp);
+        if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));
+        return SNN_OK;
+      }
+    }
     const int bn = g.OH >= 16 ? 128 : 64;
     const bool m64 = bn == 128 && d->Cout <= 64;
     const int th_ = bn / 8;
@@ -448,11 +525,17 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
     hp.halo_stride = (hp.halo_bytes + 1023) / 1024 * 1024;
     // M = 64 keeps only the 64 real weight rows resident (box of 64 rows).
     hp.a_bytes = m64 ? a_bytes / 2 : a_bytes;
-    if (m64) {
-      cuuint64_t dims[2] = {static_cast<cuuint64_t>(g.K / 2), static_cast<cuuint64_t>(g.Fpad)};
-      cuuint64_t strides[1] = {static_cast<cuuint64_t>(g.K / 2) * 2};
-      cuuint32_t box[2] = {snn::kKB / 2, 64};
-      if ((st = encode(&p.tmap_a, 2, wbytes, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B))) return st;
+    {
+      // The packed weights [Fpad][K/2] seen as [k-block][row][32 elements]:
+      // one box delivers a CTA's whole slice in the k-block-major order the
+      // MMA descriptors expect.
+      cuuint64_t dims[3] = {static_cast<cuuint64_t>(snn::kKB / 2), static_cast<cuuint64_t>(g.Fpad),
+                            static_cast<cuuint64_t>(g.n_kb)};
+      cuuint64_t strides[2] = {static_cast<cuuint64_t>(g.K / 2) * 2, static_cast<cuuint64_t>(snn::kKB / 2) * 2};
+      cuuint32_t box[3] = {snn::kKB / 2, static_cast<cuuint32_t>(m64 ? 64 : snn::kBM),
+                           static_cast<cuuint32_t>(g.n_kb)};
+      if (g.n_kb > 256) return fail(SNN_E_INVALID, "too many k-blocks for the resident weight box");
+      if ((st = encode(&p.tmap_a, 3, wbytes, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B))) return st;
     }
     const int fixed = 1024 + 512 + (m64 ? snn::kHalo64XposeBytes : snn::kEpiWarps * snn::kXposeBytes) +
                       hp.a_bytes;

@@ -109,6 +109,13 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  if (warp == kHaloTmaWarp && lane == 0) {
+    // The whole resident weight slice is one 3-D box ([k-block][row][32
+    // elements]), issued before anything else so that it lands while the
+    // metadata loads below are in flight.
+    mbar_arrive_expect_tx(a_full, hp.a_bytes);
+    tma_load_3d(sA, &p.tmap_a, a_full, 0, m_tile * kBM, 0);
+  }
   if (warp >= kEpiWarps) {
     // ------------------------------------------- metadata into TMEM (warps 8..11)
     const int q = warp & 3;
@@ -116,13 +123,24 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
     const int row = M64 ? (lane < 16 ? q * 16 + lane : -1) : q * 32 + lane;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
     const uint32_t* src = p.meta + (static_cast<size_t>(m_tile) * n_meta) * kBM + max(row, 0);
-    for (int j = 0; j < n_meta; j += 8) {
-      uint32_t r[8];
+    // Up to 40 columns' loads in flight per lane (one round trip for every
+    // resident-weight layer with at most 20 k-blocks).
+    constexpr int kChunk = 40;
+    for (int j = 0; j < n_meta; j += kChunk) {
+      uint32_t r[kChunk];
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
+      for (int i = 0; i < kChunk; ++i)
         r[i] = (j + i < n_meta && row >= 0) ? __ldg(src + static_cast<size_t>(j + i) * kBM)
                                             : 0x44444444u;
-      tmem_st8(lane_base + kHaloMetaCol + j, r);
+#pragma unroll
+      for (int u = 0; u < kChunk / 8; ++u) {
+        if (j + 8 * u < n_meta) {
+          uint32_t r8[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) r8[i] = r[8 * u + i];
+          tmem_st8(lane_base + kHaloMetaCol + j + 8 * u, r8);
+        }
+      }
     }
     tmem_st_wait();
     tc_fence_before();
@@ -132,9 +150,6 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
   if (warp == kHaloTmaWarp) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      mbar_arrive_expect_tx(a_full, hp.a_bytes);
-      for (int kb = 0; kb < p.n_kb; ++kb)
-        tma_load_2d(sA + kb * kAKb, &p.tmap_a, a_full, kb * (kKB / 2), m_tile * kBM);
       pdl_wait();                        // activations come from the previous kernel
       int stage = 0; uint32_t phase = 0;
       int issued = 0;

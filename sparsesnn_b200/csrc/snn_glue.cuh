@@ -478,6 +478,8 @@ head_pool_fc_kernel(const __half* __restrict__ x, const float* __restrict__ fc_w
   for (int task = threadIdx.x; task < c8n * kHeadSlots; task += blockDim.x) {
     const int c8 = task % c8n, slot = task / c8n;
     float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    // Unrolled so that several positions' loads are in flight at once.
+#pragma unroll 4
     for (int pos = slot; pos < T * HW; pos += kHeadSlots) {
       const int t = pos / HW, i = pos - t * HW;
       const uint4 u = __ldg(reinterpret_cast<const uint4*>(
@@ -504,6 +506,7 @@ head_pool_fc_kernel(const __half* __restrict__ x, const float* __restrict__ fc_w
   for (int n = warp; n < NC; n += nwarps) {
     const float4* wr = reinterpret_cast<const float4*>(fc_w + static_cast<size_t>(n) * C);
     float acc = 0.f;
+#pragma unroll 4
     for (int c4 = lane; c4 < C / 4; c4 += 32) {
       const float4 w = __ldg(wr + c4);
       const float4 f = *reinterpret_cast<const float4*>(feat + 4 * c4);

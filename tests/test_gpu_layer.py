@@ -280,11 +280,10 @@ def test_halo_stream_variant(cuda_device, T, residual):
 @pytest.mark.parametrize("T", [1, 3, 4])
 @pytest.mark.parametrize("residual", [False, True], ids=["plain", "res"])
 def test_m64_halo_path(cuda_device, T, residual):
-    """Layers with at most 64 output channels on images of >= 16 rows run the
-    resident-weight halo kernel with M = 64 MMAs (metadata remapped to the
-    M = 64 TMEM layout, spikes through tiles shared by four warps).  Odd T
-    checks the tile double-buffering across pixel tiles; a second call with
-    the membrane carried over checks the state read/write."""
+    """Layers with at most 64 output channels run M = 64 MMAs (metadata
+    remapped to the M = 64 TMEM layout, spikes through tiles shared by four
+    warps).  Odd T checks partial passes across pixel tiles; a second call
+    with the membrane carried over checks the state read/write."""
     import torch
     from sparsesnn_b200 import runtime as rt
     from sparsesnn_b200.layer import SparseConvBNLIF, fold_bn
@@ -313,6 +312,53 @@ def test_m64_halo_path(cuda_device, T, residual):
         spk = ys - res_np if residual else ys
         v = np.transpose(state.cpu().numpy().reshape(B, H, W, F), (0, 3, 1, 2))
         check_spikes_and_v(spk, v, r["spikes"], r["h"], r["v"])
+
+
+@pytest.mark.parametrize("cin, F, H, W, T, neuron, tau", [
+    (64, 64, 8, 8, 4, "lif", 2.0),        # one tile per image
+    (64, 64, 12, 20, 5, "lif", 2.0),      # ragged tiles, a second pass with one timestep
+    (64, 48, 17, 9, 6, "lif", 3.0),       # Cout < 64, general tau, two passes
+    (128, 64, 10, 16, 3, "if", 2.0),      # two 64-channel input blocks, IF
+    (64, 32, 16, 16, 8, "lif", 2.0),      # two full passes
+], ids=["8x8", "ragged_T5", "c48_tau3_T6", "cin128_if_T3", "c32_T8"])
+@pytest.mark.parametrize("residual", [False, True], ids=["plain", "res"])
+def test_halo4_path(cuda_device, cin, F, H, W, T, neuron, tau, residual):
+    """Spiking layers with at most 64 output channels run the four-timestep
+    halo kernel: N = 256 MMAs over 8 x 8 pixels x 4 timesteps from a
+    (C, W, T, H, B) tensor map.  Ragged images, T not a multiple of four
+    (timesteps past T read as zero and are not stored), Cin of two blocks,
+    both neurons and a membrane carried between two calls."""
+    import torch
+    from sparsesnn_b200 import runtime as rt
+    from sparsesnn_b200.layer import SparseConvBNLIF, fold_bn
+    B = 2
+    x, w, bn = L.make_config0(seed=7 * T + F + cin, T=2 * T, B=B, C=cin, F=F, H=H, W=W)
+    scale, bias = fold_bn(bn.gamma, bn.beta, bn.mean, bn.var)
+    layer = SparseConvBNLIF(w, scale, bias, T=T, B=B, H=H, W=W, neuron=neuron, tau=tau)
+    assert rt.variant(layer.desc) == rt.SNN_VARIANT_HALO_RESIDENT
+    res_np = None
+    if residual:
+        rng = np.random.default_rng(T + F)
+        res_np = rng.integers(0, 3, (2 * T, B, F, H, W)).astype(np.float32)
+    state = torch.zeros(layer.state_shape(), dtype=torch.float32, device="cuda")
+    outs = []
+    for part in range(2):                     # two calls, membrane carried over
+        sl = slice(part * T, (part + 1) * T)
+        xd = torch.from_numpy(to_nhwc(x[sl])).to("cuda", torch.float16)
+        res = (torch.from_numpy(to_nhwc(res_np[sl])).to("cuda", torch.float16)
+               if residual else None)
+        outs.append(layer(xd, state=state, residual=res).float().cpu().numpy())
+    torch.cuda.synchronize()
+    assert rt.device_error() == 0
+    # The oracle on the kernel's fp16-rounded weights: an IF membrane integrates
+    # the weight rounding error of K = 1152 without decay.
+    w16 = w.astype(np.float16).astype(np.float32)
+    r = L.fused_layer(x, w16, bn, stride=1, pad=1, neuron=neuron, tau=tau)
+    ys = np.concatenate([from_nhwc(o, T, B) for o in outs], axis=0)
+    spk = ys - res_np if residual else ys
+    assert set(np.unique(spk)) <= {0.0, 1.0}
+    v = np.transpose(state.cpu().numpy().reshape(B, H, W, F), (0, 3, 1, 2))
+    check_spikes_and_v(spk, v, r["spikes"], r["h"], r["v"])
 
 
 @pytest.mark.parametrize("cin, cout", [(384, 1536), (1536, 384), (384, 384)],
