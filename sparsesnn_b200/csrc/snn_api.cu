@@ -537,8 +537,7 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
       if (g.n_kb > 256) return fail(SNN_E_INVALID, "too many k-blocks for the resident weight box");
       if ((st = encode(&p.tmap_a, 3, wbytes, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B))) return st;
     }
-    const int fixed = 1024 + 512 + (m64 ? snn::kHalo64XposeBytes : snn::kEpiWarps * snn::kXposeBytes) +
-                      hp.a_bytes;
+    const int fixed = 1024 + 512 + (m64 ? snn::kHalo64XposeBytes : snn::kHaloXposeBytes) + hp.a_bytes;
     hp.halo_stages = std::min(snn::kHaloMaxStages, (kSmemLimit - fixed) / hp.halo_stride);
     if (hp.halo_stages >= 2) {
       p.tw = 8; p.th = th_; p.tn = 1;
@@ -552,6 +551,16 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
                            static_cast<cuuint32_t>(th_ + d->KH - 1), 1, 1};
       if ((st = encode(&p.tmap_b[0], 5, data, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)))
         return st;
+      if (!m64 && mode != snn::kModeNone) {
+        // Spike output as (F, OW, OH, B, T): a warp stores {32 ch, 8 w, 4 h}
+        // from its transpose tile (64-byte swizzle).
+        const size_t F = d->Cout, OW = g.OW, OH = g.OH;
+        cuuint64_t odims[5] = {F, OW, OH, B, static_cast<cuuint64_t>(d->T)};
+        cuuint64_t ostrides[4] = {F * 2, OW * F * 2, OH * OW * F * 2, B * OH * OW * F * 2};
+        cuuint32_t obox[5] = {32, 8, 4, 1, 1};
+        if ((st = encode(&p.tmap_b[1], 5, out, odims, ostrides, obox, CU_TENSOR_MAP_SWIZZLE_64B)))
+          return st;
+      }
       hp.c = p;
       const size_t smem = static_cast<size_t>(fixed) + static_cast<size_t>(hp.halo_stages) * hp.halo_stride;
       const int per_m = std::max(1, std::min(p.n_px_tiles, g_num_sms / p.n_m));

@@ -43,6 +43,22 @@ constexpr int kHaloMetaCol = 256;        // accumulators: 2 x up to 128 columns
 constexpr int kHaloTmemCols = 512;
 constexpr int kHalo64TileBytes = 64 * 128;                 // [64 px][64 ch] fp16
 constexpr int kHalo64XposeBytes = 4 * kHalo64TileBytes;    // 2 buffers x 2 halves
+constexpr int kHaloXposeBytes = kEpiWarps * 2 * kXposeBytes;   // M = 128: 2 tiles per warp
+
+// Adds the SEW residual rows (store layout, see load_residual_rows) into a
+// transpose tile in place.
+__device__ __forceinline__ void add_rows_into_xpose(uint8_t* xb, int lane, const uint4 (&r4)[4]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint4* d = reinterpret_cast<uint4*>(xb + xpose_off(8 * j + (lane >> 2), lane & 3));
+    uint4 o = *d;
+    __half2* a = reinterpret_cast<__half2*>(&o);
+    const __half2* b = reinterpret_cast<const __half2*>(&r4[j]);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) a[u] = __hadd2(a[u], b[u]);
+    *d = o;
+  }
+}
 
 struct HaloParams {
   ConvParams c;              // shared fields (tmap_a, tmap_b[0], meta, scale, ...)
@@ -74,7 +90,7 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
   uint8_t* sA = smem;                                              // resident weights
   uint8_t* sH = smem + hp.a_bytes;                                 // halo stages
   uint8_t* sX = sH + hp.halo_stages * hp.halo_stride;              // epilogue transposes
-  uint64_t* full = reinterpret_cast<uint64_t*>(sX + (M64 ? kHalo64XposeBytes : kEpiWarps * kXposeBytes));
+  uint64_t* full = reinterpret_cast<uint64_t*>(sX + (M64 ? kHalo64XposeBytes : kHaloXposeBytes));
   uint64_t* empty = full + kHaloMaxStages;
   uint64_t* a_full = empty + kHaloMaxStages;
   uint64_t* acc_full = a_full + 1;          // [2]
@@ -360,7 +376,14 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
     const long long P = static_cast<long long>(p.B) * p.OH * p.OW;
     const int nchunk8 = max(0, min(4, (p.F - cbase) / 8));
     const bool chunk_ok = (lane & 3) < nchunk8;
-    uint8_t* xb = sX + warp * kXposeBytes;
+    // Spikes leave through TMA stores of this warp's two transpose tiles
+    // (alternating per 32-pixel group; the tile layout is the 64-byte TMA
+    // swizzle of a {32 ch, 8 w, 4 h} box): global stores from the epilogue
+    // warps would slow the MMAs' shared-memory operand reads.  Lane 0 issues
+    // the stores and, before a tile is rewritten, waits until its previous
+    // store has read it.
+    uint8_t* xbuf = sX + warp * 2 * kXposeBytes;
+    int n_groups = 0;
     pdl_wait();                          // residual, output and state belong to the stream
 
     int it = 0;
@@ -426,26 +449,37 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
               if (cvalid && px >= 0) p.out_f32[(tbase + px) * p.F + cout] = fmaf(acc[i], sc, bi);
             }
           } else {
+            uint8_t* xb = xbuf + (n_groups & 1) * kXposeBytes;
+            if (n_groups >= 2) {                 // this tile's previous store has read it
+              if (lane == 0) bulk_wait_group_read<1>();
+              __syncwarp();
+            }
 #pragma unroll
             for (int i = 0; i < 32; ++i)
               xpose_put(xb, i, lane, neuron_step<MODE>(v[g][i], fmaf(acc[i], sx, bx), p.decay,
                                                        p.tau, p.v_th, p.v_reset));
             __syncwarp();
             if constexpr (RES) {
+              add_rows_into_xpose(xb, lane, r4[g]);
               if (g + 1 < G) {
                 int rows[4];
                 store_rows(my_px[g + 1], lane, rows);
                 load_residual_rows(p.residual, tbase, rows, p.F, cbase, lane, chunk_ok, r4[g + 1]);
               }
             }
-            int rows[4];
-            store_rows(my_px[g], lane, rows);
-            store_xpose_rows<RES>(p.out, xb, tbase, rows, p.F, cbase, lane, chunk_ok, r4[g]);
+            fence_proxy_async_smem();
             __syncwarp();
+            if (lane == 0) {
+              // Columns half*BN/2 + 32g .. +31 of the tile: 4 rows x 8 columns.
+              const int col = half * (BN / 2) + g * 32;
+              tma_store_5d(&p.tmap_b[1], xb, cbase, tc.w0, tc.h0 + col / 8, tc.n0, t);
+              bulk_commit_group();
+            }
+            ++n_groups;
           }
         }
       }
-      if (!stop && (p.flags & kWriteState) && warp_live) {
+      if (!stop && (p.flags & kWriteState) && warp_live) {  // (membranes after the last timestep)
 #pragma unroll
         for (int g = 0; g < G; ++g) {
 #pragma unroll
@@ -456,6 +490,7 @@ fused_sparse_conv_halo_kernel(const __grid_constant__ HaloParams hp) {
         }
       }
     }
+    if (lane == 0) bulk_wait_group<0>();        // stores complete before the CTA exits
     if (stop) *abort_flag = 1;
   }
 
