@@ -601,6 +601,24 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
     if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));
     return SNN_OK;
   }
+  // General kernel: spikes leave by TMA stores when each half-tile of 32
+  // pixels is a box in (w, h, image) -- tiles of 64 pixels made of whole rows
+  // or whole images.
+  if (spikes && p.tw * p.th * p.tn == snn::kBN) {
+    int bw = 0, bh = 0, bn = 0;
+    if (p.tw >= 32) { if (p.tw % 32 == 0) { bw = 32; bh = 1; bn = 1; } }
+    else if (p.tw * p.th >= 32) { if (32 % p.tw == 0) { bw = p.tw; bh = 32 / p.tw; bn = 1; } }
+    else if (32 % (p.tw * p.th) == 0) { bw = p.tw; bh = p.th; bn = 32 / (p.tw * p.th); }
+    if (bw > 0) {
+      const size_t F = d->Cout, OW = g.OW, OH = g.OH, B = d->B;
+      cuuint64_t odims[5] = {F, OW, OH, B, static_cast<cuuint64_t>(d->T)};
+      cuuint64_t ostrides[4] = {F * 2, OW * F * 2, OH * OW * F * 2, B * OH * OW * F * 2};
+      cuuint32_t obox[5] = {32, static_cast<cuuint32_t>(bw), static_cast<cuuint32_t>(bh),
+                            static_cast<cuuint32_t>(bn), 1};
+      if ((st = encode(&p.tmap_out, 5, out, odims, ostrides, obox, CU_TENSOR_MAP_SWIZZLE_64B))) return st;
+      p.tma_out = 1;
+    }
+  }
   if (pair) {
     const int n_pairs = p.n_m / 2;
     const int per_pair = std::max(1, std::min(p.n_px_tiles, (g_num_sms / 2) / n_pairs));

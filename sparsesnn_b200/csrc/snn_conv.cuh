@@ -138,6 +138,20 @@ __device__ __forceinline__ void xpose_put_rows(uint8_t* xb, int lane, const uint
   for (int j = 0; j < 4; ++j)
     *reinterpret_cast<uint4*>(xb + xpose_off(8 * j + (lane >> 2), lane & 3)) = r4[j];
 }
+// Adds the SEW residual rows (store layout, see load_residual_rows) into a
+// transpose tile in place.
+__device__ __forceinline__ void add_rows_into_xpose(uint8_t* xb, int lane, const uint4 (&r4)[4]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint4* d = reinterpret_cast<uint4*>(xb + xpose_off(8 * j + (lane >> 2), lane & 3));
+    uint4 o = *d;
+    __half2* a = reinterpret_cast<__half2*>(&o);
+    const __half2* b = reinterpret_cast<const __half2*>(&r4[j]);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) a[u] = __hadd2(a[u], b[u]);
+    *d = o;
+  }
+}
 // Pixels this lane stores (columns 8j + lane/4), from each lane's pixel of
 // column `lane` (-1 = outside the output).
 __device__ __forceinline__ void store_rows(int my_px, int lane, int (&rows)[4]) {
@@ -186,6 +200,7 @@ enum ErrCode : unsigned { kErrTimeoutFull = 1u, kErrTimeoutEmpty = 2u, kErrTimeo
 struct ConvParams {
   CUtensorMap tmap_a;        // compressed weights [Fpad][K/2] fp16 (2D)
   CUtensorMap tmap_b[4];     // activations (C, W', H', B, T), one map per stride parity
+  CUtensorMap tmap_out;      // spikes (F, OW, OH, B, T), box {32 ch, one half-tile of pixels, 1 t}
   const uint32_t* meta;      // [Fpad/128][K/32][128]
   const float* scale;        // [F]
   const float* bias;         // [F]
@@ -202,6 +217,7 @@ struct ConvParams {
   int tiles_w, tiles_h, n_px_tiles, n_m;
   int box_bytes;             // bytes of one activation TMA box (tw*th*tn*128)
   int flags;
+  int tma_out;               // general kernel: spikes leave by TMA stores through tmap_out
   float decay, tau, inv_tau, v_th, v_reset;
   int n2_lif;                // kResTwoNeuron: second neuron is a LIF (else IF)
   float decay2, tau2, v_th2, v_reset2;
@@ -502,6 +518,13 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
     const int nchunk8 = max(0, min(4, (p.F - cbase) / 8));   // valid 8-channel chunks
     const bool chunk_ok = (lane & 3) < nchunk8;
     uint8_t* xb = sX + e * kXposeBytes;
+    // With p.tma_out the transpose tile (the 64-byte TMA swizzle of a
+    // {32 ch, 32 px} box) leaves through a TMA store issued by lane 0, which
+    // waits for that store to read the tile before the tile is rewritten:
+    // global stores from the epilogue warps would slow the MMAs' and TMA's
+    // shared-memory traffic.
+    const bool tma_out = p.tma_out != 0;
+    int n_st = 0;
 
     auto pixel_of = [&](const TileCoord& tc, int col) -> int {
       const int dn = col / tile_px;
@@ -520,6 +543,13 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
       // Lane l's pixel is column half*32 + l (neuron phase: lane = channel,
       // so the column's pixel comes by shuffle).
       const int my_px = pixel_of(tc, half * 32 + lane);
+      // Origin of this half's 32 pixels as a TMA box (w, h, image).
+      int bw0, bh0, bn0;
+      {
+        const int col = half * 32;
+        const int dn = col / tile_px, rem = col - dn * tile_px;
+        bn0 = tc.n0 + dn; bh0 = tc.h0 + rem / p.tw; bw0 = tc.w0 + rem % p.tw;
+      }
       int rows[4];
       store_rows(my_px, lane, rows);
       float v[32];
@@ -595,6 +625,10 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
               // Neuron update, lane = output channel, i = pixel column.
               const float sx = MODE == kModeLifHalf ? sc * 0.5f : sc;
               const float bx = MODE == kModeLifHalf ? bi * 0.5f : bi;
+              if (tma_out && n_st > 0) {       // the tile's previous store has read it
+                if (lane == 0) bulk_wait_group_read<0>();
+                __syncwarp();
+              }
               if constexpr (RM == kResAddBefore || RM == kResTwoNeuron) {
                 // The residual enters the neuron: its rows go through the
                 // transpose tile, each lane reads its channel per column and
@@ -620,9 +654,20 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
                 xpose_put(xb, i, lane, spike);
               }
               __syncwarp();
-              store_xpose_rows<RM == kResAddAfter>(p.out, xb, tbase, rows, p.F, cbase, lane, chunk_ok,
-                                                   r4[u]);
-              __syncwarp();
+              if (tma_out) {
+                if constexpr (RM == kResAddAfter) add_rows_into_xpose(xb, lane, r4[u]);
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                  tma_store_5d(&p.tmap_out, xb, cbase, bw0, bh0, bn0, t0 + t2 + u);
+                  bulk_commit_group();
+                }
+                ++n_st;
+              } else {
+                store_xpose_rows<RM == kResAddAfter>(p.out, xb, tbase, rows, p.F, cbase, lane, chunk_ok,
+                                                     r4[u]);
+                __syncwarp();
+              }
             }
           }
         }
@@ -639,6 +684,7 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
         }
       }
     }
+    if (tma_out && lane == 0) bulk_wait_group<0>();   // stores complete before the CTA exits
     if (stop) *abort_flag = 1;
   }
 

@@ -45,21 +45,6 @@ constexpr int kHalo64TileBytes = 64 * 128;                 // [64 px][64 ch] fp1
 constexpr int kHalo64XposeBytes = 4 * kHalo64TileBytes;    // 2 buffers x 2 halves
 constexpr int kHaloXposeBytes = kEpiWarps * 2 * kXposeBytes;   // M = 128: 2 tiles per warp
 
-// Adds the SEW residual rows (store layout, see load_residual_rows) into a
-// transpose tile in place.
-__device__ __forceinline__ void add_rows_into_xpose(uint8_t* xb, int lane, const uint4 (&r4)[4]) {
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    uint4* d = reinterpret_cast<uint4*>(xb + xpose_off(8 * j + (lane >> 2), lane & 3));
-    uint4 o = *d;
-    __half2* a = reinterpret_cast<__half2*>(&o);
-    const __half2* b = reinterpret_cast<const __half2*>(&r4[j]);
-#pragma unroll
-    for (int u = 0; u < 4; ++u) a[u] = __hadd2(a[u], b[u]);
-    *d = o;
-  }
-}
-
 struct HaloParams {
   ConvParams c;              // shared fields (tmap_a, tmap_b[0], meta, scale, ...)
   int KH;
