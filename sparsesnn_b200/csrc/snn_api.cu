@@ -313,11 +313,6 @@ void general_tile(const Geometry& g, int B, int* tw, int* th, int* tn) {
   else if (g.OH * g.OW >= snn::kBN) { *tw = g.OW; *th = snn::kBN / g.OW; *tn = 1; }
   else { *tw = g.OW; *th = g.OH; *tn = std::max(1, std::min(B, snn::kBN / (g.OH * g.OW))); }
 }
-int general_tile_px(const Geometry& g) {
-  int tw, th, tn;
-  general_tile(g, 1 << 30, &tw, &th, &tn);
-  return tw * th * tn;
-}
 
 int select_variant(const snn_conv_desc* d, const Geometry& g) {
   if (d->flags & SNN_FLAG_FORCE_GENERIC) return SNN_VARIANT_GENERIC;
@@ -327,11 +322,10 @@ int select_variant(const snn_conv_desc* d, const Geometry& g) {
   if (!s1_3x3) return SNN_VARIANT_GENERIC;
   const int a_bytes = g.n_kb * snn::kABytes;
   if (a_bytes <= kHaloMaxWeightBytes && g.OH >= 8) return SNN_VARIANT_HALO_RESIDENT;
-  // With streamed weights the general kernel is faster whenever its tiles
-  // hold exactly 64 pixels (its MMAs then cover two or four timesteps at
-  // once); the streaming halo kernel serves the other image sizes.
-  if (g.OH >= 8 && g.OW >= 8 && d->T <= snn::kHsMaxT && general_tile_px(g) != snn::kBN)
-    return SNN_VARIANT_HALO_STREAM;
+  // Streamed weights: the streaming halo kernel loads each tile's input halo
+  // once for all nine taps and T <= 4 timesteps (the general kernel loads a
+  // box per tap), measured faster on 8x8 and 12x12 images.
+  if (g.OH >= 8 && g.OW >= 8 && d->T <= snn::kHsMaxT) return SNN_VARIANT_HALO_STREAM;
   return SNN_VARIANT_GENERIC;
 }
 
@@ -581,10 +575,11 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
     ph.tiles_h = (g.OH + 7) / 8;
     ph.n_px_tiles = ph.tiles_w * ph.tiles_h * d->B;
     const size_t C = d->Cin, W = d->W, H = d->H, B = d->B;
-    cuuint64_t dims[5] = {C, W, H, B, static_cast<cuuint64_t>(d->T)};
-    cuuint64_t strides[4] = {C * 2, W * C * 2, H * W * C * 2, B * H * W * C * 2};
-    cuuint32_t box[5] = {static_cast<cuuint32_t>(snn::kKB), 10, 10, 1,
-                         static_cast<cuuint32_t>(snn::kHsMaxT)};
+    // Activations seen as (C, W, T, H, B): one box holds a tile's halo for
+    // all T timesteps as [halo row][timestep][halo column].
+    cuuint64_t dims[5] = {C, W, static_cast<cuuint64_t>(d->T), H, B};
+    cuuint64_t strides[4] = {C * 2, B * H * W * C * 2, W * C * 2, H * W * C * 2};
+    cuuint32_t box[5] = {static_cast<cuuint32_t>(snn::kKB), 10, static_cast<cuuint32_t>(d->T), 10, 1};
     if ((st = encode(&ph.tmap_b[0], 5, data, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)))
       return st;
     {  // weights as (Cin/2 el of one tap, Fpad rows, 9 taps): one box = 3 taps x 128 rows
@@ -592,6 +587,14 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
       cuuint64_t ws[2] = {static_cast<cuuint64_t>(g.K / 2) * 2, (C / 2) * 2};
       cuuint32_t wb[3] = {snn::kKB / 2, snn::kBM, 3};
       if ((st = encode(&ph.tmap_b[1], 3, weight, wd, ws, wb, CU_TENSOR_MAP_SWIZZLE_64B))) return st;
+    }
+    if (spikes) {  // spikes as (F, OW, OH, B, T): a warp stores {32 ch, 8 w, 4 h}
+      const size_t F = d->Cout, OW = g.OW, OH = g.OH;
+      cuuint64_t odims[5] = {F, OW, OH, B, static_cast<cuuint64_t>(d->T)};
+      cuuint64_t ostrides[4] = {F * 2, OW * F * 2, OH * OW * F * 2, B * OH * OW * F * 2};
+      cuuint32_t obox[5] = {32, 8, 4, 1, 1};
+      if ((st = encode(&ph.tmap_out, 5, out, odims, ostrides, obox, CU_TENSOR_MAP_SWIZZLE_64B))) return st;
+      ph.tma_out = 1;
     }
     const int per_m = std::max(1, std::min(ph.n_px_tiles, g_num_sms / ph.n_m));
     const long long grid = static_cast<long long>(per_m) * ph.n_m;

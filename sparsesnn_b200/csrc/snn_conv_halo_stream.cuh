@@ -1,17 +1,19 @@
 // Streaming-weight halo variant for stride-1 3x3 convolutions whose weight
 // slice is too large to stay resident (e.g. Cin = 256), on images of at
-// least 8x8.  A tile is 8x8 output pixels of one image (UMMA N = 64); all T
-// timesteps (T <= 4) accumulate in TMEM at once, so every weight tile that
-// enters shared memory is reused for all T timesteps -- consecutive MMAs
-// share the A operand through the tensor core's A collector
-// (fill / use / lastuse) and A is read from shared memory once per tap.
+// least 8x8.  A tile is 8x8 output pixels of one image for all T timesteps
+// (T <= 4): ONE MMA per tap covers them all (UMMA N = 64*T), so every weight
+// tile that enters shared memory is read once per tap for all timesteps.
 //
 // Per (tile, 64-channel slice cb): the producer loads the T input halos
-// (10x10 pixels each) as ONE 5D TMA box spanning the timesteps, then the
-// slice's weights in three kernel-row stages, each ONE 3D box of 3 taps x
-// 128 rows.  A TMA box costs a fixed few hundred cycles whatever its size,
-// so the kernel issues as few, large boxes as it can.  Every tap reads a
-// halo through a descriptor offset of (kh*10 + kw) rows.
+// (10x10 pixels each) as ONE 5D TMA box from a (C, W, T, H, B) view of the
+// activations, so shared memory holds [halo row][timestep][halo column]
+// 128-byte pixel rows; a tap's B operand starts at row (kh*T*10 + kw) and
+// its 8-pixel groups are one timestep block (10 rows) apart: group g is
+// output row g/T of timestep g%T, and accumulator column 8*(T*r + t) + c
+// holds output row r, timestep t, column c.  The slice's weights arrive in
+// three kernel-row stages, each ONE 3D box of 3 taps x 128 rows.  A TMA box
+// costs a fixed few hundred cycles whatever its size, so the kernel issues
+// as few, large boxes as it can.
 //
 // Warp roles: 0..7 epilogue, 8..11 metadata, then 10 = MMA + TMEM owner,
 // 11 = halo loads, 8 and 9 = weight loads.
@@ -30,26 +32,6 @@ constexpr int kHsHaloStride = kHsMaxT * kHsHaloBytes;  // 51200 (1024-aligned)
 constexpr int kHsMetaCol = 256;
 constexpr int kHsSmemBytes = kHsAStages * kHsAStageBytes + kHsHaloStages * kHsHaloStride +
                              kEpiWarps * kXposeBytes + 512 + 1024;
-
-template <int OP>
-__device__ __forceinline__ void mma_sp_f16_coll(uint32_t d, uint64_t a, uint64_t b, uint32_t e,
-                                                uint32_t id, uint32_t acc) {
-  if constexpr (OP == 0) {
-    mma_sp_f16(d, a, b, e, id, acc);
-  } else if constexpr (OP == 1) {
-    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.sp.cta_group::1.kind::f16.collector::a::fill [%0], %1, %2, [%5], %3, {%6, %6, %6, %6}, p;\n\t}"
-        ::"r"(d), "l"(a), "l"(b), "r"(id), "r"(acc), "r"(e), "r"(0u) : "memory");
-  } else if constexpr (OP == 2) {
-    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.sp.cta_group::1.kind::f16.collector::a::use [%0], %1, %2, [%5], %3, {%6, %6, %6, %6}, p;\n\t}"
-        ::"r"(d), "l"(a), "l"(b), "r"(id), "r"(acc), "r"(e), "r"(0u) : "memory");
-  } else {
-    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.sp.cta_group::1.kind::f16.collector::a::lastuse [%0], %1, %2, [%5], %3, {%6, %6, %6, %6}, p;\n\t}"
-        ::"r"(d), "l"(a), "l"(b), "r"(id), "r"(acc), "r"(e), "r"(0u) : "memory");
-  }
-}
 
 template <int MODE, bool RES>
 __global__ void __launch_bounds__(kHaloThreads, 1)
@@ -137,11 +119,11 @@ fused_sparse_conv_halo_stream_kernel(const __grid_constant__ ConvParams p) {
             if (!mbar_wait_bounded(&h_empty[hs], hph ^ 1, p.timeout_ns)) {
               atomicOr(p.err, kErrTimeoutEmpty); *abort_flag = 1; stop = true; break;
             }
-            // All T halos in one box (timesteps beyond T are outside the
-            // tensor: zero-filled and never read).
-            mbar_arrive_expect_tx(&h_full[hs], kHsHaloStride);
+            // All T halos in one box: coordinates (channel, column,
+            // timestep, row, image).
+            mbar_arrive_expect_tx(&h_full[hs], T * kHsHaloBytes);
             tma_load_5d(sH + hs * kHsHaloStride, &p.tmap_b[0], &h_full[hs], cb * kKB,
-                        tc.w0 - 1, tc.h0 - 1, tc.n0, 0);
+                        tc.w0 - 1, 0, tc.h0 - 1, tc.n0);
             ++h_issued;
             if (++hs == kHsHaloStages) { hs = 0; hph ^= 1; }
             continue;
@@ -177,7 +159,7 @@ fused_sparse_conv_halo_stream_kernel(const __grid_constant__ ConvParams p) {
   } else if (warp == kHaloMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = idesc_f16(kBM, kHsBN, true);
+      const uint32_t idesc = idesc_f16(kBM, kHsBN * T, true);
       if (!mbar_wait_bounded(meta_ready, 0, p.timeout_ns)) { atomicOr(p.err, kErrTimeoutMeta); *abort_flag = 1; }
       tc_fence_after();
       const uint32_t a_base = smem_u32(sA);
@@ -210,7 +192,7 @@ fused_sparse_conv_halo_stream_kernel(const __grid_constant__ ConvParams p) {
 #pragma unroll
             for (int kw = 0; kw < 3; ++kw) {
               const int kb = (kh * 3 + kw) * p.cin_blocks + cb;
-              const uint32_t boff = static_cast<uint32_t>(kh * 10 + kw) * 128;
+              const uint32_t boff = static_cast<uint32_t>(kh * T * 10 + kw) * 128;
 #pragma unroll
               for (int s = 0; s < 2; ++s) {
                 const uint32_t ecol = kHsMetaCol + 2 * kb + s;
@@ -218,17 +200,8 @@ fused_sparse_conv_halo_stream_kernel(const __grid_constant__ ConvParams p) {
                 const uint32_t id = idesc | (ecol & 1u);
                 const uint64_t adesc = smem_desc_kmajor(abase + kw * kABytes + 32 * s, 512, 4);
                 const uint32_t acc = (cbi > 0 || kh > 0 || kw > 0 || s > 0) ? 1u : 0u;
-                const uint32_t bt = hstage + boff + 64 * s;    // timestep t at + t*kHsHaloBytes
-                if (T == 1) {
-                  mma_sp_f16_coll<0>(tmem, adesc, smem_desc_kmajor(bt, 1280, 2), e_addr, id, acc);
-                } else {
-                  mma_sp_f16_coll<1>(tmem, adesc, smem_desc_kmajor(bt, 1280, 2), e_addr, id, acc);
-                  for (int t = 1; t < T - 1; ++t)
-                    mma_sp_f16_coll<2>(tmem + t * kHsBN, adesc,
-                                       smem_desc_kmajor(bt + t * kHsHaloBytes, 1280, 2), e_addr, id, acc);
-                  mma_sp_f16_coll<3>(tmem + (T - 1) * kHsBN, adesc,
-                                     smem_desc_kmajor(bt + (T - 1) * kHsHaloBytes, 1280, 2), e_addr, id, acc);
-                }
+                mma_sp_f16(tmem, adesc, smem_desc_kmajor(hstage + boff + 64 * s, 1280, 2), e_addr, id,
+                           acc);
               }
             }
             mma_commit(&a_empty[as]);
@@ -263,6 +236,11 @@ fused_sparse_conv_halo_stream_kernel(const __grid_constant__ ConvParams p) {
     const int nchunk8 = max(0, min(4, (p.F - cbase) / 8));
     const bool chunk_ok = (lane & 3) < nchunk8;
     uint8_t* xb = sX + warp * kXposeBytes;
+    // With p.tma_out the transpose tile ({32 ch, 8 w, 4 h} in the 64-byte
+    // TMA swizzle) leaves by a TMA store issued by lane 0, which waits for it
+    // to read the tile before the tile is rewritten.
+    const bool tma_out = p.tma_out != 0;
+    int n_st = 0;
     pdl_wait();                          // residual, output and state belong to the stream
 
     int tile_it = 0;
@@ -290,7 +268,16 @@ fused_sparse_conv_halo_stream_kernel(const __grid_constant__ ConvParams p) {
         if (fail) { atomicOr(p.err, kErrTimeoutAcc); stop = true; break; }
         tc_fence_after();
         float acc[32];
-        if (warp_live) tmem_ld32(lane_base + t * kHsBN + half * 32, acc);
+        if (warp_live) {
+          // Output rows 4*half + j at timestep t: 8 columns each.
+          uint32_t r[32];
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            tmem_ld8_nowait(lane_base + 8 * (T * (4 * half + j) + t), r + 8 * j);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) acc[i] = __uint_as_float(r[i]);
+        }
         tc_fence_before();
         mbar_arrive(&acc_empty[t]);              // the next tile's MMAs may reuse it
         if (!warp_live) continue;
@@ -301,13 +288,28 @@ fused_sparse_conv_halo_stream_kernel(const __grid_constant__ ConvParams p) {
             if (cvalid && px >= 0) p.out_f32[(tbase + px) * p.F + cout] = fmaf(acc[i], sc, bi);
           }
         } else {
+          if (tma_out && n_st > 0) {
+            if (lane == 0) bulk_wait_group_read<0>();
+            __syncwarp();
+          }
 #pragma unroll
           for (int i = 0; i < 32; ++i)
             xpose_put(xb, i, lane, neuron_step<MODE>(v[i], fmaf(acc[i], sx, bx), p.decay, p.tau,
                                                      p.v_th, p.v_reset));
           __syncwarp();
-          store_xpose_rows<RES>(p.out, xb, tbase, rows, p.F, cbase, lane, chunk_ok, r4);
-          __syncwarp();
+          if (tma_out) {
+            if constexpr (RES) add_rows_into_xpose(xb, lane, r4);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_5d(&p.tmap_out, xb, cbase, tc.w0, tc.h0 + 4 * half, tc.n0, t);
+              bulk_commit_group();
+            }
+            ++n_st;
+          } else {
+            store_xpose_rows<RES>(p.out, xb, tbase, rows, p.F, cbase, lane, chunk_ok, r4);
+            __syncwarp();
+          }
         }
       }
       ++tile_it;
@@ -319,6 +321,7 @@ fused_sparse_conv_halo_stream_kernel(const __grid_constant__ ConvParams p) {
         }
       }
     }
+    if (tma_out && lane == 0) bulk_wait_group<0>();   // stores complete before the CTA exits
     if (stop) *abort_flag = 1;
   }
 

@@ -93,8 +93,8 @@ def test_forward_without_device_fails_loudly(_lib):
     (dict(Cin=64, H=32, W=32, Cout=64), rt.SNN_VARIANT_HALO_RESIDENT),
     (dict(Cin=256, H=12, W=12, Cout=256), rt.SNN_VARIANT_HALO_STREAM),
     (dict(Cin=512, H=8, W=12, Cout=512), rt.SNN_VARIANT_HALO_STREAM),
-    (dict(Cin=256, H=8, W=8, Cout=256), rt.SNN_VARIANT_GENERIC),      # 64-pixel tiles
-    (dict(Cin=512, H=16, W=16, Cout=512), rt.SNN_VARIANT_GENERIC),
+    (dict(Cin=256, H=8, W=8, Cout=256), rt.SNN_VARIANT_HALO_STREAM),
+    (dict(Cin=512, H=16, W=16, Cout=512), rt.SNN_VARIANT_HALO_STREAM),
     (dict(Cin=256, H=8, W=8, T=5), rt.SNN_VARIANT_GENERIC),          # T > 4
     (dict(Cin=512, H=4, W=4), rt.SNN_VARIANT_GENERIC),               # image < 8x8
     (dict(Cin=64, H=32, W=32, stride=2), rt.SNN_VARIANT_GENERIC),
