@@ -9,8 +9,10 @@ collective, as in the data-parallel design).  Prints ONE JSON line on rank 0.
 * value: images/s of the whole job, inputs resident in HBM, each step = one
   CUDA-graph replay of the forward (+ logits gather when N > 1), timed with
   CUDA events between barriers, max over ranks.
-* e2e: the same through the public call ``model(x_host)`` with the input
-  copied from pinned host memory and the logits read back to host every step.
+* e2e: the same through the C-ABI native executor (``snn_engine_run`` on an
+  engine file saved from the replica) with the input copied from pinned host
+  memory and the logits read back to host every step; ``python_driver`` is
+  the same measurement through the Python call ``model(x_host)``.
 * roofline: the fused sparse conv kernel (19 launches per forward), timed
   with CUDA events around each launch over K eager forwards run right after
   the timed region; FLOPs are dense-equivalent 2*M*N*K.
@@ -353,7 +355,43 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     barrier()
     ms_e2e = sd.max_over_ranks(e0.elapsed_time(e1) / args.steps, device=dev)
-    e2e = args.batch * world / (ms_e2e / 1000.0)
+    e2e_driver = args.batch * world / (ms_e2e / 1000.0)
+
+    # ---------------- timed region C: the native executor through the C-ABI
+    # (snn_engine_run: pinned host images in, host logits out, the C++ node
+    # loop replayed from its CUDA graph), on an engine file saved from the
+    # same replica.
+    import tempfile
+    from sparsesnn_b200 import engine_file as ef
+    eng_dir = tempfile.mkdtemp()
+    eng_path = os.path.join(eng_dir, f"sew18_rank{rank}.snne")
+    ef.save_engine(model, eng_path)
+    eng = ef.Engine(eng_path)
+    eng_logits = torch.empty_like(model.logits)
+    es = torch.cuda.Stream(dev)
+    with torch.cuda.stream(es):
+        eng.capture(es)
+        for _ in range(max(3, args.warmup)):
+            eng.run(x_host.data_ptr(), eng_logits.data_ptr(), es)
+            if world > 1:
+                sd.gather_logits(eng_logits, gathered)
+        es.synchronize()
+        barrier()
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record(es)
+        for _ in range(args.steps):
+            eng.run(x_host.data_ptr(), eng_logits.data_ptr(), es)   # H2D + graph replay
+            if world > 1:
+                sd.gather_logits(eng_logits, gathered)
+            logits_host.copy_(eng_logits, non_blocking=True)         # D2H of the step's result
+        c1.record(es)
+        es.synchronize()
+    barrier()
+    ms_eng = sd.max_over_ranks(c0.elapsed_time(c1) / args.steps, device=dev)
+    e2e = args.batch * world / (ms_eng / 1000.0)
+    eng.close()
+    os.remove(eng_path)
+    os.rmdir(eng_dir)
 
     # ---------------- per-launch CUDA-event timing of the fused conv kernel
     ops = model.launches()
@@ -407,7 +445,9 @@ def run_ours(args, rank, world, local_rank):
                 "dtype": "f16", "data": "synthetic", "config": config(args, world),
                 "e2e": {"value": e2e, "unit": UNIT,
                         "h2d_bytes_per_step": int(x_host.numel() * 4),
-                        "d2h_bytes_per_step": int(logits_host.numel() * 4)},
+                        "d2h_bytes_per_step": int(logits_host.numel() * 4),
+                        "path": "snn_engine_run (C-ABI native executor, CUDA graph), pinned host buffers",
+                        "python_driver": e2e_driver},
                 "gpu_launches": n_launch * args.steps,
                 "roofline": {"bound": "tensor", "achieved": achieved, "peak": sparse_peak,
                              "unit": "TFLOP/s", "frac": achieved / sparse_peak,

@@ -207,6 +207,53 @@ int snn_get_device_error(uint32_t* code, int reset);
 /* Message of the last failure on this thread ("" if none). */
 const char* snn_last_error_message(void);
 
+/* ------------------------------------------------------------------ engine
+ * Whole-model executor over an engine file: a plan of fused nodes (stem,
+ * sparse conv with optional residual, Add+LIF, MaxPool+LIF, head) in
+ * execution order plus a packed parameter blob, as written by
+ * sparsesnn_b200.engine_file.save_engine.  The loader validates the file,
+ * allocates one device arena for every activation and uploads the
+ * parameters; a forward is the node loop over the entry points above,
+ * launched eagerly or replayed from a CUDA graph.  Membranes start at zero
+ * every forward (single-call inference, as the reference executor after
+ * sengine_reset_membranes, sengine/csrc/cpp_executor.cu:1196-1203). */
+typedef struct snn_engine snn_engine;
+
+/* Validates an engine file on the host (no device use) and reports its node
+ * and tensor counts.  Replaces the parsing half of load_plan
+ * (sengine/csrc/sengine_exec.cu:516) for this library's file layout. */
+int snn_engine_check_file(const char* path, int32_t* n_nodes, int32_t* n_tensors);
+
+/* Loads an engine file onto the current device (cudaMalloc of the activation
+ * arena and the parameter blob).  Replaces load_plan
+ * (sengine/csrc/sengine_exec.cu:516) and the per-node set-up calls of the
+ * reference executor (sengine_create / sengine_set_*_node,
+ * sengine/csrc/cpp_executor.cu:595-874). */
+int snn_engine_load(const char* path, snn_engine** out);
+
+/* Timesteps, batch, and byte sizes of the images ([B][C][H][W] fp32) and
+ * logits ([B][classes] fp32) of a loaded engine. */
+int snn_engine_io(const snn_engine* e, int32_t* T, int32_t* B, size_t* image_bytes,
+                  size_t* logit_bytes);
+
+/* Captures the node loop on `stream` (not the legacy default stream) into a
+ * CUDA graph that later snn_engine_run calls replay
+ * (sengine_capture_graph / sengine_replay, sengine/csrc/cpp_executor.cu:1270-1293). */
+int snn_engine_capture(snn_engine* e, void* stream);
+
+/* One forward on `stream` (sengine_execute, sengine/csrc/cpp_executor.cu:883-1194):
+ * images (host or device, fp32) are copied into the engine's input buffer,
+ * the nodes run (or the captured graph is replayed), and the logits are
+ * copied to `logits` (host or device) -- all asynchronously on `stream`.
+ * A host buffer must be pinned for the copies to overlap other work and
+ * must stay valid until the stream reaches the copy.  images or logits may
+ * be null to reuse / leave the engine's own buffers. */
+int snn_engine_run(snn_engine* e, const float* images, float* logits, void* stream);
+
+/* Frees the graph, the arena and the parameters (sengine_destroy,
+ * sengine/csrc/cpp_executor.cu:609-629). */
+void snn_engine_destroy(snn_engine* e);
+
 #ifdef __cplusplus
 }
 #endif

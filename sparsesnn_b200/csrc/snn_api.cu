@@ -1008,3 +1008,5 @@ int snn_get_device_error(uint32_t* code, int reset) {
 }
 
 }  // extern "C"
+
+#include "snn_engine.cuh"

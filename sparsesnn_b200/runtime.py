@@ -41,6 +41,8 @@ EXPORTED = (
     "snn_stem_forward", "snn_spikformer_attn_forward", "snn_add_lif_forward",
     "snn_maxpool_lif_forward",
     "snn_head_forward", "snn_get_device_error", "snn_last_error_message",
+    "snn_engine_check_file", "snn_engine_load", "snn_engine_io", "snn_engine_capture",
+    "snn_engine_run", "snn_engine_destroy",
 )
 
 
@@ -89,6 +91,14 @@ def _declare(lib):
                                         ctypes.c_int),
         "snn_get_device_error": ([ctypes.POINTER(ctypes.c_uint32), ctypes.c_int], ctypes.c_int),
         "snn_last_error_message": ([], ctypes.c_char_p),
+        "snn_engine_check_file": ([ctypes.c_char_p, ctypes.POINTER(i32), ctypes.POINTER(i32)],
+                                  ctypes.c_int),
+        "snn_engine_load": ([ctypes.c_char_p, ctypes.POINTER(P)], ctypes.c_int),
+        "snn_engine_io": ([P, ctypes.POINTER(i32), ctypes.POINTER(i32), ctypes.POINTER(ctypes.c_size_t),
+                           ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
+        "snn_engine_capture": ([P, P], ctypes.c_int),
+        "snn_engine_run": ([P, P, P, P], ctypes.c_int),
+        "snn_engine_destroy": ([P], None),
     }
     for name, (args, res) in sig.items():
         f = getattr(lib, name)
