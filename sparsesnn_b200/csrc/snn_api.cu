@@ -117,16 +117,20 @@ HaloKernel halo_kernel_fn(int bn, bool m64, int mode, bool res) {
 
 using HsKernel = void (*)(const snn::ConvParams);
 
-HsKernel hs_kernel_fn(int mode, bool res) {
+template <bool SMALL>
+HsKernel hs_kernel_fn_t(int mode, bool res) {
   switch (mode * 2 + (res ? 1 : 0)) {
-    case 0: return snn::fused_sparse_conv_halo_stream_kernel<snn::kModeLifHalf, false>;
-    case 1: return snn::fused_sparse_conv_halo_stream_kernel<snn::kModeLifHalf, true>;
-    case 2: return snn::fused_sparse_conv_halo_stream_kernel<snn::kModeLifDiv, false>;
-    case 3: return snn::fused_sparse_conv_halo_stream_kernel<snn::kModeLifDiv, true>;
-    case 4: return snn::fused_sparse_conv_halo_stream_kernel<snn::kModeIf, false>;
-    case 5: return snn::fused_sparse_conv_halo_stream_kernel<snn::kModeIf, true>;
-    default: return snn::fused_sparse_conv_halo_stream_kernel<snn::kModeNone, false>;
+    case 0: return snn::fused_sparse_conv_halo_stream_kernel<snn::kModeLifHalf, false, SMALL>;
+    case 1: return snn::fused_sparse_conv_halo_stream_kernel<snn::kModeLifHalf, true, SMALL>;
+    case 2: return snn::fused_sparse_conv_halo_stream_kernel<snn::kModeLifDiv, false, SMALL>;
+    case 3: return snn::fused_sparse_conv_halo_stream_kernel<snn::kModeLifDiv, true, SMALL>;
+    case 4: return snn::fused_sparse_conv_halo_stream_kernel<snn::kModeIf, false, SMALL>;
+    case 5: return snn::fused_sparse_conv_halo_stream_kernel<snn::kModeIf, true, SMALL>;
+    default: return snn::fused_sparse_conv_halo_stream_kernel<snn::kModeNone, false, SMALL>;
   }
+}
+HsKernel hs_kernel_fn(int mode, bool res, bool small) {
+  return small ? hs_kernel_fn_t<true>(mode, res) : hs_kernel_fn_t<false>(mode, res);
 }
 
 using StemKernel = void (*)(const snn::StemParams);
@@ -237,10 +241,12 @@ int ensure_init() {
             return g_init_status = fail(SNN_E_CUDA, "smem attribute: %s", cudaGetErrorString(e));
         }
       }
-      e = cudaFuncSetAttribute(hs_kernel_fn(mode, res != 0),
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, snn::kHsSmemBytes);
-      if (e != cudaSuccess)
-        return g_init_status = fail(SNN_E_CUDA, "smem attribute: %s", cudaGetErrorString(e));
+      for (int small = 0; small < 2; ++small) {
+        e = cudaFuncSetAttribute(hs_kernel_fn(mode, res != 0, small != 0),
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, snn::kHsSmemBytes);
+        if (e != cudaSuccess)
+          return g_init_status = fail(SNN_E_CUDA, "smem attribute: %s", cudaGetErrorString(e));
+      }
     }
   }
   e = cudaFuncSetAttribute(snn::spikformer_attn_lif_kernel<32>,
@@ -325,7 +331,8 @@ int select_variant(const snn_conv_desc* d, const Geometry& g) {
   // Streamed weights: the streaming halo kernel loads each tile's input halo
   // once for all nine taps and T <= 4 timesteps (the general kernel loads a
   // box per tap), measured faster on 8x8 and 12x12 images.
-  if (g.OH >= 8 && g.OW >= 8 && d->T <= snn::kHsMaxT) return SNN_VARIANT_HALO_STREAM;
+  if (((g.OH >= 8 && g.OW >= 8) || (g.OH == 4 && g.OW == 4)) && d->T <= snn::kHsMaxT)
+    return SNN_VARIANT_HALO_STREAM;
   return SNN_VARIANT_GENERIC;
 }
 
@@ -570,35 +577,54 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
   // at least 8x8 whose weights do not fit in shared memory, T <= 4.
   if (variant == SNN_VARIANT_HALO_STREAM) {
     snn::ConvParams ph = p;
-    ph.tw = 8; ph.th = 8; ph.tn = 1;
-    ph.tiles_w = (g.OW + 7) / 8;
-    ph.tiles_h = (g.OH + 7) / 8;
-    ph.n_px_tiles = ph.tiles_w * ph.tiles_h * d->B;
+    // 4x4 images: a tile is 4 whole images, loaded as three column-shifted
+    // boxes per input slice (the kernel's SMALL form).
+    const bool small = g.OH == 4 && g.OW == 4;
     const size_t C = d->Cin, W = d->W, H = d->H, B = d->B;
-    // Activations seen as (C, W, T, H, B): one box holds a tile's halo for
-    // all T timesteps as [halo row][timestep][halo column].
-    cuuint64_t dims[5] = {C, W, static_cast<cuuint64_t>(d->T), H, B};
-    cuuint64_t strides[4] = {C * 2, B * H * W * C * 2, W * C * 2, H * W * C * 2};
-    cuuint32_t box[5] = {static_cast<cuuint32_t>(snn::kKB), 10, static_cast<cuuint32_t>(d->T), 10, 1};
-    if ((st = encode(&ph.tmap_b[0], 5, data, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)))
-      return st;
-    {  // weights as (Cin/2 el of one tap, Fpad rows, 9 taps): one box = 3 taps x 128 rows
+    if (small) {
+      ph.tw = 4; ph.th = 4; ph.tn = 4;
+      ph.tiles_w = 1; ph.tiles_h = 1;
+      ph.n_px_tiles = (d->B + 3) / 4;
+      // Activations seen as (C, W, T, B, H): [halo row][image][timestep][4 columns].
+      cuuint64_t dims[5] = {C, W, static_cast<cuuint64_t>(d->T), B, H};
+      cuuint64_t strides[4] = {C * 2, B * H * W * C * 2, H * W * C * 2, W * C * 2};
+      cuuint32_t box[5] = {static_cast<cuuint32_t>(snn::kKB), 4, static_cast<cuuint32_t>(d->T), 4, 6};
+      if ((st = encode(&ph.tmap_b[0], 5, data, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)))
+        return st;
+      // Weights as (Cin/2 el of one tap, Fpad rows, kh, kw): one box = taps (0..2, kw).
+      cuuint64_t wd[4] = {C / 2, static_cast<cuuint64_t>(g.Fpad), 3, 3};
+      cuuint64_t ws[3] = {static_cast<cuuint64_t>(g.K / 2) * 2, 3 * (C / 2) * 2, (C / 2) * 2};
+      cuuint32_t wb[4] = {snn::kKB / 2, snn::kBM, 3, 1};
+      if ((st = encode(&ph.tmap_b[1], 4, weight, wd, ws, wb, CU_TENSOR_MAP_SWIZZLE_64B))) return st;
+    } else {
+      ph.tw = 8; ph.th = 8; ph.tn = 1;
+      ph.tiles_w = (g.OW + 7) / 8;
+      ph.tiles_h = (g.OH + 7) / 8;
+      ph.n_px_tiles = ph.tiles_w * ph.tiles_h * d->B;
+      // Activations seen as (C, W, T, H, B): one box holds a tile's halo for
+      // all T timesteps as [halo row][timestep][halo column].
+      cuuint64_t dims[5] = {C, W, static_cast<cuuint64_t>(d->T), H, B};
+      cuuint64_t strides[4] = {C * 2, B * H * W * C * 2, W * C * 2, H * W * C * 2};
+      cuuint32_t box[5] = {static_cast<cuuint32_t>(snn::kKB), 10, static_cast<cuuint32_t>(d->T), 10, 1};
+      if ((st = encode(&ph.tmap_b[0], 5, data, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)))
+        return st;
+      // weights as (Cin/2 el of one tap, Fpad rows, 9 taps): one box = 3 taps x 128 rows
       cuuint64_t wd[3] = {C / 2, static_cast<cuuint64_t>(g.Fpad), 9};
       cuuint64_t ws[2] = {static_cast<cuuint64_t>(g.K / 2) * 2, (C / 2) * 2};
       cuuint32_t wb[3] = {snn::kKB / 2, snn::kBM, 3};
       if ((st = encode(&ph.tmap_b[1], 3, weight, wd, ws, wb, CU_TENSOR_MAP_SWIZZLE_64B))) return st;
     }
-    if (spikes) {  // spikes as (F, OW, OH, B, T): a warp stores {32 ch, 8 w, 4 h}
+    if (spikes) {  // spikes as (F, OW, OH, B, T): a warp stores {32 ch, 8 w, 4 h} ({32, 4, 4, 2} SMALL)
       const size_t F = d->Cout, OW = g.OW, OH = g.OH;
       cuuint64_t odims[5] = {F, OW, OH, B, static_cast<cuuint64_t>(d->T)};
       cuuint64_t ostrides[4] = {F * 2, OW * F * 2, OH * OW * F * 2, B * OH * OW * F * 2};
-      cuuint32_t obox[5] = {32, 8, 4, 1, 1};
+      cuuint32_t obox[5] = {32, small ? 4u : 8u, 4, small ? 2u : 1u, 1};
       if ((st = encode(&ph.tmap_out, 5, out, odims, ostrides, obox, CU_TENSOR_MAP_SWIZZLE_64B))) return st;
       ph.tma_out = 1;
     }
     const int per_m = std::max(1, std::min(ph.n_px_tiles, g_num_sms / ph.n_m));
     const long long grid = static_cast<long long>(per_m) * ph.n_m;
-    cudaError_t e = launch_pdl(hs_kernel_fn(mode, residual != nullptr),
+    cudaError_t e = launch_pdl(hs_kernel_fn(mode, residual != nullptr, small),
                                dim3(static_cast<unsigned>(grid)), dim3(snn::kHaloThreads),
                                snn::kHsSmemBytes, stream, ph);
     if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));

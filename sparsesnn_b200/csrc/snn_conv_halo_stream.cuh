@@ -15,6 +15,15 @@
 // costs a fixed few hundred cycles whatever its size, so the kernel issues
 // as few, large boxes as it can.
 //
+// SMALL (4x4 images, e.g. ResNet stage 4 on CIFAR): a tile is 4 whole images.
+// Rows of 4 pixels cannot form the 8-pixel groups of one halo row, so per
+// slice the producer loads three column-shifted boxes (kw = 0, 1, 2) from a
+// (C, W, T, B, H) view: [halo row][image][timestep][4 columns], 6 x 4 x T x 4
+// pixel rows.  Tap (kh, kw) then reads 16*T*4 CONSECUTIVE rows of box kw
+// starting at halo row kh (a plain K-major operand, groups 1024 bytes
+// apart); accumulator column ((r*4 + image)*T + t)*4 + c.  Weights come per
+// kw as one 4-D box of the three taps (0..2, kw).
+//
 // Warp roles: 0..7 epilogue, 8..11 metadata, then 10 = MMA + TMEM owner,
 // 11 = halo loads, 8 and 9 = weight loads.
 #pragma once
@@ -29,11 +38,12 @@ constexpr int kHsAStages = 4;
 constexpr int kHsAStageBytes = 3 * kABytes;        // one kernel row: 3 taps, one 3D TMA box
 constexpr int kHsHaloBytes = 10 * 10 * kKB * 2;    // 12800 per timestep
 constexpr int kHsHaloStride = kHsMaxT * kHsHaloBytes;  // 51200 (1024-aligned)
+constexpr int kHsSmallBytes = 6 * 4 * 4 * kKB * 2;     // SMALL: one kw box per timestep (12288)
 constexpr int kHsMetaCol = 256;
 constexpr int kHsSmemBytes = kHsAStages * kHsAStageBytes + kHsHaloStages * kHsHaloStride +
                              kEpiWarps * kXposeBytes + 512 + 1024;
 
-template <int MODE, bool RES>
+template <int MODE, bool RES, bool SMALL = false>
 __global__ void __launch_bounds__(kHaloThreads, 1)
 fused_sparse_conv_halo_stream_kernel(const __grid_constant__ ConvParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -86,12 +96,23 @@ fused_sparse_conv_halo_stream_kernel(const __grid_constant__ ConvParams p) {
     const int row = q * 32 + lane;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
     const uint32_t* src = p.meta + (static_cast<size_t>(m_tile) * n_meta) * kBM + row;
-    for (int j = 0; j < n_meta; j += 8) {
-      uint32_t r[8];
+    // Up to 40 columns' loads in flight per lane (a 512-channel 3x3 layer has
+    // 144 metadata columns: four round trips instead of eighteen).
+    constexpr int kChunk = 40;
+    for (int j = 0; j < n_meta; j += kChunk) {
+      uint32_t r[kChunk];
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
+      for (int i = 0; i < kChunk; ++i)
         r[i] = (j + i < n_meta) ? __ldg(src + static_cast<size_t>(j + i) * kBM) : 0x44444444u;
-      tmem_st8(lane_base + kHsMetaCol + j, r);
+#pragma unroll
+      for (int u = 0; u < kChunk / 8; ++u) {
+        if (j + 8 * u < n_meta) {
+          uint32_t r8[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) r8[i] = r[8 * u + i];
+          tmem_st8(lane_base + kHsMetaCol + j + 8 * u, r8);
+        }
+      }
     }
     tmem_st_wait();
     tc_fence_before();
@@ -116,16 +137,25 @@ fused_sparse_conv_halo_stream_kernel(const __grid_constant__ ConvParams p) {
           const int cb = (cbi + cb_rot) % p.cin_blocks;
           if (*abort_flag) { stop = true; break; }
           if (halo_warp) {
-            if (!mbar_wait_bounded(&h_empty[hs], hph ^ 1, p.timeout_ns)) {
-              atomicOr(p.err, kErrTimeoutEmpty); *abort_flag = 1; stop = true; break;
+            for (int u = 0; u < (SMALL ? 3 : 1) && !stop; ++u) {
+              if (!mbar_wait_bounded(&h_empty[hs], hph ^ 1, p.timeout_ns)) {
+                atomicOr(p.err, kErrTimeoutEmpty); *abort_flag = 1; stop = true; break;
+              }
+              if constexpr (SMALL) {
+                // Box kw = u: coordinates (channel, column, timestep, image, row).
+                mbar_arrive_expect_tx(&h_full[hs], T * kHsSmallBytes);
+                tma_load_5d(sH + hs * kHsHaloStride, &p.tmap_b[0], &h_full[hs], cb * kKB, u - 1, 0,
+                            tc.n0, -1);
+              } else {
+                // All T halos in one box: coordinates (channel, column,
+                // timestep, row, image).
+                mbar_arrive_expect_tx(&h_full[hs], T * kHsHaloBytes);
+                tma_load_5d(sH + hs * kHsHaloStride, &p.tmap_b[0], &h_full[hs], cb * kKB,
+                            tc.w0 - 1, 0, tc.h0 - 1, tc.n0);
+              }
+              ++h_issued;
+              if (++hs == kHsHaloStages) { hs = 0; hph ^= 1; }
             }
-            // All T halos in one box: coordinates (channel, column,
-            // timestep, row, image).
-            mbar_arrive_expect_tx(&h_full[hs], T * kHsHaloBytes);
-            tma_load_5d(sH + hs * kHsHaloStride, &p.tmap_b[0], &h_full[hs], cb * kKB,
-                        tc.w0 - 1, 0, tc.h0 - 1, tc.n0);
-            ++h_issued;
-            if (++hs == kHsHaloStages) { hs = 0; hph ^= 1; }
             continue;
           }
           for (int kh = 0; kh < 3 && !stop; ++kh, ++a_seq) {
@@ -134,10 +164,16 @@ fused_sparse_conv_halo_stream_kernel(const __grid_constant__ ConvParams p) {
               if (!mbar_wait_bounded(&a_empty[as], aph ^ 1, p.timeout_ns)) {
                 atomicOr(p.err, kErrTimeoutEmpty); *abort_flag = 1; stop = true; break;
               }
-              // Weights of taps (kh, 0..2) for slice cb: [tap][128 rows][32 el].
               mbar_arrive_expect_tx(&a_full[as], kHsAStageBytes);
-              tma_load_3d(sA + as * kHsAStageBytes, &p.tmap_b[1], &a_full[as], cb * (kKB / 2),
-                          m_tile * kBM, kh * 3);
+              if constexpr (SMALL) {
+                // Weights of taps (0..2, kw = kh loop index): [kh][128 rows][32 el].
+                tma_load_4d(sA + as * kHsAStageBytes, &p.tmap_b[1], &a_full[as], cb * (kKB / 2),
+                            m_tile * kBM, 0, kh);
+              } else {
+                // Weights of taps (kh, 0..2) for slice cb: [tap][128 rows][32 el].
+                tma_load_3d(sA + as * kHsAStageBytes, &p.tmap_b[1], &a_full[as], cb * (kKB / 2),
+                            m_tile * kBM, kh * 3);
+              }
               ++a_issued; a_last = a_seq;
             }
             if (++as == kHsAStages) { as = 0; aph ^= 1; }
@@ -178,17 +214,44 @@ fused_sparse_conv_halo_stream_kernel(const __grid_constant__ ConvParams p) {
         tc_fence_after();
         for (int cbi = 0; cbi < p.cin_blocks && !stop; ++cbi) {
           const int cb = (cbi + cb_rot) % p.cin_blocks;
-          if (!mbar_wait_bounded(&h_full[hs], hph, p.timeout_ns)) {
-            atomicOr(p.err, kErrTimeoutFull); *abort_flag = 1; stop = true; break;
+          if constexpr (!SMALL) {
+            if (!mbar_wait_bounded(&h_full[hs], hph, p.timeout_ns)) {
+              atomicOr(p.err, kErrTimeoutFull); *abort_flag = 1; stop = true; break;
+            }
           }
-          const uint32_t hstage = h_base + hs * kHsHaloStride;
           tc_fence_after();
-          for (int kh = 0; kh < 3; ++kh) {
+          for (int kh = 0; kh < 3; ++kh) {      // SMALL: this index is kw
+            if constexpr (SMALL) {
+              if (!mbar_wait_bounded(&h_full[hs], hph, p.timeout_ns)) {
+                atomicOr(p.err, kErrTimeoutFull); *abort_flag = 1; stop = true; break;
+              }
+            }
+            const uint32_t hstage = h_base + hs * kHsHaloStride;
             if (!mbar_wait_bounded(&a_full[as], aph, p.timeout_ns)) {
               atomicOr(p.err, kErrTimeoutFull); *abort_flag = 1; stop = true; break;
             }
             tc_fence_after();
             const uint32_t abase = a_base + as * kHsAStageBytes;
+            if constexpr (SMALL) {
+              const int kw = kh;
+#pragma unroll
+              for (int r = 0; r < 3; ++r) {     // kernel row
+                const int kb = (r * 3 + kw) * p.cin_blocks + cb;
+#pragma unroll
+                for (int s = 0; s < 2; ++s) {
+                  const uint32_t ecol = kHsMetaCol + 2 * kb + s;
+                  const uint32_t acc = (cbi > 0 || kw > 0 || r > 0 || s > 0) ? 1u : 0u;
+                  const uint64_t adesc = smem_desc_kmajor(abase + r * kABytes + 32 * s, 512, 4);
+                  const uint64_t bdesc = smem_desc_kmajor(hstage + r * (16 * T * 128) + 64 * s, 1024, 2);
+                  mma_sp_f16(tmem, adesc, bdesc, tmem + (ecol & ~1u), idesc | (ecol & 1u), acc);
+                }
+              }
+              mma_commit(&a_empty[as]);
+              if (++as == kHsAStages) { as = 0; aph ^= 1; }
+              mma_commit(&h_empty[hs]);
+              if (++hs == kHsHaloStages) { hs = 0; hph ^= 1; }
+              continue;
+            }
 #pragma unroll
             for (int kw = 0; kw < 3; ++kw) {
               const int kb = (kh * 3 + kw) * p.cin_blocks + cb;
@@ -208,8 +271,10 @@ fused_sparse_conv_halo_stream_kernel(const __grid_constant__ ConvParams p) {
             if (++as == kHsAStages) { as = 0; aph ^= 1; }
           }
           if (stop) break;
-          mma_commit(&h_empty[hs]);          // this slice's halos are consumed
-          if (++hs == kHsHaloStages) { hs = 0; hph ^= 1; }
+          if constexpr (!SMALL) {
+            mma_commit(&h_empty[hs]);        // this slice's halos are consumed
+            if (++hs == kHsHaloStages) { hs = 0; hph ^= 1; }
+          }
         }
         if (stop) break;
         for (int t = 0; t < T; ++t) mma_commit(&acc_full[t]);
@@ -247,9 +312,17 @@ fused_sparse_conv_halo_stream_kernel(const __grid_constant__ ConvParams p) {
     bool stop = false;
     for (int pt = first_pt; pt < p.n_px_tiles && !stop; pt += pt_step) {
       const TileCoord tc = tile_coord(p, pt);
-      const int col = half * 32 + lane;
-      const int oh = tc.h0 + col / 8, ow = tc.w0 + (col & 7);
-      const int my_px = (oh < p.OH && ow < p.OW) ? (tc.n0 * p.OH + oh) * p.OW + ow : -1;
+      int my_px;
+      if constexpr (SMALL) {
+        // Column `lane` of this half: image n0 + 2*half + lane/16, row
+        // (lane/4)%4, column lane%4 (4x4 images).
+        const int n = tc.n0 + 2 * half + (lane >> 4);
+        my_px = n < p.B ? (n * 4 + ((lane >> 2) & 3)) * 4 + (lane & 3) : -1;
+      } else {
+        const int col = half * 32 + lane;
+        const int oh = tc.h0 + col / 8, ow = tc.w0 + (col & 7);
+        my_px = (oh < p.OH && ow < p.OW) ? (tc.n0 * p.OH + oh) * p.OW + ow : -1;
+      }
       int rows[4];
       store_rows(my_px, lane, rows);
       float v[32];
@@ -269,11 +342,18 @@ fused_sparse_conv_halo_stream_kernel(const __grid_constant__ ConvParams p) {
         tc_fence_after();
         float acc[32];
         if (warp_live) {
-          // Output rows 4*half + j at timestep t: 8 columns each.
           uint32_t r[32];
+          if constexpr (SMALL) {
+            // Image 2*half + j/4, row j%4 at timestep t: 4 columns each.
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-            tmem_ld8_nowait(lane_base + 8 * (T * (4 * half + j) + t), r + 8 * j);
+            for (int j = 0; j < 8; ++j)
+              tmem_ld4_nowait(lane_base + 4 * (((j & 3) * 4 + 2 * half + (j >> 2)) * T + t), r + 4 * j);
+          } else {
+            // Output rows 4*half + j at timestep t: 8 columns each.
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              tmem_ld8_nowait(lane_base + 8 * (T * (4 * half + j) + t), r + 8 * j);
+          }
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) acc[i] = __uint_as_float(r[i]);
@@ -302,7 +382,8 @@ fused_sparse_conv_halo_stream_kernel(const __grid_constant__ ConvParams p) {
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-              tma_store_5d(&p.tmap_out, xb, cbase, tc.w0, tc.h0 + 4 * half, tc.n0, t);
+              if constexpr (SMALL) tma_store_5d(&p.tmap_out, xb, cbase, 0, 0, tc.n0 + 2 * half, t);
+              else tma_store_5d(&p.tmap_out, xb, cbase, tc.w0, tc.h0 + 4 * half, tc.n0, t);
               bulk_commit_group();
             }
             ++n_st;

@@ -224,6 +224,12 @@ __device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t (&r)[3
         "=r"(r[31])
       : "r"(taddr));
 }
+// 4 consecutive columns of this thread's TMEM lane (no wait).
+__device__ __forceinline__ void tmem_ld4_nowait(uint32_t taddr, uint32_t* r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(taddr));
+}
 // 8 consecutive columns of this thread's TMEM lane (no wait).
 __device__ __forceinline__ void tmem_ld8_nowait(uint32_t taddr, uint32_t* r) {
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"

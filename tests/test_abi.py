@@ -96,7 +96,8 @@ def test_forward_without_device_fails_loudly(_lib):
     (dict(Cin=256, H=8, W=8, Cout=256), rt.SNN_VARIANT_HALO_STREAM),
     (dict(Cin=512, H=16, W=16, Cout=512), rt.SNN_VARIANT_HALO_STREAM),
     (dict(Cin=256, H=8, W=8, T=5), rt.SNN_VARIANT_GENERIC),          # T > 4
-    (dict(Cin=512, H=4, W=4), rt.SNN_VARIANT_GENERIC),               # image < 8x8
+    (dict(Cin=512, H=4, W=4), rt.SNN_VARIANT_HALO_STREAM),           # 4x4: four images per tile
+    (dict(Cin=512, H=6, W=6), rt.SNN_VARIANT_GENERIC),               # other images < 8x8
     (dict(Cin=64, H=32, W=32, stride=2), rt.SNN_VARIANT_GENERIC),
     (dict(Cin=64, H=32, W=32, KH=1, KW=1, pad=0), rt.SNN_VARIANT_GENERIC),
     (dict(Cin=128, H=32, W=32, flags=rt.SNN_FLAG_FORCE_GENERIC), rt.SNN_VARIANT_GENERIC),

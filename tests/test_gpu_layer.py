@@ -247,14 +247,15 @@ def test_size_independent_properties(cuda_device):
 @pytest.mark.parametrize("T", [1, 2, 3, 4])
 @pytest.mark.parametrize("residual", [False, True], ids=["plain", "res"])
 def test_halo_stream_variant(cuda_device, T, residual):
-    """Streaming-weight halo kernel (Cin=256 on 12x12, 8x12 and 8x8 images)
-    against the oracle, for every timestep count it serves (one N = 64*T MMA
-    per tap over the [row][timestep][column] halo) and with the SEW
+    """Streaming-weight halo kernel (Cin=256 on 12x12, 8x12, 8x8 and 4x4
+    images; 4x4 takes four images per tile from three column-shifted boxes,
+    here with a ragged last tile of 3 images) against the oracle, for every
+    timestep count it serves (one N = 64*T MMA per tap) and with the SEW
     residual."""
     import torch
     from sparsesnn_b200 import runtime as rt
     from sparsesnn_b200.layer import SparseConvBNLIF, fold_bn
-    for (H, W) in ((12, 12), (8, 12), (8, 8)):
+    for (H, W) in ((12, 12), (8, 12), (8, 8), (4, 4)):
         x, w, bn = L.make_config0(seed=10 + T, T=T, B=3, C=256, F=256, H=H, W=W)
         scale, bias = fold_bn(bn.gamma, bn.beta, bn.mean, bn.var)
         layer = SparseConvBNLIF(w, scale, bias, T=T, B=3, H=H, W=W)
