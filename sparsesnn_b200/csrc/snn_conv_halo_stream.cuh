@@ -246,25 +246,23 @@ fused_sparse_conv_halo_stream_kernel(const __grid_constant__ ConvParams p) {
                   mma_sp_f16(tmem, adesc, bdesc, tmem + (ecol & ~1u), idesc | (ecol & 1u), acc);
                 }
               }
-              mma_commit(&a_empty[as]);
-              if (++as == kHsAStages) { as = 0; aph ^= 1; }
-              mma_commit(&h_empty[hs]);
+              mma_commit(&h_empty[hs]);        // this kw box is consumed
               if (++hs == kHsHaloStages) { hs = 0; hph ^= 1; }
-              continue;
-            }
+            } else {
 #pragma unroll
-            for (int kw = 0; kw < 3; ++kw) {
-              const int kb = (kh * 3 + kw) * p.cin_blocks + cb;
-              const uint32_t boff = static_cast<uint32_t>(kh * T * 10 + kw) * 128;
+              for (int kw = 0; kw < 3; ++kw) {
+                const int kb = (kh * 3 + kw) * p.cin_blocks + cb;
+                const uint32_t boff = static_cast<uint32_t>(kh * T * 10 + kw) * 128;
 #pragma unroll
-              for (int s = 0; s < 2; ++s) {
-                const uint32_t ecol = kHsMetaCol + 2 * kb + s;
-                const uint32_t e_addr = tmem + (ecol & ~1u);
-                const uint32_t id = idesc | (ecol & 1u);
-                const uint64_t adesc = smem_desc_kmajor(abase + kw * kABytes + 32 * s, 512, 4);
-                const uint32_t acc = (cbi > 0 || kh > 0 || kw > 0 || s > 0) ? 1u : 0u;
-                mma_sp_f16(tmem, adesc, smem_desc_kmajor(hstage + boff + 64 * s, 1280, 2), e_addr, id,
-                           acc);
+                for (int s = 0; s < 2; ++s) {
+                  const uint32_t ecol = kHsMetaCol + 2 * kb + s;
+                  const uint32_t e_addr = tmem + (ecol & ~1u);
+                  const uint32_t id = idesc | (ecol & 1u);
+                  const uint64_t adesc = smem_desc_kmajor(abase + kw * kABytes + 32 * s, 512, 4);
+                  const uint32_t acc = (cbi > 0 || kh > 0 || kw > 0 || s > 0) ? 1u : 0u;
+                  mma_sp_f16(tmem, adesc, smem_desc_kmajor(hstage + boff + 64 * s, 1280, 2), e_addr, id,
+                             acc);
+                }
               }
             }
             mma_commit(&a_empty[as]);
