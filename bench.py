@@ -453,7 +453,7 @@ def run_ours(args, rank, world, local_rank):
                              "unit": "TFLOP/s", "frac": achieved / sparse_peak,
                              "traffic": traffic,
                              "kernel": "fused sparse conv+BN+LIF kernels, 19 launches/forward "
-                                       "(halo4 x4, halo x3, halo_stream x3, general x9)",
+                                       "(halo4 x4, halo x3, halo_stream x6, general x6)",
                              "peak_note": f"2:4 sparse ceiling = 2 x {peak_kind} dense bf16 "
                                           f"{bf16_peak} TFLOP/s; FLOPs dense-equivalent",
                              "flops_per_forward": flops, "kernel_ms_per_forward": conv_ms,
