@@ -142,8 +142,19 @@ int parse_engine_file(const char* path, SnnEngineHeader* h, std::vector<SnnEngin
       }
       case kOpAddLif:
       case kOpMaxPoolLif: {
+        if (d.T < 1 || d.B < 1 || d.H < 1 || d.W < 1 || d.Cout < 1 || d.flags != 0)
+          return fail(SNN_E_INVALID, "engine node %u (glue): bad shape or flags", n);
         const uint64_t in_need = uint64_t(d.T) * d.B * d.H * d.W * d.Cout * 2;
-        if (in_bytes < in_need || d.flags != 0 ||
+        uint64_t out_need = in_need;
+        if (nd.op == kOpMaxPoolLif) {
+          if (d.KH < 1 || d.KW < 1 || d.stride < 1 || d.pad < 0)
+            return fail(SNN_E_INVALID, "engine node %u (maxpool): bad window", n);
+          const int64_t oh = (int64_t(d.H) + 2 * d.pad - d.KH) / d.stride + 1;
+          const int64_t ow = (int64_t(d.W) + 2 * d.pad - d.KW) / d.stride + 1;
+          if (oh < 1 || ow < 1) return fail(SNN_E_INVALID, "engine node %u (maxpool): empty output", n);
+          out_need = uint64_t(d.T) * d.B * oh * ow * d.Cout * 2;
+        }
+        if (in_bytes < in_need || out_bytes < out_need ||
             (nd.op == kOpAddLif && (nd.in1 == kNoTensor || (*tensors)[nd.in1].bytes < in_need)))
           return fail(SNN_E_INVALID, "engine node %u (glue): sizes out of range", n);
         break;

@@ -5,7 +5,8 @@ and damaged files (magic, version, size, offsets, node kinds, tensor ids)
 are rejected with SNN_E_INVALID.  GPU: an engine saved from a SEW-ResNet-18
 replica gives the Python driver's logits exactly (the same kernels on the
 same data), eagerly and replayed from its CUDA graph, with host and device
-buffers, call after call.
+buffers, call after call; an engine with the glue node kinds gives the
+logits of the same entry points called one by one.
 """
 import ctypes
 import struct
@@ -120,5 +121,80 @@ def test_engine_matches_python_driver(cuda_device, tmp_path):
         eng.run(xd.data_ptr(), out_d.data_ptr(), s)
         s.synchronize()
         assert torch.equal(out_d, r)
+    assert rt.device_error() == 0
+    eng.close()
+
+
+@pytest.mark.gpu
+def test_engine_glue_nodes_match_direct_calls(cuda_device, tmp_path):
+    """An engine with the other node kinds -- stem, MaxPool(3,2,1)+LIF, Add+LIF,
+    a 3x3 conv with the SEW residual, head -- gives the logits of the same
+    entry points called one by one."""
+    import torch
+    from sparsesnn_b200.layer import SparseConvBNLIF
+    from sparsesnn_b200.pruning import prune_conv_2_4
+    lib = rt.load()
+    T, B, H, C, F, NC = 4, 4, 32, 64, 64, 10
+    rng = np.random.default_rng(9)
+    f32 = lambda *sh: rng.standard_normal(sh).astype(np.float32)  # noqa: E731
+    stem_w = f32(C, 3, 3, 3) * 0.3
+    stem_s, stem_b = np.abs(f32(C)) + 0.5, f32(C) * 0.1
+    stem_d = rt.make_desc(T=T, B=B, Cin=3, H=H, W=H, Cout=C, KH=3, KW=3, pad=1)
+    # IF for the pooled spikes (a tau = 2 LIF fed 0/1 never reaches 1.0 in 4 steps)
+    pool_d = rt.make_desc(T=T, B=B, Cin=C, H=H, W=H, Cout=C, KH=3, KW=3, stride=2, pad=1,
+                          neuron="if")
+    P = H // 2
+    add_d = rt.make_desc(T=T, B=B, Cin=C, H=P, W=P, Cout=C, KH=1, KW=1, pad=0, neuron="if",
+                         v_threshold=1.5)
+    conv = SparseConvBNLIF(prune_conv_2_4(f32(F, C, 3, 3) * 0.1), np.ones(F, np.float32),
+                           np.zeros(F, np.float32), T=T, B=B, H=P, W=P)
+    fc_w, fc_b = f32(NC, F) * 0.1, f32(NC) * 0.1
+
+    w = ef._Writer()
+    images = w.tensor(B * 3 * H * H * 4, ef.F32)
+    a0 = w.tensor(T * B * H * H * C * 2, ef.F16)
+    p0 = w.tensor(T * B * P * P * C * 2, ef.F16)
+    q0 = w.tensor(T * B * P * P * C * 2, ef.F16)
+    r0 = w.tensor(T * B * P * P * F * 2, ef.F16)
+    logits = w.tensor(B * NC * 4, ef.F32)
+    w.node(ef.OP_STEM, images, ef.NO_TENSOR, a0, stem_d,
+           (w.param(stem_w), w.param(stem_s), w.param(stem_b), 0), (1, 0, 0, 0, 0))
+    w.node(ef.OP_MAXPOOL_LIF, a0, ef.NO_TENSOR, p0, pool_d)
+    w.node(ef.OP_ADD_LIF, p0, p0, q0, add_d)
+    w.node(ef.OP_CONV, q0, p0, r0, ef._conv_desc(conv),
+           (w.param(conv.weight_blob.cpu().numpy()), w.param(conv.bn_scale.cpu().numpy()),
+            w.param(conv.bn_bias.cpu().numpy()), 0))
+    w.node(ef.OP_HEAD, r0, ef.NO_TENSOR, logits, None, (w.param(fc_w), w.param(fc_b), 0, 0),
+           (T, B, P * P, F, NC))
+    path = tmp_path / "glue.snne"
+    w.write(path, images, logits, T, B)
+    assert ef.check_file(path) == (5, 6)
+
+    x = torch.from_numpy(f32(B, 3, H, H)).cuda()
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
+    sw, ss, sb, fw, fb = dev(stem_w), dev(stem_s), dev(stem_b), dev(fc_w), dev(fc_b)
+    a = torch.empty((T * B, H, H, C), dtype=torch.float16, device="cuda")
+    p = torch.empty((T * B, P, P, C), dtype=torch.float16, device="cuda")
+    q = torch.empty_like(p)
+    r = torch.empty((T * B, P, P, F), dtype=torch.float16, device="cuda")
+    ref = torch.empty((B, NC), dtype=torch.float32, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    rt.check(lib.snn_stem_forward(stem_d, 1, x.data_ptr(), sw.data_ptr(), ss.data_ptr(), sb.data_ptr(),
+                                  a.data_ptr(), s))
+    rt.check(lib.snn_maxpool_lif_forward(pool_d, a.data_ptr(), None, p.data_ptr(), s))
+    rt.check(lib.snn_add_lif_forward(add_d, p.data_ptr(), p.data_ptr(), None, q.data_ptr(), s))
+    conv(q, residual=p, out=r)
+    rt.check(lib.snn_head_forward(T, B, P * P, F, NC, r.data_ptr(), fw.data_ptr(), fb.data_ptr(),
+                                  ref.data_ptr(), s))
+    torch.cuda.synchronize()
+    assert p.float().abs().sum() > 0 and q.float().abs().sum() > 0     # spikes at every stage
+
+    eng = ef.Engine(path)
+    st = torch.cuda.Stream()
+    out = torch.empty_like(ref)
+    for _ in range(2):
+        eng.run(x.data_ptr(), out.data_ptr(), st)
+        st.synchronize()
+        assert torch.equal(out, ref)
     assert rt.device_error() == 0
     eng.close()
