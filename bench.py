@@ -482,6 +482,10 @@ def main():
     import torch.distributed as dist
     from sparsesnn_b200 import dist as sd
     if world > 1:
+        # NCCL's version banner goes to stdout at NCCL_DEBUG=VERSION; keep
+        # rank 0's stdout to the one JSON line.
+        if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
+            os.environ["NCCL_DEBUG"] = "WARN"
         torch.cuda.set_device(local_rank)
         sd.init_from_env("nccl", timeout_s=120.0, device_id=torch.device("cuda", local_rank))
     try:
