@@ -881,6 +881,7 @@ int snn_stem_forward(const snn_conv_desc* d, int32_t Tin, const float* x, const 
   const int OW = (d->W + 2 * d->pad - d->KW) / d->stride + 1;
   if (OH < 1 || OW < 1) return fail(SNN_E_INVALID, "empty output");
   snn::StemParams p;
+  memset(&p, 0, sizeof(p));
   p.x = x; p.w = w; p.scale = bn_scale; p.bias = bn_bias;
   p.out = static_cast<__half*>(out);
   p.T = d->T; p.Tin = Tin; p.B = d->B; p.Cin = d->Cin; p.H = d->H; p.W = d->W;
@@ -904,6 +905,16 @@ int snn_stem_forward(const snn_conv_desc* d, int32_t Tin, const float* x, const 
     const long long n_tiles = static_cast<long long>(d->B) * ((OH + R - 1) / R);
     const long long nblk = std::min<long long>(n_tiles, 3LL * g_num_sms);
     if (smem <= static_cast<size_t>(kStemTcSmemMax) && n_tiles <= 0x7fffffffLL) {
+      // Spike tiles leave by TMA stores: (64 ch, OW, OH, B, T), box {64, OW, R, 1, 1}.
+      const cuuint64_t odims[5] = {64, static_cast<cuuint64_t>(OW), static_cast<cuuint64_t>(OH),
+                                   static_cast<cuuint64_t>(d->B), static_cast<cuuint64_t>(d->T)};
+      const cuuint64_t ostrides[4] = {64 * 2, static_cast<cuuint64_t>(OW) * 64 * 2,
+                                      static_cast<cuuint64_t>(OH) * OW * 64 * 2,
+                                      static_cast<cuuint64_t>(d->B) * OH * OW * 64 * 2};
+      const cuuint32_t obox[5] = {64, static_cast<cuuint32_t>(OW), static_cast<cuuint32_t>(R), 1, 1};
+      if ((reinterpret_cast<uintptr_t>(out) & 15) == 0 &&
+          encode(&p.tmap_out, 5, out, odims, ostrides, obox, CU_TENSOR_MAP_SWIZZLE_128B) == SNN_OK)
+        p.tma_out = 1;
       cudaError_t e = launch_pdl(stem_tc_fn(d->Cin, mode), dim3(static_cast<unsigned>(nblk)),
                                  dim3(snn::kStemThreads), smem, stream, p);
       if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));

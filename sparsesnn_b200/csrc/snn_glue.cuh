@@ -13,6 +13,7 @@
 namespace snn {
 
 struct StemParams {
+  CUtensorMap tmap_out;  // tensor-core path: spikes (64 ch, OW, OH, B, T), box {64, OW, rows, 1, 1}
   const float* x;      // [Tin][B][Cin][H][W] fp32
   const float* w;      // [Cout][Cin][KH][KW] fp32
   const float* scale;  // [Cout]
@@ -22,6 +23,7 @@ struct StemParams {
   float tau, decay, v_th, v_reset;
   unsigned* err;                  // device error word (tensor-core path)
   unsigned long long timeout;     // bounded-wait budget, SM cycles
+  int tma_out;                    // tensor-core path: spike tiles leave by TMA stores
 };
 
 // One thread = one output pixel x 16 consecutive output channels
@@ -167,7 +169,7 @@ __device__ __forceinline__ int sw128_f32(int r, int k) {
 
 template <int CIN, int MODE>
 __global__ void __launch_bounds__(kStemThreads, 3)
-stem_tc_kernel(const StemParams p) {
+stem_tc_kernel(const __grid_constant__ StemParams p) {
   static_assert(9 * CIN <= 32, "stem K must fit one 32-wide tile");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -227,6 +229,9 @@ stem_tc_kernel(const StemParams p) {
       xs[i] = (ih >= 0 && ih < p.H && iw >= 0 && iw < p.W)
                   ? __ldg(xin + (static_cast<size_t>(ci) * p.H + ih) * p.W + iw) : 0.f;
     }
+    // The previous tile's spike tiles (the A tiles) must be read out before
+    // the im2col rows below overwrite them.
+    if (p.tma_out && tid == 0) bulk_wait_group_read<0>();
     __syncthreads();                                  // xs ready; the previous tile's spike tiles are out
     // im2col row of this thread's pixel, split hi/lo.
 #pragma unroll
@@ -290,6 +295,10 @@ stem_tc_kernel(const StemParams p) {
     const int n16 = nrows * OW * 8;                   // 16-byte chunks of the tile's output
     for (int t = 0; t < p.T; ++t) {
       uint8_t* tile_s = smem + (t & 1) * kStemATile;  // the A tiles are free after the MMAs
+      if (p.tma_out && t >= 2) {                      // this tile's store of t - 2 has read it
+        if (tid == 0) bulk_wait_group_read<1>();
+        __syncthreads();
+      }
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         uint32_t w[4];
@@ -307,6 +316,17 @@ stem_tc_kernel(const StemParams p) {
         *reinterpret_cast<uint4*>(tile_s + px * 128 + ((q ^ (px & 7)) << 4)) =
             make_uint4(w[0], w[1], w[2], w[3]);
       }
+      if (p.tma_out) {
+        // The tile (128-byte swizzled pixel rows) is the TMA box
+        // {64 ch, OW, R rows}; rows past OH are not written.
+        fence_proxy_async_smem();
+        __syncthreads();
+        if (tid == 0) {
+          tma_store_5d(&p.tmap_out, tile_s, 0, 0, oh0, b, t);
+          bulk_commit_group();
+        }
+        continue;
+      }
       __syncthreads();
       uint4* dst = reinterpret_cast<uint4*>(
           p.out + ((static_cast<size_t>(t) * P + static_cast<size_t>(b) * p.OH * OW +
@@ -317,6 +337,7 @@ stem_tc_kernel(const StemParams p) {
       }
     }
   }
+  if (p.tma_out && tid == 0) bulk_wait_group<0>();   // stores complete before the block exits
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
