@@ -1001,6 +1001,17 @@ int snn_spikformer_attn_forward(int32_t T, int32_t B, int32_t N, int32_t heads,
     if ((st = encode(&p.tmap_q, 3, q, dims, strides, box_q, swz))) return st;
     if ((st = encode(&p.tmap_k, 3, k, dims, strides, box_kv, swz))) return st;
     if ((st = encode(&p.tmap_v, 3, v, dims, strides, box_kv, swz))) return st;
+    if (head_dim == 32) {
+      // Spikes leave by TMA stores of {32 channels, 32 tokens} tiles: out as
+      // 4-D {C, N, B, T} (tokens past N are not written).
+      if (reinterpret_cast<uintptr_t>(out) & 15) return fail(SNN_E_INVALID, "out must be 16-byte aligned");
+      cuuint64_t odims[4] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(N),
+                             static_cast<cuuint64_t>(B), static_cast<cuuint64_t>(T)};
+      cuuint64_t ostrides[3] = {static_cast<cuuint64_t>(C) * 2, static_cast<cuuint64_t>(N * C) * 2,
+                                static_cast<cuuint64_t>(B) * N * C * 2};
+      cuuint32_t obox[4] = {32, 32, 1, 1};
+      if ((st = encode(&p.tmap_out, 4, out, odims, ostrides, obox, CU_TENSOR_MAP_SWIZZLE_64B))) return st;
+    }
   }
   p.out = static_cast<__half*>(out);
   p.state = state;

@@ -47,6 +47,7 @@ struct AttnParams {
   CUtensorMap tmap_q;        // 3-D {C, N, T*B} fp16, box {HD, min(N,128), 1}
   CUtensorMap tmap_k;        // 3-D {C, N, T*B} fp16, box {HD, kv_rows, 1}
   CUtensorMap tmap_v;
+  CUtensorMap tmap_out;      // head_dim 32: spikes as 4-D {C, N, B, T}, box {32, 32, 1, 1}
   __half* out;               // [T*B][N][C] spikes
   float* state;              // [B][N][C] membrane or null
   unsigned* err;
@@ -69,7 +70,11 @@ struct AttnCfg {
   static constexpr int kSlotBytes = 2 * kQTile + 2 * kKVTile + kDTile;
   static constexpr int kSlots = HD == 32 ? 4 : 2;
   static constexpr int kBarBytes = 256;
-  static constexpr int kSmemBytes = kSlots * kSlotBytes + kBarBytes + 1024;
+  // head_dim 32: one 2 KB spike staging tile per epilogue warp ([32 tokens]
+  // [64 B], 64-byte swizzle) written out by TMA store.
+  static constexpr int kStageOff = (kSlots * kSlotBytes + kBarBytes + 1023) / 1024 * 1024;
+  static constexpr int kStageBytes = HD == 32 ? 8 * 32 * kRowB : 0;
+  static constexpr int kSmemBytes = kStageOff + kStageBytes + 1024;
   static constexpr int kCvtWarps = HD / 16;
   // TMEM: D1 buffers at columns 0 and HD (M = 64: HD columns each); D2
   // buffers at 2*HD and 4*HD (two M-tiles of HD columns each).
@@ -280,6 +285,8 @@ spikformer_attn_lif_kernel(const __grid_constant__ AttnParams p) {
     // GEMM-2 lane quarter warp%4 of M-tile warp/4.
     const int mt = warp >> 2;
     const int tok = mt * 128 + (warp & 3) * 32 + lane;
+    uint8_t* stage = smem + Cfg::kStageOff + warp * 32 * Cfg::kRowB;   // head_dim 32 only
+    int n_st = 0;
     const bool tok_ok = tok < N;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     int i = 0;
@@ -293,6 +300,12 @@ spikformer_attn_lif_kernel(const __grid_constant__ AttnParams p) {
         vm[d] = ((p.flags & kReadState) && tok_ok) ? p.state[state_row + d] : 0.f;
       for (int t = 0; t < p.T; ++t, ++i) {
         const int j = i & 1;
+        // head_dim 32: the warp's staging tile must be read out by its
+        // previous TMA store before it is rewritten.
+        if (HD == 32 && n_st > 0) {
+          if (lane == 0) bulk_wait_group_read<0>();
+          __syncwarp();
+        }
         const bool ok = __all_sync(0xffffffffu, !*abort_flag &&
                                    mbar_wait_bounded(&d2_full[j], (i >> 1) & 1, p.timeout));
         if (!ok) {
@@ -327,7 +340,20 @@ spikformer_attn_lif_kernel(const __grid_constant__ AttnParams p) {
               }
               packed[d / 2] = (sp[0] ? 0x3C00u : 0u) | (sp[1] ? 0x3C000000u : 0u);
             }
-            if (tok_ok) {
+            if constexpr (HD == 32) {
+              // Row `lane` of the staging tile; tokens past N are not stored.
+#pragma unroll
+              for (int c = 0; c < 4; ++c)
+                *reinterpret_cast<uint4*>(stage + attn_swz<32>(lane, c)) =
+                    make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                tma_store_4d(&p.tmap_out, stage, h * HD + c0, mt * 128 + (warp & 3) * 32, b, t);
+                bulk_commit_group();
+              }
+              ++n_st;
+            } else if (tok_ok) {
               uint4* o = reinterpret_cast<uint4*>(
                   p.out + (static_cast<size_t>(t * p.B + b) * N + tok) * C + h * HD + c0);
 #pragma unroll
@@ -342,6 +368,7 @@ spikformer_attn_lif_kernel(const __grid_constant__ AttnParams p) {
         for (int d = 0; d < HD; ++d) p.state[state_row + d] = vm[d];
       }
     }
+    if (HD == 32 && n_st > 0 && lane == 0) bulk_wait_group<0>();   // stores complete before exit
   }
 
   tc_fence_before();
