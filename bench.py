@@ -475,6 +475,12 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and "NCCL_DEBUG_FILE" not in os.environ:
+        # NCCL's debug output (its version banner included) goes to a file,
+        # not stdout, so that rank 0's stdout is the one JSON line.  Set
+        # before torch loads NCCL.
+        import tempfile
+        os.environ["NCCL_DEBUG_FILE"] = os.path.join(tempfile.gettempdir(), "nccl_debug.%h.%p.log")
     if args.impl == "reference":
         run_reference(args, rank)
         return
@@ -482,10 +488,6 @@ def main():
     import torch.distributed as dist
     from sparsesnn_b200 import dist as sd
     if world > 1:
-        # NCCL's version banner goes to stdout at NCCL_DEBUG=VERSION; keep
-        # rank 0's stdout to the one JSON line.
-        if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
-            os.environ["NCCL_DEBUG"] = "WARN"
         torch.cuda.set_device(local_rank)
         sd.init_from_env("nccl", timeout_s=120.0, device_id=torch.device("cuda", local_rank))
     try:
