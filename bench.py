@@ -272,7 +272,7 @@ def run_reference(args, rank):
                              "sample": f"{CPU_SAMPLE} images per step, torch CPU fp32 port of "
                                        f"the reference forward (oracle/sew_resnet.py)"},
             "e2e": {"value": ips, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def run_ours(args, rank, world, local_rank):
@@ -467,7 +467,19 @@ def run_ours(args, rank, world, local_rank):
                 "glue": glue,
                 "clocks": dict(clk.summary(), window="timed region plus 300 replays before and 200 after"),
                 "cpu_baseline": cpu}
-        print(json.dumps(line), flush=True)
+        emit(line)
+
+
+_JSON_FD = None     # original stdout when it is redirected (N > 1)
+
+
+def emit(line):
+    """Print the one JSON result line on the original stdout."""
+    text = json.dumps(line) + "\n"
+    if _JSON_FD is None:
+        print(text, end="", flush=True)
+    else:
+        os.write(_JSON_FD, text.encode())
 
 
 def main():
@@ -475,12 +487,14 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    if world > 1 and "NCCL_DEBUG_FILE" not in os.environ:
-        # NCCL's debug output (its version banner included) goes to a file,
-        # not stdout, so that rank 0's stdout is the one JSON line.  Set
-        # before torch loads NCCL.
-        import tempfile
-        os.environ["NCCL_DEBUG_FILE"] = os.path.join(tempfile.gettempdir(), "nccl_debug.%h.%p.log")
+    if world > 1:
+        # Libraries write to file descriptor 1 directly (NCCL prints its
+        # version banner there); send all of that to stderr and keep the
+        # original stdout for the one JSON line.
+        global _JSON_FD
+        sys.stdout.flush()
+        _JSON_FD = os.dup(1)
+        os.dup2(2, 1)
     if args.impl == "reference":
         run_reference(args, rank)
         return
