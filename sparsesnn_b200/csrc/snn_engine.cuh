@@ -109,9 +109,17 @@ int parse_engine_file(const char* path, SnnEngineHeader* h, std::vector<SnnEngin
     const uint64_t in_bytes = (*tensors)[nd.in0].bytes, out_bytes = (*tensors)[nd.out].bytes;
     switch (nd.op) {
       case kOpStem: {
+        // Output extent exactly as snn_stem_forward computes it (any pad >= 0
+        // and stride >= 1), from dimensions checked positive first.
+        if (d.T < 1 || d.B < 1 || d.H < 1 || d.W < 1 || d.Cin < 1 || d.Cout < 1 || d.KH < 1 ||
+            d.KW < 1 || d.stride < 1 || d.pad < 0)
+          return fail(SNN_E_INVALID, "engine node %u (stem): non-positive dimension", n);
+        const int64_t oh = (int64_t(d.H) + 2 * d.pad - d.KH) / d.stride + 1;
+        const int64_t ow = (int64_t(d.W) + 2 * d.pad - d.KW) / d.stride + 1;
+        if (oh < 1 || ow < 1) return fail(SNN_E_INVALID, "engine node %u (stem): empty output", n);
         const uint64_t px = uint64_t(d.B) * d.H * d.W;
         if (nd.i[0] < 1 || in_bytes < uint64_t(nd.i[0]) * d.Cin * px * 4 ||
-            out_bytes < uint64_t(d.T) * px * d.Cout * 2 ||
+            out_bytes < uint64_t(d.T) * d.B * uint64_t(oh) * uint64_t(ow) * d.Cout * 2 ||
             !off_ok(nd.p0, uint64_t(d.Cout) * d.Cin * d.KH * d.KW * 4) ||
             !off_ok(nd.p1, uint64_t(d.Cout) * 4) || !off_ok(nd.p2, uint64_t(d.Cout) * 4))
           return fail(SNN_E_INVALID, "engine node %u (stem): sizes or offsets out of range", n);

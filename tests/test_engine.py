@@ -83,6 +83,40 @@ def test_damaged_engine_file_rejected(lib, tmp_path, what):
     assert ei.value.code == rt.SNN_E_INVALID
 
 
+def _stem_file(path, *, H, kh, pad, stride, out_hw, T=2, B=1, cout=16):
+    """A stem node whose output tensor holds out_hw x out_hw pixels, and a head."""
+    w = ef._Writer()
+    d = rt.make_desc(T=T, B=B, Cin=3, H=H, W=H, Cout=cout, KH=kh, KW=kh, stride=stride, pad=pad)
+    images = w.tensor(B * 3 * H * H * 4, ef.F32)
+    a0 = w.tensor(T * B * out_hw * out_hw * cout * 2, ef.F16)
+    logits = w.tensor(B * 4 * 4, ef.F32)
+    w.node(ef.OP_STEM, images, ef.NO_TENSOR, a0, d,
+           (w.param(np.zeros((cout, 3, kh, kh), np.float32)), w.param(np.ones(cout, np.float32)),
+            w.param(np.zeros(cout, np.float32)), 0), (1, 0, 0, 0, 0))
+    w.node(ef.OP_HEAD, a0, ef.NO_TENSOR, logits, None,
+           (w.param(np.zeros((4, cout), np.float32)), w.param(np.zeros(4, np.float32)), 0, 0),
+           (T, B, out_hw * out_hw, cout, 4))
+    w.write(path, images, logits, T, B)
+    return path
+
+
+def test_stem_output_size_checked_from_its_geometry(lib, tmp_path):
+    """The stem check sizes the output from OH x OW: a 1x1 stem with pad 2
+    writes (H+4)^2 pixels, so an H x H output tensor is rejected; a 7x7
+    stride-2 stem needs only its (H/2)^2 pixels."""
+    bad = _stem_file(tmp_path / "pad2.snne", H=8, kh=1, pad=2, stride=1, out_hw=8)
+    with pytest.raises(rt.SnnError) as ei:
+        ef.check_file(bad)
+    assert ei.value.code == rt.SNN_E_INVALID
+    ok = _stem_file(tmp_path / "pad2ok.snne", H=8, kh=1, pad=2, stride=1, out_hw=12)
+    assert ef.check_file(ok) == (2, 3)
+    s2 = _stem_file(tmp_path / "s2.snne", H=16, kh=7, pad=3, stride=2, out_hw=8)
+    assert ef.check_file(s2) == (2, 3)
+    neg = _stem_file(tmp_path / "neg.snne", H=16, kh=7, pad=-1, stride=2, out_hw=8)
+    with pytest.raises(rt.SnnError):
+        ef.check_file(neg)
+
+
 def test_missing_engine_file(lib, tmp_path):
     with pytest.raises(rt.SnnError):
         ef.check_file(tmp_path / "absent.snne")

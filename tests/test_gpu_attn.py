@@ -12,6 +12,8 @@ from oracle.attention import spikformer_attn_lif
 
 pytestmark = pytest.mark.gpu
 
+GUARD = 8192
+
 
 def run_attn(q, k, v, *, T, heads, scale=0.125, tau=2.0, v_th=0.5, state=None, flags=0):
     import torch
@@ -20,13 +22,18 @@ def run_attn(q, k, v, *, T, heads, scale=0.125, tau=2.0, v_th=0.5, state=None, f
     dev = "cuda"
     qd, kd, vd = (torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(dev, torch.float16)
                   for a in (q, k, v))
-    out = torch.full((tb, n, c), 7.0, dtype=torch.float16, device=dev)
+    # Output followed by a guard tail of sentinels: the spike tiles' TMA
+    # stores clip tokens past N at the tensor map's extent.
+    n_out = tb * n * c
+    buf = torch.full((n_out + GUARD,), 7.0, dtype=torch.float16, device=dev)
+    out = buf[:n_out].view(tb, n, c)
     s = torch.cuda.current_stream().cuda_stream
     sp = state.data_ptr() if state is not None else None
     rt.check(rt.load().snn_spikformer_attn_forward(T, tb // T, n, heads, c // heads, scale, tau,
                                                    v_th, 0.0, flags, qd.data_ptr(), kd.data_ptr(),
                                                    vd.data_ptr(), sp, out.data_ptr(), s))
     torch.cuda.synchronize()
+    assert bool((buf[n_out:] == 7.0).all()), "attention wrote past its output"
     return out.float().cpu().numpy()
 
 

@@ -84,7 +84,12 @@ def unflatten(g, y, state=None):
 
 
 def check_spikes_and_v(spk, v, ref_spk, ref_h, ref_v):
-    frac, explained, nmis, diverged = L.spike_agreement(spk, ref_spk, ref_h)
+    st = {}
+    frac, explained, nmis, diverged = L.spike_agreement(spk, ref_spk, ref_h, stats=st)
+    # The first-mismatch rule excuses a diverged neuron's later steps: report them.
+    print(f"spikes: agreement {frac:.6f}, {st['first']} first mismatches (in band), "
+          f"{st['later']} later excused ({st['later_off_band']} off band), "
+          f"{st['diverged']}/{st['neurons']} neurons diverged")
     assert frac >= SPIKE_MIN_AGREE, f"spike agreement {frac:.5f}"
     assert explained, "a spike mismatch lies away from the threshold band"
     keep = ~diverged

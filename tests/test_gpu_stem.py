@@ -11,6 +11,8 @@ from oracle import lif_layer as L
 
 pytestmark = pytest.mark.gpu
 
+GUARD, SENTINEL = 4096, -3.0
+
 
 def run_stem(x, w, scale, bias, T, neuron, tau, Tin):
     import torch
@@ -24,12 +26,17 @@ def run_stem(x, w, scale, bias, T, neuron, tau, Tin):
     wd = torch.from_numpy(w).cuda()
     sd = torch.from_numpy(scale).cuda()
     bd = torch.from_numpy(bias).cuda()
-    out = torch.empty((T * B, H, W, Cout), dtype=torch.float16, device="cuda")
+    # The output is followed by a guard tail of sentinels: TMA stores clip at
+    # the tensor map's extent, so nothing past the tensor may change.
+    n_out = T * B * H * W * Cout
+    buf = torch.full((n_out + GUARD,), SENTINEL, dtype=torch.float16, device="cuda")
+    out = buf[:n_out]
     rc = lib.snn_stem_forward(ctypes.byref(d), Tin, xd.data_ptr(), wd.data_ptr(), sd.data_ptr(),
                               bd.data_ptr(), out.data_ptr(), None)
     assert rc == 0, lib.snn_last_error_message()
     torch.cuda.synchronize()
     assert rt.device_error() == 0
+    assert bool((buf[n_out:] == SENTINEL).all()), "stem wrote past its output"
     return np.transpose(out.float().cpu().numpy().reshape(T, B, H, W, Cout), (0, 1, 4, 2, 3))
 
 

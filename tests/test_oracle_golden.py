@@ -112,3 +112,15 @@ def test_spike_agreement_rule_flags_far_mismatch():
     assert ok and n == 2 and div.tolist() == [False, True]
     far = ref.copy(); far[0, 0] = 1.0
     assert not L.spike_agreement(far, ref, h)[1]
+
+
+def test_spike_agreement_reports_excused_mismatches():
+    # The later mismatch of a diverged neuron is not judged, but it is
+    # counted, and counted as off-band when its reference membrane is far
+    # from the threshold.
+    h = np.array([[0.2, 0.995], [0.3, 0.4]], np.float32)
+    ref = (h >= 1.0).astype(np.float32)
+    got = ref.copy(); got[0, 1] = 1.0; got[1, 1] = 1.0
+    st = {}
+    L.spike_agreement(got, ref, h, stats=st)
+    assert st == {"first": 1, "later": 1, "later_off_band": 1, "neurons": 2, "diverged": 1}

@@ -1,6 +1,7 @@
 """The sengine-facing backend: fused anchors -> callables, and the per-node
 export shims with the reference ``init``/``call`` ABI."""
 import ctypes
+import os
 import subprocess
 import sys
 import types
@@ -14,7 +15,11 @@ import pytest
 from sparsesnn_b200 import build, runtime as rt
 from sparsesnn_b200.sengine_backend import B200Compiler, export_all_kernels
 
-REF = Path("/root/reference")
+# Checkout of the reference project (SparseSNN): $SPARSESNN_REFERENCE, else a
+# directory named "reference" beside this repository.  The tests that run its
+# own fusion pass skip when neither exists.
+REF = Path(os.environ.get("SPARSESNN_REFERENCE",
+                          str(Path(__file__).resolve().parents[2] / "reference")))
 
 
 @pytest.fixture(scope="module", autouse=True)
