@@ -3,19 +3,25 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 One process per GPU (torchrun for N > 1), one model replica per GPU, batch 128
-per GPU (weak scaling), NCCL all-gather of the logits each step (the only
-collective, as in the data-parallel design).  Prints ONE JSON line on rank 0.
+per GPU (weak scaling), NCCL all-gather of the logits after every forward (the
+only collective, as in the data-parallel design), pipelined on a side stream
+under the next forward.  Prints ONE JSON line on rank 0.
 
-* value: images/s of the whole job, inputs resident in HBM, each step = one
-  CUDA-graph replay of the forward (+ logits gather when N > 1), timed with
-  CUDA events between barriers, max over ranks.
+* A step is ``--batches-per-step`` (default 100) forwards of one batch of 128
+  images each, so that K steps span about a second of device time.
+* value: images/s of the whole job, inputs resident in HBM, each forward one
+  CUDA-graph replay, timed with CUDA events between barriers, max over ranks.
 * e2e: the same through the C-ABI native executor (``snn_engine_run`` on an
-  engine file saved from the replica) with the input copied from pinned host
-  memory and the logits read back to host every step; ``python_driver`` is
+  engine file saved from the replica) with the images copied from pinned host
+  memory and the logits read back to host every forward; ``python_driver`` is
   the same measurement through the Python call ``model(x_host)``.
-* roofline: the fused sparse conv kernel (19 launches per forward), timed
-  with CUDA events around each launch over K eager forwards run right after
-  the timed region; FLOPs are dense-equivalent 2*M*N*K.
+* roofline: the fused sparse conv kernels (19 launches per forward): their
+  share of the forward measured INSIDE a CUDA graph (timing-event nodes
+  between launches), applied to the timed forward; FLOPs are
+  dense-equivalent 2*M*N*K.  ``layers`` gives every launch's time and its
+  fraction of the tensor ceiling and of HBM.
+* strong_scaling: the same forward at a fixed global batch (``--global-batch``,
+  default 128) split over the ranks.
 * cpu_baseline (rank 0, N = 1): the CPU port of the reference PyTorch path
   (``oracle/sew_resnet.py``) on a bounded sample of images, all host threads.
 * --impl reference: only that CPU path, as the reference arm.
@@ -38,7 +44,7 @@ UNIT = "images/s"
 BATCH = 128
 T_STEPS = 4
 HW = 32
-CPU_SAMPLE = 8           # images per CPU-baseline step
+CPU_SAMPLE = 64          # images per CPU-baseline forward
 
 
 def parse():
@@ -48,8 +54,10 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--batch", type=int, default=BATCH)
+    ap.add_argument("--batches-per-step", type=int, default=100)
+    ap.add_argument("--global-batch", type=int, default=BATCH)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-steps", type=int, default=3)
+    ap.add_argument("--cpu-steps", type=int, default=5)
     return ap.parse_args()
 
 
@@ -57,6 +65,7 @@ def config(args, world):
     return {"workload": f"SEW-ResNet-18 CIFAR stem (3x3 s1, no maxpool), stages 64/128/256/512, "
                         f"ADD, 100 classes, T={T_STEPS}, 3x{HW}x{HW}, batch {args.batch} per GPU",
             "model": "sew_resnet18_cifar", "global_batch": args.batch * world,
+            "forwards_per_step": args.batches_per_step,
             "seq_len": T_STEPS, "parallelism": f"dp{world}",
             "weights": "random init (Kaiming, BN stats as config 0), 2:4 pruned except stem",
             "l2": "working set per step > 126 MB L2 (activations ~600 MB), no flush"}
@@ -211,15 +220,18 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index):
-        self.gpu = gpu_index
+    def __init__(self, device):
+        # nvidia-smi indices are physical and ignore CUDA_VISIBLE_DEVICES:
+        # select the GPU by its UUID.
+        import torch
+        self.gpu = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
         self.proc = None
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                ["nvidia-smi", "-i", self.gpu, f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -275,143 +287,219 @@ def run_reference(args, rank):
     emit(line)
 
 
+def segment_times(model, stream, replays=50):
+    """Per-launch device time of one forward INSIDE a CUDA graph: the forward
+    is captured with a timing event (an event-record node) between every two
+    launches and replayed; returns ({launch name: mean ms}, total ms).  The
+    event nodes cut the programmatic-dependent-launch overlap between
+    neighbours, so the segments sum to a little more than the plain graph's
+    step; shares are what this measures."""
+    import torch
+    ops = model._ops()
+    evs = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(len(ops) + 1)]
+    g = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(model.device)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        model._in_sel = 0
+        with torch.cuda.graph(g):
+            evs[0].record()
+            for (_, op), e in zip(ops, evs[1:]):
+                op()
+                e.record()
+    stream.wait_stream(side)
+    acc = [0.0] * len(ops)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    for _ in range(replays):
+        g.replay()
+        torch.cuda.synchronize()
+        for i in range(len(ops)):
+            acc[i] += evs[i].elapsed_time(evs[i + 1])
+    del g
+    per = {name: a / replays for (name, _), a in zip(ops, acc)}
+    return per, sum(per.values())
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
+    from sparsesnn_b200 import dist as sd
     from sparsesnn_b200.sew_resnet import SEWResNet18, conv_layer_bytes, conv_layer_flops, init_params
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
+    R = args.batches_per_step
     P = init_params(seed=0)
     model = SEWResNet18(P, T=T_STEPS, batch=args.batch, H=HW, W=HW, device=dev)
     g = torch.Generator().manual_seed(1234 + rank)
     x_host = torch.randn((args.batch, 3, HW, HW), generator=g).pin_memory()
     x_dev = x_host.to(dev)
     logits_host = torch.empty((args.batch, model.num_classes), dtype=torch.float32).pin_memory()
-    gathered = torch.empty((world * args.batch, model.num_classes), dtype=torch.float32,
-                           device=dev) if world > 1 else None
-
-    from sparsesnn_b200 import dist as sd
+    gath = sd.OverlappedGather(tuple(model.logits.shape), world, dev) if world > 1 else None
 
     def barrier():
         if world > 1:
             dist.barrier(device_ids=[local_rank])
 
-    def gather():
-        if world > 1:
-            sd.gather_logits(model.logits, gathered)
-
-    # Warm-up (eager), then capture the forward into a CUDA graph.
-    model.x_in.copy_(x_dev)
+    # Warm-up (eager), then capture the forward into CUDA graphs (one per
+    # input buffer; both buffers hold this rank's resident batch).
+    for k in range(2):
+        model.x_ins[k].copy_(x_dev)
     for _ in range(max(3, args.warmup)):
         model.run()
-        gather()
     torch.cuda.synchronize()
     model.capture(warmup=1)
+    stream = torch.cuda.current_stream(dev)
+
+    def forwards(n):
+        """n forwards on the resident batch, alternating the two graphs; at
+        N > 1 each forward's logits are gathered on a side stream under the
+        next forward."""
+        for i in range(n):
+            k = i & 1
+            if gath is not None:
+                gath.reuse(k)
+            out = model.replay(k)
+            if gath is not None:
+                gath.submit(out, k)
+        if gath is not None:
+            gath.drain()
+
     for _ in range(max(3, args.warmup)):
-        model.replay()
-        gather()
+        forwards(R)
     torch.cuda.synchronize()
     n_launch = len(model.launches())
 
     # ---------------- timed region A: device-resident inputs, graph replay
-    # The clock sampler runs across the timed region plus 300 / 200 identical
-    # replays before / after it, so that even a short timed region has
-    # samples taken under the same load.
-    stream = torch.cuda.current_stream(dev)
+    # A step is R forwards of one batch each.  The clock sampler runs across
+    # the timed region plus a second of identical replays before it.
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-
-    def roll(iters):
-        # Fixed iteration counts: every rank issues the same collectives.
-        for i in range(iters):
-            model.replay()
-            gather()
-            if i % 20 == 19:
-                torch.cuda.synchronize()
+    with ClockSampler(dev) as clk:
+        forwards(2 * R)
         torch.cuda.synchronize()
-
-    with ClockSampler(local_rank) as clk:
-        roll(300)
         barrier(); torch.cuda.synchronize()
         e0.record(stream)
         for _ in range(args.steps):
-            model.replay()
-            gather()
+            forwards(R)
         e1.record(stream)
         torch.cuda.synchronize()
         barrier()
-        roll(200)
     ms = sd.max_over_ranks(e0.elapsed_time(e1) / args.steps, device=dev)
-    value = args.batch * world / (ms / 1000.0)
+    value = args.batch * R * world / (ms / 1000.0)
 
-    # ---------------- timed region B: end to end through the public call
+    # ---------------- timed region B: end to end through the Python call
+    def e2e_forwards(n):
+        for i in range(n):
+            if gath is not None:
+                gath.reuse(i & 1)
+            out = model(x_host)                          # H2D from pinned memory + replay
+            if gath is not None:
+                gath.submit(out, i & 1)
+            logits_host.copy_(out, non_blocking=True)    # D2H of the forward's result
+        if gath is not None:
+            gath.drain()
+
+    e2e_forwards(4)
     barrier(); torch.cuda.synchronize()
     e0.record(stream)
     for _ in range(args.steps):
-        out = model(x_host)                         # H2D from pinned memory + graph replay
-        gather()
-        logits_host.copy_(out, non_blocking=True)   # D2H of the step's result
+        e2e_forwards(R)
     e1.record(stream)
     torch.cuda.synchronize()
     barrier()
     ms_e2e = sd.max_over_ranks(e0.elapsed_time(e1) / args.steps, device=dev)
-    e2e_driver = args.batch * world / (ms_e2e / 1000.0)
+    e2e_driver = args.batch * R * world / (ms_e2e / 1000.0)
 
     # ---------------- timed region C: the native executor through the C-ABI
-    # (snn_engine_run: pinned host images in, host logits out, the C++ node
-    # loop replayed from its CUDA graph), on an engine file saved from the
-    # same replica.
+    # (snn_engine_run: pinned host images in, logits out, the C++ node loop
+    # replayed from its CUDA graph), on an engine file saved from the same
+    # replica.
     import tempfile
     from sparsesnn_b200 import engine_file as ef
     eng_dir = tempfile.mkdtemp()
     eng_path = os.path.join(eng_dir, f"sew18_rank{rank}.snne")
     ef.save_engine(model, eng_path)
     eng = ef.Engine(eng_path)
-    eng_logits = torch.empty_like(model.logits)
+    eng_logits = [torch.empty_like(model.logits) for _ in range(2)]
     es = torch.cuda.Stream(dev)
+
+    def eng_forwards(n):
+        for i in range(n):
+            k = i & 1
+            if gath is not None:
+                gath.reuse(k)
+            eng.run(x_host.data_ptr(), eng_logits[k].data_ptr(), es)   # H2D + graph replay
+            if gath is not None:
+                gath.submit(eng_logits[k], k)
+            logits_host.copy_(eng_logits[k], non_blocking=True)        # D2H of the result
+        if gath is not None:
+            gath.drain()
+
     with torch.cuda.stream(es):
         eng.capture(es)
-        for _ in range(max(3, args.warmup)):
-            eng.run(x_host.data_ptr(), eng_logits.data_ptr(), es)
-            if world > 1:
-                sd.gather_logits(eng_logits, gathered)
+        eng_forwards(max(3, args.warmup))
         es.synchronize()
         barrier()
         c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         c0.record(es)
         for _ in range(args.steps):
-            eng.run(x_host.data_ptr(), eng_logits.data_ptr(), es)   # H2D + graph replay
-            if world > 1:
-                sd.gather_logits(eng_logits, gathered)
-            logits_host.copy_(eng_logits, non_blocking=True)         # D2H of the step's result
+            eng_forwards(R)
         c1.record(es)
         es.synchronize()
     barrier()
     ms_eng = sd.max_over_ranks(c0.elapsed_time(c1) / args.steps, device=dev)
-    e2e = args.batch * world / (ms_eng / 1000.0)
+    e2e = args.batch * R * world / (ms_eng / 1000.0)
     eng.close()
     os.remove(eng_path)
     os.rmdir(eng_dir)
 
-    # ---------------- per-launch CUDA-event timing of the fused conv kernel
-    ops = model.launches()
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in ops]
-    conv_ms = 0.0
-    per_layer = {name: 0.0 for name, _ in ops}
-    for _ in range(args.steps):
-        for (name, op), (a, b) in zip(ops, evs):
-            a.record(stream); op(); b.record(stream)
+    # ---------------- strong scaling: a fixed global batch split over ranks
+    strong = None
+    if args.global_batch % world == 0:
+        per = args.global_batch // world
+        sm_model = model if per == args.batch else SEWResNet18(P, T=T_STEPS, batch=per, H=HW, W=HW,
+                                                               device=dev)
+        for k in range(2):
+            sm_model.x_ins[k].copy_(x_dev[:per])
+        if sm_model is not model:
+            sm_model.capture(warmup=2)
+        sg = sd.OverlappedGather(tuple(sm_model.logits.shape), world, dev) if world > 1 else None
+
+        def sm_forwards(n):
+            for i in range(n):
+                if sg is not None:
+                    sg.reuse(i & 1)
+                out = sm_model.replay(i & 1)
+                if sg is not None:
+                    sg.submit(out, i & 1)
+            if sg is not None:
+                sg.drain()
+
+        sm_forwards(R)
+        barrier(); torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.steps):
+            sm_forwards(R)
+        e1.record(stream)
         torch.cuda.synchronize()
-        for (name, _), (a, b) in zip(ops, evs):
-            dt = a.elapsed_time(b)
-            per_layer[name] += dt / args.steps
-    conv_names = [n for n, _ in ops if n not in ("stem", "head")]
-    conv_ms = sum(per_layer[n] for n in conv_names)
-    flops = sum(conv_layer_flops(l) for l in model.conv_layers())
-    alg_bytes = sum(conv_layer_bytes(blk["l1"], False) + conv_layer_bytes(blk["l2"], True) +
-                    (conv_layer_bytes(blk["ds"], False) if blk["ds"] is not None else 0)
-                    for blk in model.blocks)
+        barrier()
+        ms_s = sd.max_over_ranks(e0.elapsed_time(e1) / args.steps, device=dev)
+        strong = {"global_batch": args.global_batch, "per_gpu_batch": per,
+                  "ms_per_step": ms_s, "forwards_per_step": R,
+                  "value": args.global_batch * R / (ms_s / 1000.0), "unit": UNIT}
+        if sm_model is not model:
+            del sm_model
+
+    # ---------------- roofline: per-launch time inside the graph
+    per_launch, seg_total = segment_times(model, stream)
+    conv_names = [n for n, _ in model.launches() if n not in ("stem", "head")]
+    conv_share = sum(per_launch[n] for n in conv_names) / seg_total
+    ms_fwd = ms / R                                  # one forward of the timed region
+    conv_ms = ms_fwd * conv_share                    # the conv launches' part of it
+    layers = list(model.conv_layers())
+    flops = sum(conv_layer_flops(l) for l in layers)
     hbm_peak, bf16_peak, peak_kind = peaks()
     sparse_peak = 2.0 * bf16_peak
     achieved = flops / (conv_ms / 1000.0) / 1e12
@@ -421,6 +509,33 @@ def run_ours(args, rank, world, local_rank):
         for line in tf.read_text().splitlines():
             if line.startswith("fused_conv_dram_bytes_per_forward:"):
                 traffic = int(float(line.split(":")[1]))
+    # Per conv launch: time = its graph segment scaled so the segments sum to
+    # the timed forward; fractions of the 2:4 tensor ceiling and of HBM, the
+    # latter for the bytes the fp16 format moves and for the byte convention
+    # of 1-byte activations / 1-bit spikes.
+    scale_t = ms_fwd / seg_total
+    per_layer = {}
+    res_of = {}
+    for i, blk in enumerate(model.blocks):
+        res_of[f"b{i}.conv1"] = (blk["l1"], False)
+        if blk["ds"] is not None:
+            res_of[f"b{i}.ds"] = (blk["ds"], False)
+        res_of[f"b{i}.conv2"] = (blk["l2"], True)
+    for name, t_ms in per_launch.items():
+        ent = {"us": round(t_ms * scale_t * 1000.0, 2)}
+        if name in res_of:
+            layer, has_res = res_of[name]
+            t_s = t_ms * scale_t / 1000.0
+            fl = conv_layer_flops(layer)
+            b16 = conv_layer_bytes(layer, has_res)
+            b8 = conv_layer_bytes(layer, has_res, act_bytes=1, binary_out=not has_res)
+            from sparsesnn_b200 import runtime as rt
+            ent.update(variant={0: "general", 1: "halo", 2: "halo_stream"}[rt.variant(layer.desc)],
+                       tflops=round(fl / t_s / 1e12, 1), frac_tensor=round(fl / t_s / 1e12 / sparse_peak, 4),
+                       frac_hbm_f16=round(b16 / t_s / 1e9 / hbm_peak, 4),
+                       frac_hbm_s8d=round(b8 / t_s / 1e9 / hbm_peak, 4))
+        per_layer[name] = ent
+    alg_bytes = sum(conv_layer_bytes(*res_of[n]) for n in conv_names)
     from sparsesnn_b200 import runtime as rt
     if rt.device_error() != 0:
         raise RuntimeError("fused kernel reported a device error")
@@ -436,19 +551,19 @@ def run_ours(args, rank, world, local_rank):
         threads = os.cpu_count() or 1
         ips, _ = cpu_reference_images_per_s(args.cpu_steps, CPU_SAMPLE, threads)
         cpu = {"value": ips, "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": f"{CPU_SAMPLE} images x {args.cpu_steps} forwards, torch CPU fp32 "
-                         f"port of the reference forward (oracle/sew_resnet.py)"}
+               "sample": f"{CPU_SAMPLE} images x {args.cpu_steps} forwards (after one warm-up), "
+                         f"torch CPU fp32 port of the reference forward (oracle/sew_resnet.py)"}
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                 "dtype": "f16", "data": "synthetic", "config": config(args, world),
                 "e2e": {"value": e2e, "unit": UNIT,
-                        "h2d_bytes_per_step": int(x_host.numel() * 4),
-                        "d2h_bytes_per_step": int(logits_host.numel() * 4),
+                        "h2d_bytes_per_step": int(x_host.numel() * 4) * R,
+                        "d2h_bytes_per_step": int(logits_host.numel() * 4) * R,
                         "path": "snn_engine_run (C-ABI native executor, CUDA graph), pinned host buffers",
                         "python_driver": e2e_driver},
-                "gpu_launches": n_launch * args.steps,
+                "gpu_launches": n_launch * args.steps * R,
                 "roofline": {"bound": "tensor", "achieved": achieved, "peak": sparse_peak,
                              "unit": "TFLOP/s", "frac": achieved / sparse_peak,
                              "traffic": traffic,
@@ -456,16 +571,22 @@ def run_ours(args, rank, world, local_rank):
                                        "(halo4 x4, halo x3, halo_stream x6, general x6)",
                              "peak_note": f"2:4 sparse ceiling = 2 x {peak_kind} dense bf16 "
                                           f"{bf16_peak} TFLOP/s; FLOPs dense-equivalent",
+                             "timing": "conv launches' share of the forward, measured inside the "
+                                       "CUDA graph (event-record nodes between launches), times the "
+                                       "timed forward (ms_per_step / forwards per step)",
                              "flops_per_forward": flops, "kernel_ms_per_forward": conv_ms,
+                             "forward_ms": ms_fwd, "conv_share": conv_share,
+                             "step_frac": flops / (ms_fwd / 1000.0) / 1e12 / sparse_peak,
                              "hbm_view": {"achieved": alg_bytes / (conv_ms / 1000.0) / 1e9,
                                           "peak": hbm_peak, "unit": "GB/s",
                                           "frac": alg_bytes / (conv_ms / 1000.0) / 1e9 / hbm_peak,
                                           "algorithmic_bytes_per_forward": alg_bytes}},
-                "layer_ms": {k: round(v, 4) for k, v in per_layer.items()},
+                "layers": per_layer,
+                "strong_scaling": strong,
                 "spikformer_linear": linear,
                 "spikformer_attention": attn,
                 "glue": glue,
-                "clocks": dict(clk.summary(), window="timed region plus 300 replays before and 200 after"),
+                "clocks": dict(clk.summary(), window="timed region plus two steps of replays before it"),
                 "cpu_baseline": cpu}
         emit(line)
 

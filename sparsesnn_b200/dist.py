@@ -65,3 +65,41 @@ def max_over_ranks(value: float, device=None, group=None) -> float:
     t = torch.tensor([value], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
     return float(t.item())
+
+
+class OverlappedGather:
+    """Logits all-gather pipelined behind the forward.
+
+    ``submit(local, slot)`` gathers ``local`` (the logits a forward just
+    wrote, in buffer ``slot``) on a side stream once the current stream has
+    reached that point, so the collective of step i runs under the forward of
+    step i+1 instead of after it.  ``reuse(slot)`` makes the current stream
+    wait until the gather that read buffer ``slot`` has finished, before a
+    forward overwrites it; ``drain()`` joins the side stream.  Every rank
+    issues the same gathers in the same order (one per step)."""
+
+    def __init__(self, shape, world, device, group=None, dtype=torch.float32):
+        self.stream = torch.cuda.Stream(device)
+        self.out = torch.empty((world * shape[0],) + tuple(shape[1:]), dtype=dtype, device=device)
+        self.group = group
+        self._done = {}
+
+    def submit(self, local: torch.Tensor, slot: int) -> None:
+        cur = torch.cuda.current_stream(local.device)
+        ready = torch.cuda.Event()
+        ready.record(cur)
+        self.stream.wait_event(ready)
+        with torch.cuda.stream(self.stream):
+            gather_logits(local, self.out, self.group)
+            done = torch.cuda.Event()
+            done.record(self.stream)
+        self._done[slot] = done
+
+    def reuse(self, slot: int) -> None:
+        ev = self._done.get(slot)
+        if ev is not None:
+            torch.cuda.current_stream(self.out.device).wait_event(ev)
+
+    def drain(self) -> torch.Tensor:
+        torch.cuda.current_stream(self.out.device).wait_stream(self.stream)
+        return self.out

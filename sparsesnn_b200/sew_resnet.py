@@ -154,7 +154,12 @@ class SEWResNet18:
         self.fc_w = torch.from_numpy(params["fc_w"]).to(dev)
         self.fc_b = torch.from_numpy(params["fc_b"]).to(dev)
         self.num_classes = self.fc_w.shape[0]
-        self.logits = torch.empty((batch, self.num_classes), dtype=torch.float32, device=dev)
+        # One logits buffer per input buffer (each captured graph writes its
+        # own), so a consumer of one forward's logits -- a copy to the host, a
+        # collective -- can overlap the next forward.
+        self.logits_bufs = [torch.empty((batch, self.num_classes), dtype=torch.float32, device=dev)
+                            for _ in range(2)]
+        self.logits = self.logits_bufs[0]
         self._graph = None
 
     # --------------------------------------------------------------- launches
@@ -193,15 +198,17 @@ class SEWResNet18:
             s = torch.cuda.current_stream(self.device).cuda_stream
             rt.check(lib.snn_head_forward(self.T, self.B, self.feat_hw, self.feat_c,
                                           self.num_classes, h.data_ptr(), self.fc_w.data_ptr(),
-                                          self.fc_b.data_ptr(), self.logits.data_ptr(), s))
+                                          self.fc_b.data_ptr(),
+                                          self.logits_bufs[self._in_sel].data_ptr(), s))
         ops.append(("head", head))
         return ops
 
     def run(self):
-        """One forward from ``self.x_in`` into ``self.logits`` (no allocation)."""
+        """One forward from input buffer ``_in_sel`` (``self.x_in`` unless a
+        call selected the other) into its logits buffer (no allocation)."""
         for _, op in self._ops():
             op()
-        return self.logits
+        return self.logits_bufs[self._in_sel]
 
     def _ops(self):
         if not hasattr(self, "_ops_cache"):
@@ -228,14 +235,16 @@ class SEWResNet18:
         self._graph = self._graphs[0]
         return self._graph
 
-    def replay(self):
-        """Replay the forward on the images in ``x_in``."""
-        self._graph.replay()
-        return self.logits
+    def replay(self, buf=0):
+        """Replay the forward on the images in input buffer ``buf`` (0 is
+        ``x_in``); returns that buffer's logits."""
+        self._graphs[buf].replay()
+        return self.logits_bufs[buf]
 
     def __call__(self, x):
         """Public API: images ``[B, C, H, W]`` fp32 (host or device) -> logits
-        (device tensor on the current stream, valid until the next call).
+        (device tensor on the current stream, valid until the call after
+        next: consecutive calls alternate between two logits buffers).
 
         The images go to the device on a copy stream into the input buffer
         the previous forward is not reading, so when calls follow each other
@@ -265,7 +274,7 @@ class SEWResNet18:
         done = torch.cuda.Event()
         done.record(cur)
         self._buf_free[k] = done
-        return self.logits
+        return self.logits_bufs[k]
 
     def spikes(self, name):
         """Device buffer of a layer output by trace name (for tests)."""
@@ -283,11 +292,16 @@ def conv_layer_flops(layer: SparseConvBNLIF) -> int:
     return 2 * m * d.Cout * d.KH * d.KW * d.Cin
 
 
-def conv_layer_bytes(layer: SparseConvBNLIF, residual: bool) -> int:
-    """Algorithmic HBM bytes of one fused layer: fp16 activations in (once),
-    packed weights + metadata, fp16 spikes out, fp16 residual in."""
+def conv_layer_bytes(layer: SparseConvBNLIF, residual: bool, act_bytes: int = 2,
+                     binary_out: bool = False) -> int:
+    """Algorithmic HBM bytes of one fused layer: activations in (once), packed
+    weights + metadata, outputs out, residual in.  Defaults count this
+    library's fp16 tensors; ``act_bytes=1, binary_out=True`` counts the byte
+    convention of 1-byte (FP8) activations and residuals and 1-bit spikes for
+    a layer whose output is binary."""
     d = layer.desc
-    act_in = d.T * d.B * d.H * d.W * d.Cin * 2
+    n_in = d.T * d.B * d.H * d.W * d.Cin
+    n_out = d.T * d.B * layer.OH * layer.OW * d.Cout
     w = rt.weight_bytes(d)
-    out = d.T * d.B * layer.OH * layer.OW * d.Cout * 2
-    return act_in + w + out + (out if residual else 0)
+    out = n_out // 8 if binary_out else n_out * act_bytes
+    return n_in * act_bytes + w + out + (n_out * act_bytes if residual else 0)
