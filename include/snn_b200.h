@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define SNN_ABI_VERSION 2
+#define SNN_ABI_VERSION 3
 
 enum {
   SNN_OK = 0,
@@ -44,7 +44,11 @@ enum {
   SNN_E_DEVICE = -5        /* kernel reported a bounded-wait timeout */
 };
 
-enum { SNN_NEURON_LIF = 0, SNN_NEURON_IF = 1, SNN_NEURON_NONE = 2 };
+/* Neuron after BN.  SNN_NEURON_NONE: fp32 BN output.  SNN_NEURON_NONE_F16:
+ * fp16 BN output, and with a residual (snn_conv_forward_res, ADD_AFTER)
+ * out = bn + residual, rounded once: the real-valued membrane-shortcut sum of
+ * MS-ResNet (models/msresnet.py:119-123). */
+enum { SNN_NEURON_LIF = 0, SNN_NEURON_IF = 1, SNN_NEURON_NONE = 2, SNN_NEURON_NONE_F16 = 3 };
 enum { SNN_FLAG_READ_STATE = 1, SNN_FLAG_WRITE_STATE = 2,
        /* Always use the general kernel (streamed weights, per-tap activation
         * tiles) even where the halo kernel applies; for testing. */
@@ -55,7 +59,15 @@ enum { SNN_FLAG_READ_STATE = 1, SNN_FLAG_WRITE_STATE = 2,
         * activations.  Measured 2-4 us faster per SEW-ResNet-18 stage-3/4
         * layer in isolation but not faster inside the whole-forward CUDA
         * graph, so it is not the default. */
-       SNN_FLAG_CTA_PAIR = 8 };
+       SNN_FLAG_CTA_PAIR = 8,
+       /* Dense (unpruned) weights: the layer runs as the sum of two 2:4
+        * layers over the same activations (weight positions 0,1 and 2,3 of
+        * every group of four input channels), which the packer splits; the
+        * packed blob holds 2*K weight columns.  General kernel only, spiking
+        * neurons with no residual or the SEW add.  For dense convs the
+        * reference keeps unpruned (e.g. a Spikformer's patch-splitting
+        * convs, models/spikformer.py:159-206). */
+       SNN_FLAG_DENSE = 16 };
 
 /* Where the residual of a fused Add enters the epilogue (the reference's
  * pattern strings and templates, sengine/kernels/interleaved_templates.py:371-397):
@@ -152,7 +164,9 @@ int snn_conv_forward_res2(const snn_conv_desc* d, const void* data, const void* 
  * executor runs naive_conv2d_bn_nhwc_kernel, sengine/csrc/cpp_executor.cu:306-347).
  * x: [Tin][B][Cin][H][W] fp32 NCHW with Tin = 1 (input repeated over T,
  * models/sewresnet.py:199-201) or Tin = T.  w: [Cout][Cin][KH][KW] fp32.
- * out: [T][B][OH][OW][Cout] fp16 spikes. */
+ * out: [T][B][OH][OW][Cout] fp16 spikes, or with d->neuron ==
+ * SNN_NEURON_NONE the fp16 BN output (MS-ResNet's stem feeds the real-valued
+ * residual stream, models/msresnet.py:135-138,161). */
 int snn_stem_forward(const snn_conv_desc* d, int32_t Tin, const float* x, const float* w,
                      const float* bn_scale, const float* bn_bias, void* out, void* stream);
 
@@ -179,10 +193,23 @@ int snn_add_lif_forward(const snn_conv_desc* d, const void* a, const void* b, fl
  * reference's maxpool_lif_fused_kernel, sengine/kernels/pool_lif_fused.py:
  * 15-79).  Window d->KH x d->KW, d->stride, d->pad (padding never wins the
  * max, as in torch MaxPool2d); channels d->Cin == d->Cout (multiple of 8).
- *   x      [T*B][H][W][C] fp16;   out [T*B][OH][OW][C] fp16 spikes
+ * d->neuron == SNN_NEURON_NONE gives the plain max pool (state unused): the
+ * pool that follows a neuron, e.g. SEW-ResNet's stem maxpool
+ * (models/sewresnet.py:202-203) or a Spikformer SPS pool
+ * (models/spikformer.py:192-197).
+ *   x      [T*B][H][W][C] fp16;   out [T*B][OH][OW][C] fp16 spikes (or maxima)
  *   state  [B*OH*OW][C] fp32 membrane */
 int snn_maxpool_lif_forward(const snn_conv_desc* d, const void* x, float* state, void* out,
                             void* stream);
+
+/* Neuron over T of one input: out = spikes of neuron(x) (the reference
+ * executor's standalone LIF node, lif_neuron_kernel,
+ * sengine/csrc/cpp_executor.cu:46-64; in MS-ResNet the neuron in front of
+ * every conv, models/msresnet.py:119-121).  Shape, neuron and state flags as
+ * for snn_add_lif_forward.
+ *   x      [T*B][H][W][C] fp16 (real-valued);   out same shape, fp16 spikes */
+int snn_lif_forward(const snn_conv_desc* d, const void* x, float* state, void* out,
+                    void* stream);
 
 /* Spikformer attention core + attention LIF (the FusedSpikformerAttention op,
  * sengine/tdl/attention_ops.py:50-82 and :85-105; model semantics

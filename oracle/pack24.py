@@ -133,6 +133,11 @@ def pack_meta(w_fk: np.ndarray, f_pad: int | None = None) -> np.ndarray:
     idx = group_indices(w_fk)
     nib = np.full((f_pad, k // 4), 0x4, np.uint32)  # padding rows: (0,1)
     nib[:f] = (idx[:, :, 0] | (idx[:, :, 1] << 2)).astype(np.uint32)
+    return _meta_words(nib, f_pad, k)
+
+
+def _meta_words(nib: np.ndarray, f_pad: int, k: int) -> np.ndarray:
+    """Metadata words from one nibble per (row, group of 4) ``[f_pad, k/4]``."""
     n_mt, n_j = f_pad // M_TILE, k // K_STEP
     out = np.zeros((n_mt, n_j, M_TILE), np.uint32)
     lanes = np.arange(M_TILE)
@@ -168,3 +173,32 @@ def unpack(values: np.ndarray, meta: np.ndarray, f: int, k: int) -> np.ndarray:
                         pos = (nibble >> sh) & 3
                         dense[rows, 4 * g + pos] = values[rows, 2 * g + s].astype(np.float32)
     return dense[:f]
+
+
+K_BLOCK = 64      # activation channels per k-block (one 128-byte row of fp16)
+
+
+def pack_dense_split(w_fchw: np.ndarray):
+    """Packed blob parts of a DENSE conv weight ``[F,C,KH,KW]`` run as two
+    2:4 halves over the same activations (this library's dense mode; the
+    reference keeps such convs unpruned).
+
+    Activation k-block ``kb`` (64 input channels of one tap, ``k = (kh*KW +
+    kw)*C + c``) meets weight k-blocks ``2kb`` and ``2kb+1``: in each group of
+    four channels the first keeps positions (0,1) (nibble ``0x4``), the second
+    positions (2,3) (nibble ``0xE``), whatever the values (zeros included).
+    Returns ``(values fp16 [F_pad, K], meta uint32 [F_pad/128, 2K/32, 128])``.
+    """
+    w_fk = conv_weight_to_fk(w_fchw).astype(np.float32)
+    f, k = w_fk.shape
+    if k % K_BLOCK:
+        raise ValueError("C must be a multiple of 64")
+    f_pad = -(-f // M_TILE) * M_TILE
+    g = w_fk.reshape(f, k // K_BLOCK, K_BLOCK // 4, 4)          # [f, kb, gi, pos]
+    halves = np.stack([g[..., 0:2], g[..., 2:4]], axis=2)      # [f, kb, h, gi, 2]
+    vals = np.zeros((f_pad, k), np.float16)
+    vals[:f] = halves.reshape(f, k).astype(np.float16)
+    nib = np.full((f_pad, 2 * k // 4), 0x4, np.uint32)
+    per_block = np.repeat(np.array([0x4, 0xE], np.uint32), K_BLOCK // 4)   # [h*16 + gi]
+    nib[:f] = np.tile(per_block, k // K_BLOCK)[None, :]
+    return vals, _meta_words(nib, f_pad, 2 * k)

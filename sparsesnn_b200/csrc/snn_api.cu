@@ -52,19 +52,42 @@ ConvKernel conv_kernel_fn_rm(int rm) {
     default: return snn::fused_sparse_conv_lif_kernel<MODE, snn::kResNone, TC>;
   }
 }
+// Dense weights (two weight tiles per activation k-block): spiking neurons,
+// no residual or the SEW add.
+template <int MODE, int TC>
+ConvKernel conv_dense_fn_rm(int rm) {
+  return rm == snn::kResAddAfter
+             ? snn::fused_sparse_conv_lif_kernel<MODE, snn::kResAddAfter, TC, false, 2>
+             : snn::fused_sparse_conv_lif_kernel<MODE, snn::kResNone, TC, false, 2>;
+}
 template <int TC>
-ConvKernel conv_kernel_fn_tc(int mode, int rm) {
+ConvKernel conv_kernel_fn_tc(int mode, int rm, bool dense) {
+  if (dense) {
+    switch (mode) {
+      case snn::kModeLifHalf: return conv_dense_fn_rm<snn::kModeLifHalf, TC>(rm);
+      case snn::kModeLifDiv: return conv_dense_fn_rm<snn::kModeLifDiv, TC>(rm);
+      default: return conv_dense_fn_rm<snn::kModeIf, TC>(rm);
+    }
+  }
   switch (mode) {
     case snn::kModeLifHalf: return conv_kernel_fn_rm<snn::kModeLifHalf, TC>(rm);
     case snn::kModeLifDiv: return conv_kernel_fn_rm<snn::kModeLifDiv, TC>(rm);
     case snn::kModeIf: return conv_kernel_fn_rm<snn::kModeIf, TC>(rm);
+    case snn::kModeBnF16:
+      return rm == snn::kResAddAfter
+                 ? snn::fused_sparse_conv_lif_kernel<snn::kModeBnF16, snn::kResAddAfter, TC>
+                 : snn::fused_sparse_conv_lif_kernel<snn::kModeBnF16, snn::kResNone, TC>;
     default: return snn::fused_sparse_conv_lif_kernel<snn::kModeNone, snn::kResNone, TC>;
   }
 }
 
 // tc = timesteps per accumulator (2 or 4, see snn::GenCfg); rm = snn::ResMode.
-ConvKernel conv_kernel_fn(int mode, int rm, int tc) {
-  return tc == 4 ? conv_kernel_fn_tc<4>(mode, rm) : conv_kernel_fn_tc<2>(mode, rm);
+ConvKernel conv_kernel_fn(int mode, int rm, int tc, bool dense = false) {
+  return tc == 4 ? conv_kernel_fn_tc<4>(mode, rm, dense) : conv_kernel_fn_tc<2>(mode, rm, dense);
+}
+int conv_smem_bytes(int tc, bool dense) {
+  if (dense) return tc == 4 ? snn::GenCfg<4, false, 2>::kSmemBytes : snn::GenCfg<2, false, 2>::kSmemBytes;
+  return tc == 4 ? snn::GenCfg<4>::kSmemBytes : snn::GenCfg<2>::kSmemBytes;
 }
 // CTA-pair variant (TC = 4; spiking modes with no residual or the SEW add).
 ConvKernel conv_pair_kernel_fn(int mode, int rm) {
@@ -249,6 +272,18 @@ int ensure_init() {
       }
     }
   }
+  for (int tc : {2, 4}) {
+    // fp16 BN output, plain and plus a residual; dense-weight spiking layers.
+    for (int rm : {snn::kResNone, snn::kResAddAfter}) {
+      e = cudaFuncSetAttribute(conv_kernel_fn(snn::kModeBnF16, rm, tc),
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, conv_smem_bytes(tc, false));
+      for (int mode = 0; mode < 3 && e == cudaSuccess; ++mode)
+        e = cudaFuncSetAttribute(conv_kernel_fn(mode, rm, tc, true),
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, conv_smem_bytes(tc, true));
+      if (e != cudaSuccess)
+        return g_init_status = fail(SNN_E_CUDA, "smem attribute: %s", cudaGetErrorString(e));
+    }
+  }
   e = cudaFuncSetAttribute(snn::spikformer_attn_lif_kernel<32>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, snn::AttnCfg<32>::kSmemBytes);
   for (int mode = 0; mode < 3 && e == cudaSuccess; ++mode)
@@ -265,6 +300,8 @@ int ensure_init() {
 
 struct Geometry {
   int OH, OW, K, Fpad, n_kb, cin_blocks;
+  int kdup;    // compressed weight tiles per activation k-block (2: dense weights)
+  int Kw;      // weight columns of the packed blob, K * kdup
 };
 
 int check_desc(const snn_conv_desc* d, Geometry* g) {
@@ -278,7 +315,7 @@ int check_desc(const snn_conv_desc* d, Geometry* g) {
   if (d->pad < 0 || d->pad >= d->KH || d->pad >= d->KW) return fail(SNN_E_INVALID, "bad pad");
   if (d->stride == 2 && ((d->H & 1) || (d->W & 1)))
     return fail(SNN_E_INVALID, "stride-2 layers need even H and W");
-  if (d->neuron < SNN_NEURON_LIF || d->neuron > SNN_NEURON_NONE)
+  if (d->neuron < SNN_NEURON_LIF || d->neuron > SNN_NEURON_NONE_F16)
     return fail(SNN_E_INVALID, "bad neuron kind");
   if (d->neuron == SNN_NEURON_LIF && !(d->tau > 0.f)) return fail(SNN_E_INVALID, "tau must be > 0");
   g->OH = (d->H + 2 * d->pad - d->KH) / d->stride + 1;
@@ -288,8 +325,11 @@ int check_desc(const snn_conv_desc* d, Geometry* g) {
   g->Fpad = (d->Cout + snn::kBM - 1) / snn::kBM * snn::kBM;
   g->cin_blocks = d->Cin / snn::kKB;
   g->n_kb = d->KH * d->KW * g->cin_blocks;
-  if (g->K / 32 > snn::kMaxMetaCols)
-    return fail(SNN_E_INVALID, "K=%d exceeds the %d supported", g->K, snn::kMaxMetaCols * 32);
+  g->kdup = (d->flags & SNN_FLAG_DENSE) ? 2 : 1;
+  g->Kw = g->K * g->kdup;
+  if (g->Kw / 32 > snn::kMaxMetaCols)
+    return fail(SNN_E_INVALID, "K=%d exceeds the %d supported%s", g->K, snn::kMaxMetaCols * 32 / g->kdup,
+                g->kdup > 1 ? " for dense weights" : "");
   if ((long long)d->T * d->B > 0x7fffffffLL) return fail(SNN_E_INVALID, "T*B too large");
   if ((long long)d->B * g->OH * g->OW > 0x7fffffffLL)
     return fail(SNN_E_INVALID, "B*OH*OW too large");
@@ -297,7 +337,7 @@ int check_desc(const snn_conv_desc* d, Geometry* g) {
 }
 
 size_t meta_offset(const Geometry& g) {
-  size_t vbytes = static_cast<size_t>(g.Fpad) * (g.K / 2) * 2;
+  size_t vbytes = static_cast<size_t>(g.Fpad) * (g.Kw / 2) * 2;
   return (vbytes + 255) & ~static_cast<size_t>(255);
 }
 
@@ -322,6 +362,8 @@ void general_tile(const Geometry& g, int B, int* tw, int* th, int* tn) {
 
 int select_variant(const snn_conv_desc* d, const Geometry& g) {
   if (d->flags & SNN_FLAG_FORCE_GENERIC) return SNN_VARIANT_GENERIC;
+  // Dense weights and the fp16 BN output run in the general kernel only.
+  if ((d->flags & SNN_FLAG_DENSE) || d->neuron == SNN_NEURON_NONE_F16) return SNN_VARIANT_GENERIC;
   // Only the general kernel has the Add-before-neuron and two-neuron epilogues.
   if (d->res_mode != SNN_RES_ADD_AFTER) return SNN_VARIANT_GENERIC;
   const bool s1_3x3 = d->stride == 1 && d->KH == 3 && d->KW == 3 && d->pad == 1;
@@ -348,7 +390,11 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
   if ((d->flags & (SNN_FLAG_READ_STATE | SNN_FLAG_WRITE_STATE)) && !state)
     return fail(SNN_E_INVALID, "state flags set but state is null");
   if (d->neuron == SNN_NEURON_NONE && residual)
-    return fail(SNN_E_INVALID, "residual needs a neuron");
+    return fail(SNN_E_INVALID, "residual needs a neuron (or the fp16 BN output)");
+  if (d->neuron == SNN_NEURON_NONE_F16 && residual && rm != snn::kResAddAfter)
+    return fail(SNN_E_INVALID, "fp16 BN output takes only the ADD_AFTER residual");
+  if (g.kdup > 1 && (d->neuron >= SNN_NEURON_NONE || (residual && rm != snn::kResAddAfter)))
+    return fail(SNN_E_INVALID, "dense weights: spiking neuron, no residual or the SEW add");
   if (rm == snn::kResTwoNeuron) {
     if ((d->flags & (SNN_FLAG_READ_STATE | SNN_FLAG_WRITE_STATE)) && !state2)
       return fail(SNN_E_INVALID, "state flags set but state2 is null");
@@ -364,9 +410,9 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
   snn::ConvParams p;
   memset(&p, 0, sizeof(p));
   const char* wbytes = static_cast<const char*>(weight);
-  {  // compressed weights [Fpad][K/2]
-    cuuint64_t dims[2] = {static_cast<cuuint64_t>(g.K / 2), static_cast<cuuint64_t>(g.Fpad)};
-    cuuint64_t strides[1] = {static_cast<cuuint64_t>(g.K / 2) * 2};
+  {  // compressed weights [Fpad][Kw/2]
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(g.Kw / 2), static_cast<cuuint64_t>(g.Fpad)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(g.Kw / 2) * 2};
     cuuint32_t box[2] = {snn::kKB / 2, snn::kBM};
     if ((st = encode(&p.tmap_a, 2, wbytes, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B))) return st;
   }
@@ -393,7 +439,7 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
   // in pairs: each CTA loads half of the four-timestep activation box.  3x3
   // only (the 1x1 downsamples measured slower).
   const bool pair = (d->flags & SNN_FLAG_CTA_PAIR) && tc == 4 && p.n_m % 2 == 0 &&
-                    d->neuron != SNN_NEURON_NONE && d->KH * d->KW > 1 &&
+                    d->neuron < SNN_NEURON_NONE && g.kdup == 1 && d->KH * d->KW > 1 &&
                     (rm == snn::kResNone || rm == snn::kResAddAfter);
   const cuuint32_t box5[5] = {static_cast<cuuint32_t>(snn::kKB), static_cast<cuuint32_t>(tw),
                               static_cast<cuuint32_t>(th), static_cast<cuuint32_t>(tn),
@@ -419,6 +465,7 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
       if ((st = encode(&p.tmap_b[m], 5, b, dims, strides, box5, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
     }
   }
+  // fp16 output (spikes, spikes + residual, or the fp16 BN output) or fp32 BN output.
   const bool spikes = d->neuron != SNN_NEURON_NONE;
   if (spikes) p.out = static_cast<__half*>(out);
   else p.out_f32 = static_cast<float*>(out);
@@ -447,6 +494,7 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
   }
   p.timeout_ns = 4000000000ull;   // SM cycles (~2 s at the highest clock)
   const int mode = d->neuron == SNN_NEURON_NONE ? snn::kModeNone
+                   : d->neuron == SNN_NEURON_NONE_F16 ? snn::kModeBnF16
                    : d->neuron == SNN_NEURON_IF ? snn::kModeIf
                    : d->tau == 2.0f ? snn::kModeLifHalf : snn::kModeLifDiv;
 
@@ -661,10 +709,9 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
   const int per_m = std::max(1, std::min(p.n_px_tiles, g_num_sms / p.n_m));
   const long long grid = static_cast<long long>(per_m) * p.n_m;
   if (grid > 0x7fffffffLL) return fail(SNN_E_INVALID, "grid too large");
-  cudaError_t e = launch_pdl(conv_kernel_fn(mode, rm, tc),
+  cudaError_t e = launch_pdl(conv_kernel_fn(mode, rm, tc, g.kdup > 1),
                              dim3(static_cast<unsigned>(grid)), dim3(snn::kThreads),
-                             tc == 4 ? snn::GenCfg<4>::kSmemBytes : snn::GenCfg<2>::kSmemBytes,
-                             stream, p);
+                             conv_smem_bytes(tc, g.kdup > 1), stream, p);
   if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));
   return SNN_OK;
 }
@@ -677,19 +724,24 @@ template <bool POOL, int KS = 0>
 GlueKernel glue_fn(int mode) {
   if (mode == snn::kModeLifHalf) return snn::glue_neuron_kernel<snn::kModeLifHalf, POOL, KS>;
   if (mode == snn::kModeLifDiv) return snn::glue_neuron_kernel<snn::kModeLifDiv, POOL, KS>;
+  if constexpr (POOL)
+    if (mode == snn::kModeNone) return snn::glue_neuron_kernel<snn::kModeNone, true, KS>;
   return snn::glue_neuron_kernel<snn::kModeIf, POOL, KS>;
 }
 
-// Shared checks and launch of the Add / MaxPool + neuron glue.
+// Shared checks and launch of the Add / MaxPool + neuron glue; one_input:
+// the neuron of `a` alone (b unused).
 int launch_glue(const snn_conv_desc* d, bool pool, const void* a, const void* b, float* state,
-                void* out, void* stream) {
+                void* out, void* stream, bool one_input = false) {
   int st = ensure_init();
   if (st) return st;
-  if (!d || !a || (!pool && !b) || !out) return fail(SNN_E_INVALID, "null pointer");
+  if (!d || !a || (!pool && !one_input && !b) || !out) return fail(SNN_E_INVALID, "null pointer");
+  if (one_input) b = nullptr;
   if (d->T < 1 || d->B < 1 || d->H < 1 || d->W < 1 || d->Cout < 8 || d->Cout % 8)
     return fail(SNN_E_INVALID, "bad shape (channels a positive multiple of 8)");
-  if (d->neuron != SNN_NEURON_LIF && d->neuron != SNN_NEURON_IF)
-    return fail(SNN_E_INVALID, "neuron must be LIF or IF");
+  const bool no_neuron = pool && d->neuron == SNN_NEURON_NONE;   // plain max pool
+  if (d->neuron != SNN_NEURON_LIF && d->neuron != SNN_NEURON_IF && !no_neuron)
+    return fail(SNN_E_INVALID, pool ? "neuron must be LIF, IF or NONE" : "neuron must be LIF or IF");
   if (d->neuron == SNN_NEURON_LIF && !(d->tau > 0.0f)) return fail(SNN_E_INVALID, "tau must be positive");
   if ((d->flags & (SNN_FLAG_READ_STATE | SNN_FLAG_WRITE_STATE)) && !state)
     return fail(SNN_E_INVALID, "state flags set but state is null");
@@ -720,7 +772,8 @@ int launch_glue(const snn_conv_desc* d, bool pool, const void* a, const void* b,
   // Reference computes (1.0 - 1.0/tau) in double, then float32 (models/neurons.py:125).
   p.decay = d->neuron == SNN_NEURON_LIF ? static_cast<float>(1.0 - 1.0 / static_cast<double>(d->tau)) : 1.0f;
   p.v_th = d->v_threshold; p.v_reset = d->v_reset;
-  const int mode = d->neuron == SNN_NEURON_IF ? snn::kModeIf
+  const int mode = no_neuron ? snn::kModeNone
+                   : d->neuron == SNN_NEURON_IF ? snn::kModeIf
                    : d->tau == 2.0f ? snn::kModeLifHalf : snn::kModeLifDiv;
   const long long n = static_cast<long long>(d->B) * p.OH * p.OW * (d->Cout / 8);
   const long long blocks = std::max<long long>(1, std::min<long long>((n + 255) / 256,
@@ -766,7 +819,7 @@ int snn_conv_weight_bytes(const snn_conv_desc* d, size_t* bytes) {
   int st = check_desc(d, &g);
   if (st) return st;
   if (!bytes) return fail(SNN_E_INVALID, "null output");
-  *bytes = meta_offset(g) + static_cast<size_t>(g.Fpad / snn::kBM) * (g.K / 32) * snn::kBM * 4;
+  *bytes = meta_offset(g) + static_cast<size_t>(g.Fpad / snn::kBM) * (g.Kw / 32) * snn::kBM * 4;
   return SNN_OK;
 }
 
@@ -775,7 +828,7 @@ int snn_pack_weight_24(const snn_conv_desc* d, const float* w, void* blob) {
   int st = check_desc(d, &g);
   if (st) return st;
   if (!w || !blob) return fail(SNN_E_INVALID, "null pointer");
-  const int F = d->Cout, C = d->Cin, KH = d->KH, KW = d->KW, K = g.K;
+  const int F = d->Cout, C = d->Cin, KH = d->KH, KW = d->KW, K = g.Kw;
   uint8_t* out = static_cast<uint8_t*>(blob);
   size_t total = 0;
   snn_conv_weight_bytes(d, &total);
@@ -786,7 +839,26 @@ int snn_pack_weight_24(const snn_conv_desc* d, const float* w, void* blob) {
   const int G = K / 4;
   uint8_t* nib = new uint8_t[static_cast<size_t>(g.Fpad) * G];
   memset(nib, 0x4, static_cast<size_t>(g.Fpad) * G);
-  for (int f = 0; f < F; ++f) {
+  if (g.kdup > 1) {
+    // Dense weights as two 2:4 halves per activation k-block kb: weight
+    // k-block 2kb keeps positions (0,1) of every group of four input
+    // channels, 2kb+1 keeps (2,3); both meet the same activations.
+    for (int f = 0; f < F; ++f)
+      for (int kh = 0; kh < KH; ++kh)
+        for (int kw = 0; kw < KW; ++kw)
+          for (int c0 = 0; c0 < C; c0 += 4) {
+            const int kb = (kh * KW + kw) * g.cin_blocks + c0 / snn::kKB;
+            const int gi = (c0 % snn::kKB) / 4;
+            for (int h = 0; h < 2; ++h) {
+              const int grp = (kb * 2 + h) * (snn::kKB / 4) + gi;
+              for (int u = 0; u < 2; ++u)
+                vals[static_cast<size_t>(f) * (K / 2) + 2 * grp + u] = __float2half_rn(
+                    w[((static_cast<size_t>(f) * C + c0 + 2 * h + u) * KH + kh) * KW + kw]);
+              nib[static_cast<size_t>(f) * G + grp] = h ? (2 | (3 << 2)) : (0 | (1 << 2));
+            }
+          }
+  }
+  for (int f = 0; f < F && g.kdup == 1; ++f) {
     for (int kh = 0; kh < KH; ++kh) {
       for (int kw = 0; kw < KW; ++kw) {
         for (int c0 = 0; c0 < C; c0 += 4) {
@@ -876,7 +948,8 @@ int snn_stem_forward(const snn_conv_desc* d, int32_t Tin, const float* x, const 
       static_cast<long long>(d->KH) * d->KW * d->Cin * d->Cout > 12288)
     return fail(SNN_E_INVALID, "unsupported stem geometry (Cout multiple of 16, K*Cout <= 12288)");
   if (Tin != 1 && Tin != d->T) return fail(SNN_E_INVALID, "Tin must be 1 or T");
-  if (d->neuron == SNN_NEURON_NONE) return fail(SNN_E_INVALID, "stem needs a neuron");
+  if (d->neuron < SNN_NEURON_LIF || d->neuron > SNN_NEURON_NONE)
+    return fail(SNN_E_INVALID, "stem neuron must be LIF, IF or NONE (fp16 BN output)");
   const int OH = (d->H + 2 * d->pad - d->KH) / d->stride + 1;
   const int OW = (d->W + 2 * d->pad - d->KW) / d->stride + 1;
   if (OH < 1 || OW < 1) return fail(SNN_E_INVALID, "empty output");
@@ -895,7 +968,8 @@ int snn_stem_forward(const snn_conv_desc* d, int32_t Tin, const float* x, const 
     return fail(SNN_E_CUDA, "error word address");
   // Tensor-core fast path: 3x3 s1 p1, 64 channels, input repeated over T,
   // rows of at most 128 pixels.
-  if (Tin == 1 && d->KH == 3 && d->KW == 3 && d->stride == 1 && d->pad == 1 && d->Cout == 64 &&
+  if (Tin == 1 && d->neuron != SNN_NEURON_NONE && d->KH == 3 && d->KW == 3 && d->stride == 1 &&
+      d->pad == 1 && d->Cout == 64 &&
       (d->Cin == 1 || d->Cin == 3) && OW <= snn::kStemPx) {
     const int mode = d->neuron == SNN_NEURON_IF ? snn::kModeIf
                      : d->tau == 2.0f ? snn::kModeLifHalf : snn::kModeLifDiv;
@@ -962,6 +1036,10 @@ int snn_add_lif_forward(const snn_conv_desc* d, const void* a, const void* b, fl
 int snn_maxpool_lif_forward(const snn_conv_desc* d, const void* x, float* state, void* out,
                             void* stream) {
   return launch_glue(d, true, x, nullptr, state, out, stream);
+}
+
+int snn_lif_forward(const snn_conv_desc* d, const void* x, float* state, void* out, void* stream) {
+  return launch_glue(d, false, x, nullptr, state, out, stream, true);
 }
 
 int snn_spikformer_attn_forward(int32_t T, int32_t B, int32_t N, int32_t heads,

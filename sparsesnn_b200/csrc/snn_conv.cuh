@@ -65,15 +65,23 @@ constexpr int kBarBytes = 512;
 //    pair's k-blocks come every ~510 cycles (the MMA then reads the peer's
 //    half of B across the pair), layers 2-4 us faster in isolation, no
 //    faster inside the whole-forward graph.
-template <int TC, bool CG2 = false>
+//  * AD = 2 (dense weights): a dense layer runs as the sum of two 2:4 layers
+//    over the same activations -- weight half 0 keeps positions 0,1 of every
+//    group of four input channels, half 1 keeps positions 2,3 -- so each
+//    activation k-block meets two compressed weight tiles (two MMAs with
+//    their own metadata columns, one B operand).  The stage holds both
+//    weight tiles; the activation bytes per MMA halve.
+template <int TC, bool CG2 = false, int AD = 1>
 struct GenCfg {
   static_assert(!CG2 || TC == 4, "CTA pairs use the four-timestep tiles");
+  static_assert(AD == 1 || (AD == 2 && !CG2), "dense weights: one-CTA tiles");
   static constexpr int kTC = TC;
+  static constexpr int kAD = AD;
   static constexpr int kNumAcc = TC == 4 ? 1 : 2;
-  static constexpr int kStages = CG2 ? 8 : TC == 4 ? 5 : 4;
+  static constexpr int kStages = CG2 ? 8 : TC == 4 ? (AD == 2 ? 4 : 5) : (AD == 2 ? 3 : 4);
   static constexpr int kKbPerStage = TC == 4 ? 1 : 2;
   static constexpr int kBTs = CG2 ? TC / 2 : TC;     // timesteps of the box this CTA loads
-  static constexpr int kStageBytes = kKbPerStage * (kABytes + kBTs * kBBytes);
+  static constexpr int kStageBytes = kKbPerStage * (AD * kABytes + kBTs * kBBytes);
   static constexpr int kAccCols = kTC * kBN;
   static constexpr int kSmemBytes = kStages * kStageBytes + kEpiWarps * kXposeBytes + kBarBytes + 1024;
   static_assert(kNumAcc * kAccCols <= kMetaCol, "accumulators overlap the metadata columns");
@@ -83,8 +91,10 @@ enum NeuronKind : int { kLIF = 0, kIF = 1, kNoNeuron = 2 };
 // Epilogue variants (template parameter): LIF with tau == 2 (every scaling
 // by 1/2 is exact, so the update folds into two FMAs with the reference's
 // rounding), LIF with general tau (v*(1-1/tau) + x/tau, each op rounded),
-// IF, and BN output without neuron.
-enum EpiMode : int { kModeLifHalf = 0, kModeLifDiv = 1, kModeIf = 2, kModeNone = 3 };
+// IF, BN output without neuron (fp32), and BN output without neuron in
+// fp16 through the store tile (plus a real-valued residual when RM is
+// kResAddAfter: out = bn + residual, rounded once).
+enum EpiMode : int { kModeLifHalf = 0, kModeLifDiv = 1, kModeIf = 2, kModeNone = 3, kModeBnF16 = 4 };
 
 // One neuron step.  x2 is the BN output pre-scaled for kModeLifHalf
 // (acc*(scale/2) + bias/2 == (acc*scale + bias)/2 exactly) and the plain BN
@@ -126,6 +136,10 @@ __device__ __forceinline__ int xpose_off(int px, int c8) {
 __device__ __forceinline__ void xpose_put(uint8_t* xb, int i, int lane, bool spike) {
   *reinterpret_cast<__half*>(xb + xpose_off(i, lane >> 3) + (lane & 7) * 2) =
       __ushort_as_half(spike ? 0x3C00 : 0);
+}
+// A real value of this lane's channel at column i (rounded to fp16).
+__device__ __forceinline__ void xpose_put_val(uint8_t* xb, int i, int lane, float x) {
+  *reinterpret_cast<__half*>(xb + xpose_off(i, lane >> 3) + (lane & 7) * 2) = __float2half_rn(x);
 }
 // Residual of this lane's channel at column i, from a transpose tile that
 // holds the residual rows in store layout (the same place xpose_put writes).
@@ -238,13 +252,16 @@ __device__ __forceinline__ TileCoord tile_coord(const ConvParams& p, int pt) {
   return c;
 }
 
-template <int MODE, int RM, int TC, bool CG2 = false>
+template <int MODE, int RM, int TC, bool CG2 = false, int AD = 1>
 __global__ void __launch_bounds__(kThreads, 1)
 fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
   constexpr bool RES = RM != kResNone;
+  constexpr bool SPIKING = MODE != kModeNone && MODE != kModeBnF16;
   static_assert(MODE != kModeNone || RM == kResNone, "a residual epilogue needs a neuron");
-  static_assert(!CG2 || (MODE != kModeNone && RM <= kResAddAfter), "CTA pairs: spiking, SEW or none");
-  using Cfg = GenCfg<TC, CG2>;
+  static_assert(MODE != kModeBnF16 || RM == kResNone || RM == kResAddAfter,
+                "fp16 BN output: plain or plus the residual");
+  static_assert(!CG2 || (SPIKING && RM <= kResAddAfter), "CTA pairs: spiking, SEW or none");
+  using Cfg = GenCfg<TC, CG2, AD>;
   constexpr int kBTs = Cfg::kBTs;
   constexpr int kTC = Cfg::kTC, kNumAcc = Cfg::kNumAcc, kStages = Cfg::kStages;
   constexpr int kKbPerStage = Cfg::kKbPerStage, kStageBytes = Cfg::kStageBytes;
@@ -252,9 +269,9 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  // Stage s holds k-blocks (A: kKbPerStage x kABytes; B: kKbPerStage x kTC x kBBytes).
+  // Stage s holds k-blocks (A: kKbPerStage x AD x kABytes; B: kKbPerStage x kTC x kBBytes).
   uint8_t* sA = smem;
-  uint8_t* sB = smem + kStages * kKbPerStage * kABytes;
+  uint8_t* sB = smem + kStages * kKbPerStage * AD * kABytes;
   uint8_t* sX = smem + kStages * kStageBytes;                // kEpiWarps x kXposeBytes
   uint64_t* full = reinterpret_cast<uint64_t*>(sX + kEpiWarps * kXposeBytes);
   uint64_t* empty = full + kStages;
@@ -284,7 +301,7 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
     pt_step = gridDim.x / p.n_m;
   }
   const int n_chunks = (p.T + kTC - 1) / kTC;
-  const int n_meta = 2 * p.n_kb;                               // sparse K steps (32 each)
+  const int n_meta = 2 * p.n_kb * AD;                          // sparse K steps (32 each)
   // Pair: one arrival per epilogue warp of both CTAs on the leader's barriers.
   constexpr int kEpiArrivals = CG2 ? 2 * kEpiWarps : kEpiThreads;
 
@@ -343,16 +360,19 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
               // The leader's barrier counts both CTAs' bytes.
               if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * nk * (kABytes + kBTs * p.box_bytes));
             } else {
-              mbar_arrive_expect_tx(&full[stage], nk * (kABytes + kTC * p.box_bytes));
+              mbar_arrive_expect_tx(&full[stage], nk * (AD * kABytes + kTC * p.box_bytes));
             }
             for (int j = 0; j < nk; ++j) {
               const int kb = kb0 + j;
-              if constexpr (CG2)
+              if constexpr (CG2) {
                 tma_load_2d_pair(sA + (stage * kKbPerStage + j) * kABytes, &p.tmap_a,
                                  full_l + stage * 8, kb * (kKB / 2), m_tile * kBM);
-              else
-                tma_load_2d(sA + (stage * kKbPerStage + j) * kABytes, &p.tmap_a, &full[stage],
-                            kb * (kKB / 2), m_tile * kBM);
+              } else {
+#pragma unroll
+                for (int h = 0; h < AD; ++h)   // weight k-block kb*AD + h meets activation k-block kb
+                  tma_load_2d(sA + ((stage * kKbPerStage + j) * AD + h) * kABytes, &p.tmap_a,
+                              &full[stage], (kb * AD + h) * (kKB / 2), m_tile * kBM);
+              }
               const int tap = kb / p.cin_blocks;
               const int cb = kb - tap * p.cin_blocks;
               const int kh = tap / p.KW, kw = tap - kh * p.KW;
@@ -420,17 +440,18 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
             }
             tc_fence_after();
             const int nk = min(kKbPerStage, p.n_kb - kb0);
-            for (int j = 0; j < nk; ++j) {
-              const int kb = kb0 + j;
+            for (int jh = 0; jh < nk * AD; ++jh) {
+              const int j = jh / AD;
+              const int kbw = (kb0 + j) * AD + (jh - j * AD);   // weight k-block
               // Descriptors advance by adding (byte offset >> 4) to the start
               // address field (shared-memory addresses stay below 2^18).
-              const uint64_t ad = a_desc0 + (((stage * kKbPerStage + j) * kABytes) >> 4);
+              const uint64_t ad = a_desc0 + (((stage * kKbPerStage * AD + jh) * kABytes) >> 4);
               const uint64_t bd = b_desc0 + (((stage * kKbPerStage + j) * kBTs * kBBytes) >> 4);
 #pragma unroll
               for (int s = 0; s < 2; ++s) {
-                const uint32_t ecol = kMetaCol + 2 * kb + s;
+                const uint32_t ecol = kMetaCol + 2 * kbw + s;
                 const uint32_t e_addr = tmem + (ecol & ~1u);
-                const uint32_t acc = (kb > 0 || s > 0) ? 1u : 0u;
+                const uint32_t acc = (kbw > 0 || s > 0) ? 1u : 0u;
                 if constexpr (CG2) {
                   // Pair: M = 256 (this CTA's rows and the follower's), N = 256
                   // (this CTA's two timesteps, then the follower's two).
@@ -629,16 +650,23 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
                 if (lane == 0) bulk_wait_group_read<0>();
                 __syncwarp();
               }
-              if constexpr (RM == kResAddBefore || RM == kResTwoNeuron) {
-                // The residual enters the neuron: its rows go through the
-                // transpose tile, each lane reads its channel per column and
-                // the spike overwrites that same half.
+              if constexpr (RM == kResAddBefore || RM == kResTwoNeuron ||
+                            (MODE == kModeBnF16 && RM == kResAddAfter)) {
+                // The residual enters the neuron (or the real-valued sum):
+                // its rows go through the transpose tile, each lane reads its
+                // channel per column and the result overwrites that same half.
                 xpose_put_rows(xb, lane, r4[u]);
                 __syncwarp();
               }
 #pragma unroll
               for (int i = 0; i < 32; ++i) {
                 float x = fmaf(__uint_as_float(accr[u][i]), sx, bx);
+                if constexpr (MODE == kModeBnF16) {
+                  // No neuron: bn (+ residual) in fp32, rounded to fp16 once.
+                  if constexpr (RM == kResAddAfter) x = __fadd_rn(x, xpose_get(xb, i, lane));
+                  xpose_put_val(xb, i, lane, x);
+                  continue;
+                }
                 if constexpr (RM == kResAddBefore) {
                   // kModeLifHalf: x is bn/2, and bn/2 + r/2 rounds to exactly
                   // (bn + r)/2, the folded form of the neuron's input.
@@ -655,7 +683,7 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
               }
               __syncwarp();
               if (tma_out) {
-                if constexpr (RM == kResAddAfter) add_rows_into_xpose(xb, lane, r4[u]);
+                if constexpr (RM == kResAddAfter && MODE != kModeBnF16) add_rows_into_xpose(xb, lane, r4[u]);
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) {
@@ -664,8 +692,8 @@ fused_sparse_conv_lif_kernel(const __grid_constant__ ConvParams p) {
                 }
                 ++n_st;
               } else {
-                store_xpose_rows<RM == kResAddAfter>(p.out, xb, tbase, rows, p.F, cbase, lane, chunk_ok,
-                                                     r4[u]);
+                store_xpose_rows<RM == kResAddAfter && MODE != kModeBnF16>(p.out, xb, tbase, rows, p.F,
+                                                                           cbase, lane, chunk_ok, r4[u]);
                 __syncwarp();
               }
             }

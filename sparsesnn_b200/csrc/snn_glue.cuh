@@ -111,6 +111,10 @@ stem_conv_lif_kernel(const StemParams p) {
       uint32_t bits = 0;
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
+        if (p.neuron == 2) {           // no neuron: the BN output in fp16
+          bits |= static_cast<uint32_t>(__half_as_ushort(__float2half_rn(xb[j + u]))) << (16 * u);
+          continue;
+        }
         float h;
         if (p.neuron == 0) h = __fadd_rn(__fmul_rn(v[j + u], p.decay), __fdiv_rn(xb[j + u], p.tau));
         else h = __fadd_rn(v[j + u], xb[j + u]);
@@ -364,20 +368,30 @@ struct GlueParams {
 
 template <int MODE>
 __device__ __forceinline__ uint4 glue_neuron8(float (&v)[8], const float (&x)[8], const GlueParams& p) {
-  uint32_t w[4];
+  if constexpr (MODE == kModeNone) {
+    // No neuron (plain max pool): the inputs pass through (exact, they came from fp16).
+    uint32_t w[4];
 #pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    uint32_t bits = 0;
+    for (int u = 0; u < 4; ++u)
+      w[u] = __half_as_ushort(__float2half_rn(x[2 * u])) |
+             (static_cast<uint32_t>(__half_as_ushort(__float2half_rn(x[2 * u + 1]))) << 16);
+    return make_uint4(w[0], w[1], w[2], w[3]);
+  } else {
+    uint32_t w[4];
 #pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const int j = 2 * u + e;
-      // kModeLifHalf takes the input pre-halved (exact).
-      const float xi = MODE == kModeLifHalf ? x[j] * 0.5f : x[j];
-      if (neuron_step<MODE>(v[j], xi, p.decay, p.tau, p.v_th, p.v_reset)) bits |= 0x3C00u << (16 * e);
+    for (int u = 0; u < 4; ++u) {
+      uint32_t bits = 0;
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int j = 2 * u + e;
+        // kModeLifHalf takes the input pre-halved (exact).
+        const float xi = MODE == kModeLifHalf ? x[j] * 0.5f : x[j];
+        if (neuron_step<MODE>(v[j], xi, p.decay, p.tau, p.v_th, p.v_reset)) bits |= 0x3C00u << (16 * e);
+      }
+      w[u] = bits;
     }
-    w[u] = bits;
+    return make_uint4(w[0], w[1], w[2], w[3]);
   }
-  return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
 // KS: compile-time square pool window (2 or 3: every window load is issued
@@ -397,7 +411,7 @@ glue_neuron_kernel(const GlueParams p) {
     float v[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j)
-      v[j] = (p.flags & kReadState) ? p.state[pix * p.C + c8 * 8 + j] : 0.f;
+      v[j] = (MODE != kModeNone && (p.flags & kReadState)) ? p.state[pix * p.C + c8 * 8 + j] : 0.f;
     for (int t = 0; t < p.T; ++t) {
       float x[8];
       if constexpr (POOL && KS > 0) {
@@ -457,9 +471,11 @@ glue_neuron_kernel(const GlueParams p) {
           x[2 * j] = f.x; x[2 * j + 1] = f.y;
         }
       } else {
+        // Add + neuron, or the neuron of one input alone when b is null.
         const size_t off = (static_cast<size_t>(t) * P + pix) * p.C;
         const uint4 ua = __ldg(reinterpret_cast<const uint4*>(p.a + off) + c8);
-        const uint4 ub = __ldg(reinterpret_cast<const uint4*>(p.b + off) + c8);
+        const uint4 ub = p.b ? __ldg(reinterpret_cast<const uint4*>(p.b + off) + c8)
+                             : make_uint4(0, 0, 0, 0);
         const __half2* ha = reinterpret_cast<const __half2*>(&ua);
         const __half2* hb = reinterpret_cast<const __half2*>(&ub);
 #pragma unroll
@@ -472,7 +488,7 @@ glue_neuron_kernel(const GlueParams p) {
       reinterpret_cast<uint4*>(p.out + (static_cast<size_t>(t) * P + pix) * p.C)[c8] =
           glue_neuron8<MODE>(v, x, p);
     }
-    if (p.flags & kWriteState) {
+    if (MODE != kModeNone && (p.flags & kWriteState)) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) p.state[pix * p.C + c8 * 8 + j] = v[j];
     }

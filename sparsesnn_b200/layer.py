@@ -43,17 +43,26 @@ class SparseConvBNLIF:
     (the neuron integrates ``bn + residual``) or ``"two_neuron"`` (``out =
     neuron2(spike + residual)``, second membrane ``state2``; ``neuron2``,
     ``tau2``, ``v_threshold2``, ``v_reset2`` describe that neuron).
+
+    ``neuron="none"`` gives the fp32 BN output, ``"none_f16"`` the fp16 BN
+    output (with a residual: ``out = bn + residual``).  ``dense=True`` takes
+    an unpruned weight and runs it as two 2:4 halves (``SNN_FLAG_DENSE``).
     """
 
     def __init__(self, weight, bn_scale, bn_bias, *, T, B, H, W, stride=1, pad=None,
                  neuron="lif", tau=2.0, v_threshold=1.0, v_reset=0.0, device="cuda",
                  force_generic=False, res_mode="add_after", neuron2="lif", tau2=2.0,
-                 v_threshold2=1.0, v_reset2=0.0):
+                 v_threshold2=1.0, v_reset2=0.0, dense=False):
         w = _np(weight).astype(np.float32)
         if w.ndim == 2:                       # Linear [out, in] -> 1x1 conv
             w = w[:, :, None, None]
         cout, cin, kh, kw = w.shape
+        self.base_flags = (rt.SNN_FLAG_FORCE_GENERIC if force_generic else 0) | \
+            (rt.SNN_FLAG_DENSE if dense else 0)
+        self.dense = dense
+        self.neuron = neuron
         self.desc = rt.make_desc(T=T, B=B, Cin=cin, H=H, W=W, Cout=cout, KH=kh, KW=kw,
+                                 flags=self.base_flags,
                                  stride=stride, pad=(kh // 2 if pad is None else pad),
                                  neuron=neuron, tau=tau, v_threshold=v_threshold,
                                  v_reset=v_reset, res_mode=res_mode, neuron2=neuron2,
@@ -68,7 +77,6 @@ class SparseConvBNLIF:
         self.T, self.B, self.Cin, self.Cout = T, B, cin, cout
         self.H, self.W = H, W
         self.out_dtype = torch.float32 if neuron == "none" else torch.float16
-        self.base_flags = rt.SNN_FLAG_FORCE_GENERIC if force_generic else 0
 
     def out_shape(self):
         return (self.T * self.B, self.OH, self.OW, self.Cout)

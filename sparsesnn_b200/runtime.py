@@ -21,10 +21,12 @@ SNN_E_DEVICE = -5
 SNN_NEURON_LIF = 0
 SNN_NEURON_IF = 1
 SNN_NEURON_NONE = 2
+SNN_NEURON_NONE_F16 = 3
 SNN_FLAG_READ_STATE = 1
 SNN_FLAG_WRITE_STATE = 2
 SNN_FLAG_FORCE_GENERIC = 4
 SNN_FLAG_CTA_PAIR = 8
+SNN_FLAG_DENSE = 16
 SNN_VARIANT_GENERIC = 0
 SNN_VARIANT_HALO_RESIDENT = 1
 SNN_VARIANT_HALO_STREAM = 2
@@ -32,14 +34,15 @@ SNN_RES_ADD_AFTER = 0
 SNN_RES_ADD_BEFORE = 1
 SNN_RES_TWO_NEURON = 2
 
-NEURONS = {"lif": SNN_NEURON_LIF, "if": SNN_NEURON_IF, "none": SNN_NEURON_NONE}
+NEURONS = {"lif": SNN_NEURON_LIF, "if": SNN_NEURON_IF, "none": SNN_NEURON_NONE,
+           "none_f16": SNN_NEURON_NONE_F16}
 
 # Every symbol include/snn_b200.h declares.
 EXPORTED = (
     "snn_abi_version", "snn_init", "snn_conv_variant", "snn_conv_out_shape", "snn_conv_weight_bytes",
     "snn_pack_weight_24", "snn_conv_forward", "snn_conv_forward_res", "snn_conv_forward_res2",
     "snn_stem_forward", "snn_spikformer_attn_forward", "snn_add_lif_forward",
-    "snn_maxpool_lif_forward",
+    "snn_maxpool_lif_forward", "snn_lif_forward",
     "snn_head_forward", "snn_get_device_error", "snn_last_error_message",
     "snn_engine_check_file", "snn_engine_load", "snn_engine_io", "snn_engine_capture",
     "snn_engine_run", "snn_engine_destroy",
@@ -86,6 +89,7 @@ def _declare(lib):
         "snn_head_forward": ([i32, i32, i32, i32, i32, P, P, P, P, P], ctypes.c_int),
         "snn_add_lif_forward": ([D, P, P, P, P, P], ctypes.c_int),
         "snn_maxpool_lif_forward": ([D, P, P, P, P], ctypes.c_int),
+        "snn_lif_forward": ([D, P, P, P, P], ctypes.c_int),
         "snn_spikformer_attn_forward": ([i32, i32, i32, i32, i32, ctypes.c_float, ctypes.c_float,
                                          ctypes.c_float, ctypes.c_float, i32, P, P, P, P, P, P],
                                         ctypes.c_int),

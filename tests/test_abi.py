@@ -34,7 +34,7 @@ def test_exports_every_declared_symbol(_lib):
 
 
 def test_abi_version(_lib):
-    assert _lib.snn_abi_version() == 2
+    assert _lib.snn_abi_version() == 3
 
 
 def test_desc_struct_layout():

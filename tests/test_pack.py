@@ -133,3 +133,35 @@ def test_rejects_dense_group():
     assert e.value.code == rt.SNN_E_NOT_24
     with pytest.raises(ValueError):
         P.pack_meta(P.conv_weight_to_fk(w))
+
+
+@pytest.mark.parametrize("f, c, k", [(96, 64, 3), (192, 128, 3), (136, 192, 1)])
+def test_dense_split_packer_bit_exact(f, c, k):
+    """Dense weights (SNN_FLAG_DENSE): the C packer's two 2:4 halves per
+    activation k-block equal the numpy restatement, zeros included, and the
+    halves sum back to the fp16 dense weight."""
+    from oracle.pack24 import conv_weight_to_fk, pack_dense_split, unpack
+    rng = np.random.default_rng(f + c + k)
+    w = rng.standard_normal((f, c, k, k)).astype(np.float32)
+    w[0, :8] = 0.0                                    # whole zero groups keep their fixed pairs
+    d = rt.make_desc(T=1, B=1, Cin=c, H=8, W=8, Cout=f, KH=k, KW=k, flags=rt.SNN_FLAG_DENSE)
+    blob = rt.pack_weight_24(d, w)
+    f_pad = -(-f // 128) * 128
+    K = c * k * k
+    vals, meta = split_blob(blob, f_pad, 2 * K)
+    rv, rm = pack_dense_split(w)
+    assert np.array_equal(vals.view(np.uint16), rv.view(np.uint16))
+    assert np.array_equal(meta, rm)
+    virt = unpack(vals, meta, f, 2 * K).reshape(f, K // 64, 2, 64)
+    dense = conv_weight_to_fk(w).astype(np.float16).astype(np.float32).reshape(f, K // 64, 64)
+    assert np.array_equal(virt.sum(axis=2), dense)
+
+
+def test_dense_flag_doubles_weight_bytes_and_limits_k():
+    d = rt.make_desc(T=1, B=1, Cin=128, H=8, W=8, Cout=128, KH=3, KW=3)
+    dd = rt.make_desc(T=1, B=1, Cin=128, H=8, W=8, Cout=128, KH=3, KW=3, flags=rt.SNN_FLAG_DENSE)
+    n1, n2 = rt.weight_bytes(d), rt.weight_bytes(dd)
+    assert n2 == 2 * n1
+    big = rt.make_desc(T=1, B=1, Cin=512, H=8, W=8, Cout=128, KH=3, KW=3, flags=rt.SNN_FLAG_DENSE)
+    with pytest.raises(rt.SnnError):
+        rt.weight_bytes(big)                          # 2 * 4608 > 8192 weight columns
