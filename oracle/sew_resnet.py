@@ -29,9 +29,15 @@ STAGES = (64, 128, 256, 512)
 BLOCKS = (2, 2, 2, 2)
 
 
-def _conv_w(rng, f, c, k):
-    # kaiming_normal_(mode='fan_out', nonlinearity='relu'): std = sqrt(2/(f*k*k))
-    return (rng.standard_normal((f, c, k, k)) * np.sqrt(2.0 / (f * k * k))).astype(np.float32)
+# Kaiming-normal, fan-in, ReLU gain, scaled by 1/sqrt(E[x^2]) of the layer's
+# input (spikes firing at about 11%: gain 3), so that random weights keep the
+# network firing through every stage (the reference's fan-out init with
+# threshold-1 neurons leaves an untrained network nearly silent).
+SPIKE_GAIN = 3.0
+
+
+def _conv_w(rng, f, c, k, gain=SPIKE_GAIN):
+    return (rng.standard_normal((f, c, k, k)) * gain * np.sqrt(2.0 / (c * k * k))).astype(np.float32)
 
 
 def _bn(rng, f):
@@ -42,10 +48,14 @@ def _bn(rng, f):
 
 
 def make_params(seed: int = 0, num_classes: int = 100, in_channels: int = 3,
-                stem_channels: int = 64):
-    """Seeded SEW-ResNet-18 parameters; every non-stem conv 2:4-pruned along Cin."""
+                stem_channels: int = 64, stem_kernel: int = 3, input_moment: float = 1.0):
+    """Seeded SEW-ResNet-18 parameters; every non-stem conv 2:4-pruned along Cin
+    (``stem_kernel`` 7: the ImageNet / DVS stem; ``input_moment``: E[x^2] of
+    the stem's input, 0.05 for Bernoulli(0.05) event frames)."""
     rng = np.random.default_rng(seed)
-    P = {"stem": {"w": _conv_w(rng, stem_channels, in_channels, 3), "bn": _bn(rng, stem_channels)},
+    P = {"stem": {"w": _conv_w(rng, stem_channels, in_channels, stem_kernel,
+                               1.0 / np.sqrt(input_moment)),
+                  "bn": _bn(rng, stem_channels)},
          "blocks": []}
     inpl = stem_channels
     for si, (planes, nb) in enumerate(zip(STAGES, BLOCKS)):
@@ -70,9 +80,23 @@ def make_input(seed: int, B: int, H: int = 32, W: int = 32, C: int = 3):
     return rng.standard_normal((B, C, H, W)).astype(np.float32)
 
 
+def make_dvs_input(seed: int, B: int, T: int = 16, H: int = 128, W: int = 128, C: int = 2,
+                   p: float = 0.05):
+    """Event frames: Bernoulli(p) {0,1} per polarity, pixel and timestep, in
+    the reference's DVS layout ``[B, T, C, H, W]``."""
+    rng = np.random.default_rng(seed + 2000)
+    return (rng.random((B, T, C, H, W)) < p).astype(np.float32)
+
+
 def forward_torch(P, x, T: int = 4, tau: float = 2.0, v_th: float = 1.0, threads: int | None = None,
-                  return_trace: bool = False):
-    """Reference-path forward in torch (CPU, fp32).  ``x`` is ``[B,3,H,W]``.
+                  return_trace: bool = False, stem_stride: int = 1, maxpool: bool = False):
+    """Reference-path forward in torch (CPU, fp32).
+
+    ``x`` is ``[B,C,H,W]`` (direct encoding: the stem's BN output repeated
+    over T, ``models/sewresnet.py:197-201``) or ``[B,T,C,H,W]`` event frames
+    (the stem runs on every timestep, ``:191-196``).  ``stem_stride=2,
+    maxpool=True`` is the ImageNet/DVS stem (7x7/2, MaxPool(3,2,1) after the
+    neuron, ``:140-143,202-203``).
 
     Returns logits ``[B, classes]`` (numpy); with ``return_trace`` also the
     per-layer spike tensors ``[T,B,C,H,W]`` keyed by layer name.
@@ -108,9 +132,23 @@ def forward_torch(P, x, T: int = 4, tau: float = 2.0, v_th: float = 1.0, threads
 
     with torch.no_grad():
         xt = t(x)
-        y = bn(F.conv2d(xt, t(P["stem"]["w"]), stride=1, padding=1), P["stem"]["bn"])
-        h = lif(y.unsqueeze(0).repeat(T, 1, 1, 1, 1))
+        w0 = P["stem"]["w"]
+        pad0 = w0.shape[2] // 2
+        if xt.dim() == 5:                                  # [B,T,C,H,W] -> [T,B,C,H,W]
+            xs = xt.transpose(0, 1).contiguous()
+            Tn, Bn = xs.shape[:2]
+            y = bn(F.conv2d(xs.flatten(0, 1), t(w0), stride=stem_stride, padding=pad0),
+                   P["stem"]["bn"])
+            h = lif(y.view(Tn, Bn, *y.shape[1:]))
+        else:
+            y = bn(F.conv2d(xt, t(w0), stride=stem_stride, padding=pad0), P["stem"]["bn"])
+            h = lif(y.unsqueeze(0).repeat(T, 1, 1, 1, 1))
         trace["stem"] = h
+        if maxpool:
+            Tn, Bn = h.shape[:2]
+            h = F.max_pool2d(h.flatten(0, 1), 3, 2, 1)
+            h = h.view(Tn, Bn, *h.shape[1:])
+            trace["maxpool"] = h
         for i, blk in enumerate(P["blocks"]):
             ident = h
             o = lif(seq_conv_bn(h, blk["w1"], blk["bn1"], blk["stride"], 1))

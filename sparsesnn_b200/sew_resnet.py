@@ -22,6 +22,7 @@ import torch
 
 from . import runtime as rt
 from .layer import SparseConvBNLIF, fold_bn
+from .netplan import CONV, HEAD, INPUT, LOGITS, MAXPOOL, STEM, Node, PlanModel, glue_desc, pool_out
 from .pruning import prune_conv_2_4
 
 STAGES = (64, 128, 256, 512)
@@ -35,19 +36,31 @@ def _bn_params(rng, f):
             "var": rng.uniform(0.5, 1.5, f).astype(np.float32)}
 
 
-def init_params(seed=0, num_classes=100, in_channels=3, stem_channels=64):
-    """Random-init parameters of the benchmark configuration.
+# Kaiming-normal (fan-in, ReLU gain) scaled by 1/sqrt(E[x^2]) of the layer's
+# input, so that a random-weight network keeps firing through every stage:
+# spike inputs firing at about 11% (E[x^2] = 1/9, gain 3); the stem sees
+# N(0,1) images (gain 1) or event frames of density p (gain 1/sqrt(p)).
+SPIKE_GAIN = 3.0
 
-    Kaiming-normal convs (fan_out, relu gain, as ``models/sewresnet.py:153-156``),
-    BN gamma~U(.5,1.5), beta~N(0,.1), mean~N(0,.1), var~U(.5,1.5); every conv
-    except the stem 2:4-pruned along C_in; nn.Linear-style uniform head.
+
+def init_params(seed=0, num_classes=100, in_channels=3, stem_channels=64, stem_kernel=3,
+                input_moment=1.0):
+    """Random-init parameters of the benchmark configuration (``stem_kernel``
+    7 for the ImageNet / DVS stem, ``models/sewresnet.py:140``;
+    ``input_moment`` = E[x^2] of the stem's input).
+
+    Kaiming-normal convs (fan-in, ReLU gain, scaled by 1/sqrt(E[x^2]) of the
+    layer's input, see ``SPIKE_GAIN``), BN gamma~U(.5,1.5), beta~N(0,.1),
+    mean~N(0,.1), var~U(.5,1.5); every conv except the stem 2:4-pruned along
+    C_in; nn.Linear-style uniform head.
     """
     rng = np.random.default_rng(seed)
 
-    def conv(f, c, k):
-        return (rng.standard_normal((f, c, k, k)) * np.sqrt(2.0 / (f * k * k))).astype(np.float32)
+    def conv(f, c, k, gain=SPIKE_GAIN):
+        return (rng.standard_normal((f, c, k, k)) * gain * np.sqrt(2.0 / (c * k * k))).astype(np.float32)
 
-    P = {"stem": {"w": conv(stem_channels, in_channels, 3), "bn": _bn_params(rng, stem_channels)},
+    P = {"stem": {"w": conv(stem_channels, in_channels, stem_kernel, 1.0 / np.sqrt(input_moment)),
+                  "bn": _bn_params(rng, stem_channels)},
          "blocks": []}
     inpl = stem_channels
     for si, (planes, nb) in enumerate(zip(STAGES, BLOCKS)):
@@ -305,3 +318,56 @@ def conv_layer_bytes(layer: SparseConvBNLIF, residual: bool, act_bytes: int = 2,
     w = rt.weight_bytes(d)
     out = n_out // 8 if binary_out else n_out * act_bytes
     return n_in * act_bytes + w + out + (n_out * act_bytes if residual else 0)
+
+
+class SEWResNet18DVS(PlanModel):
+    """SEW-ResNet-18 with the reference's ImageNet stem on event frames (the
+    DVS configuration): ``models/sewresnet.py:140-143,190-210`` --
+    conv1 7x7/2 (pad 3) + BN + LIF on every timestep's frame, MaxPool(3,2,1)
+    of the spikes, four SEW stages (64/128/256/512, ADD), avgpool + mean over
+    T + fc.
+
+    Input ``[T, B, C, H, W]`` fp32 (time-major; the reference's 5-D input is
+    ``[B, T, C, H, W]`` and is transposed first, ``:192-193``).
+    """
+
+    def __init__(self, params, *, T=16, batch=4, H=128, W=128, tau=2.0, v_threshold=1.0,
+                 device="cuda"):
+        st = params["stem"]
+        cout, cin, kh, kw = st["w"].shape
+        super().__init__(T=T, batch=batch, in_shape=(T, batch, cin, H, W),
+                         num_classes=params["fc_w"].shape[0], device=device)
+        dev = self.device
+        s, b = fold_bn(**st["bn"])
+        self.stem_desc = rt.make_desc(T=T, B=batch, Cin=cin, H=H, W=W, Cout=cout, KH=kh, KW=kw,
+                                      stride=2, pad=kh // 2, tau=tau, v_threshold=v_threshold)
+        sh, sw = (H + 2 * (kh // 2) - kh) // 2 + 1, (W + 2 * (kw // 2) - kw) // 2 + 1
+        a0 = self.buf((T * batch, sh, sw, cout))
+        self.add(Node(STEM, "stem", [INPUT], a0, self.stem_desc,
+                      (self.param(st["w"]), self.param(s), self.param(b)), (T, 0, 0, 0, 0)))
+        ph, pw = pool_out(sh, 3, 2, 1), pool_out(sw, 3, 2, 1)
+        p0 = self.buf((T * batch, ph, pw, cout))
+        self.add(Node(MAXPOOL, "maxpool", [a0], p0,
+                      glue_desc(T=T, B=batch, C=cout, H=sh, W=sw, neuron="none", k=3, stride=2,
+                                pad=1)))
+        kw_ = dict(T=T, B=batch, tau=tau, v_threshold=v_threshold, device=dev)
+        h, w_, x = ph, pw, p0
+        for i, blk in enumerate(params["blocks"]):
+            stride = blk["stride"]
+            l1 = SparseConvBNLIF(blk["w1"], *fold_bn(**blk["bn1"]), H=h, W=w_, stride=stride,
+                                 pad=1, **kw_)
+            o1 = self.add(Node(CONV, f"b{i}.conv1", [x], self.buf(l1.out_shape()), layer=l1))
+            ident = x
+            if "wd" in blk:
+                ds = SparseConvBNLIF(blk["wd"], *fold_bn(**blk["bnd"]), H=h, W=w_,
+                                     stride=stride, pad=0, **kw_)
+                ident = self.add(Node(CONV, f"b{i}.ds", [x], self.buf(ds.out_shape()), layer=ds))
+            l2 = SparseConvBNLIF(blk["w2"], *fold_bn(**blk["bn2"]), H=l1.OH, W=l1.OW, stride=1,
+                                 pad=1, **kw_)
+            x = self.add(Node(CONV, f"b{i}.conv2", [o1, ident], self.buf(l2.out_shape()), layer=l2))
+            h, w_ = l1.OH, l1.OW
+        c = params["blocks"][-1]["planes"]
+        self.feat_hw, self.feat_c = h * w_, c
+        self.add(Node(HEAD, "head", [x], LOGITS, None,
+                      (self.param(params["fc_w"]), self.param(params["fc_b"])),
+                      (T, batch, h * w_, c, self.num_classes)))

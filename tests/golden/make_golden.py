@@ -296,10 +296,54 @@ def model_case(ref, repo):
     print("wrote sew18 logits", logits.shape)
 
 
+def dvs_case(ref, repo):
+    """DVS SEW-ResNet-18 logits (7x7/2 stem on 2-channel 128x128 event frames,
+    MaxPool(3,2,1), T=16) from the reference model class as it is
+    (``sew_resnet18(in_channels=2)``, ``models/sewresnet.py:140-143,190-210``)."""
+    import torch
+    sys.path.insert(0, str(repo))
+    from oracle.sew_resnet import make_dvs_input, make_params
+    P = make_params(seed=0, num_classes=11, in_channels=2, stem_kernel=7, input_moment=0.05)
+    m = ref["sew_resnet18"](in_channels=2, neuron_type="lif", num_classes=11, T=16)
+    _load_sew_params(m, P)
+    x = make_dvs_input(seed=0, B=1, T=16)
+    with torch.no_grad():
+        logits = m(torch.from_numpy(x)).numpy()
+    np.savez_compressed(HERE / "sew18_dvs_logits.npz", x_bits=np.packbits(x.astype(np.uint8)),
+                        x_shape=np.array(x.shape), logits=logits)
+    print("wrote sew18 dvs logits", logits.shape)
+
+
+def _load_sew_params(m, P):
+    import torch
+    t = torch.from_numpy
+
+    def set_bn(bnm, p):
+        bnm.weight.data.copy_(t(p["gamma"])); bnm.bias.data.copy_(t(p["beta"]))
+        bnm.running_mean.copy_(t(p["mean"])); bnm.running_var.copy_(t(p["var"]))
+
+    m.conv1.weight.data.copy_(t(P["stem"]["w"])); set_bn(m.bn1, P["stem"]["bn"])
+    blocks = [b for layer in (m.layer1, m.layer2, m.layer3, m.layer4) for b in layer]
+    for blk, p in zip(blocks, P["blocks"]):
+        blk.conv1.module[0].weight.data.copy_(t(p["w1"])); set_bn(blk.conv1.module[1], p["bn1"])
+        blk.conv2.module[0].weight.data.copy_(t(p["w2"])); set_bn(blk.conv2.module[1], p["bn2"])
+        if "wd" in p:
+            ds = blk.downsample[0].module
+            ds[0].weight.data.copy_(t(p["wd"])); set_bn(ds[1], p["bnd"])
+    m.fc.weight.data.copy_(t(P["fc_w"])); m.fc.bias.data.copy_(t(P["fc_b"]))
+    m.eval()
+
+
+CASES = ("prune", "layers", "residual", "attention", "glue", "sew18", "dvs", "msresnet",
+         "spikformer")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="path of the SparseSNN reference checkout")
+    ap.add_argument("--only", nargs="*", choices=CASES, help="regenerate only these fixtures")
     a = ap.parse_args()
+    only = set(a.only or CASES)
     sys.path.insert(0, a.ref)
     from sparse.pruning import prune_2_4
     from models.neurons import MultiStepLIFNeuron, MultiStepIFNeuron
@@ -310,7 +354,29 @@ def main():
                sew_resnet18=sew_resnet18)
     import torch
     torch.set_num_threads(4)
-    prune_case(ref)
+    if "prune" in only:
+        prune_case(ref)
+    if "layers" in only:
+        layer_cases(ref)
+    if "residual" in only:
+        residual_case(ref, "c3addlif", mode="add_before", neuron="lif", T=4, B=2, C=64, F=128,
+                      H=8, W=8, k=3, seed=9)
+        residual_case(ref, "c1twon", mode="two_neuron", neuron="if", neuron2="lif", T=4, B=2,
+                      C=128, F=64, H=8, W=8, k=1, seed=10)
+    if "attention" in only:
+        attention_case(a.ref, "n64", T=4, B=2, N=64, heads=2, hd=32, p_spike=0.13, seed=11)
+        attention_case(a.ref, "n196", T=4, B=2, N=196, heads=2, hd=32, p_spike=0.09, seed=12)
+        attention_case(a.ref, "n100h64", T=3, B=2, N=100, heads=2, hd=64, p_spike=0.09, seed=13)
+    if "glue" in only:
+        glue_case(ref)
+    repo = HERE.parent.parent
+    if "sew18" in only:
+        model_case(ref, repo)
+    if "dvs" in only:
+        dvs_case(ref, repo)
+
+
+def layer_cases(ref):
     layer_case(ref, "c3s1", T=4, B=2, C=64, F=128, H=8, W=8, k=3, stride=1, pad=1, seed=1)
     layer_case(ref, "c3s2", T=2, B=2, C=64, F=128, H=8, W=8, k=3, stride=2, pad=1, seed=2)
     layer_case(ref, "c1s2", T=4, B=2, C=64, F=128, H=8, W=8, k=1, stride=2, pad=0, seed=3)
@@ -321,15 +387,6 @@ def main():
                seed=6)
     layer_case(ref, "lin", T=4, B=2, C=128, F=256, H=4, W=4, k=1, stride=1, pad=0, seed=8,
                linear=True)
-    residual_case(ref, "c3addlif", mode="add_before", neuron="lif", T=4, B=2, C=64, F=128,
-                  H=8, W=8, k=3, seed=9)
-    residual_case(ref, "c1twon", mode="two_neuron", neuron="if", neuron2="lif", T=4, B=2,
-                  C=128, F=64, H=8, W=8, k=1, seed=10)
-    attention_case(a.ref, "n64", T=4, B=2, N=64, heads=2, hd=32, p_spike=0.13, seed=11)
-    attention_case(a.ref, "n196", T=4, B=2, N=196, heads=2, hd=32, p_spike=0.09, seed=12)
-    attention_case(a.ref, "n100h64", T=3, B=2, N=100, heads=2, hd=64, p_spike=0.09, seed=13)
-    glue_case(ref)
-    model_case(ref, HERE.parent.parent)
 
 
 if __name__ == "__main__":
