@@ -334,6 +334,52 @@ def _load_sew_params(m, P):
     m.eval()
 
 
+def msresnet_case(ref, repo):
+    """MS-ResNet-34 logits from the reference model class (``ms_resnet34``,
+    ``models/msresnet.py:126-171,335``) with every ``MSNeuron`` replaced by the
+    reference's ``MultiStepLIFNeuron(tau=2, v_threshold=1)`` (the benchmark's
+    neuron), at 224x224, T=4."""
+    import torch
+    sys.path.insert(0, str(repo))
+    from oracle.ms_resnet import make_input, make_params
+    import models.msresnet as msr
+    P = make_params(seed=0)
+    m = msr.ms_resnet34(num_classes=1000, in_channels=3, T=4)
+    lif = lambda: ref["MultiStepLIFNeuron"](tau=2.0, v_threshold=1.0, v_reset=0.0)  # noqa: E731
+
+    def swap(mod):
+        for name, child in mod.named_children():
+            if isinstance(child, msr.MSNeuron):
+                setattr(mod, name, lif())
+            else:
+                swap(child)
+    swap(m)
+    t = torch.from_numpy
+
+    def set_bn(bnm, p):
+        bnm.weight.data.copy_(t(p["gamma"])); bnm.bias.data.copy_(t(p["beta"]))
+        bnm.running_mean.copy_(t(p["mean"])); bnm.running_var.copy_(t(p["var"]))
+
+    m.conv1.module[0].weight.data.copy_(t(P["stem"]["w"])); set_bn(m.conv1.module[1], P["stem"]["bn"])
+    blocks = [b for st in (m.conv2_x, m.conv3_x, m.conv4_x, m.conv5_x) for b in st]
+    assert len(blocks) == len(P["blocks"])
+    for blk, p in zip(blocks, P["blocks"]):
+        blk.conv_bn1.module[0].weight.data.copy_(t(p["w1"])); set_bn(blk.conv_bn1.module[1], p["bn1"])
+        blk.conv_bn2.module[0].weight.data.copy_(t(p["w2"])); set_bn(blk.conv_bn2.module[1], p["bn2"])
+        if "wsc" in p:
+            blk.shortcut.module[0].weight.data.copy_(t(p["wsc"]))
+            set_bn(blk.shortcut.module[1], p["bnsc"])
+    m.fc.weight.data.copy_(t(P["fc_w"])); m.fc.bias.data.copy_(t(P["fc_b"]))
+    m.eval()
+    x = make_input(seed=0, B=1)
+    with torch.no_grad():
+        logits = m(t(x)).numpy()
+    # the input is regenerated from its seed (oracle.ms_resnet.make_input)
+    np.savez_compressed(HERE / "msresnet34_logits.npz", seed=np.array(0), batch=np.array(1),
+                        logits=logits)
+    print("wrote msresnet34 logits", logits.shape)
+
+
 CASES = ("prune", "layers", "residual", "attention", "glue", "sew18", "dvs", "msresnet",
          "spikformer")
 
@@ -374,6 +420,8 @@ def main():
         model_case(ref, repo)
     if "dvs" in only:
         dvs_case(ref, repo)
+    if "msresnet" in only:
+        msresnet_case(ref, repo)
 
 
 def layer_cases(ref):

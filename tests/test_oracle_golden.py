@@ -162,3 +162,28 @@ def test_oracle_dvs_sew18_matches_reference_logits():
     np.testing.assert_allclose(logits, ref, rtol=0, atol=1e-5)
     assert trace["b7.sn1"].mean() > 0.01
     print("spike rates:", {k: round(float(v.mean()), 3) for k, v in trace.items()})
+
+
+def test_oracle_msresnet34_matches_reference_logits():
+    """MS-ResNet-34 port (LIF neurons, real-valued membrane shortcut) against
+    the reference model class with its neurons set to the same LIF; the
+    spikes keep firing through the last stage."""
+    from oracle.ms_resnet import forward_torch, make_input, make_params
+    m = np.load(GOLDEN / "msresnet34_logits.npz")
+    x = make_input(seed=int(m["seed"]), B=int(m["batch"]))
+    logits, trace = forward_torch(make_params(0), x, T=4, return_trace=True)
+    np.testing.assert_allclose(logits, m["logits"], rtol=0, atol=1e-5)
+    assert trace["b15.o1"].mean() > 0.05 and trace["sn_out"].mean() > 0.05
+
+
+def test_msresnet_weights_equal_oracle_weights():
+    from oracle.ms_resnet import make_params
+    from sparsesnn_b200.ms_resnet import init_params
+    a, b = init_params(seed=0), make_params(0)
+    assert np.array_equal(a["stem"]["w"], b["stem"]["w"])
+    for x, y in zip(a["blocks"], b["blocks"]):
+        for k in ("w1", "w2", "wsc"):
+            assert (k in x) == (k in y)
+            if k in x:
+                assert np.array_equal(x[k], y[k])
+    assert np.array_equal(a["fc_w"], b["fc_w"])
