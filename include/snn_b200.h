@@ -120,7 +120,10 @@ int snn_conv_variant(const snn_conv_desc* d);
 int snn_conv_out_shape(const snn_conv_desc* d, int32_t* OH, int32_t* OW);
 
 /* Bytes of the packed weight blob: compressed fp16 values [Cout_pad][K/2]
- * followed (256-byte aligned) by metadata words [Cout_pad/128][K/32][128]. */
+ * followed (256-byte aligned) by metadata words [Cout_pad/128][K/32][128],
+ * where K = KH*KW*Cin_pad (Cin rounded up to 64: a layer's last 64-channel
+ * block reads zeros past Cin; Cin must be a multiple of 8), doubled for
+ * SNN_FLAG_DENSE. */
 int snn_conv_weight_bytes(const snn_conv_desc* d, size_t* bytes);
 
 /* Host-side 2:4 packer.  `w` is the pruned weight in the reference's

@@ -88,10 +88,16 @@ def verify_2_4(w_fk: np.ndarray) -> bool:
     return bool(((g != 0).sum(axis=2) <= 2).all())
 
 
-def conv_weight_to_fk(w_fchw: np.ndarray) -> np.ndarray:
-    """``[F,C,KH,KW]`` -> ``[F, KH*KW*C]`` with ``k = (kh*KW+kw)*C + c``."""
-    f = w_fchw.shape[0]
-    return np.ascontiguousarray(np.transpose(w_fchw, (0, 2, 3, 1)).reshape(f, -1))
+def conv_weight_to_fk(w_fchw: np.ndarray, cin_pad: int | None = None) -> np.ndarray:
+    """``[F,C,KH,KW]`` -> ``[F, KH*KW*Cp]`` with ``k = (kh*KW+kw)*Cp + c``,
+    ``Cp`` = C rounded up to a multiple of 64 (one activation k-block) unless
+    ``cin_pad`` says otherwise; the padding columns are zero."""
+    f, c = w_fchw.shape[:2]
+    cp = cin_pad if cin_pad is not None else -(-c // 64) * 64
+    w = np.transpose(w_fchw, (0, 2, 3, 1))
+    if cp != c:
+        w = np.concatenate([w, np.zeros(w.shape[:3] + (cp - c,), w.dtype)], axis=3)
+    return np.ascontiguousarray(w.reshape(f, -1))
 
 
 def group_indices(w_fk: np.ndarray) -> np.ndarray:

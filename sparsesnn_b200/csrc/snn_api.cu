@@ -308,8 +308,11 @@ int check_desc(const snn_conv_desc* d, Geometry* g) {
   if (!d) return fail(SNN_E_INVALID, "null descriptor");
   if (d->T < 1 || d->B < 1 || d->H < 1 || d->W < 1 || d->Cout < 1 || d->KH < 1 || d->KW < 1)
     return fail(SNN_E_INVALID, "non-positive dimension");
-  if (d->Cin < 64 || d->Cin % 64)
-    return fail(SNN_E_INVALID, "Cin=%d must be a positive multiple of 64", d->Cin);
+  // Input channels in 64-channel k-blocks; a partial last block (Cin a
+  // multiple of 8, 16-byte pixel rows) reads zeros past Cin (TMA zero fill)
+  // and its weight columns are zero.
+  if (d->Cin < 8 || d->Cin % 8)
+    return fail(SNN_E_INVALID, "Cin=%d must be a positive multiple of 8", d->Cin);
   if (d->Cout % 8) return fail(SNN_E_INVALID, "Cout=%d must be a multiple of 8", d->Cout);
   if (d->stride != 1 && d->stride != 2) return fail(SNN_E_INVALID, "stride must be 1 or 2");
   if (d->pad < 0 || d->pad >= d->KH || d->pad >= d->KW) return fail(SNN_E_INVALID, "bad pad");
@@ -321,9 +324,9 @@ int check_desc(const snn_conv_desc* d, Geometry* g) {
   g->OH = (d->H + 2 * d->pad - d->KH) / d->stride + 1;
   g->OW = (d->W + 2 * d->pad - d->KW) / d->stride + 1;
   if (g->OH < 1 || g->OW < 1) return fail(SNN_E_INVALID, "empty output");
-  g->K = d->KH * d->KW * d->Cin;
+  g->cin_blocks = (d->Cin + snn::kKB - 1) / snn::kKB;
+  g->K = d->KH * d->KW * g->cin_blocks * snn::kKB;       // GEMM K (input channels padded)
   g->Fpad = (d->Cout + snn::kBM - 1) / snn::kBM * snn::kBM;
-  g->cin_blocks = d->Cin / snn::kKB;
   g->n_kb = d->KH * d->KW * g->cin_blocks;
   g->kdup = (d->flags & SNN_FLAG_DENSE) ? 2 : 1;
   g->Kw = g->K * g->kdup;
@@ -639,9 +642,10 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
       cuuint32_t box[5] = {static_cast<cuuint32_t>(snn::kKB), 4, static_cast<cuuint32_t>(d->T), 4, 6};
       if ((st = encode(&ph.tmap_b[0], 5, data, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)))
         return st;
-      // Weights as (Cin/2 el of one tap, Fpad rows, kh, kw): one box = taps (0..2, kw).
-      cuuint64_t wd[4] = {C / 2, static_cast<cuuint64_t>(g.Fpad), 3, 3};
-      cuuint64_t ws[3] = {static_cast<cuuint64_t>(g.K / 2) * 2, 3 * (C / 2) * 2, (C / 2) * 2};
+      // Weights as (Cpad/2 el of one tap, Fpad rows, kh, kw): one box = taps (0..2, kw).
+      const size_t Cp = static_cast<size_t>(g.cin_blocks) * snn::kKB;
+      cuuint64_t wd[4] = {Cp / 2, static_cast<cuuint64_t>(g.Fpad), 3, 3};
+      cuuint64_t ws[3] = {static_cast<cuuint64_t>(g.K / 2) * 2, 3 * (Cp / 2) * 2, (Cp / 2) * 2};
       cuuint32_t wb[4] = {snn::kKB / 2, snn::kBM, 3, 1};
       if ((st = encode(&ph.tmap_b[1], 4, weight, wd, ws, wb, CU_TENSOR_MAP_SWIZZLE_64B))) return st;
     } else {
@@ -656,9 +660,10 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
       cuuint32_t box[5] = {static_cast<cuuint32_t>(snn::kKB), 10, static_cast<cuuint32_t>(d->T), 10, 1};
       if ((st = encode(&ph.tmap_b[0], 5, data, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)))
         return st;
-      // weights as (Cin/2 el of one tap, Fpad rows, 9 taps): one box = 3 taps x 128 rows
-      cuuint64_t wd[3] = {C / 2, static_cast<cuuint64_t>(g.Fpad), 9};
-      cuuint64_t ws[2] = {static_cast<cuuint64_t>(g.K / 2) * 2, (C / 2) * 2};
+      // weights as (Cpad/2 el of one tap, Fpad rows, 9 taps): one box = 3 taps x 128 rows
+      const size_t Cp = static_cast<size_t>(g.cin_blocks) * snn::kKB;
+      cuuint64_t wd[3] = {Cp / 2, static_cast<cuuint64_t>(g.Fpad), 9};
+      cuuint64_t ws[2] = {static_cast<cuuint64_t>(g.K / 2) * 2, (Cp / 2) * 2};
       cuuint32_t wb[3] = {snn::kKB / 2, snn::kBM, 3};
       if ((st = encode(&ph.tmap_b[1], 3, weight, wd, ws, wb, CU_TENSOR_MAP_SWIZZLE_64B))) return st;
     }
@@ -843,17 +848,21 @@ int snn_pack_weight_24(const snn_conv_desc* d, const float* w, void* blob) {
     // Dense weights as two 2:4 halves per activation k-block kb: weight
     // k-block 2kb keeps positions (0,1) of every group of four input
     // channels, 2kb+1 keeps (2,3); both meet the same activations.
+    // Channels past Cin (the last k-block's padding) are zero weights with
+    // the same fixed pairs.
     for (int f = 0; f < F; ++f)
       for (int kh = 0; kh < KH; ++kh)
         for (int kw = 0; kw < KW; ++kw)
-          for (int c0 = 0; c0 < C; c0 += 4) {
+          for (int c0 = 0; c0 < g.cin_blocks * snn::kKB; c0 += 4) {
             const int kb = (kh * KW + kw) * g.cin_blocks + c0 / snn::kKB;
             const int gi = (c0 % snn::kKB) / 4;
             for (int h = 0; h < 2; ++h) {
               const int grp = (kb * 2 + h) * (snn::kKB / 4) + gi;
-              for (int u = 0; u < 2; ++u)
+              for (int u = 0; u < 2; ++u) {
+                const int c = c0 + 2 * h + u;
                 vals[static_cast<size_t>(f) * (K / 2) + 2 * grp + u] = __float2half_rn(
-                    w[((static_cast<size_t>(f) * C + c0 + 2 * h + u) * KH + kh) * KW + kw]);
+                    c < C ? w[((static_cast<size_t>(f) * C + c) * KH + kh) * KW + kw] : 0.0f);
+              }
               nib[static_cast<size_t>(f) * G + grp] = h ? (2 | (3 << 2)) : (0 | (1 << 2));
             }
           }
@@ -880,7 +889,7 @@ int snn_pack_weight_24(const snn_conv_desc* d, const float* w, void* blob) {
             if (!used) nz[cnt++] = i;
           }
           if (nz[0] > nz[1]) { int t = nz[0]; nz[0] = nz[1]; nz[1] = t; }
-          const int k = (kh * KW + kw) * C + c0;
+          const int k = (kh * KW + kw) * g.cin_blocks * snn::kKB + c0;   // padded GEMM K index
           const int grp = k / 4;
           vals[static_cast<size_t>(f) * (K / 2) + 2 * grp] = __float2half_rn(v4[nz[0]]);
           vals[static_cast<size_t>(f) * (K / 2) + 2 * grp + 1] = __float2half_rn(v4[nz[1]]);

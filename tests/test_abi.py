@@ -56,7 +56,7 @@ def test_residual_entry_points_validate_mode(_lib):
 
 
 @pytest.mark.parametrize("kw, msg", [
-    (dict(Cin=48), "multiple of 64"),
+    (dict(Cin=36), "multiple of 8"),
     (dict(stride=3), "stride"),
     (dict(H=9, stride=2), "even"),
     (dict(Cin=64 * 150), "exceeds"),

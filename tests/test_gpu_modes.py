@@ -215,3 +215,41 @@ def test_stem_without_neuron(cuda_device):
     got = from_nhwc(out.float().cpu().numpy(), T, B)
     for t in range(T):
         assert (np.abs(got[t] - z) <= 2.0 ** -10 * np.abs(z) + 1e-4).all()
+
+
+@pytest.mark.parametrize("cin, cout, hw, dense, variant", [
+    (48, 96, 16, True, 0),        # a Spikformer patch-splitting conv, 48 channels stored as 48
+    (96, 192, 14, True, 0),
+    (48, 64, 16, False, 1),       # four-timestep halo kernel, one partial input block
+    (96, 128, 16, False, 1),      # 128-channel halo kernel
+    (200, 256, 8, False, 2),      # streaming halo kernel, partial fourth block
+    (72, 128, 16, False, 0),      # general kernel (strided)
+])
+def test_partial_input_channel_block(cuda_device, cin, cout, hw, dense, variant):
+    """Cin a multiple of 8 but not of 64: the activations keep Cin channels
+    in HBM, the last 64-channel k-block reads TMA zero fill past Cin and its
+    weight columns are zero."""
+    import torch
+    from sparsesnn_b200 import runtime as rt
+    from sparsesnn_b200.layer import SparseConvBNLIF, fold_bn
+    rng = np.random.default_rng(cin + cout)
+    T, B = 4, 3
+    stride = 2 if (variant == 0 and not dense) else 1
+    x = (rng.random((T, B, cin, hw, hw)) < 0.25).astype(np.float32)
+    w = (rng.standard_normal((cout, cin, 3, 3)) * 3 * np.sqrt(2.0 / (cin * 9))).astype(np.float32)
+    if not dense:
+        from oracle.pack24 import prune_conv_weight
+        w = prune_conv_weight(w)
+    bn = _bn(rng, cout)
+    scale, bias = fold_bn(bn.gamma, bn.beta, bn.mean, bn.var)
+    layer = SparseConvBNLIF(w, scale, bias, T=T, B=B, H=hw, W=hw, stride=stride, pad=1, dense=dense)
+    assert rt.variant(layer.desc) == variant
+    st = torch.zeros(layer.state_shape(), dtype=torch.float32, device="cuda")
+    y = layer(torch.from_numpy(to_nhwc(x)).to("cuda", torch.float16), state=st)
+    torch.cuda.synchronize()
+    assert rt.device_error() == 0
+    ref = L.fused_layer_torch(x, w.astype(np.float16).astype(np.float32), bn, stride=stride, pad=1)
+    oh, ow = layer.OH, layer.OW
+    v = np.transpose(st.cpu().numpy().reshape(B, oh, ow, cout), (0, 3, 1, 2))
+    check_spikes(from_nhwc(y.float().cpu().numpy(), T, B), v, ref)
+    assert 0.01 < ref["spikes"].mean() < 0.9

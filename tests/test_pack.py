@@ -165,3 +165,30 @@ def test_dense_flag_doubles_weight_bytes_and_limits_k():
     big = rt.make_desc(T=1, B=1, Cin=512, H=8, W=8, Cout=128, KH=3, KW=3, flags=rt.SNN_FLAG_DENSE)
     with pytest.raises(rt.SnnError):
         rt.weight_bytes(big)                          # 2 * 4608 > 8192 weight columns
+
+
+@pytest.mark.parametrize("dense", [False, True], ids=["sparse", "dense"])
+@pytest.mark.parametrize("c", [8, 48, 96, 200])
+def test_partial_input_block_packs_zero_columns(c, dense):
+    """Cin not a multiple of 64: the GEMM K is padded to whole 64-channel
+    k-blocks, the padding columns carry zero weights (the activations there
+    are TMA zero fill), and the blob equals the numpy restatement of the
+    weight zero-padded to those channels."""
+    rng = np.random.default_rng(c)
+    w = rng.standard_normal((96, c, 3, 3)).astype(np.float32)
+    if not dense:
+        w = P.prune_conv_weight(w)
+    flags = rt.SNN_FLAG_DENSE if dense else 0
+    d = rt.make_desc(T=1, B=1, Cin=c, H=8, W=8, Cout=96, KH=3, KW=3, flags=flags)
+    cp = -(-c // 64) * 64
+    wp = np.zeros((96, cp, 3, 3), np.float32)
+    wp[:, :c] = w
+    dp = rt.make_desc(T=1, B=1, Cin=cp, H=8, W=8, Cout=96, KH=3, KW=3, flags=flags)
+    assert rt.weight_bytes(d) == rt.weight_bytes(dp)
+    assert np.array_equal(rt.pack_weight_24(d, w), rt.pack_weight_24(dp, wp))
+    if not dense:
+        vals, meta = split_blob(rt.pack_weight_24(d, w), 128, 9 * cp)
+        wfk = P.conv_weight_to_fk(w)
+        assert wfk.shape == (96, 9 * cp)
+        assert np.array_equal(meta, P.pack_meta(wfk))
+        assert np.array_equal(vals.view(np.uint16), P.pack_values(wfk).view(np.uint16))
