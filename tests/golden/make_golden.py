@@ -380,6 +380,67 @@ def msresnet_case(ref, repo):
     print("wrote msresnet34 logits", logits.shape)
 
 
+def spikformer_case(repo):
+    """Spikformer-8-384 logits from the reference's own modules
+    (``models/spikformer.py``): the ``SPS`` sub-modules (convs, BatchNorm2d,
+    ``MultiStepLIFNeuron``s, ``MaxPool2d``) run in the benchmark geometry --
+    a pool after each of the four stages, 224x224 -> 14x14 tokens -- then
+    eight reference ``Block``s (12 heads) and the mean / Linear head, at
+    T=4 on one 224x224 image."""
+    import torch
+    import torch.nn as nn
+    sys.path.insert(0, str(repo))
+    from oracle.spikformer import make_input, make_params
+    import models.spikformer as sf
+    P = make_params(seed=0)
+    E, T, heads = P["embed"], 4, P["heads"]
+    t = torch.from_numpy
+
+    def set_bn(bnm, p):
+        bnm.weight.data.copy_(t(p["gamma"])); bnm.bias.data.copy_(t(p["beta"]))
+        bnm.running_mean.copy_(t(p["mean"])); bnm.running_var.copy_(t(p["var"]))
+
+    def set_lin(lin, bnm, p):
+        lin.weight.data.copy_(t(p["w"])); lin.bias.data.copy_(t(p["b"])); set_bn(bnm, p["bn"])
+
+    sps = sf.SPS(img_size_h=224, img_size_w=224, patch_size=16, in_channels=3, embed_dims=E)
+    stages = [(sps.proj_conv, sps.proj_bn, sps.proj_lif), (sps.proj_conv1, sps.proj_bn1, sps.proj_lif1),
+              (sps.proj_conv2, sps.proj_bn2, sps.proj_lif2), (sps.proj_conv3, sps.proj_bn3, sps.proj_lif3)]
+    for (conv, bnm, _), p in zip(stages, P["sps"]):
+        conv.weight.data.copy_(t(p["w"])); set_bn(bnm, p["bn"])
+    sps.rpe_conv.weight.data.copy_(t(P["rpe"]["w"])); set_bn(sps.rpe_bn, P["rpe"]["bn"])
+    blocks = [sf.Block(dim=E, num_heads=heads, mlp_ratio=4) for _ in P["blocks"]]
+    for blk, p in zip(blocks, P["blocks"]):
+        a = blk.attn
+        set_lin(a.q_linear, a.q_bn, p["q"]); set_lin(a.k_linear, a.k_bn, p["k"])
+        set_lin(a.v_linear, a.v_bn, p["v"]); set_lin(a.proj_linear, a.proj_bn, p["proj"])
+        set_lin(blk.mlp.fc1_linear, blk.mlp.fc1_bn, p["fc1"])
+        set_lin(blk.mlp.fc2_linear, blk.mlp.fc2_bn, p["fc2"])
+    head = nn.Linear(E, P["fc_w"].shape[0])
+    head.weight.data.copy_(t(P["fc_w"])); head.bias.data.copy_(t(P["fc_b"]))
+    for mod in [sps, head] + blocks:
+        mod.eval()
+    x = make_input(seed=0, B=1)
+    with torch.no_grad():
+        xs = t(x).unsqueeze(0).repeat(T, 1, 1, 1, 1)
+        Tn, B, _, H, W = xs.shape
+        y = xs.flatten(0, 1)
+        pools = [sps.maxpool2, sps.maxpool2, sps.maxpool2, sps.maxpool3]
+        for (conv, bnm, lif), pool in zip(stages, pools):
+            y = bnm(conv(y)).reshape(Tn, B, -1, H, W)
+            y = pool(lif(y).flatten(0, 1))
+            H, W = H // 2, W // 2
+        x_feat = y.reshape(Tn, B, -1, H, W)
+        r = sps.rpe_lif(sps.rpe_bn(sps.rpe_conv(y)).reshape(Tn, B, -1, H, W))
+        xt = (r + x_feat).flatten(-2).transpose(-1, -2)
+        for blk in blocks:
+            xt = blk(xt)
+        logits = head(xt.mean(2).mean(0)).numpy()
+    np.savez_compressed(HERE / "spikformer_logits.npz", seed=np.array(0), batch=np.array(1),
+                        logits=logits)
+    print("wrote spikformer logits", logits.shape)
+
+
 CASES = ("prune", "layers", "residual", "attention", "glue", "sew18", "dvs", "msresnet",
          "spikformer")
 
@@ -422,6 +483,8 @@ def main():
         dvs_case(ref, repo)
     if "msresnet" in only:
         msresnet_case(ref, repo)
+    if "spikformer" in only:
+        spikformer_case(repo)
 
 
 def layer_cases(ref):

@@ -187,3 +187,27 @@ def test_msresnet_weights_equal_oracle_weights():
             if k in x:
                 assert np.array_equal(x[k], y[k])
     assert np.array_equal(a["fc_w"], b["fc_w"])
+
+
+def test_oracle_spikformer_matches_reference_modules():
+    """Spikformer-8-384 port (14x14 tokens, 12 heads) against the reference's
+    own SPS sub-modules and Block modules; every block keeps firing."""
+    from oracle.spikformer import forward_torch, make_input, make_params
+    m = np.load(GOLDEN / "spikformer_logits.npz")
+    x = make_input(seed=int(m["seed"]), B=int(m["batch"]))
+    logits, trace = forward_torch(make_params(0), x, T=4, return_trace=True)
+    np.testing.assert_allclose(logits, m["logits"], rtol=0, atol=2e-5)
+    for b in range(8):
+        assert 0.02 < trace[f"b{b}.attn"].mean() < 0.9 and trace[f"b{b}.h"].mean() > 0.02
+
+
+def test_spikformer_weights_equal_oracle_weights():
+    from oracle.spikformer import make_params
+    from sparsesnn_b200.spikformer import init_params
+    a, b = init_params(seed=0), make_params(0)
+    for x, y in zip(a["sps"] + [a["rpe"]], b["sps"] + [b["rpe"]]):
+        assert np.array_equal(x["w"], y["w"])
+    for x, y in zip(a["blocks"], b["blocks"]):
+        for k in ("q", "k", "v", "proj", "fc1", "fc2"):
+            assert np.array_equal(x[k]["w"], y[k]["w"]) and np.array_equal(x[k]["b"], y[k]["b"])
+    assert np.array_equal(a["fc_w"], b["fc_w"])
