@@ -57,6 +57,8 @@ def parse():
     ap.add_argument("--batches-per-step", type=int, default=100)
     ap.add_argument("--global-batch", type=int, default=BATCH)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the Spikformer / MS-ResNet / DVS configurations")
     ap.add_argument("--cpu-steps", type=int, default=5)
     return ap.parse_args()
 
@@ -295,7 +297,7 @@ def segment_times(model, stream, replays=50):
     neighbours, so the segments sum to a little more than the plain graph's
     step; shares are what this measures."""
     import torch
-    ops = model._ops()
+    ops = model.launches()
     evs = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(len(ops) + 1)]
     g = torch.cuda.CUDAGraph()
     side = torch.cuda.Stream(model.device)
@@ -320,6 +322,139 @@ def segment_times(model, stream, replays=50):
     del g
     per = {name: a / replays for (name, _), a in zip(ops, acc)}
     return per, sum(per.values())
+
+
+# The other configurations of the benchmark (one replica per GPU each), built
+# on the node-plan drivers; measured after the headline and reported under
+# "configs".  (name, per-GPU batch, T, builder, CPU-baseline forward)
+def _other_configs():
+    def dvs(dev, batch):
+        from sparsesnn_b200.sew_resnet import SEWResNet18DVS, init_params
+        P = init_params(seed=0, num_classes=11, in_channels=2, stem_kernel=7, input_moment=0.05)
+        m = SEWResNet18DVS(P, T=16, batch=batch, H=128, W=128, device=dev)
+        return m, P
+
+    def msr(dev, batch):
+        from sparsesnn_b200.ms_resnet import MSResNet34, init_params
+        P = init_params(seed=0)
+        return MSResNet34(P, T=4, batch=batch, H=224, W=224, device=dev), P
+
+    def spk(dev, batch):
+        from sparsesnn_b200.spikformer import Spikformer, init_params
+        P = init_params(seed=0)
+        return Spikformer(P, T=4, batch=batch, H=224, W=224, device=dev), P
+
+    def cpu_dvs(P, n):
+        from oracle.sew_resnet import forward_torch, make_dvs_input
+        x = make_dvs_input(seed=0, B=n, T=16)
+        return lambda: forward_torch(P, x, T=16, stem_stride=2, maxpool=True)
+
+    def cpu_msr(P, n):
+        from oracle.ms_resnet import forward_torch, make_input
+        x = make_input(seed=0, B=n)
+        return lambda: forward_torch(P, x, T=4)
+
+    def cpu_spk(P, n):
+        from oracle.spikformer import forward_torch, make_input
+        x = make_input(seed=0, B=n)
+        return lambda: forward_torch(P, x, T=4)
+
+    return [
+        ("spikformer_8_384", 32, 4, spk, cpu_spk,
+         "Spikformer-8-384: SPS with a stride-2 pool after each of 4 stages (224x224 -> 14x14 "
+         "tokens), 8 blocks, 12 heads, MLP ratio 4, T=4, 3x224x224, 1000 classes; Linear weights "
+         "2:4, SPS convs dense"),
+        ("msresnet34", 64, 4, msr, cpu_msr,
+         "MS-ResNet-34 (LIF -> conv -> BN, membrane shortcut; [3,4,6,3], 64/128/256/512), T=4, "
+         "3x224x224, 1000 classes; non-stem convs 2:4"),
+        ("dvs_sew_resnet18", 4, 16, dvs, cpu_dvs,
+         "DVS SEW-ResNet-18 (7x7/2 stem + MaxPool(3,2,1) on 2x128x128 Bernoulli(0.05) event "
+         "frames, ADD), T=16, 11 classes, 4 per GPU (batch 32 at 8 GPUs); non-stem convs 2:4"),
+    ]
+
+
+def measure_config(name, batch, T, build, cpu_fn, workload, *, dev, stream, world, rank,
+                   sparse_peak, dense_peak, forwards, cpu, threads):
+    """One configuration: device-resident forwards (graph replays, logits
+    gathered on a side stream at N > 1), the same through the public call
+    with host images, per-launch time inside the graph, the conv layers'
+    fraction of their tensor-core ceilings, and (rank 0, N = 1) a bounded CPU
+    sample of the reference path."""
+    import torch
+    from sparsesnn_b200 import dist as sd
+    from sparsesnn_b200.netplan import CONV, conv_flops
+    model, P = build(dev, batch)
+    g = torch.Generator().manual_seed(77 + rank)
+    if name == "dvs_sew_resnet18":
+        x_host = (torch.rand(model.in_shape, generator=g) < 0.05).float().pin_memory()
+    else:
+        x_host = torch.randn(model.in_shape, generator=g).pin_memory()
+    for k in range(2):
+        model.x_ins[k].copy_(x_host.to(dev))
+    model.run()
+    model.capture(warmup=2)
+    gath = sd.OverlappedGather(tuple(model.logits.shape), world, dev) if world > 1 else None
+
+    def fw(n, public=False):
+        for i in range(n):
+            if gath is not None:
+                gath.reuse(i & 1)
+            out = model(x_host) if public else model.replay(i & 1)
+            if gath is not None:
+                gath.submit(out, i & 1)
+        if gath is not None:
+            gath.drain()
+
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    res = {"workload": workload, "per_gpu_batch": batch, "global_batch": batch * world, "T": T}
+    for public in (False, True):
+        fw(3, public)
+        if world > 1:
+            torch.distributed.barrier(device_ids=[dev.index])
+        torch.cuda.synchronize()
+        e0.record(stream)
+        fw(forwards, public)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = sd.max_over_ranks(e0.elapsed_time(e1) / forwards, device=dev)
+        if public:
+            res["e2e"] = {"value": batch * world / (ms / 1000.0), "unit": UNIT,
+                          "path": "model(x_host): pinned H2D on a copy stream + graph replay",
+                          "h2d_bytes_per_forward": int(x_host.numel() * 4)}
+        else:
+            res.update(value=batch * world / (ms / 1000.0), unit=UNIT, ms_per_forward=ms)
+    per_launch, seg_total = segment_times(model, stream, replays=20)
+    scale_t = res["ms_per_forward"] / seg_total
+    busy, conv_ms, n_conv = 0.0, 0.0, 0
+    for n in model.nodes:
+        if n.kind != CONV:
+            continue
+        t_s = per_launch[n.name] * scale_t / 1000.0
+        peak = dense_peak if n.layer.dense else sparse_peak
+        busy += conv_flops(n.layer) / (peak * 1e12)
+        conv_ms += t_s * 1000.0
+        n_conv += 1
+    res["roofline"] = {"bound": "tensor", "frac": busy / (conv_ms / 1000.0), "unit": "TFLOP/s",
+                       "conv_launches": n_conv, "conv_ms_per_forward": conv_ms,
+                       "conv_share": conv_ms / res["ms_per_forward"],
+                       "note": "sum over fused conv launches of FLOPs / ceiling (2:4 sparse ceiling "
+                               "for 2:4 layers, dense bf16 peak for dense ones) over their time "
+                               "inside the graph"}
+    res["launches"] = {k: round(v * scale_t * 1000.0, 2) for k, v in per_launch.items()}
+    if cpu and rank == 0 and world == 1:
+        import time
+        torch.set_num_threads(threads)
+        f = cpu_fn(P, 1)
+        f()
+        t0 = time.perf_counter()
+        f()
+        dt = time.perf_counter() - t0
+        res["cpu_baseline"] = {"value": 1.0 / dt, "unit": UNIT, "cores": threads, "kind": "port",
+                               "sample": "1 image x 1 forward (after one warm-up), torch CPU fp32 "
+                                         "port of the reference forward (oracle/)"}
+    del model
+    torch.cuda.empty_cache()
+    return res
 
 
 def run_ours(args, rank, world, local_rank):
@@ -553,6 +688,15 @@ def run_ours(args, rank, world, local_rank):
         cpu = {"value": ips, "unit": UNIT, "cores": threads, "kind": "port",
                "sample": f"{CPU_SAMPLE} images x {args.cpu_steps} forwards (after one warm-up), "
                          f"torch CPU fp32 port of the reference forward (oracle/sew_resnet.py)"}
+    others = {}
+    if not args.no_configs:
+        for name, batch, T, build, cpu_fn, workload in _other_configs():
+            others[name] = measure_config(
+                name, batch, T, build, cpu_fn, workload, dev=dev, stream=stream, world=world,
+                rank=rank, sparse_peak=sparse_peak, dense_peak=bf16_peak, forwards=20,
+                cpu=not args.no_cpu_baseline, threads=os.cpu_count() or 1)
+        if rt.device_error() != 0:
+            raise RuntimeError("a kernel reported a device error")
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
@@ -586,6 +730,7 @@ def run_ours(args, rank, world, local_rank):
                 "spikformer_linear": linear,
                 "spikformer_attention": attn,
                 "glue": glue,
+                "configs": others,
                 "clocks": dict(clk.summary(), window="timed region plus two steps of replays before it"),
                 "cpu_baseline": cpu}
         emit(line)

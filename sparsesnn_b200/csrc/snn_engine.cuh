@@ -20,13 +20,21 @@
 // All integers little-endian.  Node kinds and their fields:
 //   STEM        in0 = images (fp32 NCHW, Tin x B), out; desc; p0 = w, p1 = scale,
 //               p2 = bias (fp32); i[0] = Tin
-//   CONV        in0 = data, in1 = residual or none, out; desc (flags 0: the
-//               membrane starts at zero every forward); p0 = packed weights,
-//               p1 = scale, p2 = bias
+//   CONV        in0 = data, in1 = residual or none, out; desc (no membrane
+//               flags: the membrane starts at zero every forward); p0 = packed
+//               weights, p1 = scale, p2 = bias
 //   HEAD        in0 = features, out = logits; p0 = fc_w, p1 = fc_b;
 //               i[0..4] = T, B, HW, C, NC
 //   ADD_LIF     in0, in1, out; desc
-//   MAXPOOL_LIF in0, out; desc (KH = window, stride, pad)
+//   MAXPOOL_LIF in0, out; desc (KH = window, stride, pad; neuron NONE: the
+//               plain max pool)
+//   LIF         in0, out; desc (the neuron of one input)
+//   ATTN        in0 = q, in1 = k, i[0] = v, out; desc T, B, tau,
+//               v_threshold, v_reset, tau2 = the attention scale;
+//               i[1..3] = tokens, heads, head_dim
+// Stem nodes may have no neuron (fp16 BN output); conv nodes may carry the
+// dense-weight and general-kernel flags and the fp16 BN output, but never
+// the membrane flags (every forward starts from zero).
 #pragma once
 #include <cstdio>
 #include <vector>
@@ -34,9 +42,10 @@
 namespace {
 
 constexpr char kEngineMagic[4] = {'S', 'N', 'N', 'E'};
-constexpr uint32_t kEngineVersion = 1;
+constexpr uint32_t kEngineVersion = 2;
 constexpr uint32_t kNoTensor = 0xffffffffu;
-enum EngineOp : uint32_t { kOpStem = 1, kOpConv = 2, kOpHead = 3, kOpAddLif = 4, kOpMaxPoolLif = 5 };
+enum EngineOp : uint32_t { kOpStem = 1, kOpConv = 2, kOpHead = 3, kOpAddLif = 4, kOpMaxPoolLif = 5,
+                           kOpLif = 6, kOpAttn = 7 };
 
 struct SnnEngineHeader {
   char magic[4];
@@ -135,7 +144,8 @@ int parse_engine_file(const char* path, SnnEngineHeader* h, std::vector<SnnEngin
         if (in_bytes < uint64_t(d.T) * d.B * d.H * d.W * d.Cin * 2 || out_bytes < out_need ||
             (nd.in1 != kNoTensor && (*tensors)[nd.in1].bytes < uint64_t(d.T) * d.B * oh * ow * d.Cout * 2) ||
             !off_ok(nd.p0, wbytes) || !off_ok(nd.p1, uint64_t(d.Cout) * 4) ||
-            !off_ok(nd.p2, uint64_t(d.Cout) * 4) || d.flags != 0 ||
+            !off_ok(nd.p2, uint64_t(d.Cout) * 4) ||
+            (d.flags & ~(SNN_FLAG_FORCE_GENERIC | SNN_FLAG_DENSE)) != 0 ||
             d.res_mode == SNN_RES_TWO_NEURON || (d.res_mode == SNN_RES_ADD_BEFORE && nd.in1 == kNoTensor))
           return fail(SNN_E_INVALID, "engine node %u (conv): sizes, offsets or flags out of range", n);
         break;
@@ -148,6 +158,19 @@ int parse_engine_file(const char* path, SnnEngineHeader* h, std::vector<SnnEngin
           return fail(SNN_E_INVALID, "engine node %u (head): sizes or offsets out of range", n);
         break;
       }
+      case kOpAttn: {
+        const int32_t N = nd.i[1], heads = nd.i[2], hd = nd.i[3];
+        const uint32_t v_id = static_cast<uint32_t>(nd.i[0]);
+        if (d.T < 1 || d.B < 1 || N < 1 || heads < 1 || (hd != 32 && hd != 64) || d.flags != 0 ||
+            nd.in1 == kNoTensor || !tid_ok(v_id))
+          return fail(SNN_E_INVALID, "engine node %u (attention): bad shape, flags or tensor", n);
+        const uint64_t need = uint64_t(d.T) * d.B * N * heads * hd * 2;
+        if (in_bytes < need || out_bytes < need || (*tensors)[nd.in1].bytes < need ||
+            (*tensors)[v_id].bytes < need)
+          return fail(SNN_E_INVALID, "engine node %u (attention): sizes out of range", n);
+        break;
+      }
+      case kOpLif:
       case kOpAddLif:
       case kOpMaxPoolLif: {
         if (d.T < 1 || d.B < 1 || d.H < 1 || d.W < 1 || d.Cout < 1 || d.flags != 0)
@@ -229,6 +252,16 @@ int engine_node_loop(snn_engine* e, void* stream) {
       case kOpMaxPoolLif:
         st = snn_maxpool_lif_forward(&nd.desc, in0, nullptr, out, stream);
         break;
+      case kOpLif:
+        st = snn_lif_forward(&nd.desc, in0, nullptr, out, stream);
+        break;
+      case kOpAttn: {
+        const snn_conv_desc& d = nd.desc;
+        st = snn_spikformer_attn_forward(d.T, d.B, nd.i[1], nd.i[2], nd.i[3], d.tau2, d.tau,
+                                         d.v_threshold, d.v_reset, 0, in0, in1,
+                                         e->tptr[static_cast<uint32_t>(nd.i[0])], nullptr, out, stream);
+        break;
+      }
       default:
         st = fail(SNN_E_INVALID, "engine node %u: unknown kind", n);
     }

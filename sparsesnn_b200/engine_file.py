@@ -1,10 +1,11 @@
 """Engine files for the native executor (``snn_engine_*`` in libsnnb200).
 
-``save_engine(model, path)`` writes a :class:`~sparsesnn_b200.sew_resnet.SEWResNet18`
-replica as an engine file: the fused nodes of one forward in execution order
-(stem, per block conv1 / downsample / conv2 with the SEW residual, head),
-the byte size of every activation, and one blob with the packed 2:4 weights,
-folded BN scale/bias, stem and FC parameters.  ``Engine`` loads such a file
+``save_engine(model, path)`` writes a model replica as an engine file: the
+fused nodes of one forward in execution order (for SEW-ResNet-18: stem, per
+block conv1 / downsample / conv2 with the SEW residual, head; for the
+node-plan models -- DVS SEW-ResNet-18, MS-ResNet-34, Spikformer -- their
+plan), the byte size of every activation, and one blob with the packed 2:4
+weights, folded BN scale/bias, stem and FC parameters.  ``Engine`` loads such a file
 through the C-ABI and runs it without Python in the loop (the node loop and
 its CUDA graph are C++).
 
@@ -23,9 +24,9 @@ import numpy as np
 from . import runtime as rt
 
 MAGIC = b"SNNE"
-VERSION = 1
+VERSION = 2
 NO_TENSOR = 0xFFFFFFFF
-OP_STEM, OP_CONV, OP_HEAD, OP_ADD_LIF, OP_MAXPOOL_LIF = 1, 2, 3, 4, 5
+OP_STEM, OP_CONV, OP_HEAD, OP_ADD_LIF, OP_MAXPOOL_LIF, OP_LIF, OP_ATTN = 1, 2, 3, 4, 5, 6, 7
 F16, F32 = 0, 1
 _ALIGN = 256
 
@@ -65,12 +66,77 @@ class _Writer:
 
 def _conv_desc(layer):
     d = rt.SnnConvDesc.from_buffer_copy(bytes(layer.desc))
-    d.flags = 0                    # the membrane starts at zero every forward
+    # the layer's own flags (dense weights, general kernel), no membrane
+    # flags: the membrane starts at zero every forward
+    d.flags = layer.base_flags
     return d
 
 
+def save_plan(model, path):
+    """Write a node-plan model (``netplan.PlanModel``: SEW-ResNet-18 DVS,
+    MS-ResNet-34, Spikformer) as an engine file: one engine tensor per device
+    buffer (views of a buffer map to it), the nodes in plan order."""
+    from . import netplan as npl
+    w = _Writer()
+    T, B = model.T, model.B
+    ids = {}
+
+    def tid(x):
+        if x is npl.INPUT:
+            key = ("input",)
+            if key not in ids:
+                ids[key] = w.tensor(model.x_ins[0].numel() * 4, F32)
+            return ids[key]
+        if x is npl.LOGITS:
+            key = ("logits",)
+            if key not in ids:
+                ids[key] = w.tensor(model.logits.numel() * 4, F32)
+            return ids[key]
+        st = x.untyped_storage()
+        if x.storage_offset() != 0 or x.numel() * x.element_size() != st.nbytes():
+            raise ValueError("plan tensors must be whole buffers (or views of whole buffers)")
+        key = st.data_ptr()
+        if key not in ids:
+            ids[key] = w.tensor(st.nbytes(), F32 if x.dtype.is_floating_point and x.element_size() == 4
+                                else F16)
+        return ids[key]
+
+    P = lambda t: w.param(t.detach().cpu().numpy())  # noqa: E731
+    kinds = {npl.STEM: OP_STEM, npl.CONV: OP_CONV, npl.HEAD: OP_HEAD, npl.ADD_LIF: OP_ADD_LIF,
+             npl.MAXPOOL: OP_MAXPOOL_LIF, npl.LIF: OP_LIF, npl.ATTN: OP_ATTN}
+    for n in model.nodes:
+        ins = [tid(x) for x in n.ins]
+        out = tid(n.out)
+        in1 = ins[1] if len(ins) > 1 else NO_TENSOR
+        if n.kind == npl.CONV:
+            L = n.layer
+            w.node(OP_CONV, ins[0], in1, out, _conv_desc(L),
+                   (P(L.weight_blob), P(L.bn_scale), P(L.bn_bias), 0))
+        elif n.kind == npl.STEM:
+            w.node(OP_STEM, ins[0], NO_TENSOR, out, n.desc, tuple(P(t) for t in n.params) + (0,),
+                   n.ints)
+        elif n.kind == npl.HEAD:
+            w.node(OP_HEAD, ins[0], NO_TENSOR, out, None, (P(n.params[0]), P(n.params[1]), 0, 0),
+                   n.ints)
+        elif n.kind == npl.ATTN:
+            d = rt.SnnConvDesc.from_buffer_copy(bytes(n.desc))
+            d.flags = 0
+            d.tau2 = n.attn["scale"]
+            w.node(OP_ATTN, ins[0], ins[1], out, d,
+                   i=(ins[2], n.attn["N"], n.attn["heads"], n.attn["head_dim"], 0))
+        else:
+            d = rt.SnnConvDesc.from_buffer_copy(bytes(n.desc))
+            d.flags = 0
+            w.node(kinds[n.kind], ins[0], in1, out, d)
+    w.write(path, tid(npl.INPUT), tid(npl.LOGITS), T, B)
+    return path
+
+
 def save_engine(model, path):
-    """Write ``model`` (a SEWResNet18 replica) as an engine file at ``path``."""
+    """Write ``model`` as an engine file at ``path`` (a SEWResNet18 replica,
+    or any node-plan model)."""
+    if hasattr(model, "nodes"):
+        return save_plan(model, path)
     w = _Writer()
     T, B = model.T, model.B
     cin = model.x_in.shape[1]

@@ -232,3 +232,44 @@ def test_engine_glue_nodes_match_direct_calls(cuda_device, tmp_path):
         assert torch.equal(out, ref)
     assert rt.device_error() == 0
     eng.close()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("which", ["dvs", "msresnet", "spikformer"])
+def test_plan_models_through_the_engine(cuda_device, tmp_path, which):
+    """An engine file saved from a node-plan model (plain max pool, single-input
+    LIF, fp16 BN output with the membrane shortcut, dense weights, attention
+    nodes) gives the Python driver's logits exactly, eagerly and replayed from
+    its CUDA graph, two calls in a row."""
+    import torch
+    rng = np.random.default_rng(11)
+    if which == "dvs":
+        from sparsesnn_b200.sew_resnet import SEWResNet18DVS, init_params
+        model = SEWResNet18DVS(init_params(seed=1, num_classes=11, in_channels=2, stem_kernel=7,
+                                           input_moment=0.05), T=8, batch=1, H=64, W=64)
+        xs = [(rng.random((8, 1, 2, 64, 64)) < 0.05).astype(np.float32) for _ in range(2)]
+    elif which == "msresnet":
+        from sparsesnn_b200.ms_resnet import MSResNet34, init_params
+        model = MSResNet34(init_params(seed=1, num_classes=10), T=4, batch=2, H=64, W=64)
+        xs = [rng.standard_normal((2, 3, 64, 64)).astype(np.float32) for _ in range(2)]
+    else:
+        from sparsesnn_b200.spikformer import Spikformer, init_params
+        model = Spikformer(init_params(seed=1, depth=2, num_classes=10), T=4, batch=2, H=64, W=64)
+        xs = [rng.standard_normal((2, 3, 64, 64)).astype(np.float32) for _ in range(2)]
+    imgs = [torch.from_numpy(x).pin_memory() for x in xs]
+    ref = [model(x).clone() for x in imgs]
+    torch.cuda.synchronize()
+    path = ef.save_engine(model, tmp_path / f"{which}.snne")
+    assert ef.check_file(path)[0] == len(model.nodes)
+    eng = ef.Engine(path)
+    s = torch.cuda.Stream()
+    out = torch.empty_like(ref[0])
+    for graph in (False, True):
+        if graph:
+            eng.capture(s)
+        for x, r in zip(imgs, ref):
+            eng.run(x.data_ptr(), out.data_ptr(), s)
+            s.synchronize()
+            assert torch.equal(out, r), (which, graph)
+    assert rt.device_error() == 0
+    eng.close()
