@@ -359,7 +359,14 @@ int encode(CUtensorMap* map, int rank, const void* base, const cuuint64_t* dims,
 // a run of one output row, whole rows of one image, or whole images.
 void general_tile(const Geometry& g, int B, int* tw, int* th, int* tn) {
   if (g.OW >= snn::kBN) { *tw = snn::kBN; *th = 1; *tn = 1; }
-  else if (g.OH * g.OW >= snn::kBN) { *tw = g.OW; *th = snn::kBN / g.OW; *tn = 1; }
+  else if (snn::kBN % g.OW == 0 && g.OH * g.OW >= snn::kBN) { *tw = g.OW; *th = snn::kBN / g.OW; *tn = 1; }
+  else if (g.OW > 4 && g.OH > 4) {
+    // Other widths (56, 28, 14, 7, ...): 8 x 8-pixel tiles, whose 64-pixel
+    // boxes let the four-timestep N = 256 MMAs run (ragged edges read zero
+    // fill and are not stored) -- measured faster than whole-row tiles of
+    // fewer than 64 pixels, which fall back to per-timestep N = 64 MMAs.
+    *tw = 8; *th = 8; *tn = 1;
+  }
   else { *tw = g.OW; *th = g.OH; *tn = std::max(1, std::min(B, snn::kBN / (g.OH * g.OW))); }
 }
 
