@@ -170,6 +170,15 @@ StemKernel stem_tc_fn(int cin, int mode) {
 }
 constexpr int kStemTcSmemMax = 96 * 1024;
 
+StemKernel stem_tcg_fn(int mode) {
+  switch (mode) {
+    case snn::kModeLifHalf: return snn::stem_tc_gen_kernel<snn::kModeLifHalf>;
+    case snn::kModeLifDiv: return snn::stem_tc_gen_kernel<snn::kModeLifDiv>;
+    case snn::kModeIf: return snn::stem_tc_gen_kernel<snn::kModeIf>;
+    default: return snn::stem_tc_gen_kernel<snn::kModeNone>;
+  }
+}
+
 constexpr int kSmemLimit = 232448;          // opt-in dynamic smem per block on sm_100
 
 // Launches with programmatic stream serialization: the kernel may be
@@ -284,6 +293,11 @@ int ensure_init() {
         return g_init_status = fail(SNN_E_CUDA, "smem attribute: %s", cudaGetErrorString(e));
     }
   }
+  for (int mode = 0; mode < 4 && e == cudaSuccess; ++mode)
+    e = cudaFuncSetAttribute(stem_tcg_fn(mode), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             snn::stem_tcg_smem_bytes(snn::kStemGMaxK / 32));
+  if (e != cudaSuccess)
+    return g_init_status = fail(SNN_E_CUDA, "smem attribute: %s", cudaGetErrorString(e));
   e = cudaFuncSetAttribute(snn::spikformer_attn_lif_kernel<32>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, snn::AttnCfg<32>::kSmemBytes);
   for (int mode = 0; mode < 3 && e == cudaSuccess; ++mode)
@@ -1007,6 +1021,29 @@ int snn_stem_forward(const snn_conv_desc* d, int32_t Tin, const float* x, const 
         p.tma_out = 1;
       cudaError_t e = launch_pdl(stem_tc_fn(d->Cin, mode), dim3(static_cast<unsigned>(nblk)),
                                  dim3(snn::kStemThreads), smem, stream, p);
+      if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));
+      return SNN_OK;
+    }
+  }
+  // General tensor-core stem: any window and stride, per-timestep or
+  // repeated input, up to 64 channels and K = Cin*KH*KW <= 256.
+  const int Kst = d->Cin * d->KH * d->KW;
+  const int TWst = std::min(OW, 128), Rst = 128 / TWst;
+  const long long stage_bytes = 4LL * d->Cin * ((Rst - 1) * d->stride + d->KH) *
+                                ((TWst - 1) * d->stride + d->KW);
+  if (d->Cout <= 64 && Kst <= snn::kStemGMaxK && stage_bytes <= snn::kStemGMaxStage) {
+    const int mode = d->neuron == SNN_NEURON_NONE ? snn::kModeNone
+                     : d->neuron == SNN_NEURON_IF ? snn::kModeIf
+                     : d->tau == 2.0f ? snn::kModeLifHalf : snn::kModeLifDiv;
+    const int nk = (Kst + 31) / 32;
+    const size_t smem = static_cast<size_t>(snn::stem_tcg_smem_bytes(nk));
+    const long long n_tiles = static_cast<long long>(d->B) * ((OH + Rst - 1) / Rst) *
+                              ((OW + TWst - 1) / TWst);
+    const int per_sm = smem <= 110 * 1024 ? 2 : 1;
+    const long long nblk = std::max<long long>(1, std::min<long long>(n_tiles, 1LL * per_sm * g_num_sms));
+    if ((reinterpret_cast<uintptr_t>(out) & 15) == 0) {
+      cudaError_t e = launch_pdl(stem_tcg_fn(mode), dim3(static_cast<unsigned>(nblk)),
+                                 dim3(snn::kStemGThreads), smem, stream, p);
       if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));
       return SNN_OK;
     }

@@ -350,6 +350,226 @@ stem_tc_kernel(const __grid_constant__ StemParams p) {
   }
 }
 
+// ------------------------------------------------ general tensor-core stem
+// Dense stem of any kernel size and stride (K = Cin*KH*KW <= 192), up to 64
+// output channels, input repeated over T (Tin = 1: one GEMM, the neuron runs
+// T steps on it) or one frame per timestep (Tin = T: one GEMM per timestep,
+// the membrane carried in registers), with a LIF/IF neuron or none (fp16 BN
+// output).  A tile is R rows x TW columns of one image's output (TW =
+// min(OW, 128), R = 128 / TW): the input window under it (every channel,
+// (R-1)*stride + KH rows, (TW-1)*stride + KW columns) is staged in shared
+// memory with coalesced loads, and the im2col k-tiles are built from there.
+// GEMM: D[px][co] = im2col(x)[px][k] * w[co][k], M = 128 (TMEM lanes =
+// pixels), N = 64, K in 32-wide fp32 k-tiles, 3xTF32 as in stem_tc_kernel
+// (fp32-level accuracy).  The weights' hi/lo k-tiles stay resident; the
+// im2col k-tiles are built by all 256 threads (a pixel's 32 columns split
+// between two threads) into two alternating buffers, so a k-tile's build
+// overlaps the previous one's MMAs.  Epilogue: thread = (pixel, 32 of the 64
+// channels), 16-byte stores of the pixel's channels.
+constexpr int kStemGThreads = 256;
+constexpr int kStemGMaxK = 192;
+constexpr int kStemGMaxStage = 40 * 1024;     // bytes of the staged input window
+__host__ __device__ constexpr int stem_tcg_smem_bytes(int nk) {
+  return 2 * nk * 8192 + 4 * 16384 + kStemGMaxStage + kStemGMaxK * 8 + 2 * 64 * 4 + 64 + 1024;
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kStemGThreads, 1)
+stem_tc_gen_kernel(const __grid_constant__ StemParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int K = p.Cin * p.KH * p.KW;
+  const int nk = (K + 31) / 32;
+  const int TW = min(p.OW, 128), R = 128 / TW;
+  const int IR = (R - 1) * p.stride + p.KH, IC = (TW - 1) * p.stride + p.KW;
+  uint8_t* sBh = smem;                                   // [nk][64 ch][32] fp32, 128B swizzle
+  uint8_t* sBl = sBh + nk * 8192;
+  uint8_t* sA = sBl + nk * 8192;                         // [2 buf][hi, lo][128 px][32]
+  float* xs = reinterpret_cast<float*>(sA + 4 * 16384);  // [Cin][IR][IC] staged input
+  int* kofs = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(xs) + kStemGMaxStage);
+  float* sc = reinterpret_cast<float*>(kofs + kStemGMaxK);
+  float* bi = sc + 64;
+  uint64_t* mma_done = reinterpret_cast<uint64_t*>(bi + 64);   // [2], per A buffer
+  uint64_t* acc_full = mma_done + 2;
+  uint64_t* drain = acc_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  const int tid = threadIdx.x, warp = tid / 32;
+  const int px = tid & 127, half = tid >> 7;             // pixel; column / channel half
+  const int pr = px / TW, pc = px - (px / TW) * TW;      // pixel's row and column in the tile
+
+  if (tid == 0) {
+    mbar_init(&mma_done[0], 1); mbar_init(&mma_done[1], 1);
+    mbar_init(acc_full, 1); mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) { tmem_alloc(tmem_slot, 64); tmem_relinquish(); }
+  // Resident weights (constant data): B[co][k] hi/lo, zero past Cout / K.
+  for (int i = tid; i < nk * 64 * 32; i += kStemGThreads) {
+    const int kt = i / 2048, rem = i - kt * 2048, co = rem >> 5, kk = rem & 31;
+    const int k = kt * 32 + kk;
+    const float wv = (co < p.Cout && k < K) ? __ldg(p.w + static_cast<size_t>(co) * K + k) : 0.f;
+    const float hi = to_tf32(wv);
+    *reinterpret_cast<float*>(sBh + kt * 8192 + sw128_f32(co, kk)) = hi;
+    *reinterpret_cast<float*>(sBl + kt * 8192 + sw128_f32(co, kk)) = wv - hi;
+  }
+  // Column k = (ci*KH + kh)*KW + kw (the [Cout][Cin][KH][KW] weight order)
+  // reads staged element kofs[k] + (pixel row * stride) * IC + pixel col * stride.
+  for (int k = tid; k < nk * 32; k += kStemGThreads) {
+    if (k < K) {
+      const int ci = k / (p.KH * p.KW), r = k - ci * p.KH * p.KW, kh = r / p.KW, kw = r - kh * p.KW;
+      kofs[k] = (ci * IR + kh) * IC + kw;
+    } else {
+      kofs[k] = -1;                                      // padding column: zero
+    }
+  }
+  if (tid < 64) {
+    const bool cv = tid < p.Cout;
+    // BN pre-scaled by 1/2 for the tau = 2 LIF step, as in the conv epilogues.
+    sc[tid] = cv ? (MODE == kModeLifHalf ? p.scale[tid] * 0.5f : p.scale[tid]) : 0.f;
+    bi[tid] = cv ? (MODE == kModeLifHalf ? p.bias[tid] * 0.5f : p.bias[tid]) : 0.f;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_launch_dependents();
+  pdl_wait();                                            // input and output belong to the stream
+
+  const long long P = static_cast<long long>(p.B) * p.OH * p.OW;
+  const int tiles_w = (p.OW + TW - 1) / TW, tiles_h = (p.OH + R - 1) / R;
+  const long long n_tiles = static_cast<long long>(p.B) * tiles_h * tiles_w;
+  const int n_gemm = p.Tin > 1 ? p.T : 1;
+  const int HW = p.H * p.W;
+  const int nstage = p.Cin * IR * IC;
+  const uint32_t idesc = idesc_tf32(128, 64);
+  const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+  const int pofs = pr * p.stride * IC + pc * p.stride;   // this pixel's window origin in xs
+  uint32_t use[2] = {0, 0};                              // uses of each A buffer so far
+  uint32_t acc_uses = 0;
+  int issued = 0;                                        // MMAs issued by thread 0
+  bool ok = true;
+  for (long long tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
+    const int twi = static_cast<int>(tile % tiles_w);
+    const long long rest = tile / tiles_w;
+    const int thi = static_cast<int>(rest % tiles_h);
+    const int b = static_cast<int>(rest / tiles_h);
+    const int oh0 = thi * R, ow0 = twi * TW;
+    const int oh = oh0 + pr, ow = ow0 + pc;
+    const bool pv = pr < R && oh < p.OH && ow < p.OW;
+    const long long pix = (static_cast<long long>(b) * p.OH + oh) * p.OW + ow;
+    const int ih0 = oh0 * p.stride - p.pad, iw0 = ow0 * p.stride - p.pad;
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = 0.f;
+    for (int g = 0; g < n_gemm && ok; ++g) {
+      // Stage the input window of frame g (zero outside the image).  The
+      // previous GEMM's builds have all passed a barrier since they read xs.
+      const float* xin = p.x + (static_cast<size_t>(g) * p.B + b) * static_cast<size_t>(p.Cin) * HW;
+      for (int i = tid; i < nstage; i += kStemGThreads) {
+        const int ci = i / (IR * IC), r = i - ci * IR * IC, rr = r / IC, cc = r - rr * IC;
+        const int ih = ih0 + rr, iw = iw0 + cc;
+        xs[i] = (ih >= 0 && ih < p.H && iw >= 0 && iw < p.W)
+                    ? __ldg(xin + static_cast<size_t>(ci) * HW + static_cast<size_t>(ih) * p.W + iw) : 0.f;
+      }
+      __syncthreads();
+      for (int kt = 0; kt < nk; ++kt) {
+        const int buf = (use[0] + use[1]) & 1;
+        if (use[buf] > 0) {                              // the MMAs that read this buffer are done
+          const bool okw = mbar_wait_bounded(&mma_done[buf], (use[buf] - 1) & 1, p.timeout);
+          if (!okw && p.err) atomicOr(p.err, kErrTimeoutEmpty);
+          if (!__syncthreads_and(okw)) { ok = false; break; }
+        }
+        uint8_t* ah = sA + buf * 32768;
+        uint8_t* al = ah + 16384;
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {                 // this thread's 16 columns, 4 at a time
+          float hi[4], lo[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int ko = kofs[kt * 32 + half * 16 + c4 * 4 + j];
+            const float xv = (pv && ko >= 0) ? xs[ko + pofs] : 0.f;
+            hi[j] = to_tf32(xv);
+            lo[j] = xv - hi[j];
+          }
+          const int chunk = half * 4 + c4;
+          const int off = px * 128 + ((chunk ^ (px & 7)) << 4);
+          *reinterpret_cast<float4*>(ah + off) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+          *reinterpret_cast<float4*>(al + off) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+        }
+        fence_proxy_async_smem();                        // generic writes -> tensor-core reads
+        tc_fence_before();
+        __syncthreads();
+        if (tid == 0) {
+          tc_fence_after();
+          const uint64_t dah = smem_desc_kmajor(smem_u32(ah), 1024, 2);
+          const uint64_t dal = smem_desc_kmajor(smem_u32(al), 1024, 2);
+          const uint64_t dbh = smem_desc_kmajor(smem_u32(sBh + kt * 8192), 1024, 2);
+          const uint64_t dbl = smem_desc_kmajor(smem_u32(sBl + kt * 8192), 1024, 2);
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            mma_tf32(tmem, dal + 2 * ks, dbh + 2 * ks, idesc, (kt > 0 || ks > 0) ? 1u : 0u);
+            mma_tf32(tmem, dah + 2 * ks, dbl + 2 * ks, idesc, 1u);
+            mma_tf32(tmem, dah + 2 * ks, dbh + 2 * ks, idesc, 1u);
+          }
+          issued = 1;
+          mma_commit(&mma_done[buf]);
+          if (kt == nk - 1) mma_commit(acc_full);
+        }
+        ++use[buf];
+      }
+      if (!ok) break;
+      const bool okw = mbar_wait_bounded(acc_full, acc_uses & 1, p.timeout);
+      ++acc_uses;
+      if (!okw && p.err) atomicOr(p.err, kErrTimeoutAcc);
+      tc_fence_after();
+      if (!__syncthreads_and(okw)) { ok = false; break; }
+      float a[32], x[32];
+      tmem_ld32(lane_base + 32 * half, a);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) x[j] = fmaf(a[j], sc[32 * half + j], bi[32 * half + j]);
+      tc_fence_before();
+      __syncthreads();                                   // TMEM read out: the next GEMM may overwrite it
+      const int c0 = 32 * half;
+      const int nvalid = min(32, p.Cout - c0);           // channels this thread stores (multiple of 16)
+      const int t_first = p.Tin > 1 ? g : 0, t_last = p.Tin > 1 ? g : p.T - 1;
+      for (int t = t_first; t <= t_last && pv && nvalid > 0; ++t) {
+        uint32_t w[16];
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+          uint32_t bits = 0;
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int j = 2 * u + e;
+            if constexpr (MODE == kModeNone) {
+              bits |= static_cast<uint32_t>(__half_as_ushort(__float2half_rn(x[j]))) << (16 * e);
+            } else {
+              if (neuron_step<MODE>(v[j], x[j], p.decay, p.tau, p.v_th, p.v_reset))
+                bits |= 0x3C00u << (16 * e);
+            }
+          }
+          w[u] = bits;
+        }
+        uint4* dst = reinterpret_cast<uint4*>(p.out + (static_cast<size_t>(t) * P + pix) * p.Cout + c0);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if (8 * q < nvalid) dst[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+      }
+    }
+  }
+  // Every MMA issued has completed before TMEM is released.
+  if (tid == 0 && issued) {
+    mma_commit(drain);
+    if (!mbar_wait_bounded(drain, 0, p.timeout) && p.err) atomicOr(p.err, kErrTimeoutDrain);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 64);
+  }
+}
+
 // ------------------------------------------------ elementwise neuron glue
 // Fused Add + neuron and MaxPool + neuron over T (the reference's
 // add_lif_fused_kernel and maxpool_lif_fused_kernel,

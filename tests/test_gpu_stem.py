@@ -14,14 +14,16 @@ pytestmark = pytest.mark.gpu
 GUARD, SENTINEL = 4096, -3.0
 
 
-def run_stem(x, w, scale, bias, T, neuron, tau, Tin):
+def run_stem(x, w, scale, bias, T, neuron, tau, Tin, stride=1):
     import torch
     from sparsesnn_b200 import runtime as rt
     lib = rt.load()
     B, Cin, H, W = x.shape[1:]
-    Cout = w.shape[0]
-    d = rt.make_desc(T=T, B=B, Cin=Cin, H=H, W=W, Cout=Cout, KH=3, KW=3, stride=1, pad=1,
+    Cout, k = w.shape[0], w.shape[2]
+    d = rt.make_desc(T=T, B=B, Cin=Cin, H=H, W=W, Cout=Cout, KH=k, KW=k, stride=stride, pad=k // 2,
                      neuron=neuron, tau=tau)
+    H = (H + 2 * (k // 2) - k) // stride + 1
+    W = (W + 2 * (k // 2) - k) // stride + 1
     xd = torch.from_numpy(x).cuda()
     wd = torch.from_numpy(w).cuda()
     sd = torch.from_numpy(scale).cuda()
@@ -40,8 +42,9 @@ def run_stem(x, w, scale, bias, T, neuron, tau, Tin):
     return np.transpose(out.float().cpu().numpy().reshape(T, B, H, W, Cout), (0, 1, 4, 2, 3))
 
 
-def reference(x, w, scale, bias, T, neuron, tau):
-    z = np.stack([L.conv2d_nchw(x[t], w, 1, 1) for t in range(x.shape[0])])
+def reference(x, w, scale, bias, T, neuron, tau, stride=1):
+    k = w.shape[2]
+    z = np.stack([L.conv2d_nchw(x[t], w, stride, k // 2) for t in range(x.shape[0])])
     z = (z * scale[None, None, :, None, None] + bias[None, None, :, None, None]).astype(np.float32)
     if z.shape[0] == 1:
         z = np.repeat(z, T, 0)
@@ -54,17 +57,32 @@ def reference(x, w, scale, bias, T, neuron, tau):
     dict(H=9, W=7, Cout=64, neuron="if", tau=2.0, Tin=1),       # IF, short image
     dict(H=16, W=16, Cout=32, neuron="lif", tau=2.0, Tin=1),     # general kernel (32 channels)
     dict(H=16, W=16, Cout=64, neuron="lif", tau=2.0, Tin=4),     # general kernel (input per timestep)
-], ids=["cifar", "w40_tau3", "if_9x7", "c32_general", "tin4_general"])
+    # general tensor-core stem (K <= 192): a 7x7/2 event-frame stem (2 channels, a frame
+    # per timestep), a 48-channel stem on rows wider than 128 pixels, a 7x7/2
+    # RGB stem with an IF neuron
+    dict(H=30, W=34, Cout=64, neuron="lif", tau=2.0, Tin=8, Cin=2, k=7, stride=2, binary=True),
+    dict(H=12, W=140, Cout=48, neuron="lif", tau=2.0, Tin=1),
+    dict(H=29, W=29, Cout=64, neuron="if", tau=2.0, Tin=1, k=7, stride=2),
+    # CUDA-core stem (more than 64 channels)
+    dict(H=16, W=16, Cout=96, neuron="lif", tau=2.0, Tin=1),
+], ids=["cifar", "w40_tau3", "if_9x7", "c32_general", "tin4_general", "dvs7x7s2", "c48_w140",
+        "rgb7x7s2_if", "c96_cudacore"])
 def test_stem_parity(cuda_device, case):
     rng = np.random.default_rng(7)
-    T, B, Cin = 4, 3, 3
+    Cin, k, stride = case.get("Cin", 3), case.get("k", 3), case.get("stride", 1)
+    T, B = max(4, case["Tin"]), 3
     H, W, Cout = case["H"], case["W"], case["Cout"]
-    x = rng.standard_normal((case["Tin"], B, Cin, H, W)).astype(np.float32)
-    w = (rng.standard_normal((Cout, Cin, 3, 3)) * 0.3).astype(np.float32)
+    if case.get("binary"):
+        x = (rng.random((case["Tin"], B, Cin, H, W)) < 0.3).astype(np.float32)
+        w = (rng.standard_normal((Cout, Cin, k, k)) * 0.6).astype(np.float32)
+    else:
+        x = rng.standard_normal((case["Tin"], B, Cin, H, W)).astype(np.float32)
+        w = (rng.standard_normal((Cout, Cin, k, k)) * 0.3 * 3 / k).astype(np.float32)
     scale = rng.uniform(0.5, 1.5, Cout).astype(np.float32)
     bias = rng.normal(0, 0.1, Cout).astype(np.float32)
-    got = run_stem(x, w, scale, bias, T, case["neuron"], case["tau"], case["Tin"])
-    spk, h, _ = reference(x, w, scale, bias, T, case["neuron"], case["tau"])
+    got = run_stem(x, w, scale, bias, T, case["neuron"], case["tau"], case["Tin"], stride)
+    spk, h, _ = reference(x, w, scale, bias, T, case["neuron"], case["tau"], stride)
+    assert 0.02 < spk.mean() < 0.9
     assert set(np.unique(got)) <= {0.0, 1.0}
     frac, ok, _, _ = L.spike_agreement(got, spk, h)
     assert frac >= 0.995 and ok, frac
