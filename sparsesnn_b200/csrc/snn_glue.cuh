@@ -368,9 +368,9 @@ stem_tc_kernel(const __grid_constant__ StemParams p) {
 // channels), 16-byte stores of the pixel's channels.
 constexpr int kStemGThreads = 256;
 constexpr int kStemGMaxK = 192;
-constexpr int kStemGMaxStage = 40 * 1024;     // bytes of the staged input window
+constexpr int kStemGMaxStage = 20 * 1024;     // bytes of one staged input window (two alternate)
 __host__ __device__ constexpr int stem_tcg_smem_bytes(int nk) {
-  return 2 * nk * 8192 + 4 * 16384 + kStemGMaxStage + kStemGMaxK * 8 + 2 * 64 * 4 + 64 + 1024;
+  return 2 * nk * 8192 + 4 * 16384 + 2 * kStemGMaxStage + kStemGMaxK * 4 + 2 * 64 * 4 + 64 + 1024;
 }
 
 template <int MODE>
@@ -386,15 +386,15 @@ stem_tc_gen_kernel(const __grid_constant__ StemParams p) {
   uint8_t* sBh = smem;                                   // [nk][64 ch][32] fp32, 128B swizzle
   uint8_t* sBl = sBh + nk * 8192;
   uint8_t* sA = sBl + nk * 8192;                         // [2 buf][hi, lo][128 px][32]
-  float* xs = reinterpret_cast<float*>(sA + 4 * 16384);  // [Cin][IR][IC] staged input
-  int* kofs = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(xs) + kStemGMaxStage);
+  float* xs0 = reinterpret_cast<float*>(sA + 4 * 16384); // [2][Cin][IR][IC] staged input windows
+  int* kofs = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(xs0) + 2 * kStemGMaxStage);
   float* sc = reinterpret_cast<float*>(kofs + kStemGMaxK);
   float* bi = sc + 64;
   uint64_t* mma_done = reinterpret_cast<uint64_t*>(bi + 64);   // [2], per A buffer
   uint64_t* acc_full = mma_done + 2;
   uint64_t* drain = acc_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
-  const int tid = threadIdx.x, warp = tid / 32;
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
   const int px = tid & 127, half = tid >> 7;             // pixel; column / channel half
   const int pr = px / TW, pc = px - (px / TW) * TW;      // pixel's row and column in the tile
 
@@ -441,38 +441,63 @@ stem_tc_gen_kernel(const __grid_constant__ StemParams p) {
   const long long n_tiles = static_cast<long long>(p.B) * tiles_h * tiles_w;
   const int n_gemm = p.Tin > 1 ? p.T : 1;
   const int HW = p.H * p.W;
-  const int nstage = p.Cin * IR * IC;
   const uint32_t idesc = idesc_tf32(128, 64);
   const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
   const int pofs = pr * p.stride * IC + pc * p.stride;   // this pixel's window origin in xs
+  // Work unit u of this block: tile blockIdx.x + (u / n_gemm) * gridDim.x,
+  // GEMM (frame) u % n_gemm.  The input window of unit u + 1 is copied into
+  // the other staging buffer (cp.async) while unit u computes.
+  auto unit_tile = [&](long long u) { return blockIdx.x + (u / n_gemm) * gridDim.x; };
+  auto tile_origin = [&](long long tile, int* b, int* oh0, int* ow0) {
+    const int twi = static_cast<int>(tile % tiles_w);
+    const long long rest = tile / tiles_w;
+    *oh0 = static_cast<int>(rest % tiles_h) * R;
+    *b = static_cast<int>(rest / tiles_h);
+    *ow0 = twi * TW;
+  };
+  auto stage = [&](long long u, float* dst) {
+    int b, oh0, ow0;
+    tile_origin(unit_tile(u), &b, &oh0, &ow0);
+    const int g = static_cast<int>(u % n_gemm);
+    const int ih0 = oh0 * p.stride - p.pad, iw0 = ow0 * p.stride - p.pad;
+    const float* xin = p.x + (static_cast<size_t>(g) * p.B + b) * static_cast<size_t>(p.Cin) * HW;
+    for (int row = warp; row < p.Cin * IR; row += kStemGThreads / 32) {
+      const int ci = row / IR, ih = ih0 + row - ci * IR;
+      const bool rv = ih >= 0 && ih < p.H;
+      const float* src = xin + static_cast<size_t>(ci) * HW + static_cast<size_t>(rv ? ih : 0) * p.W;
+#pragma unroll 4
+      for (int cc = lane; cc < IC; cc += 32) {
+        const int iw = iw0 + cc;
+        const bool valid = rv && iw >= 0 && iw < p.W;
+        cp_async4(dst + row * IC + cc, valid ? src + iw : p.x, valid);
+      }
+    }
+    cp_async_commit();
+  };
   uint32_t use[2] = {0, 0};                              // uses of each A buffer so far
   uint32_t acc_uses = 0;
   int issued = 0;                                        // MMAs issued by thread 0
   bool ok = true;
-  for (long long tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
-    const int twi = static_cast<int>(tile % tiles_w);
-    const long long rest = tile / tiles_w;
-    const int thi = static_cast<int>(rest % tiles_h);
-    const int b = static_cast<int>(rest / tiles_h);
-    const int oh0 = thi * R, ow0 = twi * TW;
+  float v[32];
+  if (blockIdx.x < n_tiles) stage(0, xs0);
+  for (long long un = 0; ok && unit_tile(un) < n_tiles; ++un) {
+    const long long tile = unit_tile(un);
+    const int g = static_cast<int>(un % n_gemm);
+    float* xs = xs0 + (un & 1) * (kStemGMaxStage / 4);
+    if (unit_tile(un + 1) < n_tiles) stage(un + 1, xs0 + ((un + 1) & 1) * (kStemGMaxStage / 4));
+    else cp_async_commit();                              // an empty group keeps the counting uniform
+    cp_async_wait<1>();                                  // this unit's window has landed
+    __syncthreads();
+    int b, oh0, ow0;
+    tile_origin(tile, &b, &oh0, &ow0);
     const int oh = oh0 + pr, ow = ow0 + pc;
     const bool pv = pr < R && oh < p.OH && ow < p.OW;
     const long long pix = (static_cast<long long>(b) * p.OH + oh) * p.OW + ow;
-    const int ih0 = oh0 * p.stride - p.pad, iw0 = ow0 * p.stride - p.pad;
-    float v[32];
+    if (g == 0) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = 0.f;
-    for (int g = 0; g < n_gemm && ok; ++g) {
-      // Stage the input window of frame g (zero outside the image).  The
-      // previous GEMM's builds have all passed a barrier since they read xs.
-      const float* xin = p.x + (static_cast<size_t>(g) * p.B + b) * static_cast<size_t>(p.Cin) * HW;
-      for (int i = tid; i < nstage; i += kStemGThreads) {
-        const int ci = i / (IR * IC), r = i - ci * IR * IC, rr = r / IC, cc = r - rr * IC;
-        const int ih = ih0 + rr, iw = iw0 + cc;
-        xs[i] = (ih >= 0 && ih < p.H && iw >= 0 && iw < p.W)
-                    ? __ldg(xin + static_cast<size_t>(ci) * HW + static_cast<size_t>(ih) * p.W + iw) : 0.f;
-      }
-      __syncthreads();
+      for (int j = 0; j < 32; ++j) v[j] = 0.f;
+    }
+    {
       for (int kt = 0; kt < nk; ++kt) {
         const int buf = (use[0] + use[1]) & 1;
         if (use[buf] > 0) {                              // the MMAs that read this buffer are done
@@ -536,11 +561,11 @@ stem_tc_gen_kernel(const __grid_constant__ StemParams p) {
       for (int t = t_first; t <= t_last && pv && nvalid > 0; ++t) {
         uint32_t w[16];
 #pragma unroll
-        for (int u = 0; u < 16; ++u) {
+        for (int q2 = 0; q2 < 16; ++q2) {
           uint32_t bits = 0;
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            const int j = 2 * u + e;
+            const int j = 2 * q2 + e;
             if constexpr (MODE == kModeNone) {
               bits |= static_cast<uint32_t>(__half_as_ushort(__float2half_rn(x[j]))) << (16 * e);
             } else {
@@ -548,7 +573,7 @@ stem_tc_gen_kernel(const __grid_constant__ StemParams p) {
                 bits |= 0x3C00u << (16 * e);
             }
           }
-          w[u] = bits;
+          w[q2] = bits;
         }
         uint4* dst = reinterpret_cast<uint4*>(p.out + (static_cast<size_t>(t) * P + pix) * p.Cout + c0);
 #pragma unroll
@@ -557,6 +582,7 @@ stem_tc_gen_kernel(const __grid_constant__ StemParams p) {
       }
     }
   }
+  cp_async_wait<0>();
   // Every MMA issued has completed before TMEM is released.
   if (tid == 0 && issued) {
     mma_commit(drain);
