@@ -162,6 +162,24 @@ int snn_conv_forward_res2(const snn_conv_desc* d, const void* data, const void* 
                           const float* bn_bias, const void* residual, void* out,
                           void* stream);
 
+/* Timestep-split form of the fused layer, for long T on few images (the
+ * DVS configuration: T = 16, 4 images per GPU), where the one-pass kernels
+ * have few pixel tiles to spread over the SMs because each CTA walks the T
+ * chunks of its tiles in order.  Phase 1 runs conv + BN for all T*B images at
+ * once (no neuron) into `workspace` as fp32; phase 2 runs the neuron over T
+ * from there (+ the residual: d->res_mode ADD_AFTER or ADD_BEFORE, or
+ * residual null) and writes the spikes.  Same arguments and results as
+ * snn_conv_forward / snn_conv_forward_res (LIF or IF neuron, no dense weights)
+ * plus a device workspace of at least snn_conv_tsplit_workspace_bytes()
+ * bytes, 16-byte aligned, owned by the caller, reused across calls.  No
+ * counterpart in the reference: its fused kernels keep the T loop inside one
+ * CTA (sengine/kernels/conv2d_bn_if_t4.py:952-1020). */
+int snn_conv_tsplit_workspace_bytes(const snn_conv_desc* d, size_t* bytes);
+int snn_conv_forward_tsplit(const snn_conv_desc* d, const void* data, const void* weight,
+                            float* state, const float* bn_scale, const float* bn_bias,
+                            const void* residual, void* out, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
 /* Dense direct-conv stem + BN + neuron (the Cin=3 first layer, which the
  * reference keeps dense: sengine/graph_slicer.py:106 skips Cin<4 and the
  * executor runs naive_conv2d_bn_nhwc_kernel, sengine/csrc/cpp_executor.cu:306-347).

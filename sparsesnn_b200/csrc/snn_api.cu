@@ -968,6 +968,91 @@ int snn_conv_forward_res2(const snn_conv_desc* d, const void* data, const void* 
                      snn::kResTwoNeuron, out, stream);
 }
 
+int snn_conv_tsplit_workspace_bytes(const snn_conv_desc* d, size_t* bytes) {
+  Geometry g;
+  int st = check_desc(d, &g);
+  if (st) return st;
+  if (!bytes) return fail(SNN_E_INVALID, "null output");
+  *bytes = static_cast<size_t>(d->T) * d->B * g.OH * g.OW * d->Cout * sizeof(float);
+  return SNN_OK;
+}
+
+int snn_conv_forward_tsplit(const snn_conv_desc* d, const void* data, const void* weight,
+                            float* state, const float* bn_scale, const float* bn_bias,
+                            const void* residual, void* out, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  int st = ensure_init();
+  if (st) return st;
+  Geometry g;
+  if ((st = check_desc(d, &g))) return st;
+  if (d->neuron != SNN_NEURON_LIF && d->neuron != SNN_NEURON_IF)
+    return fail(SNN_E_INVALID, "timestep split: neuron must be LIF or IF");
+  if (d->flags & (SNN_FLAG_DENSE | SNN_FLAG_CTA_PAIR))
+    return fail(SNN_E_INVALID, "timestep split: no dense weights or CTA pairs");
+  if (residual && d->res_mode != SNN_RES_ADD_AFTER && d->res_mode != SNN_RES_ADD_BEFORE)
+    return fail(SNN_E_INVALID, "timestep split: residual ADD_AFTER or ADD_BEFORE");
+  if (!out || !workspace) return fail(SNN_E_INVALID, "null tensor pointer");
+  if ((d->flags & (SNN_FLAG_READ_STATE | SNN_FLAG_WRITE_STATE)) && !state)
+    return fail(SNN_E_INVALID, "state flags set but state is null");
+  size_t need = 0;
+  snn_conv_tsplit_workspace_bytes(d, &need);
+  if (workspace_bytes < need)
+    return fail(SNN_E_INVALID, "workspace of %zu bytes, %zu needed", workspace_bytes, need);
+  if ((reinterpret_cast<uintptr_t>(workspace) | reinterpret_cast<uintptr_t>(out) |
+       reinterpret_cast<uintptr_t>(residual)) & 15)
+    return fail(SNN_E_INVALID, "workspace, out and residual must be 16-byte aligned");
+  // Phase 1: conv + BN of all T*B images, no neuron, fp32 into the
+  // workspace.  The leading [T*B] dimension is regrouped as [T'][B'] so that
+  // the general kernel keeps its four-timestep accumulators: the images are
+  // independent here, only the order of the flat index matters.
+  snn_conv_desc d1 = *d;
+  const long long tb = static_cast<long long>(d->T) * d->B;
+  d1.T = tb % 4 == 0 ? 4 : tb % 2 == 0 ? 2 : 1;
+  d1.B = static_cast<int32_t>(tb / d1.T);
+  d1.neuron = SNN_NEURON_NONE;
+  d1.flags = d->flags & SNN_FLAG_FORCE_GENERIC;
+  d1.res_mode = SNN_RES_ADD_AFTER;
+  if ((st = launch_conv(&d1, data, weight, nullptr, nullptr, bn_scale, bn_bias, nullptr,
+                        snn::kResNone, workspace, stream)))
+    return st;
+  // Phase 2: the neuron over T (+ residual), spikes out.
+  snn::TsplitParams p;
+  memset(&p, 0, sizeof(p));
+  p.z = static_cast<const float*>(workspace);
+  p.residual = static_cast<const __half*>(residual);
+  p.out = static_cast<__half*>(out);
+  p.state = state;
+  p.P = static_cast<long long>(d->B) * g.OH * g.OW;
+  p.T = d->T; p.C = d->Cout; p.flags = d->flags;
+  p.tau = d->tau;
+  // Reference computes (1.0 - 1.0/tau) in double, then float32 (models/neurons.py:125).
+  p.decay = d->neuron == SNN_NEURON_LIF ? static_cast<float>(1.0 - 1.0 / static_cast<double>(d->tau)) : 1.0f;
+  p.v_th = d->v_threshold; p.v_reset = d->v_reset;
+  const int mode = d->neuron == SNN_NEURON_IF ? snn::kModeIf
+                   : d->tau == 2.0f ? snn::kModeLifHalf : snn::kModeLifDiv;
+  const int rm = !residual ? snn::kResNone
+                 : d->res_mode == SNN_RES_ADD_BEFORE ? snn::kResAddBefore : snn::kResAddAfter;
+  using TsK = void (*)(const snn::TsplitParams);
+  TsK k = nullptr;
+  switch (mode * 3 + (rm == snn::kResNone ? 0 : rm == snn::kResAddAfter ? 1 : 2)) {
+    case 0: k = snn::tsplit_neuron_kernel<snn::kModeLifHalf, snn::kResNone>; break;
+    case 1: k = snn::tsplit_neuron_kernel<snn::kModeLifHalf, snn::kResAddAfter>; break;
+    case 2: k = snn::tsplit_neuron_kernel<snn::kModeLifHalf, snn::kResAddBefore>; break;
+    case 3: k = snn::tsplit_neuron_kernel<snn::kModeLifDiv, snn::kResNone>; break;
+    case 4: k = snn::tsplit_neuron_kernel<snn::kModeLifDiv, snn::kResAddAfter>; break;
+    case 5: k = snn::tsplit_neuron_kernel<snn::kModeLifDiv, snn::kResAddBefore>; break;
+    case 6: k = snn::tsplit_neuron_kernel<snn::kModeIf, snn::kResNone>; break;
+    case 7: k = snn::tsplit_neuron_kernel<snn::kModeIf, snn::kResAddAfter>; break;
+    default: k = snn::tsplit_neuron_kernel<snn::kModeIf, snn::kResAddBefore>; break;
+  }
+  const long long n = p.P * (d->Cout / 8);
+  const long long blocks = std::max<long long>(1, std::min<long long>((n + 255) / 256,
+                                                                    static_cast<long long>(g_num_sms) * 16));
+  cudaError_t e = launch_pdl(k, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream, p);
+  if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));
+  return SNN_OK;
+}
+
 int snn_stem_forward(const snn_conv_desc* d, int32_t Tin, const float* x, const float* w,
                      const float* bn_scale, const float* bn_bias, void* out, void* stream) {
   int st = ensure_init();

@@ -29,6 +29,8 @@
 //   MAXPOOL_LIF in0, out; desc (KH = window, stride, pad; neuron NONE: the
 //               plain max pool)
 //   LIF         in0, out; desc (the neuron of one input)
+//   CONV_TSPLIT as CONV, in the timestep-split form; i[0] = the fp32
+//               workspace tensor
 //   ATTN        in0 = q, in1 = k, i[0] = v, out; desc T, B, tau,
 //               v_threshold, v_reset, tau2 = the attention scale;
 //               i[1..3] = tokens, heads, head_dim
@@ -45,7 +47,7 @@ constexpr char kEngineMagic[4] = {'S', 'N', 'N', 'E'};
 constexpr uint32_t kEngineVersion = 2;
 constexpr uint32_t kNoTensor = 0xffffffffu;
 enum EngineOp : uint32_t { kOpStem = 1, kOpConv = 2, kOpHead = 3, kOpAddLif = 4, kOpMaxPoolLif = 5,
-                           kOpLif = 6, kOpAttn = 7 };
+                           kOpLif = 6, kOpAttn = 7, kOpConvTsplit = 8 };
 
 struct SnnEngineHeader {
   char magic[4];
@@ -134,12 +136,20 @@ int parse_engine_file(const char* path, SnnEngineHeader* h, std::vector<SnnEngin
           return fail(SNN_E_INVALID, "engine node %u (stem): sizes or offsets out of range", n);
         break;
       }
-      case kOpConv: {
+      case kOpConv:
+      case kOpConvTsplit: {
         int32_t oh = 0, ow = 0;
         size_t wbytes = 0;
         int st = snn_conv_out_shape(&d, &oh, &ow);
         if (!st) st = snn_conv_weight_bytes(&d, &wbytes);
         if (st) return st;
+        if (nd.op == kOpConvTsplit) {
+          size_t ws = 0;
+          const uint32_t ws_id = static_cast<uint32_t>(nd.i[0]);
+          if ((st = snn_conv_tsplit_workspace_bytes(&d, &ws))) return st;
+          if (!tid_ok(ws_id) || (*tensors)[ws_id].bytes < ws)
+            return fail(SNN_E_INVALID, "engine node %u (conv): workspace missing or too small", n);
+        }
         const uint64_t out_need = uint64_t(d.T) * d.B * oh * ow * d.Cout * (d.neuron == SNN_NEURON_NONE ? 4 : 2);
         if (in_bytes < uint64_t(d.T) * d.B * d.H * d.W * d.Cin * 2 || out_bytes < out_need ||
             (nd.in1 != kNoTensor && (*tensors)[nd.in1].bytes < uint64_t(d.T) * d.B * oh * ow * d.Cout * 2) ||
@@ -255,6 +265,12 @@ int engine_node_loop(snn_engine* e, void* stream) {
       case kOpLif:
         st = snn_lif_forward(&nd.desc, in0, nullptr, out, stream);
         break;
+      case kOpConvTsplit: {
+        const uint32_t ws = static_cast<uint32_t>(nd.i[0]);
+        st = snn_conv_forward_tsplit(&nd.desc, in0, e->dblob + nd.p0, nullptr, P(nd.p1), P(nd.p2), in1,
+                                     out, e->tptr[ws], e->tensors[ws].bytes, stream);
+        break;
+      }
       case kOpAttn: {
         const snn_conv_desc& d = nd.desc;
         st = snn_spikformer_attn_forward(d.T, d.B, nd.i[1], nd.i[2], nd.i[3], d.tau2, d.tau,

@@ -741,6 +741,79 @@ glue_neuron_kernel(const GlueParams p) {
   }
 }
 
+// ------------------------------------------------ timestep-split neuron scan
+// Second phase of the timestep-split fused layer (snn_conv_forward_tsplit):
+// the first phase ran the conv + BN for all T*B images at once (no neuron,
+// fp32 BN output z); here thread = (pixel, 8 channels) runs the neuron over
+// T with the membrane in registers, adds the residual (after the neuron: the
+// SEW add; before it: the neuron integrates bn + residual) and writes fp16
+// spikes.  The arithmetic is the fused epilogue's (for tau = 2 the input is
+// halved exactly, as there), so the spikes equal the one-pass layer's for
+// the same BN outputs.
+struct TsplitParams {
+  const float* z;          // [T][P][C] BN output
+  const __half* residual;  // [T][P][C] or null
+  __half* out;             // [T][P][C]
+  float* state;            // [P][C] membrane or null
+  long long P;             // pixels per timestep (B*OH*OW)
+  int T, C, flags;
+  float tau, decay, v_th, v_reset;
+};
+
+template <int MODE, int RM>
+__global__ void __launch_bounds__(256)
+tsplit_neuron_kernel(const TsplitParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int c8n = p.C / 8;
+  const long long n = p.P * c8n;
+  for (long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; idx < n;
+       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long pix = idx / c8n;
+    const int c8 = static_cast<int>(idx - pix * c8n);
+    const size_t base = static_cast<size_t>(pix) * p.C + c8 * 8;
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = (p.flags & kReadState) ? p.state[base + j] : 0.f;
+    for (int t = 0; t < p.T; ++t) {
+      const size_t off = static_cast<size_t>(t) * p.P * p.C + base;
+      const float4 za = __ldg(reinterpret_cast<const float4*>(p.z + off));
+      const float4 zb = __ldg(reinterpret_cast<const float4*>(p.z + off) + 1);
+      float x[8] = {za.x, za.y, za.z, za.w, zb.x, zb.y, zb.z, zb.w};
+      uint4 r4 = make_uint4(0, 0, 0, 0);
+      if constexpr (RM != kResNone) r4 = __ldg(reinterpret_cast<const uint4*>(p.residual + off));
+      const __half2* rh = reinterpret_cast<const __half2*>(&r4);
+      uint32_t w[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float2 rf = __half22float2(rh[u]);
+        uint32_t bits = 0;
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int j = 2 * u + e;
+          const float r = e ? rf.y : rf.x;
+          // kModeLifHalf takes bn/2 (exact), plus r/2 when the residual enters the neuron.
+          float xi = MODE == kModeLifHalf ? x[j] * 0.5f : x[j];
+          if constexpr (RM == kResAddBefore) xi = __fadd_rn(xi, MODE == kModeLifHalf ? r * 0.5f : r);
+          const bool s = neuron_step<MODE>(v[j], xi, p.decay, p.tau, p.v_th, p.v_reset);
+          if constexpr (RM == kResAddAfter) {
+            bits |= static_cast<uint32_t>(__half_as_ushort(__float2half_rn((s ? 1.f : 0.f) + r)))
+                    << (16 * e);
+          } else {
+            bits |= (s ? 0x3C00u : 0u) << (16 * e);
+          }
+        }
+        w[u] = bits;
+      }
+      *reinterpret_cast<uint4*>(p.out + off) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    if (p.flags & kWriteState) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) p.state[base + j] = v[j];
+    }
+  }
+}
+
 // One block (1024 threads) per image.  Phase 1: thread (c8, slot) sums 8
 // consecutive channels (16-byte loads) over every 16th (t, hw) position; the
 // partial sums are combined in shared memory and scaled: feat = sum / HW / T

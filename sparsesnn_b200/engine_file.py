@@ -27,6 +27,7 @@ MAGIC = b"SNNE"
 VERSION = 2
 NO_TENSOR = 0xFFFFFFFF
 OP_STEM, OP_CONV, OP_HEAD, OP_ADD_LIF, OP_MAXPOOL_LIF, OP_LIF, OP_ATTN = 1, 2, 3, 4, 5, 6, 7
+OP_CONV_TSPLIT = 8
 F16, F32 = 0, 1
 _ALIGN = 256
 
@@ -110,8 +111,13 @@ def save_plan(model, path):
         in1 = ins[1] if len(ins) > 1 else NO_TENSOR
         if n.kind == npl.CONV:
             L = n.layer
-            w.node(OP_CONV, ins[0], in1, out, _conv_desc(L),
-                   (P(L.weight_blob), P(L.bn_scale), P(L.bn_bias), 0))
+            if n.workspace is not None:
+                w.node(OP_CONV_TSPLIT, ins[0], in1, out, _conv_desc(L),
+                       (P(L.weight_blob), P(L.bn_scale), P(L.bn_bias), 0),
+                       (tid(n.workspace), 0, 0, 0, 0))
+            else:
+                w.node(OP_CONV, ins[0], in1, out, _conv_desc(L),
+                       (P(L.weight_blob), P(L.bn_scale), P(L.bn_bias), 0))
         elif n.kind == npl.STEM:
             w.node(OP_STEM, ins[0], NO_TENSOR, out, n.desc, tuple(P(t) for t in n.params) + (0,),
                    n.ints)

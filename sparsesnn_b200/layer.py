@@ -9,6 +9,8 @@ output ``(T*B, OH, OW, Cout)`` (reference
 """
 from __future__ import annotations
 
+import ctypes
+
 import numpy as np
 import torch
 
@@ -84,14 +86,22 @@ class SparseConvBNLIF:
     def state_shape(self):
         return (self.B * self.OH * self.OW, self.Cout)
 
+    def workspace_bytes(self):
+        """Bytes of the workspace the timestep-split form needs."""
+        n = ctypes.c_size_t()
+        rt.check(rt.load().snn_conv_tsplit_workspace_bytes(self.desc, ctypes.byref(n)))
+        return n.value
+
     def __call__(self, data, state=None, residual=None, out=None, *, read_state=None,
-                 write_state=None, stream=None, state2=None):
+                 write_state=None, stream=None, state2=None, workspace=None):
         """Run the layer; returns ``out``.
 
         ``state`` (optional) is the membrane buffer: read at start unless
         ``read_state=False`` and final v written unless ``write_state=False``.
         ``state2`` is the second neuron's membrane (``res_mode="two_neuron"``,
-        same shape and flags as ``state``).
+        same shape and flags as ``state``).  With ``workspace`` (a device
+        tensor of at least ``workspace_bytes()`` bytes) the layer runs in its
+        timestep-split form (``snn_conv_forward_tsplit``).
         """
         if data.dtype != torch.float16 or not data.is_contiguous():
             raise ValueError("data must be contiguous fp16 (T*B, H, W, Cin)")
@@ -122,7 +132,16 @@ class SparseConvBNLIF:
         if residual is not None:
             if residual.dtype != torch.float16 or tuple(residual.shape) != self.out_shape():
                 raise ValueError("residual must be fp16 (T*B, OH, OW, Cout)")
-        if self.res_mode == "two_neuron":
+        if workspace is not None:
+            if self.res_mode == "two_neuron":
+                raise ValueError("the timestep-split form has no two-neuron epilogue")
+            nbytes = workspace.numel() * workspace.element_size()
+            rt.check(lib.snn_conv_forward_tsplit(
+                self.desc, data.data_ptr(), self.weight_blob.data_ptr(), sp,
+                self.bn_scale.data_ptr(), self.bn_bias.data_ptr(),
+                residual.data_ptr() if residual is not None else None, out.data_ptr(),
+                workspace.data_ptr(), nbytes, s))
+        elif self.res_mode == "two_neuron":
             rt.check(lib.snn_conv_forward_res2(
                 self.desc, data.data_ptr(), self.weight_blob.data_ptr(), sp,
                 state2.data_ptr() if state2 is not None else None,

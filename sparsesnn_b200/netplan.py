@@ -37,6 +37,7 @@ class Node:
     ints: tuple = (0, 0, 0, 0, 0)
     layer: object = None           # CONV: the SparseConvBNLIF
     attn: dict = field(default_factory=dict)   # ATTN: N, heads, head_dim, scale
+    workspace: object = None       # CONV: fp32 workspace of the timestep-split form, or None
 
 
 class PlanModel:
@@ -75,6 +76,17 @@ class PlanModel:
         self.nodes.append(node)
         return node.out
 
+    def split_workspace(self, layer):
+        """The model's workspace for timestep-split layers, grown to fit
+        ``layer`` (one buffer shared by every such layer: they run in turn)."""
+        need = (layer.workspace_bytes() + 3) // 4
+        if getattr(self, "_ws", None) is None or self._ws.numel() < need:
+            self._ws = torch.empty(need, dtype=torch.float32, device=self.device)
+            for n in self.nodes:
+                if n.workspace is not None:
+                    n.workspace = self._ws
+        return self._ws
+
     # ------------------------------------------------------------ launching
     def _t(self, x):
         if x is INPUT:
@@ -89,7 +101,8 @@ class PlanModel:
         ins = [self._t(x) for x in n.ins]
         out = self._t(n.out)
         if n.kind == CONV:
-            n.layer(ins[0], residual=ins[1] if len(ins) > 1 else None, out=out)
+            n.layer(ins[0], residual=ins[1] if len(ins) > 1 else None, out=out,
+                    workspace=n.workspace)
         elif n.kind == STEM:
             w, sc, bi = n.params
             rt.check(lib.snn_stem_forward(n.desc, n.ints[0], ins[0].data_ptr(), w.data_ptr(),

@@ -332,7 +332,7 @@ class SEWResNet18DVS(PlanModel):
     """
 
     def __init__(self, params, *, T=16, batch=4, H=128, W=128, tau=2.0, v_threshold=1.0,
-                 device="cuda"):
+                 device="cuda", split_t=True):
         st = params["stem"]
         cout, cin, kh, kw = st["w"].shape
         super().__init__(T=T, batch=batch, in_shape=(T, batch, cin, H, W),
@@ -352,19 +352,31 @@ class SEWResNet18DVS(PlanModel):
                                 pad=1)))
         kw_ = dict(T=T, B=batch, tau=tau, v_threshold=v_threshold, device=dev)
         h, w_, x = ph, pw, p0
+
+        def conv(name, layer, ins):
+            # Long T on few images: 3x3 layers of >= 128 channels run in the
+            # timestep-split form (all T*B images' GEMMs spread over the SMs,
+            # then the neuron scan), measured 1.5-2.7x faster at T = 16 on 4
+            # images; the 64-channel and 1x1 layers stay one-pass.
+            ws = None
+            if split_t and T >= 8 and layer.desc.KH * layer.desc.KW > 1 and layer.Cout >= 128:
+                ws = self.split_workspace(layer)
+            return self.add(Node(CONV, name, ins, self.buf(layer.out_shape()), layer=layer,
+                                 workspace=ws))
+
         for i, blk in enumerate(params["blocks"]):
             stride = blk["stride"]
             l1 = SparseConvBNLIF(blk["w1"], *fold_bn(**blk["bn1"]), H=h, W=w_, stride=stride,
                                  pad=1, **kw_)
-            o1 = self.add(Node(CONV, f"b{i}.conv1", [x], self.buf(l1.out_shape()), layer=l1))
+            o1 = conv(f"b{i}.conv1", l1, [x])
             ident = x
             if "wd" in blk:
                 ds = SparseConvBNLIF(blk["wd"], *fold_bn(**blk["bnd"]), H=h, W=w_,
                                      stride=stride, pad=0, **kw_)
-                ident = self.add(Node(CONV, f"b{i}.ds", [x], self.buf(ds.out_shape()), layer=ds))
+                ident = conv(f"b{i}.ds", ds, [x])
             l2 = SparseConvBNLIF(blk["w2"], *fold_bn(**blk["bn2"]), H=l1.OH, W=l1.OW, stride=1,
                                  pad=1, **kw_)
-            x = self.add(Node(CONV, f"b{i}.conv2", [o1, ident], self.buf(l2.out_shape()), layer=l2))
+            x = conv(f"b{i}.conv2", l2, [o1, ident])
             h, w_ = l1.OH, l1.OW
         c = params["blocks"][-1]["planes"]
         self.feat_hw, self.feat_c = h * w_, c
