@@ -180,6 +180,23 @@ int snn_conv_forward_tsplit(const snn_conv_desc* d, const void* data, const void
                             const void* residual, void* out, void* workspace,
                             size_t workspace_bytes, void* stream);
 
+/* The timestep-split layer for callers that cannot allocate device memory
+ * (a runtime that hands out every allocation from its own pool, or a process
+ * where allocating is off limits once it serves): the fp32 intermediate lives
+ * in a fixed array inside the library, SNN_TSPLIT_STATIC_MAX_BYTES per GPU,
+ * held by every GPU that loads the library until the process exits.  Same
+ * arguments and results as snn_conv_forward_tsplit without the workspace;
+ * layers whose intermediate (snn_conv_tsplit_workspace_bytes) exceeds the
+ * array are rejected with SNN_E_INVALID.  Allocates nothing.  The first call
+ * on each device looks up the array's device address (with that device
+ * current), so make that first call before any stream capture.  Calls share
+ * the one array: two calls that overlap on the GPU (other streams, other
+ * threads) race.  No counterpart in the reference. */
+#define SNN_TSPLIT_STATIC_MAX_BYTES (8u << 20)
+int snn_conv_forward_tsplit_static(const snn_conv_desc* d, const void* data, const void* weight,
+                                   float* state, const float* bn_scale, const float* bn_bias,
+                                   const void* residual, void* out, void* stream);
+
 /* Dense direct-conv stem + BN + neuron (the Cin=3 first layer, which the
  * reference keeps dense: sengine/graph_slicer.py:106 skips Cin<4 and the
  * executor runs naive_conv2d_bn_nhwc_kernel, sengine/csrc/cpp_executor.cu:306-347).

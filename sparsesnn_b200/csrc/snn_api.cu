@@ -1273,4 +1273,65 @@ int snn_get_device_error(uint32_t* code, int reset) {
 
 }  // extern "C"
 
+// ------------------------------------------------ timestep split, no allocation
+// Some callers of this library cannot call cudaMalloc: a runtime that owns
+// every device allocation through its own pool or arena, or a host that loads
+// the library into a process where allocating is not allowed once serving
+// has started.  For them the timestep-split layer has a form whose fp32
+// intermediate lives in a fixed array inside the library, so the caller
+// passes only inputs and outputs.
+namespace {
+
+// 8 MiB of BN outputs: a DVS SEW-ResNet-18 layer at T = 16 and 4 images per
+// GPU needs at most 16*4*16*16*128 fp32 (stage 2).  Every GPU that loads the
+// library holds the array until the process exits.
+constexpr size_t kTsplitStaticBytes = SNN_TSPLIT_STATIC_MAX_BYTES;
+static __device__ __align__(256) float g_tsplit_scratch[kTsplitStaticBytes / sizeof(float)];
+
+// Device address of g_tsplit_scratch per device (the name is only a host
+// stand-in for it), resolved once per device with that device current.
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_addr[kMaxDevices] = {};
+
+int tsplit_scratch_address(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(SNN_E_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return fail(SNN_E_INVALID, "device %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  if (!g_scratch_addr[dev]) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_tsplit_scratch);
+    if (e != cudaSuccess || !ptr)
+      return fail(SNN_E_CUDA, "scratch array address: %s", cudaGetErrorString(e));
+    g_scratch_addr[dev] = ptr;
+  }
+  *out = g_scratch_addr[dev];
+  return SNN_OK;
+}
+
+}  // namespace
+
+extern "C" int snn_conv_forward_tsplit_static(const snn_conv_desc* d, const void* data,
+                                              const void* weight, float* state,
+                                              const float* bn_scale, const float* bn_bias,
+                                              const void* residual, void* out, void* stream) {
+  int st = ensure_init();
+  if (st) return st;
+  size_t need = 0;
+  if ((st = snn_conv_tsplit_workspace_bytes(d, &need))) return st;
+  if (need > kTsplitStaticBytes)
+    return fail(SNN_E_INVALID,
+                "layer needs %zu bytes of intermediate, the static array holds %zu "
+                "(snn_conv_forward_tsplit with a caller workspace has no limit)",
+                need, kTsplitStaticBytes);
+  void* scratch = nullptr;
+  if ((st = tsplit_scratch_address(&scratch))) return st;
+  // Phase 1 writes every element of the region that phase 2 reads, so the
+  // previous call's contents never leak into this one.
+  return snn_conv_forward_tsplit(d, data, weight, state, bn_scale, bn_bias, residual, out, scratch,
+                                 kTsplitStaticBytes, stream);
+}
+
 #include "snn_engine.cuh"

@@ -43,7 +43,7 @@ EXPORTED = (
     "snn_pack_weight_24", "snn_conv_forward", "snn_conv_forward_res", "snn_conv_forward_res2",
     "snn_stem_forward", "snn_spikformer_attn_forward", "snn_add_lif_forward",
     "snn_maxpool_lif_forward", "snn_lif_forward", "snn_conv_tsplit_workspace_bytes",
-    "snn_conv_forward_tsplit",
+    "snn_conv_forward_tsplit", "snn_conv_forward_tsplit_static",
     "snn_head_forward", "snn_get_device_error", "snn_last_error_message",
     "snn_engine_check_file", "snn_engine_load", "snn_engine_io", "snn_engine_capture",
     "snn_engine_run", "snn_engine_destroy",
@@ -93,6 +93,7 @@ def _declare(lib):
         "snn_lif_forward": ([D, P, P, P, P], ctypes.c_int),
         "snn_conv_tsplit_workspace_bytes": ([D, ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
         "snn_conv_forward_tsplit": ([D, P, P, P, P, P, P, P, P, ctypes.c_size_t, P], ctypes.c_int),
+        "snn_conv_forward_tsplit_static": ([D, P, P, P, P, P, P, P, P], ctypes.c_int),
         "snn_spikformer_attn_forward": ([i32, i32, i32, i32, i32, ctypes.c_float, ctypes.c_float,
                                          ctypes.c_float, ctypes.c_float, i32, P, P, P, P, P, P],
                                         ctypes.c_int),
