@@ -122,6 +122,9 @@ HaloKernel halo_kernel_fn_bn(int mode, bool res) {
 
 // bn = 128 with m64 selects the M = 64 MMA path (layers of at most 64 channels).
 HaloKernel halo4_kernel_fn(int mode, bool res) {
+  if (mode == snn::kModeBnF16)
+    return res ? snn::fused_sparse_conv_halo4_kernel<snn::kModeBnF16, true>
+               : snn::fused_sparse_conv_halo4_kernel<snn::kModeBnF16, false>;
   switch (mode * 2 + (res ? 1 : 0)) {
     case 0: return snn::fused_sparse_conv_halo4_kernel<snn::kModeLifHalf, false>;
     case 1: return snn::fused_sparse_conv_halo4_kernel<snn::kModeLifHalf, true>;
@@ -281,6 +284,9 @@ int ensure_init() {
       }
     }
   }
+  for (int res = 0; res < 2 && e == cudaSuccess; ++res)
+    e = cudaFuncSetAttribute(halo4_kernel_fn(snn::kModeBnF16, res != 0),
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
   for (int tc : {2, 4}) {
     // fp16 BN output, plain and plus a residual; dense-weight spiking layers.
     for (int rm : {snn::kResNone, snn::kResAddAfter}) {
@@ -386,8 +392,13 @@ void general_tile(const Geometry& g, int B, int* tw, int* th, int* tn) {
 
 int select_variant(const snn_conv_desc* d, const Geometry& g) {
   if (d->flags & SNN_FLAG_FORCE_GENERIC) return SNN_VARIANT_GENERIC;
-  // Dense weights and the fp16 BN output run in the general kernel only.
-  if ((d->flags & SNN_FLAG_DENSE) || d->neuron == SNN_NEURON_NONE_F16) return SNN_VARIANT_GENERIC;
+  // Dense weights run in the general kernel only; the fp16 BN output also in
+  // the four-timestep halo kernel (<= 64 channels, stride-1 3x3, below).
+  if (d->flags & SNN_FLAG_DENSE) return SNN_VARIANT_GENERIC;
+  if (d->neuron == SNN_NEURON_NONE_F16 &&
+      !(d->Cout <= 64 && d->stride == 1 && d->KH == 3 && d->KW == 3 && d->pad == 1 && g.OW >= 8 &&
+        g.OH >= 8 && g.n_kb * snn::kABytes <= kHaloMaxWeightBytes))
+    return SNN_VARIANT_GENERIC;
   // Only the general kernel has the Add-before-neuron and two-neuron epilogues.
   if (d->res_mode != SNN_RES_ADD_AFTER) return SNN_VARIANT_GENERIC;
   const bool s1_3x3 = d->stride == 1 && d->KH == 3 && d->KW == 3 && d->pad == 1;
@@ -589,6 +600,10 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
         return SNN_OK;
       }
     }
+  }
+  if (variant == SNN_VARIANT_HALO_RESIDENT && mode != snn::kModeBnF16) {
+    snn::HaloParams hp;
+    memset(&hp, 0, sizeof(hp));
     const int bn = g.OH >= 16 ? 128 : 64;
     const bool m64 = bn == 128 && d->Cout <= 64;
     const int th_ = bn / 8;

@@ -69,7 +69,7 @@ __device__ __forceinline__ void tmem_ld16x2_32_split64(uint32_t taddr, float (&v
 template <int MODE, bool RES>
 __global__ void __launch_bounds__(kH4Threads, 1)
 fused_sparse_conv_halo4_kernel(const __grid_constant__ HaloParams hp) {
-  static_assert(MODE != kModeNone, "spiking epilogues only");
+  static_assert(MODE != kModeNone, "spiking epilogues or the fp16 BN output");
   constexpr int KS = 3;
   const ConvParams& p = hp.c;
   constexpr int kAKb = 64 * (kKB / 2) * 2;       // resident weight bytes per k-block (64 rows)
@@ -314,6 +314,34 @@ fused_sparse_conv_halo4_kernel(const __grid_constant__ HaloParams hp) {
         // (bits 0..15: channels 16q.. of the lower lanes' pixel, 16..31: of
         // the upper lanes' pixel two rows down), and lane l keeps the ballots
         // of the pixel column it writes.
+        if constexpr (MODE == kModeBnF16) {
+          // No neuron: each thread writes its channel's bn (+ residual, added
+          // in fp32 and rounded once) straight into the staging tile, at
+          // pixel (t, row, column) = byte ((t*8 + row)*8 + column)*128 +
+          // (16-byte chunk ch/8 XOR column)*16 + (ch%8)*2.
+          if constexpr (RES) {
+            if (!mbar_wait_bounded(&res_full[buf], (it >> 1) & 1, p.timeout_ns)) {
+              atomicOr(p.err, kErrTimeoutRes); fail = true;
+            }
+          }
+          uint8_t* tile = sO + buf * kH4OutBytes;
+#pragma unroll
+          for (int t = 0; t < kH4Ts; ++t) {
+#pragma unroll
+            for (int a = 0; a < 2; ++a) {
+#pragma unroll
+              for (int c = 0; c < 8; ++c) {
+                float x = fmaf(a ? acc1[t * 8 + c] : acc0[t * 8 + c], sc, bi);
+                const int prow = (t * 8 + r0 + a) * 8 + c;
+                __half* dst = reinterpret_cast<__half*>(tile + prow * 128 + ((((ch >> 3) ^ c)) << 4)) +
+                              (ch & 7);
+                if constexpr (RES) x = __fadd_rn(x, fail ? 0.f : __half2float(*dst));
+                if (cvalid && !fail) *dst = __float2half_rn(x);
+              }
+            }
+          }
+          fence_proxy_async_smem();
+        } else {
         uint32_t pk[2][kH4Ts];
 #pragma unroll
         for (int t = 0; t < kH4Ts; ++t) {
@@ -363,6 +391,7 @@ fused_sparse_conv_halo4_kernel(const __grid_constant__ HaloParams hp) {
           if (!fail) *dst = o;
         }
         fence_proxy_async_smem();
+        }
         }
         // Thread 0 first waits until the other tile's previous store has read
         // it, so after this barrier that tile is free for the next pass.

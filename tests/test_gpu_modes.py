@@ -253,3 +253,41 @@ def test_partial_input_channel_block(cuda_device, cin, cout, hw, dense, variant)
     v = np.transpose(st.cpu().numpy().reshape(B, oh, ow, cout), (0, 3, 1, 2))
     check_spikes(from_nhwc(y.float().cpu().numpy(), T, B), v, ref)
     assert 0.01 < ref["spikes"].mean() < 0.9
+
+
+@pytest.mark.parametrize("T, hw, cout", [(4, 56, 64), (3, 20, 48), (6, 16, 64)])
+@pytest.mark.parametrize("residual", [False, True], ids=["plain", "res"])
+def test_bn_f16_four_timestep_halo(cuda_device, T, hw, cout, residual):
+    """The fp16 BN output (+ real residual) in the four-timestep halo kernel
+    (MS-ResNet's stage-1 conv2 with its membrane shortcut): several pixel
+    tiles per CTA, T not a multiple of four, fewer than 64 channels."""
+    import torch
+    from sparsesnn_b200 import runtime as rt
+    from sparsesnn_b200.layer import SparseConvBNLIF, fold_bn
+    rng = np.random.default_rng(T + hw + cout)
+    B = 4
+    x, w, bn = L.make_config0(seed=T + hw, T=T, B=B, C=64, F=cout, H=hw, W=hw)
+    scale, bias = fold_bn(bn.gamma, bn.beta, bn.mean, bn.var)
+    layer = SparseConvBNLIF(w, scale, bias, T=T, B=B, H=hw, W=hw, neuron="none_f16")
+    assert rt.variant(layer.desc) == rt.SNN_VARIANT_HALO_RESIDENT
+    res_np, rd = None, None
+    if residual:
+        res_np = (rng.standard_normal((T, B, cout, hw, hw)) * 2).astype(np.float16).astype(np.float32)
+        rd = torch.from_numpy(to_nhwc(res_np)).to("cuda", torch.float16)
+    y = layer(torch.from_numpy(to_nhwc(x)).to("cuda", torch.float16), residual=rd)
+    torch.cuda.synchronize()
+    assert rt.device_error() == 0
+    got = from_nhwc(y.float().cpu().numpy(), T, B)
+    ref = L.fused_layer_torch(x, w.astype(np.float16).astype(np.float32), bn, pad=1, neuron="lif")
+    # BN output of the oracle: recompute without the neuron
+    import torch.nn.functional as F
+    with torch.no_grad():
+        z = F.conv2d(torch.from_numpy(x.reshape((T * B,) + x.shape[2:])),
+                     torch.from_numpy(w.astype(np.float16).astype(np.float32)), padding=1)
+        z = z * torch.from_numpy(scale)[None, :, None, None] + torch.from_numpy(bias)[None, :, None, None]
+    zr = z.numpy().reshape(T, B, cout, hw, hw)
+    if residual:
+        zr = zr + res_np
+    assert ref is not None
+    tol = 2.0 ** -10 * np.abs(zr) + 2e-3
+    assert (np.abs(got - zr) <= tol).all(), np.abs(got - zr).max()
