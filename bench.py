@@ -59,6 +59,10 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-configs", action="store_true",
                     help="skip the Spikformer / MS-ResNet / DVS configurations")
+    ap.add_argument("--profile-config", default=None,
+                    help="only run eager forwards of one configuration (sew_resnet18, "
+                         "spikformer_8_384, msresnet34, dvs_sew_resnet18) at --batch, for a "
+                         "profiler; prints nothing")
     ap.add_argument("--cpu-steps", type=int, default=5)
     return ap.parse_args()
 
@@ -457,6 +461,32 @@ def measure_config(name, batch, T, build, cpu_fn, workload, *, dev, stream, worl
     return res
 
 
+def profile_config(args):
+    """Eager forwards of one configuration on cuda:0 at ``--batch`` images
+    (``--warmup`` + ``--steps`` forwards), for ncu captures of its kernels."""
+    import torch
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    if args.profile_config == "sew_resnet18":
+        from sparsesnn_b200.sew_resnet import SEWResNet18, init_params
+        model = SEWResNet18(init_params(seed=0), T=T_STEPS, batch=args.batch, H=HW, W=HW, device=dev)
+    else:
+        build = {c[0]: c[3] for c in _other_configs()}[args.profile_config]
+        model, _ = build(dev, args.batch)
+    for k in range(2):
+        shape = model.x_ins[k].shape
+        if args.profile_config == "dvs_sew_resnet18":
+            model.x_ins[k].copy_((torch.rand(shape, device=dev) < 0.05).float())
+        else:
+            model.x_ins[k].copy_(torch.randn(shape, device=dev))
+    for _ in range(args.warmup + args.steps):
+        model.run()
+    torch.cuda.synchronize()
+    from sparsesnn_b200 import runtime as rt
+    if rt.device_error() != 0:
+        raise RuntimeError("a kernel reported a device error")
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
@@ -763,6 +793,9 @@ def main():
         os.dup2(2, 1)
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.profile_config:
+        profile_config(args)
         return
     import torch
     import torch.distributed as dist
