@@ -301,7 +301,7 @@ int ensure_init() {
   }
   for (int mode = 0; mode < 4 && e == cudaSuccess; ++mode)
     e = cudaFuncSetAttribute(stem_tcg_fn(mode), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             snn::stem_tcg_smem_bytes(snn::kStemGMaxK / 32));
+                             snn::stem_tcg_smem_max());
   if (e != cudaSuccess)
     return g_init_status = fail(SNN_E_CUDA, "smem attribute: %s", cudaGetErrorString(e));
   e = cudaFuncSetAttribute(snn::spikformer_attn_lif_kernel<32>,
@@ -1016,6 +1016,8 @@ int snn_conv_forward_tsplit(const snn_conv_desc* d, const void* data, const void
   if ((reinterpret_cast<uintptr_t>(workspace) | reinterpret_cast<uintptr_t>(out) |
        reinterpret_cast<uintptr_t>(residual)) & 15)
     return fail(SNN_E_INVALID, "workspace, out and residual must be 16-byte aligned");
+  if (reinterpret_cast<uintptr_t>(state) & 7)
+    return fail(SNN_E_INVALID, "state must be 8-byte aligned");
   // Phase 1: conv + BN of all T*B images, no neuron, fp32 into the
   // workspace.  The leading [T*B] dimension is regrouped as [T'][B'] so that
   // the general kernel keeps its four-timestep accumulators: the images are
@@ -1060,9 +1062,9 @@ int snn_conv_forward_tsplit(const snn_conv_desc* d, const void* data, const void
     case 7: k = snn::tsplit_neuron_kernel<snn::kModeIf, snn::kResAddAfter>; break;
     default: k = snn::tsplit_neuron_kernel<snn::kModeIf, snn::kResAddBefore>; break;
   }
-  const long long n = p.P * (d->Cout / 8);
+  const long long n = p.P * (d->Cout / 2);
   const long long blocks = std::max<long long>(1, std::min<long long>((n + 255) / 256,
-                                                                    static_cast<long long>(g_num_sms) * 16));
+                                                                    static_cast<long long>(g_num_sms) * 8));
   cudaError_t e = launch_pdl(k, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream, p);
   if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));
   return SNN_OK;
@@ -1126,7 +1128,7 @@ int snn_stem_forward(const snn_conv_desc* d, int32_t Tin, const float* x, const 
     }
   }
   // General tensor-core stem: any window and stride, per-timestep or
-  // repeated input, up to 64 channels and K = Cin*KH*KW <= 256.
+  // repeated input, up to 64 channels and K = Cin*KH*KW <= 192 (warp-specialised, one block per SM).
   const int Kst = d->Cin * d->KH * d->KW;
   const int TWst = std::min(OW, 128), Rst = 128 / TWst;
   const long long stage_bytes = 4LL * d->Cin * ((Rst - 1) * d->stride + d->KH) *
@@ -1139,8 +1141,7 @@ int snn_stem_forward(const snn_conv_desc* d, int32_t Tin, const float* x, const 
     const size_t smem = static_cast<size_t>(snn::stem_tcg_smem_bytes(nk));
     const long long n_tiles = static_cast<long long>(d->B) * ((OH + Rst - 1) / Rst) *
                               ((OW + TWst - 1) / TWst);
-    const int per_sm = smem <= 110 * 1024 ? 2 : 1;
-    const long long nblk = std::max<long long>(1, std::min<long long>(n_tiles, 1LL * per_sm * g_num_sms));
+    const long long nblk = std::max<long long>(1, std::min<long long>(n_tiles, g_num_sms));
     if ((reinterpret_cast<uintptr_t>(out) & 15) == 0) {
       cudaError_t e = launch_pdl(stem_tcg_fn(mode), dim3(static_cast<unsigned>(nblk)),
                                  dim3(snn::kStemGThreads), smem, stream, p);

@@ -356,21 +356,44 @@ stem_tc_kernel(const __grid_constant__ StemParams p) {
 // T steps on it) or one frame per timestep (Tin = T: one GEMM per timestep,
 // the membrane carried in registers), with a LIF/IF neuron or none (fp16 BN
 // output).  A tile is R rows x TW columns of one image's output (TW =
-// min(OW, 128), R = 128 / TW): the input window under it (every channel,
-// (R-1)*stride + KH rows, (TW-1)*stride + KW columns) is staged in shared
-// memory with coalesced loads, and the im2col k-tiles are built from there.
+// min(OW, 128), R = 128 / TW); a work unit is one tile and one GEMM (frame).
 // GEMM: D[px][co] = im2col(x)[px][k] * w[co][k], M = 128 (TMEM lanes =
 // pixels), N = 64, K in 32-wide fp32 k-tiles, 3xTF32 as in stem_tc_kernel
-// (fp32-level accuracy).  The weights' hi/lo k-tiles stay resident; the
-// im2col k-tiles are built by all 256 threads (a pixel's 32 columns split
-// between two threads) into two alternating buffers, so a k-tile's build
-// overlaps the previous one's MMAs.  Epilogue: thread = (pixel, 32 of the 64
-// channels), 16-byte stores of the pixel's channels.
-constexpr int kStemGThreads = 256;
+// (fp32-level accuracy); the weights' hi/lo k-tiles stay resident.
+//
+// Warp-specialised so that staging, im2col, MMAs and the epilogue of
+// consecutive units overlap:
+// * warps 0-3 (builders): copy the input window under unit u + 1 (every
+//   channel, (R-1)*stride + KH rows, (TW-1)*stride + KW columns) into one of
+//   two staging buffers with cp.async while they build unit u's im2col
+//   k-tiles (hi/lo, thread = pixel) into a ring of A stages;
+// * warp 12, one thread: issues the MMAs of each k-tile and alternates
+//   between two TMEM accumulators (64 columns each), so the MMAs of unit
+//   u + 1 run while the epilogue drains unit u;
+// * warps 4-11 (epilogue): thread = (pixel, 32 of the 64 channels); BN once,
+//   neuron over T (or one step per frame, or the fp16 BN output); each
+//   timestep's [pixels][Cout] fp16 tile is written into one of two shared
+//   buffers and leaves by ONE bulk copy: the tile's valid pixels are
+//   contiguous in the NHWC output (R = 1: part of a row; R > 1: TW = OW,
+//   whole rows).
+// 13 warps: at most 4 on each SM sub-partition, so 128 registers a thread.
+// Every wait is bounded; a role whose wait expires sets the error word and
+// stops, and the roles waiting on it then expire in turn.
+constexpr int kStemGThreads = 13 * 32;
+constexpr int kStemGBuild = 128;                // builder threads (warps 0-3)
+constexpr int kStemGEpi0 = 4;                   // first epilogue warp (4-11)
+constexpr int kStemGMmaWarp = 12;
 constexpr int kStemGMaxK = 192;
-constexpr int kStemGMaxStage = 20 * 1024;     // bytes of one staged input window (two alternate)
+constexpr int kStemGMaxStage = 20 * 1024;       // bytes of one staged input window (two alternate)
+constexpr int kStemGOutBytes = 128 * 64 * 2;    // one timestep's output tile
+__host__ __device__ constexpr int stem_tcg_stages(int nk) { return nk <= 5 ? 2 : 1; }
 __host__ __device__ constexpr int stem_tcg_smem_bytes(int nk) {
-  return 2 * nk * 8192 + 4 * 16384 + 2 * kStemGMaxStage + kStemGMaxK * 4 + 2 * 64 * 4 + 64 + 1024;
+  return 2 * nk * 8192 + stem_tcg_stages(nk) * 32768 + 2 * kStemGMaxStage + 2 * kStemGOutBytes +
+         kStemGMaxK * 4 + 2 * 64 * 4 + 16 * 8 + 1024;
+}
+__host__ __device__ constexpr int stem_tcg_smem_max() {
+  return stem_tcg_smem_bytes(5) > stem_tcg_smem_bytes(6) ? stem_tcg_smem_bytes(5)
+                                                         : stem_tcg_smem_bytes(6);
 }
 
 template <int MODE>
@@ -381,29 +404,36 @@ stem_tc_gen_kernel(const __grid_constant__ StemParams p) {
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int K = p.Cin * p.KH * p.KW;
   const int nk = (K + 31) / 32;
+  const int S = stem_tcg_stages(nk);
   const int TW = min(p.OW, 128), R = 128 / TW;
   const int IR = (R - 1) * p.stride + p.KH, IC = (TW - 1) * p.stride + p.KW;
   uint8_t* sBh = smem;                                   // [nk][64 ch][32] fp32, 128B swizzle
   uint8_t* sBl = sBh + nk * 8192;
-  uint8_t* sA = sBl + nk * 8192;                         // [2 buf][hi, lo][128 px][32]
-  float* xs0 = reinterpret_cast<float*>(sA + 4 * 16384); // [2][Cin][IR][IC] staged input windows
-  int* kofs = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(xs0) + 2 * kStemGMaxStage);
+  uint8_t* sA = sBl + nk * 8192;                         // [S][hi, lo][128 px][32]
+  float* xs0 = reinterpret_cast<float*>(sA + S * 32768); // [2][Cin][IR][IC] staged input windows
+  uint8_t* so = reinterpret_cast<uint8_t*>(xs0) + 2 * kStemGMaxStage;   // [2][128 px][Cout] fp16
+  int* kofs = reinterpret_cast<int*>(so + 2 * kStemGOutBytes);
   float* sc = reinterpret_cast<float*>(kofs + kStemGMaxK);
   float* bi = sc + 64;
-  uint64_t* mma_done = reinterpret_cast<uint64_t*>(bi + 64);   // [2], per A buffer
-  uint64_t* acc_full = mma_done + 2;
-  uint64_t* drain = acc_full + 1;
+  uint64_t* a_full = reinterpret_cast<uint64_t*>(bi + 64);   // [2] builders -> MMA
+  uint64_t* a_empty = a_full + 2;                             // [2] MMA -> builders
+  uint64_t* acc_full = a_empty + 2;                           // [2] MMA -> epilogue
+  uint64_t* acc_empty = acc_full + 2;                         // [2] epilogue -> MMA
+  uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
-  const int px = tid & 127, half = tid >> 7;             // pixel; column / channel half
-  const int pr = px / TW, pc = px - (px / TW) * TW;      // pixel's row and column in the tile
 
   if (tid == 0) {
-    mbar_init(&mma_done[0], 1); mbar_init(&mma_done[1], 1);
-    mbar_init(acc_full, 1); mbar_init(drain, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&a_full[i], kStemGBuild);
+      mbar_init(&a_empty[i], 1);
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 256);
+    }
+    mbar_init(drain, 1);
     fence_mbar_init();
   }
-  if (warp == 0) { tmem_alloc(tmem_slot, 64); tmem_relinquish(); }
+  if (warp == kStemGMmaWarp) { tmem_alloc(tmem_slot, 128); tmem_relinquish(); }
   // Resident weights (constant data): B[co][k] hi/lo, zero past Cout / K.
   for (int i = tid; i < nk * 64 * 32; i += kStemGThreads) {
     const int kt = i / 2048, rem = i - kt * 2048, co = rem >> 5, kk = rem & 31;
@@ -440,13 +470,11 @@ stem_tc_gen_kernel(const __grid_constant__ StemParams p) {
   const int tiles_w = (p.OW + TW - 1) / TW, tiles_h = (p.OH + R - 1) / R;
   const long long n_tiles = static_cast<long long>(p.B) * tiles_h * tiles_w;
   const int n_gemm = p.Tin > 1 ? p.T : 1;
-  const int HW = p.H * p.W;
-  const uint32_t idesc = idesc_tf32(128, 64);
-  const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
-  const int pofs = pr * p.stride * IC + pc * p.stride;   // this pixel's window origin in xs
-  // Work unit u of this block: tile blockIdx.x + (u / n_gemm) * gridDim.x,
-  // GEMM (frame) u % n_gemm.  The input window of unit u + 1 is copied into
-  // the other staging buffer (cp.async) while unit u computes.
+  // Units of this block: tile blockIdx.x + (u / n_gemm) * gridDim.x, GEMM
+  // (frame) u % n_gemm, for u < n_units.
+  const long long my_tiles =
+      blockIdx.x < n_tiles ? (n_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const long long n_units = my_tiles * n_gemm;
   auto unit_tile = [&](long long u) { return blockIdx.x + (u / n_gemm) * gridDim.x; };
   auto tile_origin = [&](long long tile, int* b, int* oh0, int* ow0) {
     const int twi = static_cast<int>(tile % tiles_w);
@@ -455,110 +483,162 @@ stem_tc_gen_kernel(const __grid_constant__ StemParams p) {
     *b = static_cast<int>(rest / tiles_h);
     *ow0 = twi * TW;
   };
-  auto stage = [&](long long u, float* dst) {
-    int b, oh0, ow0;
-    tile_origin(unit_tile(u), &b, &oh0, &ow0);
-    const int g = static_cast<int>(u % n_gemm);
-    const int ih0 = oh0 * p.stride - p.pad, iw0 = ow0 * p.stride - p.pad;
-    const float* xin = p.x + (static_cast<size_t>(g) * p.B + b) * static_cast<size_t>(p.Cin) * HW;
-    for (int row = warp; row < p.Cin * IR; row += kStemGThreads / 32) {
-      const int ci = row / IR, ih = ih0 + row - ci * IR;
-      const bool rv = ih >= 0 && ih < p.H;
-      const float* src = xin + static_cast<size_t>(ci) * HW + static_cast<size_t>(rv ? ih : 0) * p.W;
+  if (warp < kStemGEpi0) {
+    // ------------------------------------------------ builders
+    const int HW = p.H * p.W;
+    const int px = tid;                                  // pixel (TMEM lane / A row)
+    const int pr = px / TW, pc = px - (px / TW) * TW;    // pixel's row and column in the tile
+    const int pofs = pr * p.stride * IC + pc * p.stride; // this pixel's window origin
+    auto stage = [&](long long u, float* dst) {
+      int b, oh0, ow0;
+      tile_origin(unit_tile(u), &b, &oh0, &ow0);
+      const int g = static_cast<int>(u % n_gemm);
+      const int ih0 = oh0 * p.stride - p.pad, iw0 = ow0 * p.stride - p.pad;
+      const float* xin = p.x + (static_cast<size_t>(g) * p.B + b) * static_cast<size_t>(p.Cin) * HW;
+      for (int row = warp; row < p.Cin * IR; row += kStemGBuild / 32) {
+        const int ci = row / IR, ih = ih0 + row - ci * IR;
+        const bool rv = ih >= 0 && ih < p.H;
+        const float* src = xin + static_cast<size_t>(ci) * HW + static_cast<size_t>(rv ? ih : 0) * p.W;
 #pragma unroll 4
-      for (int cc = lane; cc < IC; cc += 32) {
-        const int iw = iw0 + cc;
-        const bool valid = rv && iw >= 0 && iw < p.W;
-        cp_async4(dst + row * IC + cc, valid ? src + iw : p.x, valid);
-      }
-    }
-    cp_async_commit();
-  };
-  uint32_t use[2] = {0, 0};                              // uses of each A buffer so far
-  uint32_t acc_uses = 0;
-  int issued = 0;                                        // MMAs issued by thread 0
-  bool ok = true;
-  float v[32];
-  if (blockIdx.x < n_tiles) stage(0, xs0);
-  for (long long un = 0; ok && unit_tile(un) < n_tiles; ++un) {
-    const long long tile = unit_tile(un);
-    const int g = static_cast<int>(un % n_gemm);
-    float* xs = xs0 + (un & 1) * (kStemGMaxStage / 4);
-    if (unit_tile(un + 1) < n_tiles) stage(un + 1, xs0 + ((un + 1) & 1) * (kStemGMaxStage / 4));
-    else cp_async_commit();                              // an empty group keeps the counting uniform
-    cp_async_wait<1>();                                  // this unit's window has landed
-    __syncthreads();
-    int b, oh0, ow0;
-    tile_origin(tile, &b, &oh0, &ow0);
-    const int oh = oh0 + pr, ow = ow0 + pc;
-    const bool pv = pr < R && oh < p.OH && ow < p.OW;
-    const long long pix = (static_cast<long long>(b) * p.OH + oh) * p.OW + ow;
-    if (g == 0) {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = 0.f;
-    }
-    {
-      for (int kt = 0; kt < nk; ++kt) {
-        const int buf = (use[0] + use[1]) & 1;
-        if (use[buf] > 0) {                              // the MMAs that read this buffer are done
-          const bool okw = mbar_wait_bounded(&mma_done[buf], (use[buf] - 1) & 1, p.timeout);
-          if (!okw && p.err) atomicOr(p.err, kErrTimeoutEmpty);
-          if (!__syncthreads_and(okw)) { ok = false; break; }
+        for (int cc = lane; cc < IC; cc += 32) {
+          const int iw = iw0 + cc;
+          const bool valid = rv && iw >= 0 && iw < p.W;
+          cp_async4(dst + row * IC + cc, valid ? src + iw : p.x, valid);
         }
-        uint8_t* ah = sA + buf * 32768;
+      }
+      cp_async_commit();
+    };
+    long long kc = 0;                                    // k-tiles built so far (ring position)
+    bool ok = true;
+    if (n_units > 0) stage(0, xs0);
+    for (long long un = 0; ok && un < n_units; ++un) {
+      // Every builder is done with unit un-1's window: its buffer takes unit un+1.
+      named_barrier(1, kStemGBuild);
+      if (un + 1 < n_units) stage(un + 1, xs0 + ((un + 1) & 1) * (kStemGMaxStage / 4));
+      else cp_async_commit();                            // an empty group keeps the counting uniform
+      cp_async_wait<1>();                                // this unit's window has landed
+      named_barrier(1, kStemGBuild);
+      const float* xs = xs0 + (un & 1) * (kStemGMaxStage / 4);
+      int b, oh0, ow0;
+      tile_origin(unit_tile(un), &b, &oh0, &ow0);
+      const bool pv = pr < R && oh0 + pr < p.OH && ow0 + pc < p.OW;
+      for (int kt = 0; kt < nk; ++kt, ++kc) {
+        const int s = static_cast<int>(kc % S);
+        const long long use = kc / S;
+        bool okw = true;
+        if (tid == 0 && use > 0) {                       // the MMAs that read this stage are done
+          okw = mbar_wait_bounded(&a_empty[s], static_cast<uint32_t>((use - 1) & 1), p.timeout);
+          if (!okw && p.err) atomicOr(p.err, kErrTimeoutEmpty);
+        }
+        if (named_barrier_or(1, kStemGBuild, !okw)) { ok = false; break; }
+        uint8_t* ah = sA + s * 32768;
         uint8_t* al = ah + 16384;
 #pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {                 // this thread's 16 columns, 4 at a time
+        for (int chunk = 0; chunk < 8; ++chunk) {        // the pixel's 32 columns, 4 at a time
           float hi[4], lo[4];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const int ko = kofs[kt * 32 + half * 16 + c4 * 4 + j];
+            const int ko = kofs[kt * 32 + chunk * 4 + j];
             const float xv = (pv && ko >= 0) ? xs[ko + pofs] : 0.f;
             hi[j] = to_tf32(xv);
             lo[j] = xv - hi[j];
           }
-          const int chunk = half * 4 + c4;
           const int off = px * 128 + ((chunk ^ (px & 7)) << 4);
           *reinterpret_cast<float4*>(ah + off) = make_float4(hi[0], hi[1], hi[2], hi[3]);
           *reinterpret_cast<float4*>(al + off) = make_float4(lo[0], lo[1], lo[2], lo[3]);
         }
         fence_proxy_async_smem();                        // generic writes -> tensor-core reads
-        tc_fence_before();
-        __syncthreads();
-        if (tid == 0) {
+        mbar_arrive(&a_full[s]);
+      }
+    }
+    cp_async_wait<0>();
+  } else if (warp == kStemGMmaWarp) {
+    // ------------------------------------------------ MMA issuer
+    bool issued = false;
+    if (lane == 0) {
+      const uint32_t idesc = idesc_tf32(128, 64);
+      long long kc = 0;
+      for (long long un = 0; un < n_units; ++un) {
+        const int a = static_cast<int>(un & 1);
+        if (un >= 2) {                                   // the epilogue has read this accumulator
+          if (!mbar_wait_bounded(&acc_empty[a], static_cast<uint32_t>(((un >> 1) - 1) & 1),
+                                 p.timeout)) {
+            if (p.err) atomicOr(p.err, kErrTimeoutAccEmpty);
+            break;
+          }
+        }
+        tc_fence_after();
+        const uint32_t acc = tmem + static_cast<uint32_t>(a * 64);
+        bool okk = true;
+        for (int kt = 0; kt < nk; ++kt, ++kc) {
+          const int s = static_cast<int>(kc % S);
+          if (!mbar_wait_bounded(&a_full[s], static_cast<uint32_t>((kc / S) & 1), p.timeout)) {
+            if (p.err) atomicOr(p.err, kErrTimeoutFull);
+            okk = false;
+            break;
+          }
           tc_fence_after();
+          uint8_t* ah = sA + s * 32768;
           const uint64_t dah = smem_desc_kmajor(smem_u32(ah), 1024, 2);
-          const uint64_t dal = smem_desc_kmajor(smem_u32(al), 1024, 2);
+          const uint64_t dal = smem_desc_kmajor(smem_u32(ah + 16384), 1024, 2);
           const uint64_t dbh = smem_desc_kmajor(smem_u32(sBh + kt * 8192), 1024, 2);
           const uint64_t dbl = smem_desc_kmajor(smem_u32(sBl + kt * 8192), 1024, 2);
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks) {
-            mma_tf32(tmem, dal + 2 * ks, dbh + 2 * ks, idesc, (kt > 0 || ks > 0) ? 1u : 0u);
-            mma_tf32(tmem, dah + 2 * ks, dbl + 2 * ks, idesc, 1u);
-            mma_tf32(tmem, dah + 2 * ks, dbh + 2 * ks, idesc, 1u);
+            mma_tf32(acc, dal + 2 * ks, dbh + 2 * ks, idesc, (kt > 0 || ks > 0) ? 1u : 0u);
+            mma_tf32(acc, dah + 2 * ks, dbl + 2 * ks, idesc, 1u);
+            mma_tf32(acc, dah + 2 * ks, dbh + 2 * ks, idesc, 1u);
           }
-          issued = 1;
-          mma_commit(&mma_done[buf]);
-          if (kt == nk - 1) mma_commit(acc_full);
+          issued = true;
+          mma_commit(&a_empty[s]);
         }
-        ++use[buf];
+        if (!okk) break;
+        mma_commit(&acc_full[a]);
       }
-      if (!ok) break;
-      const bool okw = mbar_wait_bounded(acc_full, acc_uses & 1, p.timeout);
-      ++acc_uses;
-      if (!okw && p.err) atomicOr(p.err, kErrTimeoutAcc);
+      // Every MMA issued has completed before TMEM is released.
+      if (issued) {
+        mma_commit(drain);
+        if (!mbar_wait_bounded(drain, 0, p.timeout) && p.err) atomicOr(p.err, kErrTimeoutDrain);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------ epilogue
+    const int et = tid - kStemGEpi0 * 32;                // 0..255
+    const int q = warp & 3, h = (warp - kStemGEpi0) >> 2;   // TMEM lane quarter; channel half
+    const int px = q * 32 + lane;
+    const int c0 = 32 * h;
+    const int nch = max(0, min(32, p.Cout - c0)) / 8;    // 16-byte chunks this thread stores
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    const int row_bytes = p.Cout * 2;
+    float v[32];
+    uint32_t out_uses = 0;                               // timestep tiles written so far
+    for (long long un = 0; un < n_units; ++un) {
+      const int a = static_cast<int>(un & 1);
+      const int g = static_cast<int>(un % n_gemm);
+      bool okw = true;
+      if (et == 0) {
+        okw = mbar_wait_bounded(&acc_full[a], static_cast<uint32_t>((un >> 1) & 1), p.timeout);
+        if (!okw && p.err) atomicOr(p.err, kErrTimeoutAcc);
+      }
+      if (named_barrier_or(2, 256, !okw)) break;
       tc_fence_after();
-      if (!__syncthreads_and(okw)) { ok = false; break; }
-      float a[32], x[32];
-      tmem_ld32(lane_base + 32 * half, a);
-#pragma unroll
-      for (int j = 0; j < 32; ++j) x[j] = fmaf(a[j], sc[32 * half + j], bi[32 * half + j]);
+      float x[32];
+      tmem_ld32(lane_base + static_cast<uint32_t>(a * 64 + c0), x);
       tc_fence_before();
-      __syncthreads();                                   // TMEM read out: the next GEMM may overwrite it
-      const int c0 = 32 * half;
-      const int nvalid = min(32, p.Cout - c0);           // channels this thread stores (multiple of 16)
+      mbar_arrive(&acc_empty[a]);                        // this accumulator may be overwritten
+#pragma unroll
+      for (int j = 0; j < 32; ++j) x[j] = fmaf(x[j], sc[c0 + j], bi[c0 + j]);
+      if (g == 0) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = 0.f;
+      }
+      int b, oh0, ow0;
+      tile_origin(unit_tile(un), &b, &oh0, &ow0);
+      const int npix = R == 1 ? min(TW, p.OW - ow0) : min(R, p.OH - oh0) * p.OW;
+      const long long pix0 = (static_cast<long long>(b) * p.OH + oh0) * p.OW + ow0;
       const int t_first = p.Tin > 1 ? g : 0, t_last = p.Tin > 1 ? g : p.T - 1;
-      for (int t = t_first; t <= t_last && pv && nvalid > 0; ++t) {
+      for (int t = t_first; t <= t_last; ++t, ++out_uses) {
         uint32_t w[16];
 #pragma unroll
         for (int q2 = 0; q2 < 16; ++q2) {
@@ -575,24 +655,39 @@ stem_tc_gen_kernel(const __grid_constant__ StemParams p) {
           }
           w[q2] = bits;
         }
-        uint4* dst = reinterpret_cast<uint4*>(p.out + (static_cast<size_t>(t) * P + pix) * p.Cout + c0);
+        uint8_t* ob = so + (out_uses & 1) * kStemGOutBytes;
+        // The bulk copy that last read this buffer (two tiles ago) is done reading.
+        if (et == 0) bulk_wait_group_read<1>();
+        named_barrier(2, 256);
+        // 16-byte chunks in a lane-rotated order: fewer threads of a warp meet in one bank.
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-          if (8 * q < nvalid) dst[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+        for (int i = 0; i < 4; ++i) {
+          const int c = (i + lane) & 3;
+          if (c < nch) {
+            uint32_t w0 = w[0], w1 = w[1], w2 = w[2], w3 = w[3];
+            if (c == 1) { w0 = w[4]; w1 = w[5]; w2 = w[6]; w3 = w[7]; }
+            if (c == 2) { w0 = w[8]; w1 = w[9]; w2 = w[10]; w3 = w[11]; }
+            if (c == 3) { w0 = w[12]; w1 = w[13]; w2 = w[14]; w3 = w[15]; }
+            *reinterpret_cast<uint4*>(ob + px * row_bytes + (c0 + 8 * c) * 2) =
+                make_uint4(w0, w1, w2, w3);
+          }
+        }
+        fence_proxy_async_smem();                        // generic writes -> bulk-copy reads
+        named_barrier(2, 256);
+        if (et == 0) {                                   // npix >= 1: one group per timestep tile
+          bulk_store_1d(p.out + (static_cast<size_t>(t) * P + pix0) * p.Cout, ob,
+                        static_cast<uint32_t>(npix) * row_bytes);
+          bulk_commit_group();
+        }
       }
     }
-  }
-  cp_async_wait<0>();
-  // Every MMA issued has completed before TMEM is released.
-  if (tid == 0 && issued) {
-    mma_commit(drain);
-    if (!mbar_wait_bounded(drain, 0, p.timeout) && p.err) atomicOr(p.err, kErrTimeoutDrain);
+    if (et == 0) bulk_wait_group<0>();                   // stores complete before the block exits
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == kStemGMmaWarp) {
     tc_fence_after();
-    tmem_dealloc(tmem, 64);
+    tmem_dealloc(tmem, 128);
   }
 }
 
@@ -744,12 +839,16 @@ glue_neuron_kernel(const GlueParams p) {
 // ------------------------------------------------ timestep-split neuron scan
 // Second phase of the timestep-split fused layer (snn_conv_forward_tsplit):
 // the first phase ran the conv + BN for all T*B images at once (no neuron,
-// fp32 BN output z); here thread = (pixel, 8 channels) runs the neuron over
+// fp32 BN output z); here thread = (pixel, 2 channels) runs the neuron over
 // T with the membrane in registers, adds the residual (after the neuron: the
 // SEW add; before it: the neuron integrates bn + residual) and writes fp16
-// spikes.  The arithmetic is the fused epilogue's (for tau = 2 the input is
-// halved exactly, as there), so the spikes equal the one-pass layer's for
-// the same BN outputs.
+// spikes.  The layers this form serves have few neurons per timestep (a
+// 4x4x512 DVS stage-4 map is 32k), so a thread owns only two of them, and
+// the loads of kTsplitBatch timesteps are issued together before their
+// neuron steps run, keeping that many HBM round trips in flight per thread.
+// The arithmetic is the fused epilogue's (for tau = 2 the input is halved
+// exactly, as there), so the spikes equal the one-pass layer's for the same
+// BN outputs.
 struct TsplitParams {
   const float* z;          // [T][P][C] BN output
   const __half* residual;  // [T][P][C] or null
@@ -759,43 +858,51 @@ struct TsplitParams {
   int T, C, flags;
   float tau, decay, v_th, v_reset;
 };
+constexpr int kTsplitBatch = 8;
 
 template <int MODE, int RM>
 __global__ void __launch_bounds__(256)
 tsplit_neuron_kernel(const TsplitParams p) {
   pdl_launch_dependents();
   pdl_wait();
-  const int c8n = p.C / 8;
-  const long long n = p.P * c8n;
+  const int c2n = p.C / 2;
+  const long long n = p.P * c2n;
+  const size_t plane = static_cast<size_t>(p.P) * p.C;     // elements per timestep
   for (long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; idx < n;
        idx += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const long long pix = idx / c8n;
-    const int c8 = static_cast<int>(idx - pix * c8n);
-    const size_t base = static_cast<size_t>(pix) * p.C + c8 * 8;
-    float v[8];
+    const size_t base = static_cast<size_t>(idx) * 2;       // = pixel * C + 2 * (channel pair)
+    float v[2];
+    if (p.flags & kReadState) {
+      const float2 s2 = *reinterpret_cast<const float2*>(p.state + base);
+      v[0] = s2.x; v[1] = s2.y;
+    } else {
+      v[0] = v[1] = 0.f;
+    }
+    for (int t0 = 0; t0 < p.T; t0 += kTsplitBatch) {
+      float2 zb[kTsplitBatch];
+      __half2 rb[kTsplitBatch];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = (p.flags & kReadState) ? p.state[base + j] : 0.f;
-    for (int t = 0; t < p.T; ++t) {
-      const size_t off = static_cast<size_t>(t) * p.P * p.C + base;
-      const float4 za = __ldg(reinterpret_cast<const float4*>(p.z + off));
-      const float4 zb = __ldg(reinterpret_cast<const float4*>(p.z + off) + 1);
-      float x[8] = {za.x, za.y, za.z, za.w, zb.x, zb.y, zb.z, zb.w};
-      uint4 r4 = make_uint4(0, 0, 0, 0);
-      if constexpr (RM != kResNone) r4 = __ldg(reinterpret_cast<const uint4*>(p.residual + off));
-      const __half2* rh = reinterpret_cast<const __half2*>(&r4);
-      uint32_t w[4];
+      for (int j = 0; j < kTsplitBatch; ++j) {
+        if (t0 + j < p.T) {
+          const size_t off = static_cast<size_t>(t0 + j) * plane + base;
+          zb[j] = __ldg(reinterpret_cast<const float2*>(p.z + off));
+          if constexpr (RM != kResNone) rb[j] = __ldg(reinterpret_cast<const __half2*>(p.residual + off));
+        }
+      }
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const float2 rf = __half22float2(rh[u]);
+      for (int j = 0; j < kTsplitBatch; ++j) {
+        if (t0 + j >= p.T) break;
+        float2 rf = make_float2(0.f, 0.f);
+        if constexpr (RM != kResNone) rf = __half22float2(rb[j]);
         uint32_t bits = 0;
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          const int j = 2 * u + e;
+          const float x = e ? zb[j].y : zb[j].x;
           const float r = e ? rf.y : rf.x;
           // kModeLifHalf takes bn/2 (exact), plus r/2 when the residual enters the neuron.
-          float xi = MODE == kModeLifHalf ? x[j] * 0.5f : x[j];
+          float xi = MODE == kModeLifHalf ? x * 0.5f : x;
           if constexpr (RM == kResAddBefore) xi = __fadd_rn(xi, MODE == kModeLifHalf ? r * 0.5f : r);
-          const bool s = neuron_step<MODE>(v[j], xi, p.decay, p.tau, p.v_th, p.v_reset);
+          const bool s = neuron_step<MODE>(v[e], xi, p.decay, p.tau, p.v_th, p.v_reset);
           if constexpr (RM == kResAddAfter) {
             bits |= static_cast<uint32_t>(__half_as_ushort(__float2half_rn((s ? 1.f : 0.f) + r)))
                     << (16 * e);
@@ -803,14 +910,10 @@ tsplit_neuron_kernel(const TsplitParams p) {
             bits |= (s ? 0x3C00u : 0u) << (16 * e);
           }
         }
-        w[u] = bits;
+        *reinterpret_cast<uint32_t*>(p.out + static_cast<size_t>(t0 + j) * plane + base) = bits;
       }
-      *reinterpret_cast<uint4*>(p.out + off) = make_uint4(w[0], w[1], w[2], w[3]);
     }
-    if (p.flags & kWriteState) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) p.state[base + j] = v[j];
-    }
+    if (p.flags & kWriteState) *reinterpret_cast<float2*>(p.state + base) = make_float2(v[0], v[1]);
   }
 }
 

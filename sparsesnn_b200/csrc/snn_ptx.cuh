@@ -125,6 +125,13 @@ __device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void*
         "r"(c0), "r"(c1), "r"(c2), "r"(c3)
       : "memory");
 }
+// Shared -> global copy of `bytes` contiguous bytes (both addresses 16-byte
+// aligned, bytes a multiple of 16), tracked by this thread's bulk groups.
+__device__ __forceinline__ void bulk_store_1d(void* gdst, const void* ssrc, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
+               ::"l"(reinterpret_cast<uint64_t>(gdst)), "r"(smem_u32(ssrc)), "r"(bytes)
+               : "memory");
+}
 __device__ __forceinline__ void bulk_commit_group() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
