@@ -365,9 +365,10 @@ size_t meta_offset(const Geometry& g) {
 }
 
 int encode(CUtensorMap* map, int rank, const void* base, const cuuint64_t* dims,
-           const cuuint64_t* strides_bytes, const cuuint32_t* box, CUtensorMapSwizzle swz) {
+           const cuuint64_t* strides_bytes, const cuuint32_t* box, CUtensorMapSwizzle swz,
+           CUtensorMapDataType dtype = CU_TENSOR_MAP_DATA_TYPE_FLOAT16) {
   cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, rank, const_cast<void*>(base), dims,
+  CUresult r = g_encode(map, dtype, rank, const_cast<void*>(base), dims,
                         strides_bytes, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(SNN_E_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
@@ -1131,9 +1132,34 @@ int snn_stem_forward(const snn_conv_desc* d, int32_t Tin, const float* x, const 
   // repeated input, up to 64 channels and K = Cin*KH*KW <= 192 (warp-specialised, one block per SM).
   const int Kst = d->Cin * d->KH * d->KW;
   const int TWst = std::min(OW, 128), Rst = 128 / TWst;
-  const long long stage_bytes = 4LL * d->Cin * ((Rst - 1) * d->stride + d->KH) *
-                                ((TWst - 1) * d->stride + d->KW);
-  if (d->Cout <= 64 && Kst <= snn::kStemGMaxK && stage_bytes <= snn::kStemGMaxStage) {
+  const int IRst = (Rst - 1) * d->stride + d->KH, ICst = (TWst - 1) * d->stride + d->KW;
+  // Input windows by TMA where the fp32 rows allow it (16-byte row pitch, W % 4
+  // == 0): the box starts at the window's first column rounded down to 16
+  // bytes, so it is up to 3 columns wider, rounded up to 16 bytes.
+  const int ICp = (ICst + 6) & ~3;
+  const bool tma_in = d->W % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 && ICp <= 256 &&
+                      IRst <= 256 && d->Cin <= 256 &&
+                      4LL * d->Cin * IRst * ICp <= snn::kStemGMaxStage;
+  const long long stage_bytes = 4LL * d->Cin * IRst * (tma_in ? ICp : ICst);
+  const long long units = static_cast<long long>(d->B) * ((OH + Rst - 1) / Rst) *
+                          ((OW + TWst - 1) / TWst) * (Tin > 1 ? d->T : 1);
+  if (d->Cout <= 64 && Kst <= snn::kStemGMaxK && stage_bytes <= snn::kStemGMaxStage &&
+      units < 0x7fffffffLL) {
+    p.in_pitch = tma_in ? ICp : ICst;
+    if (tma_in) {
+      const cuuint64_t idims[5] = {static_cast<cuuint64_t>(d->W), static_cast<cuuint64_t>(d->H),
+                                   static_cast<cuuint64_t>(d->Cin), static_cast<cuuint64_t>(d->B),
+                                   static_cast<cuuint64_t>(Tin)};
+      const cuuint64_t row = static_cast<cuuint64_t>(d->W) * 4;
+      const cuuint64_t istrides[4] = {row, row * d->H, row * d->H * d->Cin,
+                                      row * d->H * d->Cin * d->B};
+      const cuuint32_t ibox[5] = {static_cast<cuuint32_t>(ICp), static_cast<cuuint32_t>(IRst),
+                                  static_cast<cuuint32_t>(d->Cin), 1, 1};
+      if ((st = encode(&p.tmap_in, 5, x, idims, istrides, ibox, CU_TENSOR_MAP_SWIZZLE_NONE,
+                       CU_TENSOR_MAP_DATA_TYPE_FLOAT32)))
+        return st;
+      p.tma_in = 1;
+    }
     const int mode = d->neuron == SNN_NEURON_NONE ? snn::kModeNone
                      : d->neuron == SNN_NEURON_IF ? snn::kModeIf
                      : d->tau == 2.0f ? snn::kModeLifHalf : snn::kModeLifDiv;

@@ -14,6 +14,7 @@ namespace snn {
 
 struct StemParams {
   CUtensorMap tmap_out;  // tensor-core path: spikes (64 ch, OW, OH, B, T), box {64, OW, rows, 1, 1}
+  CUtensorMap tmap_in;   // general tensor-core path: x as (W, H, Cin, B, Tin) fp32, box {ICp, IR, Cin, 1, 1}
   const float* x;      // [Tin][B][Cin][H][W] fp32
   const float* w;      // [Cout][Cin][KH][KW] fp32
   const float* scale;  // [Cout]
@@ -24,6 +25,8 @@ struct StemParams {
   unsigned* err;                  // device error word (tensor-core path)
   unsigned long long timeout;     // bounded-wait budget, SM cycles
   int tma_out;                    // tensor-core path: spike tiles leave by TMA stores
+  int tma_in;                     // general tensor-core path: input windows arrive by TMA
+  int in_pitch;                   // general path: staged row pitch (ICp with TMA, else IC)
 };
 
 // One thread = one output pixel x 16 consecutive output channels
@@ -358,31 +361,36 @@ stem_tc_kernel(const __grid_constant__ StemParams p) {
 // output).  A tile is R rows x TW columns of one image's output (TW =
 // min(OW, 128), R = 128 / TW); a work unit is one tile and one GEMM (frame).
 // GEMM: D[px][co] = im2col(x)[px][k] * w[co][k], M = 128 (TMEM lanes =
-// pixels), N = 64, K in 32-wide fp32 k-tiles, 3xTF32 as in stem_tc_kernel
-// (fp32-level accuracy); the weights' hi/lo k-tiles stay resident.
+// pixels), K in 32-wide fp32 k-tiles, split into tf32 hi + lo parts on both
+// sides (fp32-level accuracy): the resident weight k-tile holds the hi rows
+// and then the lo rows, so ONE N = 128 MMA per 8-wide K step and A part
+// gives x_a * [w_hi | w_lo]; two such MMAs (A = x_hi, x_lo) accumulate all
+// four products, D[:, co] + D[:, 64 + co] being the full product.
 //
-// Warp-specialised so that staging, im2col, MMAs and the epilogue of
-// consecutive units overlap:
-// * warps 0-3 (builders): copy the input window under unit u + 1 (every
-//   channel, (R-1)*stride + KH rows, (TW-1)*stride + KW columns) into one of
-//   two staging buffers with cp.async while they build unit u's im2col
-//   k-tiles (hi/lo, thread = pixel) into a ring of A stages;
-// * warp 12, one thread: issues the MMAs of each k-tile and alternates
-//   between two TMEM accumulators (64 columns each), so the MMAs of unit
-//   u + 1 run while the epilogue drains unit u;
-// * warps 4-11 (epilogue): thread = (pixel, 32 of the 64 channels); BN once,
+// Two warp groups, so that the im2col work of one unit overlaps the
+// epilogue of the previous one:
+// * warps 0-7 (builders): the input window under a unit (every channel,
+//   (R-1)*stride + KH rows, (TW-1)*stride + KW columns) arrives in one of two
+//   staging buffers -- one TMA box issued a unit ahead (fp32 rows with a
+//   16-byte aligned pitch; the window's first column sits dx in), or
+//   cp.async copies where the rows' pitch rules TMA out; the builders expand
+//   it into im2col k-tiles (hi/lo, a pixel's 32 columns split between two
+//   threads) in a ring of two A stages, meet at a named barrier per k-tile,
+//   and thread 0 then issues that k-tile's 8 MMAs into one of two TMEM
+//   accumulators (128 columns each);
+// * warps 8-15 (epilogue): thread = (pixel, 32 of the 64 channels); BN once,
 //   neuron over T (or one step per frame, or the fp16 BN output); each
 //   timestep's [pixels][Cout] fp16 tile is written into one of two shared
-//   buffers and leaves by ONE bulk copy: the tile's valid pixels are
-//   contiguous in the NHWC output (R = 1: part of a row; R > 1: TW = OW,
-//   whole rows).
-// 13 warps: at most 4 on each SM sub-partition, so 128 registers a thread.
-// Every wait is bounded; a role whose wait expires sets the error word and
-// stops, and the roles waiting on it then expire in turn.
-constexpr int kStemGThreads = 13 * 32;
-constexpr int kStemGBuild = 128;                // builder threads (warps 0-3)
-constexpr int kStemGEpi0 = 4;                   // first epilogue warp (4-11)
-constexpr int kStemGMmaWarp = 12;
+//   buffers; the two warps of a TMEM lane quarter (32 pixels, both channel
+//   halves) meet at their own named barrier and send their 32 pixels by one
+//   bulk copy: a tile's valid pixels are contiguous in the NHWC output
+//   (R = 1: part of a row; R > 1: TW = OW, whole rows).
+// 16 warps, 4 per SM sub-partition: 128 registers a thread.  Every wait is
+// bounded; a group whose wait expires sets the error word and stops, and the
+// group waiting on it then expires in turn.
+constexpr int kStemGThreads = 16 * 32;
+constexpr int kStemGBuild = 256;                // builder threads (warps 0-7)
+constexpr int kStemGEpi0 = 8;                   // first epilogue warp (8-15)
 constexpr int kStemGMaxK = 192;
 constexpr int kStemGMaxStage = 20 * 1024;       // bytes of one staged input window (two alternate)
 constexpr int kStemGOutBytes = 128 * 64 * 2;    // one timestep's output tile
@@ -396,6 +404,23 @@ __host__ __device__ constexpr int stem_tcg_smem_max() {
                                                          : stem_tcg_smem_bytes(6);
 }
 
+// Two channels of the stem epilogue: the neuron step of each (membrane v[j],
+// input x[j], tau = 2 input pre-halved) as fp16 spikes, or the fp16 BN output.
+template <int MODE>
+__device__ __forceinline__ uint32_t stem_pack2(float (&v)[32], const float (&x)[32], int j,
+                                               const StemParams& p) {
+  float2 f;
+  if constexpr (MODE == kModeNone) {
+    f = make_float2(x[j], x[j + 1]);
+  } else {
+    // Spikes as 0.0 / 1.0 floats, converted in pairs (exact).
+    f.x = neuron_step<MODE>(v[j], x[j], p.decay, p.tau, p.v_th, p.v_reset) ? 1.f : 0.f;
+    f.y = neuron_step<MODE>(v[j + 1], x[j + 1], p.decay, p.tau, p.v_th, p.v_reset) ? 1.f : 0.f;
+  }
+  const __half2 hv = __float22half2_rn(f);
+  return *reinterpret_cast<const uint32_t*>(&hv);
+}
+
 template <int MODE>
 __global__ void __launch_bounds__(kStemGThreads, 1)
 stem_tc_gen_kernel(const __grid_constant__ StemParams p) {
@@ -407,48 +432,49 @@ stem_tc_gen_kernel(const __grid_constant__ StemParams p) {
   const int S = stem_tcg_stages(nk);
   const int TW = min(p.OW, 128), R = 128 / TW;
   const int IR = (R - 1) * p.stride + p.KH, IC = (TW - 1) * p.stride + p.KW;
-  uint8_t* sBh = smem;                                   // [nk][64 ch][32] fp32, 128B swizzle
-  uint8_t* sBl = sBh + nk * 8192;
-  uint8_t* sA = sBl + nk * 8192;                         // [S][hi, lo][128 px][32]
-  float* xs0 = reinterpret_cast<float*>(sA + S * 32768); // [2][Cin][IR][IC] staged input windows
-  uint8_t* so = reinterpret_cast<uint8_t*>(xs0) + 2 * kStemGMaxStage;   // [2][128 px][Cout] fp16
+  const int XP = p.in_pitch;                             // staged row pitch (floats)
+  uint8_t* sB = smem;                                    // [nk][hi 64 ch, lo 64 ch][32] fp32, 128B swizzle
+  uint8_t* sA = sB + nk * 16384;                         // [S][hi, lo][128 px][32]
+  float* xs0 = reinterpret_cast<float*>(sA + S * 32768); // [2][Cin][IR][XP] staged input windows
+  uint8_t* so = reinterpret_cast<uint8_t*>(xs0) + 2 * kStemGMaxStage;   // [2][4 quarters][32 px][Cout] fp16
   int* kofs = reinterpret_cast<int*>(so + 2 * kStemGOutBytes);
   float* sc = reinterpret_cast<float*>(kofs + kStemGMaxK);
   float* bi = sc + 64;
-  uint64_t* a_full = reinterpret_cast<uint64_t*>(bi + 64);   // [2] builders -> MMA
-  uint64_t* a_empty = a_full + 2;                             // [2] MMA -> builders
+  uint64_t* a_empty = reinterpret_cast<uint64_t*>(bi + 64);   // [2] MMAs done with an A stage
   uint64_t* acc_full = a_empty + 2;                           // [2] MMA -> epilogue
   uint64_t* acc_empty = acc_full + 2;                         // [2] epilogue -> MMA
-  uint64_t* drain = acc_empty + 2;
+  uint64_t* in_full = acc_empty + 2;                          // [2] staged window landed (TMA)
+  uint64_t* drain = in_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
 
   if (tid == 0) {
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&a_full[i], kStemGBuild);
       mbar_init(&a_empty[i], 1);
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], 256);
+      mbar_init(&in_full[i], 1);
     }
     mbar_init(drain, 1);
     fence_mbar_init();
+    if (p.tma_in) prefetch_tmap(&p.tmap_in);
   }
-  if (warp == kStemGMmaWarp) { tmem_alloc(tmem_slot, 128); tmem_relinquish(); }
+  if (warp == 0) { tmem_alloc(tmem_slot, 256); tmem_relinquish(); }
   // Resident weights (constant data): B[co][k] hi/lo, zero past Cout / K.
   for (int i = tid; i < nk * 64 * 32; i += kStemGThreads) {
     const int kt = i / 2048, rem = i - kt * 2048, co = rem >> 5, kk = rem & 31;
     const int k = kt * 32 + kk;
     const float wv = (co < p.Cout && k < K) ? __ldg(p.w + static_cast<size_t>(co) * K + k) : 0.f;
     const float hi = to_tf32(wv);
-    *reinterpret_cast<float*>(sBh + kt * 8192 + sw128_f32(co, kk)) = hi;
-    *reinterpret_cast<float*>(sBl + kt * 8192 + sw128_f32(co, kk)) = wv - hi;
+    *reinterpret_cast<float*>(sB + kt * 16384 + sw128_f32(co, kk)) = hi;
+    *reinterpret_cast<float*>(sB + kt * 16384 + 8192 + sw128_f32(co, kk)) = wv - hi;
   }
   // Column k = (ci*KH + kh)*KW + kw (the [Cout][Cin][KH][KW] weight order)
-  // reads staged element kofs[k] + (pixel row * stride) * IC + pixel col * stride.
+  // reads staged element kofs[k] + (pixel row * stride) * XP + pixel col * stride.
   for (int k = tid; k < nk * 32; k += kStemGThreads) {
     if (k < K) {
       const int ci = k / (p.KH * p.KW), r = k - ci * p.KH * p.KW, kh = r / p.KW, kw = r - kh * p.KW;
-      kofs[k] = (ci * IR + kh) * IC + kw;
+      kofs[k] = (ci * IR + kh) * XP + kw;
     } else {
       kofs[k] = -1;                                      // padding column: zero
     }
@@ -468,31 +494,46 @@ stem_tc_gen_kernel(const __grid_constant__ StemParams p) {
 
   const long long P = static_cast<long long>(p.B) * p.OH * p.OW;
   const int tiles_w = (p.OW + TW - 1) / TW, tiles_h = (p.OH + R - 1) / R;
-  const long long n_tiles = static_cast<long long>(p.B) * tiles_h * tiles_w;
+  // 32-bit unit arithmetic: the host keeps B * tiles * frames below 2^31.
+  const int n_tiles = p.B * tiles_h * tiles_w;
   const int n_gemm = p.Tin > 1 ? p.T : 1;
   // Units of this block: tile blockIdx.x + (u / n_gemm) * gridDim.x, GEMM
   // (frame) u % n_gemm, for u < n_units.
-  const long long my_tiles =
-      blockIdx.x < n_tiles ? (n_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-  const long long n_units = my_tiles * n_gemm;
-  auto unit_tile = [&](long long u) { return blockIdx.x + (u / n_gemm) * gridDim.x; };
-  auto tile_origin = [&](long long tile, int* b, int* oh0, int* ow0) {
-    const int twi = static_cast<int>(tile % tiles_w);
-    const long long rest = tile / tiles_w;
-    *oh0 = static_cast<int>(rest % tiles_h) * R;
-    *b = static_cast<int>(rest / tiles_h);
-    *ow0 = twi * TW;
+  const int bx = static_cast<int>(blockIdx.x), gx = static_cast<int>(gridDim.x);
+  const int my_tiles = bx < n_tiles ? (n_tiles - 1 - bx) / gx + 1 : 0;
+  const int n_units = my_tiles * n_gemm;
+  auto unit_tile = [&](int u) { return bx + (u / n_gemm) * gx; };
+  auto tile_origin = [&](int tile, int* b, int* oh0, int* ow0) {
+    const int rest = tile / tiles_w;
+    *ow0 = (tile - rest * tiles_w) * TW;
+    const int bb = rest / tiles_h;
+    *oh0 = (rest - bb * tiles_h) * R;
+    *b = bb;
   };
   if (warp < kStemGEpi0) {
-    // ------------------------------------------------ builders
+    // ------------------------------------------------ builders + MMA issue
     const int HW = p.H * p.W;
-    const int px = tid;                                  // pixel (TMEM lane / A row)
+    const int px = tid & 127, half = tid >> 7;           // pixel; column half of each k-tile
     const int pr = px / TW, pc = px - (px / TW) * TW;    // pixel's row and column in the tile
-    const int pofs = pr * p.stride * IC + pc * p.stride; // this pixel's window origin
-    auto stage = [&](long long u, float* dst) {
+    const int pofs = pr * p.stride * XP + pc * p.stride; // this pixel's window origin
+    const uint32_t in_bytes = static_cast<uint32_t>(XP) * IR * p.Cin * 4;
+    // TMA (thread 0): unit u's window into buffer u & 1, its first column
+    // rounded down to a 16-byte boundary (negative coordinates read zero).
+    auto load_window = [&](int u) {
       int b, oh0, ow0;
       tile_origin(unit_tile(u), &b, &oh0, &ow0);
-      const int g = static_cast<int>(u % n_gemm);
+      const int g = u % n_gemm;
+      const int iw0 = ow0 * p.stride - p.pad;
+      fence_proxy_async_smem();
+      mbar_arrive_expect_tx(&in_full[u & 1], in_bytes);
+      tma_load_5d(xs0 + (u & 1) * (kStemGMaxStage / 4), &p.tmap_in, &in_full[u & 1], iw0 & ~3,
+                  oh0 * p.stride - p.pad, 0, b, g);
+    };
+    // cp.async (all builders): unit u's window, rows of pitch XP = IC.
+    auto stage_window = [&](int u, float* dst) {
+      int b, oh0, ow0;
+      tile_origin(unit_tile(u), &b, &oh0, &ow0);
+      const int g = u % n_gemm;
       const int ih0 = oh0 * p.stride - p.pad, iw0 = ow0 * p.stride - p.pad;
       const float* xin = p.x + (static_cast<size_t>(g) * p.B + b) * static_cast<size_t>(p.Cin) * HW;
       for (int row = warp; row < p.Cin * IR; row += kStemGBuild / 32) {
@@ -503,128 +544,146 @@ stem_tc_gen_kernel(const __grid_constant__ StemParams p) {
         for (int cc = lane; cc < IC; cc += 32) {
           const int iw = iw0 + cc;
           const bool valid = rv && iw >= 0 && iw < p.W;
-          cp_async4(dst + row * IC + cc, valid ? src + iw : p.x, valid);
+          cp_async4(dst + row * XP + cc, valid ? src + iw : p.x, valid);
         }
       }
       cp_async_commit();
     };
-    long long kc = 0;                                    // k-tiles built so far (ring position)
-    bool ok = true;
-    if (n_units > 0) stage(0, xs0);
-    for (long long un = 0; ok && un < n_units; ++un) {
-      // Every builder is done with unit un-1's window: its buffer takes unit un+1.
-      named_barrier(1, kStemGBuild);
-      if (un + 1 < n_units) stage(un + 1, xs0 + ((un + 1) & 1) * (kStemGMaxStage / 4));
-      else cp_async_commit();                            // an empty group keeps the counting uniform
-      cp_async_wait<1>();                                // this unit's window has landed
-      named_barrier(1, kStemGBuild);
-      const float* xs = xs0 + (un & 1) * (kStemGMaxStage / 4);
+    const uint32_t idesc = idesc_tf32(128, 128);
+    int kc = 0;                                          // k-tiles built so far (ring position)
+    int requested = 0, waited = 0;                       // TMA windows (thread 0 issues)
+    bool ok = true, ok0 = true, issued = false;          // ok0, issued: thread 0 (MMA issuer)
+    if (n_units > 0) {
+      if (!p.tma_in) stage_window(0, xs0);
+      else if (tid == 0) { load_window(0); requested = 1; }
+    }
+    for (int un = 0; ok && un < n_units; ++un) {
+      // Every builder passed the previous unit's last k-tile barrier, so the
+      // buffer of unit un - 1 is free for unit un + 1.
+      bool okw = true;
+      if (p.tma_in) {
+        if (tid == 0 && un + 1 < n_units) { load_window(un + 1); requested = un + 2; }
+        okw = mbar_wait_bounded_sleep(&in_full[un & 1], static_cast<uint32_t>((un >> 1) & 1), p.timeout);
+        waited = un + 1;
+        if (!okw && p.err) atomicOr(p.err, kErrTimeoutFull);
+      } else {
+        if (un + 1 < n_units) stage_window(un + 1, xs0 + ((un + 1) & 1) * (kStemGMaxStage / 4));
+        else cp_async_commit();                          // an empty group keeps the counting uniform
+        cp_async_wait<1>();                              // this unit's window has landed
+        named_barrier(1, kStemGBuild);
+      }
       int b, oh0, ow0;
       tile_origin(unit_tile(un), &b, &oh0, &ow0);
+      const int iw0 = ow0 * p.stride - p.pad;
+      const float* xs = xs0 + (un & 1) * (kStemGMaxStage / 4) + (p.tma_in ? iw0 - (iw0 & ~3) : 0);
       const bool pv = pr < R && oh0 + pr < p.OH && ow0 + pc < p.OW;
+      const int a = un & 1;
       for (int kt = 0; kt < nk; ++kt, ++kc) {
-        const int s = static_cast<int>(kc % S);
-        const long long use = kc / S;
-        bool okw = true;
-        if (tid == 0 && use > 0) {                       // the MMAs that read this stage are done
-          okw = mbar_wait_bounded(&a_empty[s], static_cast<uint32_t>((use - 1) & 1), p.timeout);
-          if (!okw && p.err) atomicOr(p.err, kErrTimeoutEmpty);
+        const int s = kc % S;
+        const int use = kc / S;
+        bool okk = okw;
+        if (okk && use > 0) {                            // the MMAs that read this stage are done
+          okk = mbar_wait_bounded_sleep(&a_empty[s], static_cast<uint32_t>((use - 1) & 1), p.timeout);
+          if (!okk && p.err) atomicOr(p.err, kErrTimeoutEmpty);
         }
-        if (named_barrier_or(1, kStemGBuild, !okw)) { ok = false; break; }
-        uint8_t* ah = sA + s * 32768;
-        uint8_t* al = ah + 16384;
+        if (okk) {
+          // This thread's 16 columns: their window offsets (4 vector loads),
+          // then all 16 values, then the hi/lo split and the stores.
+          int ko[16];
 #pragma unroll
-        for (int chunk = 0; chunk < 8; ++chunk) {        // the pixel's 32 columns, 4 at a time
-          float hi[4], lo[4];
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int ko = kofs[kt * 32 + chunk * 4 + j];
-            const float xv = (pv && ko >= 0) ? xs[ko + pofs] : 0.f;
-            hi[j] = to_tf32(xv);
-            lo[j] = xv - hi[j];
+          for (int c4 = 0; c4 < 4; ++c4) {
+            const int4 k4 = *reinterpret_cast<const int4*>(kofs + kt * 32 + half * 16 + c4 * 4);
+            ko[4 * c4] = k4.x; ko[4 * c4 + 1] = k4.y; ko[4 * c4 + 2] = k4.z; ko[4 * c4 + 3] = k4.w;
           }
-          const int off = px * 128 + ((chunk ^ (px & 7)) << 4);
-          *reinterpret_cast<float4*>(ah + off) = make_float4(hi[0], hi[1], hi[2], hi[3]);
-          *reinterpret_cast<float4*>(al + off) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+          float xv[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) xv[j] = (pv && ko[j] >= 0) ? xs[ko[j] + pofs] : 0.f;
+          uint8_t* ah = sA + s * 32768;
+          uint8_t* al = ah + 16384;
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4) {
+            float hi[4], lo[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              hi[j] = to_tf32(xv[4 * c4 + j]);
+              lo[j] = xv[4 * c4 + j] - hi[j];
+            }
+            const int chunk = half * 4 + c4;
+            const int off = px * 128 + ((chunk ^ (px & 7)) << 4);
+            *reinterpret_cast<float4*>(ah + off) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+            *reinterpret_cast<float4*>(al + off) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+          }
         }
         fence_proxy_async_smem();                        // generic writes -> tensor-core reads
-        mbar_arrive(&a_full[s]);
+        if (named_barrier_or(1, kStemGBuild, !okk || !ok0)) { ok = false; break; }
+        if (tid == 0) {
+          if (kt == 0 && un >= 2) {                      // the epilogue has read this accumulator
+            ok0 = mbar_wait_bounded_sleep(&acc_empty[a], static_cast<uint32_t>(((un >> 1) - 1) & 1),
+                                          p.timeout);
+            if (!ok0 && p.err) atomicOr(p.err, kErrTimeoutAccEmpty);
+          }
+          if (ok0) {
+            tc_fence_after();
+            const uint32_t acc = tmem + static_cast<uint32_t>(a * 128);
+            uint8_t* ah = sA + s * 32768;
+            const uint64_t dah = smem_desc_kmajor(smem_u32(ah), 1024, 2);
+            const uint64_t dal = smem_desc_kmajor(smem_u32(ah + 16384), 1024, 2);
+            const uint64_t db = smem_desc_kmajor(smem_u32(sB + kt * 16384), 1024, 2);
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+              mma_tf32(acc, dah + 2 * ks, db + 2 * ks, idesc, (kt > 0 || ks > 0) ? 1u : 0u);
+              mma_tf32(acc, dal + 2 * ks, db + 2 * ks, idesc, 1u);
+            }
+            issued = true;
+            mma_commit(&a_empty[s]);
+            if (kt == nk - 1) mma_commit(&acc_full[a]);
+          }
+        }
       }
     }
-    cp_async_wait<0>();
-  } else if (warp == kStemGMmaWarp) {
-    // ------------------------------------------------ MMA issuer
-    bool issued = false;
-    if (lane == 0) {
-      const uint32_t idesc = idesc_tf32(128, 64);
-      long long kc = 0;
-      for (long long un = 0; un < n_units; ++un) {
-        const int a = static_cast<int>(un & 1);
-        if (un >= 2) {                                   // the epilogue has read this accumulator
-          if (!mbar_wait_bounded(&acc_empty[a], static_cast<uint32_t>(((un >> 1) - 1) & 1),
-                                 p.timeout)) {
-            if (p.err) atomicOr(p.err, kErrTimeoutAccEmpty);
-            break;
-          }
-        }
-        tc_fence_after();
-        const uint32_t acc = tmem + static_cast<uint32_t>(a * 64);
-        bool okk = true;
-        for (int kt = 0; kt < nk; ++kt, ++kc) {
-          const int s = static_cast<int>(kc % S);
-          if (!mbar_wait_bounded(&a_full[s], static_cast<uint32_t>((kc / S) & 1), p.timeout)) {
-            if (p.err) atomicOr(p.err, kErrTimeoutFull);
-            okk = false;
-            break;
-          }
-          tc_fence_after();
-          uint8_t* ah = sA + s * 32768;
-          const uint64_t dah = smem_desc_kmajor(smem_u32(ah), 1024, 2);
-          const uint64_t dal = smem_desc_kmajor(smem_u32(ah + 16384), 1024, 2);
-          const uint64_t dbh = smem_desc_kmajor(smem_u32(sBh + kt * 8192), 1024, 2);
-          const uint64_t dbl = smem_desc_kmajor(smem_u32(sBl + kt * 8192), 1024, 2);
-#pragma unroll
-          for (int ks = 0; ks < 4; ++ks) {
-            mma_tf32(acc, dal + 2 * ks, dbh + 2 * ks, idesc, (kt > 0 || ks > 0) ? 1u : 0u);
-            mma_tf32(acc, dah + 2 * ks, dbl + 2 * ks, idesc, 1u);
-            mma_tf32(acc, dah + 2 * ks, dbh + 2 * ks, idesc, 1u);
-          }
-          issued = true;
-          mma_commit(&a_empty[s]);
-        }
-        if (!okk) break;
-        mma_commit(&acc_full[a]);
-      }
-      // Every MMA issued has completed before TMEM is released.
+    if (!p.tma_in) cp_async_wait<0>();
+    if (tid == 0) {
+      // Windows requested but not waited for (a stopped run) land before the
+      // block exits; every MMA issued completes before TMEM is released.
+      for (int u = waited; u < requested; ++u)
+        mbar_wait_bounded_sleep(&in_full[u & 1], static_cast<uint32_t>((u >> 1) & 1), p.timeout);
       if (issued) {
         mma_commit(drain);
         if (!mbar_wait_bounded(drain, 0, p.timeout) && p.err) atomicOr(p.err, kErrTimeoutDrain);
       }
     }
-    __syncwarp();
   } else {
     // ------------------------------------------------ epilogue
-    const int et = tid - kStemGEpi0 * 32;                // 0..255
     const int q = warp & 3, h = (warp - kStemGEpi0) >> 2;   // TMEM lane quarter; channel half
-    const int px = q * 32 + lane;
     const int c0 = 32 * h;
     const int nch = max(0, min(32, p.Cout - c0)) / 8;    // 16-byte chunks this thread stores
+    const bool lead = h == 0 && lane == 0;               // issues the quarter's bulk copies
+    const int qbar = 2 + q;                              // the quarter's two warps
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
     const int row_bytes = p.Cout * 2;
     float v[32];
     uint32_t out_uses = 0;                               // timestep tiles written so far
-    for (long long un = 0; un < n_units; ++un) {
-      const int a = static_cast<int>(un & 1);
-      const int g = static_cast<int>(un % n_gemm);
+    for (int un = 0; un < n_units; ++un) {
+      const int a = un & 1;
+      const int g = un % n_gemm;
       bool okw = true;
-      if (et == 0) {
-        okw = mbar_wait_bounded(&acc_full[a], static_cast<uint32_t>((un >> 1) & 1), p.timeout);
+      if (lead) {
+        okw = mbar_wait_bounded_sleep(&acc_full[a], static_cast<uint32_t>((un >> 1) & 1), p.timeout);
         if (!okw && p.err) atomicOr(p.err, kErrTimeoutAcc);
       }
-      if (named_barrier_or(2, 256, !okw)) break;
+      if (named_barrier_or(qbar, 64, !okw)) break;
       tc_fence_after();
       float x[32];
-      tmem_ld32(lane_base + static_cast<uint32_t>(a * 64 + c0), x);
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {                   // 16 columns at a time
+        uint32_t rh[16], rl[16];                         // x_a * w_hi and x_a * w_lo columns
+        tmem_ld16_nowait(lane_base + static_cast<uint32_t>(a * 128 + c0 + 16 * hh), rh);
+        tmem_ld16_nowait(lane_base + static_cast<uint32_t>(a * 128 + 64 + c0 + 16 * hh), rl);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          x[16 * hh + j] = __uint_as_float(rh[j]) + __uint_as_float(rl[j]);
+      }
       tc_fence_before();
       mbar_arrive(&acc_empty[a]);                        // this accumulator may be overwritten
 #pragma unroll
@@ -636,58 +695,63 @@ stem_tc_gen_kernel(const __grid_constant__ StemParams p) {
       int b, oh0, ow0;
       tile_origin(unit_tile(un), &b, &oh0, &ow0);
       const int npix = R == 1 ? min(TW, p.OW - ow0) : min(R, p.OH - oh0) * p.OW;
-      const long long pix0 = (static_cast<long long>(b) * p.OH + oh0) * p.OW + ow0;
+      const int nq = max(0, min(32, npix - 32 * q));     // this quarter's valid pixels
+      const long long pix0 = (static_cast<long long>(b) * p.OH + oh0) * p.OW + ow0 + 32 * q;
       const int t_first = p.Tin > 1 ? g : 0, t_last = p.Tin > 1 ? g : p.T - 1;
       for (int t = t_first; t <= t_last; ++t, ++out_uses) {
         uint32_t w[16];
+        if (nch == 4) {
 #pragma unroll
-        for (int q2 = 0; q2 < 16; ++q2) {
-          uint32_t bits = 0;
+          for (int q2 = 0; q2 < 16; ++q2) w[q2] = stem_pack2<MODE>(v, x, 2 * q2, p);
+        } else {                                         // 16 channels (Cout = 48) or none
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int j = 2 * q2 + e;
-            if constexpr (MODE == kModeNone) {
-              bits |= static_cast<uint32_t>(__half_as_ushort(__float2half_rn(x[j]))) << (16 * e);
-            } else {
-              if (neuron_step<MODE>(v[j], x[j], p.decay, p.tau, p.v_th, p.v_reset))
-                bits |= 0x3C00u << (16 * e);
+          for (int q2 = 0; q2 < 8; ++q2) w[q2] = stem_pack2<MODE>(v, x, 2 * q2, p);
+#pragma unroll
+          for (int q2 = 8; q2 < 16; ++q2) w[q2] = 0u;
+        }
+        uint8_t* ob = so + (out_uses & 1) * kStemGOutBytes + q * (kStemGOutBytes / 4);
+        // The bulk copy that last read this buffer (two tiles ago) is done reading.
+        if (lead) bulk_wait_group_read<1>();
+        named_barrier(qbar, 64);
+        uint8_t* orow = ob + lane * row_bytes + c0 * 2;
+        if (row_bytes % 128 == 0) {
+          // 128-byte pixel rows put every lane's chunk c in one bank group:
+          // write the chunks in a lane-rotated order instead.
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int c = (i + lane) & 3;
+            if (c < nch) {
+              uint32_t w0 = w[0], w1 = w[1], w2 = w[2], w3 = w[3];
+              if (c == 1) { w0 = w[4]; w1 = w[5]; w2 = w[6]; w3 = w[7]; }
+              if (c == 2) { w0 = w[8]; w1 = w[9]; w2 = w[10]; w3 = w[11]; }
+              if (c == 3) { w0 = w[12]; w1 = w[13]; w2 = w[14]; w3 = w[15]; }
+              *reinterpret_cast<uint4*>(orow + 16 * c) = make_uint4(w0, w1, w2, w3);
             }
           }
-          w[q2] = bits;
-        }
-        uint8_t* ob = so + (out_uses & 1) * kStemGOutBytes;
-        // The bulk copy that last read this buffer (two tiles ago) is done reading.
-        if (et == 0) bulk_wait_group_read<1>();
-        named_barrier(2, 256);
-        // 16-byte chunks in a lane-rotated order: fewer threads of a warp meet in one bank.
+        } else {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int c = (i + lane) & 3;
-          if (c < nch) {
-            uint32_t w0 = w[0], w1 = w[1], w2 = w[2], w3 = w[3];
-            if (c == 1) { w0 = w[4]; w1 = w[5]; w2 = w[6]; w3 = w[7]; }
-            if (c == 2) { w0 = w[8]; w1 = w[9]; w2 = w[10]; w3 = w[11]; }
-            if (c == 3) { w0 = w[12]; w1 = w[13]; w2 = w[14]; w3 = w[15]; }
-            *reinterpret_cast<uint4*>(ob + px * row_bytes + (c0 + 8 * c) * 2) =
-                make_uint4(w0, w1, w2, w3);
-          }
+          for (int c = 0; c < 4; ++c)
+            if (c < nch)
+              *reinterpret_cast<uint4*>(orow + 16 * c) =
+                  make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
         }
         fence_proxy_async_smem();                        // generic writes -> bulk-copy reads
-        named_barrier(2, 256);
-        if (et == 0) {                                   // npix >= 1: one group per timestep tile
-          bulk_store_1d(p.out + (static_cast<size_t>(t) * P + pix0) * p.Cout, ob,
-                        static_cast<uint32_t>(npix) * row_bytes);
+        named_barrier(qbar, 64);
+        if (lead) {                                      // one group per timestep tile
+          if (nq > 0)
+            bulk_store_1d(p.out + (static_cast<size_t>(t) * P + pix0) * p.Cout, ob,
+                          static_cast<uint32_t>(nq) * row_bytes);
           bulk_commit_group();
         }
       }
     }
-    if (et == 0) bulk_wait_group<0>();                   // stores complete before the block exits
+    if (lead) bulk_wait_group<0>();                      // stores complete before the block exits
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == kStemGMmaWarp) {
+  if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc(tmem, 128);
+    tmem_dealloc(tmem, 256);
   }
 }
 
