@@ -67,7 +67,11 @@ enum { SNN_FLAG_READ_STATE = 1, SNN_FLAG_WRITE_STATE = 2,
         * neurons with no residual or the SEW add.  For dense convs the
         * reference keeps unpruned (e.g. a Spikformer's patch-splitting
         * convs, models/spikformer.py:159-206). */
-       SNN_FLAG_DENSE = 16 };
+       SNN_FLAG_DENSE = 16,
+       /* Attention only: q, k and v are the three channel blocks of one
+        * [T*B][N][3*heads*head_dim] tensor (rows of 3*C elements, as one
+        * fused q|k|v Linear writes them); pass q, k = q + C and v = q + 2C. */
+       SNN_FLAG_QKV_PACKED = 32 };
 
 /* Where the residual of a fused Add enters the epilogue (the reference's
  * pattern strings and templates, sengine/kernels/interleaved_templates.py:371-397):
@@ -256,7 +260,8 @@ int snn_lif_forward(const snn_conv_desc* d, const void* x, float* state, void* o
  * v_threshold), :97).  Per timestep and head: x = (q k^T * scale) v, then the
  * LIF over T with hard reset to v_reset.
  *   q, k, v  [T*B][N][heads*head_dim] fp16 spikes (0/1: the kernel forms
- *            q (k^T v) with k^T v rounded to fp16, exact for spikes)
+ *            q (k^T v) with k^T v rounded to fp16, exact for spikes), or with
+ *            SNN_FLAG_QKV_PACKED the blocks of one [T*B][N][3*C] tensor
  *   out      [T*B][N][heads*head_dim] fp16 spikes
  *   state    [B][N][heads*head_dim] fp32 membrane, per SNN_FLAG_*_STATE
  * 1 <= N <= 256, head_dim 32 or 64.  x is exact (integer counts times scale)

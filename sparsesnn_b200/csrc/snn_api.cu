@@ -1240,7 +1240,8 @@ int snn_spikformer_attn_forward(int32_t T, int32_t B, int32_t N, int32_t heads,
     return fail(SNN_E_INVALID, "q, k, v and out must be 16-byte aligned");
   const long long TB = static_cast<long long>(T) * B;
   const long long C = static_cast<long long>(heads) * head_dim;
-  if (TB * N * C > 0x7fffffffLL || static_cast<long long>(B) * heads > 0x7fffffffLL)
+  if (TB * N * C * ((flags & SNN_FLAG_QKV_PACKED) ? 3 : 1) > 0x7fffffffLL ||
+      static_cast<long long>(B) * heads > 0x7fffffffLL)
     return fail(SNN_E_INVALID, "attention tensors too large");
   snn::AttnParams p;
   memset(&p, 0, sizeof(p));
@@ -1250,7 +1251,9 @@ int snn_spikformer_attn_forward(int32_t T, int32_t B, int32_t N, int32_t heads,
     // all kv_rows tokens (rows past N read as zero).
     cuuint64_t dims[3] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(N),
                           static_cast<cuuint64_t>(TB)};
-    cuuint64_t strides[2] = {static_cast<cuuint64_t>(C) * 2, static_cast<cuuint64_t>(N * C) * 2};
+    // SNN_FLAG_QKV_PACKED: rows of 3C elements (q | k | v of one token).
+    const long long ld = (flags & SNN_FLAG_QKV_PACKED) ? 3 * C : C;
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * 2, static_cast<cuuint64_t>(N * ld) * 2};
     const CUtensorMapSwizzle swz =
         head_dim == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
     cuuint32_t box_q[3] = {static_cast<cuuint32_t>(head_dim),

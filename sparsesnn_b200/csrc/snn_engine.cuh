@@ -33,7 +33,8 @@
 //               workspace tensor
 //   ATTN        in0 = q, in1 = k, i[0] = v, out; desc T, B, tau,
 //               v_threshold, v_reset, tau2 = the attention scale;
-//               i[1..3] = tokens, heads, head_dim
+//               i[1..3] = tokens, heads, head_dim; desc flags
+//               SNN_FLAG_QKV_PACKED: in0 = in1 = i[0] = one q|k|v tensor
 // Stem nodes may have no neuron (fp16 BN output); conv nodes may carry the
 // dense-weight and general-kernel flags and the fp16 BN output, but never
 // the membrane flags (every forward starts from zero).
@@ -171,12 +172,17 @@ int parse_engine_file(const char* path, SnnEngineHeader* h, std::vector<SnnEngin
       case kOpAttn: {
         const int32_t N = nd.i[1], heads = nd.i[2], hd = nd.i[3];
         const uint32_t v_id = static_cast<uint32_t>(nd.i[0]);
-        if (d.T < 1 || d.B < 1 || N < 1 || heads < 1 || (hd != 32 && hd != 64) || d.flags != 0 ||
-            nd.in1 == kNoTensor || !tid_ok(v_id))
+        // SNN_FLAG_QKV_PACKED: in0 is one [T*B][N][3C] tensor (in1 and the
+        // v id name the same tensor).
+        const bool packed = d.flags == SNN_FLAG_QKV_PACKED;
+        if (d.T < 1 || d.B < 1 || N < 1 || heads < 1 || (hd != 32 && hd != 64) ||
+            (d.flags != 0 && !packed) || nd.in1 == kNoTensor || !tid_ok(v_id) ||
+            (packed && (nd.in1 != nd.in0 || v_id != nd.in0)))
           return fail(SNN_E_INVALID, "engine node %u (attention): bad shape, flags or tensor", n);
         const uint64_t need = uint64_t(d.T) * d.B * N * heads * hd * 2;
-        if (in_bytes < need || out_bytes < need || (*tensors)[nd.in1].bytes < need ||
-            (*tensors)[v_id].bytes < need)
+        const uint64_t in_need = packed ? 3 * need : need;
+        if (in_bytes < in_need || out_bytes < need || (*tensors)[nd.in1].bytes < in_need ||
+            (*tensors)[v_id].bytes < in_need)
           return fail(SNN_E_INVALID, "engine node %u (attention): sizes out of range", n);
         break;
       }
@@ -273,9 +279,15 @@ int engine_node_loop(snn_engine* e, void* stream) {
       }
       case kOpAttn: {
         const snn_conv_desc& d = nd.desc;
+        const void* vp = e->tptr[static_cast<uint32_t>(nd.i[0])];
+        if (d.flags == SNN_FLAG_QKV_PACKED) {            // k and v: the next channel blocks
+          const size_t cb = static_cast<size_t>(nd.i[2]) * nd.i[3] * 2;
+          in1 = static_cast<char*>(in0) + cb;
+          vp = static_cast<char*>(in0) + 2 * cb;
+        }
         st = snn_spikformer_attn_forward(d.T, d.B, nd.i[1], nd.i[2], nd.i[3], d.tau2, d.tau,
-                                         d.v_threshold, d.v_reset, 0, in0, in1,
-                                         e->tptr[static_cast<uint32_t>(nd.i[0])], nullptr, out, stream);
+                                         d.v_threshold, d.v_reset, d.flags, in0, in1, vp, nullptr,
+                                         out, stream);
         break;
       }
       default:

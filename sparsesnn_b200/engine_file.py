@@ -126,10 +126,15 @@ def save_plan(model, path):
                    n.ints)
         elif n.kind == npl.ATTN:
             d = rt.SnnConvDesc.from_buffer_copy(bytes(n.desc))
-            d.flags = 0
             d.tau2 = n.attn["scale"]
-            w.node(OP_ATTN, ins[0], ins[1], out, d,
-                   i=(ins[2], n.attn["N"], n.attn["heads"], n.attn["head_dim"], 0))
+            if n.attn.get("packed"):                     # q | k | v blocks of one tensor
+                d.flags = rt.SNN_FLAG_QKV_PACKED
+                w.node(OP_ATTN, ins[0], ins[0], out, d,
+                       i=(ins[0], n.attn["N"], n.attn["heads"], n.attn["head_dim"], 0))
+            else:
+                d.flags = 0
+                w.node(OP_ATTN, ins[0], ins[1], out, d,
+                       i=(ins[2], n.attn["N"], n.attn["heads"], n.attn["head_dim"], 0))
         else:
             d = rt.SnnConvDesc.from_buffer_copy(bytes(n.desc))
             d.flags = 0

@@ -121,10 +121,15 @@ class PlanModel:
             rt.check(lib.snn_lif_forward(n.desc, ins[0].data_ptr(), None, out.data_ptr(), s))
         elif n.kind == ATTN:
             a, d = n.attn, n.desc
-            q, k, v = ins
+            if a.get("packed"):                          # one [T*B][N][3C] q | k | v tensor
+                cb = a["heads"] * a["head_dim"] * 2
+                q = ins[0].data_ptr()
+                qkv, flags = (q, q + cb, q + 2 * cb), rt.SNN_FLAG_QKV_PACKED
+            else:
+                qkv, flags = tuple(x.data_ptr() for x in ins), 0
             rt.check(lib.snn_spikformer_attn_forward(
                 d.T, d.B, a["N"], a["heads"], a["head_dim"], a["scale"], d.tau, d.v_threshold,
-                d.v_reset, 0, q.data_ptr(), k.data_ptr(), v.data_ptr(), None, out.data_ptr(), s))
+                d.v_reset, flags, *qkv, None, out.data_ptr(), s))
         else:
             raise ValueError(f"unknown node kind {n.kind}")
 

@@ -7,9 +7,10 @@ geometry (a stride-2 pool after each of the four patch-splitting stages:
   three dense 3x3 convs + BN + LIF as fused layers with unpruned weights
   (``SNN_FLAG_DENSE``); a plain spike max pool after every stage; the RPE
   conv + BN + LIF with ``x + x_feat`` fused as its SEW add;
-* ``Block`` (``:140-152``) x 8: q, k, v = Linear + BN1d + LIF (fused 2:4
-  layers over the T*B*N token rows); the attention core + attention LIF
-  (v_th 0.5, one kernel); proj = Linear + BN1d + LIF with ``x + ...`` in its
+* ``Block`` (``:140-152``) x 8: q, k, v = Linear + BN1d + LIF as ONE fused
+  2:4 layer over the T*B*N token rows (the three weights stacked, 3E output
+  channels, each row q | k | v); the attention core + attention LIF (v_th
+  0.5, one kernel) reading q, k, v as packed blocks; proj = Linear + BN1d + LIF with ``x + ...`` in its
   epilogue; MLP fc1 / fc2 likewise, fc2 adding ``x1``;
 * the head (mean over tokens and T, Linear) in the head kernel.
 
@@ -107,8 +108,16 @@ class Spikformer(PlanModel):
         rows = batch * N
 
         def lin(pp, name, src, res=None, out_c=None):
-            layer = SparseConvBNLIF(pp["w"], *fold_bn(**pp["bn"], conv_bias=pp["b"]), T=T, B=1,
-                                    H=1, W=rows, device=dev, **lif)
+            if isinstance(pp, (list, tuple)):
+                # Linears over the same input as one layer: weights stacked
+                # along the output channels, BN folded per part.
+                folds = [fold_bn(**x["bn"], conv_bias=x["b"]) for x in pp]
+                w = np.concatenate([np.asarray(x["w"]) for x in pp], 0)
+                sc = np.concatenate([f[0] for f in folds])
+                bi = np.concatenate([f[1] for f in folds])
+            else:
+                w, (sc, bi) = pp["w"], fold_bn(**pp["bn"], conv_bias=pp["b"])
+            layer = SparseConvBNLIF(w, sc, bi, T=T, B=1, H=1, W=rows, device=dev, **lif)
             out = self.buf(layer.out_shape())
             ins = [src.view(T, 1, rows, src.shape[-1])]
             if res is not None:
@@ -120,13 +129,12 @@ class Spikformer(PlanModel):
         attn_desc = rt.make_desc(T=T, B=batch, Cin=E, H=1, W=N, Cout=E, KH=1, KW=1, tau=tau,
                                  v_threshold=attn_v_threshold)
         for i, blk in enumerate(params["blocks"]):
-            q = lin(blk["q"], f"b{i}.q", xs)
-            k = lin(blk["k"], f"b{i}.k", xs)
-            v = lin(blk["v"], f"b{i}.v", xs)
-            a = self.add(Node(ATTN, f"b{i}.attn", [q.view(TB, N, E), k.view(TB, N, E),
-                                                  v.view(TB, N, E)], self.buf((TB, N, E)),
+            # q, k, v: one launch of the three Linears (3E output channels,
+            # rows of q | k | v), read by the attention core as packed blocks.
+            qkv = lin([blk["q"], blk["k"], blk["v"]], f"b{i}.qkv", xs)
+            a = self.add(Node(ATTN, f"b{i}.attn", [qkv.view(TB, N, 3 * E)], self.buf((TB, N, E)),
                               attn_desc, attn={"N": N, "heads": heads, "head_dim": E // heads,
-                                               "scale": 0.125}))
+                                               "scale": 0.125, "packed": True}))
             x1 = lin(blk["proj"], f"b{i}.proj", a, res=xs)
             hm = lin(blk["fc1"], f"b{i}.fc1", x1)
             xs = lin(blk["fc2"], f"b{i}.fc2", hm, res=x1)

@@ -93,3 +93,29 @@ def test_single_token_and_small_heads(cuda_device):
         assert rt.device_error() == 0
         ref, _, _, _ = spikformer_attn_lif(q, k, v, T=T, heads=heads)
         assert np.array_equal(y, ref), (N, hd)
+
+
+def test_packed_qkv_layout(cuda_device):
+    """SNN_FLAG_QKV_PACKED: q, k, v as the channel blocks of one
+    [T*B][N][3C] tensor (a fused q|k|v Linear's output) give the same spikes
+    as three separate tensors, at the Spikformer-8-384 size and an edge size."""
+    import torch
+    from sparsesnn_b200 import runtime as rt
+    rng = np.random.default_rng(12)
+    for T, B, N, heads, hd in ((4, 32, 196, 12, 32), (2, 3, 129, 3, 64)):
+        C = heads * hd
+        q, k, v = ((rng.random((T * B, N, C)) < 0.09).astype(np.float32) for _ in range(3))
+        qkv = torch.from_numpy(np.concatenate([q, k, v], -1)).to("cuda", torch.float16)
+        n_out = T * B * N * C
+        buf = torch.full((n_out + GUARD,), 7.0, dtype=torch.float16, device="cuda")
+        out = buf[:n_out]
+        cb = C * 2
+        rt.check(rt.load().snn_spikformer_attn_forward(
+            T, B, N, heads, hd, 0.125, 2.0, 0.5, 0.0, rt.SNN_FLAG_QKV_PACKED, qkv.data_ptr(),
+            qkv.data_ptr() + cb, qkv.data_ptr() + 2 * cb, None, out.data_ptr(),
+            torch.cuda.current_stream().cuda_stream))
+        torch.cuda.synchronize()
+        assert rt.device_error() == 0
+        assert bool((buf[n_out:] == 7.0).all()), "attention wrote past its output"
+        ref, _, _, _ = spikformer_attn_lif(q, k, v, T=T, heads=heads)
+        assert np.array_equal(out.float().cpu().numpy().reshape(T * B, N, C), ref), (N, hd)

@@ -122,19 +122,24 @@ def test_spikformer_teacher_forced_blocks(setup):
     s = torch.cuda.current_stream().cuda_stream
     xs = trace["x0"]
     for i, p in enumerate(P["blocks"]):
-        for nm in ("q", "k", "v"):
-            got = back(nodes[f"b{i}.{nm}"].layer(tok(xs)))
+        # q, k, v: one fused layer whose output rows are q | k | v
+        got = back(nodes[f"b{i}.qkv"].layer(tok(xs)))
+        for j, nm in enumerate(("q", "k", "v")):
             spk, h, _ = linear_h(xs, p[nm], threads)
-            judge(got, spk, h, f"b{i}.{nm}")
-        # attention core + attention LIF on the oracle's q, k, v: exact
+            judge(got[..., j * E:(j + 1) * E], spk, h, f"b{i}.{nm}")
+        # attention core + attention LIF on the oracle's q, k, v packed the
+        # same way: exact
         n = nodes[f"b{i}.attn"]
-        q, k, v = (tok(trace[f"b{i}.{nm}"]) for nm in ("q", "k", "v"))
-        out = torch.empty_like(q)
+        qkv = tok(np.concatenate([trace[f"b{i}.{nm}"] for nm in ("q", "k", "v")], -1))
+        out = torch.empty((T, 1, rows, E), dtype=torch.float16, device="cuda:0")
         a = n.attn
+        assert a["packed"]
+        cb = E * 2
         rt.check(lib.snn_spikformer_attn_forward(T, B, N, a["heads"], a["head_dim"], a["scale"],
-                                                 n.desc.tau, n.desc.v_threshold, 0.0, 0,
-                                                 q.data_ptr(), k.data_ptr(), v.data_ptr(), None,
-                                                 out.data_ptr(), s))
+                                                 n.desc.tau, n.desc.v_threshold, 0.0,
+                                                 rt.SNN_FLAG_QKV_PACKED, qkv.data_ptr(),
+                                                 qkv.data_ptr() + cb, qkv.data_ptr() + 2 * cb,
+                                                 None, out.data_ptr(), s))
         torch.cuda.synchronize()
         assert np.array_equal(back(out), trace[f"b{i}.attn"]), f"b{i}.attn"
         # proj + x, fc1, fc2 + x1
