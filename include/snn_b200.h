@@ -213,6 +213,20 @@ int snn_conv_forward_tsplit_static(const snn_conv_desc* d, const void* data, con
 int snn_stem_forward(const snn_conv_desc* d, int32_t Tin, const float* x, const float* w,
                      const float* bn_scale, const float* bn_bias, void* out, void* stream);
 
+/* The stem without neuron followed by a standalone neuron node, in one pass:
+ * out_bn gets the fp16 BN output (as snn_stem_forward with SNN_NEURON_NONE)
+ * and out_spikes the spikes of d->neuron (LIF or IF, tau, v_threshold,
+ * v_reset) run over T on that fp16 output, exactly as snn_lif_forward would
+ * compute them from out_bn.  MS-ResNet's stem and the LIF in front of its
+ * first block's conv (models/msresnet.py:119-121,135-138), which the
+ * reference runs as the stem node plus lif_neuron_kernel
+ * (sengine/csrc/cpp_executor.cu:46-64).  Both outputs [T][B][OH][OW][Cout]
+ * fp16, 16-byte aligned; general tensor-core stem geometries only (Cout <=
+ * 64, Cin*KH*KW <= 192), else SNN_E_INVALID. */
+int snn_stem_forward_dual(const snn_conv_desc* d, int32_t Tin, const float* x, const float* w,
+                          const float* bn_scale, const float* bn_bias, void* out_bn,
+                          void* out_spikes, void* stream);
+
 /* Classifier tail: global average pool over HW, mean over T, then
  * logits = feat @ fc_w^T + fc_b (models/sewresnet.py:207-210; the reference
  * executor runs global_avgpool, temporal_mean and a cuBLAS GEMM,

@@ -173,12 +173,21 @@ StemKernel stem_tc_fn(int cin, int mode) {
 }
 constexpr int kStemTcSmemMax = 96 * 1024;
 
-StemKernel stem_tcg_fn(int mode) {
+// mode: the neuron (kModeNone: fp16 BN output); dual: fp16 BN output plus
+// the spikes of `mode`'s neuron on it.
+StemKernel stem_tcg_fn(int mode, bool dual = false) {
+  if (dual) {
+    switch (mode) {
+      case snn::kModeLifHalf: return snn::stem_tc_gen_kernel<snn::kModeLifHalf, true>;
+      case snn::kModeLifDiv: return snn::stem_tc_gen_kernel<snn::kModeLifDiv, true>;
+      default: return snn::stem_tc_gen_kernel<snn::kModeIf, true>;
+    }
+  }
   switch (mode) {
-    case snn::kModeLifHalf: return snn::stem_tc_gen_kernel<snn::kModeLifHalf>;
-    case snn::kModeLifDiv: return snn::stem_tc_gen_kernel<snn::kModeLifDiv>;
-    case snn::kModeIf: return snn::stem_tc_gen_kernel<snn::kModeIf>;
-    default: return snn::stem_tc_gen_kernel<snn::kModeNone>;
+    case snn::kModeLifHalf: return snn::stem_tc_gen_kernel<snn::kModeLifHalf, false>;
+    case snn::kModeLifDiv: return snn::stem_tc_gen_kernel<snn::kModeLifDiv, false>;
+    case snn::kModeIf: return snn::stem_tc_gen_kernel<snn::kModeIf, false>;
+    default: return snn::stem_tc_gen_kernel<snn::kModeNone, false>;
   }
 }
 
@@ -300,8 +309,9 @@ int ensure_init() {
     }
   }
   for (int mode = 0; mode < 4 && e == cudaSuccess; ++mode)
-    e = cudaFuncSetAttribute(stem_tcg_fn(mode), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             snn::stem_tcg_smem_max());
+    for (int dual = 0; dual < 2 && e == cudaSuccess; ++dual)
+      e = cudaFuncSetAttribute(stem_tcg_fn(mode, dual != 0), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               snn::stem_tcg_smem_max());
   if (e != cudaSuccess)
     return g_init_status = fail(SNN_E_CUDA, "smem attribute: %s", cudaGetErrorString(e));
   e = cudaFuncSetAttribute(snn::spikformer_attn_lif_kernel<32>,
@@ -1071,8 +1081,11 @@ int snn_conv_forward_tsplit(const snn_conv_desc* d, const void* data, const void
   return SNN_OK;
 }
 
-int snn_stem_forward(const snn_conv_desc* d, int32_t Tin, const float* x, const float* w,
-                     const float* bn_scale, const float* bn_bias, void* out, void* stream) {
+// out2 non-null: the dual form (fp16 BN output in `out`, spikes of d->neuron
+// on it in `out2`), general tensor-core stem only.
+static int stem_forward_impl(const snn_conv_desc* d, int32_t Tin, const float* x, const float* w,
+                             const float* bn_scale, const float* bn_bias, void* out, void* out2,
+                             void* stream) {
   int st = ensure_init();
   if (st) return st;
   if (!d || !x || !w || !bn_scale || !bn_bias || !out) return fail(SNN_E_INVALID, "null pointer");
@@ -1083,6 +1096,10 @@ int snn_stem_forward(const snn_conv_desc* d, int32_t Tin, const float* x, const 
   if (Tin != 1 && Tin != d->T) return fail(SNN_E_INVALID, "Tin must be 1 or T");
   if (d->neuron < SNN_NEURON_LIF || d->neuron > SNN_NEURON_NONE)
     return fail(SNN_E_INVALID, "stem neuron must be LIF, IF or NONE (fp16 BN output)");
+  if (out2 && d->neuron == SNN_NEURON_NONE)
+    return fail(SNN_E_INVALID, "dual stem: the neuron of the spike output must be LIF or IF");
+  if (out2 && ((reinterpret_cast<uintptr_t>(out2) & 15) || out2 == out))
+    return fail(SNN_E_INVALID, "dual stem: out_spikes must be a separate 16-byte aligned tensor");
   const int OH = (d->H + 2 * d->pad - d->KH) / d->stride + 1;
   const int OW = (d->W + 2 * d->pad - d->KW) / d->stride + 1;
   if (OH < 1 || OW < 1) return fail(SNN_E_INVALID, "empty output");
@@ -1101,7 +1118,7 @@ int snn_stem_forward(const snn_conv_desc* d, int32_t Tin, const float* x, const 
     return fail(SNN_E_CUDA, "error word address");
   // Tensor-core fast path: 3x3 s1 p1, 64 channels, input repeated over T,
   // rows of at most 128 pixels.
-  if (Tin == 1 && d->neuron != SNN_NEURON_NONE && d->KH == 3 && d->KW == 3 && d->stride == 1 &&
+  if (!out2 && Tin == 1 && d->neuron != SNN_NEURON_NONE && d->KH == 3 && d->KW == 3 && d->stride == 1 &&
       d->pad == 1 && d->Cout == 64 &&
       (d->Cin == 1 || d->Cin == 3) && OW <= snn::kStemPx) {
     const int mode = d->neuron == SNN_NEURON_IF ? snn::kModeIf
@@ -1169,12 +1186,17 @@ int snn_stem_forward(const snn_conv_desc* d, int32_t Tin, const float* x, const 
                               ((OW + TWst - 1) / TWst);
     const long long nblk = std::max<long long>(1, std::min<long long>(n_tiles, g_num_sms));
     if ((reinterpret_cast<uintptr_t>(out) & 15) == 0) {
-      cudaError_t e = launch_pdl(stem_tcg_fn(mode), dim3(static_cast<unsigned>(nblk)),
+      p.out2 = static_cast<__half*>(out2);
+      cudaError_t e = launch_pdl(stem_tcg_fn(mode, out2 != nullptr), dim3(static_cast<unsigned>(nblk)),
                                  dim3(snn::kStemGThreads), smem, stream, p);
       if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));
       return SNN_OK;
     }
   }
+  if (out2)
+    return fail(SNN_E_INVALID, "dual stem needs the general tensor-core stem (Cout <= 64, "
+                "Cin*KH*KW <= %d, staged window <= %d bytes, out 16-byte aligned)",
+                snn::kStemGMaxK, snn::kStemGMaxStage);
   const long long pixels = static_cast<long long>(d->B) * OH * OW;
   const int px_per_block = 256 / (d->Cout / 16);
   if (px_per_block < 1) return fail(SNN_E_INVALID, "stem Cout too large");
@@ -1189,6 +1211,18 @@ int snn_stem_forward(const snn_conv_desc* d, int32_t Tin, const float* x, const 
   cudaError_t e = launch_pdl(k, grid, block, smem, stream, p);
   if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));
   return SNN_OK;
+}
+
+int snn_stem_forward(const snn_conv_desc* d, int32_t Tin, const float* x, const float* w,
+                     const float* bn_scale, const float* bn_bias, void* out, void* stream) {
+  return stem_forward_impl(d, Tin, x, w, bn_scale, bn_bias, out, nullptr, stream);
+}
+
+int snn_stem_forward_dual(const snn_conv_desc* d, int32_t Tin, const float* x, const float* w,
+                          const float* bn_scale, const float* bn_bias, void* out_bn,
+                          void* out_spikes, void* stream) {
+  if (!out_spikes) return fail(SNN_E_INVALID, "null pointer");
+  return stem_forward_impl(d, Tin, x, w, bn_scale, bn_bias, out_bn, out_spikes, stream);
 }
 
 int snn_head_forward(int32_t T, int32_t B, int32_t HW, int32_t C, int32_t NC, const void* x,

@@ -19,7 +19,9 @@
 //
 // All integers little-endian.  Node kinds and their fields:
 //   STEM        in0 = images (fp32 NCHW, Tin x B), out; desc; p0 = w, p1 = scale,
-//               p2 = bias (fp32); i[0] = Tin
+//               p2 = bias (fp32); i[0] = Tin; in1 = none, or the spike output of
+//               the dual form (out = fp16 BN output, in1 = spikes of
+//               desc.neuron on it)
 //   CONV        in0 = data, in1 = residual or none, out; desc (no membrane
 //               flags: the membrane starts at zero every forward); p0 = packed
 //               weights, p1 = scale, p2 = bias
@@ -135,6 +137,10 @@ int parse_engine_file(const char* path, SnnEngineHeader* h, std::vector<SnnEngin
             !off_ok(nd.p0, uint64_t(d.Cout) * d.Cin * d.KH * d.KW * 4) ||
             !off_ok(nd.p1, uint64_t(d.Cout) * 4) || !off_ok(nd.p2, uint64_t(d.Cout) * 4))
           return fail(SNN_E_INVALID, "engine node %u (stem): sizes or offsets out of range", n);
+        if (nd.in1 != kNoTensor &&
+            (nd.in1 == nd.out || nd.in1 == nd.in0 ||
+             (*tensors)[nd.in1].bytes < uint64_t(d.T) * d.B * uint64_t(oh) * uint64_t(ow) * d.Cout * 2))
+          return fail(SNN_E_INVALID, "engine node %u (stem): bad spike output tensor", n);
         break;
       }
       case kOpConv:
@@ -249,8 +255,10 @@ int engine_node_loop(snn_engine* e, void* stream) {
     int st = SNN_OK;
     switch (nd.op) {
       case kOpStem:
-        st = snn_stem_forward(&nd.desc, nd.i[0], static_cast<const float*>(in0), P(nd.p0), P(nd.p1),
-                              P(nd.p2), out, stream);
+        st = in1 ? snn_stem_forward_dual(&nd.desc, nd.i[0], static_cast<const float*>(in0), P(nd.p0),
+                                         P(nd.p1), P(nd.p2), out, in1, stream)
+                 : snn_stem_forward(&nd.desc, nd.i[0], static_cast<const float*>(in0), P(nd.p0),
+                                    P(nd.p1), P(nd.p2), out, stream);
         break;
       case kOpConv:
         st = in1 ? snn_conv_forward_res(&nd.desc, in0, e->dblob + nd.p0, nullptr, P(nd.p1), P(nd.p2), in1,

@@ -27,6 +27,7 @@ struct StemParams {
   int tma_out;                    // tensor-core path: spike tiles leave by TMA stores
   int tma_in;                     // general tensor-core path: input windows arrive by TMA
   int in_pitch;                   // general path: staged row pitch (ICp with TMA, else IC)
+  __half* out2;                   // general path, dual output: spikes of the fp16 BN output
 };
 
 // One thread = one output pixel x 16 consecutive output channels
@@ -421,7 +422,26 @@ __device__ __forceinline__ uint32_t stem_pack2(float (&v)[32], const float (&x)[
   return *reinterpret_cast<const uint32_t*>(&hv);
 }
 
+// Dual output: two channels' neuron step on the fp16-rounded BN output
+// (packed in `h2`), exactly as the standalone LIF node computes it from that
+// stored tensor (tau = 2: the input halved), as fp16 spikes.
 template <int MODE>
+__device__ __forceinline__ uint32_t stem_spike2(float (&v)[32], uint32_t h2, int j,
+                                                const StemParams& p) {
+  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h2));
+  const float a = MODE == kModeLifHalf ? f.x * 0.5f : f.x;
+  const float b = MODE == kModeLifHalf ? f.y * 0.5f : f.y;
+  float2 s2;
+  s2.x = neuron_step<MODE>(v[j], a, p.decay, p.tau, p.v_th, p.v_reset) ? 1.f : 0.f;
+  s2.y = neuron_step<MODE>(v[j + 1], b, p.decay, p.tau, p.v_th, p.v_reset) ? 1.f : 0.f;
+  const __half2 hv = __float22half2_rn(s2);
+  return *reinterpret_cast<const uint32_t*>(&hv);
+}
+
+// DUAL (MODE = the neuron): `out` gets the fp16 BN output and `out2` the
+// spikes of MODE's neuron over T on it -- the stem and the standalone neuron
+// node after it in one pass (MS-ResNet's stem and its first block's LIF).
+template <int MODE, bool DUAL>
 __global__ void __launch_bounds__(kStemGThreads, 1)
 stem_tc_gen_kernel(const __grid_constant__ StemParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -482,8 +502,10 @@ stem_tc_gen_kernel(const __grid_constant__ StemParams p) {
   if (tid < 64) {
     const bool cv = tid < p.Cout;
     // BN pre-scaled by 1/2 for the tau = 2 LIF step, as in the conv epilogues.
-    sc[tid] = cv ? (MODE == kModeLifHalf ? p.scale[tid] * 0.5f : p.scale[tid]) : 0.f;
-    bi[tid] = cv ? (MODE == kModeLifHalf ? p.bias[tid] * 0.5f : p.bias[tid]) : 0.f;
+    // (DUAL: unscaled, the fp16 BN output is stored.)
+    constexpr bool half_bn = MODE == kModeLifHalf && !DUAL;
+    sc[tid] = cv ? (half_bn ? p.scale[tid] * 0.5f : p.scale[tid]) : 0.f;
+    bi[tid] = cv ? (half_bn ? p.bias[tid] * 0.5f : p.bias[tid]) : 0.f;
   }
   tc_fence_before();
   __syncthreads();
@@ -698,25 +720,12 @@ stem_tc_gen_kernel(const __grid_constant__ StemParams p) {
       const int nq = max(0, min(32, npix - 32 * q));     // this quarter's valid pixels
       const long long pix0 = (static_cast<long long>(b) * p.OH + oh0) * p.OW + ow0 + 32 * q;
       const int t_first = p.Tin > 1 ? g : 0, t_last = p.Tin > 1 ? g : p.T - 1;
-      for (int t = t_first; t <= t_last; ++t, ++out_uses) {
-        uint32_t w[16];
-        if (nch == 4) {
-#pragma unroll
-          for (int q2 = 0; q2 < 16; ++q2) w[q2] = stem_pack2<MODE>(v, x, 2 * q2, p);
-        } else {                                         // 16 channels (Cout = 48) or none
-#pragma unroll
-          for (int q2 = 0; q2 < 8; ++q2) w[q2] = stem_pack2<MODE>(v, x, 2 * q2, p);
-#pragma unroll
-          for (int q2 = 8; q2 < 16; ++q2) w[q2] = 0u;
-        }
-        uint8_t* ob = so + (out_uses & 1) * kStemGOutBytes + q * (kStemGOutBytes / 4);
-        // The bulk copy that last read this buffer (two tiles ago) is done reading.
-        if (lead) bulk_wait_group_read<1>();
-        named_barrier(qbar, 64);
+      // One quarter's 32 pixel rows of a [pixels][Cout] fp16 tile; 128-byte
+      // pixel rows put every lane's chunk c in one bank group, so those are
+      // written in a lane-rotated order.
+      auto write_tile = [&](uint8_t* ob, const uint32_t (&w)[16]) {
         uint8_t* orow = ob + lane * row_bytes + c0 * 2;
         if (row_bytes % 128 == 0) {
-          // 128-byte pixel rows put every lane's chunk c in one bank group:
-          // write the chunks in a lane-rotated order instead.
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             const int c = (i + lane) & 3;
@@ -735,6 +744,65 @@ stem_tc_gen_kernel(const __grid_constant__ StemParams p) {
               *reinterpret_cast<uint4*>(orow + 16 * c) =
                   make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
         }
+      };
+      if constexpr (DUAL) {
+        // The unit's fp16 BN output tile (slot 0) is written once and sent
+        // for each of its timesteps; the spike tile (slot 1) each timestep.
+        uint32_t wx[16];
+#pragma unroll
+        for (int q2 = 0; q2 < 16; ++q2) {
+          const __half2 hv = __float22half2_rn(make_float2(x[2 * q2], x[2 * q2 + 1]));
+          wx[q2] = *reinterpret_cast<const uint32_t*>(&hv);
+        }
+        uint8_t* ox = so + q * (kStemGOutBytes / 4);
+        uint8_t* os = so + kStemGOutBytes + q * (kStemGOutBytes / 4);
+        if (lead) bulk_wait_group_read<0>();             // the previous unit's copies read both
+        named_barrier(qbar, 64);
+        write_tile(ox, wx);
+        for (int t = t_first; t <= t_last; ++t) {
+          uint32_t w[16];
+#pragma unroll
+          for (int q2 = 0; q2 < 16; ++q2) w[q2] = 0u;
+          if (nch == 4) {
+#pragma unroll
+            for (int q2 = 0; q2 < 16; ++q2) w[q2] = stem_spike2<MODE>(v, wx[q2], 2 * q2, p);
+          } else {
+#pragma unroll
+            for (int q2 = 0; q2 < 8; ++q2) w[q2] = stem_spike2<MODE>(v, wx[q2], 2 * q2, p);
+          }
+          if (t > t_first) {                             // the last spike tile has been read
+            if (lead) bulk_wait_group_read<0>();
+            named_barrier(qbar, 64);
+          }
+          write_tile(os, w);
+          fence_proxy_async_smem();                      // generic writes -> bulk-copy reads
+          named_barrier(qbar, 64);
+          if (lead) {
+            if (nq > 0) {
+              const size_t o = (static_cast<size_t>(t) * P + pix0) * p.Cout;
+              bulk_store_1d(p.out + o, ox, static_cast<uint32_t>(nq) * row_bytes);
+              bulk_store_1d(p.out2 + o, os, static_cast<uint32_t>(nq) * row_bytes);
+            }
+            bulk_commit_group();
+          }
+        }
+      } else {
+      for (int t = t_first; t <= t_last; ++t, ++out_uses) {
+        uint32_t w[16];
+        if (nch == 4) {
+#pragma unroll
+          for (int q2 = 0; q2 < 16; ++q2) w[q2] = stem_pack2<MODE>(v, x, 2 * q2, p);
+        } else {                                         // 16 channels (Cout = 48) or none
+#pragma unroll
+          for (int q2 = 0; q2 < 8; ++q2) w[q2] = stem_pack2<MODE>(v, x, 2 * q2, p);
+#pragma unroll
+          for (int q2 = 8; q2 < 16; ++q2) w[q2] = 0u;
+        }
+        uint8_t* ob = so + (out_uses & 1) * kStemGOutBytes + q * (kStemGOutBytes / 4);
+        // The bulk copy that last read this buffer (two tiles ago) is done reading.
+        if (lead) bulk_wait_group_read<1>();
+        named_barrier(qbar, 64);
+        write_tile(ob, w);
         fence_proxy_async_smem();                        // generic writes -> bulk-copy reads
         named_barrier(qbar, 64);
         if (lead) {                                      // one group per timestep tile
@@ -743,6 +811,7 @@ stem_tc_gen_kernel(const __grid_constant__ StemParams p) {
                           static_cast<uint32_t>(nq) * row_bytes);
           bulk_commit_group();
         }
+      }
       }
     }
     if (lead) bulk_wait_group<0>();                      // stores complete before the block exits

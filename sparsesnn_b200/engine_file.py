@@ -118,9 +118,9 @@ def save_plan(model, path):
             else:
                 w.node(OP_CONV, ins[0], in1, out, _conv_desc(L),
                        (P(L.weight_blob), P(L.bn_scale), P(L.bn_bias), 0))
-        elif n.kind == npl.STEM:
-            w.node(OP_STEM, ins[0], NO_TENSOR, out, n.desc, tuple(P(t) for t in n.params) + (0,),
-                   n.ints)
+        elif n.kind == npl.STEM:                         # dual form: in1 = the spike output
+            w.node(OP_STEM, ins[0], NO_TENSOR if n.out2 is None else tid(n.out2), out, n.desc,
+                   tuple(P(t) for t in n.params) + (0,), n.ints)
         elif n.kind == npl.HEAD:
             w.node(OP_HEAD, ins[0], NO_TENSOR, out, None, (P(n.params[0]), P(n.params[1]), 0, 0),
                    n.ints)

@@ -2,8 +2,9 @@
 
 Mirrors the reference model (``models/msresnet.py``):
 * stem ``TDBNContainer(Conv2d 7x7/2, BatchNorm3d)`` without a neuron
-  (``:135-138``): ``snn_stem_forward`` with no neuron writes the fp16 BN
-  output, computed once and repeated over T (direct encoding, ``:156-158``);
+  (``:135-138``): ``snn_stem_forward_dual`` writes the fp16 BN output,
+  computed once and repeated over T (direct encoding, ``:156-158``), and in
+  the same pass block 0's ``sn1`` (the LIF of that output);
 * ``BasicBlock18`` (``:94-123``) as three fused launches: the LIF of the
   real-valued stream (``sn1``, ``snn_lif_forward``); conv1 + BN + LIF
   (``conv_bn1`` then ``sn2``, one fused sparse layer); conv2 + BN with the
@@ -72,19 +73,26 @@ class MSResNet34(PlanModel):
                          num_classes=params["fc_w"].shape[0], device=device)
         dev = self.device
         s, b = fold_bn(**st["bn"])
+        # The stem writes its fp16 BN output AND block 0's sn1 (the LIF of that
+        # output over T) in one pass (snn_stem_forward_dual).
         self.stem_desc = rt.make_desc(T=T, B=batch, Cin=cin, H=H, W=W, Cout=cout, KH=kh, KW=kw,
-                                      stride=2, pad=kh // 2, neuron="none")
+                                      stride=2, pad=kh // 2, tau=tau, v_threshold=v_threshold)
         h = (H + 2 * (kh // 2) - kh) // 2 + 1
         w_ = (W + 2 * (kw // 2) - kw) // 2 + 1
+        s1_stem = self.buf((T * batch, h, w_, cout))
         x = self.add(Node(STEM, "stem", [INPUT], self.buf((T * batch, h, w_, cout)), self.stem_desc,
-                          (self.param(st["w"]), self.param(s), self.param(b)), (1, 0, 0, 0, 0)))
+                          (self.param(st["w"]), self.param(s), self.param(b)), (1, 0, 0, 0, 0),
+                          out2=s1_stem))
         nkw = dict(T=T, B=batch, tau=tau, v_threshold=v_threshold, device=dev)
         c = cout
         for i, blk in enumerate(params["blocks"]):
             stride = blk["stride"]
-            s1 = self.add(Node(LIF, f"b{i}.sn1", [x], self.buf((T * batch, h, w_, c)),
-                               glue_desc(T=T, B=batch, C=c, H=h, W=w_, tau=tau,
-                                         v_threshold=v_threshold)))
+            if i == 0:
+                s1 = s1_stem
+            else:
+                s1 = self.add(Node(LIF, f"b{i}.sn1", [x], self.buf((T * batch, h, w_, c)),
+                                   glue_desc(T=T, B=batch, C=c, H=h, W=w_, tau=tau,
+                                             v_threshold=v_threshold)))
             l1 = SparseConvBNLIF(blk["w1"], *fold_bn(**blk["bn1"]), H=h, W=w_, stride=stride,
                                  pad=1, **nkw)
             o1 = self.add(Node(CONV, f"b{i}.conv1", [s1], self.buf(l1.out_shape()), layer=l1))

@@ -38,6 +38,7 @@ class Node:
     layer: object = None           # CONV: the SparseConvBNLIF
     attn: dict = field(default_factory=dict)   # ATTN: N, heads, head_dim, scale
     workspace: object = None       # CONV: fp32 workspace of the timestep-split form, or None
+    out2: object = None            # STEM: spikes of desc.neuron on the fp16 BN output (dual form)
 
 
 class PlanModel:
@@ -105,8 +106,13 @@ class PlanModel:
                     workspace=n.workspace)
         elif n.kind == STEM:
             w, sc, bi = n.params
-            rt.check(lib.snn_stem_forward(n.desc, n.ints[0], ins[0].data_ptr(), w.data_ptr(),
-                                          sc.data_ptr(), bi.data_ptr(), out.data_ptr(), s))
+            if n.out2 is not None:
+                rt.check(lib.snn_stem_forward_dual(n.desc, n.ints[0], ins[0].data_ptr(),
+                                                   w.data_ptr(), sc.data_ptr(), bi.data_ptr(),
+                                                   out.data_ptr(), n.out2.data_ptr(), s))
+            else:
+                rt.check(lib.snn_stem_forward(n.desc, n.ints[0], ins[0].data_ptr(), w.data_ptr(),
+                                              sc.data_ptr(), bi.data_ptr(), out.data_ptr(), s))
         elif n.kind == HEAD:
             fw, fb = n.params
             T, B, HW, C, NC = n.ints

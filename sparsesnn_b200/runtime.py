@@ -42,7 +42,7 @@ NEURONS = {"lif": SNN_NEURON_LIF, "if": SNN_NEURON_IF, "none": SNN_NEURON_NONE,
 EXPORTED = (
     "snn_abi_version", "snn_init", "snn_conv_variant", "snn_conv_out_shape", "snn_conv_weight_bytes",
     "snn_pack_weight_24", "snn_conv_forward", "snn_conv_forward_res", "snn_conv_forward_res2",
-    "snn_stem_forward", "snn_spikformer_attn_forward", "snn_add_lif_forward",
+    "snn_stem_forward", "snn_stem_forward_dual", "snn_spikformer_attn_forward", "snn_add_lif_forward",
     "snn_maxpool_lif_forward", "snn_lif_forward", "snn_conv_tsplit_workspace_bytes",
     "snn_conv_forward_tsplit", "snn_conv_forward_tsplit_static",
     "snn_head_forward", "snn_get_device_error", "snn_last_error_message",
@@ -88,6 +88,7 @@ def _declare(lib):
         "snn_conv_forward_res": ([D, P, P, P, P, P, P, P, P], ctypes.c_int),
         "snn_conv_forward_res2": ([D, P, P, P, P, P, P, P, P, P], ctypes.c_int),
         "snn_stem_forward": ([D, i32, P, P, P, P, P, P], ctypes.c_int),
+        "snn_stem_forward_dual": ([D, i32, P, P, P, P, P, P, P], ctypes.c_int),
         "snn_head_forward": ([i32, i32, i32, i32, i32, P, P, P, P, P], ctypes.c_int),
         "snn_add_lif_forward": ([D, P, P, P, P, P], ctypes.c_int),
         "snn_maxpool_lif_forward": ([D, P, P, P, P], ctypes.c_int),

@@ -78,6 +78,13 @@ def test_msresnet_stem(setup):
     got = from_nhwc(model.buffer("stem").float().cpu().numpy(), T, B)
     ref = trace["stem"]
     assert (np.abs(got - ref) <= 2.0 ** -10 * np.abs(ref) + 1e-4).all()
+    # The same pass writes block 0's sn1: the LIF of the stem's own fp16
+    # output over T, bit for bit.
+    stem = next(n for n in model.nodes if n.name == "stem")
+    s1 = from_nhwc(stem.out2.float().cpu().numpy(), T, B)
+    spk, _, _ = L.multistep_lif(got)
+    assert np.array_equal(s1, spk)
+    assert 0.01 < s1.mean() < 0.9
 
 
 def test_msresnet_teacher_forced_blocks(setup):
@@ -91,12 +98,14 @@ def test_msresnet_teacher_forced_blocks(setup):
     worst_rel = 0.0
     for i, p in enumerate(P["blocks"]):
         xin = f16(prev)                               # the stream as the kernels store it
-        # sn1: LIF of the fp16 stream, exact
-        n = nodes[f"b{i}.sn1"]
-        s1 = torch.empty_like(dev(xin))
-        rt.check(lib.snn_lif_forward(n.desc, dev(xin).data_ptr(), None, s1.data_ptr(), stream))
-        spk, _, _ = L.multistep_lif(xin)
-        assert np.array_equal(from_nhwc(s1.float().cpu().numpy(), T, B), spk), f"b{i}.sn1"
+        # sn1: LIF of the fp16 stream, exact (block 0's comes from the stem's
+        # dual pass, checked in test_msresnet_stem)
+        if i > 0:
+            n = nodes[f"b{i}.sn1"]
+            s1 = torch.empty_like(dev(xin))
+            rt.check(lib.snn_lif_forward(n.desc, dev(xin).data_ptr(), None, s1.data_ptr(), stream))
+            spk, _, _ = L.multistep_lif(xin)
+            assert np.array_equal(from_nhwc(s1.float().cpu().numpy(), T, B), spk), f"b{i}.sn1"
         # conv1 + BN + LIF on the oracle's sn1 spikes
         l1 = nodes[f"b{i}.conv1"].layer
         got = from_nhwc(l1(dev(trace[f"b{i}.s1"])).float().cpu().numpy(), T, B)

@@ -86,3 +86,49 @@ def test_stem_parity(cuda_device, case):
     assert set(np.unique(got)) <= {0.0, 1.0}
     frac, ok, _, _ = L.spike_agreement(got, spk, h)
     assert frac >= 0.995 and ok, frac
+
+
+@pytest.mark.parametrize("case", [
+    dict(H=40, W=40, Cout=64, k=7, stride=2, Tin=1, neuron="lif", tau=2.0),     # TMA windows
+    dict(H=29, W=29, Cout=64, k=7, stride=2, Tin=1, neuron="lif", tau=3.0),     # cp.async windows
+    dict(H=30, W=36, Cout=64, k=7, stride=2, Tin=8, Cin=2, neuron="if", tau=2.0),
+    dict(H=12, W=140, Cout=48, k=3, stride=1, Tin=1, neuron="lif", tau=2.0),
+], ids=["rgb7x7s2_tma", "rgb7x7s2_cpasync_tau3", "frames_if", "c48_w140"])
+def test_stem_dual_output(cuda_device, case):
+    """snn_stem_forward_dual: its fp16 BN output equals the no-neuron stem's
+    bit for bit, and its spikes equal the neuron over T run on that output
+    (the standalone LIF node after MS-ResNet's stem), bit for bit."""
+    import torch
+    from sparsesnn_b200 import runtime as rt
+    lib = rt.load()
+    rng = np.random.default_rng(21)
+    Cin, k, stride, Tin = case.get("Cin", 3), case["k"], case["stride"], case["Tin"]
+    T, B = max(4, Tin), 3
+    H, W, Cout = case["H"], case["W"], case["Cout"]
+    x = rng.standard_normal((Tin, B, Cin, H, W)).astype(np.float32)
+    w = (rng.standard_normal((Cout, Cin, k, k)) * 0.6 / k).astype(np.float32)
+    scale = rng.uniform(0.5, 1.5, Cout).astype(np.float32)
+    bias = rng.normal(0.3, 0.2, Cout).astype(np.float32)
+    plain = run_stem(x, w, scale, bias, T, "none", 2.0, Tin, stride)      # [T][B][C][OH][OW]
+    d = rt.make_desc(T=T, B=B, Cin=Cin, H=H, W=W, Cout=Cout, KH=k, KW=k, stride=stride,
+                     pad=k // 2, neuron=case["neuron"], tau=case["tau"])
+    OH, OW = plain.shape[3], plain.shape[4]
+    n_out = T * B * OH * OW * Cout
+    bufs = [torch.full((n_out + GUARD,), SENTINEL, dtype=torch.float16, device="cuda")
+            for _ in range(2)]
+    xd, wd, sd, bd = (torch.from_numpy(a).cuda() for a in (x, w, scale, bias))
+    rc = lib.snn_stem_forward_dual(ctypes.byref(d), Tin, xd.data_ptr(), wd.data_ptr(),
+                                   sd.data_ptr(), bd.data_ptr(), bufs[0].data_ptr(),
+                                   bufs[1].data_ptr(), None)
+    assert rc == 0, lib.snn_last_error_message()
+    torch.cuda.synchronize()
+    assert rt.device_error() == 0
+    for b in bufs:
+        assert bool((b[n_out:] == SENTINEL).all()), "dual stem wrote past an output"
+    conv = lambda t: np.transpose(t[:n_out].float().cpu().numpy().reshape(T, B, OH, OW, Cout),  # noqa: E731
+                                  (0, 1, 4, 2, 3))
+    bn, spikes = conv(bufs[0]), conv(bufs[1])
+    assert np.array_equal(bn, plain)
+    ref, _, _ = L.multistep_lif(bn, tau=case["tau"], neuron=case["neuron"])
+    assert np.array_equal(spikes, ref)
+    assert 0.02 < ref.mean() < 0.9
