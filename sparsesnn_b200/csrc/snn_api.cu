@@ -1040,6 +1040,14 @@ int snn_conv_forward_tsplit(const snn_conv_desc* d, const void* data, const void
   d1.neuron = SNN_NEURON_NONE;
   d1.flags = d->flags & SNN_FLAG_FORCE_GENERIC;
   d1.res_mode = SNN_RES_ADD_AFTER;
+  // With fewer 64-pixel tiles per timestep group than SMs, the general
+  // kernel (a 64-pixel x 4-timestep tile per CTA) spreads the work wider than
+  // the resident-weight halo kernel (timesteps walked in order inside a CTA):
+  // measured 16.3 against 21.3 us for a DVS stage-2 conv (16 x 16, 128
+  // channels, 16 images per group).
+  if (select_variant(&d1, g) == SNN_VARIANT_HALO_RESIDENT &&
+      static_cast<long long>(d1.B) * g.OH * g.OW < 64LL * g_num_sms)
+    d1.flags |= SNN_FLAG_FORCE_GENERIC;
   if ((st = launch_conv(&d1, data, weight, nullptr, nullptr, bn_scale, bn_bias, nullptr,
                         snn::kResNone, workspace, stream)))
     return st;
