@@ -176,7 +176,7 @@ int snn_conv_forward_res2(const snn_conv_desc* d, const void* data, const void* 
  * snn_conv_forward / snn_conv_forward_res (LIF or IF neuron, no dense weights)
  * plus a device workspace of at least snn_conv_tsplit_workspace_bytes()
  * bytes, 16-byte aligned, owned by the caller, reused across calls (out and
- * residual 16-byte aligned, state 8-byte aligned).  No
+ * residual 16-byte aligned).  No
  * counterpart in the reference: its fused kernels keep the T loop inside one
  * CTA (sengine/kernels/conv2d_bn_if_t4.py:952-1020). */
 int snn_conv_tsplit_workspace_bytes(const snn_conv_desc* d, size_t* bytes);

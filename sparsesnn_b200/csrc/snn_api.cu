@@ -1027,8 +1027,6 @@ int snn_conv_forward_tsplit(const snn_conv_desc* d, const void* data, const void
   if ((reinterpret_cast<uintptr_t>(workspace) | reinterpret_cast<uintptr_t>(out) |
        reinterpret_cast<uintptr_t>(residual)) & 15)
     return fail(SNN_E_INVALID, "workspace, out and residual must be 16-byte aligned");
-  if (reinterpret_cast<uintptr_t>(state) & 7)
-    return fail(SNN_E_INVALID, "state must be 8-byte aligned");
   // Phase 1: conv + BN of all T*B images, no neuron, fp32 into the
   // workspace.  The leading [T*B] dimension is regrouped as [T'][B'] so that
   // the general kernel keeps its four-timestep accumulators: the images are
@@ -1081,7 +1079,7 @@ int snn_conv_forward_tsplit(const snn_conv_desc* d, const void* data, const void
     case 7: k = snn::tsplit_neuron_kernel<snn::kModeIf, snn::kResAddAfter>; break;
     default: k = snn::tsplit_neuron_kernel<snn::kModeIf, snn::kResAddBefore>; break;
   }
-  const long long n = p.P * (d->Cout / 2);
+  const long long n = p.P * d->Cout;
   const long long blocks = std::max<long long>(1, std::min<long long>((n + 255) / 256,
                                                                     static_cast<long long>(g_num_sms) * 8));
   cudaError_t e = launch_pdl(k, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream, p);

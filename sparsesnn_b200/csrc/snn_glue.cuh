@@ -972,16 +972,15 @@ glue_neuron_kernel(const GlueParams p) {
 // ------------------------------------------------ timestep-split neuron scan
 // Second phase of the timestep-split fused layer (snn_conv_forward_tsplit):
 // the first phase ran the conv + BN for all T*B images at once (no neuron,
-// fp32 BN output z); here thread = (pixel, 2 channels) runs the neuron over
-// T with the membrane in registers, adds the residual (after the neuron: the
-// SEW add; before it: the neuron integrates bn + residual) and writes fp16
-// spikes.  The layers this form serves have few neurons per timestep (a
-// 4x4x512 DVS stage-4 map is 32k), so a thread owns only two of them, and
-// the loads of kTsplitBatch timesteps are issued together before their
-// neuron steps run, keeping that many HBM round trips in flight per thread.
-// The arithmetic is the fused epilogue's (for tau = 2 the input is halved
-// exactly, as there), so the spikes equal the one-pass layer's for the same
-// BN outputs.
+// fp32 BN output z); here thread = (pixel, channel) runs the neuron over T
+// with the membrane in a register, adds the residual (after the neuron: the
+// SEW add; before it: the neuron integrates bn + residual) and writes the
+// fp16 spike.  The layers this form serves have few neurons per timestep (a
+// 4x4x512 DVS stage-4 map is 32k), so a thread owns one, and the loads of
+// kTsplitBatch timesteps are issued together before their neuron steps run:
+// one HBM round trip for all of T <= 16.  The arithmetic is the fused
+// epilogue's (for tau = 2 the input is halved exactly, as there), so the
+// spikes equal the one-pass layer's for the same BN outputs.
 struct TsplitParams {
   const float* z;          // [T][P][C] BN output
   const __half* residual;  // [T][P][C] or null
@@ -991,62 +990,45 @@ struct TsplitParams {
   int T, C, flags;
   float tau, decay, v_th, v_reset;
 };
-constexpr int kTsplitBatch = 8;
+constexpr int kTsplitBatch = 16;
 
 template <int MODE, int RM>
 __global__ void __launch_bounds__(256)
 tsplit_neuron_kernel(const TsplitParams p) {
   pdl_launch_dependents();
   pdl_wait();
-  const int c2n = p.C / 2;
-  const long long n = p.P * c2n;
-  const size_t plane = static_cast<size_t>(p.P) * p.C;     // elements per timestep
+  const long long n = p.P * p.C;                           // neurons per timestep
+  const size_t plane = static_cast<size_t>(n);
   for (long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; idx < n;
        idx += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const size_t base = static_cast<size_t>(idx) * 2;       // = pixel * C + 2 * (channel pair)
-    float v[2];
-    if (p.flags & kReadState) {
-      const float2 s2 = *reinterpret_cast<const float2*>(p.state + base);
-      v[0] = s2.x; v[1] = s2.y;
-    } else {
-      v[0] = v[1] = 0.f;
-    }
+    const size_t base = static_cast<size_t>(idx);          // = pixel * C + channel
+    float v = (p.flags & kReadState) ? p.state[base] : 0.f;
     for (int t0 = 0; t0 < p.T; t0 += kTsplitBatch) {
-      float2 zb[kTsplitBatch];
-      __half2 rb[kTsplitBatch];
+      float zb[kTsplitBatch];
+      __half rb[kTsplitBatch];
 #pragma unroll
       for (int j = 0; j < kTsplitBatch; ++j) {
         if (t0 + j < p.T) {
           const size_t off = static_cast<size_t>(t0 + j) * plane + base;
-          zb[j] = __ldg(reinterpret_cast<const float2*>(p.z + off));
-          if constexpr (RM != kResNone) rb[j] = __ldg(reinterpret_cast<const __half2*>(p.residual + off));
+          zb[j] = __ldg(p.z + off);
+          if constexpr (RM != kResNone) rb[j] = p.residual[off];
         }
       }
 #pragma unroll
       for (int j = 0; j < kTsplitBatch; ++j) {
         if (t0 + j >= p.T) break;
-        float2 rf = make_float2(0.f, 0.f);
-        if constexpr (RM != kResNone) rf = __half22float2(rb[j]);
-        uint32_t bits = 0;
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const float x = e ? zb[j].y : zb[j].x;
-          const float r = e ? rf.y : rf.x;
-          // kModeLifHalf takes bn/2 (exact), plus r/2 when the residual enters the neuron.
-          float xi = MODE == kModeLifHalf ? x * 0.5f : x;
-          if constexpr (RM == kResAddBefore) xi = __fadd_rn(xi, MODE == kModeLifHalf ? r * 0.5f : r);
-          const bool s = neuron_step<MODE>(v[e], xi, p.decay, p.tau, p.v_th, p.v_reset);
-          if constexpr (RM == kResAddAfter) {
-            bits |= static_cast<uint32_t>(__half_as_ushort(__float2half_rn((s ? 1.f : 0.f) + r)))
-                    << (16 * e);
-          } else {
-            bits |= (s ? 0x3C00u : 0u) << (16 * e);
-          }
-        }
-        *reinterpret_cast<uint32_t*>(p.out + static_cast<size_t>(t0 + j) * plane + base) = bits;
+        const float r = RM != kResNone ? __half2float(rb[j]) : 0.f;
+        // kModeLifHalf takes bn/2 (exact), plus r/2 when the residual enters the neuron.
+        float xi = MODE == kModeLifHalf ? zb[j] * 0.5f : zb[j];
+        if constexpr (RM == kResAddBefore) xi = __fadd_rn(xi, MODE == kModeLifHalf ? r * 0.5f : r);
+        const bool sp = neuron_step<MODE>(v, xi, p.decay, p.tau, p.v_th, p.v_reset);
+        __half o;
+        if constexpr (RM == kResAddAfter) o = __float2half_rn((sp ? 1.f : 0.f) + r);
+        else o = __ushort_as_half(sp ? 0x3C00u : 0u);
+        p.out[static_cast<size_t>(t0 + j) * plane + base] = o;
       }
     }
-    if (p.flags & kWriteState) *reinterpret_cast<float2*>(p.state + base) = make_float2(v[0], v[1]);
+    if (p.flags & kWriteState) p.state[base] = v;
   }
 }
 
