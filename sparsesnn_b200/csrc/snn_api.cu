@@ -1028,24 +1028,27 @@ int snn_conv_forward_tsplit(const snn_conv_desc* d, const void* data, const void
        reinterpret_cast<uintptr_t>(residual)) & 15)
     return fail(SNN_E_INVALID, "workspace, out and residual must be 16-byte aligned");
   // Phase 1: conv + BN of all T*B images, no neuron, fp32 into the
-  // workspace.  The leading [T*B] dimension is regrouped as [T'][B'] so that
-  // the general kernel keeps its four-timestep accumulators: the images are
-  // independent here, only the order of the flat index matters.
+  // workspace.  The images are independent here, only the order of the flat
+  // [T*B] index matters, so it is regrouped as [T'][B'] to suit the kernel:
+  // T' = 1 where the halo kernels then serve it -- the resident-weight halo
+  // kernel (timesteps outer, so B' = T*B images give it many tiles), or the
+  // streaming halo kernel on 4x4 images (a tile is four whole images) --
+  // else T' = 2: two-timestep tiles, twice the CTAs of four-timestep ones.
+  // Measured at the DVS shapes (64 images): stage-2 3x3 21.3 (T' = 4) ->
+  // 10.3 us, stage-3 19.8 -> 13.8, stage-4 28.6 -> 18.0, strided 3x3
+  // 16.4 -> 12.0 and 21.2 -> 16.0 us.
   snn_conv_desc d1 = *d;
   const long long tb = static_cast<long long>(d->T) * d->B;
-  d1.T = tb % 4 == 0 ? 4 : tb % 2 == 0 ? 2 : 1;
-  d1.B = static_cast<int32_t>(tb / d1.T);
   d1.neuron = SNN_NEURON_NONE;
   d1.flags = d->flags & SNN_FLAG_FORCE_GENERIC;
   d1.res_mode = SNN_RES_ADD_AFTER;
-  // With fewer 64-pixel tiles per timestep group than SMs, the general
-  // kernel (a 64-pixel x 4-timestep tile per CTA) spreads the work wider than
-  // the resident-weight halo kernel (timesteps walked in order inside a CTA):
-  // measured 16.3 against 21.3 us for a DVS stage-2 conv (16 x 16, 128
-  // channels, 16 images per group).
-  if (select_variant(&d1, g) == SNN_VARIANT_HALO_RESIDENT &&
-      static_cast<long long>(d1.B) * g.OH * g.OW < 64LL * g_num_sms)
-    d1.flags |= SNN_FLAG_FORCE_GENERIC;
+  d1.T = 1;
+  d1.B = static_cast<int32_t>(tb);
+  const int v1 = select_variant(&d1, g);
+  const bool t1 = v1 == SNN_VARIANT_HALO_RESIDENT ||
+                  (v1 == SNN_VARIANT_HALO_STREAM && g.OH == 4 && g.OW == 4);
+  d1.T = (t1 || tb % 2) ? 1 : 2;
+  d1.B = static_cast<int32_t>(tb / d1.T);
   if ((st = launch_conv(&d1, data, weight, nullptr, nullptr, bn_scale, bn_bias, nullptr,
                         snn::kResNone, workspace, stream)))
     return st;

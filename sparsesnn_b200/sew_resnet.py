@@ -356,10 +356,12 @@ class SEWResNet18DVS(PlanModel):
         def conv(name, layer, ins):
             # Long T on few images: 3x3 layers of >= 128 channels run in the
             # timestep-split form (all T*B images' GEMMs spread over the SMs,
-            # then the neuron scan), measured 1.5-2.7x faster at T = 16 on 4
-            # images; the 64-channel and 1x1 layers stay one-pass.
+            # then the neuron scan), measured 1.2-4.6x faster at T = 16 on 4
+            # images, as are the 1x1 downsamples to >= 256 channels (1.4x);
+            # the 64-channel layers and the first 1x1 downsample stay one-pass.
             ws = None
-            if split_t and T >= 8 and layer.desc.KH * layer.desc.KW > 1 and layer.Cout >= 128:
+            d = layer.desc
+            if split_t and T >= 8 and ((d.KH * d.KW > 1 and layer.Cout >= 128) or layer.Cout >= 256):
                 ws = self.split_workspace(layer)
             return self.add(Node(CONV, name, ins, self.buf(layer.out_shape()), layer=layer,
                                  workspace=ws))
