@@ -87,8 +87,9 @@ def peaks():
 
 def spikformer_linear_layers(dev, stream, sparse_peak, iters=10):
     """The Linear + BN + LIF twin at Spikformer-8-384 shapes (T=4, batch 32,
-    196 tokens: 6272 rows per timestep; q/k/v/proj 384->384, fc1 384->1536,
-    fc2 1536->384), random 2:4 weights and Bernoulli(0.2) spikes: per-layer
+    196 tokens: 6272 rows per timestep; one of q/k/v and proj 384->384, the
+    fused q|k|v layer the model runs 384->1152, fc1 384->1536, fc2
+    1536->384), random 2:4 weights and Bernoulli(0.2) spikes: per-layer
     CUDA-event time and dense-equivalent TFLOP/s against the 2:4 ceiling."""
     import numpy as np
     import torch
@@ -96,7 +97,8 @@ def spikformer_linear_layers(dev, stream, sparse_peak, iters=10):
     from sparsesnn_b200.pruning import prune_2_4_last
     T, rows = 4, 32 * 196
     out = {}
-    for name, cin, cout in (("qkv", 384, 384), ("fc1", 384, 1536), ("fc2", 1536, 384)):
+    for name, cin, cout in (("q", 384, 384), ("qkv_fused", 384, 1152), ("fc1", 384, 1536),
+                            ("fc2", 1536, 384)):
         rng = np.random.default_rng(0)
         w = prune_2_4_last(rng.standard_normal((cout, cin)).astype(np.float32) * (2.0 / cin) ** 0.5)
         layer = SparseConvBNLIF(w, np.ones(cout, np.float32), np.zeros(cout, np.float32),
