@@ -71,7 +71,15 @@ enum { SNN_FLAG_READ_STATE = 1, SNN_FLAG_WRITE_STATE = 2,
        /* Attention only: q, k and v are the three channel blocks of one
         * [T*B][N][3*heads*head_dim] tensor (rows of 3*C elements, as one
         * fused q|k|v Linear writes them); pass q, k = q + C and v = q + 2C. */
-       SNN_FLAG_QKV_PACKED = 32 };
+       SNN_FLAG_QKV_PACKED = 32,
+       /* Bit-packed spikes: a [T*B][H][W][C] spike tensor stored as
+        * [T*B][H][W][C/8] bytes, channel c in bit c%8 of byte c/8 (C a
+        * multiple of 16).  Written by snn_stem_forward (LIF or IF neuron,
+        * general tensor-core stem geometries), read by
+        * snn_maxpool_lif_forward with SNN_NEURON_NONE (the pool after a
+        * neuron, whose fp16 output is then the pooled spikes): an eighth of
+        * the fp16 bytes between the two. */
+       SNN_FLAG_SPIKE_BITS = 64 };
 
 /* Where the residual of a fused Add enters the epilogue (the reference's
  * pattern strings and templates, sengine/kernels/interleaved_templates.py:371-397):
@@ -209,7 +217,9 @@ int snn_conv_forward_tsplit_static(const snn_conv_desc* d, const void* data, con
  * models/sewresnet.py:199-201) or Tin = T.  w: [Cout][Cin][KH][KW] fp32.
  * out: [T][B][OH][OW][Cout] fp16 spikes, or with d->neuron ==
  * SNN_NEURON_NONE the fp16 BN output (MS-ResNet's stem feeds the real-valued
- * residual stream, models/msresnet.py:135-138,161). */
+ * residual stream, models/msresnet.py:135-138,161).  With SNN_FLAG_SPIKE_BITS
+ * in d->flags the spikes leave bit-packed, [T][B][OH][OW][Cout/8] bytes
+ * (general tensor-core stem geometries only, as for snn_stem_forward_dual). */
 int snn_stem_forward(const snn_conv_desc* d, int32_t Tin, const float* x, const float* w,
                      const float* bn_scale, const float* bn_bias, void* out, void* stream);
 
@@ -253,7 +263,9 @@ int snn_add_lif_forward(const snn_conv_desc* d, const void* a, const void* b, fl
  * d->neuron == SNN_NEURON_NONE gives the plain max pool (state unused): the
  * pool that follows a neuron, e.g. SEW-ResNet's stem maxpool
  * (models/sewresnet.py:202-203) or a Spikformer SPS pool
- * (models/spikformer.py:192-197).
+ * (models/spikformer.py:192-197).  That plain pool also reads bit-packed
+ * spikes (SNN_FLAG_SPIKE_BITS in d->flags, C a multiple of 16, no state
+ * flags): x is then [T*B][H][W][C/8] bytes and out the pooled fp16 spikes.
  *   x      [T*B][H][W][C] fp16;   out [T*B][OH][OW][C] fp16 spikes (or maxima)
  *   state  [B*OH*OW][C] fp32 membrane */
 int snn_maxpool_lif_forward(const snn_conv_desc* d, const void* x, float* state, void* out,

@@ -800,6 +800,11 @@ int launch_glue(const snn_conv_desc* d, bool pool, const void* a, const void* b,
   if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
        reinterpret_cast<uintptr_t>(out)) & 15)
     return fail(SNN_E_INVALID, "tensors must be 16-byte aligned");
+  const bool bits = (d->flags & SNN_FLAG_SPIKE_BITS) != 0;
+  if (bits && (!pool || !no_neuron || d->Cout % 16 ||
+               (d->flags & (SNN_FLAG_READ_STATE | SNN_FLAG_WRITE_STATE))))
+    return fail(SNN_E_INVALID, "bit-packed input: plain max pool (SNN_NEURON_NONE, no state) of "
+                               "a multiple of 16 channels only");
   snn::GlueParams p;
   memset(&p, 0, sizeof(p));
   p.a = static_cast<const __half*>(a);
@@ -831,6 +836,17 @@ int launch_glue(const snn_conv_desc* d, bool pool, const void* a, const void* b,
   const long long blocks = std::max<long long>(1, std::min<long long>((n + 255) / 256,
                                                                     static_cast<long long>(g_num_sms) * 16));
   GlueKernel k = glue_fn<false>(mode);
+  if (bits) {
+    // Thread = (output pixel of one image, 16-channel word), over all T*B images.
+    const long long nb = static_cast<long long>(d->T) * d->B * p.OH * p.OW * (d->Cout / 16);
+    const long long bb = std::max<long long>(1, std::min<long long>((nb + 255) / 256,
+                                                                  static_cast<long long>(g_num_sms) * 16));
+    k = (d->KH == 3 && d->KW == 3) ? snn::maxpool_bits_kernel<3>
+      : (d->KH == 2 && d->KW == 2) ? snn::maxpool_bits_kernel<2> : snn::maxpool_bits_kernel<0>;
+    cudaError_t e = launch_pdl(k, dim3(static_cast<unsigned>(bb)), dim3(256), 0, stream, p);
+    if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));
+    return SNN_OK;
+  }
   if (pool) {
     // Square 2x2 / 3x3 windows issue all their loads at once.
     k = (d->KH == 3 && d->KW == 3) ? glue_fn<true, 3>(mode)
@@ -1109,6 +1125,9 @@ static int stem_forward_impl(const snn_conv_desc* d, int32_t Tin, const float* x
     return fail(SNN_E_INVALID, "dual stem: the neuron of the spike output must be LIF or IF");
   if (out2 && ((reinterpret_cast<uintptr_t>(out2) & 15) || out2 == out))
     return fail(SNN_E_INVALID, "dual stem: out_spikes must be a separate 16-byte aligned tensor");
+  const bool bits = (d->flags & SNN_FLAG_SPIKE_BITS) != 0;
+  if (bits && (out2 || d->neuron == SNN_NEURON_NONE))
+    return fail(SNN_E_INVALID, "bit-packed stem output: spikes of a LIF or IF neuron, single output");
   const int OH = (d->H + 2 * d->pad - d->KH) / d->stride + 1;
   const int OW = (d->W + 2 * d->pad - d->KW) / d->stride + 1;
   if (OH < 1 || OW < 1) return fail(SNN_E_INVALID, "empty output");
@@ -1127,7 +1146,7 @@ static int stem_forward_impl(const snn_conv_desc* d, int32_t Tin, const float* x
     return fail(SNN_E_CUDA, "error word address");
   // Tensor-core fast path: 3x3 s1 p1, 64 channels, input repeated over T,
   // rows of at most 128 pixels.
-  if (!out2 && Tin == 1 && d->neuron != SNN_NEURON_NONE && d->KH == 3 && d->KW == 3 && d->stride == 1 &&
+  if (!out2 && !bits && Tin == 1 && d->neuron != SNN_NEURON_NONE && d->KH == 3 && d->KW == 3 && d->stride == 1 &&
       d->pad == 1 && d->Cout == 64 &&
       (d->Cin == 1 || d->Cin == 3) && OW <= snn::kStemPx) {
     const int mode = d->neuron == SNN_NEURON_IF ? snn::kModeIf
@@ -1196,14 +1215,15 @@ static int stem_forward_impl(const snn_conv_desc* d, int32_t Tin, const float* x
     const long long nblk = std::max<long long>(1, std::min<long long>(n_tiles, g_num_sms));
     if ((reinterpret_cast<uintptr_t>(out) & 15) == 0) {
       p.out2 = static_cast<__half*>(out2);
+      p.bits_out = bits ? 1 : 0;
       cudaError_t e = launch_pdl(stem_tcg_fn(mode, out2 != nullptr), dim3(static_cast<unsigned>(nblk)),
                                  dim3(snn::kStemGThreads), smem, stream, p);
       if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));
       return SNN_OK;
     }
   }
-  if (out2)
-    return fail(SNN_E_INVALID, "dual stem needs the general tensor-core stem (Cout <= 64, "
+  if (out2 || bits)
+    return fail(SNN_E_INVALID, "dual or bit-packed stem needs the general tensor-core stem (Cout <= 64, "
                 "Cin*KH*KW <= %d, staged window <= %d bytes, out 16-byte aligned)",
                 snn::kStemGMaxK, snn::kStemGMaxStage);
   const long long pixels = static_cast<long long>(d->B) * OH * OW;

@@ -132,8 +132,10 @@ int parse_engine_file(const char* path, SnnEngineHeader* h, std::vector<SnnEngin
         const int64_t ow = (int64_t(d.W) + 2 * d.pad - d.KW) / d.stride + 1;
         if (oh < 1 || ow < 1) return fail(SNN_E_INVALID, "engine node %u (stem): empty output", n);
         const uint64_t px = uint64_t(d.B) * d.H * d.W;
+        // SNN_FLAG_SPIKE_BITS: the spikes leave bit-packed, Cout/8 bytes a pixel.
+        const uint64_t px_bytes = (d.flags & SNN_FLAG_SPIKE_BITS) ? uint64_t(d.Cout) / 8 : uint64_t(d.Cout) * 2;
         if (nd.i[0] < 1 || in_bytes < uint64_t(nd.i[0]) * d.Cin * px * 4 ||
-            out_bytes < uint64_t(d.T) * d.B * uint64_t(oh) * uint64_t(ow) * d.Cout * 2 ||
+            out_bytes < uint64_t(d.T) * d.B * uint64_t(oh) * uint64_t(ow) * px_bytes ||
             !off_ok(nd.p0, uint64_t(d.Cout) * d.Cin * d.KH * d.KW * 4) ||
             !off_ok(nd.p1, uint64_t(d.Cout) * 4) || !off_ok(nd.p2, uint64_t(d.Cout) * 4))
           return fail(SNN_E_INVALID, "engine node %u (stem): sizes or offsets out of range", n);
@@ -195,10 +197,12 @@ int parse_engine_file(const char* path, SnnEngineHeader* h, std::vector<SnnEngin
       case kOpLif:
       case kOpAddLif:
       case kOpMaxPoolLif: {
-        if (d.T < 1 || d.B < 1 || d.H < 1 || d.W < 1 || d.Cout < 1 || d.flags != 0)
+        // The max pool may read bit-packed spikes (SNN_FLAG_SPIKE_BITS, Cout/8 bytes a pixel).
+        const bool bits = nd.op == kOpMaxPoolLif && d.flags == SNN_FLAG_SPIKE_BITS;
+        if (d.T < 1 || d.B < 1 || d.H < 1 || d.W < 1 || d.Cout < 1 || (d.flags != 0 && !bits))
           return fail(SNN_E_INVALID, "engine node %u (glue): bad shape or flags", n);
-        const uint64_t in_need = uint64_t(d.T) * d.B * d.H * d.W * d.Cout * 2;
-        uint64_t out_need = in_need;
+        const uint64_t in_need = uint64_t(d.T) * d.B * d.H * d.W * (bits ? uint64_t(d.Cout) / 8 : uint64_t(d.Cout) * 2);
+        uint64_t out_need = uint64_t(d.T) * d.B * d.H * d.W * d.Cout * 2;
         if (nd.op == kOpMaxPoolLif) {
           if (d.KH < 1 || d.KW < 1 || d.stride < 1 || d.pad < 0)
             return fail(SNN_E_INVALID, "engine node %u (maxpool): bad window", n);

@@ -28,6 +28,7 @@ struct StemParams {
   int tma_in;                     // general tensor-core path: input windows arrive by TMA
   int in_pitch;                   // general path: staged row pitch (ICp with TMA, else IC)
   __half* out2;                   // general path, dual output: spikes of the fp16 BN output
+  int bits_out;                   // general path: `out` holds bit-packed spikes [T][B][OH][OW][Cout/8]
 };
 
 // One thread = one output pixel x 16 consecutive output channels
@@ -786,6 +787,29 @@ stem_tc_gen_kernel(const __grid_constant__ StemParams p) {
             bulk_commit_group();
           }
         }
+      } else if (MODE != kModeNone && p.bits_out) {
+        // Bit-packed spikes (SNN_FLAG_SPIKE_BITS), stored straight from
+        // registers: this pixel's 32 (or 16) channels as u16 words, channel
+        // c in bit c%16 of word c/16 -- a sixteenth of the fp16 tile.
+        const int wn = p.Cout / 16;
+        uint16_t* ob = reinterpret_cast<uint16_t*>(p.out) + (pix0 + lane) * wn + c0 / 16;
+        for (int t = t_first; t <= t_last; ++t) {
+          uint32_t m = 0;
+          if (nch == 4) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              m |= neuron_step<MODE>(v[j], x[j], p.decay, p.tau, p.v_th, p.v_reset) ? 1u << j : 0u;
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              m |= neuron_step<MODE>(v[j], x[j], p.decay, p.tau, p.v_th, p.v_reset) ? 1u << j : 0u;
+          }
+          if (lane < nq && nch > 0) {
+            uint16_t* o = ob + static_cast<size_t>(t) * P * wn;
+            o[0] = static_cast<uint16_t>(m);
+            if (nch == 4) o[1] = static_cast<uint16_t>(m >> 16);
+          }
+        }
       } else {
       for (int t = t_first; t <= t_last; ++t, ++out_uses) {
         uint32_t w[16];
@@ -966,6 +990,51 @@ glue_neuron_kernel(const GlueParams p) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) p.state[pix * p.C + c8 * 8 + j] = v[j];
     }
+  }
+}
+
+// Plain max pool of bit-packed spikes (no neuron): the maximum of 0/1
+// spikes is their OR, so thread = (output pixel of one of the T*B images,
+// 16-channel word) ORs the u16 words of its window (padding contributes
+// nothing, as -inf never wins the max of a window holding a real pixel) and
+// writes the 16 channels as fp16 0/1, two 16-byte stores.  a: the packed
+// input [T*B][H][W][C/8] bytes; out: [T*B][OH][OW][C] fp16.
+template <int KS>
+__global__ void __launch_bounds__(256)
+maxpool_bits_kernel(const GlueParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int wn = p.C / 16;
+  const uint16_t* in = reinterpret_cast<const uint16_t*>(p.a);
+  const long long n = static_cast<long long>(p.T) * p.B * p.OH * p.OW * wn;
+  const int KH = KS > 0 ? KS : p.KH, KW = KS > 0 ? KS : p.KW;
+  for (long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; idx < n;
+       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long pix = idx / wn;                           // over T*B*OH*OW
+    const int w = static_cast<int>(idx - pix * wn);
+    const int ow = static_cast<int>(pix % p.OW);
+    const long long r = pix / p.OW;
+    const int oh = static_cast<int>(r % p.OH);
+    const long long img = r / p.OH;
+    const uint16_t* plane = in + static_cast<size_t>(img) * p.H * p.W * wn + w;
+    uint32_t m = 0;
+#pragma unroll
+    for (int kh = 0; kh < KH; ++kh) {
+      const int ih = oh * p.stride + kh - p.pad;
+#pragma unroll
+      for (int kw = 0; kw < KW; ++kw) {
+        const int iw = ow * p.stride + kw - p.pad;
+        if (ih >= 0 && ih < p.H && iw >= 0 && iw < p.W)
+          m |= __ldg(plane + (static_cast<size_t>(ih) * p.W + iw) * wn);
+      }
+    }
+    uint32_t o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      o[j] = ((m >> (2 * j)) & 1u ? 0x3C00u : 0u) | ((m >> (2 * j + 1)) & 1u ? 0x3C000000u : 0u);
+    uint4* dst = reinterpret_cast<uint4*>(p.out + static_cast<size_t>(pix) * p.C + w * 16);
+    dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+    dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
   }
 }
 

@@ -137,7 +137,7 @@ def save_plan(model, path):
                        i=(ins[2], n.attn["N"], n.attn["heads"], n.attn["head_dim"], 0))
         else:
             d = rt.SnnConvDesc.from_buffer_copy(bytes(n.desc))
-            d.flags = 0
+            d.flags = n.desc.flags & rt.SNN_FLAG_SPIKE_BITS   # a pool of bit-packed spikes
             w.node(kinds[n.kind], ins[0], in1, out, d)
     w.write(path, tid(npl.INPUT), tid(npl.LOGITS), T, B)
     return path

@@ -28,6 +28,7 @@ SNN_FLAG_FORCE_GENERIC = 4
 SNN_FLAG_CTA_PAIR = 8
 SNN_FLAG_DENSE = 16
 SNN_FLAG_QKV_PACKED = 32
+SNN_FLAG_SPIKE_BITS = 64
 SNN_VARIANT_GENERIC = 0
 SNN_VARIANT_HALO_RESIDENT = 1
 SNN_VARIANT_HALO_STREAM = 2

@@ -20,6 +20,7 @@ last 64-channel k-block reads zeros past its input channels.
 from __future__ import annotations
 
 import numpy as np
+import torch
 
 from . import runtime as rt
 from .layer import SparseConvBNLIF, fold_bn
@@ -84,7 +85,12 @@ class Spikformer(PlanModel):
         s, b = fold_bn(**st["bn"])
         self.stem_desc = rt.make_desc(T=T, B=batch, Cin=cin, H=H, W=W, Cout=c0, KH=3, KW=3,
                                       stride=1, pad=1, **lif)
-        x = self.add(Node(STEM, "sps0", [INPUT], self.buf((TB, H, W, c0)), self.stem_desc,
+        # The stem's spikes go only to the first max pool: they travel
+        # bit-packed (an eighth of the fp16 bytes at full resolution).
+        bits = rt.SNN_FLAG_SPIKE_BITS if c0 % 16 == 0 else 0
+        self.stem_desc.flags = bits
+        sps0 = self.buf((TB, H, W, c0 // 8), torch.uint8) if bits else self.buf((TB, H, W, c0))
+        x = self.add(Node(STEM, "sps0", [INPUT], sps0, self.stem_desc,
                           (self.param(st["w"]), self.param(s), self.param(b)), (1, 0, 0, 0, 0)))
         h, w_, c = H, W, c0
         for i in range(4):
@@ -95,9 +101,10 @@ class Spikformer(PlanModel):
                 x = self.add(Node(CONV, f"sps{i}", [x], self.buf(layer.out_shape()), layer=layer))
                 c = layer.Cout
             ph, pw = pool_out(h, 3, 2, 1), pool_out(w_, 3, 2, 1)
-            x = self.add(Node(MAXPOOL, f"pool{i}", [x], self.buf((TB, ph, pw, c)),
-                              glue_desc(T=T, B=batch, C=c, H=h, W=w_, neuron="none", k=3,
-                                        stride=2, pad=1)))
+            pd = glue_desc(T=T, B=batch, C=c, H=h, W=w_, neuron="none", k=3, stride=2, pad=1)
+            if i == 0:
+                pd.flags = bits
+            x = self.add(Node(MAXPOOL, f"pool{i}", [x], self.buf((TB, ph, pw, c)), pd))
             h, w_ = ph, pw
         p = params["rpe"]
         rpe = SparseConvBNLIF(p["w"], *fold_bn(**p["bn"]), T=T, B=batch, H=h, W=w_, pad=1,

@@ -87,3 +87,34 @@ def test_add_lif_vs_oracle(cuda_device, neuron, tau, v_th):
     ref, _, rv = add_lif(a, b, neuron=neuron, tau=tau, v_th=v_th)
     assert np.array_equal(y, ref)
     assert np.array_equal(v, rv)
+
+
+@pytest.mark.parametrize("k, s, pad, H, W, C", [(3, 2, 1, 17, 23, 48), (2, 2, 0, 8, 6, 32),
+                                                (3, 1, 1, 5, 7, 16), (1, 1, 0, 3, 4, 64)])
+def test_maxpool_of_bit_packed_spikes(cuda_device, k, s, pad, H, W, C):
+    """SNN_FLAG_SPIKE_BITS: the plain max pool of bit-packed spikes
+    ([T*B][H][W][C/8] bytes, channel c in bit c%8 of byte c/8) equals the
+    pool of the same spikes as fp16, bit for bit, and writes nothing past
+    its output."""
+    import torch
+    from sparsesnn_b200 import runtime as rt
+    rng = np.random.default_rng(k * 1000 + H * 10 + C)
+    T, B = 3, 2
+    x = (rng.random((T, B, C, H, W)) < 0.2).astype(np.float32)
+    ref, _ = run("pool", x, k=k, s=s, pad=pad, neuron="none")
+    packed = np.packbits(nhwc(x).astype(np.uint8), axis=-1, bitorder="little")
+    d = rt.make_desc(T=T, B=B, Cin=C, H=H, W=W, Cout=C, KH=k, KW=k, stride=s, pad=pad,
+                     neuron="none", flags=rt.SNN_FLAG_SPIKE_BITS)
+    OH, OW = (H + 2 * pad - k) // s + 1, (W + 2 * pad - k) // s + 1
+    n_out = T * B * OH * OW * C
+    buf = torch.full((n_out + 4096,), 7.0, dtype=torch.float16, device="cuda")
+    src = torch.from_numpy(packed).cuda()
+    lib = rt.load()
+    rt.check(lib.snn_maxpool_lif_forward(d, src.data_ptr(), None, buf.data_ptr(),
+                                         torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    assert rt.device_error() == 0
+    assert bool((buf[n_out:] == 7.0).all()), "bit-packed pool wrote past its output"
+    y = from_nhwc(buf[:n_out].float().cpu().numpy().reshape(T * B, OH, OW, C), T, B)
+    assert np.array_equal(y, ref)
+    assert 0.1 < y.mean() < 0.95

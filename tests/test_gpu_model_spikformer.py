@@ -33,6 +33,15 @@ def from_nhwc(y, T_, B_):
     return np.transpose(y.reshape(T_, B_, h, w, c), (0, 1, 4, 2, 3))
 
 
+def pack_bits(y_nhwc):
+    """fp16 0/1 spikes [.., C] -> bit-packed bytes [.., C/8] (channel c in bit c%8 of byte c/8)."""
+    return np.packbits(y_nhwc.astype(np.uint8), axis=-1, bitorder="little")
+
+
+def unpack_bits(b_nhwc):
+    return np.unpackbits(b_nhwc, axis=-1, bitorder="little").astype(np.float32)
+
+
 def _bn(p):
     return L.BNParams(p["gamma"], p["beta"], p["mean"], p["var"])
 
@@ -81,7 +90,11 @@ def test_spikformer_patch_splitting(setup):
     model(torch.from_numpy(x))
     torch.cuda.synchronize()
     # stem
-    got = from_nhwc(model.buffer("sps0").float().cpu().numpy(), T, B)
+    sps0 = model.buffer("sps0")
+    if nodes["sps0"].desc.flags & rt.SNN_FLAG_SPIKE_BITS:   # bit-packed stem spikes
+        got = from_nhwc(unpack_bits(sps0.cpu().numpy()), T, B)
+    else:
+        got = from_nhwc(sps0.float().cpu().numpy(), T, B)
     z = L.batchnorm_eval(L.conv2d_nchw(x, P["sps"][0]["w"], 1, 1), _bn(P["sps"][0]["bn"]))
     _, h, _ = L.multistep_lif(np.repeat(z[None], T, 0))
     judge(got, trace["sps0"], h, "sps0")
@@ -96,6 +109,8 @@ def test_spikformer_patch_splitting(setup):
         # pool of the oracle's spikes, exact
         n = nodes[f"pool{i}"]
         src = dev(trace[f"sps{i}"])
+        if n.desc.flags & rt.SNN_FLAG_SPIKE_BITS:            # the pool reads packed spikes
+            src = torch.from_numpy(pack_bits(to_nhwc(trace[f"sps{i}"]))).to("cuda:0")
         out = torch.empty_like(dev(trace[f"pool{i}"]))
         rt.check(lib.snn_maxpool_lif_forward(n.desc, src.data_ptr(), None, out.data_ptr(), s))
         torch.cuda.synchronize()

@@ -132,3 +132,53 @@ def test_stem_dual_output(cuda_device, case):
     ref, _, _ = L.multistep_lif(bn, tau=case["tau"], neuron=case["neuron"])
     assert np.array_equal(spikes, ref)
     assert 0.02 < ref.mean() < 0.9
+
+
+@pytest.mark.parametrize("case", [
+    dict(H=12, W=140, Cout=48, k=3, stride=1, Tin=1, neuron="lif", tau=2.0),     # Spikformer's
+    dict(H=29, W=29, Cout=64, k=7, stride=2, Tin=1, neuron="if", tau=2.0),
+    dict(H=30, W=36, Cout=32, k=7, stride=2, Tin=8, Cin=2, neuron="lif", tau=3.0),
+    dict(H=16, W=16, Cout=16, k=3, stride=1, Tin=1, neuron="lif", tau=2.0),
+    dict(H=32, W=32, Cout=64, k=3, stride=1, Tin=1, neuron="lif", tau=2.0),     # CIFAR geometry
+], ids=["c48_w140", "rgb7x7s2_if", "frames_tau3", "c16", "cifar"])
+def test_stem_bit_packed_output(cuda_device, case):
+    """SNN_FLAG_SPIKE_BITS: the stem's spikes bit-packed ([T*B][OH][OW][C/8]
+    bytes, channel c in bit c%8 of byte c/8) unpack to the fp16 spikes of the
+    same general stem bit for bit (the CIFAR geometry's fp16 spikes come
+    from the row-tiled kernel: there the oracle's parity rule), and nothing
+    past the packed tensor is written."""
+    import torch
+    from sparsesnn_b200 import runtime as rt
+    lib = rt.load()
+    rng = np.random.default_rng(33)
+    Cin, k, stride, Tin = case.get("Cin", 3), case["k"], case["stride"], case["Tin"]
+    T, B = max(4, Tin), 3
+    H, W, Cout = case["H"], case["W"], case["Cout"]
+    x = rng.standard_normal((Tin, B, Cin, H, W)).astype(np.float32)
+    w = (rng.standard_normal((Cout, Cin, k, k)) * 0.9 / k).astype(np.float32)
+    scale = rng.uniform(0.5, 1.5, Cout).astype(np.float32)
+    bias = rng.normal(0.3, 0.2, Cout).astype(np.float32)
+    fp16 = run_stem(x, w, scale, bias, T, case["neuron"], case["tau"], Tin, stride)
+    d = rt.make_desc(T=T, B=B, Cin=Cin, H=H, W=W, Cout=Cout, KH=k, KW=k, stride=stride,
+                     pad=k // 2, neuron=case["neuron"], tau=case["tau"],
+                     flags=rt.SNN_FLAG_SPIKE_BITS)
+    OH, OW = fp16.shape[3], fp16.shape[4]
+    n_out = T * B * OH * OW * Cout // 8
+    buf = torch.full((n_out + GUARD,), 0xA5, dtype=torch.uint8, device="cuda")
+    xd, wd, sd, bd = (torch.from_numpy(a).cuda() for a in (x, w, scale, bias))
+    rc = lib.snn_stem_forward(ctypes.byref(d), Tin, xd.data_ptr(), wd.data_ptr(), sd.data_ptr(),
+                              bd.data_ptr(), buf.data_ptr(), None)
+    assert rc == 0, lib.snn_last_error_message()
+    torch.cuda.synchronize()
+    assert rt.device_error() == 0
+    assert bool((buf[n_out:] == 0xA5).all()), "bit-packed stem wrote past its output"
+    packed = buf[:n_out].cpu().numpy().reshape(T, B, OH, OW, Cout // 8)
+    got = np.transpose(np.unpackbits(packed, axis=-1, bitorder="little").astype(np.float32),
+                       (0, 1, 4, 2, 3))
+    if Cout == 64 and k == 3 and stride == 1 and Tin == 1:      # fp16 from the row-tiled kernel
+        spk, h, _ = reference(x, w, scale, bias, T, case["neuron"], case["tau"], stride)
+        frac, ok, _, _ = L.spike_agreement(got, spk, h)
+        assert frac >= 0.995 and ok, frac
+    else:
+        assert np.array_equal(got, fp16)
+    assert 0.02 < got.mean() < 0.9
