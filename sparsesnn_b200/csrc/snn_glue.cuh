@@ -467,6 +467,9 @@ stem_tc_gen_kernel(const __grid_constant__ StemParams p) {
   uint64_t* in_full = acc_empty + 2;                          // [2] staged window landed (TMA)
   uint64_t* drain = in_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  // TMA windows: [0] requested by the builders' thread 0, [1] waited for by
+  // the builders, [2] requested by the epilogue's window thread.
+  int* win_state = reinterpret_cast<int*>(tmem_slot + 1);
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
 
   if (tid == 0) {
@@ -477,6 +480,7 @@ stem_tc_gen_kernel(const __grid_constant__ StemParams p) {
       mbar_init(&in_full[i], 1);
     }
     mbar_init(drain, 1);
+    win_state[0] = win_state[1] = win_state[2] = 0;
     fence_mbar_init();
     if (p.tma_in) prefetch_tmap(&p.tmap_in);
   }
@@ -533,25 +537,29 @@ stem_tc_gen_kernel(const __grid_constant__ StemParams p) {
     *oh0 = (rest - bb * tiles_h) * R;
     *b = bb;
   };
+  // TMA input windows: unit u's window into buffer u & 1, its first column
+  // rounded down to a 16-byte boundary (negative coordinates read zero).
+  // The builders' thread 0 requests units 0 and 1; the window of unit u + 2
+  // is requested by one epilogue thread once the MMAs of unit u are complete
+  // (so every builder is done reading buffer u & 1), keeping the ~1k-cycle
+  // issue off the builders' path.
+  const uint32_t in_bytes = static_cast<uint32_t>(XP) * IR * p.Cin * 4;
+  auto load_window = [&](int u) {
+    int b, oh0, ow0;
+    tile_origin(unit_tile(u), &b, &oh0, &ow0);
+    const int g = u % n_gemm;
+    const int iw0 = ow0 * p.stride - p.pad;
+    fence_proxy_async_smem();
+    mbar_arrive_expect_tx(&in_full[u & 1], in_bytes);
+    tma_load_5d(xs0 + (u & 1) * (kStemGMaxStage / 4), &p.tmap_in, &in_full[u & 1], iw0 & ~3,
+                oh0 * p.stride - p.pad, 0, b, g);
+  };
   if (warp < kStemGEpi0) {
     // ------------------------------------------------ builders + MMA issue
     const int HW = p.H * p.W;
     const int px = tid & 127, half = tid >> 7;           // pixel; column half of each k-tile
     const int pr = px / TW, pc = px - (px / TW) * TW;    // pixel's row and column in the tile
     const int pofs = pr * p.stride * XP + pc * p.stride; // this pixel's window origin
-    const uint32_t in_bytes = static_cast<uint32_t>(XP) * IR * p.Cin * 4;
-    // TMA (thread 0): unit u's window into buffer u & 1, its first column
-    // rounded down to a 16-byte boundary (negative coordinates read zero).
-    auto load_window = [&](int u) {
-      int b, oh0, ow0;
-      tile_origin(unit_tile(u), &b, &oh0, &ow0);
-      const int g = u % n_gemm;
-      const int iw0 = ow0 * p.stride - p.pad;
-      fence_proxy_async_smem();
-      mbar_arrive_expect_tx(&in_full[u & 1], in_bytes);
-      tma_load_5d(xs0 + (u & 1) * (kStemGMaxStage / 4), &p.tmap_in, &in_full[u & 1], iw0 & ~3,
-                  oh0 * p.stride - p.pad, 0, b, g);
-    };
     // cp.async (all builders): unit u's window, rows of pitch XP = IC.
     auto stage_window = [&](int u, float* dst) {
       int b, oh0, ow0;
@@ -574,18 +582,21 @@ stem_tc_gen_kernel(const __grid_constant__ StemParams p) {
     };
     const uint32_t idesc = idesc_tf32(128, 128);
     int kc = 0;                                          // k-tiles built so far (ring position)
-    int requested = 0, waited = 0;                       // TMA windows (thread 0 issues)
+    int requested = 0, waited = 0;                       // TMA windows (thread 0: the first two)
     bool ok = true, ok0 = true, issued = false;          // ok0, issued: thread 0 (MMA issuer)
     if (n_units > 0) {
       if (!p.tma_in) stage_window(0, xs0);
-      else if (tid == 0) { load_window(0); requested = 1; }
+      else if (tid == 0) {
+        load_window(0);
+        if (n_units > 1) load_window(1);
+        requested = min(n_units, 2);
+      }
     }
     for (int un = 0; ok && un < n_units; ++un) {
       // Every builder passed the previous unit's last k-tile barrier, so the
       // buffer of unit un - 1 is free for unit un + 1.
       bool okw = true;
       if (p.tma_in) {
-        if (tid == 0 && un + 1 < n_units) { load_window(un + 1); requested = un + 2; }
         okw = mbar_wait_bounded_sleep(&in_full[un & 1], static_cast<uint32_t>((un >> 1) & 1), p.timeout);
         waited = un + 1;
         if (!okw && p.err) atomicOr(p.err, kErrTimeoutFull);
@@ -666,10 +677,9 @@ stem_tc_gen_kernel(const __grid_constant__ StemParams p) {
     }
     if (!p.tma_in) cp_async_wait<0>();
     if (tid == 0) {
-      // Windows requested but not waited for (a stopped run) land before the
-      // block exits; every MMA issued completes before TMEM is released.
-      for (int u = waited; u < requested; ++u)
-        mbar_wait_bounded_sleep(&in_full[u & 1], static_cast<uint32_t>((u >> 1) & 1), p.timeout);
+      win_state[0] = requested;
+      win_state[1] = waited;
+      // Every MMA issued completes before TMEM is released.
       if (issued) {
         mma_commit(drain);
         if (!mbar_wait_bounded(drain, 0, p.timeout) && p.err) atomicOr(p.err, kErrTimeoutDrain);
@@ -684,6 +694,8 @@ stem_tc_gen_kernel(const __grid_constant__ StemParams p) {
     const int qbar = 2 + q;                              // the quarter's two warps
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
     const int row_bytes = p.Cout * 2;
+    const bool win_thread = p.tma_in && q == 0 && h == 1 && lane == 0;   // requests windows u + 2
+    int win_req = 0;
     float v[32];
     uint32_t out_uses = 0;                               // timestep tiles written so far
     for (int un = 0; un < n_units; ++un) {
@@ -695,6 +707,7 @@ stem_tc_gen_kernel(const __grid_constant__ StemParams p) {
         if (!okw && p.err) atomicOr(p.err, kErrTimeoutAcc);
       }
       if (named_barrier_or(qbar, 64, !okw)) break;
+      if (win_thread && un + 2 < n_units) { load_window(un + 2); win_req = un + 3; }
       tc_fence_after();
       float x[32];
 #pragma unroll
@@ -839,10 +852,19 @@ stem_tc_gen_kernel(const __grid_constant__ StemParams p) {
       }
     }
     if (lead) bulk_wait_group<0>();                      // stores complete before the block exits
+    if (win_thread) win_state[2] = win_req;
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
+    if (lane == 0) {
+      // Windows requested but not waited for (a stopped run) land before the
+      // block exits.
+      const int req = max(win_state[0], win_state[2]);
+      for (int u = win_state[1]; u < req; ++u)
+        mbar_wait_bounded_sleep(&in_full[u & 1], static_cast<uint32_t>((u >> 1) & 1), p.timeout);
+    }
+    __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, 256);
   }
