@@ -529,13 +529,32 @@ stem_tc_gen_kernel(const __grid_constant__ StemParams p) {
   const int bx = static_cast<int>(blockIdx.x), gx = static_cast<int>(gridDim.x);
   const int my_tiles = bx < n_tiles ? (n_tiles - 1 - bx) / gx + 1 : 0;
   const int n_units = my_tiles * n_gemm;
-  auto unit_tile = [&](int u) { return bx + (u / n_gemm) * gx; };
-  auto tile_origin = [&](int tile, int* b, int* oh0, int* ow0) {
-    const int rest = tile / tiles_w;
-    *ow0 = (tile - rest * tiles_w) * TW;
-    const int bb = rest / tiles_h;
-    *oh0 = (rest - bb * tiles_h) * R;
-    *b = bb;
+  // Unit cursor: unit u's GEMM g and tile (column wi, row hi, image b),
+  // stepped one unit at a time with compares instead of divisions (the
+  // kernel is issue-bound): the next unit is the next GEMM of the same tile,
+  // or the first GEMM of the tile gx further on.
+  struct UnitCursor { int g, wi, hi, b; };
+  const int step_w = gx % tiles_w, step_r = gx / tiles_w;
+  const int step_h = step_r % tiles_h, step_b = step_r / tiles_h;
+  auto cursor_at_first = [&]() {
+    UnitCursor c;
+    const int rest = bx / tiles_w;
+    c.g = 0;
+    c.wi = bx - rest * tiles_w;
+    c.b = rest / tiles_h;
+    c.hi = rest - c.b * tiles_h;
+    return c;
+  };
+  auto cursor_next = [&](UnitCursor& c) {
+    if (++c.g < n_gemm) return;
+    c.g = 0;
+    c.wi += step_w;
+    int cy = c.wi >= tiles_w;
+    if (cy) c.wi -= tiles_w;
+    c.hi += step_h + cy;
+    cy = c.hi >= tiles_h;
+    if (cy) c.hi -= tiles_h;
+    c.b += step_b + cy;
   };
   // TMA input windows: unit u's window into buffer u & 1, its first column
   // rounded down to a 16-byte boundary (negative coordinates read zero).
@@ -544,15 +563,12 @@ stem_tc_gen_kernel(const __grid_constant__ StemParams p) {
   // (so every builder is done reading buffer u & 1), keeping the ~1k-cycle
   // issue off the builders' path.
   const uint32_t in_bytes = static_cast<uint32_t>(XP) * IR * p.Cin * 4;
-  auto load_window = [&](int u) {
-    int b, oh0, ow0;
-    tile_origin(unit_tile(u), &b, &oh0, &ow0);
-    const int g = u % n_gemm;
-    const int iw0 = ow0 * p.stride - p.pad;
+  auto load_window = [&](const UnitCursor& c, int u) {
+    const int iw0 = c.wi * TW * p.stride - p.pad;
     fence_proxy_async_smem();
     mbar_arrive_expect_tx(&in_full[u & 1], in_bytes);
     tma_load_5d(xs0 + (u & 1) * (kStemGMaxStage / 4), &p.tmap_in, &in_full[u & 1], iw0 & ~3,
-                oh0 * p.stride - p.pad, 0, b, g);
+                c.hi * R * p.stride - p.pad, 0, c.b, c.g);
   };
   if (warp < kStemGEpi0) {
     // ------------------------------------------------ builders + MMA issue
@@ -561,12 +577,9 @@ stem_tc_gen_kernel(const __grid_constant__ StemParams p) {
     const int pr = px / TW, pc = px - (px / TW) * TW;    // pixel's row and column in the tile
     const int pofs = pr * p.stride * XP + pc * p.stride; // this pixel's window origin
     // cp.async (all builders): unit u's window, rows of pitch XP = IC.
-    auto stage_window = [&](int u, float* dst) {
-      int b, oh0, ow0;
-      tile_origin(unit_tile(u), &b, &oh0, &ow0);
-      const int g = u % n_gemm;
-      const int ih0 = oh0 * p.stride - p.pad, iw0 = ow0 * p.stride - p.pad;
-      const float* xin = p.x + (static_cast<size_t>(g) * p.B + b) * static_cast<size_t>(p.Cin) * HW;
+    auto stage_window = [&](const UnitCursor& c, float* dst) {
+      const int ih0 = c.hi * R * p.stride - p.pad, iw0 = c.wi * TW * p.stride - p.pad;
+      const float* xin = p.x + (static_cast<size_t>(c.g) * p.B + c.b) * static_cast<size_t>(p.Cin) * HW;
       for (int row = warp; row < p.Cin * IR; row += kStemGBuild / 32) {
         const int ci = row / IR, ih = ih0 + row - ci * IR;
         const bool rv = ih >= 0 && ih < p.H;
@@ -584,15 +597,18 @@ stem_tc_gen_kernel(const __grid_constant__ StemParams p) {
     int kc = 0;                                          // k-tiles built so far (ring position)
     int requested = 0, waited = 0;                       // TMA windows (thread 0: the first two)
     bool ok = true, ok0 = true, issued = false;          // ok0, issued: thread 0 (MMA issuer)
+    UnitCursor cur = cursor_at_first();                  // unit un
     if (n_units > 0) {
-      if (!p.tma_in) stage_window(0, xs0);
+      if (!p.tma_in) stage_window(cur, xs0);
       else if (tid == 0) {
-        load_window(0);
-        if (n_units > 1) load_window(1);
+        load_window(cur, 0);
+        UnitCursor c1 = cur;
+        cursor_next(c1);
+        if (n_units > 1) load_window(c1, 1);
         requested = min(n_units, 2);
       }
     }
-    for (int un = 0; ok && un < n_units; ++un) {
+    for (int un = 0; ok && un < n_units; ++un, cursor_next(cur)) {
       // Every builder passed the previous unit's last k-tile barrier, so the
       // buffer of unit un - 1 is free for unit un + 1.
       bool okw = true;
@@ -601,20 +617,23 @@ stem_tc_gen_kernel(const __grid_constant__ StemParams p) {
         waited = un + 1;
         if (!okw && p.err) atomicOr(p.err, kErrTimeoutFull);
       } else {
-        if (un + 1 < n_units) stage_window(un + 1, xs0 + ((un + 1) & 1) * (kStemGMaxStage / 4));
+        if (un + 1 < n_units) {
+          UnitCursor c1 = cur;
+          cursor_next(c1);
+          stage_window(c1, xs0 + ((un + 1) & 1) * (kStemGMaxStage / 4));
+        }
         else cp_async_commit();                          // an empty group keeps the counting uniform
         cp_async_wait<1>();                              // this unit's window has landed
         named_barrier(1, kStemGBuild);
       }
-      int b, oh0, ow0;
-      tile_origin(unit_tile(un), &b, &oh0, &ow0);
+      const int oh0 = cur.hi * R, ow0 = cur.wi * TW;
       const int iw0 = ow0 * p.stride - p.pad;
       const float* xs = xs0 + (un & 1) * (kStemGMaxStage / 4) + (p.tma_in ? iw0 - (iw0 & ~3) : 0);
       const bool pv = pr < R && oh0 + pr < p.OH && ow0 + pc < p.OW;
       const int a = un & 1;
       for (int kt = 0; kt < nk; ++kt, ++kc) {
-        const int s = kc % S;
-        const int use = kc / S;
+        const int s = S == 2 ? (kc & 1) : 0;             // S is 1 or 2
+        const int use = S == 2 ? (kc >> 1) : kc;
         bool okk = okw;
         if (okk && use > 0) {                            // the MMAs that read this stage are done
           okk = mbar_wait_bounded_sleep(&a_empty[s], static_cast<uint32_t>((use - 1) & 1), p.timeout);
@@ -698,16 +717,23 @@ stem_tc_gen_kernel(const __grid_constant__ StemParams p) {
     int win_req = 0;
     float v[32];
     uint32_t out_uses = 0;                               // timestep tiles written so far
-    for (int un = 0; un < n_units; ++un) {
+    UnitCursor cur = cursor_at_first();                  // unit un
+    for (int un = 0; un < n_units; ++un, cursor_next(cur)) {
       const int a = un & 1;
-      const int g = un % n_gemm;
+      const int g = cur.g;
       bool okw = true;
       if (lead) {
         okw = mbar_wait_bounded_sleep(&acc_full[a], static_cast<uint32_t>((un >> 1) & 1), p.timeout);
         if (!okw && p.err) atomicOr(p.err, kErrTimeoutAcc);
       }
       if (named_barrier_or(qbar, 64, !okw)) break;
-      if (win_thread && un + 2 < n_units) { load_window(un + 2); win_req = un + 3; }
+      if (win_thread && un + 2 < n_units) {
+        UnitCursor c2 = cur;
+        cursor_next(c2);
+        cursor_next(c2);
+        load_window(c2, un + 2);
+        win_req = un + 3;
+      }
       tc_fence_after();
       float x[32];
 #pragma unroll
@@ -728,8 +754,7 @@ stem_tc_gen_kernel(const __grid_constant__ StemParams p) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = 0.f;
       }
-      int b, oh0, ow0;
-      tile_origin(unit_tile(un), &b, &oh0, &ow0);
+      const int b = cur.b, oh0 = cur.hi * R, ow0 = cur.wi * TW;
       const int npix = R == 1 ? min(TW, p.OW - ow0) : min(R, p.OH - oh0) * p.OW;
       const int nq = max(0, min(32, npix - 32 * q));     // this quarter's valid pixels
       const long long pix0 = (static_cast<long long>(b) * p.OH + oh0) * p.OW + ow0 + 32 * q;
