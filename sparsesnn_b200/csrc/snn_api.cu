@@ -772,13 +772,18 @@ int launch_conv(const snn_conv_desc* d, const void* data, const void* weight, fl
 
 namespace {
 using GlueKernel = void (*)(const snn::GlueParams);
-template <bool POOL, int KS = 0>
+template <bool POOL, int KS = 0, typename I = long long>
 GlueKernel glue_fn(int mode) {
-  if (mode == snn::kModeLifHalf) return snn::glue_neuron_kernel<snn::kModeLifHalf, POOL, KS>;
-  if (mode == snn::kModeLifDiv) return snn::glue_neuron_kernel<snn::kModeLifDiv, POOL, KS>;
+  if (mode == snn::kModeLifHalf) return snn::glue_neuron_kernel<snn::kModeLifHalf, POOL, KS, I>;
+  if (mode == snn::kModeLifDiv) return snn::glue_neuron_kernel<snn::kModeLifDiv, POOL, KS, I>;
   if constexpr (POOL)
-    if (mode == snn::kModeNone) return snn::glue_neuron_kernel<snn::kModeNone, true, KS>;
-  return snn::glue_neuron_kernel<snn::kModeIf, POOL, KS>;
+    if (mode == snn::kModeNone) return snn::glue_neuron_kernel<snn::kModeNone, true, KS, I>;
+  return snn::glue_neuron_kernel<snn::kModeIf, POOL, KS, I>;
+}
+// 32-bit element indices where the grid-stride loop stays below 2^31.
+template <bool POOL, int KS = 0>
+GlueKernel glue_fn_sized(int mode, bool small) {
+  return small ? glue_fn<POOL, KS, int>(mode) : glue_fn<POOL, KS, long long>(mode);
 }
 
 // Shared checks and launch of the Add / MaxPool + neuron glue; one_input:
@@ -832,25 +837,38 @@ int launch_glue(const snn_conv_desc* d, bool pool, const void* a, const void* b,
   const int mode = no_neuron ? snn::kModeNone
                    : d->neuron == SNN_NEURON_IF ? snn::kModeIf
                    : d->tau == 2.0f ? snn::kModeLifHalf : snn::kModeLifDiv;
-  const long long n = static_cast<long long>(d->B) * p.OH * p.OW * (d->Cout / 8);
+  if (no_neuron && !bits && static_cast<long long>(d->T) * d->B <= 0x7fffffffLL &&
+      static_cast<long long>(d->B) * p.OH * p.OW * (d->Cout / 8) < static_cast<long long>(g_num_sms) * 2048) {
+    // The plain pool carries nothing across timesteps: where one thread per
+    // (pixel, 8 channels) would not fill the GPU, its T*B images run as
+    // independent ones, T times the threads (larger pools keep the timestep
+    // loop, which amortises a thread's index arithmetic).
+    p.B = d->T * d->B;
+    p.T = 1;
+  }
+  const long long n = static_cast<long long>(p.B) * p.OH * p.OW * (d->Cout / 8);
   const long long blocks = std::max<long long>(1, std::min<long long>((n + 255) / 256,
                                                                     static_cast<long long>(g_num_sms) * 16));
-  GlueKernel k = glue_fn<false>(mode);
+  const bool small = n + blocks * 256 < (1LL << 31);
+  GlueKernel k = glue_fn_sized<false>(mode, small);
   if (bits) {
-    // Thread = (output pixel of one image, 16-channel word), over all T*B images.
-    const long long nb = static_cast<long long>(d->T) * d->B * p.OH * p.OW * (d->Cout / 16);
-    const long long bb = std::max<long long>(1, std::min<long long>((nb + 255) / 256,
-                                                                  static_cast<long long>(g_num_sms) * 16));
+    // Thread = (output pixel, 16-channel word) of one image (grid y: the
+    // T*B images), 32-bit within an image.
+    if (static_cast<long long>(d->H) * d->W * (d->Cout / 16) >= (1LL << 30))
+      return fail(SNN_E_INVALID, "bit-packed pool: image too large");
+    const long long per_img = static_cast<long long>(p.OH) * p.OW * (d->Cout / 16);
+    const unsigned gxb = static_cast<unsigned>(std::min<long long>((per_img + 255) / 256, 1024));
+    const unsigned gyb = static_cast<unsigned>(std::min<long long>(static_cast<long long>(d->T) * d->B, 65535));
     k = (d->KH == 3 && d->KW == 3) ? snn::maxpool_bits_kernel<3>
       : (d->KH == 2 && d->KW == 2) ? snn::maxpool_bits_kernel<2> : snn::maxpool_bits_kernel<0>;
-    cudaError_t e = launch_pdl(k, dim3(static_cast<unsigned>(bb)), dim3(256), 0, stream, p);
+    cudaError_t e = launch_pdl(k, dim3(gxb, gyb), dim3(256), 0, stream, p);
     if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));
     return SNN_OK;
   }
   if (pool) {
     // Square 2x2 / 3x3 windows issue all their loads at once.
-    k = (d->KH == 3 && d->KW == 3) ? glue_fn<true, 3>(mode)
-      : (d->KH == 2 && d->KW == 2) ? glue_fn<true, 2>(mode) : glue_fn<true>(mode);
+    k = (d->KH == 3 && d->KW == 3) ? glue_fn_sized<true, 3>(mode, small)
+      : (d->KH == 2 && d->KW == 2) ? glue_fn_sized<true, 2>(mode, small) : glue_fn_sized<true>(mode, small);
   }
   cudaError_t e = launch_pdl(k, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream, p);
   if (e != cudaSuccess) return fail(SNN_E_CUDA, "launch: %s", cudaGetErrorString(e));

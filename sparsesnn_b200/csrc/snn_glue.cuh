@@ -940,29 +940,37 @@ __device__ __forceinline__ uint4 glue_neuron8(float (&v)[8], const float (&x)[8]
 }
 
 // KS: compile-time square pool window (2 or 3: every window load is issued
-// before the max, padding reads as -inf), or 0 for a runtime window.
-template <int MODE, bool POOL, int KS = 0>
+// before the max, padding reads as -inf), or 0 for a runtime window.  I: the
+// element index type, int wherever (pixels x 8-channel groups) fits (its
+// divisions are several times cheaper than 64-bit ones), else long long.
+template <int MODE, bool POOL, int KS = 0, typename I = long long>
 __global__ void __launch_bounds__(256)
 glue_neuron_kernel(const GlueParams p) {
   pdl_launch_dependents();
   pdl_wait();
   const int c8n = p.C / 8;
-  const long long P = static_cast<long long>(p.B) * p.OH * p.OW;
-  const long long n = P * c8n;
-  for (long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; idx < n;
-       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const long long pix = idx / c8n;
+  const I P = static_cast<I>(p.B) * p.OH * p.OW;
+  const I n = P * c8n;
+  for (I idx = static_cast<I>(blockIdx.x) * blockDim.x + threadIdx.x; idx < n;
+       idx += static_cast<I>(gridDim.x) * blockDim.x) {
+    const I pix = idx / c8n;
     const int c8 = static_cast<int>(idx - pix * c8n);
+    const size_t spix = static_cast<size_t>(pix);
+    int ow = 0, oh = 0, b = 0;
+    if constexpr (POOL) {
+      const I r = pix / p.OW;
+      ow = static_cast<int>(pix - r * p.OW);
+      const I bb = r / p.OH;
+      oh = static_cast<int>(r - bb * p.OH);
+      b = static_cast<int>(bb);
+    }
     float v[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j)
-      v[j] = (MODE != kModeNone && (p.flags & kReadState)) ? p.state[pix * p.C + c8 * 8 + j] : 0.f;
+      v[j] = (MODE != kModeNone && (p.flags & kReadState)) ? p.state[spix * p.C + c8 * 8 + j] : 0.f;
     for (int t = 0; t < p.T; ++t) {
       float x[8];
       if constexpr (POOL && KS > 0) {
-        const int ow = static_cast<int>(pix % p.OW);
-        const int oh = static_cast<int>((pix / p.OW) % p.OH);
-        const int b = static_cast<int>(pix / (static_cast<long long>(p.OW) * p.OH));
         const uint4 ninf4 = make_uint4(0xFC00FC00u, 0xFC00FC00u, 0xFC00FC00u, 0xFC00FC00u);
         const __half* plane = p.a + (static_cast<size_t>(t) * p.B + b) * p.H * p.W * p.C;
         uint4 win[KS * KS];
@@ -990,9 +998,6 @@ glue_neuron_kernel(const GlueParams p) {
           x[2 * j] = f.x; x[2 * j + 1] = f.y;
         }
       } else if constexpr (POOL) {
-        const int ow = static_cast<int>(pix % p.OW);
-        const int oh = static_cast<int>((pix / p.OW) % p.OH);
-        const int b = static_cast<int>(pix / (static_cast<long long>(p.OW) * p.OH));
         __half2 m[4];
         const __half2 ninf = __halves2half2(__ushort_as_half(0xFC00), __ushort_as_half(0xFC00));
 #pragma unroll
@@ -1017,7 +1022,7 @@ glue_neuron_kernel(const GlueParams p) {
         }
       } else {
         // Add + neuron, or the neuron of one input alone when b is null.
-        const size_t off = (static_cast<size_t>(t) * P + pix) * p.C;
+        const size_t off = (static_cast<size_t>(t) * static_cast<size_t>(P) + spix) * p.C;
         const uint4 ua = __ldg(reinterpret_cast<const uint4*>(p.a + off) + c8);
         const uint4 ub = p.b ? __ldg(reinterpret_cast<const uint4*>(p.b + off) + c8)
                              : make_uint4(0, 0, 0, 0);
@@ -1030,12 +1035,12 @@ glue_neuron_kernel(const GlueParams p) {
           x[2 * j + 1] = fa.y + fb.y;
         }
       }
-      reinterpret_cast<uint4*>(p.out + (static_cast<size_t>(t) * P + pix) * p.C)[c8] =
+      reinterpret_cast<uint4*>(p.out + (static_cast<size_t>(t) * static_cast<size_t>(P) + spix) * p.C)[c8] =
           glue_neuron8<MODE>(v, x, p);
     }
     if (MODE != kModeNone && (p.flags & kWriteState)) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) p.state[pix * p.C + c8 * 8 + j] = v[j];
+      for (int j = 0; j < 8; ++j) p.state[spix * p.C + c8 * 8 + j] = v[j];
     }
   }
 }
@@ -1051,19 +1056,19 @@ __global__ void __launch_bounds__(256)
 maxpool_bits_kernel(const GlueParams p) {
   pdl_launch_dependents();
   pdl_wait();
+  // y: the T*B images; x: (output pixel, word) of one image, 32-bit (the
+  // host keeps H*W*C/16 below 2^31).
   const int wn = p.C / 16;
-  const uint16_t* in = reinterpret_cast<const uint16_t*>(p.a);
-  const long long n = static_cast<long long>(p.T) * p.B * p.OH * p.OW * wn;
+  const int per_img = p.OH * p.OW * wn;
   const int KH = KS > 0 ? KS : p.KH, KW = KS > 0 ? KS : p.KW;
-  for (long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; idx < n;
-       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const long long pix = idx / wn;                           // over T*B*OH*OW
-    const int w = static_cast<int>(idx - pix * wn);
-    const int ow = static_cast<int>(pix % p.OW);
-    const long long r = pix / p.OW;
-    const int oh = static_cast<int>(r % p.OH);
-    const long long img = r / p.OH;
-    const uint16_t* plane = in + static_cast<size_t>(img) * p.H * p.W * wn + w;
+  for (int img = blockIdx.y; img < p.T * p.B; img += gridDim.y) {
+  const uint16_t* plane = reinterpret_cast<const uint16_t*>(p.a) + static_cast<size_t>(img) * p.H * p.W * wn;
+  __half* out_img = p.out + static_cast<size_t>(img) * p.OH * p.OW * p.C;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < per_img; i += gridDim.x * blockDim.x) {
+    const int pix = i / wn;
+    const int w = i - pix * wn;
+    const int oh = pix / p.OW;
+    const int ow = pix - oh * p.OW;
     uint32_t m = 0;
 #pragma unroll
     for (int kh = 0; kh < KH; ++kh) {
@@ -1072,16 +1077,17 @@ maxpool_bits_kernel(const GlueParams p) {
       for (int kw = 0; kw < KW; ++kw) {
         const int iw = ow * p.stride + kw - p.pad;
         if (ih >= 0 && ih < p.H && iw >= 0 && iw < p.W)
-          m |= __ldg(plane + (static_cast<size_t>(ih) * p.W + iw) * wn);
+          m |= __ldg(plane + (ih * p.W + iw) * wn + w);
       }
     }
     uint32_t o[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j)
       o[j] = ((m >> (2 * j)) & 1u ? 0x3C00u : 0u) | ((m >> (2 * j + 1)) & 1u ? 0x3C000000u : 0u);
-    uint4* dst = reinterpret_cast<uint4*>(p.out + static_cast<size_t>(pix) * p.C + w * 16);
+    uint4* dst = reinterpret_cast<uint4*>(out_img + static_cast<size_t>(pix) * p.C + w * 16);
     dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
     dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+  }
   }
 }
 
