@@ -1157,8 +1157,8 @@ tsplit_neuron_kernel(const TsplitParams p) {
 // One block (1024 threads) per image.  Phase 1: thread (c8, slot) sums 8
 // consecutive channels (16-byte loads) over every 16th (t, hw) position; the
 // partial sums are combined in shared memory and scaled: feat = sum / HW / T
-// (exact for the small-integer SEW activations).  Phase 2: one warp per
-// output class, 16-byte weight loads.  dynamic smem = 17*C floats.
+// (exact for the small-integer SEW activations).  Phase 2: a warp per four
+// output classes, 16-byte weight loads.  dynamic smem = 17*C floats.
 constexpr int kHeadSlots = 16;
 __global__ void __launch_bounds__(1024)
 head_pool_fc_kernel(const __half* __restrict__ x, const float* __restrict__ fc_w,
@@ -1174,12 +1174,16 @@ head_pool_fc_kernel(const __half* __restrict__ x, const float* __restrict__ fc_w
   for (int task = threadIdx.x; task < c8n * kHeadSlots; task += blockDim.x) {
     const int c8 = task % c8n, slot = task / c8n;
     float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    // Unrolled so that several positions' loads are in flight at once.
+    // Position pos = t*HW + i stepped by kHeadSlots without divisions;
+    // unrolled so that several positions' loads are in flight at once.
+    int t = 0, i = slot;
+    while (i >= HW) { i -= HW; ++t; }
 #pragma unroll 4
     for (int pos = slot; pos < T * HW; pos += kHeadSlots) {
-      const int t = pos / HW, i = pos - t * HW;
       const uint4 u = __ldg(reinterpret_cast<const uint4*>(
           x + ((static_cast<size_t>(t) * B + b) * HW + i) * C) + c8);
+      i += kHeadSlots;
+      while (i >= HW) { i -= HW; ++t; }
       const __half2* h = reinterpret_cast<const __half2*>(&u);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -1198,19 +1202,37 @@ head_pool_fc_kernel(const __half* __restrict__ x, const float* __restrict__ fc_w
     feat[c] = acc / static_cast<float>(HW) / static_cast<float>(T);
   }
   __syncthreads();
+  // Phase 2: with at least four classes per warp, a warp takes four at a
+  // time, so four rows' weight loads (and their reductions) are in flight
+  // together; fewer classes keep one per warp.
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, nwarps = blockDim.x / 32;
-  for (int n = warp; n < NC; n += nwarps) {
-    const float4* wr = reinterpret_cast<const float4*>(fc_w + static_cast<size_t>(n) * C);
-    float acc = 0.f;
-#pragma unroll 4
+  constexpr int kCls = 4;
+  const int cls = NC >= nwarps * kCls ? kCls : 1;
+  for (int n0 = warp * cls; n0 < NC; n0 += nwarps * cls) {
+    float acc[kCls];
+#pragma unroll
+    for (int u = 0; u < kCls; ++u) acc[u] = 0.f;
+#pragma unroll 2
     for (int c4 = lane; c4 < C / 4; c4 += 32) {
-      const float4 w = __ldg(wr + c4);
       const float4 f = *reinterpret_cast<const float4*>(feat + 4 * c4);
-      acc = fmaf(f.x, w.x, fmaf(f.y, w.y, fmaf(f.z, w.z, fmaf(f.w, w.w, acc))));
+#pragma unroll
+      for (int u = 0; u < kCls; ++u) {
+        if (u < cls && n0 + u < NC) {
+          const float4 w = __ldg(reinterpret_cast<const float4*>(fc_w + static_cast<size_t>(n0 + u) * C) + c4);
+          acc[u] = fmaf(f.x, w.x, fmaf(f.y, w.y, fmaf(f.z, w.z, fmaf(f.w, w.w, acc[u]))));
+        }
+      }
     }
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-    if (lane == 0) logits[static_cast<size_t>(b) * NC + n] = acc + (fc_b ? fc_b[n] : 0.f);
+    for (int off = 16; off > 0; off >>= 1) {
+#pragma unroll
+      for (int u = 0; u < kCls; ++u) acc[u] += __shfl_xor_sync(0xffffffffu, acc[u], off);
+    }
+    if (lane == 0) {
+#pragma unroll
+      for (int u = 0; u < kCls; ++u)
+        if (u < cls && n0 + u < NC) logits[static_cast<size_t>(b) * NC + n0 + u] = acc[u] + (fc_b ? fc_b[n0 + u] : 0.f);
+    }
   }
 }
 
