@@ -852,11 +852,11 @@ int launch_glue(const snn_conv_desc* d, bool pool, const void* a, const void* b,
   const bool small = n + blocks * 256 < (1LL << 31);
   GlueKernel k = glue_fn_sized<false>(mode, small);
   if (bits) {
-    // Thread = (output pixel, 16-channel word) of one image (grid y: the
-    // T*B images), 32-bit within an image.
+    // Thread = one output pixel of one image (grid y: the T*B images),
+    // 32-bit within an image.
     if (static_cast<long long>(d->H) * d->W * (d->Cout / 16) >= (1LL << 30))
       return fail(SNN_E_INVALID, "bit-packed pool: image too large");
-    const long long per_img = static_cast<long long>(p.OH) * p.OW * (d->Cout / 16);
+    const long long per_img = static_cast<long long>(p.OH) * p.OW;
     const unsigned gxb = static_cast<unsigned>(std::min<long long>((per_img + 255) / 256, 1024));
     const unsigned gyb = static_cast<unsigned>(std::min<long long>(static_cast<long long>(d->T) * d->B, 65535));
     k = (d->KH == 3 && d->KW == 3) ? snn::maxpool_bits_kernel<3>
