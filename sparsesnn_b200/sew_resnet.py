@@ -342,14 +342,20 @@ class SEWResNet18DVS(PlanModel):
         self.stem_desc = rt.make_desc(T=T, B=batch, Cin=cin, H=H, W=W, Cout=cout, KH=kh, KW=kw,
                                       stride=2, pad=kh // 2, tau=tau, v_threshold=v_threshold)
         sh, sw = (H + 2 * (kh // 2) - kh) // 2 + 1, (W + 2 * (kw // 2) - kw) // 2 + 1
-        a0 = self.buf((T * batch, sh, sw, cout))
+        # The stem's spikes go only to the max pool: bit-packed between the
+        # two where the tensor-core stem serves it (up to 64 channels, K <= 192).
+        bits = (rt.SNN_FLAG_SPIKE_BITS
+                if cout % 16 == 0 and cout <= 64 and cin * kh * kw <= 192 else 0)
+        self.stem_desc.flags = bits
+        a0 = (self.buf((T * batch, sh, sw, cout // 8), torch.uint8) if bits
+              else self.buf((T * batch, sh, sw, cout)))
         self.add(Node(STEM, "stem", [INPUT], a0, self.stem_desc,
                       (self.param(st["w"]), self.param(s), self.param(b)), (T, 0, 0, 0, 0)))
         ph, pw = pool_out(sh, 3, 2, 1), pool_out(sw, 3, 2, 1)
         p0 = self.buf((T * batch, ph, pw, cout))
-        self.add(Node(MAXPOOL, "maxpool", [a0], p0,
-                      glue_desc(T=T, B=batch, C=cout, H=sh, W=sw, neuron="none", k=3, stride=2,
-                                pad=1)))
+        pd = glue_desc(T=T, B=batch, C=cout, H=sh, W=sw, neuron="none", k=3, stride=2, pad=1)
+        pd.flags = bits
+        self.add(Node(MAXPOOL, "maxpool", [a0], p0, pd))
         kw_ = dict(T=T, B=batch, tau=tau, v_threshold=v_threshold, device=dev)
         h, w_, x = ph, pw, p0
 

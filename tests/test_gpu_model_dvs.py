@@ -62,7 +62,13 @@ def test_dvs_stem_and_pool(setup):
     P, x, x_tb, logits_ref, trace, model, torch, threads = setup
     model(torch.from_numpy(x_tb))
     torch.cuda.synchronize()
-    got = from_nhwc(model.buffer("stem").float().cpu().numpy(), T, B)
+    from sparsesnn_b200 import runtime as rt
+    stem = model.buffer("stem")
+    if model.stem_desc.flags & rt.SNN_FLAG_SPIKE_BITS:       # bit-packed stem spikes
+        got = from_nhwc(np.unpackbits(stem.cpu().numpy(), axis=-1, bitorder="little")
+                        .astype(np.float32), T, B)
+    else:
+        got = from_nhwc(stem.float().cpu().numpy(), T, B)
     st = P["stem"]
     with torch.no_grad():
         z = F.conv2d(torch.from_numpy(x_tb).flatten(0, 1), torch.from_numpy(st["w"]), stride=2,
