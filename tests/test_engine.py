@@ -117,6 +117,49 @@ def test_stem_output_size_checked_from_its_geometry(lib, tmp_path):
         ef.check_file(neg)
 
 
+def _bits_file(path, *, stem_flags, pool_flags, a0_bytes_per_px, pool_op=ef.OP_MAXPOOL_LIF,
+               T=2, B=1, H=16, cout=16):
+    """Stem -> plain max pool (3x3/2/1) -> head; the stem output tensor holds
+    a0_bytes_per_px bytes a pixel."""
+    w = ef._Writer()
+    d = rt.make_desc(T=T, B=B, Cin=3, H=H, W=H, Cout=cout, KH=3, KW=3, stride=1, pad=1,
+                     flags=stem_flags)
+    images = w.tensor(B * 3 * H * H * 4, ef.F32)
+    a0 = w.tensor(T * B * H * H * a0_bytes_per_px, ef.F16)
+    P = (H + 2 - 3) // 2 + 1
+    p0 = w.tensor(T * B * P * P * cout * 2, ef.F16)
+    logits = w.tensor(B * 4 * 4, ef.F32)
+    w.node(ef.OP_STEM, images, ef.NO_TENSOR, a0, d,
+           (w.param(np.zeros((cout, 3, 3, 3), np.float32)), w.param(np.ones(cout, np.float32)),
+            w.param(np.zeros(cout, np.float32)), 0), (1, 0, 0, 0, 0))
+    pd = rt.make_desc(T=T, B=B, Cin=cout, H=H, W=H, Cout=cout, KH=3, KW=3, stride=2, pad=1,
+                      neuron="none", flags=pool_flags)
+    w.node(pool_op, a0, a0 if pool_op == ef.OP_ADD_LIF else ef.NO_TENSOR, p0, pd)
+    w.node(ef.OP_HEAD, p0, ef.NO_TENSOR, logits, None,
+           (w.param(np.zeros((4, cout), np.float32)), w.param(np.zeros(4, np.float32)), 0, 0),
+           (T, B, P * P, cout, 4))
+    w.write(path, images, logits, T, B)
+    return path
+
+
+def test_bit_packed_stem_and_pool_nodes(lib, tmp_path):
+    """SNN_FLAG_SPIKE_BITS between a stem and its max pool: the tensor needs
+    only Cout/8 bytes a pixel when both nodes carry the flag; without it the
+    same tensor is too small, and no other glue node may take the flag."""
+    bits = rt.SNN_FLAG_SPIKE_BITS
+    ok = _bits_file(tmp_path / "bits.snne", stem_flags=bits, pool_flags=bits, a0_bytes_per_px=2)
+    assert ef.check_file(ok) == (3, 4)
+    for name, kw in [("stem_fp16", dict(stem_flags=0, pool_flags=bits)),
+                     ("pool_fp16", dict(stem_flags=bits, pool_flags=0)),
+                     ("add_bits", dict(stem_flags=bits, pool_flags=bits, pool_op=ef.OP_ADD_LIF))]:
+        bad = _bits_file(tmp_path / f"{name}.snne", a0_bytes_per_px=2, **kw)
+        with pytest.raises(rt.SnnError) as ei:
+            ef.check_file(bad)
+        assert ei.value.code == rt.SNN_E_INVALID, name
+    fp16 = _bits_file(tmp_path / "fp16.snne", stem_flags=0, pool_flags=0, a0_bytes_per_px=32)
+    assert ef.check_file(fp16) == (3, 4)
+
+
 def test_missing_engine_file(lib, tmp_path):
     with pytest.raises(rt.SnnError):
         ef.check_file(tmp_path / "absent.snne")
