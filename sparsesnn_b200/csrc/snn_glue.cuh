@@ -373,9 +373,11 @@ stem_tc_kernel(const __grid_constant__ StemParams p) {
 // epilogue of the previous one:
 // * warps 0-7 (builders): the input window under a unit (every channel,
 //   (R-1)*stride + KH rows, (TW-1)*stride + KW columns) arrives in one of two
-//   staging buffers -- one TMA box issued a unit ahead (fp32 rows with a
-//   16-byte aligned pitch; the window's first column sits dx in), or
-//   cp.async copies where the rows' pitch rules TMA out; the builders expand
+//   staging buffers -- one TMA box requested two units ahead, by the
+//   builders' thread 0 for the first two units and then by one epilogue
+//   thread (fp32 rows with a 16-byte aligned pitch; the window's first
+//   column sits dx in), or cp.async copies where the rows' pitch rules TMA
+//   out; the builders expand
 //   it into im2col k-tiles (hi/lo, a pixel's 32 columns split between two
 //   threads) in a ring of two A stages, meet at a named barrier per k-tile,
 //   and thread 0 then issues that k-tile's 8 MMAs into one of two TMEM
@@ -386,7 +388,8 @@ stem_tc_kernel(const __grid_constant__ StemParams p) {
 //   buffers; the two warps of a TMEM lane quarter (32 pixels, both channel
 //   halves) meet at their own named barrier and send their 32 pixels by one
 //   bulk copy: a tile's valid pixels are contiguous in the NHWC output
-//   (R = 1: part of a row; R > 1: TW = OW, whole rows).
+//   (R = 1: part of a row; R > 1: TW = OW, whole rows).  Bit-packed spikes
+//   (p.bits_out) leave straight from registers as 16-bit words instead.
 // 16 warps, 4 per SM sub-partition: 128 registers a thread.  Every wait is
 // bounded; a group whose wait expires sets the error word and stops, and the
 // group waiting on it then expires in turn.
